@@ -1,0 +1,44 @@
+"""Loading the committed golden fixtures (tests/golden/*, made by tests/golden/make_fixtures.py
+from the reference implementation)."""
+from __future__ import annotations
+
+import functools
+import gzip
+import json
+from pathlib import Path
+
+import numpy as np
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@functools.lru_cache(None)
+def queues() -> dict:
+    with gzip.open(GOLDEN / "queues.json.gz", "rt") as f:
+        return json.load(f)
+
+
+@functools.lru_cache(None)
+def numerics() -> dict:
+    with np.load(GOLDEN / "numerics.npz") as z:
+        return {k: z[k] for k in z.files}
+
+
+@functools.lru_cache(None)
+def models() -> dict:
+    p = GOLDEN / "models.json"
+    return json.loads(p.read_text()) if p.exists() else {}
+
+
+def queue_params():
+    """(set name, case) pairs for parametrisation."""
+    q = queues()
+    return [(name, c) for name, s in q.items() for c in s["cases"]]
+
+
+def build(name: str, case: dict):
+    from tests.golden import cases
+    q = queues()[name]
+    if name == "chains":
+        return cases.build_chain(case["seed"])
+    return cases.build_case(case["seed"], tuple(q["kinds"]), q["n_desc"], q["p_corrupt"])

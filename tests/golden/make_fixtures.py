@@ -1,0 +1,222 @@
+"""Generate the golden fixtures under tests/golden/ by running the REFERENCE implementation.
+
+Run in a container that holds the reference checkout (it is never needed at test time):
+
+    PYTHONDONTWRITEBYTECODE=1 python -m tests.golden.make_fixtures --ref <path to openTARS> [--models]
+
+What it stores (all small):
+  queues.json.gz   per seeded program (tests/golden/cases.py): the reference golden Machine's
+                   end status, ContractError flag, per-descriptor stats and the SHA-256 of the
+                   whole DDR image after the run
+  numerics.npz     seeded inputs' output bits from the reference's numerics.py functions
+  models.json      (--models) per-step logits SHA-256 / argmax of the reference's QwenLowering
+                   + golden Machine greedy decode for small Qwen3 / Gemma-3 configs, and the
+                   SHA-256 of the lowered DDR image and queue bytes
+"""
+from __future__ import annotations
+
+import argparse
+import gzip
+import hashlib
+import json
+import os
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parent.parent))
+
+from tests.golden import cases  # noqa: E402
+
+QUEUE_SETS = {
+    # name: (first seed, count, kinds, descriptors per queue or None, corruption probability)
+    "mixed": (0, 400, tuple(cases.GENS), None, 0.06),
+    "gemm": (10000, 120, ("gemm",), 4, 0.0),
+    "w4": (20000, 80, ("w4",), 3, 0.0),
+    "row": (30000, 120, ("row",), 4, 0.0),
+    "elt": (40000, 160, ("elt",), 4, 0.0),
+    "rope": (50000, 60, ("rope",), 3, 0.0),
+    "fdot": (60000, 80, ("fdot",), 3, 0.0),
+    "relu": (70000, 60, ("relu",), 4, 0.0),
+    "conv": (80000, 40, ("conv",), 2, 0.0),
+    "errors": (90000, 120, tuple(cases.GENS), 3, 0.5),
+}
+CHAINS = (100000, 30)
+
+
+def ref_modules(ref: str):
+    sys.path.insert(0, ref)
+    import tars_mini.golden as G
+    import tars_mini.numerics as F
+    return G, F
+
+
+def run_ref_queue(G, ddr, qaddr, qlen, gemv_only=False):
+    m = G.Machine(bytearray(ddr), gemv_only=gemv_only)
+    try:
+        st = m.run_queue(qaddr, qlen)
+        status = [bool(st.done), int(st.err_code), int(st.op_idx)]
+        cerr = False
+    except G.ContractError:
+        status, cerr = [bool(m.status.done), int(m.status.err_code), int(m.status.op_idx)], True
+    stats = [[s.opcode, s.macs, s.bytes_read, s.bytes_written] for s in m.stats]
+    return dict(status=status, contract_error=cerr, stats=stats,
+                sha256=hashlib.sha256(bytes(m.ddr)).hexdigest())
+
+
+def make_queues(G):
+    out = {}
+    for name, (s0, cnt, kinds, nd, pc) in QUEUE_SETS.items():
+        rows = []
+        for s in range(s0, s0 + cnt):
+            ddr, qa, ql = cases.build_case(s, kinds, nd, pc)
+            r = run_ref_queue(G, ddr, qa, ql)
+            r.update(seed=s, qlen=ql)
+            rows.append(r)
+        out[name] = dict(kinds=list(kinds), n_desc=nd, p_corrupt=pc, cases=rows)
+    s0, cnt = CHAINS
+    rows = []
+    for s in range(s0, s0 + cnt):
+        ddr, qa, ql = cases.build_chain(s)
+        r = run_ref_queue(G, ddr, qa, ql)
+        r.update(seed=s, qlen=ql)
+        rows.append(r)
+    out["chains"] = dict(cases=rows)
+    return out
+
+
+def numerics_inputs(seed: int = 7, n: int = 1 << 11):
+    """Float32 inputs covering the interesting ranges and every special value."""
+    rng = np.random.default_rng(seed)
+    parts = [
+        rng.uniform(-110, 95, n).astype(np.float32),
+        rng.normal(0, 3, n).astype(np.float32),
+        (np.exp(rng.uniform(-87, 88, n)) * rng.choice([-1, 1], n)).astype(np.float32),
+        rng.integers(0, 1 << 32, n, dtype=np.uint64).astype(np.uint32).view(np.float32),
+        np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e-40, -1e-40, 89.0, -104.0, 88.99, -103.99,
+                  20.0, 20.000002, 2.0 ** 126, 1.5 * 2.0 ** 126, 2.0 ** -126, 3.4e38, -3.4e38,
+                  0.5, 1.5, 2.5, -0.5, 127.5, -127.5], np.float32),
+    ]
+    return np.concatenate(parts)
+
+
+def make_numerics(F):
+    x = numerics_inputs()
+    res = {"x": x}
+    for name in ("exp_f", "recip_f", "rsqrt_f", "gelu_f", "silu_f", "sigmoid_f", "softplus_f", "ftz", "fabs"):
+        res[name] = getattr(F, name)(x).view(np.uint32)
+    for act in range(8):
+        res[f"act{act}"] = F.act_fn(x, act).view(np.uint32)
+    res["bf16"] = F.to_bf16_bits(x)
+    res["fp16"] = F.to_fp16_bits(x)
+    res["from_fp16"] = F.from_fp16_bits(np.arange(1 << 16, dtype=np.uint16)).view(np.uint32)
+    rng = np.random.default_rng(8)
+    y = x[rng.permutation(x.size)]
+    res["fmul"] = F.fmul(x, y).view(np.uint32)
+    res["fadd"] = F.fadd(x, y).view(np.uint32)
+    res["fmax"] = F.fmax(x, y).view(np.uint32)
+    res["q8_inv"] = np.float32(rng.uniform(0.5, 50))
+    res["q8"] = F.q8(x, res["q8_inv"]).astype(np.int8)
+    # row functions on [64, 256] tiles (with a few special values and zero rows)
+    xr = rng.normal(0, 2, (64, 256)).astype(np.float32)
+    xr[3] = 0
+    xr[5, 7] = np.nan
+    xr[6, 9] = np.inf
+    xr[7, :] *= np.float32(1e-39)
+    res["rows_x"] = xr
+    q, s = F.quant_rows(xr)
+    res["quant_q"], res["quant_s"] = q, s.view(np.uint32)
+    res["sum16"] = F.sum16(xr).view(np.uint32)
+    res["max16"] = F.max16(xr).view(np.uint32)
+    gam = rng.normal(1, 0.2, 256).astype(np.float32)
+    bet = rng.normal(0, 0.2, 256).astype(np.float32)
+    res["gamma"], res["beta"] = gam, bet
+    res["rmsnorm"] = F.rmsnorm_rows(xr, gam, None, np.float32(1e-6)).view(np.uint32)
+    res["layernorm"] = F.layernorm_rows(xr, gam, bet, np.float32(1e-5)).view(np.uint32)
+    res["l2norm"] = F.l2norm_rows(xr, gam, None, np.float32(1e-6)).view(np.uint32)
+    valid = rng.integers(1, 257, 64)
+    res["valid"] = valid
+    res["softmax_causal"] = F.softmax_rows_causal(xr, valid).view(np.uint32)
+    res["softmax"] = F.softmax_rows(xr).view(np.uint32)
+    b = rng.normal(0, 2, (32, 256)).astype(np.float32)
+    res["fdot_b"] = b
+    res["fdot_nt"] = F.fdot_nt(xr[:16], b).view(np.uint32)
+    bn = rng.normal(0, 2, (256, 48)).astype(np.float32)
+    res["fdot_bn"] = bn
+    res["fdot_nn"] = F.fdot_nn(xr[:16], bn).view(np.uint32)
+    tab = rng.uniform(-1, 1, (32, 128)).astype(np.float32)
+    res["rope_tab"] = tab
+    res["rope"] = F.rope_rows(xr, tab, 2, 128).view(np.uint32)
+    xa = (rng.normal(0, 1, (8, 1024)) * (2.0 ** rng.integers(-40, 40, (8, 1024)))).astype(np.float32)
+    xa[0, 5] = np.nan
+    xa[1, 130] = np.inf
+    xa[2, :128] = 0
+    res["w4_x"] = xa
+    aq, asc = F.align_w4_groups(xa)
+    res["w4_q"], res["w4_s"] = aq, asc.view(np.uint32)
+    return res
+
+
+# ------------------------------------------------------------------------- model fixtures
+MODEL_CASES = [
+    # name, base config, layer types, vocab, max_tokens, prompt, new tokens, chunk of prefill
+    ("qwen3_small", "CFG_Q3_SMALL", ["full_attention"] * 3, 4096, 32, [5, 77, 901, 12, 3000, 2, 9], 4),
+    ("gemma3_small", "G3_SMALL_K2", ["sliding_attention", "full_attention", "sliding_attention"], 4096, 32,
+     [5, 77, 901, 12, 3000, 2], 4),
+]
+
+
+def make_models(ref: str):
+    import tars_mini.qwen_ref as Q
+    from tars_mini import golden as G
+    from tars_mini.llm import QwenLowering
+    out = {}
+    for name, base, types, vocab, T, prompt, new in MODEL_CASES:
+        bcfg = dict(Q.CFG_G3_SMALL, intermediate_size=4608) if base == "G3_SMALL_K2" else getattr(Q, base)
+        cfg = Q.make_config(bcfg, types, vocab=vocab)
+        w = Q.random_weights(cfg, seed=0, embed=True)
+        low = QwenLowering(cfg, w, max_tokens=T, ddr_bytes=1 << 26, head=True, queue_cap=4096)
+        image_sha = hashlib.sha256(bytes(low.p.ddr)).hexdigest()
+        queues = []
+
+        def run(ddr, q, n):
+            queues.append(hashlib.sha256(bytes(ddr[q:q + 64 * n])).hexdigest())
+            m = G.Machine(ddr, gemv_only=True)
+            assert m.run_queue(q, n).done
+            return m.ddr
+        ids, logits, counts = low.generate(run, prompt, new)
+        out[name] = dict(base=base, types=types, vocab=vocab, T=T, prompt=prompt, new=new, image_sha256=image_sha,
+                         queue_sha256=queues, counts=counts, ids=ids,
+                         logits_sha256=[hashlib.sha256(lg.astype("<f4").tobytes()).hexdigest() for lg in logits],
+                         logits_head=[lg[:8].astype(np.float32).view(np.uint32).tolist() for lg in logits],
+                         final_ddr_sha256=hashlib.sha256(bytes(low.p.ddr)).hexdigest())
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("OPENTARS_REF", ""), required=False)
+    ap.add_argument("--models", action="store_true")
+    ap.add_argument("--skip-queues", action="store_true")
+    a = ap.parse_args()
+    if not a.ref:
+        raise SystemExit("--ref <path to the openTARS checkout> is required")
+    G, F = ref_modules(a.ref)
+    t = time.time()
+    if not a.skip_queues:
+        q = make_queues(G)
+        with gzip.open(HERE / "queues.json.gz", "wt") as f:
+            json.dump(q, f)
+        np.savez_compressed(HERE / "numerics.npz", **make_numerics(F))
+        print(f"queues + numerics in {time.time() - t:.1f}s")
+    if a.models:
+        m = make_models(a.ref)
+        (HERE / "models.json").write_text(json.dumps(m, indent=1))
+        print(f"models in {time.time() - t:.1f}s")
+
+
+if __name__ == "__main__":
+    main()
