@@ -1,0 +1,100 @@
+/* libtarscuda - the tars_mini golden executor on an NVIDIA B200 (sm_100a), as a C ABI.
+ *
+ * The reference implements one NPU "device" behind two call surfaces:
+ *   - tars_mini/golden.py  Machine(ddr).run_queue(queue_addr, queue_len) -> Status   (golden.py:41-492)
+ *   - deploy/kv260/sw/tars_board.py device backends: mem / to_dev(a, n) / from_dev(a, n) /
+ *     run(q, n) -> (done, err, op_idx, cycles)  (tars_board.py:1-13, 50-178), whose board
+ *     backend loads a tiny C library with ctypes (libtmdrv: tm_open / tm_alloc / tm_wr / tm_rd /
+ *     tm_clean / tm_inval, tars_board.py:58-65).
+ * This library is that device for a B200: the DDR image lives in HBM, descriptors are checked on
+ * the host in the contract's order and executed by CUDA kernels in queue order. Plain C types
+ * only; every function returns TC_OK or a negative error (tc_last_error gives the text), except
+ * where noted.
+ */
+#ifndef TARSCUDA_H
+#define TARSCUDA_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TC_ABI_VERSION 1
+#define TC_OK 0
+#define TC_CONTRACT 1      /* an illegal program: golden.py raises ContractError (golden.py:473-479) */
+#define TC_ERR_CUDA (-1)
+#define TC_ERR_ARG (-2)
+
+typedef struct tc_machine tc_machine;
+typedef struct tc_graph tc_graph;
+
+/* golden.py:22-29 Status(done, err_code, op_idx) */
+typedef struct { int32_t done, err_code, op_idx; } tc_status;
+/* golden.py:32-39 OpStat(opcode, macs, bytes_read, bytes_written) */
+typedef struct { uint64_t opcode, macs, bytes_read, bytes_written; } tc_opstat;
+/* One set of byte segments [base + i*ld, base + i*ld + nbytes), i < count. kind >= 0: the
+ * descriptor's read tensor of that index; -1: its output rows; -2: ROW_QUANT's second output.
+ * base = base_hi * 2^64 + base_lo (BASE_ADDR + offset can exceed 64 bits). */
+typedef struct { int32_t kind; uint64_t base_lo, base_hi, ld, nbytes, count; } tc_seg;
+
+int tc_version(void);
+
+/* An HBM image of ddr_bytes zero bytes on CUDA device `device`; replaces the board backend's
+ * tm_open + tm_alloc (tars_board.py:58-65, tmdrv.c) and golden.Machine's ddr bytearray. */
+int tc_open(int device, uint64_t ddr_bytes, tc_machine** out);
+int tc_close(tc_machine* m);
+const char* tc_last_error(tc_machine* m);
+/* The image's device address and CUDA stream (cudaStream_t), for callers that launch work in
+ * the same stream order (the decode engine). */
+uint64_t tc_device_ptr(tc_machine* m);
+void* tc_stream(tc_machine* m);
+
+/* Host <-> image copies; replace tars_board's to_dev(a, n) / from_dev(a, n) (tars_board.py:101-110)
+ * and golden.Machine.write / read (golden.py:52-56). */
+int tc_upload(tc_machine* m, uint64_t addr, const void* src, uint64_t n);
+int tc_download(tc_machine* m, uint64_t addr, void* dst, uint64_t n);
+/* Makes the image equal to `host` (n == image size): every 64 KiB block that differs from
+ * `shadow` (the caller's copy of what the image held) is uploaded and copied into shadow.
+ * The drop-in Machine uses it to honour host writes made between runs (llm.py:793-799). */
+int tc_sync_up(tc_machine* m, const void* host, void* shadow, uint64_t n, uint64_t* uploaded);
+/* Copies every byte range the last tc_run_queue wrote back into `host` (and `shadow` if given),
+ * so the caller's bytearray is mutated in place as golden.Machine mutates its ddr. */
+int tc_sync_down(tc_machine* m, void* host, void* shadow);
+
+/* Runs queue_len descriptors at queue_addr strictly in order; replaces golden.Machine.run_queue
+ * (golden.py:450-492) and tars_board's dev.run(q, n) (tars_board.py:117-152, 173-178). Returns
+ * TC_OK with *st set (done, or the first error code and its descriptor), or TC_CONTRACT with
+ * *contract_op = the illegal descriptor's index (earlier descriptors' writes kept), or < 0. */
+int tc_run_queue(tc_machine* m, uint64_t queue_addr, uint32_t queue_len, int32_t core_id,
+                 int32_t gemv_only, tc_status* st, int32_t* contract_op);
+/* The last run's per-descriptor stats (golden.Machine.stats); returns how many there are. */
+uint32_t tc_stats(tc_machine* m, tc_opstat* out, uint32_t cap);
+
+/* Checks a queue exactly as tc_run_queue does and captures its kernels as one CUDA graph without
+ * running them; *st is the status the run would end with. The board runtime runs one fixed queue
+ * per position (tars_board.py:316-329, llm.py:548-571), so a queue is checked once and replayed.
+ * timing != 0 records an event between descriptors (tc_graph_times). A queue whose descriptors
+ * rewrite later descriptors of the same queue is refused (TC_ERR_ARG). */
+int tc_queue_capture(tc_machine* m, uint64_t queue_addr, uint32_t queue_len, int32_t core_id,
+                     int32_t gemv_only, int32_t timing, tc_status* st, int32_t* contract_op,
+                     tc_graph** out);
+/* Enqueues the captured queue on `stream` (NULL: the machine's stream); the next tc_sync_down
+ * copies back the ranges it writes. */
+int tc_graph_launch(tc_graph* g, void* stream);
+/* Per-descriptor milliseconds of the last launch of a graph captured with timing; returns the count. */
+int tc_graph_times(tc_graph* g, float* ms, uint32_t cap);
+int tc_graph_destroy(tc_graph* g);
+/* Waits for everything enqueued on the machine's stream. */
+int tc_synchronize(tc_machine* m);
+
+/* Host-only helpers (no device needed). golden.Machine.validate (golden.py:59-169): decodes the
+ * 23 fields of contract.py:14-38 into fields[23] (in that table's order) and returns the first
+ * failing check (E_OK .. E_ALIGN). */
+int tc_validate(const uint8_t* raw64, int32_t core_id, int32_t gemv_only, uint64_t* fields23);
+/* golden.Machine.segments / extra_out (golden.py:195-256) as strided sets; *count = how many. */
+int tc_footprint(const uint8_t* raw64, tc_seg* out, uint32_t cap, uint32_t* count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

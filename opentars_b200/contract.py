@@ -1,0 +1,130 @@
+"""The tars_mini v0.4 descriptor contract on the host: field table, codes, encode/decode.
+
+Mirrors the reference's tars_mini/contract.py call surface (contract.py:14-181) so descriptor
+emitters (the compiler and the lowering) and tests written against it run unchanged. The device
+side decodes and validates in C++ (libtarscuda); this module only builds and reads descriptors.
+"""
+from __future__ import annotations
+
+import struct
+import zlib
+
+import numpy as np
+
+# (hi, lo) bit positions, little endian: byte i holds bits 8i+7..8i (contract.py:14-38)
+LAYOUT = {
+    "MAGIC": (511, 496), "VERSION": (495, 480), "CORE_ID": (479, 472), "HDR_RSV": (471, 448),
+    "OPCODE": (447, 432), "CTRL": (431, 416), "GROUP_SIZE": (415, 400), "EPI": (399, 384),
+    "BASE_ADDR": (383, 320), "A_OFF": (319, 288), "W_OFF": (287, 256), "Y_OFF": (255, 224),
+    "SCALE_OFF": (223, 192), "BIAS_OFF": (191, 160), "M": (159, 144), "N": (143, 128), "K": (127, 112),
+    "LDA16": (111, 96), "OUT_SCALE": (95, 64), "CRC32": (63, 32), "VALID": (31, 31), "LDY16": (30, 16),
+    "DEP_SIG": (15, 0),
+}
+FIELD_ORDER = tuple(LAYOUT)            # the order libtarscuda's tc_validate returns fields in
+
+DESC_BYTES = 64
+MAGIC, VERSION = 0xAA55, 0x0002
+OP_GEMM, OP_RELU, OP_ROW = 0x02, 0x03, 0x04
+ROW_SOFTMAX, ROW_LAYERNORM, ROW_RMSNORM = 0, 1, 2
+OP_CONV, OP_CONV_ACT = 0x01, 0x05
+CONV_OPS = (OP_CONV, OP_CONV_ACT)
+OP_ELT, OP_ROPE, OP_FDOT = 0x06, 0x07, 0x08
+V04_OPS = (OP_ELT, OP_ROPE, OP_FDOT)
+ELT_MUL, ELT_ADD, ELT_MULADD, ELT_SUB = 0, 1, 2, 3
+BM_DENSE, BM_ROW, BM_COL, BM_SCALAR = 0, 1, 2, 3
+AM_DENSE, AM_ROW = 0, 1
+FDOT_NT, FDOT_NN = 0, 1
+ROW_L2NORM, ROW_QUANT = 3, 4
+QM_NONE, QM_TENSOR, QM_CHANNEL, QM_ROWCOL = 0, 1, 2, 3
+QM_GROUP = QM_ROWCOL
+DT_BF16, DT_INT8, DT_INT4, DT_FP8, DT_FP32 = 0, 1, 2, 3, 4
+W4_GROUP = 128
+W4A16_MIN_VERSION = 0x00040001
+ACT_NONE, ACT_RELU, ACT_RELU6, ACT_GELU, ACT_SILU = 0, 1, 2, 3, 4
+ACT_SIGMOID, ACT_SOFTPLUS, ACT_EXP = 5, 6, 7
+OUT_FP32, OUT_BF16, OUT_INT8, OUT_FP16 = 0, 1, 2, 3
+ESIZE = {OUT_FP32: 4, OUT_BF16: 2, OUT_INT8: 1, OUT_FP16: 2}
+STATE_FP16 = 1 << 3
+FP16_MIN_VERSION = 0x00030400
+E_OK, E_MAGIC, E_VERSION, E_CRC, E_VALID, E_OPCODE, E_FIELD, E_ALIGN, E_RANGE = range(9)
+ERR_NAMES = {E_OK: "OK", E_MAGIC: "E_MAGIC", E_VERSION: "E_VERSION", E_CRC: "E_CRC", E_VALID: "E_VALID",
+             E_OPCODE: "E_OPCODE", E_FIELD: "E_FIELD", E_ALIGN: "E_ALIGN", E_RANGE: "E_RANGE"}
+K_MAX = 65535
+CANON_NAN = 0x7FC00000
+
+
+def check_layout() -> None:
+    used = np.zeros(512, dtype=int)
+    for hi, lo in LAYOUT.values():
+        assert 511 >= hi >= lo >= 0
+        used[lo:hi + 1] += 1
+    assert (used == 1).all(), "fields overlap or leave holes"
+
+
+def width(name: str) -> int:
+    hi, lo = LAYOUT[name]
+    return hi - lo + 1
+
+
+def conv_geom(h: int, kh: int, kw: int, stride: int = 1, pad: int = 0) -> int:
+    assert 0 < h < 4096 and 0 < kh < 16 and 0 < kw < 16 and 1 <= stride <= 4 and 0 <= pad <= 3
+    return h << 12 | kh << 8 | kw << 4 | (stride - 1) << 2 | pad
+
+
+def conv_params(d: dict) -> dict:
+    g = d["HDR_RSV"]
+    h, kh, kw, s, p, w = g >> 12, g >> 8 & 15, g >> 4 & 15, (g >> 2 & 3) + 1, g & 3, d["GROUP_SIZE"]
+    cin = d["K"] // (kh * kw) if kh and kw else 0
+    return dict(H=h, W=w, KH=kh, KW=kw, S=s, P=p, Cin=cin,
+                OH=(h + 2 * p - kh) // s + 1, OW=(w + 2 * p - kw) // s + 1)
+
+
+def ctrl(qmode: int = QM_TENSOR, symmetric: int = 1, a_dtype: int = DT_INT8, w_dtype: int = DT_INT8,
+         fusion: int = 0) -> int:
+    return (qmode & 7) | (symmetric & 1) << 3 | (a_dtype & 15) << 4 | (w_dtype & 15) << 8 | (fusion & 1) << 12
+
+
+def epi(act: int = ACT_NONE, out: int = OUT_FP32, bias: int = 0) -> int:
+    return (act & 3) | (out & 3) << 2 | (bias & 1) << 4 | (act >> 2 & 1) << 5
+
+
+def act_of(e: int) -> int:
+    return (e & 3) | (e >> 5 & 1) << 2
+
+
+def f32_bits(x: float) -> int:
+    return struct.unpack("<I", struct.pack("<f", x))[0]
+
+
+def bits_f32(b: int) -> np.float32:
+    return np.frombuffer(struct.pack("<I", b & 0xFFFFFFFF), dtype="<f4")[0]
+
+
+def _crc(raw: bytes) -> int:
+    z = bytearray(raw)
+    z[4:8] = b"\0\0\0\0"
+    return zlib.crc32(bytes(z)) & 0xFFFFFFFF
+
+
+def encode(fields: dict, *, fix_crc: bool = True) -> bytes:
+    """64 bytes, little endian; fields not given are 0; the CRC (CRC-32/ISO-HDLC over all 64
+    bytes with bytes 4..7 zeroed) is filled in unless fix_crc is False."""
+    v = 0
+    for name, val in fields.items():
+        hi, lo = LAYOUT[name]
+        if not 0 <= val < (1 << (hi - lo + 1)):
+            raise ValueError(f"{name}={val} does not fit {hi - lo + 1} bits")
+        v |= val << lo
+    raw = bytearray(v.to_bytes(DESC_BYTES, "little"))
+    if fix_crc:
+        raw[4:8] = struct.pack("<I", _crc(bytes(raw)))
+    return bytes(raw)
+
+
+def decode(raw: bytes) -> dict:
+    v = int.from_bytes(raw, "little")
+    return {n: (v >> lo) & ((1 << (hi - lo + 1)) - 1) for n, (hi, lo) in LAYOUT.items()}
+
+
+def crc_ok(raw: bytes) -> bool:
+    return struct.unpack("<I", bytes(raw[4:8]))[0] == _crc(raw)

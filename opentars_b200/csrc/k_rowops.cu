@@ -1,0 +1,216 @@
+// Row ops (golden.py:358-380), the RELU/activation op (351-356), ELT (393-418), ROPE (420-424)
+// and FDOT (426-435) for sm_100a, bit-exact to numerics.py.
+//
+// Reductions keep the contract's order: sum16 = 16 lanes (a half-warp), lane j mod 16, each a
+// sequential fadd chain from +0, then the pairwise fold (0+1),(2+3).. done as xor-shuffles 1,2,4,8
+// (IEEE addition is commutative, so lane l and lane l^1 compute the same pair sum). max16 uses
+// fmax, which is order-free by construction. FDOT NN is the strict k-order chain, one thread per
+// output. Elementwise ops are one thread per element: in-place ELT (A or C is the output itself)
+// reads an element before the same thread writes it.
+#include <cuda_runtime.h>
+
+#include "fp32.cuh"
+#include "ops.h"
+
+namespace tc {
+
+namespace {
+
+__device__ __forceinline__ float sum16_fold(float v) {
+  v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+  v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
+  v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));
+  v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 8));
+  return v;
+}
+__device__ __forceinline__ float max_fold(float v) {
+  v = fmax_c(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+  v = fmax_c(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
+  v = fmax_c(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));
+  v = fmax_c(v, __shfl_xor_sync(0xFFFFFFFFu, v, 8));
+  return v;
+}
+
+// One half-warp per row; 8 rows per 128-thread block.
+__global__ void __launch_bounds__(128) k_rowop(RowArgs a) {
+  const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
+  const int m = blockIdx.x * 8 + hw;
+  const bool live = m < a.M;            // dead half-warps still join the shuffles
+  const int mm = live ? m : 0;
+  const uint8_t* x = a.X + (uint64_t)mm * a.lda;
+  uint8_t* y = a.Y + (uint64_t)mm * a.ldy;
+  const int N = a.N;
+  auto X = [&](int j) { return ftz(ld_f32(x + 4 * (uint64_t)j)); };
+
+  if (a.fn == ROW_QUANT) {
+    float amax = 0.0f;
+    for (int j = l; j < N; j += 16) amax = fmax_c(amax, fabs_c(X(j)));
+    amax = max_fold(amax);
+    const float inv = fmul(127.0f, recip_f(amax));
+    if (live) {
+      for (int j = l; j < N; j += 16) y[j] = (uint8_t)q8(X(j), inv);
+      if (l == 0) st_u32(a.scale_out + 4 * (uint64_t)m, fb(ftz(fmul(amax, bf(0x3C010204u)))));
+    }
+    return;
+  }
+  if (a.fn == ROW_SOFTMAX) {
+    const int valid = a.K ? min(N, a.K + m) : N;
+    float mx = bf(0xFF800000u);          // -inf: the identity of fmax
+    for (int j = l; j < valid; j += 16) mx = fmax_c(mx, X(j));
+    mx = max_fold(mx);
+    float s = 0.0f;
+    for (int j = l; j < N; j += 16) s = fadd(s, j < valid ? exp_f(fadd(X(j), neg(mx))) : 0.0f);
+    const float r = recip_f(sum16_fold(s));
+    if (live)
+      for (int j = l; j < N; j += 16)
+        store_out(y, j, fmul(j < valid ? exp_f(fadd(X(j), neg(mx))) : 0.0f, r), a.out, a.out_scale);
+    return;
+  }
+  // norms: gamma at SCALE_OFF, optional beta, eps from W_OFF
+  const float kinv = recip_f(i2f(N));
+  float mean = 0.0f;
+  if (a.fn == ROW_LAYERNORM) {
+    float s = 0.0f;
+    for (int j = l; j < N; j += 16) s = fadd(s, X(j));
+    mean = fmul(sum16_fold(s), kinv);
+  }
+  float s = 0.0f;
+  for (int j = l; j < N; j += 16) {
+    const float v = a.fn == ROW_LAYERNORM ? fadd(X(j), neg(mean)) : X(j);
+    s = fadd(s, fmul(v, v));
+  }
+  s = sum16_fold(s);
+  const float rs = rsqrt_f(a.fn == ROW_L2NORM ? fadd(s, a.eps) : fadd(fmul(s, kinv), a.eps));
+  if (!live) return;
+  for (int j = l; j < N; j += 16) {
+    const float v = a.fn == ROW_LAYERNORM ? fadd(X(j), neg(mean)) : X(j);
+    float o = fmul(fmul(v, rs), ld_f32(a.gamma + 4 * (uint64_t)j));
+    if (a.beta) o = fadd(o, ld_f32(a.beta + 4 * (uint64_t)j));
+    store_out(y, j, o, a.out, a.out_scale);
+  }
+}
+
+__global__ void k_act(ActArgs a) {
+  const uint64_t total = (uint64_t)a.M * a.N;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / a.N), n = (int)(i - (uint64_t)m * a.N);
+    const float v = ld_f32(a.X + (uint64_t)m * a.lda + 4 * (uint64_t)n);
+    store_out(a.Y + (uint64_t)m * a.ldy, n, act_fn(v, a.act), a.out, a.out_scale);
+  }
+}
+
+__global__ void k_elt(EltArgs a) {
+  const uint64_t total = (uint64_t)a.M * a.N;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / a.N), n = (int)(i - (uint64_t)m * a.N);
+    const uint8_t* ap = a.A + (uint64_t)m * a.lda;
+    float av = a.a_fp16 ? from_fp16(ld_u16(ap + 2 * (uint64_t)n)) : ld_f32(ap + 4 * (uint64_t)n);
+    float bv;
+    switch (a.bmode) {
+      case BM_DENSE: bv = ld_f32(a.B + (uint64_t)m * a.ldb + 4 * (uint64_t)n); break;
+      case BM_ROW: bv = ld_f32(a.B + 4 * (uint64_t)n); break;
+      case BM_COL: bv = ld_f32(a.B + 4 * (uint64_t)m); break;
+      default: bv = ld_f32(a.B); break;
+    }
+    uint8_t* yrow = a.Y + (uint64_t)m * a.ldy;
+    float cv = 0.0f;
+    if (a.op == ELT_MULADD)
+      cv = a.out == OUT_FP16 ? from_fp16(ld_u16(a.C + (uint64_t)m * a.ldy + 2 * (uint64_t)n))
+                             : ld_f32(a.C + (uint64_t)m * a.ldy + 4 * (uint64_t)n);
+    av = act_fn(av, a.act);
+    float r;
+    switch (a.op) {
+      case ELT_MUL: r = fmul(av, bv); break;
+      case ELT_ADD: r = fadd(av, bv); break;
+      case ELT_SUB: r = fadd(av, neg(ftz(bv))); break;
+      default: r = fadd(cv, fmul(av, bv)); break;
+    }
+    store_out(yrow, n, r, a.out, a.out_scale);
+  }
+}
+
+__global__ void k_rope(RopeArgs a) {
+  const uint64_t total = (uint64_t)a.M * a.N;
+  const int h = a.R / 2;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / a.N), n = (int)(i - (uint64_t)m * a.N);
+    const uint8_t* x = a.X + (uint64_t)m * a.lda;
+    const uint8_t* t = a.tab + (uint64_t)(m / a.G) * 4 * a.R;
+    float r;
+    if (n < h) {
+      const float c = ftz(ld_f32(t + 4 * n)), s = ftz(ld_f32(t + 4 * (h + n)));
+      r = fadd(fmul(ld_f32(x + 4 * n), c), neg(fmul(ld_f32(x + 4 * (n + h)), s)));
+    } else if (n < a.R) {
+      const int i0 = n - h;
+      const float c = ftz(ld_f32(t + 4 * i0)), s = ftz(ld_f32(t + 4 * (h + i0)));
+      r = fadd(fmul(ld_f32(x + 4 * n), c), fmul(ld_f32(x + 4 * i0), s));
+    } else {
+      r = ftz(ld_f32(x + 4 * (uint64_t)n));
+    }
+    store_out(a.Y + (uint64_t)m * a.ldy, n, r, a.out, a.out_scale);
+  }
+}
+
+// FDOT NT: one half-warp per output (m, n), sum16 order over k.
+__global__ void __launch_bounds__(128) k_fdot_nt(FdotArgs a) {
+  const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
+  const uint64_t o = blockIdx.x * 8ull + hw;
+  const bool live = o < (uint64_t)a.M * a.N;
+  const int m = live ? (int)(o / a.N) : 0, n = live ? (int)(o % a.N) : 0;
+  const uint8_t* ar = a.A + (uint64_t)m * a.lda;
+  const uint8_t* br = a.B + (uint64_t)n * a.ldb;
+  float s = 0.0f;
+  for (int k = l; k < a.K; k += 16) s = fadd(s, fmul(ld_f32(ar + 4 * k), ld_f32(br + 4 * k)));
+  s = sum16_fold(s);
+  if (live && l == 0) store_out(a.Y + (uint64_t)m * a.ldy, n, s, a.out, a.out_scale);
+}
+
+// FDOT NN: one thread per output, y = (((+0 + a0 b0) + a1 b1) + ...) in k order.
+__global__ void k_fdot_nn(FdotArgs a) {
+  const uint64_t total = (uint64_t)a.M * a.N;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / a.N), n = (int)(i - (uint64_t)m * a.N);
+    const uint8_t* ar = a.A + (uint64_t)m * a.lda;
+    float s = 0.0f;
+    for (int k = 0; k < a.K; ++k) {
+      const uint8_t* bp = a.B + (uint64_t)k * a.ldb;
+      const float bv = a.b_fp16 ? from_fp16(ld_u16(bp + 2 * (uint64_t)n)) : ld_f32(bp + 4 * (uint64_t)n);
+      s = fadd(s, fmul(ld_f32(ar + 4 * (uint64_t)k), bv));
+    }
+    store_out(a.Y + (uint64_t)m * a.ldy, n, s, a.out, a.out_scale);
+  }
+}
+
+inline int grid_for(uint64_t total, int threads) {
+  const uint64_t b = (total + threads - 1) / threads;
+  return (int)std::min<uint64_t>(std::max<uint64_t>(b, 1), 148ull * 32);
+}
+}  // namespace
+
+cudaError_t launch_rowop(const RowArgs& a, cudaStream_t st) {
+  k_rowop<<<(a.M + 7) / 8, 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t launch_act(const ActArgs& a, cudaStream_t st) {
+  k_act<<<grid_for((uint64_t)a.M * a.N, 256), 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t launch_elt(const EltArgs& a, cudaStream_t st) {
+  k_elt<<<grid_for((uint64_t)a.M * a.N, 256), 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t launch_rope(const RopeArgs& a, cudaStream_t st) {
+  k_rope<<<grid_for((uint64_t)a.M * a.N, 256), 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t launch_fdot(const FdotArgs& a, cudaStream_t st) {
+  if (a.nn) {
+    k_fdot_nn<<<grid_for((uint64_t)a.M * a.N, 128), 128, 0, st>>>(a);
+  } else {
+    const uint64_t outs = (uint64_t)a.M * a.N;
+    k_fdot_nt<<<(unsigned)((outs + 7) / 8), 128, 0, st>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace tc

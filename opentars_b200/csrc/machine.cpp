@@ -1,0 +1,542 @@
+// libtarscuda: the DDR image in HBM and the in-order descriptor queue executor (C-ABI).
+//
+// Replaces the execution half of the reference's golden Machine (tars_mini/golden.py:450-492):
+// descriptors run strictly in queue order; every check of a descriptor (decode, CRC, field,
+// alignment, range; overlap refusal) happens on the host before anything of it is launched; a
+// failing descriptor stops the queue with its error code and keeps the earlier descriptors'
+// writes. The arithmetic runs as sm_100a kernels on one CUDA stream, so descriptor i+1 sees
+// every write of descriptor i (RAW/WAR/WAW in queue order).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/tarscuda.h"
+#include "desc.h"
+#include "ops.h"
+
+using namespace tc;
+
+struct tc_machine {
+  int device = 0;
+  uint8_t* dev = nullptr;
+  uint64_t size = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<tc_opstat> stats;
+  std::vector<std::pair<uint64_t, uint64_t>> written;  // [lo, hi) of the last run's outputs
+  uint8_t* scratch = nullptr;
+  uint64_t scratch_size = 0;
+  std::string err;
+};
+
+// A validated queue captured as one CUDA graph (tc_queue_capture).
+struct tc_graph {
+  tc_machine* m = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  std::vector<cudaEvent_t> events;                     // before each descriptor, and one after the last
+  std::vector<tc_opstat> stats;
+  std::vector<std::pair<uint64_t, uint64_t>> written;
+  tc_status status{};
+};
+
+namespace {
+
+int fail(tc_machine* m, const char* what, cudaError_t e) {
+  if (m) m->err = std::string(what) + ": " + cudaGetErrorString(e);
+  return TC_ERR_CUDA;
+}
+
+float f32(uint64_t bits) {
+  uint32_t b = (uint32_t)bits;
+  float f;
+  std::memcpy(&f, &b, 4);
+  return f;
+}
+
+cudaError_t ensure_scratch(tc_machine* m, uint64_t n) {
+  if (n <= m->scratch_size) return cudaSuccess;
+  if (m->scratch) {
+    cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return e;
+    cudaFree(m->scratch);
+    m->scratch = nullptr;
+    m->scratch_size = 0;
+  }
+  cudaError_t e = cudaMalloc(&m->scratch, n);
+  if (e == cudaSuccess) m->scratch_size = n;
+  return e;
+}
+
+// Enqueues the kernels of one validated, in-range descriptor.
+cudaError_t launch(tc_machine* mc, const Desc& d) {
+  uint8_t* B = mc->dev + d[F_BASE_ADDR];
+  const Strides s = strides(d);
+  const int op = d.op();
+  const float osc = f32(d[F_OUT_SCALE]);
+  if (op == OP_GEMM || d.conv()) {
+    if (d.w4()) {
+      W4Args g{};
+      g.A = B + d[F_A_OFF]; g.lda = s.lda;
+      g.a_bf16 = ((d[F_CTRL] >> 4) & 15) == DT_BF16;
+      g.W = B + d[F_W_OFF]; g.scale = B + d[F_SCALE_OFF];
+      g.bias = d.bias() ? B + d[F_BIAS_OFF] : nullptr;
+      g.Y = B + d[F_Y_OFF]; g.ldy = s.ldy;
+      g.M = (int)d[F_M]; g.N = (int)d[F_N]; g.K = (int)d[F_K];
+      g.act = d.act(); g.out = d.out(); g.out_scale = osc;
+      return launch_gemm_w4a16(g, mc->stream);
+    }
+    GemmArgs g{};
+    g.A = B + d[F_A_OFF]; g.lda = s.lda;
+    if (d.conv()) {
+      const ConvGeom cg = conv_geom(d);
+      const uint64_t need = d[F_M] * d[F_K];
+      cudaError_t e = ensure_scratch(mc, need);
+      if (e != cudaSuccess) return e;
+      Im2colArgs ia{};
+      ia.img = B + d[F_A_OFF]; ia.ld = s.lda; ia.out = mc->scratch;
+      ia.H = cg.H; ia.W = cg.W; ia.KH = cg.KH; ia.KW = cg.KW; ia.S = cg.S; ia.P = cg.P;
+      ia.Cin = cg.Cin; ia.OH = cg.OH; ia.OW = cg.OW;
+      e = launch_im2col(ia, mc->stream);
+      if (e != cudaSuccess) return e;
+      g.A = mc->scratch; g.lda = d[F_K];
+    }
+    g.W = B + d[F_W_OFF]; g.scale = B + d[F_SCALE_OFF];
+    g.per_channel = d.qmode() != QM_TENSOR;
+    g.srow = (d.qmode() == QM_ROWCOL) ? mc->dev + d[F_BASE_ADDR] + 16 * d[F_HDR_RSV] : nullptr;
+    g.bias = d.bias() ? B + d[F_BIAS_OFF] : nullptr;
+    g.Y = B + d[F_Y_OFF]; g.ldy = s.ldy;
+    g.M = (int)d[F_M]; g.N = (int)d[F_N]; g.K = (int)d[F_K];
+    g.act = d.act(); g.out = d.out(); g.out_scale = osc;
+    return launch_gemm_w8a8(g, mc->stream);
+  }
+  if (op == OP_RELU) {
+    ActArgs a{};
+    a.X = B + d[F_A_OFF]; a.lda = s.lda; a.Y = B + d[F_Y_OFF]; a.ldy = s.ldy;
+    a.M = (int)d[F_M]; a.N = (int)d[F_N]; a.act = d.act(); a.out = d.out(); a.out_scale = osc;
+    return launch_act(a, mc->stream);
+  }
+  if (op == OP_ROW) {
+    RowArgs a{};
+    a.X = B + d[F_A_OFF]; a.lda = s.lda; a.Y = B + d[F_Y_OFF]; a.ldy = s.ldy;
+    a.fn = (int)(d[F_CTRL] & 7);
+    a.M = (int)d[F_M]; a.N = (int)d[F_N]; a.K = (int)d[F_K]; a.out = d.out(); a.out_scale = osc;
+    if (a.fn == ROW_QUANT) a.scale_out = B + d[F_SCALE_OFF];
+    if (a.fn == ROW_LAYERNORM || a.fn == ROW_RMSNORM || a.fn == ROW_L2NORM) {
+      a.gamma = B + d[F_SCALE_OFF];
+      a.beta = d.bias() ? B + d[F_BIAS_OFF] : nullptr;
+      a.eps = f32(d[F_W_OFF]);
+    }
+    return launch_rowop(a, mc->stream);
+  }
+  if (op == OP_ELT) {
+    EltArgs a{};
+    const uint64_t hdr = d[F_HDR_RSV];
+    a.A = B + d[F_A_OFF]; a.lda = (hdr >> 2 & 1) ? 0 : s.lda; a.a_fp16 = (hdr & STATE_FP16) != 0;
+    uint64_t ldb, brow;
+    bstride(d, &ldb, &brow);
+    a.B = B + d[F_W_OFF]; a.ldb = ldb; a.bmode = (int)(hdr & 3);
+    a.op = (int)(d[F_CTRL] & 3);
+    a.C = a.op == ELT_MULADD ? B + d[F_BIAS_OFF] : nullptr;
+    a.Y = B + d[F_Y_OFF]; a.ldy = s.ldy;
+    a.M = (int)d[F_M]; a.N = (int)d[F_N]; a.act = d.act(); a.out = d.out(); a.out_scale = osc;
+    return launch_elt(a, mc->stream);
+  }
+  if (op == OP_ROPE) {
+    RopeArgs a{};
+    a.X = B + d[F_A_OFF]; a.lda = s.lda; a.tab = B + d[F_W_OFF]; a.Y = B + d[F_Y_OFF]; a.ldy = s.ldy;
+    a.M = (int)d[F_M]; a.N = (int)d[F_N]; a.R = (int)d[F_K]; a.G = (int)d[F_GROUP_SIZE];
+    a.out = d.out(); a.out_scale = osc;
+    return launch_rope(a, mc->stream);
+  }
+  // FDOT
+  FdotArgs a{};
+  uint64_t ldb, brow;
+  bstride(d, &ldb, &brow);
+  a.A = B + d[F_A_OFF]; a.lda = s.lda; a.B = B + d[F_W_OFF]; a.ldb = ldb;
+  a.nn = (int)(d[F_CTRL] & 1); a.b_fp16 = (d[F_HDR_RSV] & STATE_FP16) != 0;
+  a.Y = B + d[F_Y_OFF]; a.ldy = s.ldy;
+  a.M = (int)d[F_M]; a.N = (int)d[F_N]; a.K = (int)d[F_K]; a.out = d.out(); a.out_scale = osc;
+  return launch_fdot(a, mc->stream);
+}
+
+bool in_range(const Footprint& fp, u128 size) {
+  for (const auto& t : fp.reads)
+    for (const auto& sg : t)
+      if (seg_end(sg) > size) return false;
+  if (seg_end(fp.y) > size) return false;
+  if (fp.has_extra && seg_end(fp.extra) > size) return false;
+  return true;
+}
+
+// golden.py:473-479: an output over an input (except the in-place ELT reads) or over the other output
+const char* illegal(const Desc& d, const Footprint& fp) {
+  for (size_t j = 0; j < fp.reads.size(); ++j)
+    for (const auto& sg : fp.reads[j]) {
+      if (overlaps(sg, fp.y) && !in_place(d, (int)j)) return "output overlaps an input";
+      if (fp.has_extra && overlaps(sg, fp.extra)) return "output overlaps an input";
+    }
+  if (fp.has_extra && overlaps(fp.extra, fp.y)) return "the two outputs overlap";
+  return nullptr;
+}
+
+uint64_t read_bytes(const Footprint& fp) {
+  u128 s = 0;
+  for (const auto& t : fp.reads)
+    for (const auto& sg : t) s += seg_bytes(sg);
+  return (uint64_t)s;
+}
+
+// The in-order loop shared by tc_run_queue and tc_queue_capture. `before(i)` runs before the
+// kernels of descriptor i are enqueued; `capturing` forbids host synchronisation (a queue that
+// rewrites its own later descriptors cannot be captured).
+template <class Before>
+int execute(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, int32_t gemv_only, tc_status* st,
+            int32_t* contract_op, const std::vector<uint8_t>& q0, bool capturing, Before before) {
+  std::vector<uint8_t> q = q0;
+  const u128 size = m->size;
+  auto fetch = [&](uint32_t from) -> cudaError_t {
+    uint64_t n_ok = 0;
+    if ((u128)qaddr + 64 * (u128)from < size) n_ok = (uint64_t)((size - qaddr) / 64);
+    n_ok = std::min<uint64_t>(n_ok, qlen);
+    if (n_ok <= from) return cudaSuccess;
+    cudaError_t e = cudaMemcpyAsync(q.data() + 64 * (size_t)from, m->dev + qaddr + 64 * (uint64_t)from,
+                                    64 * (n_ok - from), cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    return e;
+  };
+  const u128 qend = (u128)qaddr + 64 * (u128)qlen;
+  int rc = TC_OK;
+  uint32_t i = 0;
+  for (; i < qlen; ++i) {
+    const u128 qa = (u128)qaddr + 64 * (u128)i;
+    if (qa + 64 > size) { st->err_code = E_RANGE; st->op_idx = (int32_t)i; break; }
+    const uint8_t* raw = q.data() + 64 * (size_t)i;
+    Desc d;
+    decode(raw, &d);
+    int err = validate(raw, d, core_id, gemv_only);
+    Footprint fp;
+    if (err == E_OK) {
+      fp = footprint(d);
+      if (!in_range(fp, size)) err = E_RANGE;
+    }
+    if (err != E_OK) { st->err_code = err; st->op_idx = (int32_t)i; break; }
+    if (const char* why = illegal(d, fp)) {
+      *contract_op = (int32_t)i;
+      m->err = std::string("descriptor ") + std::to_string(i) + ": " + why;
+      rc = TC_CONTRACT;
+      break;
+    }
+    before(i);
+    cudaError_t e = launch(m, d);
+    if (e != cudaSuccess) { rc = fail(m, "launch", e); break; }
+    const int op = d.op();
+    const uint64_t macs = (op == OP_GEMM || op == OP_FDOT || d.conv()) ? d[F_M] * d[F_N] * d[F_K] : 0;
+    const Strides s = strides(d);
+    m->stats.push_back(tc_opstat{(uint64_t)op, macs, read_bytes(fp), d[F_M] * s.yrow});
+    const u128 ylo = fp.y.base, yhi = seg_end(fp.y);
+    m->written.push_back({(uint64_t)ylo, (uint64_t)yhi});
+    u128 xlo = 0, xhi = 0;
+    if (fp.has_extra) {
+      xlo = fp.extra.base; xhi = seg_end(fp.extra);
+      m->written.push_back({(uint64_t)xlo, (uint64_t)xhi});
+    }
+    // a descriptor that rewrites later descriptors of this queue: read them again
+    const u128 rest = qa + 64;
+    if (i + 1 < qlen && ((ylo < qend && yhi > rest) || (fp.has_extra && xlo < qend && xhi > rest))) {
+      if (capturing) { m->err = "the queue rewrites its own descriptors: not capturable"; rc = TC_ERR_ARG; break; }
+      e = fetch(i + 1);
+      if (e != cudaSuccess) { rc = fail(m, "queue refetch", e); break; }
+    }
+  }
+  if (rc == TC_OK && i == qlen) { st->done = 1; st->err_code = E_OK; st->op_idx = (int32_t)qlen; }
+  return rc;
+}
+
+cudaError_t fetch_queue(tc_machine* m, uint64_t qaddr, uint32_t qlen, std::vector<uint8_t>& q) {
+  q.assign((size_t)qlen * 64, 0);
+  uint64_t n_ok = 0;
+  if ((u128)qaddr < (u128)m->size) n_ok = std::min<uint64_t>((m->size - qaddr) / 64, qlen);
+  if (!n_ok) return cudaSuccess;
+  cudaError_t e = cudaMemcpyAsync(q.data(), m->dev + qaddr, 64 * n_ok, cudaMemcpyDeviceToHost, m->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+  return e;
+}
+
+// The conv scratch a queue needs (so capture never allocates).
+uint64_t scratch_need(const std::vector<uint8_t>& q, uint32_t qlen, int core_id, int gemv_only) {
+  uint64_t need = 0;
+  for (uint32_t i = 0; i < qlen; ++i) {
+    const uint8_t* raw = q.data() + 64 * (size_t)i;
+    Desc d;
+    decode(raw, &d);
+    if (d.conv() && validate(raw, d, core_id, gemv_only) == E_OK) need = std::max<uint64_t>(need, d[F_M] * d[F_K]);
+  }
+  return need;
+}
+}  // namespace
+
+extern "C" {
+
+int tc_run_queue(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, int32_t gemv_only,
+                 tc_status* st, int32_t* contract_op) {
+  cudaSetDevice(m->device);
+  m->stats.clear();
+  m->written.clear();
+  m->err.clear();
+  st->done = 0; st->err_code = E_OK; st->op_idx = 0;
+  *contract_op = -1;
+  std::vector<uint8_t> q;
+  cudaError_t e = fetch_queue(m, qaddr, qlen, q);
+  if (e != cudaSuccess) return fail(m, "queue fetch", e);
+  int rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, false, [](uint32_t) {});
+  cudaError_t se = cudaStreamSynchronize(m->stream);
+  if (se != cudaSuccess && rc >= 0) rc = fail(m, "queue run", se);
+  return rc;
+}
+
+int tc_queue_capture(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, int32_t gemv_only,
+                     int32_t timing, tc_status* st, int32_t* contract_op, tc_graph** out) {
+  *out = nullptr;
+  cudaSetDevice(m->device);
+  m->stats.clear();
+  m->written.clear();
+  m->err.clear();
+  st->done = 0; st->err_code = E_OK; st->op_idx = 0;
+  *contract_op = -1;
+  std::vector<uint8_t> q;
+  cudaError_t e = fetch_queue(m, qaddr, qlen, q);
+  if (e == cudaSuccess) e = ensure_scratch(m, scratch_need(q, qlen, core_id, gemv_only));
+  if (e != cudaSuccess) return fail(m, "capture setup", e);
+  tc_graph* g = new tc_graph();
+  g->m = m;
+  if (timing) {
+    g->events.resize((size_t)qlen + 1);
+    for (auto& ev : g->events) cudaEventCreate(&ev);
+  }
+  e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeRelaxed);
+  if (e != cudaSuccess) { delete g; return fail(m, "begin capture", e); }
+  uint32_t last = 0;
+  int rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, true, [&](uint32_t i) {
+    if (timing) cudaEventRecord(g->events[i], m->stream);
+    last = i + 1;
+  });
+  if (timing && last) cudaEventRecord(g->events[last], m->stream);
+  cudaGraph_t graph = nullptr;
+  cudaError_t ce = cudaStreamEndCapture(m->stream, &graph);
+  if (rc == TC_OK && ce != cudaSuccess) rc = fail(m, "end capture", ce);
+  if (rc == TC_OK) {
+    ce = cudaGraphInstantiate(&g->exec, graph, 0);
+    if (ce != cudaSuccess) rc = fail(m, "instantiate", ce);
+  }
+  if (graph) cudaGraphDestroy(graph);
+  if (rc != TC_OK) {
+    for (auto& ev : g->events) cudaEventDestroy(ev);
+    if (g->exec) cudaGraphExecDestroy(g->exec);
+    delete g;
+    return rc;
+  }
+  if (timing) g->events.resize(last + (last ? 1 : 0));
+  g->stats = m->stats;
+  g->written = m->written;
+  g->status = *st;
+  *out = g;
+  return TC_OK;
+}
+
+int tc_graph_launch(tc_graph* g, void* stream) {
+  tc_machine* m = g->m;
+  cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+  cudaError_t e = cudaGraphLaunch(g->exec, s);
+  if (e != cudaSuccess) return fail(m, "graph launch", e);
+  m->stats = g->stats;
+  m->written = g->written;
+  return TC_OK;
+}
+
+int tc_graph_times(tc_graph* g, float* ms, uint32_t cap) {
+  if (g->events.size() < 2) return 0;
+  const uint32_t n = (uint32_t)g->events.size() - 1;
+  for (uint32_t i = 0; i < std::min(cap, n); ++i) {
+    cudaError_t e = cudaEventElapsedTime(&ms[i], g->events[i], g->events[i + 1]);
+    if (e != cudaSuccess) return fail(g->m, "event time", e);
+  }
+  return (int)n;
+}
+
+int tc_graph_destroy(tc_graph* g) {
+  if (!g) return TC_OK;
+  cudaSetDevice(g->m->device);
+  for (auto& ev : g->events) cudaEventDestroy(ev);
+  if (g->exec) cudaGraphExecDestroy(g->exec);
+  delete g;
+  return TC_OK;
+}
+
+int tc_synchronize(tc_machine* m) {
+  cudaSetDevice(m->device);
+  cudaError_t e = cudaStreamSynchronize(m->stream);
+  return e == cudaSuccess ? TC_OK : fail(m, "synchronize", e);
+}
+
+
+int tc_version(void) { return TC_ABI_VERSION; }
+
+int tc_open(int device, uint64_t ddr_bytes, tc_machine** out) {
+  *out = nullptr;
+  tc_machine* m = new tc_machine();
+  m->device = device;
+  m->size = ddr_bytes;
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&m->dev, std::max<uint64_t>(ddr_bytes, 256));
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->dev, 0, std::max<uint64_t>(ddr_bytes, 256), m->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+  if (e != cudaSuccess) {
+    if (m->dev) cudaFree(m->dev);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+    return TC_ERR_CUDA;
+  }
+  *out = m;
+  return TC_OK;
+}
+
+int tc_close(tc_machine* m) {
+  if (!m) return TC_OK;
+  cudaSetDevice(m->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  if (m->scratch) cudaFree(m->scratch);
+  if (m->dev) cudaFree(m->dev);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+  return TC_OK;
+}
+
+const char* tc_last_error(tc_machine* m) { return m ? m->err.c_str() : ""; }
+
+uint64_t tc_device_ptr(tc_machine* m) { return (uint64_t)(uintptr_t)m->dev; }
+void* tc_stream(tc_machine* m) { return (void*)m->stream; }
+
+int tc_upload(tc_machine* m, uint64_t addr, const void* src, uint64_t n) {
+  if (addr > m->size || n > m->size - addr) { m->err = "upload out of range"; return TC_ERR_ARG; }
+  cudaSetDevice(m->device);
+  cudaError_t e = cudaMemcpyAsync(m->dev + addr, src, n, cudaMemcpyHostToDevice, m->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+  return e == cudaSuccess ? TC_OK : fail(m, "upload", e);
+}
+
+int tc_download(tc_machine* m, uint64_t addr, void* dst, uint64_t n) {
+  if (addr > m->size || n > m->size - addr) { m->err = "download out of range"; return TC_ERR_ARG; }
+  cudaSetDevice(m->device);
+  cudaError_t e = cudaMemcpyAsync(dst, m->dev + addr, n, cudaMemcpyDeviceToHost, m->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+  return e == cudaSuccess ? TC_OK : fail(m, "download", e);
+}
+
+int tc_sync_up(tc_machine* m, const void* host, void* shadow, uint64_t n, uint64_t* uploaded) {
+  if (n != m->size) { m->err = "image size mismatch"; return TC_ERR_ARG; }
+  const uint8_t* h = (const uint8_t*)host;
+  uint8_t* s = (uint8_t*)shadow;
+  const uint64_t blk = 1 << 16;
+  const uint64_t nblk = (n + blk - 1) / blk;
+  std::vector<uint8_t> dirty(nblk, 0);
+  const unsigned nt = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  auto work = [&](unsigned t) {
+    for (uint64_t b = t; b < nblk; b += nt) {
+      const uint64_t lo = b * blk, len = std::min(blk, n - lo);
+      if (std::memcmp(h + lo, s + lo, len) != 0) {
+        dirty[b] = 1;
+        std::memcpy(s + lo, h + lo, len);
+      }
+    }
+  };
+  if (n >= (32u << 20) && nt > 1) {
+    std::vector<std::thread> th;
+    for (unsigned t = 0; t < nt; ++t) th.emplace_back(work, t);
+    for (auto& t : th) t.join();
+  } else {
+    work(0);
+    for (unsigned t = 1; t < nt; ++t) work(t);
+  }
+  cudaSetDevice(m->device);
+  uint64_t total = 0;
+  for (uint64_t b = 0; b < nblk;) {
+    if (!dirty[b]) { ++b; continue; }
+    uint64_t e = b;
+    while (e < nblk && dirty[e]) ++e;
+    const uint64_t lo = b * blk, hi = std::min(n, e * blk);
+    cudaError_t err = cudaMemcpyAsync(m->dev + lo, s + lo, hi - lo, cudaMemcpyHostToDevice, m->stream);
+    if (err != cudaSuccess) return fail(m, "sync_up", err);
+    total += hi - lo;
+    b = e;
+  }
+  cudaError_t err = cudaStreamSynchronize(m->stream);
+  if (err != cudaSuccess) return fail(m, "sync_up", err);
+  if (uploaded) *uploaded = total;
+  return TC_OK;
+}
+
+int tc_sync_down(tc_machine* m, void* host, void* shadow) {
+  cudaSetDevice(m->device);
+  auto& w = m->written;
+  std::sort(w.begin(), w.end());
+  std::vector<std::pair<uint64_t, uint64_t>> merged;
+  for (auto& r : w) {
+    if (!merged.empty() && r.first <= merged.back().second) merged.back().second = std::max(merged.back().second, r.second);
+    else merged.push_back(r);
+  }
+  uint8_t* h = (uint8_t*)host;
+  for (auto& r : merged) {
+    cudaError_t e = cudaMemcpyAsync(h + r.first, m->dev + r.first, r.second - r.first, cudaMemcpyDeviceToHost, m->stream);
+    if (e != cudaSuccess) return fail(m, "sync_down", e);
+  }
+  cudaError_t e = cudaStreamSynchronize(m->stream);
+  if (e != cudaSuccess) return fail(m, "sync_down", e);
+  if (shadow)
+    for (auto& r : merged) std::memcpy((uint8_t*)shadow + r.first, h + r.first, r.second - r.first);
+  w.clear();
+  return TC_OK;
+}
+
+int tc_validate(const uint8_t* raw, int32_t core_id, int32_t gemv_only, uint64_t* fields) {
+  Desc d;
+  decode(raw, &d);
+  if (fields) std::memcpy(fields, d.f, sizeof(d.f));
+  return validate(raw, d, core_id, gemv_only);
+}
+
+int tc_footprint(const uint8_t* raw, tc_seg* out, uint32_t cap, uint32_t* count) {
+  Desc d;
+  decode(raw, &d);
+  Footprint fp = footprint(d);
+  std::vector<tc_seg> v;
+  auto put = [&](int kind, const Seg& s) {
+    tc_seg t;
+    t.kind = kind;
+    t.base_lo = (uint64_t)s.base;
+    t.base_hi = (uint64_t)(s.base >> 64);
+    t.ld = (uint64_t)s.ld;
+    t.nbytes = (uint64_t)s.nbytes;
+    t.count = (uint64_t)s.count;
+    v.push_back(t);
+  };
+  for (size_t j = 0; j < fp.reads.size(); ++j)
+    for (auto& s : fp.reads[j]) put((int)j, s);
+  put(-1, fp.y);
+  if (fp.has_extra) put(-2, fp.extra);
+  *count = (uint32_t)v.size();
+  for (uint32_t i = 0; i < std::min<uint32_t>(cap, *count); ++i) out[i] = v[i];
+  return TC_OK;
+}
+
+uint32_t tc_stats(tc_machine* m, tc_opstat* out, uint32_t cap) {
+  const uint32_t n = (uint32_t)m->stats.size();
+  for (uint32_t i = 0; i < std::min(cap, n); ++i) out[i] = m->stats[i];
+  return n;
+}
+
+}  // extern "C"

@@ -1,0 +1,101 @@
+// Kernel launch interfaces of libtarscuda (device pointers + sizes; no torch types).
+//
+// Each launcher enqueues the work of one descriptor (or of one fused engine step) on `st`.
+// Pointers are device addresses inside the HBM copy of the DDR image unless noted.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "codes.h"
+
+namespace tc {
+
+// W8A8 GEMM / GEMV, golden.py:326-349 (and the conv's implicit GEMM, golden.py:282-293)
+struct GemmArgs {
+  const uint8_t* A;  uint64_t lda;   // int8 [M, K] rows
+  const uint8_t* W;                  // int8 [N, K] dense
+  const uint8_t* scale;              // fp32 [N] (per channel) or [1] (per tensor)
+  int per_channel;
+  const uint8_t* srow;               // fp32 [M] row scales (QM_ROWCOL) or nullptr
+  const uint8_t* bias;               // fp32 [N] or nullptr
+  uint8_t* Y;  uint64_t ldy;
+  int M, N, K, act, out;
+  float out_scale;
+};
+cudaError_t launch_gemm_w8a8(const GemmArgs& g, cudaStream_t st);
+
+// W4A16 GEMM / GEMV, golden.py:295-324
+struct W4Args {
+  const uint8_t* A;  uint64_t lda;   // fp32 or bf16 [M, K] rows
+  int a_bf16;
+  const uint8_t* W;                  // packed int4 [N, K/2] (low nibble = even k)
+  const uint8_t* scale;              // fp16 bits [N, K/128]
+  const uint8_t* bias;               // fp32 [N] or nullptr
+  uint8_t* Y;  uint64_t ldy;
+  int M, N, K, act, out;
+  float out_scale;
+};
+cudaError_t launch_gemm_w4a16(const W4Args& g, cudaStream_t st);
+
+// conv: the NHWC int8 image gathered into [OH*OW, KH*KW*Cin] rows (zero padding), golden.py:282-293
+struct Im2colArgs {
+  const uint8_t* img;  uint64_t ld;  // H*W pixel rows of Cin bytes, row stride ld
+  uint8_t* out;                      // [OH*OW, K] dense
+  int H, W, KH, KW, S, P, Cin, OH, OW;
+};
+cudaError_t launch_im2col(const Im2colArgs& a, cudaStream_t st);
+
+// Row ops (OPCODE 0x04), golden.py:358-380 and the RELU op (0x03), golden.py:351-356
+struct RowArgs {
+  const uint8_t* X;  uint64_t lda;   // fp32 [M, N]
+  uint8_t* Y;  uint64_t ldy;
+  const uint8_t* gamma;              // fp32 [N] (norms)
+  const uint8_t* beta;               // fp32 [N] or nullptr
+  uint8_t* scale_out;                // ROW_QUANT: fp32 [M]
+  int M, N, fn, out, K;              // K: causal softmax start (0 = plain)
+  float eps, out_scale;
+};
+cudaError_t launch_rowop(const RowArgs& a, cudaStream_t st);
+
+struct ActArgs {
+  const uint8_t* X;  uint64_t lda;
+  uint8_t* Y;  uint64_t ldy;
+  int M, N, act, out;
+  float out_scale;
+};
+cudaError_t launch_act(const ActArgs& a, cudaStream_t st);
+
+// ELT (0x06), golden.py:393-418
+struct EltArgs {
+  const uint8_t* A;  uint64_t lda;   // lda = 0: one row broadcast
+  int a_fp16;
+  const uint8_t* B;  uint64_t ldb;  int bmode;
+  const uint8_t* C;                  // MULADD addend (output format, stride ldy) or nullptr
+  uint8_t* Y;  uint64_t ldy;
+  int M, N, op, act, out;
+  float out_scale;
+};
+cudaError_t launch_elt(const EltArgs& a, cudaStream_t st);
+
+// ROPE (0x07), golden.py:420-424
+struct RopeArgs {
+  const uint8_t* X;  uint64_t lda;
+  const uint8_t* tab;                // fp32 [rows, R]: cos[0:R/2], sin[0:R/2]
+  uint8_t* Y;  uint64_t ldy;
+  int M, N, R, G, out;
+  float out_scale;
+};
+cudaError_t launch_rope(const RopeArgs& a, cudaStream_t st);
+
+// FDOT (0x08), golden.py:426-435
+struct FdotArgs {
+  const uint8_t* A;  uint64_t lda;   // fp32 [M, K]
+  const uint8_t* B;  uint64_t ldb;   // NT: fp32 [N, K]; NN: fp32 or fp16 [K, N]
+  int nn, b_fp16;
+  uint8_t* Y;  uint64_t ldy;
+  int M, N, K, out;
+  float out_scale;
+};
+cudaError_t launch_fdot(const FdotArgs& a, cudaStream_t st);
+
+}  // namespace tc
