@@ -1,0 +1,388 @@
+#!/usr/bin/env python
+"""Benchmark of the tars_mini hot path on B200s (one JSON line from rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemv|w4] [--impl ours|reference]
+
+Workloads (synthetic seeded data with the configs' distributions):
+  gemv  config 0: one unit = ROW_QUANT of x [1, 1024] + W8A8 GEMV (QM_ROWCOL) against W [3072, 1024];
+        a step runs R units on R distinct weight copies (R * 3 MiB > the 126 MB L2)
+  w4    config 2: one unit = W4A16 GEMV, M=1, K=8192, N=16384 (64 MiB of packed weights);
+        a step runs R units on distinct weight copies
+value: algorithmic bytes of all units of all ranks / device time of the timed steps (max over
+ranks), in GB/s. e2e: the same metric through the board-runtime API (opentars_b200.board.Cuda:
+host writes x into pinned memory, to_dev, run, from_dev of y) timed on the host clock.
+--impl reference: the reference's numpy golden path restated in oracle/ (the reference itself is
+Python and cannot travel), on all host cores, over a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = json.loads((ROOT / "BASELINE.json").read_text())["metric"] if (ROOT / "BASELINE.json").exists() else \
+    "W8A8/W4A16 GEMV HBM GB/s vs peak; Qwen3-0.6B-shape decode tok/s, bit-exact"
+QA_ALIGN = 128
+
+
+# ----------------------------------------------------------------------------- programs
+def _desc(**f):
+    from opentars_b200 import contract as C
+    return C.encode(dict(MAGIC=C.MAGIC, VERSION=C.VERSION, VALID=1, **f))
+
+
+def _align(x, a=QA_ALIGN):
+    return -(-x // a) * a
+
+
+def build_gemv(R: int, seed: int, M: int = 1, K: int = 1024, N: int = 3072):
+    """R independent config-0 GEMVs (quant + GEMM) in one image; returns the program and layout."""
+    from opentars_b200 import contract as C
+    rng = np.random.default_rng(seed)
+    w0 = 0x1000
+    s0 = _align(w0 + R * N * K)
+    x0 = _align(s0 + R * 4 * N)
+    q0 = _align(x0 + R * 4 * M * K)
+    r0 = _align(q0 + R * M * K)
+    y0 = _align(r0 + R * 16)
+    qa = _align(y0 + R * 4 * M * N)
+    size = _align(qa + 64 * 2 * R + 4096, 1 << 16)
+    ddr = np.zeros(size, np.uint8)
+    for r in range(R):
+        ddr[w0 + r * N * K:w0 + (r + 1) * N * K] = rng.integers(-127, 128, N * K, dtype=np.int8).view(np.uint8)
+    ddr[s0:s0 + R * 4 * N] = rng.uniform(1e-3, 1e-2, R * N).astype("<f4").view(np.uint8)
+    ddr[x0:x0 + R * 4 * M * K] = rng.normal(0, 1, R * M * K).astype("<f4").view(np.uint8)
+    for r in range(R):
+        q, sr = q0 + r * M * K, r0 + r * 16
+        d0 = _desc(OPCODE=C.OP_ROW, CTRL=C.ROW_QUANT, EPI=C.epi(C.ACT_NONE, C.OUT_INT8),
+                   A_OFF=x0 + r * 4 * M * K, Y_OFF=q, SCALE_OFF=sr, M=M, N=K)
+        d1 = _desc(OPCODE=C.OP_GEMM, CTRL=C.ctrl(C.QM_ROWCOL), EPI=C.epi(), A_OFF=q, W_OFF=w0 + r * N * K,
+                   SCALE_OFF=s0 + r * 4 * N, Y_OFF=y0 + r * 4 * M * N, M=M, N=N, K=K, HDR_RSV=sr // 16)
+        ddr[qa + 128 * r:qa + 128 * r + 64] = np.frombuffer(d0, np.uint8)
+        ddr[qa + 128 * r + 64:qa + 128 * (r + 1)] = np.frombuffer(d1, np.uint8)
+    gemm_bytes = N * K + 4 * N + M * K + 4 * M + 4 * M * N          # 3,171,332 at config 0
+    quant_bytes = 4 * M * K + M * K + 4 * M
+    return dict(ddr=ddr, qa=qa, qlen=2 * R, units=R, unit_bytes=gemm_bytes + quant_bytes,
+                kernel_bytes=gemm_bytes, kernel_desc=lambda i: i % 2 == 1, kernel="k_gemv_i8 (W8A8 GEMV)",
+                inputs=(x0, R * 4 * M * K), outputs=(y0, R * 4 * M * N),
+                config=dict(workload="config0_w8a8_gemv", M=M, K=K, N=N, units_per_step=R,
+                            weights_bytes_per_step=R * N * K,
+                            l2="inputs larger than L2: each step streams R distinct weight copies"))
+
+
+def build_w4(R: int, seed: int, M: int = 1, K: int = 8192, N: int = 16384):
+    from opentars_b200 import contract as C
+    rng = np.random.default_rng(seed)
+    G = K // 128
+    w0 = 0x1000
+    s0 = _align(w0 + R * N * K // 2)
+    x0 = _align(s0 + R * 2 * N * G)
+    y0 = _align(x0 + R * 4 * M * K)
+    qa = _align(y0 + R * 4 * M * N)
+    size = _align(qa + 64 * R + 4096, 1 << 16)
+    ddr = np.zeros(size, np.uint8)
+    for r in range(R):
+        ddr[w0 + r * N * K // 2:w0 + (r + 1) * N * K // 2] = rng.integers(0, 256, N * K // 2, dtype=np.uint8)
+    ddr[s0:s0 + R * 2 * N * G] = rng.uniform(1e-3, 2e-2, R * N * G).astype("<f2").view(np.uint8)
+    ddr[x0:x0 + R * 4 * M * K] = rng.normal(0, 1, R * M * K).astype("<f4").view(np.uint8)
+    for r in range(R):
+        d = _desc(OPCODE=C.OP_GEMM, CTRL=C.ctrl(C.QM_GROUP, a_dtype=C.DT_FP32, w_dtype=C.DT_INT4), EPI=C.epi(),
+                  A_OFF=x0 + r * 4 * M * K, W_OFF=w0 + r * N * K // 2, SCALE_OFF=s0 + r * 2 * N * G,
+                  Y_OFF=y0 + r * 4 * M * N, M=M, N=N, K=K, GROUP_SIZE=128)
+        ddr[qa + 64 * r:qa + 64 * (r + 1)] = np.frombuffer(d, np.uint8)
+    unit = N * K // 2 + 2 * N * G + 4 * M * K + 4 * M * N               # 69,304,320 here
+    return dict(ddr=ddr, qa=qa, qlen=R, units=R, unit_bytes=unit, kernel_bytes=unit, kernel_desc=lambda i: True,
+                kernel="k_gemv_w4 (W4A16 GEMV)", inputs=(x0, R * 4 * M * K), outputs=(y0, R * 4 * M * N),
+                config=dict(workload="config2_w4a16_gemv", M=M, K=K, N=N, units_per_step=R,
+                            weights_bytes_per_step=R * N * K // 2,
+                            l2="inputs larger than L2: each step streams R distinct weight copies"))
+
+
+WORKLOADS = {"gemv": (build_gemv, 64), "w4": (build_w4, 4)}
+
+
+# ----------------------------------------------------------------------------- clocks (NVML)
+class Clocks:
+    """Samples SM clock and throttle reasons of one GPU every 5 ms while running."""
+
+    def __init__(self, index: int):
+        self.index, self.samples, self.reasons, self.max_mhz = index, [], set(), None
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        try:
+            import pynvml as N
+            N.nvmlInit()
+            h = N.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+            names = {getattr(N, k): k for k in dir(N) if k.startswith("nvmlClocksEventReason")
+                     and k not in ("nvmlClocksEventReasonAll", "nvmlClocksEventReasonNone")}
+
+            def loop():
+                while not self._stop.is_set():
+                    self.samples.append(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM))
+                    r = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for bit, name in names.items():
+                        if isinstance(bit, int) and r & bit:
+                            self.reasons.add(name.replace("nvmlClocksEventReason", ""))
+                    time.sleep(0.005)
+            self._t = threading.Thread(target=loop, daemon=True)
+            self._t.start()
+        except Exception as e:                      # no NVML: report that instead of numbers
+            self.error = str(e)
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "note": getattr(self, "error", "no samples")}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- CPU oracle timing
+def _oracle_unit_worker(args):
+    """Runs the oracle on one-unit images for `seconds`; returns (units, elapsed)."""
+    workload, seed, seconds = args
+    sys.path.insert(0, str(ROOT))
+    from oracle.machine import OracleMachine
+    p = WORKLOADS[workload][0](1, seed)
+    ddr = bytearray(p["ddr"].tobytes())
+    n, t0 = 0, time.perf_counter()
+    while True:
+        m = OracleMachine(bytearray(ddr))
+        assert m.run_queue(p["qa"], p["qlen"]).done
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    return n, time.perf_counter() - t0
+
+
+def cpu_oracle_gbs(workload: str, seconds: float, procs: int) -> dict:
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    unit_bytes = WORKLOADS[workload][0](1, 0)["unit_bytes"]
+    t0 = time.perf_counter()
+    with ctx.Pool(procs) as pool:
+        res = pool.map(_oracle_unit_worker, [(workload, 100 + i, seconds) for i in range(procs)])
+    wall = time.perf_counter() - t0
+    units = sum(n for n, _ in res)
+    span = max(t for _, t in res)
+    return dict(value=units * unit_bytes / span / 1e9, unit="GB/s", cores=procs, kind="port",
+                sample=f"{units} units of {workload} (one per image) on {procs} processes, {span:.1f}s each",
+                wall_s=round(wall, 1))
+
+
+# ----------------------------------------------------------------------------- distributed plumbing
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(a, world, rank, local) -> dict | None:
+    import ctypes
+
+    import torch
+    os.environ["TC_DEVICE"] = str(local)
+    torch.cuda.set_device(local)
+    from opentars_b200._lib import check, lib
+    from opentars_b200.board import Cuda
+    build, R = WORKLOADS[a.workload]
+    R = a.units or R
+    p = build(R, seed=1234 + rank)
+    L = lib()
+    ddr = p["ddr"]
+    dev = Cuda(len(ddr), device=local, pinned=True)
+    dev.mem[:] = ddr
+    dev.to_dev(0, len(ddr))
+    g, st = dev.graph(p["qa"], p["qlen"])
+    assert g is not None and st.done, "the benchmark queue must capture"
+    stream = torch.cuda.ExternalStream(L.tc_stream(dev.h), device=local)
+
+    # parity spot check: unit 0 against the oracle happens after timing (rank 0)
+    for _ in range(a.warmup):
+        check(L.tc_graph_launch(g, None), dev.h)
+    check(L.tc_synchronize(dev.h), dev.h)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(stream)
+        for _ in range(a.steps):
+            check(L.tc_graph_launch(g, None), dev.h)
+        e1.record(stream)
+        check(L.tc_synchronize(dev.h), dev.h)
+    ms = e0.elapsed_time(e1)
+    barrier(world)
+    ms_max = max_over_ranks(ms, world)
+    total_bytes = world * R * p["unit_bytes"] * a.steps
+    value = total_bytes / (ms_max / 1e3) / 1e9
+
+    # roofline: per-descriptor device times from a graph captured with events between descriptors
+    from opentars_b200._lib import Status_t
+    st2, cop, gt = Status_t(), ctypes.c_int32(-1), ctypes.c_void_p()
+    check(L.tc_queue_capture(dev.h, p["qa"], p["qlen"], 0, 0, 1, ctypes.byref(st2), ctypes.byref(cop),
+                             ctypes.byref(gt)), dev.h)
+    kt = []
+    for _ in range(3):
+        check(L.tc_graph_launch(gt, None), dev.h)
+        check(L.tc_synchronize(dev.h), dev.h)
+        arr = (ctypes.c_float * p["qlen"])()
+        n = L.tc_graph_times(gt, arr, p["qlen"])
+        kt += [arr[i] for i in range(n) if p["kernel_desc"](i)]
+    L.tc_graph_destroy(gt)
+    k_ms = statistics.mean(kt)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = p["kernel_bytes"] / (k_ms / 1e3) / 1e9
+    traffic_file = ROOT / "profiles" / f"traffic_{a.workload}.json"
+    traffic = json.loads(traffic_file.read_text()).get("bytes_per_launch") if traffic_file.exists() else None
+    roofline = dict(bound="hbm", achieved=round(achieved, 1), peak=peak, unit="GB/s", frac=round(achieved / peak, 4),
+                    traffic=traffic, kernel=p["kernel"], kernel_bytes_per_launch=p["kernel_bytes"],
+                    kernel_us=round(k_ms * 1e3, 3), peak_source="measured" if peaks else "fallback")
+
+    # e2e through the board API with host (pinned) buffers, host clock
+    x0, xn = p["inputs"]
+    y0, yn = p["outputs"]
+    rng = np.random.default_rng(7 + rank)
+    xs = [rng.normal(0, 1, xn // 4).astype("<f4").view(np.uint8) for _ in range(4)]
+    for i in range(2):
+        dev.mem[x0:x0 + xn] = xs[i % 4]
+        dev.to_dev(x0, xn)
+        dev.run(p["qa"], p["qlen"])
+        dev.from_dev(y0, yn)
+    barrier(world)
+    t0 = time.perf_counter()
+    for i in range(a.steps):
+        dev.mem[x0:x0 + xn] = xs[i % 4]
+        dev.to_dev(x0, xn)
+        dev.run(p["qa"], p["qlen"])
+        dev.from_dev(y0, yn)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e = dict(value=round(total_bytes / e2e_s / 1e9, 2), unit="GB/s", h2d_bytes_per_step=xn, d2h_bytes_per_step=yn,
+               api="opentars_b200.board.Cuda: mem write, to_dev, run (cached graph), from_dev")
+
+    # parity: unit 0's output of the last run against the oracle
+    bit_exact = None
+    if rank == 0:
+        from oracle.machine import OracleMachine
+        # unit 0 of the benchmark image with the last e2e input
+        dev.from_dev(0, len(ddr))
+        img = dev.mem.copy()
+        o = OracleMachine(bytearray(img.tobytes()))
+        qa = p["qa"]
+        o.run_queue(qa, 2 if a.workload == "gemv" else 1)
+        bit_exact = bytes(o.ddr[y0:y0 + yn // R]) == img[y0:y0 + yn // R].tobytes()
+    dev.close()
+    if rank != 0:
+        return None
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(ms_max / a.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8" if a.workload == "gemv" else "int4xint16",
+        "data": "synthetic, seeded (BASELINE config distributions)",
+        "config": dict(p["config"], parallelism=f"replicas x{world} (independent GEMV batches per GPU)"),
+        "roofline": roofline, "e2e": e2e,
+        "gpu_launches": a.steps * p["qlen"], "clocks": clk.summary(), "bit_exact_unit0": bit_exact,
+    }
+    if world == 1 and not a.no_cpu:
+        cb = cpu_oracle_gbs(a.workload, a.cpu_seconds, os.cpu_count() or 1)
+        out["cpu_baseline"] = cb
+    return out
+
+
+# ----------------------------------------------------------------------------- the reference arm
+def run_reference(a, world, rank) -> dict | None:
+    if rank != 0:
+        return None
+    procs = os.cpu_count() or 1
+    for _ in range(a.warmup):
+        cpu_oracle_gbs(a.workload, 0.5, procs)
+    vals = [cpu_oracle_gbs(a.workload, a.ref_seconds, procs) for _ in range(a.steps)]
+    v = statistics.mean(x["value"] for x in vals)
+    build, R = WORKLOADS[a.workload]
+    cfg = build(1, 0)["config"]
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8" if a.workload == "gemv" else "int4xint16", "data": "synthetic, seeded",
+        "config": dict(cfg, units_per_step="bounded CPU sample"),
+        "cpu_baseline": dict(value=round(v, 4), unit="GB/s", cores=procs, kind="port",
+                             sample=vals[-1]["sample"]),
+        "e2e": dict(value=round(v, 4), unit="GB/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+        "note": "the reference is Python (numpy golden model); its restatement in oracle/ is timed here",
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="gemv", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--units", type=int, default=0)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-seconds", type=float, default=3.0)
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+    if a.impl == "reference":                       # CPU only: no process group, no GPU
+        world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+        out = run_reference(a, world, rank)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+    world, rank, local = dist_setup(a.gpus)
+    out = run_ours(a, world, rank, local)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -28,10 +28,15 @@ class Cuda:
     params = dict(backend="cuda (B200, libtarscuda)")
 
     def __init__(self, mem: int = 1 << 30, device: int | None = None, graphs: bool = True,
-                 core_id: int = 0, gemv_only: bool = False):
+                 core_id: int = 0, gemv_only: bool = False, pinned: bool = False):
         self.device = default_device() if device is None else device
         self.n = int(mem)
-        self.buf = np.zeros(self.n, np.uint8)
+        if pinned:                                   # page-locked host memory: direct DMA both ways
+            import torch
+            self._pinned = torch.zeros(self.n, dtype=torch.uint8, pin_memory=True)
+            self.buf = self._pinned.numpy()
+        else:
+            self.buf = np.zeros(self.n, np.uint8)
         self.mem = self.buf
         self.core_id, self.gemv_only, self.graphs = core_id, gemv_only, graphs
         h = ctypes.c_void_p()
