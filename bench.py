@@ -270,8 +270,10 @@ def run_ours(a, world, rank, local) -> dict | None:
         check(L.tc_graph_launch(gt, None), dev.h)
         check(L.tc_synchronize(dev.h), dev.h)
         arr = (ctypes.c_float * p["qlen"])()
-        n = L.tc_graph_times(gt, arr, p["qlen"])
+        n = check(L.tc_graph_times(gt, arr, p["qlen"]), dev.h, "graph_times")
         kt += [arr[i] for i in range(n) if p["kernel_desc"](i)]
+    if not kt:
+        raise RuntimeError("no per-descriptor timings")
     L.tc_graph_destroy(gt)
     k_ms = statistics.mean(kt)
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}

@@ -3,10 +3,10 @@
 // Each function restates one function of the reference's tars_mini/numerics.py (cited per
 // function). Contract: one round-to-nearest-even per step, operands and results flushed to a
 // signed zero when denormal, no fused multiply-add, every NaN a step produces is 0x7FC00000.
-// The library is compiled with -ftz=false -fmad=false; the steps use __fmul_rn / __fadd_rn
-// (IEEE with gradual underflow, never contracted) and flush explicitly afterwards, which is what
-// numpy's float32 arithmetic followed by the reference's ftz() computes, including results that
-// round up to the smallest normal. exp/recip/rsqrt are the contract's own published sequences
+// The library is compiled with -ftz=false -fmad=false: products use __fmul_rn (IEEE with gradual
+// underflow, never contracted) and are flushed explicitly afterwards, which is what numpy's
+// float32 multiply followed by the reference's ftz() computes, including products that round up
+// to the smallest normal; sums use the hardware's flush-to-zero add, exact for sums (see fadd). exp/recip/rsqrt are the contract's own published sequences
 // (magic-constant seeds, Newton steps in correction form, a degree-6 Horner polynomial); CUDA's
 // math library is not used for them.
 #pragma once
@@ -26,9 +26,18 @@ __device__ __forceinline__ float ftz(float x) {
 }
 // numerics.py:34-37
 __device__ __forceinline__ float canon(float x) { return is_nan(x) ? bf(0x7FC00000u) : x; }
-// numerics.py:40-47
+// numerics.py:40-47. fmul: IEEE product with gradual underflow, then the flush (a product just
+// below 2^-126 may round up to the smallest normal, so the hardware's flush-to-zero multiply,
+// which judges tininess on the 24-bit rounded value, could differ). fadd: the hardware's
+// flush-to-zero add is exact here: both operands are multiples of 2^-149, so a sum below 2^-126
+// is exactly representable, is never rounded, and is flushed with its sign either way.
 __device__ __forceinline__ float fmul(float a, float b) { return canon(ftz(__fmul_rn(ftz(a), ftz(b)))); }
-__device__ __forceinline__ float fadd(float a, float b) { return canon(ftz(__fadd_rn(ftz(a), ftz(b)))); }
+__device__ __forceinline__ float fadd_nc(float a, float b) {   // without canonicalising NaN
+  float r;
+  asm("add.rn.ftz.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float fadd(float a, float b) { return canon(fadd_nc(a, b)); }
 // numerics.py:50-52
 __device__ __forceinline__ float i2f(int v) { return __int2float_rn(v); }
 // numerics.py:111-113

@@ -11,6 +11,8 @@
 // are staged in shared memory in K-chunks of KC bytes. One warp owns NCW output columns.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "fp32.cuh"
 #include "ops.h"
 
@@ -113,6 +115,88 @@ cudaError_t launch_gemv(const GemmArgs& g, bool vec, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// Decode GEMV (M <= 8, K <= 512 * KU, 16-byte aligned operands). Persistent warps: each warp owns
+// output columns gw, gw + nw, ...; a lane holds the 16-byte slices k = lane*16 + 512u of one
+// column's weights in registers. The first column's loads are issued before the block stages its
+// activation rows in shared memory, and each next column's loads before the current one is
+// reduced, so every warp keeps two columns of weights in flight.
+template <int MB, int KU>
+__global__ void __launch_bounds__(kThreads) k_gemv8(GemmArgs g) {
+  __shared__ __align__(16) uint8_t sA[MB * 512 * KU];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * MB;
+  const int mb = min(MB, g.M - m0);
+  const int nw = gridDim.x * kWarps;
+  int n = blockIdx.x * kWarps + warp;
+  uint4 w[KU], wn[KU];
+  auto load_col = [&](int col, uint4* dst) {
+    const uint8_t* row = g.W + (uint64_t)col * g.K;
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      const int k = lane * 16 + 512 * u;
+      dst[u] = k < g.K ? ldg_stream(row + k) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  if (n < g.N) load_col(n, w);
+  const int kv = g.K / 16;
+  for (int i = threadIdx.x; i < mb * kv; i += kThreads) {
+    const int m = i / kv, kk = (i - m * kv) * 16;
+    *reinterpret_cast<uint4*>(&sA[m * 512 * KU + kk]) =
+        *reinterpret_cast<const uint4*>(g.A + (uint64_t)(m0 + m) * g.lda + kk);
+  }
+  __syncthreads();
+  for (; n < g.N; n += nw) {
+    const int nn = n + nw;
+    if (nn < g.N) load_col(nn, wn);
+    int acc[MB];
+#pragma unroll
+    for (int m = 0; m < MB; ++m) acc[m] = 0;
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      const int k = lane * 16 + 512 * u;
+      if (k < g.K) {
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+          if (m < mb) {
+            const uint4 a = *reinterpret_cast<const uint4*>(&sA[m * 512 * KU + k]);
+            int s = acc[m];
+            s = __dp4a((int)a.x, (int)w[u].x, s);
+            s = __dp4a((int)a.y, (int)w[u].y, s);
+            s = __dp4a((int)a.z, (int)w[u].z, s);
+            s = __dp4a((int)a.w, (int)w[u].w, s);
+            acc[m] = s;
+          }
+        }
+      }
+    }
+    int mine = 0;
+#pragma unroll
+    for (int m = 0; m < MB; ++m) {
+      int v = acc[m];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+      if (lane == m) mine = v;
+    }
+    if (lane < mb) gemm_epilogue(g, m0 + lane, n, mine);
+#pragma unroll
+    for (int u = 0; u < KU; ++u) w[u] = wn[u];
+  }
+}
+
+template <int MB, int KU>
+cudaError_t launch_gemv8(const GemmArgs& g, cudaStream_t st) {
+  const int blocks = std::min((g.N + kWarps - 1) / kWarps, 148 * 4);
+  k_gemv8<MB, KU><<<dim3(blocks, (g.M + MB - 1) / MB), kThreads, 0, st>>>(g);
+  return cudaGetLastError();
+}
+
+template <int MB>
+cudaError_t launch_gemv8_k(const GemmArgs& g, cudaStream_t st) {
+  if (g.K <= 1024) return launch_gemv8<MB, 2>(g, st);
+  if (g.K <= 2048) return launch_gemv8<MB, 4>(g, st);
+  return launch_gemv8<MB, 8>(g, st);
+}
+
 __global__ void k_im2col(Im2colArgs a) {
   const int K = a.KH * a.KW * a.Cin;
   const uint64_t total = (uint64_t)a.OH * a.OW * K;
@@ -131,6 +215,12 @@ __global__ void k_im2col(Im2colArgs a) {
 
 cudaError_t launch_gemm_w8a8(const GemmArgs& g, cudaStream_t st) {
   const bool vec = ((uintptr_t)g.A % 16 == 0) && (g.lda % 16 == 0) && ((uintptr_t)g.W % 16 == 0) && (g.K % 16 == 0);
+  if (vec && g.K <= 4096 && g.M <= 8) {
+    if (g.M == 1) return launch_gemv8_k<1>(g, st);
+    if (g.M == 2) return launch_gemv8_k<2>(g, st);
+    if (g.M <= 4) return launch_gemv8_k<4>(g, st);
+    return launch_gemv8_k<8>(g, st);
+  }
   if (g.M == 1) return launch_gemv<1, 4>(g, vec, st);
   if (g.M == 2) return launch_gemv<2, 4>(g, vec, st);
   if (g.M <= 4) return launch_gemv<4, 4>(g, vec, st);

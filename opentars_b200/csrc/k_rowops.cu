@@ -16,11 +16,11 @@ namespace tc {
 
 namespace {
 
-__device__ __forceinline__ float sum16_fold(float v) {
-  v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
-  v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
-  v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));
-  v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 8));
+__device__ __forceinline__ float sum16_fold(float v, unsigned mask = 0xFFFFFFFFu) {
+  v = fadd(v, __shfl_xor_sync(mask, v, 1));
+  v = fadd(v, __shfl_xor_sync(mask, v, 2));
+  v = fadd(v, __shfl_xor_sync(mask, v, 4));
+  v = fadd(v, __shfl_xor_sync(mask, v, 8));
   return v;
 }
 __device__ __forceinline__ float max_fold(float v) {
@@ -31,8 +31,8 @@ __device__ __forceinline__ float max_fold(float v) {
   return v;
 }
 
-// One half-warp per row; 8 rows per 128-thread block.
-__global__ void __launch_bounds__(128) k_rowop(RowArgs a) {
+// Long rows (N > kRowSmem floats): one half-warp per row, loads straight from global memory.
+__global__ void __launch_bounds__(128) k_rowop_long(RowArgs a) {
   const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
   const int m = blockIdx.x * 8 + hw;
   const bool live = m < a.M;            // dead half-warps still join the shuffles
@@ -66,7 +66,6 @@ __global__ void __launch_bounds__(128) k_rowop(RowArgs a) {
         store_out(y, j, fmul(j < valid ? exp_f(fadd(X(j), neg(mx))) : 0.0f, r), a.out, a.out_scale);
     return;
   }
-  // norms: gamma at SCALE_OFF, optional beta, eps from W_OFF
   const float kinv = recip_f(i2f(N));
   float mean = 0.0f;
   if (a.fn == ROW_LAYERNORM) {
@@ -85,6 +84,99 @@ __global__ void __launch_bounds__(128) k_rowop(RowArgs a) {
   for (int j = l; j < N; j += 16) {
     const float v = a.fn == ROW_LAYERNORM ? fadd(X(j), neg(mean)) : X(j);
     float o = fmul(fmul(v, rs), ld_f32(a.gamma + 4 * (uint64_t)j));
+    if (a.beta) o = fadd(o, ld_f32(a.beta + 4 * (uint64_t)j));
+    store_out(y, j, o, a.out, a.out_scale);
+  }
+}
+
+constexpr int kRT = 256;                 // threads per row block
+constexpr int kRowSmem = 16384;          // rows up to this many floats are staged in shared memory
+
+// Block-wide fmax (order-free) of one value per thread; every thread gets the result.
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = fmax_c(v, __shfl_xor_sync(0xFFFFFFFFu, v, 16));
+  v = max_fold(v);
+  const int w = threadIdx.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int i = 1; i < kRT / 32; ++i) r = fmax_c(r, red[i]);
+  return r;
+}
+
+// sum16 of v[0..N) in the contract's order: threads 0..15 run the lane chains over shared memory
+// (hardware flush-to-zero adds, canonicalised once), then the pairwise fold; broadcast to all.
+__device__ __forceinline__ float block_sum16(const float* v, int N, float* red) {
+  __syncthreads();
+  if (threadIdx.x < 16) {
+    float acc = 0.0f;
+    for (int j = threadIdx.x; j < N; j += 16) acc = fadd_nc(acc, v[j]);
+    acc = sum16_fold(canon(acc), 0x0000FFFFu);
+    if (threadIdx.x == 0) red[kRT / 32] = acc;
+  }
+  __syncthreads();
+  return red[kRT / 32];
+}
+
+// One block per row: the row (flushed) is staged in shared memory with 16-byte loads when
+// aligned; elementwise work is spread over the block, the ordered sums run on 16 threads.
+__global__ void __launch_bounds__(kRT) k_rowop(RowArgs a) {
+  extern __shared__ float sm[];
+  float* sx = sm;                  // the row
+  float* sv = sm + a.N;            // per-element terms (x*x, d*d, e)
+  __shared__ float red[kRT / 32 + 1];
+  const int m = blockIdx.x, N = a.N, t = threadIdx.x;
+  const uint8_t* x = a.X + (uint64_t)m * a.lda;
+  uint8_t* y = a.Y + (uint64_t)m * a.ldy;
+  if (((uintptr_t)x & 15) == 0) {
+    for (int i = t; i < N / 4; i += kRT) {
+      const float4 v = reinterpret_cast<const float4*>(x)[i];
+      sx[4 * i] = ftz(v.x); sx[4 * i + 1] = ftz(v.y); sx[4 * i + 2] = ftz(v.z); sx[4 * i + 3] = ftz(v.w);
+    }
+  } else {
+    for (int j = t; j < N; j += kRT) sx[j] = ftz(ld_f32(x + 4 * (uint64_t)j));
+  }
+  __syncthreads();
+  if (a.fn == ROW_QUANT) {
+    float amax = 0.0f;
+    for (int j = t; j < N; j += kRT) amax = fmax_c(amax, fabs_c(sx[j]));
+    amax = block_max(amax, red);
+    const float inv = fmul(127.0f, recip_f(amax));
+    if (((uintptr_t)y & 3) == 0) {
+      for (int i = t; i < N / 4; i += kRT) {
+        const uint32_t b = (uint32_t)(uint8_t)q8(sx[4 * i], inv) | (uint32_t)(uint8_t)q8(sx[4 * i + 1], inv) << 8 |
+                           (uint32_t)(uint8_t)q8(sx[4 * i + 2], inv) << 16 | (uint32_t)(uint8_t)q8(sx[4 * i + 3], inv) << 24;
+        reinterpret_cast<uint32_t*>(y)[i] = b;
+      }
+    } else {
+      for (int j = t; j < N; j += kRT) y[j] = (uint8_t)q8(sx[j], inv);
+    }
+    if (t == 0) st_u32(a.scale_out + 4 * (uint64_t)m, fb(ftz(fmul(amax, bf(0x3C010204u)))));
+    return;
+  }
+  if (a.fn == ROW_SOFTMAX) {
+    const int valid = a.K ? min(N, a.K + m) : N;
+    float mx = bf(0xFF800000u);
+    for (int j = t; j < valid; j += kRT) mx = fmax_c(mx, sx[j]);
+    mx = block_max(mx, red);
+    for (int j = t; j < N; j += kRT) sv[j] = j < valid ? exp_f(fadd(sx[j], neg(mx))) : 0.0f;
+    const float r = recip_f(block_sum16(sv, N, red));
+    for (int j = t; j < N; j += kRT) store_out(y, j, fmul(sv[j], r), a.out, a.out_scale);
+    return;
+  }
+  const float kinv = recip_f(i2f(N));
+  if (a.fn == ROW_LAYERNORM) {
+    const float mean = fmul(block_sum16(sx, N, red), kinv);
+    __syncthreads();
+    for (int j = t; j < N; j += kRT) sx[j] = fadd(sx[j], neg(mean));     // d
+  }
+  __syncthreads();
+  for (int j = t; j < N; j += kRT) sv[j] = fmul(sx[j], sx[j]);
+  const float s = block_sum16(sv, N, red);
+  const float rs = rsqrt_f(a.fn == ROW_L2NORM ? fadd(s, a.eps) : fadd(fmul(s, kinv), a.eps));
+  for (int j = t; j < N; j += kRT) {
+    float o = fmul(fmul(sx[j], rs), ld_f32(a.gamma + 4 * (uint64_t)j));
     if (a.beta) o = fadd(o, ld_f32(a.beta + 4 * (uint64_t)j));
     store_out(y, j, o, a.out, a.out_scale);
   }
@@ -188,7 +280,16 @@ inline int grid_for(uint64_t total, int threads) {
 }  // namespace
 
 cudaError_t launch_rowop(const RowArgs& a, cudaStream_t st) {
-  k_rowop<<<(a.M + 7) / 8, 128, 0, st>>>(a);
+  if (a.N > kRowSmem) {
+    k_rowop_long<<<(a.M + 7) / 8, 128, 0, st>>>(a);
+    return cudaGetLastError();
+  }
+  const int smem = 2 * a.N * 4;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_rowop, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * kRowSmem * 4);
+    if (e != cudaSuccess) return e;
+  }
+  k_rowop<<<a.M, kRT, smem, st>>>(a);
   return cudaGetLastError();
 }
 cudaError_t launch_act(const ActArgs& a, cudaStream_t st) {

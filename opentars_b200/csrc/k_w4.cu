@@ -13,6 +13,8 @@
 // lanes 0..3, and y = (b0 + b1) + (b2 + b3), bias, activation and the output conversion follow.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "fp32.cuh"
 #include "ops.h"
 
@@ -29,15 +31,10 @@ __device__ __forceinline__ uint4 ldg_stream(const uint8_t* p) {
   return v;
 }
 
-// One activation element's fp32 bits (fp32 rows or bf16 rows widened exactly).
-__device__ __forceinline__ uint32_t act_bits(const W4Args& g, int m, int k) {
-  const uint8_t* row = g.A + (uint64_t)m * g.lda;
-  return g.a_bf16 ? ((uint32_t)ld_u16(row + 2 * (uint64_t)k) << 16) : ld_u32(row + 4 * (uint64_t)k);
-}
-
-// Aligns rows [m0, m0 + mb) into sQ [MB][K] int16 and sS [MB][G] fp32 bits; one warp per group.
+// Aligns rows [m0, m0 + mb) from their fp32 bit patterns in sX [MB][K] into sQ [MB][K] int16 and
+// sS [MB][64] fp32 bits; one warp per (row, group), four elements per lane.
 template <int MB>
-__device__ void align_rows(const W4Args& g, int m0, int mb, int16_t* sQ, uint32_t* sS) {
+__device__ void align_rows(const W4Args& g, int mb, const uint32_t* sX, int16_t* sQ, uint32_t* sS) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = g.K / W4_GROUP;
   for (int p = warp; p < mb * G; p += kWarps) {
@@ -48,7 +45,7 @@ __device__ void align_rows(const W4Args& g, int m0, int mb, int16_t* sQ, uint32_
     int emax = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      uint32_t v = act_bits(g, m0 + m, gi * W4_GROUP + lane * 4 + j);
+      uint32_t v = sX[m * g.K + gi * W4_GROUP + lane * 4 + j];
       if ((v & 0x7F800000u) == 0) v &= 0x80000000u;        // ftz
       b[j] = v;
       e[j] = (int)((v >> 23) & 0xFF);
@@ -94,19 +91,56 @@ __device__ __forceinline__ void unpack8(uint32_t w, uint32_t& lo, uint32_t& hi) 
   hi = __byte_perm(ev, od, 0x7362);
 }
 
+// One persistent block stages its activation rows once (16-byte loads when aligned), aligns them
+// in shared memory, then its warps stream columns n = gw, gw + nw, ...; each lane keeps the
+// packed weights of its groups (lane, lane + 32) for this column and the next one in registers.
 template <int MB>
 __global__ void __launch_bounds__(kThreads) k_gemv_w4(W4Args g, bool vec) {
   extern __shared__ __align__(16) uint8_t smem[];
-  int16_t* sQ = reinterpret_cast<int16_t*>(smem);
-  uint32_t* sS = reinterpret_cast<uint32_t*>(smem + (size_t)MB * g.K * 2);
+  uint32_t* sX = reinterpret_cast<uint32_t*>(smem);                                 // [MB][K] fp32 bits
+  int16_t* sQ = reinterpret_cast<int16_t*>(smem + (size_t)MB * g.K * 4);             // [MB][K]
+  uint32_t* sS = reinterpret_cast<uint32_t*>(smem + (size_t)MB * g.K * 6);            // [MB][64]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * MB;
   const int mb = min(MB, g.M - m0);
   const int G = g.K / W4_GROUP;
-  align_rows<MB>(g, m0, mb, sQ, sS);
+  const int nw = gridDim.x * kWarps;
+  int n = blockIdx.x * kWarps + warp;
+  uint4 w[2][4], wn[2][4];
+  auto load_col = [&](int col, uint4 (*dst)[4]) {
+#pragma unroll
+    for (int slot = 0; slot < 2; ++slot) {
+      const int gi = lane + 32 * slot;
+      const uint8_t* wp = g.W + (uint64_t)col * (g.K / 2) + gi * 64;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (gi >= G) dst[slot][i] = make_uint4(0, 0, 0, 0);
+        else if (vec) dst[slot][i] = ldg_stream(wp + 16 * i);
+        else dst[slot][i] = make_uint4(ld_u32(wp + 16 * i), ld_u32(wp + 16 * i + 4), ld_u32(wp + 16 * i + 8),
+                                       ld_u32(wp + 16 * i + 12));
+      }
+    }
+  };
+  if (n < g.N) load_col(n, w);
+  // the block's activation rows as fp32 bit patterns (bf16 widened exactly)
+  for (int m = 0; m < mb; ++m) {
+    const uint8_t* row = g.A + (uint64_t)(m0 + m) * g.lda;
+    uint32_t* dst = sX + m * g.K;
+    if (!g.a_bf16 && ((uintptr_t)row & 15) == 0) {
+      for (int i = threadIdx.x; i < g.K / 4; i += kThreads)
+        reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(row)[i];
+    } else {
+      for (int k = threadIdx.x; k < g.K; k += kThreads)
+        dst[k] = g.a_bf16 ? ((uint32_t)ld_u16(row + 2 * (uint64_t)k) << 16) : ld_u32(row + 4 * (uint64_t)k);
+    }
+  }
+  __syncthreads();
+  align_rows<MB>(g, mb, sX, sQ, sS);
   __syncthreads();
 
-  for (int n = blockIdx.x * kWarps + warp; n < g.N; n += gridDim.x * kWarps) {
+  for (; n < g.N; n += nw) {
+    const int nn = n + nw;
+    if (nn < g.N) load_col(nn, wn);
     float term[MB][2];
 #pragma unroll
     for (int slot = 0; slot < 2; ++slot) {
@@ -114,13 +148,6 @@ __global__ void __launch_bounds__(kThreads) k_gemv_w4(W4Args g, bool vec) {
 #pragma unroll
       for (int m = 0; m < MB; ++m) term[m][slot] = 0.0f;
       if (gi < G) {
-        const uint8_t* wp = g.W + (uint64_t)n * (g.K / 2) + gi * 64;
-        uint4 w[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          w[i] = vec ? ldg_stream(wp + 16 * i)
-                     : make_uint4(ld_u32(wp + 16 * i), ld_u32(wp + 16 * i + 4), ld_u32(wp + 16 * i + 8),
-                                  ld_u32(wp + 16 * i + 12));
         const float ws = from_fp16(ld_u16(g.scale + 2 * ((uint64_t)n * G + gi)));
 #pragma unroll
         for (int m = 0; m < MB; ++m) {
@@ -129,12 +156,12 @@ __global__ void __launch_bounds__(kThreads) k_gemv_w4(W4Args g, bool vec) {
             int dot = 0;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const uint32_t words[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+              const uint32_t words[4] = {w[slot][i].x, w[slot][i].y, w[slot][i].z, w[slot][i].w};
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 uint32_t lo, hi;
                 unpack8(words[j], lo, hi);
-                const int base = (i * 4 + j) * 4;  // pairs of int16 mantissas: 8 elements = 4 words
+                const int base = (i * 4 + j) * 4;  // 8 elements = 4 words of int16 pairs
                 dot = __dp2a_lo((int)q[base + 0], (int)lo, dot);
                 dot = __dp2a_hi((int)q[base + 1], (int)lo, dot);
                 dot = __dp2a_lo((int)q[base + 2], (int)hi, dot);
@@ -155,8 +182,9 @@ __global__ void __launch_bounds__(kThreads) k_gemv_w4(W4Args g, bool vec) {
         const int gi = b + 4 * i;
         const float t0 = __shfl_sync(0xFFFFFFFFu, term[m][0], gi & 31);
         const float t1 = __shfl_sync(0xFFFFFFFFu, term[m][1], gi & 31);
-        if (gi < G) bank = fadd(bank, gi < 32 ? t0 : t1);
+        if (gi < G) bank = fadd_nc(bank, gi < 32 ? t0 : t1);
       }
+      bank = canon(bank);
       const float b1 = __shfl_sync(0xFFFFFFFFu, bank, 1);
       const float b2 = __shfl_sync(0xFFFFFFFFu, bank, 2);
       const float b3 = __shfl_sync(0xFFFFFFFFu, bank, 3);
@@ -167,16 +195,20 @@ __global__ void __launch_bounds__(kThreads) k_gemv_w4(W4Args g, bool vec) {
         store_out(g.Y + (uint64_t)(m0 + m) * g.ldy, n, y, g.out, g.out_scale);
       }
     }
+#pragma unroll
+    for (int slot = 0; slot < 2; ++slot)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[slot][i] = wn[slot][i];
   }
 }
 
 template <int MB>
 cudaError_t launch_w4(const W4Args& g, cudaStream_t st) {
-  const size_t smem = (size_t)MB * g.K * 2 + (size_t)MB * 64 * 4;
+  const size_t smem = (size_t)MB * g.K * 6 + (size_t)MB * 64 * 4;
   auto kern = k_gemv_w4<MB>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  const int nblk = (g.N + kWarps - 1) / kWarps;
+  const int nblk = std::min((g.N + kWarps - 1) / kWarps, 148 * 2);
   dim3 grid(nblk, (g.M + MB - 1) / MB);
   kern<<<grid, kThreads, smem, st>>>(g, (uintptr_t)g.W % 16 == 0);
   return cudaGetLastError();

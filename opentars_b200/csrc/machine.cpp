@@ -321,10 +321,11 @@ int tc_queue_capture(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_
   if (e != cudaSuccess) { delete g; return fail(m, "begin capture", e); }
   uint32_t last = 0;
   int rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, true, [&](uint32_t i) {
-    if (timing) cudaEventRecord(g->events[i], m->stream);
+    // an external record node: a plain cudaEventRecord inside a capture only orders work
+    if (timing) cudaEventRecordWithFlags(g->events[i], m->stream, cudaEventRecordExternal);
     last = i + 1;
   });
-  if (timing && last) cudaEventRecord(g->events[last], m->stream);
+  if (timing && last) cudaEventRecordWithFlags(g->events[last], m->stream, cudaEventRecordExternal);
   cudaGraph_t graph = nullptr;
   cudaError_t ce = cudaStreamEndCapture(m->stream, &graph);
   if (rc == TC_OK && ce != cudaSuccess) rc = fail(m, "end capture", ce);

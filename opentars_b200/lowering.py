@@ -1,0 +1,486 @@
+"""The step driver: Qwen3 / Gemma 3 models lowered to tars_mini v0.4 descriptors.
+
+Restates, for the families on the hot path, the reference's program builder and LLM lowering so
+that the same DDR image and the same descriptor queues come out byte for byte (pinned by the
+committed fixtures):
+  * Program (alloc / _put / _emit / build)       tars_mini/compiler.py:134-155, 186-188, 384-391
+  * V, Dev emitters (rowop, norm, quant, gemm_rc, gemm_w4, fdot, elt, rope)   tars_mini/llm.py:34-178
+  * QwenLowering: weights, state, chunk, _fa_block, _mlp, _head, stage, put_input, logits_of,
+    logits_rows, generate                                                     llm.py:213-836
+Every linear is W8A8 (ROW_QUANT then GEMM QM_ROWCOL); Gemma 3's down projection runs as equal
+K blocks (llm.py:303-321) whose fp32 partials are added by ELT ADD in block order. Qwen3.5's
+linear attention, MTP and Gemma 4 are outside this path.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, replace
+
+import numpy as np
+
+from . import contract as C
+from .models import head_rows, input_embedding, quantize_weight, quantize_weight4
+
+F32 = np.float32
+ALIGN = 128
+GEMV_K = 4096
+
+
+def pad16(n: int) -> int:
+    return -(-n // 16) * 16
+
+
+@dataclass
+class V:
+    """A matrix in the image: offset from the program base, shape, row stride in bytes, format."""
+    off: int
+    rows: int
+    cols: int
+    ld: int
+    fmt: int = C.OUT_FP32
+
+    def rowv(self, r0: int, n: int) -> "V":
+        return replace(self, off=self.off + r0 * self.ld, rows=n)
+
+    def colv(self, c0: int, n: int) -> "V":
+        return replace(self, off=self.off + c0 * C.ESIZE[self.fmt], cols=n)
+
+    def heads(self, hd: int) -> "V":
+        assert self.ld == self.cols * C.ESIZE[self.fmt] and self.cols % hd == 0
+        return V(self.off, self.rows * self.cols // hd, hd, hd * C.ESIZE[self.fmt], self.fmt)
+
+
+@dataclass
+class QLin:
+    w_off: int
+    s_off: int
+    b_off: int | None
+    n: int
+    k: int
+    wbits: int = 8
+
+
+def _ld16(ld: int, rowbytes: int) -> int:
+    if ld == rowbytes:
+        return 0
+    assert ld % 16 == 0 and ld > rowbytes
+    return ld // 16
+
+
+class Program:
+    """A DDR image being laid out (bump allocator, 128-byte aligned; offset 0 kept unused) and the
+    descriptors emitted against it."""
+
+    def __init__(self, ddr_bytes: int = 1 << 24, base_addr: int = 0):
+        self.base = base_addr
+        self.ddr = bytearray(base_addr + ddr_bytes)
+        self.top = ALIGN
+        self.descs: list[bytes] = []
+        self.queue_off: int | None = None
+
+    def alloc(self, nbytes: int) -> int:
+        off = self.top
+        self.top = -(-(off + nbytes) // ALIGN) * ALIGN
+        if self.base + self.top > len(self.ddr):
+            raise MemoryError(f"program needs {self.top} bytes of DDR, has {len(self.ddr)}")
+        return off
+
+    def _put(self, arr: np.ndarray, dtype: str) -> int:
+        data = np.ascontiguousarray(arr).astype(dtype).tobytes()
+        off = self.alloc(len(data))
+        self.ddr[self.base + off:self.base + off + len(data)] = data
+        return off
+
+    def _emit(self, **f) -> None:
+        self.descs.append(C.encode({"MAGIC": C.MAGIC, "VERSION": C.VERSION, "VALID": 1, "BASE_ADDR": self.base, **f}))
+
+    def build(self) -> tuple[bytearray, int, int]:
+        if self.queue_off is None:
+            self.queue_off = self.alloc(C.DESC_BYTES * len(self.descs))
+            for i, r in enumerate(self.descs):
+                a = self.base + self.queue_off + 64 * i
+                self.ddr[a:a + 64] = r
+        return self.ddr, self.base + self.queue_off, len(self.descs)
+
+
+class Dev(Program):
+    """Descriptor emitters on V views (offsets relative to the program base)."""
+
+    def mat(self, rows: int, cols: int, fmt: int = C.OUT_FP32) -> V:
+        es = C.ESIZE[fmt]
+        return V(self.alloc(rows * cols * es), rows, cols, cols * es, fmt)
+
+    def put(self, a: np.ndarray, dt: str = "<f4") -> int:
+        return self._put(np.asarray(a), dt)
+
+    def const(self, a: np.ndarray) -> V:
+        a = np.asarray(a, F32).reshape(1, -1) if np.ndim(a) < 2 else np.asarray(a, F32)
+        return V(self.put(a), a.shape[0], a.shape[1], 4 * a.shape[1])
+
+    def rowop(self, x: V, fn: int, y: V, gamma: V | None = None, eps: float = 0.0, start: int = 0,
+              scale_out: int = 0, beta: V | None = None) -> None:
+        assert x.cols == y.cols and x.rows == y.rows and x.fmt == C.OUT_FP32 and y.fmt != C.OUT_FP16
+        self._emit(OPCODE=C.OP_ROW, CTRL=fn, EPI=C.epi(C.ACT_NONE, y.fmt, int(beta is not None)),
+                   A_OFF=x.off, Y_OFF=y.off, M=x.rows, N=x.cols, K=start,
+                   SCALE_OFF=gamma.off if gamma is not None else scale_out,
+                   BIAS_OFF=beta.off if beta is not None else 0,
+                   W_OFF=C.f32_bits(eps) if gamma is not None else 0,
+                   LDA16=_ld16(x.ld, 4 * x.cols), LDY16=_ld16(y.ld, y.cols * C.ESIZE[y.fmt]))
+
+    def norm(self, x: V, gamma: V, eps: float, y: V, l2: bool = False) -> None:
+        self.rowop(x, C.ROW_L2NORM if l2 else C.ROW_RMSNORM, y, gamma, eps)
+
+    def quant(self, x: V, q: V | None = None, s: int | None = None) -> tuple[V, int]:
+        q = self.mat(x.rows, x.cols, C.OUT_INT8) if q is None else q
+        s = self.alloc(4 * x.rows) if s is None else s
+        self.rowop(x, C.ROW_QUANT, q, scale_out=s)
+        return q, s
+
+    def softmax_causal(self, x: V, y: V, first_valid: int) -> None:
+        self.rowop(x, C.ROW_SOFTMAX, y, start=first_valid)
+
+    def gemm_rc(self, xq: V, srow: int, w: QLin, y: V, act: int = C.ACT_NONE) -> None:
+        assert xq.fmt == C.OUT_INT8 and xq.cols == w.k and y.cols == w.n and srow % 16 == 0 and y.fmt != C.OUT_FP16
+        self._emit(OPCODE=C.OP_GEMM, CTRL=C.ctrl(C.QM_ROWCOL, fusion=int(act != C.ACT_NONE)),
+                   EPI=C.epi(act, y.fmt, int(w.b_off is not None)), A_OFF=xq.off, W_OFF=w.w_off,
+                   SCALE_OFF=w.s_off, BIAS_OFF=w.b_off or 0, Y_OFF=y.off, M=xq.rows, N=w.n, K=w.k,
+                   HDR_RSV=srow // 16, LDA16=_ld16(xq.ld, xq.cols), LDY16=_ld16(y.ld, y.cols * C.ESIZE[y.fmt]))
+
+    def gemm_w4(self, x: V, w: QLin, y: V, act: int = C.ACT_NONE) -> None:
+        assert x.fmt in (C.OUT_FP32, C.OUT_BF16) and x.cols == w.k and y.cols == w.n
+        assert w.wbits == 4 and w.k >= 256 and w.k % 256 == 0 and w.w_off % 128 == 0 and y.fmt != C.OUT_FP16
+        adt = C.DT_FP32 if x.fmt == C.OUT_FP32 else C.DT_BF16
+        self._emit(OPCODE=C.OP_GEMM, CTRL=C.ctrl(C.QM_GROUP, a_dtype=adt, w_dtype=C.DT_INT4,
+                                                 fusion=int(act != C.ACT_NONE)),
+                   EPI=C.epi(act, y.fmt, int(w.b_off is not None)), A_OFF=x.off, W_OFF=w.w_off,
+                   SCALE_OFF=w.s_off, BIAS_OFF=w.b_off or 0, Y_OFF=y.off, M=x.rows, N=w.n, K=w.k,
+                   GROUP_SIZE=C.W4_GROUP, LDA16=_ld16(x.ld, C.ESIZE[x.fmt] * x.cols),
+                   LDY16=_ld16(y.ld, y.cols * C.ESIZE[y.fmt]))
+
+    def fdot(self, a: V, b: V, y: V, nn: bool) -> None:
+        K = a.cols
+        N = b.cols if nn else b.rows
+        assert (b.rows if nn else b.cols) == K and y.cols == N and y.rows == a.rows
+        brow = C.ESIZE[b.fmt] * b.cols
+        self._emit(OPCODE=C.OP_FDOT, CTRL=int(nn), EPI=C.epi(C.ACT_NONE, y.fmt), A_OFF=a.off, W_OFF=b.off,
+                   Y_OFF=y.off, M=a.rows, N=N, K=K, GROUP_SIZE=_ld16(b.ld, brow),
+                   HDR_RSV=C.STATE_FP16 if b.fmt == C.OUT_FP16 else 0,
+                   LDA16=_ld16(a.ld, 4 * a.cols), LDY16=_ld16(y.ld, y.cols * C.ESIZE[y.fmt]))
+
+    def elt(self, op: int, a: V, b: V, y: V, bmode: int = C.BM_DENSE, arow: bool = False,
+            act: int = C.ACT_NONE, c: V | None = None) -> None:
+        M, N = y.rows, y.cols
+        g = _ld16(b.ld, 4 * N) if bmode == C.BM_DENSE else 0
+        self._emit(OPCODE=C.OP_ELT, CTRL=op, EPI=C.epi(act, y.fmt, int(c is not None)),
+                   A_OFF=a.off, W_OFF=b.off, Y_OFF=y.off, BIAS_OFF=c.off if c is not None else 0,
+                   M=M, N=N, HDR_RSV=bmode | int(arow) << 2 | (C.STATE_FP16 if a.fmt == C.OUT_FP16 else 0),
+                   GROUP_SIZE=g, LDA16=0 if arow else _ld16(a.ld, C.ESIZE[a.fmt] * N),
+                   LDY16=_ld16(y.ld, N * C.ESIZE[y.fmt]))
+
+    def rope(self, x: V, tab: V, rows_per_pos: int, rot: int, y: V) -> None:
+        self._emit(OPCODE=C.OP_ROPE, CTRL=0, EPI=C.epi(C.ACT_NONE, y.fmt), A_OFF=x.off, W_OFF=tab.off,
+                   Y_OFF=y.off, M=x.rows, N=x.cols, K=rot, GROUP_SIZE=rows_per_pos,
+                   LDA16=_ld16(x.ld, 4 * x.cols), LDY16=_ld16(y.ld, y.cols * C.ESIZE[y.fmt]))
+
+
+class QwenLowering:
+    """A Qwen3 or Gemma 3 text model as data in one DDR image plus per-chunk descriptor queues.
+
+        low = QwenLowering(cfg, weights, max_tokens=256, head=True, queue_cap=4096)
+        ids, logits, counts = low.generate(run, prompt, n_new)     # run(ddr, q, n) -> ddr
+    """
+
+    def __init__(self, cfg, weights: dict[str, np.ndarray], max_tokens: int, ddr_bytes: int = 1 << 27,
+                 head: bool = False, queue_cap: int = 0, scratch_bytes: int = 1 << 22, verify_rows: int = 1,
+                 keep_layers: bool = True, wbits: int = 8):
+        if wbits not in (4, 8):
+            raise ValueError("wbits must be 4 (W4A16) or 8 (W8A8)")
+        mt = getattr(cfg, "model_type", "")
+        if mt not in ("qwen3", "gemma3_text"):
+            raise ValueError(f"model type {mt!r}: this lowering covers Qwen3 and Gemma 3")
+        self.wbits, self.keep_layers = wbits, keep_layers
+        self.cfg, self.w, self.T = cfg, weights, max_tokens
+        self.verify_rows = verify_rows
+        self.p = self.prog = Dev(ddr_bytes=ddr_bytes)
+        self.H, self.eps = cfg.hidden_size, cfg.rms_norm_eps
+        self.q3 = mt == "qwen3"
+        self.gemma = mt == "gemma3_text"
+        self.types = list(cfg.layer_types)
+        if self.gemma:
+            assert set(self.types) <= {"sliding_attention", "full_attention"}
+            assert cfg.attn_logit_softcapping is None and cfg.final_logit_softcapping is None
+            assert cfg.hidden_activation == "gelu_pytorch_tanh"
+            assert max_tokens <= cfg.sliding_window, "the context must fit the sliding window"
+        else:
+            assert set(self.types) == {"full_attention"}
+        self.nh, self.nkv, self.hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        self.rot = self.hd if self.gemma else int(self.hd * cfg.rope_parameters.get("partial_rotary_factor", 1.0))
+        self.qmul = cfg.query_pre_attn_scalar ** -0.5 if self.gemma else self.hd ** -0.5
+        self.Tp = pad16(max_tokens)
+        self.head = head
+        self.vocab = weights["embed_tokens.weight"].shape[0] if head else 0
+        self._state()
+        self.queue_cap = queue_cap
+        self.qbase = self.p.alloc(64 * queue_cap) if queue_cap else None
+        self.scratch0 = self.p.top
+        self.scratch_end = self.p.alloc(scratch_bytes) + scratch_bytes
+        self._weights()
+        self.end = self.p.top
+
+    # ------------------------------------------------------------------ weights (host side)
+    def lin(self, w: np.ndarray, bias: np.ndarray | None = None) -> QLin:
+        b = self.p.put(np.asarray(bias, F32)) if bias is not None else None
+        if self.wbits == 4:
+            qw = quantize_weight4(w)
+            return QLin(self.p.put(qw.q, "u1"), self.p.put(qw.scale, "<u2"), b, qw.n, qw.k, 4)
+        qw = quantize_weight(np.asarray(w, np.float64), per_channel=True)
+        assert qw.n % 16 == 0 and qw.k % 16 == 0
+        return QLin(self.p.put(qw.q, "i1"), self.p.put(qw.scale), b, qw.n, qw.k)
+
+    def lin_k(self, w: np.ndarray, parts: int = 0) -> list[QLin]:
+        """Equal K blocks sharing one per-channel scale (W8) or with their own group scales (W4)."""
+        if self.wbits == 4:
+            qw = quantize_weight4(w)
+            parts = parts or -(-qw.k // GEMV_K)
+            kb = qw.k // parts
+            assert kb * parts == qw.k and kb % C.W4_GROUP == 0
+            return [QLin(self.p.put(np.ascontiguousarray(qw.q[:, c // 2:(c + kb) // 2]), "u1"),
+                         self.p.put(np.ascontiguousarray(qw.scale[:, c // C.W4_GROUP:(c + kb) // C.W4_GROUP]), "<u2"),
+                         None, qw.n, kb, 4) for c in range(0, qw.k, kb)]
+        qw = quantize_weight(np.asarray(w, np.float64), per_channel=True)
+        parts = parts or -(-qw.k // GEMV_K)
+        kb = qw.k // parts
+        assert kb * parts == qw.k and kb % 16 == 0 and qw.n % 16 == 0
+        s = self.p.put(qw.scale)
+        return [QLin(self.p.put(np.ascontiguousarray(qw.q[:, c:c + kb]), "i1"), s, None, qw.n, kb)
+                for c in range(0, qw.k, kb)]
+
+    def gamma1(self, w: np.ndarray, mul: float = 1.0) -> V:
+        """Qwen3: the RMSNorm weight itself; Gemma 3: fp32(1 + w). Times `mul` (the attention
+        scaling folded into q_norm)."""
+        g = np.asarray(w, F32) if self.q3 else (F32(1.0) + np.asarray(w, F32)).astype(F32)
+        return self.p.const((g * F32(mul)).astype(F32))
+
+    def linear(self, x: V, w: QLin, y: V, act: int = C.ACT_NONE, qs: tuple[V, int] | None = None) -> None:
+        if self.wbits == 4:
+            self.p.gemm_w4(x, w, y, act)
+        else:
+            xq, xs = self.p.quant(x) if qs is None else qs
+            self.p.gemm_rc(xq, xs, w, y, act)
+
+    def _fa_weights(self, A: str) -> dict:
+        W = self.w
+        sa = A + "self_attn."
+        if self.gemma:
+            g1 = lambda n, mul=1.0: self.gamma1(W[A + n + ".weight"], mul)  # noqa: E731
+            return dict(
+                ln_in=g1("input_layernorm"), attn_norm=g1("post_attention_layernorm"),
+                ln_post=g1("pre_feedforward_layernorm"), mlp_norm=g1("post_feedforward_layernorm"),
+                q=self.lin(W[sa + "q_proj.weight"]), g=None,
+                k=self.lin(W[sa + "k_proj.weight"]), v=self.lin(W[sa + "v_proj.weight"]),
+                qn=g1("self_attn.q_norm", self.qmul), kn=g1("self_attn.k_norm"),
+                o=self.lin(W[sa + "o_proj.weight"]),
+                gate=self.lin(W[A + "mlp.gate_proj.weight"]), up=self.lin(W[A + "mlp.up_proj.weight"]),
+                down=self.lin_k(W[A + "mlp.down_proj.weight"]))
+        q = self.lin(W[sa + "q_proj.weight"])
+        return dict(
+            ln_in=self.gamma1(W[A + "input_layernorm.weight"]),
+            ln_post=self.gamma1(W[A + "post_attention_layernorm.weight"]),
+            q=q, g=None,
+            k=self.lin(W[sa + "k_proj.weight"]), v=self.lin(W[sa + "v_proj.weight"]),
+            qn=self.gamma1(W[sa + "q_norm.weight"], self.qmul), kn=self.gamma1(W[sa + "k_norm.weight"]),
+            o=self.lin(W[sa + "o_proj.weight"]),
+            gate=self.lin(W[A + "mlp.gate_proj.weight"]), up=self.lin(W[A + "mlp.up_proj.weight"]),
+            down=self.lin(W[A + "mlp.down_proj.weight"]))
+
+    def _weights(self) -> None:
+        p = self.p
+        self.lw = [self._fa_weights(f"layers.{i}.") for i in range(len(self.types))]
+        if self.gemma:
+            for w, t in zip(self.lw, self.types):
+                w["rope"] = t
+        self.final_norm = self.gamma1(self.w["norm.weight"])
+
+        def table(theta: float) -> V:
+            """RoPE rows t = cos(t * inv_freq), sin(t * inv_freq) in fp32, as torch computes them."""
+            th = F32(theta)
+            inv = (1.0 / (th ** (np.arange(0, self.rot, 2, dtype=F32) / F32(self.rot)))).astype(F32)
+            fr = (np.arange(self.T, dtype=F32)[:, None] * inv[None, :]).astype(F32)
+            return p.const(np.concatenate([np.cos(fr), np.sin(fr)], axis=1).astype(F32))
+        if self.gemma:
+            self.rope_tabs = {t: table(self.cfg.rope_parameters[t]["rope_theta"]) for t in sorted(set(self.types))}
+        else:
+            self.rope_tab = table(self.cfg.rope_parameters["rope_theta"])
+        self.head_lins = []
+        if self.head:
+            e = self.w["embed_tokens.weight"]
+            hr = head_rows(e.shape[0])
+            self.head_lins = [self.lin(e[r:r + hr]) for r in range(0, e.shape[0], hr)]
+
+    def embed(self, ids) -> np.ndarray:
+        return input_embedding(self.cfg, self.w["embed_tokens.weight"][np.asarray(ids)])
+
+    # ------------------------------------------------------------------ state in DDR
+    def _state(self) -> None:
+        p, T, H = self.p, self.T, self.H
+        if self.keep_layers:
+            self.xs = [p.mat(T, H) for _ in range(len(self.types) + 1)]
+            self.x0 = self.xs[0]
+        else:
+            self.x0 = p.mat(T, H)
+            xb0, xb1 = p.mat(T, H), p.mat(T, H)
+            self.xs = [self.x0] + [xb0 if i % 2 == 0 else xb1 for i in range(len(self.types))]
+        self.y = p.mat(T, H)
+        self.st = [dict(kc=p.mat(self.Tp, self.nkv * self.hd), vc=p.mat(self.Tp, self.nkv * self.hd))
+                   for _ in self.types]
+        self.logits = p.mat(self.verify_rows, self.vocab) if self.head else None
+
+    def input(self, x: np.ndarray, t0: int = 0) -> None:
+        a = self.p.base + self.x0.off + t0 * self.x0.ld
+        self.p.ddr[a:a + x.size * 4] = np.asarray(x, F32).tobytes()
+
+    # ------------------------------------------------------------------ blocks
+    def chunk(self, t0: int, n: int, all_rows: bool = False) -> None:
+        """Tokens t0 .. t0 + n - 1 through every layer, the final norm and (with the head) the last
+        token's logits (all_rows: every token's)."""
+        assert not all_rows or n <= self.verify_rows
+        p = self.p
+        for i in range(len(self.types)):
+            p.top = self.scratch0
+            self._fa_block(self.lw[i], self.st[i], self.xs[i].rowv(t0, n), self.xs[i + 1].rowv(t0, n), t0, n)
+            assert p.top <= self.scratch_end, "scratch_bytes too small for this chunk"
+        p.top = self.scratch0
+        p.norm(self.xs[-1].rowv(t0, n), self.final_norm, self.eps, self.y.rowv(t0, n))
+        if self.head:
+            r = n if all_rows else 1
+            self._head(self.y.rowv(t0 + n - r, r))
+        assert p.top <= self.scratch_end, "scratch_bytes too small for this chunk"
+        p.top = self.end
+
+    def _head(self, y: V) -> None:
+        p, r, c0 = self.p, y.rows, 0
+        qs = p.quant(y) if self.wbits == 8 else None
+        for lin in self.head_lins:
+            out = V(self.logits.off + 4 * c0 * r, r, lin.n, 4 * lin.n)
+            self.linear(y, lin, out, qs=qs)
+            c0 += lin.n
+
+    def _linear_k(self, x: V, lins, qs, out: V) -> None:
+        """A linear whose weights may be split into K blocks: partials added in block order."""
+        p, n = self.p, x.rows
+        lins = lins if isinstance(lins, list) else [lins]
+        c0 = 0
+        for i, lin in enumerate(lins):
+            part = out if i == 0 else p.mat(n, self.H)
+            self.linear(x.colv(c0, lin.k), lin, part, qs=None if qs is None else (qs[0].colv(c0, lin.k), qs[1]))
+            if i:
+                p.elt(C.ELT_ADD, out, part, out)
+            c0 += lin.k
+
+    def _mlp(self, w: dict, x: V, out: V) -> None:
+        p, n = self.p, x.rows
+        h = p.mat(n, self.H)
+        p.norm(x, w["ln_post"], self.eps, h)
+        qs = p.quant(h) if self.wbits == 8 else None
+        g, u = p.mat(n, w["gate"].n), p.mat(n, w["up"].n)
+        self.linear(h, w["gate"], g, act=C.ACT_GELU if self.gemma else C.ACT_SILU, qs=qs)
+        self.linear(h, w["up"], u, qs=qs)
+        p.elt(C.ELT_MUL, g, u, g)
+        gqs = p.quant(g) if self.wbits == 8 else None
+        d = p.mat(n, self.H)
+        self._linear_k(g, w["down"], gqs, d)
+        if w.get("mlp_norm") is not None:
+            dn = p.mat(n, self.H)
+            p.norm(d, w["mlp_norm"], self.eps, dn)
+            d = dn
+        p.elt(C.ELT_ADD, x, d, out)
+
+    def _fa_block(self, w: dict, st: dict, x: V, out: V, t0: int, n: int) -> None:
+        p = self.p
+        kc, vc = st["kc"], st["vc"]
+        nh, nkv, hd, rot = self.nh, self.nkv, self.hd, self.rot
+        h = p.mat(n, self.H)
+        p.norm(x, w["ln_in"], self.eps, h)
+        qs = p.quant(h) if self.wbits == 8 else None
+        q = p.mat(n, nh * hd)
+        self.linear(h, w["q"], q, qs=qs)
+        qn = p.mat(n, nh * hd)
+        p.norm(q.heads(hd), w["qn"], self.eps, qn.heads(hd))
+        qr = p.mat(n, nh * hd)
+        tab = (self.rope_tabs[w["rope"]] if "rope" in w else self.rope_tab).rowv(t0, (n * nh - 1) // nh + 1)
+        p.rope(qn.heads(hd), tab, nh, rot, qr.heads(hd))
+        k = p.mat(n, nkv * hd)
+        self.linear(h, w["k"], k, qs=qs)
+        self.linear(h, w["v"], vc.rowv(t0, n), qs=qs)          # V straight into the cache
+        kn = p.mat(n, nkv * hd)
+        p.norm(k.heads(hd), w["kn"], self.eps, kn.heads(hd))
+        p.rope(kn.heads(hd), tab, nkv, rot, kc.rowv(t0, n).heads(hd))
+        nk = pad16(t0 + n)
+        att = p.mat(n, nh * hd)
+        sc, pr = p.mat(n, nk), p.mat(n, nk)
+        for hh in range(nh):
+            kv = hh // (nh // nkv)
+            qv = V(qr.off + hh * hd * 4, n, hd, qr.ld)
+            kmat = V(kc.off + kv * hd * 4, nk, hd, kc.ld)
+            vmat = V(vc.off + kv * hd * 4, nk, hd, vc.ld)
+            p.fdot(qv, kmat, sc, nn=False)
+            p.softmax_causal(sc, pr, t0 + 1)
+            p.fdot(pr, vmat, V(att.off + hh * hd * 4, n, hd, att.ld), nn=True)
+        aqs = p.quant(att) if self.wbits == 8 else None
+        o = p.mat(n, self.H)
+        self._linear_k(att, w["o"], aqs, o)
+        if w.get("attn_norm") is not None:
+            on = p.mat(n, self.H)
+            p.norm(o, w["attn_norm"], self.eps, on)
+            o = on
+        x1 = p.mat(n, self.H)
+        p.elt(C.ELT_ADD, x, o, x1)
+        self._mlp(w, x1, out)
+
+    # ------------------------------------------------------------------ running chunk by chunk
+    def stage(self, ddr: bytearray, a: int, b: int) -> tuple[int, int]:
+        assert self.qbase is not None and b - a <= self.queue_cap, "queue_cap too small"
+        q = self.p.base + self.qbase
+        for i in range(a, b):
+            ddr[q + 64 * (i - a):q + 64 * (i - a + 1)] = self.p.descs[i]
+        return q, b - a
+
+    def put_input(self, ddr: bytearray, t0: int, x: np.ndarray) -> None:
+        a = self.p.base + self.x0.off + t0 * self.x0.ld
+        ddr[a:a + x.size * 4] = np.asarray(x, F32).tobytes()
+
+    def logits_of(self, ddr) -> np.ndarray:
+        a = self.p.base + self.logits.off
+        return np.frombuffer(bytes(ddr[a:a + 4 * self.vocab]), "<f4").copy()
+
+    def logits_rows(self, ddr, n: int) -> np.ndarray:
+        a = self.p.base + self.logits.off
+        flat = np.frombuffer(bytes(ddr[a:a + 4 * self.vocab * n]), "<f4")
+        out, c0 = np.empty((n, self.vocab), F32), 0
+        for lin in self.head_lins:
+            out[:, c0:c0 + lin.n] = flat[c0 * n:(c0 + lin.n) * n].reshape(n, lin.n)
+            c0 += lin.n
+        return out
+
+    def generate(self, run, prompt, n_new: int, chunk: int = 0):
+        """Greedy decoding with the host in the loop: run(ddr, q, n) -> ddr executes one chunk's
+        queue. chunk > 0 feeds the prompt in chunks of that many tokens (the board runtime's
+        prefill); 0 feeds it whole (llm.py:815-836). Returns (ids, logits per run, descriptors per run)."""
+        assert self.head
+        ddr = self.p.ddr
+        ids, logits, counts = list(prompt), [], []
+        spans = [(s, min(chunk, len(prompt) - s)) for s in range(0, len(prompt), chunk)] if chunk else \
+            [(0, len(prompt))]
+        for i in range(len(spans) + n_new):
+            t0, n = spans[i] if i < len(spans) else (len(ids) - 1, 1)
+            self.put_input(ddr, t0, self.embed(ids[t0:t0 + n]))
+            a = len(self.p.descs)
+            self.chunk(t0, n)
+            q, cnt = self.stage(ddr, a, len(self.p.descs))
+            out = run(ddr, q, cnt)
+            ddr = out if isinstance(out, bytearray) else bytearray(out)
+            if i >= len(spans) - 1:
+                lg = self.logits_of(ddr)
+                logits.append(lg)
+                counts.append(cnt)
+                ids.append(int(np.argmax(lg)))
+        return ids, logits, counts

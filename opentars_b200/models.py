@@ -1,0 +1,146 @@
+"""Host model data for the lowering: configs, seeded random weights, weight quantisers.
+
+Restates, for the model families on the hot path (Qwen3 and Gemma 3 text models):
+  * make_config          tars_mini/qwen_ref.py:109-146 (transformers config objects)
+  * random_weights       qwen_ref.py:165-198 (same generator, same draw order: the model's state_dict)
+  * head_rows            qwen_ref.py:371-378 (the vocabulary in the fewest equal blocks <= 65535 rows)
+  * quantize_weight      tars_mini/compiler.py:51-57 (per-channel symmetric INT8, float64 then fp32)
+  * quantize_weight4     compiler.py:69-85 (group-128 INT4 with binary16 scales)
+  * input_embedding      tars_mini/llm.py:198-204
+The host quantisers define data, not device arithmetic: they run once when an image is built.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+F32 = np.float32
+W4_GROUP = 128
+
+VOCAB_Q3_06B = 151936
+CFG_Q3_06B = dict(model_type="qwen3", hidden_size=1024, intermediate_size=3072, num_attention_heads=16,
+                  num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6, vocab_size=16,
+                  max_position_embeddings=40960, num_hidden_layers=28,
+                  rope_parameters=dict(rope_type="default", rope_theta=1000000.0))
+CFG_Q3_SMALL = dict(CFG_Q3_06B, hidden_size=256, intermediate_size=512, num_attention_heads=4,
+                    num_key_value_heads=2, head_dim=64)
+VOCAB_G3_1B = 262144
+LAYERS_G3_1B = (["sliding_attention"] * 5 + ["full_attention"]) * 4 + ["sliding_attention"] * 2
+CFG_G3_1B = dict(model_type="gemma3_text", hidden_size=1152, intermediate_size=6912, num_attention_heads=4,
+                 num_key_value_heads=1, head_dim=256, query_pre_attn_scalar=256, rms_norm_eps=1e-6, vocab_size=16,
+                 sliding_window=512, hidden_activation="gelu_pytorch_tanh", max_position_embeddings=32768,
+                 attn_logit_softcapping=None, final_logit_softcapping=None,
+                 rope_parameters={"full_attention": dict(rope_type="default", rope_theta=1000000.0),
+                                  "sliding_attention": dict(rope_type="default", rope_theta=10000.0)})
+CFG_G3_SMALL = dict(CFG_G3_1B, hidden_size=256, intermediate_size=512, num_attention_heads=4,
+                    num_key_value_heads=2, head_dim=64, query_pre_attn_scalar=64, sliding_window=64)
+
+
+def make_config(base: dict, layer_types: list[str] | None = None, vocab: int | None = None):
+    """A transformers config for a Qwen3 or Gemma 3 text model (tied embeddings, eager attention)."""
+    b = {k: v for k, v in base.items() if k != "model_type"}
+    if base.get("model_type") == "gemma3_text":
+        from transformers.models.gemma3.configuration_gemma3 import Gemma3TextConfig
+        lt = list(layer_types or ["sliding_attention", "full_attention"])
+        cfg = Gemma3TextConfig(**dict(b, vocab_size=vocab or b["vocab_size"], tie_word_embeddings=True),
+                               num_hidden_layers=len(lt), layer_types=lt)
+    elif base.get("model_type") == "qwen3":
+        from transformers.models.qwen3.configuration_qwen3 import Qwen3Config
+        n = len(layer_types) if layer_types else b.pop("num_hidden_layers")
+        b.pop("num_hidden_layers", None)
+        cfg = Qwen3Config(**dict(b, vocab_size=vocab or b["vocab_size"], tie_word_embeddings=True),
+                          num_hidden_layers=n, layer_types=["full_attention"] * n)
+    else:
+        raise ValueError(f"model type {base.get('model_type')!r} is not on this path (Qwen3, Gemma 3)")
+    cfg._attn_implementation = "eager"
+    return cfg
+
+
+def param_shapes(cfg) -> list[tuple[str, tuple[int, ...]]]:
+    """The model's parameters (name, shape) in state_dict order, built on the meta device."""
+    import torch
+    if cfg.model_type == "qwen3":
+        from transformers.models.qwen3.modeling_qwen3 import Qwen3Model as Model
+    else:
+        from transformers.models.gemma3.modeling_gemma3 import Gemma3TextModel as Model
+    with torch.device("meta"):
+        m = Model(cfg)
+    return [(n, tuple(p.shape)) for n, p in m.state_dict().items()]
+
+
+def random_weights(cfg, seed: int = 0, embed: bool = False) -> dict[str, np.ndarray]:
+    """Linears N(0, 0.02) with 2 % of the output rows x4; norms 1 + N(0, 0.1) (Qwen3) or N(0, 0.1)
+    (Gemma 3, zero-centred); with `embed` the tied embedding N(0, 0.02), drawn 8192 rows at a time."""
+    rng = np.random.default_rng(seed)
+    w = {}
+    for name, shape in param_shapes(cfg):
+        if name.startswith("embed_tokens"):
+            if embed:
+                e = np.empty(shape, np.float32)
+                for r in range(0, shape[0], 8192):
+                    e[r:r + 8192] = rng.normal(0, 0.02, (min(8192, shape[0] - r), shape[1]))
+                w[name] = e
+            continue
+        if len(shape) == 2:
+            a = rng.normal(0, 0.02, shape) * np.where(rng.random(shape[0]) < 0.02, 4.0, 1.0)[:, None]
+        elif cfg.model_type == "qwen3":
+            a = 1 + rng.normal(0, 0.1, shape)
+        else:
+            a = rng.normal(0, 0.1, shape)
+        w[name] = a.astype(np.float32)
+    return w
+
+
+def head_rows(vocab: int) -> int:
+    for b in range(1, vocab // 16 + 1):
+        r = vocab // b
+        if vocab % b == 0 and r <= 65535 and r % 16 == 0:
+            return r
+    raise ValueError(f"vocabulary {vocab}: no block split")
+
+
+def input_embedding(cfg, rows: np.ndarray) -> np.ndarray:
+    """Gemma scales embedding rows by fp32(sqrt(hidden)), one fp32 rounding."""
+    rows = np.asarray(rows, F32)
+    if getattr(cfg, "model_type", "") != "gemma3_text":
+        return rows
+    return (rows * F32(cfg.hidden_size ** 0.5)).astype(F32)
+
+
+@dataclass
+class QWeight:
+    q: np.ndarray            # int8 [N, K]
+    scale: np.ndarray        # fp32 [N] or [1]
+    n: int
+    k: int
+
+
+def quantize_weight(w: np.ndarray, per_channel: bool = True) -> QWeight:
+    w = np.asarray(w, dtype=np.float64)
+    amax = np.abs(w).max(axis=1) if per_channel else np.array([np.abs(w).max()])
+    s = np.where(amax > 0, amax / 127.0, 1.0)
+    q = np.clip(np.rint(w / (s[:, None] if per_channel else s[0])), -127, 127).astype(np.int8)
+    return QWeight(q=q, scale=s.astype(np.float32), n=w.shape[0], k=w.shape[1])
+
+
+@dataclass
+class QWeight4:
+    q: np.ndarray            # uint8 [N, K / 2], low nibble = even k
+    scale: np.ndarray        # uint16 [N, K / 128], binary16 bits
+    n: int
+    k: int
+
+
+def quantize_weight4(w: np.ndarray) -> QWeight4:
+    w = np.asarray(w, dtype=np.float64)
+    if w.ndim != 2 or w.shape[1] == 0 or w.shape[1] % W4_GROUP:
+        raise ValueError("W4A16 weights need [N, K], K a nonzero multiple of 128")
+    n, k = w.shape
+    groups = w.reshape(n, k // W4_GROUP, W4_GROUP)
+    amax = np.abs(groups).max(axis=2)
+    sb = np.where(amax > 0, amax / 7.0, 1.0).astype(np.float32).astype(np.float16)
+    s = sb.astype(np.float32).astype(np.float64)
+    q = np.clip(np.rint(groups / s[:, :, None]), -7, 7).astype(np.int16)
+    packed = ((q[:, :, 0::2] & 15) | ((q[:, :, 1::2] & 15) << 4)).astype(np.uint8)
+    return QWeight4(packed.reshape(n, k // 2), sb.view(np.uint16), n, k)

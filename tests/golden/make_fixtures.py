@@ -196,11 +196,69 @@ def make_models(ref: str):
     return out
 
 
+# name, base config, layer types (None: the model's own), prompt seed, new tokens, prefill chunk
+FULL_CASES = [
+    ("qwen3_0.6b", "CFG_Q3_06B", None, "VOCAB_Q3_06B", 0, 3, 4),
+    ("gemma3_1b", "CFG_G3_1B", "LAYERS_G3_1B", "VOCAB_G3_1B", 0, 2, 4),
+]
+
+
+def prompt_ids(seed: int, vocab: int, n: int = 20) -> list[int]:
+    """The seeded prompt of configs 3 / 4: n token ids uniform over the vocabulary."""
+    return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, n)]
+
+
+def make_full_models(ref: str, only: str = ""):
+    """Full-size models, one sequence: the prompt in prefill chunks of 4, then greedy decode. Each
+    chunk is staged and run through the reference's golden Machine exactly as its generate()
+    does, with the prompt split as the board runtime prefills it."""
+    import tars_mini.qwen_ref as Q
+    from tars_mini import golden as G
+    from tars_mini.llm import QwenLowering
+    out = {}
+    for name, base, types, vocab_name, seed, new, chunk in FULL_CASES:
+        if only and only != name:
+            continue
+        t = time.time()
+        vocab = getattr(Q, vocab_name)
+        cfg = Q.make_config(getattr(Q, base), list(getattr(Q, types)) if types else None, vocab=vocab)
+        w = Q.random_weights(cfg, seed=0, embed=True)
+        low = QwenLowering(cfg, w, max_tokens=256, ddr_bytes=3 << 29, head=True, queue_cap=8192)
+        image_sha = hashlib.sha256(bytes(low.p.ddr)).hexdigest()
+        build_s = time.time() - t
+        prompt = prompt_ids(seed, vocab)
+        ddr, ids, rec = low.p.ddr, list(prompt), []
+        spans = [(s, min(chunk, len(prompt) - s)) for s in range(0, len(prompt), chunk)]
+        for i in range(len(spans) + new):
+            t0, n = spans[i] if i < len(spans) else (len(ids) - 1, 1)
+            low.put_input(ddr, t0, low.embed(ids[t0:t0 + n]))
+            a = len(low.p.descs)
+            low.chunk(t0, n)
+            q, cnt = low.stage(ddr, a, len(low.p.descs))
+            qsha = hashlib.sha256(bytes(ddr[q:q + 64 * cnt])).hexdigest()
+            ts = time.time()
+            m = G.Machine(ddr)
+            assert m.run_queue(q, cnt).done
+            ddr = m.ddr
+            r = dict(t0=t0, n=n, count=cnt, queue_sha256=qsha, golden_s=round(time.time() - ts, 2))
+            if i >= len(spans) - 1:
+                lg = low.logits_of(ddr)
+                ids.append(int(np.argmax(lg)))
+                r.update(logits_sha256=hashlib.sha256(lg.astype("<f4").tobytes()).hexdigest(),
+                         logits_head=lg[:8].view(np.uint32).tolist(), argmax=ids[-1])
+            rec.append(r)
+            print(name, r, flush=True)
+        out[name] = dict(base=base, types=types, vocab=vocab, T=256, prompt=prompt, chunk=chunk, new=new,
+                         image_sha256=image_sha, ids=ids, runs=rec, build_s=round(build_s, 1))
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("OPENTARS_REF", ""), required=False)
     ap.add_argument("--models", action="store_true")
     ap.add_argument("--skip-queues", action="store_true")
+    ap.add_argument("--full", default="", help="full-size models: 'all' or one name")
     a = ap.parse_args()
     if not a.ref:
         raise SystemExit("--ref <path to the openTARS checkout> is required")
@@ -216,6 +274,12 @@ def main():
         m = make_models(a.ref)
         (HERE / "models.json").write_text(json.dumps(m, indent=1))
         print(f"models in {time.time() - t:.1f}s")
+    if a.full:
+        path = HERE / "full_models.json"
+        old = json.loads(path.read_text()) if path.exists() else {}
+        old.update(make_full_models(a.ref, "" if a.full == "all" else a.full))
+        path.write_text(json.dumps(old, indent=1))
+        print(f"full models in {time.time() - t:.1f}s")
 
 
 if __name__ == "__main__":

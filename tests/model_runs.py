@@ -1,0 +1,68 @@
+"""Shared drivers for the model-level parity tests: build a fixture's model with the package's
+lowering and run its greedy decode through a given backend."""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+
+
+def build_lowering(fx: dict, full: bool = False):
+    from opentars_b200 import models as Mo
+    from opentars_b200.lowering import QwenLowering
+    if full:
+        base = getattr(Mo, fx["base"])
+        types = list(getattr(Mo, fx["types"])) if fx["types"] else None
+        cfg = Mo.make_config(base, types, vocab=fx["vocab"])
+        w = Mo.random_weights(cfg, seed=0, embed=True)
+        return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=3 << 29, head=True, queue_cap=8192)
+    base = dict(Mo.CFG_G3_SMALL, intermediate_size=4608) if fx["base"] == "G3_SMALL_K2" else getattr(Mo, fx["base"])
+    cfg = Mo.make_config(base, fx["types"], vocab=fx["vocab"])
+    w = Mo.random_weights(cfg, seed=0, embed=True)
+    return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096)
+
+
+def sha(a) -> str:
+    return hashlib.sha256(bytes(a)).hexdigest()
+
+
+def logits_sha(lg: np.ndarray) -> str:
+    return hashlib.sha256(np.asarray(lg, "<f4").tobytes()).hexdigest()
+
+
+def machine_runner(machine_cls, queues: list, gemv_only: bool = True):
+    def run(ddr, q, n):
+        queues.append(sha(ddr[q:q + 64 * n]))
+        m = machine_cls(ddr, gemv_only=gemv_only)
+        assert m.run_queue(q, n).done
+        return m.ddr
+    return run
+
+
+class BoardRunner:
+    """run(ddr, q, n) over the board backend: the image uploaded once, then per run only the
+    input rows and the queue go up and the logits come back (as the board runtime moves data)."""
+
+    def __init__(self, low, graphs: bool = True):
+        from opentars_b200.board import Cuda
+        self.low = low
+        self.dev = Cuda(len(low.p.ddr), graphs=graphs, gemv_only=True)
+        self.dev.mem[:] = np.frombuffer(bytes(low.p.ddr), np.uint8)
+        self.dev.to_dev(0, len(low.p.ddr))
+        self.queues = []
+
+    def __call__(self, ddr, q, n):
+        low, dev = self.low, self.dev
+        x0, ld, T = low.p.base + low.x0.off, low.x0.ld, low.T
+        dev.mem[x0:x0 + ld * T] = np.frombuffer(bytes(ddr[x0:x0 + ld * T]), np.uint8)
+        dev.to_dev(x0, ld * T)
+        dev.mem[q:q + 64 * n] = np.frombuffer(bytes(ddr[q:q + 64 * n]), np.uint8)
+        dev.to_dev(q, 64 * n)
+        self.queues.append(sha(ddr[q:q + 64 * n]))
+        done, err, op, _ = dev.run(q, n)
+        assert done, (err, op)
+        la = low.p.base + low.logits.off
+        nb = 4 * low.vocab * low.verify_rows
+        dev.from_dev(la, nb)
+        ddr[la:la + nb] = dev.mem[la:la + nb].tobytes()
+        return ddr

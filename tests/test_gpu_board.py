@@ -55,3 +55,25 @@ def test_graph_replay_is_idempotent_and_sees_new_inputs():
         assert dev.mem[0x40000:0x40000 + 2 * 4 * 3072].tobytes() == bytes(o.ddr[0x40000:0x40000 + 2 * 4 * 3072])
     assert len(dev._cache) == 1
     dev.close()
+
+
+def test_captured_queue_reports_per_descriptor_times():
+    import ctypes
+
+    from __graft_entry__ import _gemv_program
+    from opentars_b200._lib import Status_t, lib
+    from opentars_b200.board import Cuda
+    ddr, qa, n = _gemv_program(seed=4)
+    dev = Cuda(len(ddr))
+    dev.mem[:] = np.frombuffer(bytes(ddr), np.uint8)
+    dev.to_dev(0, len(ddr))
+    L = lib()
+    st, cop, g = Status_t(), ctypes.c_int32(-1), ctypes.c_void_p()
+    assert L.tc_queue_capture(dev.h, qa, n, 0, 0, 1, ctypes.byref(st), ctypes.byref(cop), ctypes.byref(g)) == 0
+    assert st.done and st.op_idx == n
+    assert L.tc_graph_launch(g, None) == 0 and L.tc_synchronize(dev.h) == 0
+    ms = (ctypes.c_float * n)()
+    assert L.tc_graph_times(g, ms, n) == n
+    assert all(0 < ms[i] < 100 for i in range(n))
+    L.tc_graph_destroy(g)
+    dev.close()

@@ -1,0 +1,33 @@
+"""The package's lowering (opentars_b200.lowering) against the reference's own lowering + golden
+model (committed fixtures): identical DDR image, identical descriptor queues, identical logits,
+run here through the CPU oracle."""
+import numpy as np
+import pytest
+
+from tests import fixtures as FX
+from tests.model_runs import build_lowering, logits_sha, machine_runner, sha
+
+
+@pytest.mark.parametrize("name", sorted(FX.models()))
+def test_lowering_matches_reference_small_models(name):
+    from oracle.machine import OracleMachine
+    fx = FX.models()[name]
+    low = build_lowering(fx)
+    assert sha(low.p.ddr) == fx["image_sha256"]
+    queues = []
+    ids, logits, counts = low.generate(machine_runner(OracleMachine, queues), fx["prompt"], fx["new"])
+    assert queues == fx["queue_sha256"] and counts == fx["counts"]
+    assert ids == fx["ids"]
+    assert [logits_sha(lg) for lg in logits] == fx["logits_sha256"]
+
+
+def test_chunked_prefill_equals_whole_prompt_logits():
+    """Prefill in chunks of 4 ends at the same last-token logits as one prompt chunk (the
+    reference pins chunk == single steps, test_v04.py:370-422)."""
+    from oracle.machine import OracleMachine
+    fx = FX.models()["qwen3_small"]
+    a, b = build_lowering(fx), build_lowering(fx)
+    ids1, lg1, _ = a.generate(machine_runner(OracleMachine, []), fx["prompt"], 2)
+    ids2, lg2, _ = b.generate(machine_runner(OracleMachine, []), fx["prompt"], 2, chunk=4)
+    assert ids1 == ids2
+    assert all(np.array_equal(x.view(np.uint32), y.view(np.uint32)) for x, y in zip(lg1, lg2))
