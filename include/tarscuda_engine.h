@@ -1,0 +1,69 @@
+/* libtarscuda decode engine: B independent sequences of a Qwen3 / Gemma 3 model decoded together
+ * on one B200, bit-exact per sequence with the descriptor path (and so with the reference's golden
+ * model).
+ *
+ * Replaces, for a whole batch, the per-token loop of the reference's QwenLowering.generate
+ * (tars_mini/llm.py:815-836: host embedding lookup, run(ddr, q, n) of the chunk's queue, argmax of
+ * the logits) and of the board runtime's Qwen.step / prefill (deploy/kv260/sw/tars_board.py:
+ * 400-435). The weights are the DDR image that the lowering built (QwenLowering, llm.py:213-476),
+ * opened with tc_open/tc_upload; the model description gives the image offsets of every layer's
+ * tensors (the lowering's QLin / V records).
+ */
+#ifndef TARSCUDA_ENGINE_H
+#define TARSCUDA_ENGINE_H
+#include <stdint.h>
+
+#include "tarscuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct tc_engine tc_engine;
+
+/* One W8A8 linear in the image: int8 rows [n, k] at w_off, fp32 per-row scales at s_off (llm.py:181-188). */
+typedef struct { uint64_t w_off, s_off; int32_t n, k; } tc_lin;
+
+/* One full-attention layer (llm.py:365-418): norm gammas (0 = absent: Gemma 3 has attn_norm and
+ * mlp_norm, Qwen3 not), q/k head-norm gammas (q's with the attention scaling folded in), the RoPE
+ * table of the layer's type, the linears; down in n_down K blocks sharing one scale (llm.py:303-321). */
+typedef struct {
+  uint64_t ln_in, ln_post, attn_norm, mlp_norm, qn, kn, rope_tab;
+  tc_lin q, k, v, o, gate, up;
+  tc_lin down[4];
+  int32_t n_down;
+} tc_layer_desc;
+
+typedef struct {
+  int32_t n_layers, hidden, inter, n_heads, n_kv, head_dim, rot, vocab, max_tokens;
+  int32_t act;            /* the gate's activation code: 4 SiLU (Qwen3), 3 tanh GELU (Gemma 3) */
+  int32_t gemma;          /* Gemma 3: scaled embedding, attn_norm / mlp_norm */
+  float eps, embed_scale;  /* the RMSNorm epsilon as fp32; Gemma's embedding scale fp32(sqrt(hidden)) */
+  uint64_t final_norm;
+  int32_t n_head_blocks;
+  tc_lin head[8];         /* the tied head in row blocks of <= 65535 (qwen_ref.py:371-378) */
+} tc_model_desc;
+
+/* A decode engine over the weights in `image` for `batch` sequences; uploads the fp32 embedding
+ * table [vocab][hidden] from embed_host; KV caches zeroed, position 0. */
+int tc_engine_create(tc_machine* image, const tc_model_desc* md, const tc_layer_desc* layers,
+                     const float* embed_host, int32_t batch, tc_engine** out);
+int tc_engine_destroy(tc_engine* e);
+const char* tc_engine_error(tc_engine* e);
+void* tc_engine_stream(tc_engine* e);
+/* Zeroes every KV cache and the position (a new batch of conversations). */
+int tc_engine_reset(tc_engine* e);
+/* One chunk of n (1..4) tokens per sequence: tokens_host [batch][n] ids, or NULL to feed each
+ * sequence's greedy pick of the previous chunk (n = 1). Enqueued on the engine's stream. */
+int tc_engine_step(tc_engine* e, const int32_t* tokens_host, int32_t n);
+/* The next token of each sequence (np.argmax of its last logits row) into / from the host. */
+int tc_engine_tokens(tc_engine* e, int32_t* tokens_host);
+int tc_engine_set_tokens(tc_engine* e, const int32_t* tokens_host);
+/* Each sequence's logits of its last token [batch][vocab]. */
+int tc_engine_logits(tc_engine* e, float* logits_host);
+int tc_engine_sync(tc_engine* e);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,326 @@
+// The batched decode engine (host side): resident model, per-sequence KV caches, one CUDA graph
+// per chunk length, a device-side position counter and greedy pick.
+//
+// It replaces, for B sequences at once, the per-step path of the reference's QwenLowering.generate
+// (tars_mini/llm.py:815-836) and the board runtime's Qwen.step / prefill (deploy/kv260/sw/
+// tars_board.py:400-435): embedding lookup, every layer, the final norm, the head and the argmax
+// run on the GPU; the host only moves token ids (and logits when asked). The weights are read
+// from the DDR image the lowering laid out (the same bytes the descriptor path executes).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/tarscuda.h"
+#include "../../include/tarscuda_engine.h"
+#include "engine.h"
+
+using namespace tc;
+
+struct tc_machine;
+extern "C" uint64_t tc_device_ptr(tc_machine* m);
+
+namespace {
+struct Lin { const int8_t* W; const float* s; int n, k; };
+struct Layer {
+  const float *ln_in, *ln_post, *attn_norm, *mlp_norm, *qn, *kn, *tab;
+  Lin q, k, v, o, gate, up;
+  Lin down[4];
+  int n_down;
+};
+}  // namespace
+
+struct tc_engine {
+  int device = 0;
+  cudaStream_t st = nullptr;
+  tc_model_desc md{};
+  std::vector<Layer> layers;
+  std::vector<Lin> head;
+  const float* final_norm = nullptr;
+  int B = 0, T = 0, Tp = 0, nmax = 4, H = 0, I = 0, qw = 0, kvw = 0;
+  // device buffers
+  float* E = nullptr;                       // fp32 embedding table [vocab][H]
+  int *tok = nullptr, *next = nullptr, *pos = nullptr;
+  float *x = nullptr, *x1 = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *att = nullptr;
+  float *o = nullptr, *g = nullptr, *d = nullptr, *logits = nullptr;
+  int8_t* q8 = nullptr;                      // quantised rows [M][max(H, I, qw)]
+  float* qs = nullptr;
+  float *kc = nullptr, *vc = nullptr;        // [L][B][Tp][kvw]
+  cudaGraphExec_t graph[5] = {};
+  std::string err;
+};
+
+namespace {
+int fail(tc_engine* e, const char* what, cudaError_t c) {
+  e->err = std::string(what) + ": " + cudaGetErrorString(c);
+  return TC_ERR_CUDA;
+}
+#define TRY(expr)                                   \
+  do {                                              \
+    cudaError_t _c = (expr);                        \
+    if (_c != cudaSuccess) return fail(e, #expr, _c); \
+  } while (0)
+
+Lin lin_of(const uint8_t* base, const tc_lin& l) {
+  return Lin{(const int8_t*)(base + l.w_off), (const float*)(base + l.s_off), l.n, l.k};
+}
+const float* vec_of(const uint8_t* base, uint64_t off) { return off ? (const float*)(base + off) : nullptr; }
+
+EngGemvArgs gemv_args(const int8_t* A, uint64_t lda, const float* srow, int M, int K) {
+  EngGemvArgs g{};
+  g.A = A; g.lda = lda; g.srow = srow; g.M = M; g.K = K; g.kb = K;
+  return g;
+}
+void add_seg(EngGemvArgs& g, const Lin& l, float* out, uint64_t ldo) {
+  EngSeg& s = g.seg[g.nseg++];
+  s.W = l.W; s.scale = l.s; s.out = out; s.ldo = ldo; s.n0 = g.ncols; s.n = l.n;
+  g.ncols += l.n;
+}
+
+// Enqueues one step for chunks of n tokens per sequence, starting at the device position.
+int enqueue_step(tc_engine* e, int n, const int* tok_in) {
+  const tc_model_desc& md = e->md;
+  const int B = e->B, M = B * n, H = e->H, I = e->I, qw = e->qw, kvw = e->kvw;
+  const int ldq = std::max(std::max(H, I), qw);
+  cudaStream_t st = e->st;
+  TRY(eng_embed(e->E, tok_in, e->x, H, md.gemma, md.embed_scale, M, st));
+  const float eps = md.eps;
+  for (int li = 0; li < md.n_layers; ++li) {
+    const Layer& L = e->layers[li];
+    float* kc = e->kc + (uint64_t)li * B * e->Tp * kvw;
+    float* vc = e->vc + (uint64_t)li * B * e->Tp * kvw;
+    // ln_in + quant (for li > 0 on Gemma this was fused into the previous layer's tail)
+    if (li == 0 || !md.gemma) {
+      NormQuantArgs a{};
+      a.in = e->x; a.ld_in = H; a.gamma = L.ln_in; a.eps = eps; a.q = e->q8; a.ldq = ldq; a.qs = e->qs;
+      a.H = H; a.rows = M; a.mode = 0;
+      TRY(eng_norm_quant(a, st));
+    }
+    {  // q | k | v
+      EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, M, H);
+      add_seg(g, L.q, e->q, qw);
+      add_seg(g, L.k, e->k, kvw);
+      add_seg(g, L.v, e->v, kvw);
+      g.mode = kEpiStore;
+      TRY(eng_gemv(g, st));
+    }
+    {
+      QkRopeArgs a{};
+      a.q = e->q; a.k = e->k; a.v = e->v; a.qr = e->qr; a.kc = kc; a.vc = vc; a.qn = L.qn; a.kn = L.kn;
+      a.tab = L.tab; a.pos = e->pos; a.rows = M; a.n = n; a.nh = md.n_heads; a.nkv = md.n_kv; a.hd = md.head_dim;
+      a.rot = md.rot; a.Tp = e->Tp; a.eps = eps;
+      TRY(eng_qk_rope(a, st));
+    }
+    {
+      AttnArgs a{};
+      a.qr = e->qr; a.kc = kc; a.vc = vc; a.att = e->att; a.pos = e->pos; a.n = n; a.nh = md.n_heads;
+      a.nkv = md.n_kv; a.hd = md.head_dim; a.Tp = e->Tp;
+      TRY(eng_attention(a, B, st));
+    }
+    TRY(eng_quant(e->att, qw, qw, e->q8, ldq, e->qs, M, st));
+    {  // o; Qwen3 adds the residual in the epilogue
+      EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, M, qw);
+      add_seg(g, L.o, md.gemma ? e->o : e->x1, H);
+      if (md.gemma) g.mode = kEpiStore;
+      else { g.mode = kEpiResid; g.res = e->x; g.ldres = H; }
+      TRY(eng_gemv(g, st));
+    }
+    {  // [Gemma: attn_norm + residual] + ln_post + quant
+      NormQuantArgs a{};
+      a.eps = eps; a.q = e->q8; a.ldq = ldq; a.qs = e->qs; a.H = H; a.rows = M; a.gamma = L.ln_post;
+      if (md.gemma) { a.mode = 2; a.in = e->o; a.ld_in = H; a.pre_gamma = L.attn_norm; a.res = e->x; a.x_out = e->x1; }
+      else { a.mode = 0; a.in = e->x1; a.ld_in = H; }
+      TRY(eng_norm_quant(a, st));
+    }
+    {  // gate, up: act(gate) * up
+      EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, M, H);
+      add_seg(g, L.gate, e->g, I);
+      add_seg(g, L.up, e->g, I);
+      g.mode = kEpiGated;
+      g.act = md.act;
+      TRY(eng_gemv(g, st));
+    }
+    TRY(eng_quant(e->g, I, I, e->q8, ldq, e->qs, M, st));
+    {  // down (K blocks on Gemma); Qwen3 adds the residual into x
+      EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, M, I);
+      Lin dl = L.down[0];
+      if (L.n_down == 2) {
+        g.kb = L.down[0].k;
+        dl.k = I;
+      }
+      if (md.gemma) {
+        add_seg(g, dl, e->d, H);
+        g.mode = L.n_down == 2 ? kEpiKSplit : kEpiStore;
+      } else {
+        add_seg(g, dl, e->x, H);
+        g.mode = kEpiResid;
+        g.res = e->x1;
+        g.ldres = H;
+      }
+      if (L.n_down == 2) g.seg[0].W2 = L.down[1].W;   // the second K block's rows
+      TRY(eng_gemv(g, st));
+    }
+    if (md.gemma) {  // mlp_norm + residual, fused with the next layer's ln_in (or the final norm)
+      NormQuantArgs a{};
+      a.mode = 2; a.in = e->d; a.ld_in = H; a.pre_gamma = L.mlp_norm; a.res = e->x1; a.x_out = e->x;
+      a.gamma = li + 1 < md.n_layers ? e->layers[li + 1].ln_in : e->final_norm;
+      a.eps = eps; a.q = e->q8; a.ldq = ldq; a.qs = e->qs; a.H = H; a.rows = M;
+      TRY(eng_norm_quant(a, st));
+    }
+  }
+  {  // final norm + quant of each sequence's last row, the head, the greedy pick
+    NormQuantArgs a{};
+    a.mode = 0; a.in = e->x + (uint64_t)(n - 1) * H; a.ld_in = (uint64_t)n * H; a.gamma = e->final_norm;
+    a.eps = eps; a.q = e->q8; a.ldq = ldq; a.qs = e->qs; a.H = H; a.rows = B;
+    TRY(eng_norm_quant(a, st));
+    EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, B, H);
+    for (const Lin& l : e->head) {
+      EngSeg& s = g.seg[g.nseg++];
+      s.W = l.W; s.scale = l.s; s.out = e->logits + g.ncols; s.ldo = md.vocab; s.n0 = g.ncols; s.n = l.n;
+      g.ncols += l.n;
+    }
+    g.mode = kEpiStore;
+    TRY(eng_gemv(g, st));
+    TRY(eng_argmax(e->logits, md.vocab, B, e->next, 1, st));
+  }
+  TRY(eng_advance(e->pos, n, st));
+  return TC_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int tc_engine_create(tc_machine* image, const tc_model_desc* md, const tc_layer_desc* layers, const float* embed_host,
+                     int32_t batch, tc_engine** out) {
+  *out = nullptr;
+  tc_engine* e = new tc_engine();
+  e->md = *md;
+  const uint8_t* base = (const uint8_t*)(uintptr_t)tc_device_ptr(image);
+  e->B = batch;
+  e->T = md->max_tokens;
+  e->Tp = (md->max_tokens + 15) / 16 * 16;
+  e->H = md->hidden;
+  e->I = md->inter;
+  e->qw = md->n_heads * md->head_dim;
+  e->kvw = md->n_kv * md->head_dim;
+  if (md->n_head_blocks > kMaxSegs || md->head_dim > 256 || md->max_tokens > 256 || batch < 1) {
+    delete e;
+    return TC_ERR_ARG;
+  }
+  for (int i = 0; i < md->n_layers; ++i) {
+    const tc_layer_desc& ld = layers[i];
+    Layer L{};
+    L.ln_in = vec_of(base, ld.ln_in); L.ln_post = vec_of(base, ld.ln_post);
+    L.attn_norm = vec_of(base, ld.attn_norm); L.mlp_norm = vec_of(base, ld.mlp_norm);
+    L.qn = vec_of(base, ld.qn); L.kn = vec_of(base, ld.kn); L.tab = vec_of(base, ld.rope_tab);
+    L.q = lin_of(base, ld.q); L.k = lin_of(base, ld.k); L.v = lin_of(base, ld.v); L.o = lin_of(base, ld.o);
+    L.gate = lin_of(base, ld.gate); L.up = lin_of(base, ld.up);
+    L.n_down = ld.n_down;
+    for (int j = 0; j < ld.n_down; ++j) L.down[j] = lin_of(base, ld.down[j]);
+    e->layers.push_back(L);
+  }
+  for (int j = 0; j < md->n_head_blocks; ++j) e->head.push_back(lin_of(base, md->head[j]));
+  e->final_norm = vec_of(base, md->final_norm);
+  cudaGetDevice(&e->device);
+  const int M = e->B * e->nmax, ldq = std::max(std::max(e->H, e->I), e->qw);
+  auto alloc = [&](void** p, size_t n) { return cudaMalloc(p, std::max<size_t>(n, 16)); };
+  cudaError_t c = cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking);
+  if (c == cudaSuccess) c = alloc((void**)&e->E, (size_t)md->vocab * e->H * 4);
+  if (c == cudaSuccess) c = cudaMemcpy(e->E, embed_host, (size_t)md->vocab * e->H * 4, cudaMemcpyHostToDevice);
+  if (c == cudaSuccess) c = alloc((void**)&e->tok, (size_t)M * 4);
+  if (c == cudaSuccess) c = alloc((void**)&e->next, (size_t)e->B * 4);
+  if (c == cudaSuccess) c = alloc((void**)&e->pos, 4);
+  float** fbufs[] = {&e->x, &e->x1, &e->o, &e->d};
+  for (auto p : fbufs) if (c == cudaSuccess) c = alloc((void**)p, (size_t)M * e->H * 4);
+  if (c == cudaSuccess) c = alloc((void**)&e->q, (size_t)M * e->qw * 4);
+  if (c == cudaSuccess) c = alloc((void**)&e->qr, (size_t)M * e->qw * 4);
+  if (c == cudaSuccess) c = alloc((void**)&e->att, (size_t)M * e->qw * 4);
+  if (c == cudaSuccess) c = alloc((void**)&e->k, (size_t)M * e->kvw * 4);
+  if (c == cudaSuccess) c = alloc((void**)&e->v, (size_t)M * e->kvw * 4);
+  if (c == cudaSuccess) c = alloc((void**)&e->g, (size_t)M * e->I * 4);
+  if (c == cudaSuccess) c = alloc((void**)&e->logits, (size_t)e->B * md->vocab * 4);
+  if (c == cudaSuccess) c = alloc((void**)&e->q8, (size_t)M * ldq);
+  if (c == cudaSuccess) c = alloc((void**)&e->qs, (size_t)M * 4);
+  const size_t cache = (size_t)md->n_layers * e->B * e->Tp * e->kvw * 4;
+  if (c == cudaSuccess) c = alloc((void**)&e->kc, cache);
+  if (c == cudaSuccess) c = alloc((void**)&e->vc, cache);
+  if (c != cudaSuccess) {
+    tc_engine_destroy(e);
+    return TC_ERR_CUDA;
+  }
+  *out = e;
+  return tc_engine_reset(e);
+}
+
+int tc_engine_destroy(tc_engine* e) {
+  if (!e) return TC_OK;
+  if (e->st) cudaStreamSynchronize(e->st);
+  for (auto& gx : e->graph) if (gx) cudaGraphExecDestroy(gx);
+  void* bufs[] = {e->E, e->tok, e->next, e->pos, e->x, e->x1, e->q, e->k, e->v, e->qr, e->att, e->o, e->g, e->d,
+                  e->logits, e->q8, e->qs, e->kc, e->vc};
+  for (void* p : bufs) if (p) cudaFree(p);
+  if (e->st) cudaStreamDestroy(e->st);
+  delete e;
+  return TC_OK;
+}
+
+const char* tc_engine_error(tc_engine* e) { return e ? e->err.c_str() : ""; }
+void* tc_engine_stream(tc_engine* e) { return (void*)e->st; }
+
+int tc_engine_reset(tc_engine* e) {
+  const size_t cache = (size_t)e->md.n_layers * e->B * e->Tp * e->kvw * 4;
+  TRY(cudaMemsetAsync(e->kc, 0, cache, e->st));
+  TRY(cudaMemsetAsync(e->vc, 0, cache, e->st));
+  TRY(cudaMemsetAsync(e->pos, 0, 4, e->st));
+  TRY(cudaStreamSynchronize(e->st));
+  return TC_OK;
+}
+
+// Runs one chunk of n tokens per sequence (tokens_host: [B][n] ids, or NULL to feed each
+// sequence's greedy pick of the previous step, n = 1). The step is captured as a CUDA graph on
+// first use for that n and replayed afterwards; the position advances on the device.
+int tc_engine_step(tc_engine* e, const int32_t* tokens_host, int32_t n) {
+  if (n < 1 || n > e->nmax || (!tokens_host && n != 1)) { e->err = "bad chunk"; return TC_ERR_ARG; }
+  const int* src = e->next;
+  if (tokens_host) {
+    TRY(cudaMemcpyAsync(e->tok, tokens_host, (size_t)e->B * n * 4, cudaMemcpyHostToDevice, e->st));
+    src = e->tok;
+  }
+  const int slot = tokens_host ? n : 0;
+  if (!e->graph[slot]) {
+    cudaGraph_t graph;
+    TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeRelaxed));
+    const int rc = enqueue_step(e, n, src);
+    cudaError_t c = cudaStreamEndCapture(e->st, &graph);
+    if (rc != TC_OK) return rc;
+    if (c != cudaSuccess) return fail(e, "end capture", c);
+    c = cudaGraphInstantiate(&e->graph[slot], graph, 0);
+    cudaGraphDestroy(graph);
+    if (c != cudaSuccess) return fail(e, "instantiate", c);
+  }
+  TRY(cudaGraphLaunch(e->graph[slot], e->st));
+  return TC_OK;
+}
+
+int tc_engine_set_tokens(tc_engine* e, const int32_t* tokens_host) {
+  TRY(cudaMemcpyAsync(e->next, tokens_host, (size_t)e->B * 4, cudaMemcpyHostToDevice, e->st));
+  return TC_OK;
+}
+int tc_engine_tokens(tc_engine* e, int32_t* tokens_host) {
+  TRY(cudaMemcpyAsync(tokens_host, e->next, (size_t)e->B * 4, cudaMemcpyDeviceToHost, e->st));
+  TRY(cudaStreamSynchronize(e->st));
+  return TC_OK;
+}
+int tc_engine_logits(tc_engine* e, float* logits_host) {
+  TRY(cudaMemcpyAsync(logits_host, e->logits, (size_t)e->B * e->md.vocab * 4, cudaMemcpyDeviceToHost, e->st));
+  TRY(cudaStreamSynchronize(e->st));
+  return TC_OK;
+}
+int tc_engine_sync(tc_engine* e) {
+  TRY(cudaStreamSynchronize(e->st));
+  return TC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,428 @@
+// The batched decode engine's kernels (Qwen3 / Gemma 3 full-attention layers), sm_100a.
+//
+// The engine runs the step that QwenLowering.chunk lowers to descriptors (tars_mini/llm.py:548-571,
+// 582-593, 614-640, 705-782) for B independent sequences at once: every row-wise op and every
+// GEMM takes the B sequences' rows together (one weight stream for the whole batch), attention
+// runs per (sequence, query head) on that sequence's own KV cache. Each kernel computes exactly
+// the values the descriptors would write (same steps, same rounding, same reduction orders), so
+// each sequence's logits equal the golden model's for that sequence alone, bit for bit. Rows are
+// ordered sequence-major: row r = b * n + m is token t0 + m of sequence b.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "engine.h"
+#include "fp32.cuh"
+
+namespace tc {
+namespace {
+
+constexpr int kT = 256;
+
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float sum16_fold(float v, unsigned mask = 0xFFFFFFFFu) {
+  v = fadd(v, __shfl_xor_sync(mask, v, 1));
+  v = fadd(v, __shfl_xor_sync(mask, v, 2));
+  v = fadd(v, __shfl_xor_sync(mask, v, 4));
+  v = fadd(v, __shfl_xor_sync(mask, v, 8));
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmax_c(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) r = fmax_c(r, red[i]);
+  return r;
+}
+// sum16 of v[0..N) (shared memory) in the contract's order, broadcast to the block
+__device__ __forceinline__ float block_sum16(const float* v, int N, float* red) {
+  __syncthreads();
+  if (threadIdx.x < 16) {
+    float acc = 0.0f;
+    for (int j = threadIdx.x; j < N; j += 16) acc = fadd_nc(acc, v[j]);
+    acc = sum16_fold(canon(acc), 0x0000FFFFu);
+    if (threadIdx.x == 0) red[32] = acc;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// ------------------------------------------------------------------------------- embedding
+// x[r] = E[tok[r]] (Gemma: times fp32(sqrt(H)) in IEEE fp32, as the host's numpy does), llm.py:198-204
+__global__ void k_embed(const float* E, const int* tok, float* x, int H, int scale_on, float scale, int rows) {
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  const float* e = E + (uint64_t)tok[r] * H;
+  for (int j = threadIdx.x; j < H; j += blockDim.x) x[(uint64_t)r * H + j] = scale_on ? __fmul_rn(e[j], scale) : e[j];
+}
+
+// ------------------------------------------------------------------------------- row kernels
+// Optional pre-step, then RMSNorm(x, gamma) and ROW_QUANT of the normalised row:
+//   mode 0: x = in                                          (a layer's ln_in, the final norm)
+//   mode 1: x = fadd(res, in)          and x is written out (Qwen3: after o / down)
+//   mode 2: x = fadd(res, rmsnorm(in, pre_gamma)), written   (Gemma 3: attn_norm / mlp_norm)
+// Outputs the int8 row and its row scale (llm.py:97-104, numerics.py:353-390).
+__global__ void __launch_bounds__(256) k_norm_quant(NormQuantArgs a) {
+  extern __shared__ float sm[];
+  float* sx = sm;
+  float* sv = sm + a.H;
+  __shared__ float red[33];
+  const int r = blockIdx.x, H = a.H, t = threadIdx.x;
+  const float kinv = recip_f(i2f(H));
+  const float* in = a.in + (uint64_t)r * a.ld_in;
+  for (int j = t; j < H; j += blockDim.x) sx[j] = ftz(in[j]);
+  if (a.mode == 2) {
+    __syncthreads();
+    for (int j = t; j < H; j += blockDim.x) sv[j] = fmul(sx[j], sx[j]);
+    const float s = block_sum16(sv, H, red);
+    const float rs = rsqrt_f(fadd(fmul(s, kinv), a.eps));
+    for (int j = t; j < H; j += blockDim.x) sx[j] = ftz(fmul(fmul(sx[j], rs), a.pre_gamma[j]));
+  }
+  if (a.mode >= 1) {
+    const float* res = a.res + (uint64_t)r * H;
+    for (int j = t; j < H; j += blockDim.x) {
+      const float v = fadd(res[j], sx[j]);
+      sx[j] = ftz(v);
+      a.x_out[(uint64_t)r * H + j] = ftz(v);
+    }
+  }
+  __syncthreads();
+  for (int j = t; j < H; j += blockDim.x) sv[j] = fmul(sx[j], sx[j]);
+  const float s = block_sum16(sv, H, red);
+  const float rs = rsqrt_f(fadd(fmul(s, kinv), a.eps));
+  float amax = 0.0f;
+  for (int j = t; j < H; j += blockDim.x) {
+    const float h = ftz(fmul(fmul(sx[j], rs), a.gamma[j]));
+    sv[j] = h;
+    amax = fmax_c(amax, fabs_c(h));
+  }
+  amax = block_max(amax, red);
+  const float inv = fmul(127.0f, recip_f(amax));
+  int8_t* q = a.q + (uint64_t)r * a.ldq;
+  for (int j = t; j < H; j += blockDim.x) q[j] = q8(sv[j], inv);
+  if (t == 0) a.qs[r] = ftz(fmul(amax, bf(0x3C010204u)));
+}
+
+// ROW_QUANT alone (attention output, gate * up), numerics.py:383-390
+__global__ void __launch_bounds__(256) k_quant(const float* x, int ldx, int N, int8_t* q, int ldq, float* qs) {
+  __shared__ float red[33];
+  const int r = blockIdx.x;
+  const float* row = x + (uint64_t)r * ldx;
+  float amax = 0.0f;
+  for (int j = threadIdx.x; j < N; j += blockDim.x) amax = fmax_c(amax, fabs_c(row[j]));
+  amax = block_max(amax, red);
+  const float inv = fmul(127.0f, recip_f(amax));
+  for (int j = threadIdx.x; j < N; j += blockDim.x) q[(uint64_t)r * ldq + j] = q8(row[j], inv);
+  if (threadIdx.x == 0) qs[r] = ftz(fmul(amax, bf(0x3C010204u)));
+}
+
+// ------------------------------------------------------------------------------- GEMV
+// y[m][col] over the concatenated output columns of up to kMaxSegs weight blocks. Epilogue per
+// output: y = fmul(fmul(i2f(acc), srow[m]), scale[n]) (golden.py:336-344), then by mode:
+//   kEpiStore   store y (flushed) to the segment's output
+//   kEpiResid   store fadd(res[m][col], y)
+//   kEpiGated   segments 0 (gate) and 1 (up) of equal width: out = fmul(act(y_gate), y_up)
+//   kEpiKSplit  K blocks of kb: y = fadd(ep(acc_0), ep(acc_1)), then store (or add res if given)
+template <int MB, int KU>
+__global__ void __launch_bounds__(256) k_eng_gemv(EngGemvArgs g) {
+  __shared__ __align__(16) int8_t sA[MB * 512 * KU];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * MB;
+  const int mb = min(MB, g.M - m0);
+  const int nw = gridDim.x * 8;
+  const int ncols = g.mode == kEpiGated ? g.seg[0].n : g.ncols;
+  const int kv = g.K / 16;
+  for (int i = threadIdx.x; i < mb * kv; i += blockDim.x) {
+    const int m = i / kv, kk = (i - m * kv) * 16;
+    *reinterpret_cast<uint4*>(&sA[m * 512 * KU + kk]) = *reinterpret_cast<const uint4*>(g.A + (uint64_t)(m0 + m) * g.lda + kk);
+  }
+  __syncthreads();
+  for (int col = blockIdx.x * 8 + warp; col < ncols; col += nw) {
+    int s = 0;
+    while (s + 1 < g.nseg && col >= g.seg[s + 1].n0) ++s;
+    const int c = col - g.seg[s].n0;
+    const int nrows = g.mode == kEpiGated ? 2 : 1;
+    int acc[2][2][MB];                       // [weight row][K block][m]
+#pragma unroll
+    for (int w = 0; w < 2; ++w)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int m = 0; m < MB; ++m) acc[w][h][m] = 0;
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      if (w >= nrows) break;
+      const EngSeg& sg = g.seg[w == 0 ? s : 1];
+      const int8_t* w1 = sg.W + (uint64_t)c * g.kb;
+      const int8_t* w2 = sg.W2 + (uint64_t)c * (g.K - g.kb) - g.kb;
+      uint4 wv[KU];
+#pragma unroll
+      for (int u = 0; u < KU; ++u) {
+        const int k = lane * 16 + 512 * u;
+        wv[u] = k >= g.K ? make_uint4(0, 0, 0, 0) : ldg_stream(k < g.kb ? w1 + k : w2 + k);
+      }
+#pragma unroll
+      for (int u = 0; u < KU; ++u) {
+        const int k = lane * 16 + 512 * u;
+        if (k < g.K) {
+          const int h = k >= g.kb ? 1 : 0;
+#pragma unroll
+          for (int m = 0; m < MB; ++m) {
+            if (m < mb) {
+              const uint4 av = *reinterpret_cast<const uint4*>(&sA[m * 512 * KU + k]);
+              int v = acc[w][h][m];
+              v = __dp4a((int)av.x, (int)wv[u].x, v);
+              v = __dp4a((int)av.y, (int)wv[u].y, v);
+              v = __dp4a((int)av.z, (int)wv[u].z, v);
+              v = __dp4a((int)av.w, (int)wv[u].w, v);
+              acc[w][h][m] = v;
+            }
+          }
+        }
+      }
+    }
+    // reduce the partial sums over the 32 lanes; lane m keeps row m
+    int mine[2][2] = {{0, 0}, {0, 0}};
+#pragma unroll
+    for (int w = 0; w < 2; ++w)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+          int v = acc[w][h][m];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+          if (lane == m) mine[w][h] = v;
+        }
+    if (lane < mb) {
+      const int m = m0 + lane;
+      const float sr = g.srow[m];
+      auto ep = [&](int acc_v, const EngSeg& sg) { return fmul(fmul(i2f(acc_v), sr), sg.scale[c]); };
+      const EngSeg& sg = g.seg[s];
+      float y;
+      if (g.mode == kEpiGated) {
+        const float yg = ftz(act_fn(ep(mine[0][0], g.seg[0]), g.act));
+        const float yu = ep(mine[1][0], g.seg[1]);
+        g.seg[0].out[(uint64_t)m * g.seg[0].ldo + c] = ftz(fmul(yg, yu));
+        continue;
+      }
+      if (g.mode == kEpiKSplit) y = fadd(ftz(ep(mine[0][0], sg)), ftz(ep(mine[0][1], sg)));
+      else y = ep(mine[0][0], sg);
+      if (g.res) y = fadd(g.res[(uint64_t)m * g.ldres + col], y);
+      sg.out[(uint64_t)m * sg.ldo + c] = ftz(y);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------- q / k heads
+// Per row and head: RMSNorm over the head (gamma = q_norm * scaling or k_norm), then RoPE with the
+// table row of the token's position (llm.py:718-734, numerics.py:353-358, 412-424). q -> qr;
+// k -> the K cache row of (sequence, position). One half-warp per (row, head).
+__global__ void __launch_bounds__(128) k_qk_rope(QkRopeArgs a) {
+  const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
+  const int heads = a.nh + a.nkv;
+  const int item = blockIdx.x * 8 + hw;
+  const bool live = item < a.rows * heads;
+  const int r = live ? item / heads : 0, h = live ? item % heads : 0;
+  const bool isq = h < a.nh;
+  const int b = r / a.n, m = r - b * a.n;
+  const int t = *a.pos + m;
+  const int hd = a.hd;
+  const float* src = isq ? a.q + (uint64_t)r * a.nh * hd + h * hd : a.k + (uint64_t)r * a.nkv * hd + (h - a.nh) * hd;
+  const float* gam = isq ? a.qn : a.kn;
+  float v[16];                                 // hd <= 256: 16 elements per lane, j = l + 16 i
+  float s = 0.0f;
+  for (int i = 0; i < hd / 16; ++i) {
+    v[i] = ftz(src[l + 16 * i]);
+    s = fadd_nc(s, fmul(v[i], v[i]));
+  }
+  s = sum16_fold(canon(s));
+  const float rs = rsqrt_f(fadd(fmul(s, recip_f(i2f(hd))), a.eps));
+  __shared__ float sn[8][256];
+  for (int i = 0; i < hd / 16; ++i) sn[hw][l + 16 * i] = ftz(fmul(fmul(v[i], rs), gam[l + 16 * i]));
+  __syncwarp();
+  if (!live) return;
+  const float* tab = a.tab + (uint64_t)t * a.rot;
+  float* dst = isq ? a.qr + (uint64_t)r * a.nh * hd + h * hd
+                   : a.kc + (((uint64_t)b * a.Tp + t) * a.nkv + (h - a.nh)) * hd;
+  const int half = a.rot / 2;
+  for (int j = l; j < hd; j += 16) {
+    float y;
+    if (j < half) y = fadd(fmul(sn[hw][j], ftz(tab[j])), neg(fmul(sn[hw][j + half], ftz(tab[half + j]))));
+    else if (j < a.rot) y = fadd(fmul(sn[hw][j], ftz(tab[j - half])), fmul(sn[hw][j - half], ftz(tab[j])));
+    else y = sn[hw][j];
+    dst[j] = ftz(y);
+  }
+  if (!isq) {                                  // V goes to the cache as the GEMM wrote it (llm.py:731)
+    const int kh = h - a.nh;
+    const float* vs = a.v + (uint64_t)r * a.nkv * hd + kh * hd;
+    float* vd = a.vc + (((uint64_t)b * a.Tp + t) * a.nkv + kh) * hd;
+    for (int j = l; j < hd; j += 16) vd[j] = vs[j];
+  }
+}
+
+// ------------------------------------------------------------------------------- attention
+// One block per (sequence, query head): FDOT NT of the head's n query rows against the sequence's
+// K cache rows 0 .. nk-1 (nk = pad16(t0 + n), zero rows beyond the tokens written), the causal
+// softmax of each row over its first t0 + 1 + m keys, FDOT NN against the V cache in key order
+// (llm.py:735-746; numerics.py:362-371, 393-409).
+__global__ void __launch_bounds__(128) k_attention(AttnArgs a) {
+  __shared__ float sq[4][256];
+  __shared__ float sp[4][kT];
+  __shared__ float red[33];
+  const int b = blockIdx.x / a.nh, h = blockIdx.x - b * a.nh;
+  const int kvh = h / (a.nh / a.nkv);
+  const int n = a.n, hd = a.hd, t0 = *a.pos;
+  const int nk = ((t0 + n) + 15) / 16 * 16;
+  const int tid = threadIdx.x, hw = tid >> 4, l = tid & 15;
+  for (int i = tid; i < n * hd; i += blockDim.x) {
+    const int m = i / hd, d = i - m * hd;
+    sq[m][d] = ftz(a.qr[((uint64_t)(b * n + m) * a.nh + h) * hd + d]);
+  }
+  __syncthreads();
+  const float* K = a.kc + ((uint64_t)b * a.Tp * a.nkv + kvh) * hd;       // row j at K + j * nkv * hd
+  const float* V = a.vc + ((uint64_t)b * a.Tp * a.nkv + kvh) * hd;
+  const uint64_t kstride = (uint64_t)a.nkv * hd;
+  // scores: one half-warp per (m, j), lane chains over d = l, l + 16, ...
+  for (int p = hw; p < n * nk; p += 8) {
+    const int m = p / nk, j = p - m * nk;
+    const float* kr = K + (uint64_t)j * kstride;
+    float s = 0.0f;
+    for (int d = l; d < hd; d += 16) s = fadd_nc(s, fmul(sq[m][d], kr[d]));
+    s = sum16_fold(canon(s));
+    if (l == 0) sp[m][j] = s;
+  }
+  __syncthreads();
+  // causal softmax per row (valid = t0 + 1 + m), numerics.py:362-371
+  for (int m = 0; m < n; ++m) {
+    const int valid = min(nk, t0 + 1 + m);
+    float mx = bf(0xFF800000u);
+    for (int j = tid; j < valid; j += blockDim.x) mx = fmax_c(mx, ftz(sp[m][j]));
+    mx = block_max(mx, red);
+    __syncthreads();
+    for (int j = tid; j < nk; j += blockDim.x) sp[m][j] = j < valid ? exp_f(fadd(sp[m][j], neg(mx))) : 0.0f;
+    const float r = recip_f(block_sum16(sp[m], nk, red));
+    __syncthreads();
+    for (int j = tid; j < nk; j += blockDim.x) sp[m][j] = ftz(fmul(sp[m][j], r));
+    __syncthreads();
+  }
+  // FDOT NN: out[m][d] = k-order chain over the nk keys
+  for (int i = tid; i < n * hd; i += blockDim.x) {
+    const int m = i / hd, d = i - m * hd;
+    float acc = 0.0f;
+    for (int j = 0; j < nk; ++j) acc = fadd_nc(acc, fmul(sp[m][j], V[(uint64_t)j * kstride + d]));
+    a.att[((uint64_t)(b * n + m) * a.nh + h) * hd + d] = ftz(canon(acc));
+  }
+}
+
+// ------------------------------------------------------------------------------- greedy pick
+// np.argmax of each sequence's logits: the first maximum; the first NaN wins over numbers.
+__global__ void __launch_bounds__(1024) k_argmax(const float* logits, int vocab, int* tok_out, int tok_stride) {
+  const int b = blockIdx.x;
+  const float* row = logits + (uint64_t)b * vocab;
+  float best = 0.0f;
+  int bi = -1;
+  bool bnan = false;
+  for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+    const float v = row[j];
+    const bool vn = is_nan(v);
+    if (bi < 0 || (vn && !bnan) || (!bnan && !vn && v > best)) { best = v; bi = j; bnan = vn; }
+  }
+  // combine (value, index, nan) pairs: smaller index wins ties
+  __shared__ float sv[1024];
+  __shared__ int si[1024];
+  __shared__ int sn[1024];
+  sv[threadIdx.x] = best; si[threadIdx.x] = bi; sn[threadIdx.x] = bnan;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) {
+      const int j = threadIdx.x + o;
+      if (si[j] >= 0) {
+        bool take;
+        if (si[threadIdx.x] < 0) take = true;
+        else if (sn[j] != sn[threadIdx.x]) take = sn[j];
+        else if (sn[j]) take = si[j] < si[threadIdx.x];
+        else take = sv[j] > sv[threadIdx.x] || (sv[j] == sv[threadIdx.x] && si[j] < si[threadIdx.x]);
+        if (take) { sv[threadIdx.x] = sv[j]; si[threadIdx.x] = si[j]; sn[threadIdx.x] = sn[j]; }
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) tok_out[b * tok_stride] = si[0];
+}
+
+__global__ void k_advance(int* pos, int n) { *pos += n; }
+
+}  // namespace
+
+// --------------------------------------------------------------------------------- launchers
+cudaError_t eng_embed(const float* E, const int* tok, float* x, int H, int scale_on, float scale, int rows, cudaStream_t st) {
+  k_embed<<<rows, 256, 0, st>>>(E, tok, x, H, scale_on, scale, rows);
+  return cudaGetLastError();
+}
+cudaError_t eng_norm_quant(const NormQuantArgs& a, cudaStream_t st) {
+  const int smem = 2 * a.H * 4;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_norm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+  }
+  k_norm_quant<<<a.rows, 256, smem, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t eng_quant(const float* x, int ldx, int N, int8_t* q, int ldq, float* qs, int rows, cudaStream_t st) {
+  k_quant<<<rows, 256, 0, st>>>(x, ldx, N, q, ldq, qs);
+  return cudaGetLastError();
+}
+template <int MB, int KU>
+static cudaError_t gemv_mk(const EngGemvArgs& g, cudaStream_t st) {
+  const int ncols = g.mode == kEpiGated ? g.seg[0].n : g.ncols;
+  const int blocks = std::min((ncols + 7) / 8, 148 * 4);
+  k_eng_gemv<MB, KU><<<dim3(blocks, (g.M + MB - 1) / MB), 256, 0, st>>>(g);
+  return cudaGetLastError();
+}
+template <int MB>
+static cudaError_t gemv_m(const EngGemvArgs& g, cudaStream_t st) {
+  if (g.K <= 1024) return gemv_mk<MB, 2>(g, st);
+  if (g.K <= 2048) return gemv_mk<MB, 4>(g, st);
+  if (g.K <= 4096) return gemv_mk<MB, 8>(g, st);
+  if constexpr (MB <= 4) return gemv_mk<MB, 14>(g, st);
+  return cudaErrorInvalidValue;
+}
+cudaError_t eng_gemv(const EngGemvArgs& g, cudaStream_t st) {
+  if (g.K > 14 * 512 || g.K % 16) return cudaErrorInvalidValue;
+  if (g.M == 1) return gemv_m<1>(g, st);
+  if (g.M == 2) return gemv_m<2>(g, st);
+  if (g.M <= 4 || g.K > 4096) return gemv_m<4>(g, st);   // 8 rows of K > 4096 exceed static shared memory
+  return gemv_m<8>(g, st);
+}
+cudaError_t eng_qk_rope(const QkRopeArgs& a, cudaStream_t st) {
+  const int items = a.rows * (a.nh + a.nkv);
+  k_qk_rope<<<(items + 7) / 8, 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t eng_attention(const AttnArgs& a, int batch, cudaStream_t st) {
+  k_attention<<<batch * a.nh, 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+cudaError_t eng_argmax(const float* logits, int vocab, int batch, int* tok_out, int tok_stride, cudaStream_t st) {
+  k_argmax<<<batch, 1024, 0, st>>>(logits, vocab, tok_out, tok_stride);
+  return cudaGetLastError();
+}
+cudaError_t eng_advance(int* pos, int n, cudaStream_t st) {
+  k_advance<<<1, 1, 0, st>>>(pos, n);
+  return cudaGetLastError();
+}
+
+}  // namespace tc

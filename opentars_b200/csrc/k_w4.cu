@@ -23,6 +23,9 @@ namespace tc {
 namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+// int16 slots per group in shared memory: 128 mantissas + 2 of padding, so a group starts 65 words
+// after the previous one and the 32 lanes (one group each) read 32 different banks
+constexpr int kQStride = 130;
 
 __device__ __forceinline__ uint4 ldg_stream(const uint8_t* p) {
   uint4 v;
@@ -71,7 +74,7 @@ __device__ void align_rows(const W4Args& g, int mb, const uint32_t* sX, int16_t*
       const bool isinf_j = e[j] == 255 && !(b[j] & 0x7FFFFFu);
       if (isinf_j && !gnan) mag = 16384;
       if (gnan) mag = 0;
-      sQ[m * g.K + gi * W4_GROUP + lane * 4 + j] = (int16_t)((b[j] >> 31) ? -mag : mag);
+      sQ[(m * 64 + gi) * kQStride + lane * 4 + j] = (int16_t)((b[j] >> 31) ? -mag : mag);
     }
     if (lane == 0) {
       uint32_t sb = (uint32_t)min(max(eff - 13, 0), 255) << 23;
@@ -98,8 +101,8 @@ template <int MB>
 __global__ void __launch_bounds__(kThreads) k_gemv_w4(W4Args g, bool vec) {
   extern __shared__ __align__(16) uint8_t smem[];
   uint32_t* sX = reinterpret_cast<uint32_t*>(smem);                                 // [MB][K] fp32 bits
-  int16_t* sQ = reinterpret_cast<int16_t*>(smem + (size_t)MB * g.K * 4);             // [MB][K]
-  uint32_t* sS = reinterpret_cast<uint32_t*>(smem + (size_t)MB * g.K * 6);            // [MB][64]
+  int16_t* sQ = reinterpret_cast<int16_t*>(smem + (size_t)MB * g.K * 4);             // [MB][64][kQStride]
+  uint32_t* sS = reinterpret_cast<uint32_t*>(smem + (size_t)MB * g.K * 4 + (size_t)MB * 64 * kQStride * 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * MB;
   const int mb = min(MB, g.M - m0);
@@ -152,7 +155,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_w4(W4Args g, bool vec) {
 #pragma unroll
         for (int m = 0; m < MB; ++m) {
           if (m < mb) {
-            const uint32_t* q = reinterpret_cast<const uint32_t*>(sQ + m * g.K + gi * W4_GROUP);
+            const uint32_t* q = reinterpret_cast<const uint32_t*>(sQ + (m * 64 + gi) * kQStride);
             int dot = 0;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -204,7 +207,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_w4(W4Args g, bool vec) {
 
 template <int MB>
 cudaError_t launch_w4(const W4Args& g, cudaStream_t st) {
-  const size_t smem = (size_t)MB * g.K * 6 + (size_t)MB * 64 * 4;
+  const size_t smem = (size_t)MB * g.K * 4 + (size_t)MB * 64 * kQStride * 2 + (size_t)MB * 64 * 4;
   auto kern = k_gemv_w4<MB>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;

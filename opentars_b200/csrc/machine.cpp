@@ -31,6 +31,8 @@ struct tc_machine {
   uint8_t* scratch = nullptr;
   uint64_t scratch_size = 0;
   std::string err;
+  cudaStream_t cur = nullptr;                          // the stream launch() enqueues on
+  std::vector<cudaStream_t> lanes;                     // extra capture streams (dependency graphs)
 };
 
 // A validated queue captured as one CUDA graph (tc_queue_capture).
@@ -72,7 +74,10 @@ cudaError_t ensure_scratch(tc_machine* m, uint64_t n) {
 }
 
 // Enqueues the kernels of one validated, in-range descriptor.
-cudaError_t launch(tc_machine* mc, const Desc& d) {
+cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream);
+cudaError_t launch(tc_machine* mc, const Desc& d) { return launch_on(mc, d, mc->cur ? mc->cur : mc->stream); }
+
+cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream) {
   uint8_t* B = mc->dev + d[F_BASE_ADDR];
   const Strides s = strides(d);
   const int op = d.op();
@@ -87,7 +92,7 @@ cudaError_t launch(tc_machine* mc, const Desc& d) {
       g.Y = B + d[F_Y_OFF]; g.ldy = s.ldy;
       g.M = (int)d[F_M]; g.N = (int)d[F_N]; g.K = (int)d[F_K];
       g.act = d.act(); g.out = d.out(); g.out_scale = osc;
-      return launch_gemm_w4a16(g, mc->stream);
+      return launch_gemm_w4a16(g, stream);
     }
     GemmArgs g{};
     g.A = B + d[F_A_OFF]; g.lda = s.lda;
@@ -100,7 +105,7 @@ cudaError_t launch(tc_machine* mc, const Desc& d) {
       ia.img = B + d[F_A_OFF]; ia.ld = s.lda; ia.out = mc->scratch;
       ia.H = cg.H; ia.W = cg.W; ia.KH = cg.KH; ia.KW = cg.KW; ia.S = cg.S; ia.P = cg.P;
       ia.Cin = cg.Cin; ia.OH = cg.OH; ia.OW = cg.OW;
-      e = launch_im2col(ia, mc->stream);
+      e = launch_im2col(ia, stream);
       if (e != cudaSuccess) return e;
       g.A = mc->scratch; g.lda = d[F_K];
     }
@@ -111,13 +116,13 @@ cudaError_t launch(tc_machine* mc, const Desc& d) {
     g.Y = B + d[F_Y_OFF]; g.ldy = s.ldy;
     g.M = (int)d[F_M]; g.N = (int)d[F_N]; g.K = (int)d[F_K];
     g.act = d.act(); g.out = d.out(); g.out_scale = osc;
-    return launch_gemm_w8a8(g, mc->stream);
+    return launch_gemm_w8a8(g, stream);
   }
   if (op == OP_RELU) {
     ActArgs a{};
     a.X = B + d[F_A_OFF]; a.lda = s.lda; a.Y = B + d[F_Y_OFF]; a.ldy = s.ldy;
     a.M = (int)d[F_M]; a.N = (int)d[F_N]; a.act = d.act(); a.out = d.out(); a.out_scale = osc;
-    return launch_act(a, mc->stream);
+    return launch_act(a, stream);
   }
   if (op == OP_ROW) {
     RowArgs a{};
@@ -130,7 +135,7 @@ cudaError_t launch(tc_machine* mc, const Desc& d) {
       a.beta = d.bias() ? B + d[F_BIAS_OFF] : nullptr;
       a.eps = f32(d[F_W_OFF]);
     }
-    return launch_rowop(a, mc->stream);
+    return launch_rowop(a, stream);
   }
   if (op == OP_ELT) {
     EltArgs a{};
@@ -143,14 +148,14 @@ cudaError_t launch(tc_machine* mc, const Desc& d) {
     a.C = a.op == ELT_MULADD ? B + d[F_BIAS_OFF] : nullptr;
     a.Y = B + d[F_Y_OFF]; a.ldy = s.ldy;
     a.M = (int)d[F_M]; a.N = (int)d[F_N]; a.act = d.act(); a.out = d.out(); a.out_scale = osc;
-    return launch_elt(a, mc->stream);
+    return launch_elt(a, stream);
   }
   if (op == OP_ROPE) {
     RopeArgs a{};
     a.X = B + d[F_A_OFF]; a.lda = s.lda; a.tab = B + d[F_W_OFF]; a.Y = B + d[F_Y_OFF]; a.ldy = s.ldy;
     a.M = (int)d[F_M]; a.N = (int)d[F_N]; a.R = (int)d[F_K]; a.G = (int)d[F_GROUP_SIZE];
     a.out = d.out(); a.out_scale = osc;
-    return launch_rope(a, mc->stream);
+    return launch_rope(a, stream);
   }
   // FDOT
   FdotArgs a{};
@@ -160,7 +165,7 @@ cudaError_t launch(tc_machine* mc, const Desc& d) {
   a.nn = (int)(d[F_CTRL] & 1); a.b_fp16 = (d[F_HDR_RSV] & STATE_FP16) != 0;
   a.Y = B + d[F_Y_OFF]; a.ldy = s.ldy;
   a.M = (int)d[F_M]; a.N = (int)d[F_N]; a.K = (int)d[F_K]; a.out = d.out(); a.out_scale = osc;
-  return launch_fdot(a, mc->stream);
+  return launch_fdot(a, stream);
 }
 
 bool in_range(const Footprint& fp, u128 size) {
@@ -193,9 +198,9 @@ uint64_t read_bytes(const Footprint& fp) {
 // The in-order loop shared by tc_run_queue and tc_queue_capture. `before(i)` runs before the
 // kernels of descriptor i are enqueued; `capturing` forbids host synchronisation (a queue that
 // rewrites its own later descriptors cannot be captured).
-template <class Before>
+template <class Before, class After>
 int execute(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, int32_t gemv_only, tc_status* st,
-            int32_t* contract_op, const std::vector<uint8_t>& q0, bool capturing, Before before) {
+            int32_t* contract_op, const std::vector<uint8_t>& q0, bool capturing, Before before, After after) {
   std::vector<uint8_t> q = q0;
   const u128 size = m->size;
   auto fetch = [&](uint32_t from) -> cudaError_t {
@@ -230,9 +235,10 @@ int execute(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, int32
       rc = TC_CONTRACT;
       break;
     }
-    before(i);
+    before(i, d, fp);
     cudaError_t e = launch(m, d);
     if (e != cudaSuccess) { rc = fail(m, "launch", e); break; }
+    after(i);
     const int op = d.op();
     const uint64_t macs = (op == OP_GEMM || op == OP_FDOT || d.conv()) ? d[F_M] * d[F_N] * d[F_K] : 0;
     const Strides s = strides(d);
@@ -277,6 +283,92 @@ uint64_t scratch_need(const std::vector<uint8_t>& q, uint32_t qlen, int core_id,
   }
   return need;
 }
+// Captures a queue as a graph whose edges are the queue's real hazards. Every descriptor's byte
+// footprint (bounding interval per input tensor and per output) is compared with those of the
+// earlier descriptors; a read-after-write, write-after-read or write-after-write overlap orders
+// the pair, anything else may run concurrently. Each descriptor goes on the capture stream of its
+// latest predecessor (so that edge is the stream order) and waits for its other predecessors'
+// events. The conv gather buffer counts as a written input of every conv. Independent work
+// commutes, so the bytes written are those of the in-order run.
+struct Iv { u128 lo, hi; };
+struct DagNode { std::vector<Iv> r, w; int lane; };
+
+bool hits(const std::vector<Iv>& a, const std::vector<Iv>& b) {
+  for (const Iv& x : a)
+    for (const Iv& y : b)
+      if (x.lo < y.hi && y.lo < x.hi) return true;
+  return false;
+}
+
+int capture_dag(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, int32_t gemv_only, tc_status* st,
+                int32_t* contract_op, const std::vector<uint8_t>& q, std::vector<cudaEvent_t>& evs) {
+  const int kLanes = 16;
+  while ((int)m->lanes.size() < kLanes) {
+    cudaStream_t s;
+    cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return fail(m, "capture streams", e);
+    m->lanes.push_back(s);
+  }
+  auto new_event = [&]() {
+    cudaEvent_t ev;
+    cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    evs.push_back(ev);
+    return ev;
+  };
+  // fork: every lane joins the capture after the origin stream's work so far
+  cudaEvent_t fork = new_event();
+  cudaEventRecord(fork, m->stream);
+  for (auto s : m->lanes) cudaStreamWaitEvent(s, fork, 0);
+  std::vector<DagNode> nodes;
+  std::vector<cudaEvent_t> done;
+  std::vector<int> lane_last(kLanes, -1);
+  int rr = 0;
+  const u128 kScratch = ((u128)1) << 120;          // a key outside every image for the gather buffer
+  int rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, true,
+                   [&](uint32_t, const Desc& d, const Footprint& fp) {
+    DagNode nd;
+    for (const auto& t : fp.reads)
+      for (const auto& sg : t) nd.r.push_back(Iv{sg.base, seg_end(sg)});
+    nd.w.push_back(Iv{fp.y.base, seg_end(fp.y)});
+    if (fp.has_extra) nd.w.push_back(Iv{fp.extra.base, seg_end(fp.extra)});
+    if (d.conv()) nd.w.push_back(Iv{kScratch, kScratch + 1});
+    std::vector<int> latest(kLanes, -1);
+    int pick = -1;
+    for (int k = (int)nodes.size() - 1; k >= 0; --k) {
+      const DagNode& o = nodes[k];
+      if (latest[o.lane] >= 0) continue;              // a later one on that lane already orders us
+      if (hits(o.w, nd.r) || hits(o.w, nd.w) || hits(o.r, nd.w)) {
+        latest[o.lane] = k;
+        if (pick < 0) pick = o.lane;                  // the most recent predecessor's lane
+      }
+    }
+    if (pick < 0) {                                   // independent: the least recently used lane
+      pick = rr;
+      rr = (rr + 1) % kLanes;
+    }
+    for (int l = 0; l < kLanes; ++l)
+      if (l != pick && latest[l] >= 0) cudaStreamWaitEvent(m->lanes[pick], done[latest[l]], 0);
+    nd.lane = pick;
+    m->cur = m->lanes[pick];
+    nodes.push_back(std::move(nd));
+  }, [&](uint32_t) {
+    cudaEvent_t ev = new_event();
+    cudaEventRecord(ev, m->cur);                      // this descriptor's completion on its lane
+    done.push_back(ev);
+    lane_last[nodes.back().lane] = (int)done.size() - 1;
+  });
+  m->cur = nullptr;
+  // join: the origin stream waits for every lane's last descriptor
+  for (int l = 0; l < kLanes; ++l)
+    if (lane_last[l] >= 0) cudaStreamWaitEvent(m->stream, done[lane_last[l]], 0);
+    else {
+      cudaEvent_t ev = new_event();                   // an idle lane still has to rejoin
+      cudaEventRecord(ev, m->lanes[l]);
+      cudaStreamWaitEvent(m->stream, ev, 0);
+    }
+  (void)evs;
+  return rc;
+}
 }  // namespace
 
 extern "C" {
@@ -292,7 +384,8 @@ int tc_run_queue(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, 
   std::vector<uint8_t> q;
   cudaError_t e = fetch_queue(m, qaddr, qlen, q);
   if (e != cudaSuccess) return fail(m, "queue fetch", e);
-  int rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, false, [](uint32_t) {});
+  int rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, false,
+                   [](uint32_t, const Desc&, const Footprint&) {}, [](uint32_t) {});
   cudaError_t se = cudaStreamSynchronize(m->stream);
   if (se != cudaSuccess && rc >= 0) rc = fail(m, "queue run", se);
   return rc;
@@ -320,12 +413,19 @@ int tc_queue_capture(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_
   e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeRelaxed);
   if (e != cudaSuccess) { delete g; return fail(m, "begin capture", e); }
   uint32_t last = 0;
-  int rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, true, [&](uint32_t i) {
-    // an external record node: a plain cudaEventRecord inside a capture only orders work
-    if (timing) cudaEventRecordWithFlags(g->events[i], m->stream, cudaEventRecordExternal);
-    last = i + 1;
-  });
-  if (timing && last) cudaEventRecordWithFlags(g->events[last], m->stream, cudaEventRecordExternal);
+  int rc;
+  std::vector<cudaEvent_t> dag_events;
+  if (timing) {
+    rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, true,
+                 [&](uint32_t i, const Desc&, const Footprint&) {
+      // an external record node: a plain cudaEventRecord inside a capture only orders work
+      cudaEventRecordWithFlags(g->events[i], m->stream, cudaEventRecordExternal);
+      last = i + 1;
+    }, [](uint32_t) {});
+    if (last) cudaEventRecordWithFlags(g->events[last], m->stream, cudaEventRecordExternal);
+  } else {
+    rc = capture_dag(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, dag_events);
+  }
   cudaGraph_t graph = nullptr;
   cudaError_t ce = cudaStreamEndCapture(m->stream, &graph);
   if (rc == TC_OK && ce != cudaSuccess) rc = fail(m, "end capture", ce);
@@ -334,6 +434,7 @@ int tc_queue_capture(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_
     if (ce != cudaSuccess) rc = fail(m, "instantiate", ce);
   }
   if (graph) cudaGraphDestroy(graph);
+  for (auto ev : dag_events) cudaEventDestroy(ev);
   if (rc != TC_OK) {
     for (auto& ev : g->events) cudaEventDestroy(ev);
     if (g->exec) cudaGraphExecDestroy(g->exec);
@@ -410,6 +511,7 @@ int tc_close(tc_machine* m) {
   if (!m) return TC_OK;
   cudaSetDevice(m->device);
   if (m->stream) cudaStreamSynchronize(m->stream);
+  for (auto s : m->lanes) cudaStreamDestroy(s);
   if (m->scratch) cudaFree(m->scratch);
   if (m->dev) cudaFree(m->dev);
   if (m->stream) cudaStreamDestroy(m->stream);
