@@ -24,6 +24,7 @@ extern "C" {
 #define TC_CONTRACT 1      /* an illegal program: golden.py raises ContractError (golden.py:473-479) */
 #define TC_ERR_CUDA (-1)
 #define TC_ERR_ARG (-2)
+#define TC_ERR_TOO_LARGE (-3) /* tc_conv_w8a8_noalloc: the gathered input exceeds its fixed buffer */
 
 typedef struct tc_machine tc_machine;
 typedef struct tc_graph tc_graph;
@@ -93,6 +94,23 @@ int tc_synchronize(tc_machine* m);
 int tc_validate(const uint8_t* raw64, int32_t core_id, int32_t gemv_only, uint64_t* fields23);
 /* golden.Machine.segments / extra_out (golden.py:195-256) as strided sets; *count = how many. */
 int tc_footprint(const uint8_t* raw64, tc_seg* out, uint32_t cap, uint32_t* count);
+
+/* No counterpart in the reference: the W8A8 convolution of a conv descriptor (same arithmetic,
+ * same bytes) for callers that must not have the library allocate device memory during a call,
+ * such as a server that reserved all of HBM for its own pool up front or an embedder whose
+ * device footprint must be fixed when the library loads. The window gather uses a fixed 16 MiB
+ * array in device memory that every GPU loading the library holds until exit; OH*OW*KH*KW*Cin
+ * bytes above that return TC_ERR_TOO_LARGE. All pointers are device pointers of the caller
+ * (img: H*W pixel rows of Cin int8 with row stride ld; weights: int8 [N, KH*KW*Cin]; scale: fp32
+ * [N] or [1]; bias: fp32 [N] or NULL; y: OH*OW rows with stride ldy in format out: 0 fp32,
+ * 1 bf16, 2 int8 via out_scale); work is enqueued on `stream` (a cudaStream_t, NULL = default).
+ * The first call on a device looks the array up with that device current. Calls share the array
+ * and it keeps the last call's contents (every byte a call reads it writes first); calls that
+ * overlap on the GPU race, so order them on one stream. */
+int tc_conv_w8a8_noalloc(const uint8_t* img, uint64_t ld, int32_t H, int32_t W, int32_t Cin, int32_t KH,
+                         int32_t KW, int32_t stride, int32_t pad, const uint8_t* weights, const float* scale,
+                         int32_t per_channel, const float* bias, uint8_t* y, uint64_t ldy, int32_t N,
+                         int32_t act, int32_t out, float out_scale, void* stream);
 
 #ifdef __cplusplus
 }

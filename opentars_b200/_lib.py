@@ -11,7 +11,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libtarscuda.so"
 
-TC_OK, TC_CONTRACT, TC_ERR_CUDA, TC_ERR_ARG = 0, 1, -1, -2
+TC_OK, TC_CONTRACT, TC_ERR_CUDA, TC_ERR_ARG, TC_ERR_TOO_LARGE = 0, 1, -1, -2, -3
 ABI_VERSION = 1
 
 
@@ -55,6 +55,10 @@ SIGNATURES = {
     "tc_graph_times": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_float), ctypes.c_uint32]),
     "tc_graph_destroy": (ctypes.c_int, [P]),
     "tc_synchronize": (ctypes.c_int, [P]),
+    "tc_conv_w8a8_noalloc": (ctypes.c_int, [VP, ctypes.c_uint64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, VP, VP,
+                                            ctypes.c_int32, VP, VP, ctypes.c_uint64, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_int32, ctypes.c_float, VP]),
 }
 
 
