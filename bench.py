@@ -1,15 +1,21 @@
 #!/usr/bin/env python
 """Benchmark of the tars_mini hot path on B200s (one JSON line from rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemv|w4] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|decode-gemma|gemv|w4]
+                    [--batch B] [--impl ours|reference]
 
 Workloads (synthetic seeded data with the configs' distributions):
+  decode        (default) config 3: Qwen3-0.6B shapes, random-init weights, B sequences per GPU
+                (default 64) with seeded 20-token prompts prefilled in chunks of 4, then greedy
+                decode; a step = one token for every sequence; value in tok/s (all GPUs). Sequence
+                0 is checked bit for bit against the reference's logits (committed fixture).
+  decode-gemma  config 4: the same for Gemma-3-1B shapes
   gemv  config 0: one unit = ROW_QUANT of x [1, 1024] + W8A8 GEMV (QM_ROWCOL) against W [3072, 1024];
         a step runs R units on R distinct weight copies (R * 3 MiB > the 126 MB L2)
   w4    config 2: one unit = W4A16 GEMV, M=1, K=8192, N=16384 (64 MiB of packed weights);
         a step runs R units on distinct weight copies
-value: algorithmic bytes of all units of all ranks / device time of the timed steps (max over
-ranks), in GB/s. e2e: the same metric through the board-runtime API (opentars_b200.board.Cuda:
+gemv / w4 value: algorithmic bytes of all units of all ranks / device time of the timed steps
+(max over ranks), in GB/s. e2e: the same metric through the board-runtime API (opentars_b200.board.Cuda:
 host writes x into pinned memory, to_dev, run, from_dev of y) timed on the host clock.
 --impl reference: the reference's numpy golden path restated in oracle/ (the reference itself is
 Python and cannot travel), on all host cores, over a bounded sample of the same workload.
@@ -358,12 +364,257 @@ def run_reference(a, world, rank) -> dict | None:
     }
 
 
+
+# ----------------------------------------------------------------------------- decode (configs 3 / 4)
+DECODE_MODELS = {
+    # name: (base config, layer types, vocab, fixture name)
+    "decode": ("CFG_Q3_06B", None, "VOCAB_Q3_06B", "qwen3_0.6b"),
+    "decode-gemma": ("CFG_G3_1B", "LAYERS_G3_1B", "VOCAB_G3_1B", "gemma3_1b"),
+}
+PROMPT_LEN, CHUNK, CONTEXT = 20, 4, 256
+
+
+def prompt_ids(seed: int, vocab: int, n: int = PROMPT_LEN) -> list[int]:
+    """Configs 3 / 4: a seeded prompt of n token ids uniform over the vocabulary."""
+    return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, n)]
+
+
+def build_decode_model(workload: str):
+    """The model lowered exactly as the reference lowers it (random weights, seed 0)."""
+    from opentars_b200 import models as Mo
+    from opentars_b200.lowering import QwenLowering
+    base, types, vocab_name, _ = DECODE_MODELS[workload]
+    vocab = getattr(Mo, vocab_name)
+    cfg = Mo.make_config(getattr(Mo, base), list(getattr(Mo, types)) if types else None, vocab=vocab)
+    w = Mo.random_weights(cfg, seed=0, embed=True)
+    return QwenLowering(cfg, w, max_tokens=CONTEXT, ddr_bytes=3 << 29, head=True, queue_cap=8192)
+
+
+_CPU: dict = {}
+
+
+def _cpu_decode_prepare(low) -> None:
+    """One decode step's queue (position 0) staged in the image, for the forked oracle workers."""
+    tok = prompt_ids(0, low.vocab)[:1]
+    ddr = low.p.ddr
+    low.put_input(ddr, 0, low.embed(tok))
+    a = len(low.p.descs)
+    low.chunk(0, 1)
+    q, n = low.stage(ddr, a, len(low.p.descs))
+    _CPU.update(ddr=ddr, q=q, n=n, pos=0)
+
+
+def _cpu_decode_tokens(seconds: float):
+    """Whole decode steps of the oracle (a restatement of the reference's golden Machine) for at
+    least `seconds`: (steps, elapsed)."""
+    from oracle.machine import OracleMachine
+    t0, k = time.perf_counter(), 0
+    while True:
+        assert OracleMachine(_CPU["ddr"], gemv_only=True).run_queue(_CPU["q"], _CPU["n"]).done
+        k += 1
+        if time.perf_counter() - t0 >= seconds:
+            return k, time.perf_counter() - t0
+
+
+def _cpu_decode_slice(count: int):
+    """The next `count` descriptors of the decode queue, in order, cycling (the worker keeps its
+    place between calls): (descriptors run, elapsed)."""
+    from oracle.machine import OracleMachine
+    q, n, pos = _CPU["q"], _CPU["n"], _CPU["pos"]
+    t0 = time.perf_counter()
+    done = 0
+    while done < count:
+        k = min(count - done, n - pos)
+        assert OracleMachine(_CPU["ddr"], gemv_only=True).run_queue(q + 64 * pos, k).done
+        pos = (pos + k) % n
+        done += k
+    _CPU["pos"] = pos
+    return done, time.perf_counter() - t0
+
+
+def _fork_pool(procs: int):
+    import multiprocessing as mp
+    return mp.get_context("fork").Pool(procs)     # forked before any CUDA context exists
+
+
+def cpu_decode_baseline(procs: int, seconds: float) -> dict:
+    with _fork_pool(procs) as pool:
+        t0 = time.perf_counter()
+        res = pool.map(_cpu_decode_tokens, [seconds] * procs, chunksize=1)
+        wall = time.perf_counter() - t0
+    toks = sum(k for k, _ in res)
+    return dict(value=round(toks / wall, 4), unit="tok/s", cores=procs, kind="port",
+                sample=f"{toks} whole decode steps (one token, one sequence, 1,910-descriptor queue at position 0) "
+                       f"of the oracle on {procs} forked processes in {wall:.1f}s")
+
+
+def run_decode(a, world, rank, local) -> dict | None:
+    import torch
+    t_build = time.perf_counter()
+    low = build_decode_model(a.workload)
+    build_s = time.perf_counter() - t_build
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:          # before the GPU is touched: fork is safe
+        _cpu_decode_prepare(low)
+        cpu = cpu_decode_baseline(os.cpu_count() or 1, a.cpu_seconds)
+    os.environ["TC_DEVICE"] = str(local)
+    torch.cuda.set_device(local)
+    from opentars_b200.engine import DecodeEngine
+    B = a.batch
+    eng = DecodeEngine(low, batch=B, device=local)
+    vocab = low.vocab
+    prompts = np.array([prompt_ids(rank * B + b, vocab) for b in range(B)], np.int32)
+    stream = torch.cuda.ExternalStream(_engine_stream(eng), device=local)
+
+    def prefill():
+        eng.reset()
+        for s0 in range(0, PROMPT_LEN, CHUNK):
+            eng.step(prompts[:, s0:s0 + CHUNK], CHUNK)
+        return PROMPT_LEN
+
+    # parity: sequence 0 of rank 0 is the committed reference fixture's prompt
+    fx = None
+    fpath = ROOT / "tests" / "golden" / "full_models.json"
+    if rank == 0 and fpath.exists():
+        fx = json.loads(fpath.read_text()).get(DECODE_MODELS[a.workload][3])
+    pos = prefill()
+    bit_exact = None
+    if fx is not None and fx["prompt"] == prompts[0].tolist():
+        import hashlib
+        want = [r["logits_sha256"] for r in fx["runs"] if "logits_sha256" in r]
+        got = []
+        for i in range(len(want)):
+            if i:
+                eng.step(None)
+                pos += 1
+            got.append(hashlib.sha256(eng.logits()[0].astype("<f4").tobytes()).hexdigest())
+        bit_exact = got == want
+
+    def decode_steps(k: int):
+        nonlocal pos
+        for _ in range(k):
+            if pos + 1 > CONTEXT:                         # context full: start the batch over
+                pos = prefill()
+            eng.step(None)
+            pos += 1
+
+    decode_steps(a.warmup)
+    eng.sync()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(stream)
+        decode_steps(a.steps)
+        e1.record(stream)
+        eng.sync()
+    ms = e0.elapsed_time(e1)
+    barrier(world)
+    ms_max = max_over_ranks(ms, world)
+    value = world * B * a.steps / (ms_max / 1e3)
+
+    # roofline: the step's GEMV kernels (the weight stream) from one profiled step
+    if pos + 1 > CONTEXT:
+        pos = prefill()
+    prof = eng.profile()
+    pos += 1
+    kinds = {}
+    for k, t, nb in prof:
+        d = kinds.setdefault(k, [0, 0.0, 0])
+        d[0] += 1
+        d[1] += t
+        d[2] += nb
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    g = kinds["gemv"]
+    achieved = g[2] / (g[1] / 1e3) / 1e9
+    roofline = dict(bound="hbm", achieved=round(achieved, 1), peak=peak, unit="GB/s", frac=round(achieved / peak, 4),
+                    traffic=None, kernel="k_eng_gemv (W8A8 GEMV, all linears and the head)",
+                    kernel_bytes_per_step=g[2], kernel_launches_per_step=g[0], kernel_ms_per_step=round(g[1], 4),
+                    peak_source="measured" if peaks else "fallback",
+                    step_breakdown_ms={k: round(v[1], 4) for k, v in kinds.items()})
+
+    # e2e: the host in the loop as the reference's generate runs it: each step the token ids go up
+    # from pinned memory and the greedy picks come back
+    host_tok = torch.empty(B, dtype=torch.int32, pin_memory=True).numpy()
+    host_tok[:] = eng.tokens()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        if pos + 1 > CONTEXT:
+            pos = prefill()
+            host_tok[:] = eng.tokens()
+        eng.set_tokens(host_tok)
+        eng.step(None)
+        pos += 1
+        host_tok[:] = eng.tokens()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e = dict(value=round(world * B * a.steps / e2e_s, 1), unit="tok/s", h2d_bytes_per_step=4 * B,
+               d2h_bytes_per_step=4 * B, api="opentars_b200.engine.DecodeEngine: set_tokens, step, tokens")
+    eng.close()
+    if rank != 0:
+        return None
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(ms_max / a.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic: random-init weights (seeded, the reference's random_weights), seeded prompts",
+        "config": dict(workload=("config3_qwen3_0.6b_decode" if a.workload == "decode" else "config4_gemma3_1b_decode"),
+                       batch_per_gpu=B, prompt=PROMPT_LEN, prefill_chunk=CHUNK, context=CONTEXT,
+                       parallelism=f"independent sequences, {B} per GPU x {world} GPUs",
+                       l2="weights (596 MB Qwen3 / 1 GB Gemma-3) larger than L2, streamed once per step",
+                       model_build_s=round(build_s, 1)),
+        "roofline": roofline, "e2e": e2e, "gpu_launches": a.steps * len(prof), "clocks": clk.summary(),
+        "bit_exact_seq0_vs_reference": bit_exact,
+    }
+    if cpu is not None:
+        out["cpu_baseline"] = cpu
+    return out
+
+
+def _engine_stream(eng) -> int:
+    from opentars_b200.engine import lib as elib
+    return elib().tc_engine_stream(eng.h)
+
+
+def run_decode_reference(a, world, rank) -> dict | None:
+    """The reference arm for decode: the oracle's golden-Machine restatement on all host cores.
+    Each step every worker runs the next 1/16 of a decode step's queue (cycling in order)."""
+    if rank != 0:
+        return None
+    low = build_decode_model(a.workload)
+    _cpu_decode_prepare(low)
+    procs = os.cpu_count() or 1
+    per = -(-_CPU["n"] // 16)
+    vals = []
+    with _fork_pool(procs) as pool:
+        for i in range(a.warmup + a.steps):
+            t0 = time.perf_counter()
+            res = pool.map(_cpu_decode_slice, [per] * procs, chunksize=1)
+            dt = time.perf_counter() - t0
+            if i >= a.warmup:
+                vals.append(sum(d for d, _ in res) / _CPU["n"] / dt)
+    v = statistics.mean(vals)
+    cfg = dict(workload=("config3_qwen3_0.6b_decode" if a.workload == "decode" else "config4_gemma3_1b_decode"),
+               batch_per_gpu="one sequence per core", context=CONTEXT)
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic, seeded", "config": cfg,
+        "cpu_baseline": dict(value=round(v, 4), unit="tok/s", cores=procs, kind="port",
+                             sample=f"per step {procs} processes each run {per} descriptors of the decode queue "
+                                    f"({_CPU['n']} per token), in order"),
+        "e2e": dict(value=round(v, 4), unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+        "note": "the reference is Python (numpy golden model); its restatement in oracle/ is timed here",
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="gemv", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS) + sorted(DECODE_MODELS))
+    ap.add_argument("--batch", type=int, default=64, help="decode: sequences per GPU")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--units", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true")
@@ -373,12 +624,12 @@ def main():
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":                       # CPU only: no process group, no GPU
         world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
-        out = run_reference(a, world, rank)
+        out = run_decode_reference(a, world, rank) if a.workload in DECODE_MODELS else run_reference(a, world, rank)
         if out is not None:
             print(json.dumps(out), flush=True)
         return
     world, rank, local = dist_setup(a.gpus)
-    out = run_ours(a, world, rank, local)
+    out = run_decode(a, world, rank, local) if a.workload in DECODE_MODELS else run_ours(a, world, rank, local)
     if out is not None:
         print(json.dumps(out), flush=True)
     if world > 1:

@@ -62,6 +62,11 @@ int tc_engine_set_tokens(tc_engine* e, const int32_t* tokens_host);
 /* Each sequence's logits of its last token [batch][vocab]. */
 int tc_engine_logits(tc_engine* e, float* logits_host);
 int tc_engine_sync(tc_engine* e);
+/* Runs one decode step (n = 1, the previous picks as input) kernel by kernel, not captured, with
+ * events around each launch: ms[i], kind[i] (0 embed, 1 norm+quant, 2 GEMV, 3 q/k norm+RoPE,
+ * 4 attention, 5 quant, 6 argmax, 7 position) and the kernel's algorithmic bytes[i]. Returns the
+ * number of kernels (the step counts as a decode step: the position advances). */
+int tc_engine_profile(tc_engine* e, float* ms, int32_t* kind, uint64_t* bytes, uint32_t cap);
 
 #ifdef __cplusplus
 }

@@ -50,6 +50,11 @@ struct tc_engine {
   float *kc = nullptr, *vc = nullptr;        // [L][B][Tp][kvw]
   cudaGraphExec_t graph[5] = {};
   std::string err;
+  // profiling (tc_engine_profile): events around every kernel of one uncaptured step
+  bool prof = false;
+  std::vector<cudaEvent_t> pev;
+  std::vector<int> pkind;
+  std::vector<uint64_t> pbytes;
 };
 
 namespace {
@@ -61,6 +66,27 @@ int fail(tc_engine* e, const char* what, cudaError_t c) {
   do {                                              \
     cudaError_t _c = (expr);                        \
     if (_c != cudaSuccess) return fail(e, #expr, _c); \
+  } while (0)
+
+// A kernel launch of the step; when profiling, bracketed by events and tagged with its kind and
+// algorithmic bytes.
+enum { kKEmbed, kKNormQuant, kKGemv, kKQkRope, kKAttention, kKQuant, kKArgmax, kKAdvance };
+#define KERNEL(kind, bytes, expr)                                              \
+  do {                                                                         \
+    if (e->prof) {                                                             \
+      cudaEvent_t _a, _b;                                                      \
+      cudaEventCreate(&_a);                                                    \
+      cudaEventCreate(&_b);                                                    \
+      cudaEventRecord(_a, e->st);                                              \
+      TRY(expr);                                                               \
+      cudaEventRecord(_b, e->st);                                              \
+      e->pev.push_back(_a);                                                    \
+      e->pev.push_back(_b);                                                    \
+      e->pkind.push_back(kind);                                                \
+      e->pbytes.push_back(bytes);                                              \
+    } else {                                                                   \
+      TRY(expr);                                                               \
+    }                                                                          \
   } while (0)
 
 Lin lin_of(const uint8_t* base, const tc_lin& l) {
@@ -79,13 +105,23 @@ void add_seg(EngGemvArgs& g, const Lin& l, float* out, uint64_t ldo) {
   g.ncols += l.n;
 }
 
+// The algorithmic bytes of one engine GEMV: every weight row and scale once, the int8 rows and
+// their scales, the fp32 outputs (and residual rows read).
+uint64_t gemv_bytes(const EngGemvArgs& g) {
+  uint64_t b = (uint64_t)g.M * g.K + 4ull * g.M;
+  for (int s = 0; s < g.nseg; ++s) b += (uint64_t)g.seg[s].n * g.K + 4ull * g.seg[s].n;
+  const uint64_t ncols = g.mode == kEpiGated ? g.seg[0].n : g.ncols;
+  b += 4ull * g.M * ncols * (g.res ? 2 : 1);
+  return b;
+}
+
 // Enqueues one step for chunks of n tokens per sequence, starting at the device position.
 int enqueue_step(tc_engine* e, int n, const int* tok_in) {
   const tc_model_desc& md = e->md;
   const int B = e->B, M = B * n, H = e->H, I = e->I, qw = e->qw, kvw = e->kvw;
   const int ldq = std::max(std::max(H, I), qw);
   cudaStream_t st = e->st;
-  TRY(eng_embed(e->E, tok_in, e->x, H, md.gemma, md.embed_scale, M, st));
+  KERNEL(kKEmbed, (uint64_t)M * H * 8, eng_embed(e->E, tok_in, e->x, H, md.gemma, md.embed_scale, M, st));
   const float eps = md.eps;
   for (int li = 0; li < md.n_layers; ++li) {
     const Layer& L = e->layers[li];
@@ -96,7 +132,7 @@ int enqueue_step(tc_engine* e, int n, const int* tok_in) {
       NormQuantArgs a{};
       a.in = e->x; a.ld_in = H; a.gamma = L.ln_in; a.eps = eps; a.q = e->q8; a.ldq = ldq; a.qs = e->qs;
       a.H = H; a.rows = M; a.mode = 0;
-      TRY(eng_norm_quant(a, st));
+      KERNEL(kKNormQuant, (uint64_t)a.rows * a.H * (a.mode ? 13 : 5), eng_norm_quant(a, st));
     }
     {  // q | k | v
       EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, M, H);
@@ -104,35 +140,35 @@ int enqueue_step(tc_engine* e, int n, const int* tok_in) {
       add_seg(g, L.k, e->k, kvw);
       add_seg(g, L.v, e->v, kvw);
       g.mode = kEpiStore;
-      TRY(eng_gemv(g, st));
+      KERNEL(kKGemv, gemv_bytes(g), eng_gemv(g, st));
     }
     {
       QkRopeArgs a{};
       a.q = e->q; a.k = e->k; a.v = e->v; a.qr = e->qr; a.kc = kc; a.vc = vc; a.qn = L.qn; a.kn = L.kn;
       a.tab = L.tab; a.pos = e->pos; a.rows = M; a.n = n; a.nh = md.n_heads; a.nkv = md.n_kv; a.hd = md.head_dim;
       a.rot = md.rot; a.Tp = e->Tp; a.eps = eps;
-      TRY(eng_qk_rope(a, st));
+      KERNEL(kKQkRope, (uint64_t)M * (qw + 3 * kvw) * 8, eng_qk_rope(a, st));
     }
     {
       AttnArgs a{};
       a.qr = e->qr; a.kc = kc; a.vc = vc; a.att = e->att; a.pos = e->pos; a.n = n; a.nh = md.n_heads;
       a.nkv = md.n_kv; a.hd = md.head_dim; a.Tp = e->Tp;
-      TRY(eng_attention(a, B, st));
+      KERNEL(kKAttention, 0, eng_attention(a, B, st));
     }
-    TRY(eng_quant(e->att, qw, qw, e->q8, ldq, e->qs, M, st));
+    KERNEL(kKQuant, (uint64_t)M * qw * 5, eng_quant(e->att, qw, qw, e->q8, ldq, e->qs, M, st));
     {  // o; Qwen3 adds the residual in the epilogue
       EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, M, qw);
       add_seg(g, L.o, md.gemma ? e->o : e->x1, H);
       if (md.gemma) g.mode = kEpiStore;
       else { g.mode = kEpiResid; g.res = e->x; g.ldres = H; }
-      TRY(eng_gemv(g, st));
+      KERNEL(kKGemv, gemv_bytes(g), eng_gemv(g, st));
     }
     {  // [Gemma: attn_norm + residual] + ln_post + quant
       NormQuantArgs a{};
       a.eps = eps; a.q = e->q8; a.ldq = ldq; a.qs = e->qs; a.H = H; a.rows = M; a.gamma = L.ln_post;
       if (md.gemma) { a.mode = 2; a.in = e->o; a.ld_in = H; a.pre_gamma = L.attn_norm; a.res = e->x; a.x_out = e->x1; }
       else { a.mode = 0; a.in = e->x1; a.ld_in = H; }
-      TRY(eng_norm_quant(a, st));
+      KERNEL(kKNormQuant, (uint64_t)a.rows * a.H * (a.mode ? 13 : 5), eng_norm_quant(a, st));
     }
     {  // gate, up: act(gate) * up
       EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, M, H);
@@ -140,9 +176,9 @@ int enqueue_step(tc_engine* e, int n, const int* tok_in) {
       add_seg(g, L.up, e->g, I);
       g.mode = kEpiGated;
       g.act = md.act;
-      TRY(eng_gemv(g, st));
+      KERNEL(kKGemv, gemv_bytes(g), eng_gemv(g, st));
     }
-    TRY(eng_quant(e->g, I, I, e->q8, ldq, e->qs, M, st));
+    KERNEL(kKQuant, (uint64_t)M * I * 5, eng_quant(e->g, I, I, e->q8, ldq, e->qs, M, st));
     {  // down (K blocks on Gemma); Qwen3 adds the residual into x
       EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, M, I);
       Lin dl = L.down[0];
@@ -160,21 +196,21 @@ int enqueue_step(tc_engine* e, int n, const int* tok_in) {
         g.ldres = H;
       }
       if (L.n_down == 2) g.seg[0].W2 = L.down[1].W;   // the second K block's rows
-      TRY(eng_gemv(g, st));
+      KERNEL(kKGemv, gemv_bytes(g), eng_gemv(g, st));
     }
     if (md.gemma) {  // mlp_norm + residual, fused with the next layer's ln_in (or the final norm)
       NormQuantArgs a{};
       a.mode = 2; a.in = e->d; a.ld_in = H; a.pre_gamma = L.mlp_norm; a.res = e->x1; a.x_out = e->x;
       a.gamma = li + 1 < md.n_layers ? e->layers[li + 1].ln_in : e->final_norm;
       a.eps = eps; a.q = e->q8; a.ldq = ldq; a.qs = e->qs; a.H = H; a.rows = M;
-      TRY(eng_norm_quant(a, st));
+      KERNEL(kKNormQuant, (uint64_t)a.rows * a.H * (a.mode ? 13 : 5), eng_norm_quant(a, st));
     }
   }
   {  // final norm + quant of each sequence's last row, the head, the greedy pick
     NormQuantArgs a{};
     a.mode = 0; a.in = e->x + (uint64_t)(n - 1) * H; a.ld_in = (uint64_t)n * H; a.gamma = e->final_norm;
     a.eps = eps; a.q = e->q8; a.ldq = ldq; a.qs = e->qs; a.H = H; a.rows = B;
-    TRY(eng_norm_quant(a, st));
+    KERNEL(kKNormQuant, (uint64_t)a.rows * a.H * (a.mode ? 13 : 5), eng_norm_quant(a, st));
     EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, B, H);
     for (const Lin& l : e->head) {
       EngSeg& s = g.seg[g.nseg++];
@@ -182,10 +218,10 @@ int enqueue_step(tc_engine* e, int n, const int* tok_in) {
       g.ncols += l.n;
     }
     g.mode = kEpiStore;
-    TRY(eng_gemv(g, st));
-    TRY(eng_argmax(e->logits, md.vocab, B, e->next, 1, st));
+    KERNEL(kKGemv, gemv_bytes(g), eng_gemv(g, st));
+    KERNEL(kKArgmax, (uint64_t)B * md.vocab * 4, eng_argmax(e->logits, md.vocab, B, e->next, 1, st));
   }
-  TRY(eng_advance(e->pos, n, st));
+  KERNEL(kKAdvance, 0, eng_advance(e->pos, n, st));
   return TC_OK;
 }
 }  // namespace
@@ -302,6 +338,25 @@ int tc_engine_step(tc_engine* e, const int32_t* tokens_host, int32_t n) {
   }
   TRY(cudaGraphLaunch(e->graph[slot], e->st));
   return TC_OK;
+}
+
+int tc_engine_profile(tc_engine* e, float* ms, int32_t* kind, uint64_t* bytes, uint32_t cap) {
+  e->prof = true;
+  e->pev.clear(); e->pkind.clear(); e->pbytes.clear();
+  const int rc = enqueue_step(e, 1, e->next);
+  e->prof = false;
+  cudaError_t c = cudaStreamSynchronize(e->st);
+  const int n = (int)e->pkind.size();
+  for (int i = 0; i < n && i < (int)cap; ++i) {
+    cudaEventElapsedTime(&ms[i], e->pev[2 * i], e->pev[2 * i + 1]);
+    kind[i] = e->pkind[i];
+    bytes[i] = e->pbytes[i];
+  }
+  for (auto ev : e->pev) cudaEventDestroy(ev);
+  e->pev.clear();
+  if (rc != TC_OK) return rc;
+  if (c != cudaSuccess) return fail(e, "profile", c);
+  return n;
 }
 
 int tc_engine_set_tokens(tc_engine* e, const int32_t* tokens_host) {

@@ -54,7 +54,9 @@ ENGINE_SIGNATURES = {
     "tc_engine_set_tokens": (ctypes.c_int, [P, P]),
     "tc_engine_logits": (ctypes.c_int, [P, P]),
     "tc_engine_sync": (ctypes.c_int, [P]),
+    "tc_engine_profile": (ctypes.c_int, [P, P, P, P, ctypes.c_uint32]),
 }
+KERNEL_KINDS = ("embed", "norm_quant", "gemv", "qk_rope", "attention", "quant", "argmax", "advance")
 
 
 def lib():
@@ -171,6 +173,18 @@ class DecodeEngine:
 
     def sync(self):
         self._check(lib().tc_engine_sync(self.h), "sync")
+
+    def profile(self) -> list[tuple[str, float, int]]:
+        """One decode step kernel by kernel: [(kind, ms, algorithmic bytes)]."""
+        cap = 4096
+        ms = np.zeros(cap, np.float32)
+        kind = np.zeros(cap, np.int32)
+        nb = np.zeros(cap, np.uint64)
+        n = lib().tc_engine_profile(self.h, ms.ctypes.data_as(ctypes.c_void_p), kind.ctypes.data_as(ctypes.c_void_p),
+                                    nb.ctypes.data_as(ctypes.c_void_p), cap)
+        if n < 0:
+            self._check(n, "profile")
+        return [(KERNEL_KINDS[kind[i]], float(ms[i]), int(nb[i])) for i in range(n)]
 
     def generate(self, prompts, n_new: int, chunk: int = 4, keep_logits: bool = True):
         """Greedy decoding of B prompts of equal length: prefill in chunks of `chunk` tokens, then
