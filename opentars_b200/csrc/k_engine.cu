@@ -195,12 +195,14 @@ __global__ void __launch_bounds__(256) k_eng_gemv(EngGemvArgs g) {
     }
     // reduce the partial sums over the 32 lanes; lane m keeps row m
     int mine[2][2] = {{0, 0}, {0, 0}};
+    const int nsplit = g.kb < g.K ? 2 : 1;
 #pragma unroll
     for (int w = 0; w < 2; ++w)
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int m = 0; m < MB; ++m) {
+          if (w >= nrows || h >= nsplit || m >= mb) continue;   // warp-uniform
           int v = acc[w][h][m];
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
@@ -220,6 +222,86 @@ __global__ void __launch_bounds__(256) k_eng_gemv(EngGemvArgs g) {
       }
       if (g.mode == kEpiKSplit) y = fadd(ftz(ep(mine[0][0], sg)), ftz(ep(mine[0][1], sg)));
       else y = ep(mine[0][0], sg);
+      if (g.res) y = fadd(g.res[(uint64_t)m * g.ldres + col], y);
+      sg.out[(uint64_t)m * sg.ldo + c] = ftz(y);
+    }
+  }
+}
+
+// Batched GEMM for M > 8 token rows: one lane per token row. A block stages 32 rows of A in shared
+// memory (row stride K + 16 bytes, so the 8 lanes of each 16-byte access phase hit 8 different
+// bank groups) and its warps stream output columns: each lane holds the 16-byte weight slices
+// k = lane*16 + 512u of the column, and the slices are broadcast to the warp with shuffles, so
+// every lane accumulates its own row's exact int32 dot product with no cross-lane reduction.
+// Same segments and epilogue modes as k_eng_gemv.
+template <int KU>
+__global__ void __launch_bounds__(128) k_eng_gemm_tl(EngGemvArgs g) {
+  extern __shared__ __align__(16) int8_t sAt[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * 32;
+  const int mb = min(32, g.M - m0);
+  const int ld = g.K + 16;
+  const int nw = gridDim.x * 4;
+  const int ncols = g.mode == kEpiGated ? g.seg[0].n : g.ncols;
+  const int kv = g.K / 16;
+  for (int i = threadIdx.x; i < mb * kv; i += blockDim.x) {
+    const int m = i / kv, kk = (i - m * kv) * 16;
+    *reinterpret_cast<uint4*>(&sAt[m * ld + kk]) = *reinterpret_cast<const uint4*>(g.A + (uint64_t)(m0 + m) * g.lda + kk);
+  }
+  __syncthreads();
+  const int nrows = g.mode == kEpiGated ? 2 : 1;
+  const int8_t* arow = sAt + (lane < mb ? lane : 0) * ld;
+  for (int col = blockIdx.x * 4 + warp; col < ncols; col += nw) {
+    int s = 0;
+    while (s + 1 < g.nseg && col >= g.seg[s + 1].n0) ++s;
+    const int c = col - g.seg[s].n0;
+    int acc[2][2] = {{0, 0}, {0, 0}};          // [weight row][K block]
+    for (int w = 0; w < nrows; ++w) {
+      const EngSeg& sg = g.seg[w == 0 ? s : 1];
+      const int8_t* w1 = sg.W + (uint64_t)c * g.kb;
+      const int8_t* w2 = sg.W2 + (uint64_t)c * (g.K - g.kb) - g.kb;
+      uint4 wv[KU];
+#pragma unroll
+      for (int u = 0; u < KU; ++u) {
+        const int k = lane * 16 + 512 * u;
+        wv[u] = k >= g.K ? make_uint4(0, 0, 0, 0) : ldg_stream(k < g.kb ? w1 + k : w2 + k);
+      }
+#pragma unroll
+      for (int u = 0; u < KU; ++u) {
+        if (512 * u >= g.K) break;
+#pragma unroll 4
+        for (int src = 0; src < 32; ++src) {
+          const int k = src * 16 + 512 * u;
+          if (k >= g.K) break;
+          const uint32_t x = __shfl_sync(0xFFFFFFFFu, wv[u].x, src);
+          const uint32_t y = __shfl_sync(0xFFFFFFFFu, wv[u].y, src);
+          const uint32_t z = __shfl_sync(0xFFFFFFFFu, wv[u].z, src);
+          const uint32_t q = __shfl_sync(0xFFFFFFFFu, wv[u].w, src);
+          const uint4 av = *reinterpret_cast<const uint4*>(arow + k);
+          const int h = k >= g.kb ? 1 : 0;
+          int v = acc[w][h];
+          v = __dp4a((int)av.x, (int)x, v);
+          v = __dp4a((int)av.y, (int)y, v);
+          v = __dp4a((int)av.z, (int)z, v);
+          v = __dp4a((int)av.w, (int)q, v);
+          acc[w][h] = v;
+        }
+      }
+    }
+    if (lane < mb) {
+      const int m = m0 + lane;
+      const float sr = g.srow[m];
+      auto ep = [&](int acc_v, const EngSeg& sg) { return fmul(fmul(i2f(acc_v), sr), sg.scale[c]); };
+      const EngSeg& sg = g.seg[s];
+      if (g.mode == kEpiGated) {
+        const float yg = ftz(act_fn(ep(acc[0][0] + acc[0][1], g.seg[0]), g.act));
+        const float yu = ep(acc[1][0] + acc[1][1], g.seg[1]);
+        g.seg[0].out[(uint64_t)m * g.seg[0].ldo + c] = ftz(fmul(yg, yu));
+        continue;
+      }
+      float y;
+      if (g.mode == kEpiKSplit) y = fadd(ftz(ep(acc[0][0], sg)), ftz(ep(acc[0][1], sg)));
+      else y = ep(acc[0][0] + acc[0][1], sg);
       if (g.res) y = fadd(g.res[(uint64_t)m * g.ldres + col], y);
       sg.out[(uint64_t)m * sg.ldo + c] = ftz(y);
     }
@@ -274,56 +356,101 @@ __global__ void __launch_bounds__(128) k_qk_rope(QkRopeArgs a) {
 }
 
 // ------------------------------------------------------------------------------- attention
-// One block per (sequence, query head): FDOT NT of the head's n query rows against the sequence's
-// K cache rows 0 .. nk-1 (nk = pad16(t0 + n), zero rows beyond the tokens written), the causal
-// softmax of each row over its first t0 + 1 + m keys, FDOT NN against the V cache in key order
-// (llm.py:735-746; numerics.py:362-371, 393-409).
-__global__ void __launch_bounds__(128) k_attention(AttnArgs a) {
-  __shared__ float sq[4][256];
-  __shared__ float sp[4][kT];
-  __shared__ float red[33];
-  const int b = blockIdx.x / a.nh, h = blockIdx.x - b * a.nh;
-  const int kvh = h / (a.nh / a.nkv);
-  const int n = a.n, hd = a.hd, t0 = *a.pos;
+// One block per (sequence, KV head), serving the G = nh / nkv query heads that share it: FDOT NT of
+// each head's n query rows against the sequence's K cache rows 0 .. nk-1 (nk = pad16(t0 + n), the
+// rows beyond the tokens written are zeros), the causal softmax of each row over its first
+// t0 + 1 + m keys, FDOT NN against the V cache in key order (llm.py:735-746; numerics.py:362-371,
+// 393-409). K and V are staged in shared memory in tiles of up to kTile keys (all threads load,
+// many 16-byte loads in flight); the per-output FDOT NN chain carries its accumulator across tiles.
+constexpr int kAttnThreads = 256;
+constexpr int kMaxRows = 16;                 // G * n query rows per block
+__global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a, int tile) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int hd = a.hd, n = a.n, G = a.nh / a.nkv, R = G * n;
+  float* sq = sm;                          // [R][hd] query rows (flushed)
+  float* sp = sq + R * hd;                 // [R][kT] scores, then probabilities
+  float* skv = sp + R * kT;                // [tile][hd] K or V rows
+  const int b = blockIdx.x / a.nkv, kvh = blockIdx.x - b * a.nkv;
+  const int t0 = *a.pos;
   const int nk = ((t0 + n) + 15) / 16 * 16;
-  const int tid = threadIdx.x, hw = tid >> 4, l = tid & 15;
-  for (int i = tid; i < n * hd; i += blockDim.x) {
-    const int m = i / hd, d = i - m * hd;
-    sq[m][d] = ftz(a.qr[((uint64_t)(b * n + m) * a.nh + h) * hd + d]);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hw = tid >> 4, l = tid & 15;
+  // query rows: r = g * n + m is head kvh * G + g, token m
+  for (int i = tid; i < R * hd; i += kAttnThreads) {
+    const int r = i / hd, d = i - r * hd, g = r / n, m = r - g * n;
+    sq[i] = ftz(a.qr[((uint64_t)(b * n + m) * a.nh + kvh * G + g) * hd + d]);
   }
-  __syncthreads();
-  const float* K = a.kc + ((uint64_t)b * a.Tp * a.nkv + kvh) * hd;       // row j at K + j * nkv * hd
-  const float* V = a.vc + ((uint64_t)b * a.Tp * a.nkv + kvh) * hd;
   const uint64_t kstride = (uint64_t)a.nkv * hd;
-  // scores: one half-warp per (m, j), lane chains over d = l, l + 16, ...
-  for (int p = hw; p < n * nk; p += 8) {
-    const int m = p / nk, j = p - m * nk;
-    const float* kr = K + (uint64_t)j * kstride;
-    float s = 0.0f;
-    for (int d = l; d < hd; d += 16) s = fadd_nc(s, fmul(sq[m][d], kr[d]));
-    s = sum16_fold(canon(s));
-    if (l == 0) sp[m][j] = s;
+  const float* K = a.kc + ((uint64_t)b * a.Tp * a.nkv + kvh) * hd;
+  const float* V = a.vc + ((uint64_t)b * a.Tp * a.nkv + kvh) * hd;
+  const int hd4 = hd / 4;
+  // scores, tile by tile: one half-warp per (row, key), lane chains over d = l, l + 16, ...
+  for (int j0 = 0; j0 < nk; j0 += tile) {
+    const int tk = min(tile, nk - j0);
+    __syncthreads();
+    for (int i = tid; i < tk * hd4; i += kAttnThreads) {
+      const int j = i / hd4, d4 = i - j * hd4;
+      reinterpret_cast<float4*>(skv)[i] = reinterpret_cast<const float4*>(K + (uint64_t)(j0 + j) * kstride)[d4];
+    }
+    __syncthreads();
+    for (int p = hw; p < R * tk; p += kAttnThreads / 16) {
+      const int r = p / tk, j = p - r * tk;
+      float s = 0.0f;
+      for (int d = l; d < hd; d += 16) s = fadd_nc(s, fmul(sq[r * hd + d], skv[j * hd + d]));
+      s = sum16_fold(canon(s), 0xFFFFu << (lane & 16));
+      if (l == 0) sp[r * kT + j0 + j] = s;
+    }
   }
   __syncthreads();
-  // causal softmax per row (valid = t0 + 1 + m), numerics.py:362-371
-  for (int m = 0; m < n; ++m) {
+  // causal softmax, one warp per row; valid = t0 + 1 + m keys (numerics.py:362-371)
+  for (int r = warp; r < R; r += kAttnThreads / 32) {
+    const int m = r % n;
     const int valid = min(nk, t0 + 1 + m);
+    float* row = sp + r * kT;
     float mx = bf(0xFF800000u);
-    for (int j = tid; j < valid; j += blockDim.x) mx = fmax_c(mx, ftz(sp[m][j]));
-    mx = block_max(mx, red);
-    __syncthreads();
-    for (int j = tid; j < nk; j += blockDim.x) sp[m][j] = j < valid ? exp_f(fadd(sp[m][j], neg(mx))) : 0.0f;
-    const float r = recip_f(block_sum16(sp[m], nk, red));
-    __syncthreads();
-    for (int j = tid; j < nk; j += blockDim.x) sp[m][j] = ftz(fmul(sp[m][j], r));
-    __syncthreads();
+    for (int j = lane; j < valid; j += 32) mx = fmax_c(mx, ftz(row[j]));
+    mx = warp_max(mx);
+    for (int j = lane; j < nk; j += 32) row[j] = j < valid ? exp_f(fadd(ftz(row[j]), neg(mx))) : 0.0f;
+    __syncwarp();
+    float acc = 0.0f;                                    // lanes 16..31 repeat lanes 0..15's chains
+    for (int j = lane & 15; j < nk; j += 16) acc = fadd_nc(acc, row[j]);
+    const float r_ = recip_f(sum16_fold(canon(acc)));
+    __syncwarp();
+    for (int j = lane; j < nk; j += 32) row[j] = ftz(fmul(row[j], r_));
   }
-  // FDOT NN: out[m][d] = k-order chain over the nk keys
-  for (int i = tid; i < n * hd; i += blockDim.x) {
-    const int m = i / hd, d = i - m * hd;
-    float acc = 0.0f;
-    for (int j = 0; j < nk; ++j) acc = fadd_nc(acc, fmul(sp[m][j], V[(uint64_t)j * kstride + d]));
-    a.att[((uint64_t)(b * n + m) * a.nh + h) * hd + d] = ftz(canon(acc));
+  // FDOT NN: out[r][d] = k-order chain over the nk keys, V staged tile by tile
+  constexpr int kPer = (kMaxRows * 256 + kAttnThreads - 1) / kAttnThreads;
+  float acc[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) acc[i] = 0.0f;
+  const int outs = R * hd;
+  for (int j0 = 0; j0 < nk; j0 += tile) {
+    const int tk = min(tile, nk - j0);
+    __syncthreads();
+    for (int i = tid; i < tk * hd4; i += kAttnThreads) {
+      const int j = i / hd4, d4 = i - j * hd4;
+      reinterpret_cast<float4*>(skv)[i] = reinterpret_cast<const float4*>(V + (uint64_t)(j0 + j) * kstride)[d4];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int o = tid + i * kAttnThreads;
+      if (o < outs) {
+        const int r = o / hd, d = o - r * hd;
+        const float* pr = sp + r * kT + j0;
+        float v = acc[i];
+        for (int j = 0; j < tk; ++j) v = fadd_nc(v, fmul(pr[j], skv[j * hd + d]));
+        acc[i] = v;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int o = tid + i * kAttnThreads;
+    if (o < outs) {
+      const int r = o / hd, d = o - r * hd, g = r / n, m = r - g * n;
+      a.att[((uint64_t)(b * n + m) * a.nh + kvh * G + g) * hd + d] = ftz(canon(acc[i]));
+    }
   }
 }
 
@@ -400,8 +527,26 @@ static cudaError_t gemv_m(const EngGemvArgs& g, cudaStream_t st) {
   if constexpr (MB <= 4) return gemv_mk<MB, 14>(g, st);
   return cudaErrorInvalidValue;
 }
+template <int KU>
+static cudaError_t gemm_tl(const EngGemvArgs& g, cudaStream_t st) {
+  const int ncols = g.mode == kEpiGated ? g.seg[0].n : g.ncols;
+  const int smem = 32 * (g.K + 16);
+  cudaError_t e = cudaFuncSetAttribute(k_eng_gemm_tl<KU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  const int yb = (g.M + 31) / 32;
+  const int blocks = std::min((ncols + 3) / 4, std::max(1, 148 * 8 / yb));
+  k_eng_gemm_tl<KU><<<dim3(blocks, yb), 128, smem, st>>>(g);
+  return cudaGetLastError();
+}
+
 cudaError_t eng_gemv(const EngGemvArgs& g, cudaStream_t st) {
   if (g.K > 14 * 512 || g.K % 16) return cudaErrorInvalidValue;
+  if (g.M > 8) {
+    if (g.K <= 1024) return gemm_tl<2>(g, st);
+    if (g.K <= 2048) return gemm_tl<4>(g, st);
+    if (g.K <= 4096) return gemm_tl<8>(g, st);
+    return gemm_tl<14>(g, st);
+  }
   if (g.M == 1) return gemv_m<1>(g, st);
   if (g.M == 2) return gemv_m<2>(g, st);
   if (g.M <= 4 || g.K > 4096) return gemv_m<4>(g, st);   // 8 rows of K > 4096 exceed static shared memory
@@ -413,7 +558,16 @@ cudaError_t eng_qk_rope(const QkRopeArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 cudaError_t eng_attention(const AttnArgs& a, int batch, cudaStream_t st) {
-  k_attention<<<batch * a.nh, 128, 0, st>>>(a);
+  const int G = a.nh / a.nkv, R = G * a.n;
+  if (a.nh % a.nkv || R > kMaxRows || a.hd > 256 || a.hd % 16) return cudaErrorInvalidValue;
+  const int fixed = (R * a.hd + R * kT) * 4;
+  const int budget = 200 * 1024 - fixed;                  // shared memory left for a K / V tile
+  int tile = std::min(kT, budget / (a.hd * 4)) / 16 * 16;
+  if (tile < 16) return cudaErrorInvalidValue;
+  const int smem = fixed + tile * a.hd * 4;
+  cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  k_attention<<<batch * a.nkv, kAttnThreads, smem, st>>>(a, tile);
   return cudaGetLastError();
 }
 cudaError_t eng_argmax(const float* logits, int vocab, int batch, int* tok_out, int tok_stride, cudaStream_t st) {

@@ -24,16 +24,18 @@ def test_engine_batch1_matches_reference_small(name):
     eng.close()
 
 
+@pytest.mark.parametrize("batch", [3, 33])
 @pytest.mark.parametrize("name", sorted(FX.models()))
-def test_engine_batch3_each_sequence_matches_oracle(name):
-    """Three prompts decoded together; each sequence equals its own single-sequence oracle run."""
+def test_engine_batch_each_sequence_matches_oracle(name, batch):
+    """Prompts decoded together (batch 33: the batched-GEMM path, two row blocks); each sequence
+    equals its own single-sequence oracle run."""
     from opentars_b200.engine import DecodeEngine
     from oracle.machine import OracleMachine
     fx = FX.models()[name]
     rng = np.random.default_rng(11)
     P = len(fx["prompt"])
-    prompts = [fx["prompt"]] + [list(map(int, rng.integers(0, fx["vocab"], P))) for _ in range(2)]
-    eng = DecodeEngine(build_lowering(fx), batch=3)
+    prompts = [fx["prompt"]] + [list(map(int, rng.integers(0, fx["vocab"], P))) for _ in range(batch - 1)]
+    eng = DecodeEngine(build_lowering(fx), batch=batch)
     ids, logits = eng.generate(prompts, 3, chunk=4)
     eng.close()
     for b, pr in enumerate(prompts):
