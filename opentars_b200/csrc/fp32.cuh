@@ -220,6 +220,16 @@ __device__ __forceinline__ void st_u16(uint8_t* p, uint16_t v) {
   p[0] = (uint8_t)v; p[1] = (uint8_t)(v >> 8);
 }
 
+// Asynchronous 16-byte global -> shared copies (both addresses 16-byte aligned): a staging loop
+// issues all of its copies before waiting once, instead of one dependent load per iteration.
+__device__ __forceinline__ void cp16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // golden.py:273-280: one output element in the descriptor's format (fp32 flushed, bf16 RNE,
 // int8 via q8 with OUT_SCALE, fp16 IEEE RNE)
 __device__ __forceinline__ void store_out(uint8_t* row, int n, float y, int out, float out_scale) {

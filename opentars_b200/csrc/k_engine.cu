@@ -82,7 +82,10 @@ __global__ void __launch_bounds__(256) k_norm_quant(NormQuantArgs a) {
   const int r = blockIdx.x, H = a.H, t = threadIdx.x;
   const float kinv = recip_f(i2f(H));
   const float* in = a.in + (uint64_t)r * a.ld_in;
-  for (int j = t; j < H; j += blockDim.x) sx[j] = ftz(in[j]);
+  for (int j4 = t; j4 < H / 4; j4 += blockDim.x) cp16(sx + 4 * j4, in + 4 * j4);
+  cp_wait_all();
+  __syncthreads();
+  for (int j = t; j < H; j += blockDim.x) sx[j] = ftz(sx[j]);
   if (a.mode == 2) {
     __syncthreads();
     for (int j = t; j < H; j += blockDim.x) sv[j] = fmul(sx[j], sx[j]);
@@ -117,9 +120,14 @@ __global__ void __launch_bounds__(256) k_norm_quant(NormQuantArgs a) {
 
 // ROW_QUANT alone (attention output, gate * up), numerics.py:383-390
 __global__ void __launch_bounds__(256) k_quant(const float* x, int ldx, int N, int8_t* q, int ldq, float* qs) {
+  extern __shared__ float4 qrow4[];
+  float* row = reinterpret_cast<float*>(qrow4);
   __shared__ float red[33];
   const int r = blockIdx.x;
-  const float* row = x + (uint64_t)r * ldx;
+  const float* src = x + (uint64_t)r * ldx;
+  for (int j4 = threadIdx.x; j4 < N / 4; j4 += blockDim.x) cp16(row + 4 * j4, src + 4 * j4);
+  cp_wait_all();
+  __syncthreads();
   float amax = 0.0f;
   for (int j = threadIdx.x; j < N; j += blockDim.x) amax = fmax_c(amax, fabs_c(row[j]));
   amax = block_max(amax, red);
@@ -146,8 +154,9 @@ __global__ void __launch_bounds__(256) k_eng_gemv(EngGemvArgs g) {
   const int kv = g.K / 16;
   for (int i = threadIdx.x; i < mb * kv; i += blockDim.x) {
     const int m = i / kv, kk = (i - m * kv) * 16;
-    *reinterpret_cast<uint4*>(&sA[m * 512 * KU + kk]) = *reinterpret_cast<const uint4*>(g.A + (uint64_t)(m0 + m) * g.lda + kk);
+    cp16(&sA[m * 512 * KU + kk], g.A + (uint64_t)(m0 + m) * g.lda + kk);
   }
+  cp_wait_all();
   __syncthreads();
   for (int col = blockIdx.x * 8 + warp; col < ncols; col += nw) {
     int s = 0;
@@ -246,8 +255,9 @@ __global__ void __launch_bounds__(128) k_eng_gemm_tl(EngGemvArgs g) {
   const int kv = g.K / 16;
   for (int i = threadIdx.x; i < mb * kv; i += blockDim.x) {
     const int m = i / kv, kk = (i - m * kv) * 16;
-    *reinterpret_cast<uint4*>(&sAt[m * ld + kk]) = *reinterpret_cast<const uint4*>(g.A + (uint64_t)(m0 + m) * g.lda + kk);
+    cp16(&sAt[m * ld + kk], g.A + (uint64_t)(m0 + m) * g.lda + kk);
   }
+  cp_wait_all();
   __syncthreads();
   const int nrows = g.mode == kEpiGated ? 2 : 1;
   const int8_t* arow = sAt + (lane < mb ? lane : 0) * ld;
@@ -390,8 +400,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a, int tile
     __syncthreads();
     for (int i = tid; i < tk * hd4; i += kAttnThreads) {
       const int j = i / hd4, d4 = i - j * hd4;
-      reinterpret_cast<float4*>(skv)[i] = reinterpret_cast<const float4*>(K + (uint64_t)(j0 + j) * kstride)[d4];
+      cp16(reinterpret_cast<float4*>(skv) + i, reinterpret_cast<const float4*>(K + (uint64_t)(j0 + j) * kstride) + d4);
     }
+    cp_wait_all();
     __syncthreads();
     for (int p = hw; p < R * tk; p += kAttnThreads / 16) {
       const int r = p / tk, j = p - r * tk;
@@ -429,8 +440,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a, int tile
     __syncthreads();
     for (int i = tid; i < tk * hd4; i += kAttnThreads) {
       const int j = i / hd4, d4 = i - j * hd4;
-      reinterpret_cast<float4*>(skv)[i] = reinterpret_cast<const float4*>(V + (uint64_t)(j0 + j) * kstride)[d4];
+      cp16(reinterpret_cast<float4*>(skv) + i, reinterpret_cast<const float4*>(V + (uint64_t)(j0 + j) * kstride) + d4);
     }
+    cp_wait_all();
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
@@ -509,7 +521,12 @@ cudaError_t eng_norm_quant(const NormQuantArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 cudaError_t eng_quant(const float* x, int ldx, int N, int8_t* q, int ldq, float* qs, int rows, cudaStream_t st) {
-  k_quant<<<rows, 256, 0, st>>>(x, ldx, N, q, ldq, qs);
+  const int smem = N * 4;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+  }
+  k_quant<<<rows, 256, smem, st>>>(x, ldx, N, q, ldq, qs);
   return cudaGetLastError();
 }
 template <int MB, int KU>

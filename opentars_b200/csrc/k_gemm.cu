@@ -141,9 +141,9 @@ __global__ void __launch_bounds__(kThreads) k_gemv8(GemmArgs g) {
   const int kv = g.K / 16;
   for (int i = threadIdx.x; i < mb * kv; i += kThreads) {
     const int m = i / kv, kk = (i - m * kv) * 16;
-    *reinterpret_cast<uint4*>(&sA[m * 512 * KU + kk]) =
-        *reinterpret_cast<const uint4*>(g.A + (uint64_t)(m0 + m) * g.lda + kk);
+    cp16(&sA[m * 512 * KU + kk], g.A + (uint64_t)(m0 + m) * g.lda + kk);
   }
+  cp_wait_all();
   __syncthreads();
   for (; n < g.N; n += nw) {
     const int nn = n + nw;

@@ -130,10 +130,10 @@ __global__ void __launch_bounds__(kRT) k_rowop(RowArgs a) {
   const uint8_t* x = a.X + (uint64_t)m * a.lda;
   uint8_t* y = a.Y + (uint64_t)m * a.ldy;
   if (((uintptr_t)x & 15) == 0) {
-    for (int i = t; i < N / 4; i += kRT) {
-      const float4 v = reinterpret_cast<const float4*>(x)[i];
-      sx[4 * i] = ftz(v.x); sx[4 * i + 1] = ftz(v.y); sx[4 * i + 2] = ftz(v.z); sx[4 * i + 3] = ftz(v.w);
-    }
+    for (int i = t; i < N / 4; i += kRT) cp16(sx + 4 * i, x + 16 * (uint64_t)i);
+    cp_wait_all();
+    __syncthreads();
+    for (int j = t; j < N; j += kRT) sx[j] = ftz(sx[j]);
   } else {
     for (int j = t; j < N; j += kRT) sx[j] = ftz(ld_f32(x + 4 * (uint64_t)j));
   }

@@ -130,8 +130,8 @@ __global__ void __launch_bounds__(kThreads) k_gemv_w4(W4Args g, bool vec) {
     const uint8_t* row = g.A + (uint64_t)(m0 + m) * g.lda;
     uint32_t* dst = sX + m * g.K;
     if (!g.a_bf16 && ((uintptr_t)row & 15) == 0) {
-      for (int i = threadIdx.x; i < g.K / 4; i += kThreads)
-        reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(row)[i];
+      for (int i = threadIdx.x; i < g.K / 4; i += kThreads) cp16(dst + 4 * i, row + 16 * (uint64_t)i);
+      cp_wait_all();
     } else {
       for (int k = threadIdx.x; k < g.K; k += kThreads)
         dst[k] = g.a_bf16 ? ((uint32_t)ld_u16(row + 2 * (uint64_t)k) << 16) : ld_u32(row + 4 * (uint64_t)k);
