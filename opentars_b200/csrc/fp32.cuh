@@ -32,6 +32,9 @@ __device__ __forceinline__ float canon(float x) { return is_nan(x) ? bf(0x7FC000
 // flush-to-zero add is exact here: both operands are multiples of 2^-149, so a sum below 2^-126
 // is exactly representable, is never rounded, and is flushed with its sign either way.
 __device__ __forceinline__ float fmul(float a, float b) { return canon(ftz(__fmul_rn(ftz(a), ftz(b)))); }
+// The product of operands already flushed (values this library stored): only the result's
+// flush remains; a NaN it returns is canonicalised by the caller where the value is kept.
+__device__ __forceinline__ float fmul_ff(float a, float b) { return ftz(__fmul_rn(a, b)); }
 __device__ __forceinline__ float fadd_nc(float a, float b) {   // without canonicalising NaN
   float r;
   asm("add.rn.ftz.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));

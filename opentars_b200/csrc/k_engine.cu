@@ -374,84 +374,112 @@ __global__ void __launch_bounds__(128) k_qk_rope(QkRopeArgs a) {
 // many 16-byte loads in flight); the per-output FDOT NN chain carries its accumulator across tiles.
 constexpr int kAttnThreads = 256;
 constexpr int kMaxRows = 16;                 // G * n query rows per block
+// K / V rows in shared memory are padded by 4 floats: a warp's 32 threads read 32 different rows
+// at the same column, and the padding puts each 16-byte access of a phase in its own bank group.
+template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a, int tile) {
+  constexpr int LD = HD + 4;
   extern __shared__ float4 smem4[];
-  float* sm = reinterpret_cast<float*>(smem4);
-  const int hd = a.hd, n = a.n, G = a.nh / a.nkv, R = G * n;
-  float* sq = sm;                          // [R][hd] query rows (flushed)
-  float* sp = sq + R * hd;                 // [R][kT] scores, then probabilities
-  float* skv = sp + R * kT;                // [tile][hd] K or V rows
+  const int n = a.n, G = a.nh / a.nkv, R = G * n;
+  float* sq = reinterpret_cast<float*>(smem4);   // [R][HD] query rows (flushed)
+  float* sp = sq + R * HD;                        // [R][kT] scores, then probabilities
+  float* skv = sp + R * kT;                       // [tile][LD] K or V rows
+  __shared__ float srow[2][kMaxRows];             // per row: max, then 1 / sum
   const int b = blockIdx.x / a.nkv, kvh = blockIdx.x - b * a.nkv;
   const int t0 = *a.pos;
   const int nk = ((t0 + n) + 15) / 16 * 16;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hw = tid >> 4, l = tid & 15;
-  // query rows: r = g * n + m is head kvh * G + g, token m
-  for (int i = tid; i < R * hd; i += kAttnThreads) {
-    const int r = i / hd, d = i - r * hd, g = r / n, m = r - g * n;
-    sq[i] = ftz(a.qr[((uint64_t)(b * n + m) * a.nh + kvh * G + g) * hd + d]);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < R * HD; i += kAttnThreads) {
+    const int r = i / HD, d = i - r * HD, g = r / n, m = r - g * n;
+    sq[i] = ftz(a.qr[((uint64_t)(b * n + m) * a.nh + kvh * G + g) * HD + d]);
   }
-  const uint64_t kstride = (uint64_t)a.nkv * hd;
-  const float* K = a.kc + ((uint64_t)b * a.Tp * a.nkv + kvh) * hd;
-  const float* V = a.vc + ((uint64_t)b * a.Tp * a.nkv + kvh) * hd;
-  const int hd4 = hd / 4;
-  // scores, tile by tile: one half-warp per (row, key), lane chains over d = l, l + 16, ...
-  for (int j0 = 0; j0 < nk; j0 += tile) {
-    const int tk = min(tile, nk - j0);
+  const uint64_t kstride = (uint64_t)a.nkv * HD;
+  const float* K = a.kc + ((uint64_t)b * a.Tp * a.nkv + kvh) * HD;
+  const float* V = a.vc + ((uint64_t)b * a.Tp * a.nkv + kvh) * HD;
+  auto stage = [&](const float* src, int j0, int tk) {
     __syncthreads();
-    for (int i = tid; i < tk * hd4; i += kAttnThreads) {
-      const int j = i / hd4, d4 = i - j * hd4;
-      cp16(reinterpret_cast<float4*>(skv) + i, reinterpret_cast<const float4*>(K + (uint64_t)(j0 + j) * kstride) + d4);
+    for (int i = tid; i < tk * (HD / 4); i += kAttnThreads) {
+      const int j = i / (HD / 4), d4 = i - j * (HD / 4);
+      cp16(skv + j * LD + 4 * d4, src + (uint64_t)(j0 + j) * kstride + 4 * d4);
     }
     cp_wait_all();
     __syncthreads();
-    for (int p = hw; p < R * tk; p += kAttnThreads / 16) {
+  };
+  // scores: one thread per (row, key) runs the 16 lane chains of sum16 (element d to chain d mod 16,
+  // in d order) and their pairwise fold itself
+  for (int j0 = 0; j0 < nk; j0 += tile) {
+    const int tk = min(tile, nk - j0);
+    stage(K, j0, tk);
+    for (int p = tid; p < R * tk; p += kAttnThreads) {
       const int r = p / tk, j = p - r * tk;
-      float s = 0.0f;
-      for (int d = l; d < hd; d += 16) s = fadd_nc(s, fmul(sq[r * hd + d], skv[j * hd + d]));
-      s = sum16_fold(canon(s), 0xFFFFu << (lane & 16));
-      if (l == 0) sp[r * kT + j0 + j] = s;
+      const float* qr = sq + r * HD;
+      const float* kr = skv + j * LD;
+      float c[16];
+#pragma unroll
+      for (int l = 0; l < 16; ++l) c[l] = 0.0f;
+#pragma unroll
+      for (int d = 0; d < HD; d += 16) {
+#pragma unroll
+        for (int l4 = 0; l4 < 4; ++l4) {
+          const float4 qv = *reinterpret_cast<const float4*>(qr + d + 4 * l4);
+          const float4 kv = *reinterpret_cast<const float4*>(kr + d + 4 * l4);
+          c[4 * l4 + 0] = fadd_nc(c[4 * l4 + 0], fmul_ff(qv.x, kv.x));
+          c[4 * l4 + 1] = fadd_nc(c[4 * l4 + 1], fmul_ff(qv.y, kv.y));
+          c[4 * l4 + 2] = fadd_nc(c[4 * l4 + 2], fmul_ff(qv.z, kv.z));
+          c[4 * l4 + 3] = fadd_nc(c[4 * l4 + 3], fmul_ff(qv.w, kv.w));
+        }
+      }
+#pragma unroll
+      for (int w = 1; w < 16; w *= 2)
+#pragma unroll
+        for (int l = 0; l < 16; l += 2 * w) c[l] = fadd_nc(c[l], c[l + w]);
+      sp[r * kT + j0 + j] = ftz(canon(c[0]));
     }
   }
   __syncthreads();
-  // causal softmax, one warp per row; valid = t0 + 1 + m keys (numerics.py:362-371)
+  // causal softmax (numerics.py:362-371): row maxima, exps over the block, ordered sums, scaling
   for (int r = warp; r < R; r += kAttnThreads / 32) {
-    const int m = r % n;
-    const int valid = min(nk, t0 + 1 + m);
-    float* row = sp + r * kT;
+    const int valid = min(nk, t0 + 1 + r % n);
     float mx = bf(0xFF800000u);
-    for (int j = lane; j < valid; j += 32) mx = fmax_c(mx, ftz(row[j]));
+    for (int j = lane; j < valid; j += 32) mx = fmax_c(mx, sp[r * kT + j]);
     mx = warp_max(mx);
-    for (int j = lane; j < nk; j += 32) row[j] = j < valid ? exp_f(fadd(ftz(row[j]), neg(mx))) : 0.0f;
-    __syncwarp();
-    float acc = 0.0f;                                    // lanes 16..31 repeat lanes 0..15's chains
-    for (int j = lane & 15; j < nk; j += 16) acc = fadd_nc(acc, row[j]);
-    const float r_ = recip_f(sum16_fold(canon(acc)));
-    __syncwarp();
-    for (int j = lane; j < nk; j += 32) row[j] = ftz(fmul(row[j], r_));
+    if (lane == 0) srow[0][r] = mx;
+  }
+  __syncthreads();
+  for (int p = tid; p < R * nk; p += kAttnThreads) {
+    const int r = p / nk, j = p - r * nk;
+    const int valid = min(nk, t0 + 1 + r % n);
+    sp[r * kT + j] = j < valid ? exp_f(fadd(sp[r * kT + j], neg(srow[0][r]))) : 0.0f;
+  }
+  __syncthreads();
+  for (int r = warp; r < R; r += kAttnThreads / 32) {
+    float acc = 0.0f;                                     // lanes 16..31 repeat lanes 0..15
+    for (int j = lane & 15; j < nk; j += 16) acc = fadd_nc(acc, sp[r * kT + j]);
+    const float rinv = recip_f(sum16_fold(canon(acc)));
+    if (lane == 0) srow[1][r] = rinv;
+  }
+  __syncthreads();
+  for (int p = tid; p < R * nk; p += kAttnThreads) {
+    const int r = p / nk, j = p - r * nk;
+    sp[r * kT + j] = ftz(fmul(sp[r * kT + j], srow[1][r]));
   }
   // FDOT NN: out[r][d] = k-order chain over the nk keys, V staged tile by tile
-  constexpr int kPer = (kMaxRows * 256 + kAttnThreads - 1) / kAttnThreads;
+  constexpr int kPer = (kMaxRows * HD + kAttnThreads - 1) / kAttnThreads;
   float acc[kPer];
 #pragma unroll
   for (int i = 0; i < kPer; ++i) acc[i] = 0.0f;
-  const int outs = R * hd;
   for (int j0 = 0; j0 < nk; j0 += tile) {
     const int tk = min(tile, nk - j0);
-    __syncthreads();
-    for (int i = tid; i < tk * hd4; i += kAttnThreads) {
-      const int j = i / hd4, d4 = i - j * hd4;
-      cp16(reinterpret_cast<float4*>(skv) + i, reinterpret_cast<const float4*>(V + (uint64_t)(j0 + j) * kstride) + d4);
-    }
-    cp_wait_all();
-    __syncthreads();
+    stage(V, j0, tk);
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
       const int o = tid + i * kAttnThreads;
-      if (o < outs) {
-        const int r = o / hd, d = o - r * hd;
+      if (o < R * HD) {
+        const int r = o / HD, d = o - r * HD;
         const float* pr = sp + r * kT + j0;
         float v = acc[i];
-        for (int j = 0; j < tk; ++j) v = fadd_nc(v, fmul(pr[j], skv[j * hd + d]));
+#pragma unroll 8
+        for (int j = 0; j < tk; ++j) v = fadd_nc(v, fmul_ff(pr[j], skv[j * LD + d]));
         acc[i] = v;
       }
     }
@@ -459,11 +487,25 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a, int tile
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
     const int o = tid + i * kAttnThreads;
-    if (o < outs) {
-      const int r = o / hd, d = o - r * hd, g = r / n, m = r - g * n;
-      a.att[((uint64_t)(b * n + m) * a.nh + kvh * G + g) * hd + d] = ftz(canon(acc[i]));
+    if (o < R * HD) {
+      const int r = o / HD, d = o - r * HD, g = r / n, m = r - g * n;
+      a.att[((uint64_t)(b * n + m) * a.nh + kvh * G + g) * HD + d] = ftz(canon(acc[i]));
     }
   }
+}
+
+template <int HD>
+static cudaError_t attention_hd(const AttnArgs& a, int batch, cudaStream_t st) {
+  const int R = (a.nh / a.nkv) * a.n;
+  const int fixed = (R * HD + R * kT) * 4;
+  const int budget = 200 * 1024 - fixed;                  // shared memory left for a K / V tile
+  const int tile = std::min(kT, budget / ((HD + 4) * 4)) / 16 * 16;
+  if (tile < 16) return cudaErrorInvalidValue;
+  const int smem = fixed + tile * (HD + 4) * 4;
+  cudaError_t e = cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  k_attention<HD><<<batch * a.nkv, kAttnThreads, smem, st>>>(a, tile);
+  return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------------------- greedy pick
@@ -575,17 +617,14 @@ cudaError_t eng_qk_rope(const QkRopeArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 cudaError_t eng_attention(const AttnArgs& a, int batch, cudaStream_t st) {
-  const int G = a.nh / a.nkv, R = G * a.n;
-  if (a.nh % a.nkv || R > kMaxRows || a.hd > 256 || a.hd % 16) return cudaErrorInvalidValue;
-  const int fixed = (R * a.hd + R * kT) * 4;
-  const int budget = 200 * 1024 - fixed;                  // shared memory left for a K / V tile
-  int tile = std::min(kT, budget / (a.hd * 4)) / 16 * 16;
-  if (tile < 16) return cudaErrorInvalidValue;
-  const int smem = fixed + tile * a.hd * 4;
-  cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  k_attention<<<batch * a.nkv, kAttnThreads, smem, st>>>(a, tile);
-  return cudaGetLastError();
+  const int R = (a.nh / a.nkv) * a.n;
+  if (a.nh % a.nkv || R > kMaxRows) return cudaErrorInvalidValue;
+  switch (a.hd) {
+    case 64: return attention_hd<64>(a, batch, st);
+    case 128: return attention_hd<128>(a, batch, st);
+    case 256: return attention_hd<256>(a, batch, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 cudaError_t eng_argmax(const float* logits, int vocab, int batch, int* tok_out, int tok_stride, cudaStream_t st) {
   k_argmax<<<batch, 1024, 0, st>>>(logits, vocab, tok_out, tok_stride);
