@@ -88,6 +88,13 @@ int tc_graph_destroy(tc_graph* g);
 /* Waits for everything enqueued on the machine's stream. */
 int tc_synchronize(tc_machine* m);
 
+/* The W8A8 GEMM kernel choice: GEMMs of at least `rows` token rows (M) whose operands meet the
+ * TMA rules (16-byte aligned A, W and row stride, K % 16 == 0) run on the tensor cores (tcgen05,
+ * int8 MMA); the others on the CUDA-core GEMV kernels. Both are bit-exact. Values below 2 mean 2.
+ * Default 16 (or the environment variable TARSCUDA_MMA_MIN_M). Returns the previous value; it
+ * applies to every machine and engine of the process, to launches enqueued afterwards. */
+int tc_set_mma_min_rows(int32_t rows);
+
 /* Host-only helpers (no device needed). golden.Machine.validate (golden.py:59-169): decodes the
  * 23 fields of contract.py:14-38 into fields[23] (in that table's order) and returns the first
  * failing check (E_OK .. E_ALIGN). */

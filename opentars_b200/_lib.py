@@ -55,6 +55,7 @@ SIGNATURES = {
     "tc_graph_times": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_float), ctypes.c_uint32]),
     "tc_graph_destroy": (ctypes.c_int, [P]),
     "tc_synchronize": (ctypes.c_int, [P]),
+    "tc_set_mma_min_rows": (ctypes.c_int, [ctypes.c_int32]),
     "tc_conv_w8a8_noalloc": (ctypes.c_int, [VP, ctypes.c_uint64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                             ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, VP, VP,
                                             ctypes.c_int32, VP, VP, ctypes.c_uint64, ctypes.c_int32, ctypes.c_int32,

@@ -12,6 +12,7 @@
 #include <algorithm>
 
 #include "engine.h"
+#include "mma.h"
 #include "fp32.cuh"
 
 namespace tc {
@@ -599,6 +600,7 @@ static cudaError_t gemm_tl(const EngGemvArgs& g, cudaStream_t st) {
 }
 
 cudaError_t eng_gemv(const EngGemvArgs& g, cudaStream_t st) {
+  if (g.M >= mma_min_rows() && mma_engine_ok(g)) return eng_gemm_mma(g, st);
   if (g.K > 14 * 512 || g.K % 16) return cudaErrorInvalidValue;
   if (g.M > 8) {
     if (g.K <= 1024) return gemm_tl<2>(g, st);

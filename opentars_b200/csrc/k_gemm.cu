@@ -14,6 +14,8 @@
 #include <algorithm>
 
 #include "fp32.cuh"
+#include "gemm_epi.cuh"
+#include "mma.h"
 #include "ops.h"
 
 namespace tc {
@@ -34,15 +36,6 @@ template <bool VEC>
 __device__ __forceinline__ uint4 load16(const uint8_t* p) {
   if (VEC) return ldg_stream(p);
   return make_uint4(ld_u32(p), ld_u32(p + 4), ld_u32(p + 8), ld_u32(p + 12));
-}
-
-__device__ __forceinline__ void gemm_epilogue(const GemmArgs& g, int m, int n, int acc) {
-  float y = i2f(acc);
-  if (g.srow) y = fmul(y, ld_f32(g.srow + 4 * (uint64_t)m));
-  y = fmul(y, ld_f32(g.scale + (g.per_channel ? 4 * (uint64_t)n : 0)));
-  if (g.bias) y = fadd(y, ld_f32(g.bias + 4 * (uint64_t)n));
-  y = act_fn(y, g.act);
-  store_out(g.Y + (uint64_t)m * g.ldy, n, y, g.out, g.out_scale);
 }
 
 // One pass: rows [m0, m0 + mb) of A (mb <= MB), NCW columns per warp.
@@ -214,6 +207,7 @@ __global__ void k_im2col(Im2colArgs a) {
 }  // namespace
 
 cudaError_t launch_gemm_w8a8(const GemmArgs& g, cudaStream_t st) {
+  if (g.M >= mma_min_rows() && mma_machine_ok(g)) return gemm_mma(g, st);
   const bool vec = ((uintptr_t)g.A % 16 == 0) && (g.lda % 16 == 0) && ((uintptr_t)g.W % 16 == 0) && (g.K % 16 == 0);
   if (vec && g.K <= 4096 && g.M <= 8) {
     if (g.M == 1) return launch_gemv8_k<1>(g, st);

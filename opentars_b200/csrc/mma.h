@@ -1,0 +1,21 @@
+// The tensor-core (tcgen05, kind::i8) W8A8 GEMM of k_mma.cu: entry points for the decode engine
+// and for the descriptor path. Each *_ok check says whether the operands meet the TMA rules
+// (16-byte aligned bases and row strides, K a multiple of 16) so the caller can pick the kernel.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "engine.h"
+#include "ops.h"
+
+namespace tc {
+
+bool mma_engine_ok(const EngGemvArgs& g);
+cudaError_t eng_gemm_mma(const EngGemvArgs& g, cudaStream_t st);
+bool mma_machine_ok(const GemmArgs& g);
+cudaError_t gemm_mma(const GemmArgs& g, cudaStream_t st);
+// Smallest token-row count routed to the tensor-core kernel (TARSCUDA_MMA_MIN_M, default 16).
+int mma_min_rows();
+// Nonzero when a bounded wait of the tensor-core kernel gave up (1 producer, 2 MMA, 3 epilogue).
+int mma_error_code();
+
+}  // namespace tc
