@@ -14,6 +14,10 @@ Workloads (synthetic seeded data with the configs' distri
         a step runs R units on R distinct weight copies (R * 3 MiB > the 126 MB L2)
   w4    config 2: one unit = W4A16 GEMV, M=1, K=8192, N=16384 (64 MiB of packed weights);
         a step runs R units on distinct weight copies
+  gemm  config 1: the W8A8 prefill GEMM sweep, M in {4, 16, 64, 256} x (K, N) in {(1024, 3072),
+        (3072, 1024), (1024, 151936), (6912, 1152) as K blocks 4096 + 2816}; a step = every GEMM of
+        the sweep (one queue); value in int8 TOPS (2 M N K per GEMM); on N GPUs every shape's N is
+        split over the ranks and the outputs are all-gathered with NCCL (strong scaling)
 gemv / w4 value: algorithmic bytes of all units of all ranks / device time of the timed steps
 (max over ranks), in GB/s. e2e: the same metric through the board-runtime API (opentars_b200.board.Cuda:
 host writes x into pinned memory, to_dev, run, from_dev of y) timed on the host clock.
@@ -365,6 +369,295 @@ def run_reference(a, world, rank) -> dict | None:
 
 
 
+# ----------------------------------------------------------------------------- config 1: GEMM sweep
+GEMM_M = (4, 16, 64, 256)
+GEMM_SHAPES = ((1024, 3072, 0), (3072, 1024, 0), (1024, 151936, 0), (6912, 1152, 4096))   # (K, N, first K block)
+DESC_N_MAX = 65520                 # the descriptor's N field is 16 bits; blocks are multiples of 16
+
+
+def _row_blocks(n: int, cap: int = DESC_N_MAX) -> list[tuple[int, int]]:
+    parts = -(-n // cap)
+    q = -(-n // parts // 16) * 16
+    return [(c, min(n, c + q)) for c in range(0, n, q)]
+
+
+def build_gemm(world: int = 1, rank: int = 0, seed: int = 1234, ms=GEMM_M, shapes=GEMM_SHAPES):
+    """Config 1 on one rank: activations ~N(0,1) quantised per row (a setup queue), int8 weights
+    uniform in [-127, 127] with per-channel scales uniform in [1e-3, 1e-2] (seeded, the same full
+    operands on every rank); rank r owns output columns [r N / world, (r+1) N / world) of every
+    shape. The (6912, 1152) shape runs as two K blocks (4096 + 2816) sharing the scales, their
+    fp32 partial results added by an ELT descriptor. N above the descriptor's 16-bit field runs as
+    row blocks. Returns the image, both queues, the output region and per-descriptor metadata."""
+    from opentars_b200 import contract as C
+    from opentars_b200.lowering import Dev, QLin
+    rng = np.random.default_rng(seed)
+    Mx = max(ms)
+    Ks = sorted({K for K, _, _ in shapes})
+    xs = {K: rng.normal(0, 1, (max(GEMM_M), K)).astype(np.float32)[:Mx] for K in Ks}   # row m: the same for any ms
+    full = [(rng.integers(-127, 128, (N, K), dtype=np.int8), rng.uniform(1e-3, 1e-2, N).astype(np.float32))
+            for K, N, _ in shapes]
+    for K, N, _ in shapes:
+        assert N % (16 * world) == 0, "every shape's N splits into 16-column multiples per rank"
+    nl = [N // world for _, N, _ in shapes]
+    need = sum(5 * Mx * K + 4 * Mx + 512 for K in Ks) + sum(n * K + 4 * n + 512 for n, (K, _, _) in zip(nl, shapes))
+    need += sum(4 * M * n * (2 if kb else 1) + 512 for M in ms for n, (_, _, kb) in zip(nl, shapes)) + (1 << 16)
+    p = Dev(need)
+    xv = {K: p.const(xs[K]) for K in Ks}
+    qv = {K: p.quant(xv[K]) for K in Ks}
+    _, q_setup, n_setup = p.build()
+    p.descs, p.queue_off = [], None
+    lins = []
+    for (K, N, kb), (W, sc), n in zip(shapes, full, nl):
+        Wl, sl = W[rank * n:(rank + 1) * n], sc[rank * n:(rank + 1) * n]
+        s_off = p.put(sl)
+        if kb:
+            lins.append(("k", [QLin(p.put(np.ascontiguousarray(Wl[:, :kb]), "i1"), s_off, None, n, kb),
+                               QLin(p.put(np.ascontiguousarray(Wl[:, kb:]), "i1"), s_off, None, n, K - kb)]))
+        else:
+            w_off = p.put(Wl, "i1")
+            lins.append(("n", [(c0, QLin(w_off + c0 * K, s_off + 4 * c0, None, c1 - c0, K))
+                               for c0, c1 in _row_blocks(n)]))
+    # outputs: row-block-major for N above one descriptor block (the row stride field is 15 bits
+    # of 16 bytes), as the lowering lays out the vocabulary head's logits
+    y0 = p.top
+    ys = {(M, i): [(c0, p.mat(M, c1 - c0)) for c0, c1 in _row_blocks(n)] for M in ms for i, n in enumerate(nl)}
+    y1 = p.top
+    meta = []                      # per GEMM queue descriptor: (M, shape index, ops, weight bytes) or None
+    for M in ms:
+        for i, ((K, N, kb), (kind, parts), n) in enumerate(zip(shapes, lins, nl)):
+            xq, xs_off = qv[K]
+            xq = xq.rowv(0, M)
+            if kind == "n":
+                for (c0, lin), (_, y) in zip(parts, ys[(M, i)]):
+                    p.gemm_rc(xq, xs_off, lin, y)
+                    meta.append((M, i, 2 * M * lin.n * K, lin.n * K))
+            else:
+                y = ys[(M, i)][0][1]
+                part = p.mat(M, n)
+                p.gemm_rc(xq.colv(0, kb), xs_off, parts[0], y)
+                meta.append((M, i, 2 * M * n * kb, n * kb))
+                p.gemm_rc(xq.colv(kb, K - kb), xs_off, parts[1], part)
+                meta.append((M, i, 2 * M * n * (K - kb), n * (K - kb)))
+                p.elt(C.ELT_ADD, y, part, y)
+                meta.append(None)
+    ddr, q_main, n_main = p.build()
+    x_first, x_last = min(v.off for v in xv.values()), max(v.off + v.rows * v.ld for v in xv.values())
+    return dict(ddr=np.frombuffer(bytes(ddr), np.uint8).copy(), q_setup=q_setup, n_setup=n_setup, q_main=q_main,
+                n_main=n_main, y_region=(y0, y1 - y0), x_region=(x_first, x_last - x_first), ys=ys, nl=nl,
+                meta=meta, ms=ms, shapes=shapes, world=world,
+                ops=sum(2 * M * N * K for M in ms for K, N, _ in shapes))
+
+
+def gemm_outputs(p: dict, gathered: list[np.ndarray]) -> dict:
+    """Per (M, shape) the full [M, N] fp32 output from every rank's copy of its output region."""
+    y0 = p["y_region"][0]
+    out = {}
+    for (M, i), blocks in p["ys"].items():
+        cols = [g[v.off - y0:v.off - y0 + v.rows * v.ld].view("<f4").reshape(M, -1) for g in gathered
+                for _, v in blocks]
+        out[(M, i)] = np.concatenate(cols, axis=1)
+    return out
+
+
+def gemm_hashes(outs: dict) -> dict:
+    import hashlib
+    return {f"M{M}_s{i}": hashlib.sha256(np.ascontiguousarray(y).tobytes()).hexdigest() for (M, i), y in outs.items()}
+
+
+class _DevBytes:
+    """A device byte range as a CUDA array (for torch.as_tensor without a copy)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+def _oracle_gemm_worker(args):
+    """Runs one config-1 GEMM descriptor (M=64, K=1024, N=3072) on the oracle for `seconds`."""
+    seconds, = args
+    sys.path.insert(0, str(ROOT))
+    from oracle.machine import OracleMachine
+    p = build_gemm(1, 0, seed=99, ms=(64,), shapes=((1024, 3072, 0),))
+    o = OracleMachine(bytearray(p["ddr"].tobytes()))
+    assert o.run_queue(p["q_setup"], p["n_setup"]).done
+    n, t0 = 0, time.perf_counter()
+    while True:
+        assert o.run_queue(p["q_main"], p["n_main"]).done
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    return n, time.perf_counter() - t0
+
+
+def cpu_oracle_gemm(seconds: float, procs: int) -> dict:
+    import multiprocessing as mp
+    with mp.get_context("spawn").Pool(procs) as pool:
+        res = pool.map(_oracle_gemm_worker, [(seconds,)] * procs)
+    units = sum(n for n, _ in res)
+    span = max(t for _, t in res)
+    ops = 2 * 64 * 3072 * 1024
+    return dict(value=round(units * ops / span / 1e12, 6), unit="TOPS", cores=procs, kind="port",
+                sample=f"{units} W8A8 GEMMs of M=64 K=1024 N=3072 (config 1's first shape) on {procs} processes, "
+                       f"{span:.1f}s each")
+
+
+def run_gemm(a, world, rank, local) -> dict | None:
+    import ctypes
+
+    import torch
+    os.environ["TC_DEVICE"] = str(local)
+    torch.cuda.set_device(local)
+    from opentars_b200._lib import Status_t, check, lib
+    from opentars_b200.board import Cuda
+    p = build_gemm(world, rank)
+    L = lib()
+    ddr = p["ddr"]
+    dev = Cuda(len(ddr), device=local, pinned=True)
+    dev.mem[:] = ddr
+    dev.to_dev(0, len(ddr))
+    ok = dev.run(p["q_setup"], p["n_setup"])[0]
+    g, st = dev.graph(p["q_main"], p["n_main"])
+    assert ok and g is not None and st.done, "the GEMM queue must capture"
+    stream = torch.cuda.ExternalStream(L.tc_stream(dev.h), device=local)
+    y0, yn = p["y_region"]
+    base = int(L.tc_device_ptr(dev.h))
+    yt = torch.as_tensor(_DevBytes(base + y0, yn), device=f"cuda:{local}")
+    gath = torch.empty(world * yn, dtype=torch.uint8, device=f"cuda:{local}") if world > 1 else None
+
+    def step():
+        check(L.tc_graph_launch(g, None), dev.h)
+        if world > 1:                               # N-split: every rank gets every output block
+            import torch.distributed as dist
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(gath, yt)
+
+    for _ in range(a.warmup):
+        step()
+    check(L.tc_synchronize(dev.h), dev.h)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(stream)
+        for _ in range(a.steps):
+            step()
+        e1.record(stream)
+        check(L.tc_synchronize(dev.h), dev.h)
+    ms = e0.elapsed_time(e1)
+    barrier(world)
+    ms_max = max_over_ranks(ms, world)
+    value = p["ops"] * a.steps / (ms_max / 1e3) / 1e12
+
+    # parity: the full outputs (gathered over ranks) against the reference oracle's hashes
+    torch.cuda.synchronize(local)
+    if world > 1:
+        regions = [gath[r * yn:(r + 1) * yn].cpu().numpy() for r in range(world)]
+    else:
+        regions = [yt.cpu().numpy()]
+    fx = ROOT / "tests" / "golden" / "gemm_sweep.json"
+    bit_exact = None
+    if rank == 0 and fx.exists():
+        want = json.loads(fx.read_text())["sha256"]
+        got = gemm_hashes(gemm_outputs(p, regions))
+        bit_exact = got == want
+        if not bit_exact:
+            bit_exact = {k: got[k] == want.get(k) for k in got}
+
+    # roofline: per-descriptor device times (graph captured with events between descriptors)
+    st2, cop, gt = Status_t(), ctypes.c_int32(-1), ctypes.c_void_p()
+    check(L.tc_queue_capture(dev.h, p["q_main"], p["n_main"], 0, 0, 1, ctypes.byref(st2), ctypes.byref(cop),
+                             ctypes.byref(gt)), dev.h)
+    times = np.zeros(p["n_main"])
+    reps = 3
+    for _ in range(reps):
+        check(L.tc_graph_launch(gt, None), dev.h)
+        check(L.tc_synchronize(dev.h), dev.h)
+        arr = (ctypes.c_float * p["n_main"])()
+        check(L.tc_graph_times(gt, arr, p["n_main"]), dev.h, "graph_times")
+        times += np.array(arr[:p["n_main"]]) / reps
+    L.tc_graph_destroy(gt)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    i8 = 2 * peaks.get("bf16_tflops", 1590.0)
+    cases = {}
+    for t, m in zip(times, p["meta"]):
+        if m is None:
+            continue
+        M, i, ops, wb = m
+        c = cases.setdefault((M, i), [0.0, 0, 0])
+        c[0] += t
+        c[1] += ops
+        c[2] += wb
+    rows = []
+    for (M, i), (t, ops, wb) in sorted(cases.items()):
+        K, N, kb = p["shapes"][i]
+        ideal = max(wb / (hbm * 1e9), ops / (i8 * 1e12)) * 1e3
+        rows.append(dict(M=M, K=K, N=N // world, ms=round(t, 4), tops=round(ops / (t / 1e3) / 1e12, 1),
+                         weight_gbs=round(wb / (t / 1e3) / 1e9, 1), roofline_frac=round(ideal / t, 3)))
+    gemm_ms = sum(t for t, m in zip(times, p["meta"]) if m is not None)
+    gemm_ops = sum(m[2] for m in p["meta"] if m is not None)
+    achieved = gemm_ops / (gemm_ms / 1e3) / 1e12
+    roofline = dict(bound="tensor", achieved=round(achieved, 1), peak=round(i8, 1), unit="TOPS",
+                    frac=round(achieved / i8, 4), traffic=None,
+                    kernel="k_mma_i8 (tcgen05 int8 GEMM) / k_gemv8 for M=4", kernel_ms_per_step=round(gemm_ms, 4),
+                    peak_source="2 x measured bf16 burst (int8 dense = 2 x bf16 on B200)", cases=rows)
+
+    # e2e through the board API: fp32 activations up from pinned memory, quantise + GEMMs, outputs back
+    x0, xn = p["x_region"]
+    for i in range(2):
+        dev.to_dev(x0, xn)
+        dev.run(p["q_setup"], p["n_setup"])
+        dev.run(p["q_main"], p["n_main"])
+        dev.from_dev(y0, yn)
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        dev.to_dev(x0, xn)
+        dev.run(p["q_setup"], p["n_setup"])
+        dev.run(p["q_main"], p["n_main"])
+        dev.from_dev(y0, yn)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e = dict(value=round(p["ops"] / world * world * a.steps / e2e_s / 1e12, 2), unit="TOPS",
+               h2d_bytes_per_step=xn, d2h_bytes_per_step=yn,
+               api="opentars_b200.board.Cuda: to_dev, run (quant queue, GEMM queue), from_dev")
+    if world > 1:
+        e2e["note"] = "per-rank output blocks only (the all-gather runs in the device-timed steps)"
+    dev.close()
+    if rank != 0:
+        return None
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(ms_max / a.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic, seeded (config 1 distributions)",
+        "config": dict(workload="config1_w8a8_gemm_sweep", M=list(GEMM_M), shapes=[list(s) for s in GEMM_SHAPES],
+                       descriptors_per_step=p["n_main"],
+                       parallelism=f"N split over {world} GPUs + NCCL all-gather of the outputs" if world > 1
+                       else "1 GPU", l2="weights (170 MB per step) larger than L2, streamed once per step"),
+        "roofline": roofline, "e2e": e2e, "gpu_launches": a.steps * p["n_main"], "clocks": clk.summary(),
+        "bit_exact_vs_reference": bit_exact,
+    }
+    if world == 1 and not a.no_cpu:
+        out["cpu_baseline"] = cpu_oracle_gemm(a.cpu_seconds, os.cpu_count() or 1)
+    return out
+
+
+def run_gemm_reference(a, world, rank) -> dict | None:
+    if rank != 0:
+        return None
+    procs = os.cpu_count() or 1
+    vals = [cpu_oracle_gemm(a.ref_seconds, procs) for _ in range(a.warmup + a.steps)][a.warmup:]
+    v = statistics.mean(x["value"] for x in vals)
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(v, 6), "unit": "TOPS", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic, seeded",
+        "config": dict(workload="config1_w8a8_gemm_sweep", sample="bounded CPU sample"),
+        "cpu_baseline": dict(value=round(v, 6), unit="TOPS", cores=procs, kind="port", sample=vals[-1]["sample"]),
+        "e2e": dict(value=round(v, 6), unit="TOPS", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+        "note": "the reference is Python (numpy golden model); its restatement in oracle/ is timed here",
+    }
+
+
 # ----------------------------------------------------------------------------- decode (configs 3 / 4)
 DECODE_MODELS = {
     # name: (base config, layer types, vocab, fixture name)
@@ -532,6 +825,9 @@ def run_decode(a, world, rank, local) -> dict | None:
                     kernel_bytes_per_step=g[2], kernel_launches_per_step=g[0], kernel_ms_per_step=round(g[1], 4),
                     peak_source="measured" if peaks else "fallback",
                     step_breakdown_ms={k: round(v[1], 4) for k, v in kinds.items()})
+    gl = [(t, nb) for k, t, nb in prof if k == "gemv"]
+    if len(gl) > 5:   # layer 0's four GEMMs and the head: [ms, algorithmic GB/s]
+        roofline["gemv_layer0_and_head"] = [[round(t, 4), round(nb / (t / 1e3) / 1e9, 1)] for t, nb in gl[:4] + gl[-1:]]
 
     # e2e: the host in the loop as the reference's generate runs it: each step the token ids go up
     # from pinned memory and the greedy picks come back
@@ -613,7 +909,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS) + sorted(DECODE_MODELS))
+    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS) + sorted(DECODE_MODELS) + ["gemm"])
     ap.add_argument("--batch", type=int, default=64, help="decode: sequences per GPU")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--units", type=int, default=0)
@@ -624,12 +920,22 @@ def main():
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":                       # CPU only: no process group, no GPU
         world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
-        out = run_decode_reference(a, world, rank) if a.workload in DECODE_MODELS else run_reference(a, world, rank)
+        if a.workload == "gemm":
+            out = run_gemm_reference(a, world, rank)
+        elif a.workload in DECODE_MODELS:
+            out = run_decode_reference(a, world, rank)
+        else:
+            out = run_reference(a, world, rank)
         if out is not None:
             print(json.dumps(out), flush=True)
         return
     world, rank, local = dist_setup(a.gpus)
-    out = run_decode(a, world, rank, local) if a.workload in DECODE_MODELS else run_ours(a, world, rank, local)
+    if a.workload == "gemm":
+        out = run_gemm(a, world, rank, local)
+    elif a.workload in DECODE_MODELS:
+        out = run_decode(a, world, rank, local)
+    else:
+        out = run_ours(a, world, rank, local)
     if out is not None:
         print(json.dumps(out), flush=True)
     if world > 1:

@@ -77,9 +77,9 @@ enum { kKEmbed, kKNormQuant, kKGemv, kKQkRope, kKAttention, kKQuant, kKArgmax, k
       cudaEvent_t _a, _b;                                                      \
       cudaEventCreate(&_a);                                                    \
       cudaEventCreate(&_b);                                                    \
-      cudaEventRecord(_a, e->st);                                              \
+      cudaEventRecordWithFlags(_a, e->st, cudaEventRecordExternal);            \
       TRY(expr);                                                               \
-      cudaEventRecord(_b, e->st);                                              \
+      cudaEventRecordWithFlags(_b, e->st, cudaEventRecordExternal);            \
       e->pev.push_back(_a);                                                    \
       e->pev.push_back(_b);                                                    \
       e->pkind.push_back(kind);                                                \
@@ -341,17 +341,30 @@ int tc_engine_step(tc_engine* e, const int32_t* tokens_host, int32_t n) {
 }
 
 int tc_engine_profile(tc_engine* e, float* ms, int32_t* kind, uint64_t* bytes, uint32_t cap) {
+  // The step is captured with an event node on each side of every kernel and launched once, so
+  // the times are the kernels' own (no host work between the events, as in the timed graphs).
   e->prof = true;
   e->pev.clear(); e->pkind.clear(); e->pbytes.clear();
-  const int rc = enqueue_step(e, 1, e->next);
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t c = cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal);
+  int rc = c == cudaSuccess ? enqueue_step(e, 1, e->next) : TC_OK;
+  if (c == cudaSuccess) {
+    const cudaError_t c2 = cudaStreamEndCapture(e->st, &graph);
+    if (rc == TC_OK && c2 != cudaSuccess) c = c2;
+  }
   e->prof = false;
-  cudaError_t c = cudaStreamSynchronize(e->st);
+  if (c == cudaSuccess && rc == TC_OK) c = cudaGraphInstantiate(&exec, graph, 0);
+  if (c == cudaSuccess && rc == TC_OK) c = cudaGraphLaunch(exec, e->st);
+  if (c == cudaSuccess && rc == TC_OK) c = cudaStreamSynchronize(e->st);
   const int n = (int)e->pkind.size();
-  for (int i = 0; i < n && i < (int)cap; ++i) {
+  for (int i = 0; i < n && i < (int)cap && c == cudaSuccess && rc == TC_OK; ++i) {
     cudaEventElapsedTime(&ms[i], e->pev[2 * i], e->pev[2 * i + 1]);
     kind[i] = e->pkind[i];
     bytes[i] = e->pbytes[i];
   }
+  if (exec) cudaGraphExecDestroy(exec);
+  if (graph) cudaGraphDestroy(graph);
   for (auto ev : e->pev) cudaEventDestroy(ev);
   e->pev.clear();
   if (rc != TC_OK) return rc;

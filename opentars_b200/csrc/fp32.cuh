@@ -168,6 +168,26 @@ __device__ __forceinline__ float act_fn(float x, int act) {
   }
 }
 
+// act_fn with the transcendental cases (3-7) in one out-of-line function: for epilogues that run
+// the activation inside long per-element loops, whose body must stay small in the instruction
+// cache. The same results as act_fn.
+static __device__ __noinline__ float act_transcendental(float x, int act) {
+  switch (act) {
+    case 3: return gelu_f(x);
+    case 4: return silu_f(x);
+    case 5: return sigmoid_f(x);
+    case 6: return softplus_f(x);
+    default: return exp_f(x);
+  }
+}
+__device__ __forceinline__ float act_fn_lean(float x, int act) {
+  x = ftz(x);
+  if (act == 0) return x;
+  if (act == 1) return x > 0.0f ? x : 0.0f;
+  if (act == 2) { const float r = x > 0.0f ? x : 0.0f; return r > 6.0f ? 6.0f : r; }
+  return act_transcendental(x, act);
+}
+
 // numerics.py:293-303: NaN wins; equal values (+0 / -0 included) give the AND of the sign bits
 __device__ __forceinline__ float fmax_c(float a, float b) {
   a = ftz(a);

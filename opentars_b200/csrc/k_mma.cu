@@ -1,19 +1,26 @@
 // W8A8 GEMM on the 5th-generation tensor cores (tcgen05.mma kind::i8) for M > 1 token rows:
 // the prefill / batched-decode contraction of golden.py:326-349 and of the decode engine.
 //
-// Roles in a 128-thread CTA: thread 0 streams 128-byte K slices of a 128-row weight tile (UMMA
-// operand A) and of the token tile (operand B, NT rows) into a ring of shared-memory stages with
-// TMA (128-byte swizzle, zero fill past every edge); thread 32 issues 4 MMAs of K = 32 per stage
-// into int32 accumulators in TMEM (lane = weight row, column = token) and releases each stage with
-// tcgen05.commit; then all four warps read the accumulators back (warp w: lanes 32w..32w+31) and
-// run the caller's exact fp32 epilogue. int32 sums are exact in any order (|acc| < 2^31 for every
-// legal K), so tiling and split-K change nothing in the result.
-//
-// Split-K: a tile's K slices are shared by the `split` CTAs of a thread-block cluster. Each CTA
-// writes its int32 partial tile into its own shared memory; after a cluster barrier CTA r sums
-// rows [r*128/split, (r+1)*128/split) over all peers through distributed shared memory and runs
-// the epilogue for them. No global workspace, so concurrent launches never share state.
-//
+// A tile is 128 weight rows (UMMA operand A, M = 128) x NT token rows (operand B, N = NT <= 256);
+// its accumulator is int32 in TMEM (lane = weight row, column = token). int32 sums are exact in
+// any order (|acc| < 2^31 for every legal K), so tiling and split-K change nothing in the result.
+// Warp roles in a 320-thread CTA:
+//   warp 0     TMA producer: 128-byte K slices of the weight tile(s) and of the token tile into a
+//              ring of shared-memory stages (128-byte swizzle, zero fill past every edge)
+//   warp 1     TMEM owner and MMA issuer: 4 MMAs of K = 32 per stage, tcgen05.commit releases
+//              the stage; a finished accumulator is committed to the epilogue
+//   warps 2-9  epilogue: tcgen05.ld of the accumulator (warp w reads lanes 32(w%4).., warps
+//              2-5 the even 16-column chunks, 6-9 the odd ones), the caller's exact fp32
+//              epilogue, coalesced stores (consecutive lanes = consecutive output columns)
+// Two modes:
+//   persistent  CTAs loop over tiles; two TMEM accumulators, so the epilogue of one tile overlaps
+//               the loads and MMAs of the next
+//   split-K     few tiles: the K slices of one tile are shared by the `split` CTAs of a thread-
+//               block cluster. Each CTA writes its partial tile to its own shared memory and frees
+//               its TMEM; after a cluster barrier CTA r sums rows [r*128/split, (r+1)*128/split)
+//               over all peers through distributed shared memory and runs the epilogue for them.
+//               No global workspace, so concurrent launches never share state, and no CTA holds
+//               TMEM while it waits on another CTA.
 // Two accumulators per tile: the gated MLP (gate rows -> acc 0, up rows -> acc 1 from one staged
 // token slice) and the K-split linear (first K block -> acc 0, second -> acc 1).
 #include <cuda.h>
@@ -24,6 +31,7 @@
 #include <atomic>
 #include <cstdlib>
 
+#include "../../include/tarscuda.h"
 #include "engine.h"
 #include "fp32.cuh"
 #include "gemm_epi.cuh"
@@ -36,220 +44,487 @@ namespace tc {
 namespace {
 constexpr int kRows = 128;          // weight rows per tile (UMMA M)
 constexpr int kSlice = 128;         // K bytes per stage (one swizzle row)
-constexpr int kThreads = 128;
+constexpr int kEpiWarps = 8;                // two per TMEM lane quarter, alternating 16-column chunks
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxStages = 8;
 constexpr int kSmemBudget = 200 * 1024;
 constexpr int kSmemPerSM = 228 * 1024;     // shared memory of one SM (1 KB of it reserved per CTA)
+constexpr int kSMs = 148;
 
 struct MmaMaps {
   CUtensorMap x;                    // token rows [M, K] int8
   CUtensorMap w[2 * kMaxSegs];      // segment s: w[2s] first K block, w[2s+1] second K block
 };
 
+// Phase trace (tc_mma_trace): per CTA, globaltimer stamps of kernel entry, setup done, first TMA
+// issued, first stage consumed by the MMA thread, last MMA issued, first accumulator seen by the
+// epilogue, epilogue done, exit. Off unless enabled; it changes no work.
+constexpr int kTraceCtas = 2048, kTraceStamps = 8;
+__device__ unsigned long long g_mma_trace[kTraceCtas * kTraceStamps];
+std::atomic<int> g_trace_on{0};
+
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 struct MmaShape {
   int M, NT, ntt;                   // token rows, token tile (multiple of 16, <= 256), token tiles
   int nseg, tile0[kMaxSegs + 1];    // row tiles of segment s: [tile0[s], tile0[s+1])
   int nrow[kMaxSegs];
   int nkb1, nkb2, kb;               // K slices of the two K blocks; kb = first token column of block 2
-  int gated, nacc, split, stages;
+  int gated, nacc, split, stages, items, nbuf, trace;
   int* err;
 };
 
-// The decode engine's epilogue (k_eng_gemv's, restated per element): acc0 is the (first K block's)
-// dot of segment s's row c with token row m; acc1 the second K block's (kEpiKSplit) or the up
-// row's (kEpiGated).
+// Epilogues. row() holds what depends on the weight row only (scales pre-flushed), tok() the
+// per-token factor (the row scale of the token's int8 row; staged flushed in shared memory once
+// per tile), put16() 16 consecutive tokens of one weight row: first the 16 values, branch-free
+// (the choices that are uniform over the launch - output format, activation, residual, mode -
+// are template instances picked outside the loop), then the stores, predicated on the token
+// count. A branch per element would split the unrolled loop into blocks whose dependent chains
+// (convert, multiply, flush, store) the scheduler could not overlap.
+// ep(a, s) = fmul(fmul(i2f(a), sr), s) is computed as canon(ftz(ftz(i2f(a) * sr) * s)): i2f of an
+// int is never denormal, sr and s are flushed once, and a NaN stays a NaN through a product, so
+// canonicalising once at the end gives the same bits.
+__device__ __forceinline__ float ep_fast(int a, float sr, float sc) { return canon(fmul_ff(fmul_ff(i2f(a), sr), sc)); }
+
+// ACT 0-2 without a branch; -1: any code through act_fn_lean
+template <int ACT>
+__device__ __forceinline__ float act_static(float x, int act) {
+  if constexpr (ACT == 3) return gelu_f(x);
+  else if constexpr (ACT == 4) return silu_f(x);
+  else if constexpr (ACT == 0) {
+    x = ftz(x);
+    const float r = x > 0.0f ? x : 0.0f;
+    const float r6 = r > 6.0f ? 6.0f : r;
+    return act == 0 ? x : (act == 1 ? r : r6);
+  } else {
+    return act_fn_lean(x, act);
+  }
+}
+
+// The decode engine's epilogue (k_eng_gemv's): acc0 is the (first K block's) dot of segment s's row
+// c with a token row; acc1 the second K block's (kEpiKSplit) or the up row's (kEpiGated).
 struct EngEpi {
   EngGemvArgs g;
-  __device__ __forceinline__ void operator()(int s, int c, int m, int acc0, int acc1) const {
-    const float sr = g.srow[m];
-    auto ep = [&](int a, const EngSeg& sg) { return fmul(fmul(i2f(a), sr), sg.scale[c]); };
+  struct Row {
+    float s0, s1;
+    float* out;
+    uint64_t ldo;
+    int col;
+  };
+  __device__ __forceinline__ Row row(int s, int c) const {
+    Row r;
     if (g.mode == kEpiGated) {
-      const float yg = ftz(act_fn(ep(acc0, g.seg[0]), g.act));
-      const float yu = ep(acc1, g.seg[1]);
-      g.seg[0].out[(uint64_t)m * g.seg[0].ldo + c] = ftz(fmul(yg, yu));
-      return;
+      r.s0 = ftz(g.seg[0].scale[c]);
+      r.s1 = ftz(g.seg[1].scale[c]);
+      r.out = g.seg[0].out + c;
+      r.ldo = g.seg[0].ldo;
+      r.col = c;
+    } else {
+      const EngSeg& sg = g.seg[s];
+      r.s0 = r.s1 = ftz(sg.scale[c]);
+      r.out = sg.out + c;
+      r.ldo = sg.ldo;
+      r.col = sg.n0 + c;
     }
-    const EngSeg& sg = g.seg[s];
-    float y = g.mode == kEpiKSplit ? fadd(ftz(ep(acc0, sg)), ftz(ep(acc1, sg))) : ep(acc0 + acc1, sg);
-    if (g.res) y = fadd(g.res[(uint64_t)m * g.ldres + sg.n0 + c], y);
-    sg.out[(uint64_t)m * sg.ldo + c] = ftz(y);
+    return r;
+  }
+  __device__ __forceinline__ float tok(int m) const { return g.srow[m]; }
+
+  template <int ACT>
+  __device__ __forceinline__ void gated16(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[16],
+                                          const uint32_t (&v1)[16]) const {
+    float y[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float yg = ep_fast((int)v0[j], tk[j], r.s0);
+      const float yu = ep_fast((int)v1[j], tk[j], r.s1);
+      y[j] = ftz(fmul(ftz(act_static<ACT>(yg, g.act)), yu));
+    }
+    store16(r, m0, mc, y);
+  }
+  template <bool RES, bool KSPLIT>
+  __device__ __forceinline__ void plain16(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[16],
+                                          const uint32_t (&v1)[16], bool two) const {
+    float y[16];
+    float pre[16];
+    if constexpr (RES) {
+      const float* rp = g.res + r.col;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) pre[j] = rp[(uint64_t)(m0 + min(j, mc - 1)) * g.ldres];
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int a0 = (int)v0[j], a1 = two ? (int)v1[j] : 0;
+      float v;
+      if constexpr (KSPLIT) v = fadd(ftz(ep_fast(a0, tk[j], r.s0)), ftz(ep_fast(a1, tk[j], r.s0)));
+      else v = ep_fast(a0 + a1, tk[j], r.s0);
+      if constexpr (RES) v = fadd(pre[j], v);
+      y[j] = ftz(v);
+    }
+    store16(r, m0, mc, y);
+  }
+  __device__ __forceinline__ void store16(const Row& r, int m0, int mc, const float (&y)[16]) const {
+    float* o = r.out + (uint64_t)m0 * r.ldo;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < mc) o[(uint64_t)j * r.ldo] = y[j];
+  }
+  __device__ __forceinline__ void put16(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[16],
+                                        const uint32_t (&v1)[16], bool two) const {
+    if (mc <= 0) return;
+    if (g.mode == kEpiGated) {
+      if (g.act == 4) gated16<4>(r, tk, m0, mc, v0, v1);
+      else if (g.act == 3) gated16<3>(r, tk, m0, mc, v0, v1);
+      else gated16<-1>(r, tk, m0, mc, v0, v1);
+    } else if (g.mode == kEpiKSplit) {
+      if (g.res) plain16<true, true>(r, tk, m0, mc, v0, v1, two);
+      else plain16<false, true>(r, tk, m0, mc, v0, v1, two);
+    } else {
+      if (g.res) plain16<true, false>(r, tk, m0, mc, v0, v1, two);
+      else plain16<false, false>(r, tk, m0, mc, v0, v1, two);
+    }
   }
 };
 
-// The descriptor path's epilogue (one segment, one K block).
+// The descriptor path's epilogue (gemm_epilogue, golden.py:326-349).
 struct MachEpi {
   GemmArgs g;
-  __device__ __forceinline__ void operator()(int, int c, int m, int acc0, int acc1) const {
-    gemm_epilogue(g, m, c, acc0 + acc1);
+  struct Row {
+    float sc, bias;
+    int n;
+  };
+  __device__ __forceinline__ Row row(int, int c) const {
+    Row r;
+    r.n = c;
+    r.sc = ftz(ld_f32(g.scale + (g.per_channel ? 4 * (uint64_t)c : 0)));
+    r.bias = g.bias ? ld_f32(g.bias + 4 * (uint64_t)c) : 0.0f;
+    return r;
+  }
+  __device__ __forceinline__ float tok(int m) const { return g.srow ? ld_f32(g.srow + 4 * (uint64_t)m) : 1.0f; }
+
+  template <int ACT, int OUT>
+  __device__ __forceinline__ void run16(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[16],
+                                        const uint32_t (&v1)[16], bool two) const {
+    const bool srow = g.srow != nullptr, bias = g.bias != nullptr;
+    uint32_t bits[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float y = i2f((int)v0[j] + (two ? (int)v1[j] : 0));
+      const float ys = fmul_ff(y, tk[j]);
+      y = srow ? ys : y;
+      y = canon(fmul_ff(y, r.sc));
+      const float yb = fadd(y, r.bias);
+      y = bias ? yb : y;
+      y = act_static<ACT>(y, g.act);
+      if constexpr (OUT == 0) bits[j] = fb(ftz(y));
+      else if constexpr (OUT == 1) bits[j] = to_bf16(y);
+      else if constexpr (OUT == 2) bits[j] = (uint8_t)q8(y, g.out_scale);
+      else bits[j] = to_fp16(y);
+    }
+    uint8_t* yrow = g.Y + (uint64_t)m0 * g.ldy;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j < mc) {
+        uint8_t* p = yrow + (uint64_t)j * g.ldy;
+        if constexpr (OUT == 0) st_u32(p + 4 * (uint64_t)r.n, bits[j]);
+        else if constexpr (OUT == 2) p[r.n] = (uint8_t)bits[j];
+        else st_u16(p + 2 * (uint64_t)r.n, (uint16_t)bits[j]);
+      }
+    }
+  }
+  template <int ACT>
+  __device__ __forceinline__ void run_act(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[16],
+                                          const uint32_t (&v1)[16], bool two) const {
+    switch (g.out) {
+      case 0: run16<ACT, 0>(r, tk, m0, mc, v0, v1, two); break;
+      case 1: run16<ACT, 1>(r, tk, m0, mc, v0, v1, two); break;
+      case 2: run16<ACT, 2>(r, tk, m0, mc, v0, v1, two); break;
+      default: run16<ACT, 3>(r, tk, m0, mc, v0, v1, two); break;
+    }
+  }
+  __device__ __forceinline__ void put16(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[16],
+                                        const uint32_t (&v1)[16], bool two) const {
+    if (mc <= 0) return;
+    if (g.act <= 2) run_act<0>(r, tk, m0, mc, v0, v1, two);
+    else run_act<-1>(r, tk, m0, mc, v0, v1, two);
   }
 };
+
+__device__ __forceinline__ bool aborted(const int* flag) { return *(volatile const int*)flag != 0; }
 
 template <class Epi>
 __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ MmaMaps maps, const MmaShape sh,
                                                         const Epi epi) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_full[kMaxStages], bar_empty[kMaxStages], bar_acc;
+  __shared__ uint64_t bar_full[kMaxStages], bar_empty[kMaxStages], bar_accf[2], bar_acce[2];
   __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+  __shared__ float s_tok[2][256];             // the tile's token factors (double buffered per tile)
+  // barrier of the epilogue warps that also ORs a flag over them, so all of them take the same
+  // branch after it
+  auto epi_sync_or = [](bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, 1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(32 * kEpiWarps)
+        : "memory");
+    return r != 0;
+  };
   // the swizzled tiles want 1024-byte aligned shared addresses
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int split = sh.split;
+  const int S = sh.stages, NT = sh.NT, split = sh.split, nacc = sh.nacc;
   const int crank = split > 1 ? (int)cluster_rank() : 0;
-  const int item = blockIdx.x / split;
-  const int tt = item % sh.ntt, rt = item / sh.ntt;
-  int s = 0;
-  while (s + 1 < sh.nseg && rt >= sh.tile0[s + 1]) ++s;
-  const int row0 = (rt - sh.tile0[s]) * kRows;
-  const int tok0 = tt * sh.NT;
-  const int NT = sh.NT;
   const int nkb = sh.nkb1 + sh.nkb2;
   const int per = (nkb + split - 1) / split;
   const int k_lo = min(nkb, crank * per), k_hi = min(nkb, k_lo + per);
   const int nk = k_hi - k_lo;
-  const int nacc = sh.nacc;
   const bool used0 = nk > 0 && (sh.gated || k_lo < sh.nkb1);
   const bool used1 = nk > 0 && (sh.gated || k_hi > sh.nkb1);
-  const uint32_t a_bytes = kRows * kSlice, b_bytes = (uint32_t)NT * kSlice;
   const int na = sh.gated ? 2 : 1;
-  const uint32_t stage_bytes = na * a_bytes + b_bytes;
-  const int S = sh.stages;
+  const uint32_t a_bytes = kRows * kSlice;
+  const uint32_t stage_bytes = na * a_bytes + (uint32_t)NT * kSlice;
+  const uint32_t acc_cols = nacc * NT;
   uint32_t ncols = 32;
-  while (ncols < (uint32_t)(nacc * NT)) ncols <<= 1;
+  while (ncols < sh.nbuf * acc_cols) ncols <<= 1;
+  const int item0 = blockIdx.x / split, istride = gridDim.x / split;
+  auto stamp = [&](int k) {
+    if (sh.trace && blockIdx.x < kTraceCtas) g_mma_trace[blockIdx.x * kTraceStamps + k] = gtimer();
+  };
+  if (threadIdx.x == 0) stamp(0);
+  auto coords = [&](int item, int& s, int& row0, int& tok0) {
+    const int tt = item % sh.ntt, rt = item / sh.ntt;
+    s = 0;
+    while (s + 1 < sh.nseg && rt >= sh.tile0[s + 1]) ++s;
+    row0 = (rt - sh.tile0[s]) * kRows;
+    tok0 = tt * NT;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&bar_full[i], 1);
       mbar_init(&bar_empty[i], 1);
     }
-    mbar_init(&bar_acc, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_accf[i], 1);
+      mbar_init(&bar_acce[i], kEpiWarps);
+    }
+    s_abort = 0;
     mbar_fence_init();
     tma_prefetch_desc(&maps.x);
   }
-  if (warp == 0) tmem_alloc(&s_tmem, ncols);
+  if (warp == 1) tmem_alloc(&s_tmem, ncols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
+  if (threadIdx.x == 0) stamp(1);
 
-  if (threadIdx.x == 0) {
-    // producer: K slice i of this CTA's range into stage i % S
-    for (int i = 0; i < nk; ++i) {
-      const int st = i % S;
-      const uint32_t use = i / S;
-      if (i >= S && !mbar_wait(&bar_empty[st], (use & 1) ^ 1, sh.err, 1)) break;
-      uint8_t* sa = smem + st * stage_bytes;
-      const int k = k_lo + i;
-      int xk;
-      mbar_expect_tx(&bar_full[st], stage_bytes);
-      if (sh.gated) {
-        tma_load_2d(sa, &maps.w[0], k * kSlice, row0, &bar_full[st]);
-        tma_load_2d(sa + a_bytes, &maps.w[2], k * kSlice, row0, &bar_full[st]);
-        xk = k * kSlice;
-      } else if (k < sh.nkb1) {
-        tma_load_2d(sa, &maps.w[2 * s], k * kSlice, row0, &bar_full[st]);
-        xk = k * kSlice;
-      } else {
-        tma_load_2d(sa, &maps.w[2 * s + 1], (k - sh.nkb1) * kSlice, row0, &bar_full[st]);
-        xk = sh.kb + (k - sh.nkb1) * kSlice;
-      }
-      tma_load_2d(sa + na * a_bytes, &maps.x, xk, tok0, &bar_full[st]);
-    }
-  } else if (threadIdx.x == 32 && nk > 0) {
-    // MMA issuer
-    const uint32_t idesc = idesc_i8(kRows, NT);
-    bool first0 = true, first1 = true;
-    for (int i = 0; i < nk; ++i) {
-      const int st = i % S;
-      if (!mbar_wait(&bar_full[st], (i / S) & 1, sh.err, 2)) break;
-      tc_fence_after();
-      const uint32_t sa = smem_u32(smem + st * stage_bytes);
-      const uint32_t sb = sa + na * a_bytes;
-      const int k = k_lo + i;
-      auto run = [&](uint32_t a_addr, uint32_t d, bool& first) {
-#pragma unroll
-        for (int kk = 0; kk < kSlice / 32; ++kk)
-          mma_i8(d, sdesc_k128(a_addr + 32 * kk), sdesc_k128(sb + 32 * kk), idesc, (first && kk == 0) ? 0u : 1u);
-        first = false;
-      };
-      if (sh.gated) {
-        run(sa, tmem, first0);
-        run(sa + a_bytes, tmem + NT, first1);
-      } else if (k < sh.nkb1) {
-        run(sa, tmem, first0);
-      } else {
-        run(sa, tmem + NT, first1);
-      }
-      mma_commit(&bar_empty[st]);
-    }
-    mma_commit(&bar_acc);
-  }
-  __syncwarp();
-  bool ok = true;
-  if (nk > 0) ok = mbar_wait(&bar_acc, 0, sh.err, 3);
-  if (threadIdx.x == 0 && !ok) {   // after a timeout: wait (bounded) for copies still in flight
-    for (int i = max(0, nk - S); i < nk; ++i) mbar_wait(&bar_full[i % S], (i / S) & 1, nullptr, 0);
-  }
-  __syncwarp();
-  tc_fence_after();
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-  const int r = warp * 32 + lane;               // this thread's TMEM lane = weight row in the tile
-  const int nrow = sh.nrow[s];
-
-  if (split == 1) {
-    const int c = row0 + r;
-    for (int j0 = 0; j0 < NT; j0 += 16) {
-      uint32_t v0[16], v1[16];
-      tmem_ld16(trow + j0, v0);
-      if (nacc == 2) tmem_ld16(trow + NT + j0, v1);
-      tmem_wait_ld();
-      if (ok && c < nrow) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = tok0 + j0 + j;
-          if (m < sh.M) epi(s, c, m, used0 ? (int)v0[j] : 0, (nacc == 2 && used1) ? (int)v1[j] : 0);
+  if (warp == 0) {
+    if (lane == 0 && nk > 0) {
+      // producer: K slice q (counted over all items of this CTA) into stage q % S
+      uint32_t q = 0;
+      bool stop = false;
+      for (int item = item0; item < sh.items && !stop; item += istride) {
+        int s, row0, tok0;
+        coords(item, s, row0, tok0);
+        for (int i = 0; i < nk; ++i, ++q) {
+          const int st = q % S;
+          if (q >= (uint32_t)S && !mbar_wait(&bar_empty[st], ((q / S) & 1) ^ 1, sh.err, 1)) {
+            s_abort = 1;
+            stop = true;
+            break;
+          }
+          if (aborted(&s_abort)) {
+            stop = true;
+            break;
+          }
+          uint8_t* sa = smem + st * stage_bytes;
+          const int k = k_lo + i;
+          int xk;
+          mbar_expect_tx(&bar_full[st], stage_bytes);
+          if (sh.gated) {
+            tma_load_2d(sa, &maps.w[0], k * kSlice, row0, &bar_full[st]);
+            tma_load_2d(sa + a_bytes, &maps.w[2], k * kSlice, row0, &bar_full[st]);
+            xk = k * kSlice;
+          } else if (k < sh.nkb1) {
+            tma_load_2d(sa, &maps.w[2 * s], k * kSlice, row0, &bar_full[st]);
+            xk = k * kSlice;
+          } else {
+            tma_load_2d(sa, &maps.w[2 * s + 1], (k - sh.nkb1) * kSlice, row0, &bar_full[st]);
+            xk = sh.kb + (k - sh.nkb1) * kSlice;
+          }
+          tma_load_2d(sa + na * a_bytes, &maps.x, xk, tok0, &bar_full[st]);
+          if (q == 0) stamp(2);
         }
       }
+      if (stop) {   // wait (bounded) for the copies still in flight before the CTA ends
+        for (uint32_t i = q > (uint32_t)S ? q - S : 0; i < q; ++i) mbar_wait(&bar_full[i % S], (i / S) & 1, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nk > 0) {
+      // MMA issuer
+      const uint32_t idesc = idesc_i8(kRows, NT);
+      uint32_t q = 0;
+      int t = 0;
+      bool stop = false;
+      for (int item = item0; item < sh.items && !stop; item += istride, ++t) {
+        const int buf = sh.nbuf == 2 ? (t & 1) : 0;
+        const uint32_t use = sh.nbuf == 2 ? (t >> 1) : t;
+        if (use > 0 && !mbar_wait(&bar_acce[buf], (use & 1) ^ 1, sh.err, 2)) {
+          s_abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d0 = tmem + buf * acc_cols;
+        bool first0 = true, first1 = true;
+        for (int i = 0; i < nk; ++i, ++q) {
+          const int st = q % S;
+          if (!mbar_wait(&bar_full[st], (q / S) & 1, sh.err, 3) || aborted(&s_abort)) {
+            s_abort = 1;
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          if (q == 0) stamp(3);
+          const uint32_t sa = smem_u32(smem + st * stage_bytes);
+          const uint32_t sb = sa + na * a_bytes;
+          const int k = k_lo + i;
+          auto run = [&](uint32_t a_addr, uint32_t d, bool& first) {
+#pragma unroll
+            for (int kk = 0; kk < kSlice / 32; ++kk)
+              mma_i8(d, sdesc_k128(a_addr + 32 * kk), sdesc_k128(sb + 32 * kk), idesc, (first && kk == 0) ? 0u : 1u);
+            first = false;
+          };
+          if (sh.gated) {
+            run(sa, d0, first0);
+            run(sa + a_bytes, d0 + NT, first1);
+          } else if (k < sh.nkb1) {
+            run(sa, d0, first0);
+          } else {
+            run(sa, d0 + NT, first1);
+          }
+          mma_commit(&bar_empty[st]);
+        }
+        mma_commit(&bar_accf[buf]);
+      }
+      stamp(4);
     }
   } else {
-    // The partial tile goes to shared memory (P[a][token][row], int32, in the drained stages) and
-    // the TMEM columns are freed before the first cluster barrier: a CTA that holds TMEM never
-    // waits on another CTA, so CTAs of concurrent launches blocked in tcgen05.alloc always
-    // progress.
-    int* P = reinterpret_cast<int*>(smem);
-    for (int j0 = 0; j0 < NT; j0 += 16) {
-      uint32_t v0[16], v1[16];
-      tmem_ld16(trow + j0, v0);
-      if (nacc == 2) tmem_ld16(trow + NT + j0, v1);
-      tmem_wait_ld();
+    // epilogue warps
+    const int ew = warp & 3, half = (warp - 2) >> 2;
+    const int r = ew * 32 + lane;
+    const int et = threadIdx.x - 64;             // 0..255
+    const uint32_t tlane = tmem + ((uint32_t)(ew * 32) << 16);
+    int t = 0;
+    for (int item = item0; item < sh.items; item += istride, ++t) {
+      const int buf = sh.nbuf == 2 ? (t & 1) : 0;
+      const uint32_t use = sh.nbuf == 2 ? (t >> 1) : t;
+      int s, row0, tok0;
+      coords(item, s, row0, tok0);
+      float* tk = s_tok[t & 1];
+      for (int j = et; j < NT; j += 32 * kEpiWarps) tk[j] = ftz(epi.tok(min(tok0 + j, sh.M - 1)));
+      if (epi_sync_or(aborted(&s_abort))) break;
+      bool ok = true;
+      if (nk > 0) {
+        ok = mbar_wait(&bar_accf[buf], use & 1, sh.err, 4);
+        if (!ok) s_abort = 1;
+      }
+      __syncwarp();
+      tc_fence_after();
+      const uint32_t tb = tlane + buf * acc_cols;
+      if (split > 1) {
+        // the partial tile to shared memory: P[a][token][row]
+        int* P = reinterpret_cast<int*>(smem);
+        for (int j0 = 16 * half; j0 < NT; j0 += 32) {
+          uint32_t v0[16], v1[16];
+          tmem_ld16(tb + j0, v0);
+          if (nacc == 2) tmem_ld16(tb + NT + j0, v1);
+          tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        P[(j0 + j) * kRows + r] = used0 ? (int)v0[j] : 0;
-        if (nacc == 2) P[(NT + j0 + j) * kRows + r] = used1 ? (int)v1[j] : 0;
+          for (int j = 0; j < 16; ++j) {
+            P[(j0 + j) * kRows + r] = used0 ? (int)v0[j] : 0;
+            if (nacc == 2) P[(NT + j0 + j) * kRows + r] = used1 ? (int)v1[j] : 0;
+          }
+        }
+        break;                                   // one tile per CTA in this mode
+      }
+      const int c = row0 + r;
+      const bool live = ok && c < sh.nrow[s];
+      typename Epi::Row rw{};
+      if (live) rw = epi.row(s, c);
+      const int last = (NT - 16 - 16 * half) / 32 * 32 + 16 * half;   // this warp's last chunk
+      for (int j0 = 16 * half; j0 < NT; j0 += 32) {
+        uint32_t v0[16], v1[16];
+        tmem_ld16(tb + j0, v0);
+        if (nacc == 2) tmem_ld16(tb + NT + j0, v1);
+        tmem_wait_ld();
+        if (j0 == last && sh.nbuf == 2) {        // the accumulator is in registers: release it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar_acce[buf]);
+        }
+        if (live) epi.put16(rw, tk + j0, tok0 + j0, min(16, sh.M - tok0 - j0), v0, v1, nacc == 2);
+      }
+      if (NT <= 16 * half && sh.nbuf == 2) {     // no chunk for this warp: release at once
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_acce[buf]);
       }
     }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, ncols);
-    cluster_sync();
-    const int rs = kRows / split, r0 = crank * rs;
-    const uint32_t pbase = smem_u32(P);
-    for (int idx = threadIdx.x; idx < rs * NT; idx += kThreads) {
-      const int rr = r0 + idx % rs, j = idx / rs;
-      const uint32_t off = (uint32_t)(j * kRows + rr) * 4;
-      int a0 = 0, a1 = 0;
-      for (int p = 0; p < split; ++p) {
-        a0 += dsmem_ld_s32(pbase + off, p);
-        if (nacc == 2) a1 += dsmem_ld_s32(pbase + NT * kRows * 4 + off, p);
-      }
-      const int c = row0 + rr, m = tok0 + j;
-      if (ok && c < nrow && m < sh.M) epi(s, c, m, a0, a1);
-    }
-    cluster_sync();      // peers have read this CTA's partials
-    return;
   }
+
+  __syncwarp();                              // lanes 1-31 of warps 0 / 1 wait for their lane 0
+  if (threadIdx.x == 64) stamp(6);
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, ncols);
+  if (warp == 1) tmem_dealloc(tmem, ncols);
+  if (split == 1) {
+    if (threadIdx.x == 0) stamp(7);
+    return;
+  }
+
+  // split-K: sum the peers' partial tiles for this CTA's rows, then the epilogue (16 tokens of one
+  // row per thread and pass; s_tok[0] holds the tile's token factors)
+  cluster_sync();
+  {
+    int s, row0, tok0;
+    coords(item0, s, row0, tok0);
+    const int rs = kRows / split, r0 = crank * rs, ng = kThreads / rs;
+    const int rr = r0 + threadIdx.x % rs, jg = threadIdx.x / rs;
+    const int c = row0 + rr;
+    const bool live = !aborted(&s_abort) && c < sh.nrow[s];
+    const uint32_t p0 = smem_u32(smem) + (uint32_t)rr * 4;
+    typename Epi::Row rw{};
+    if (live) rw = epi.row(s, c);
+    for (int j0 = 16 * jg; j0 < NT; j0 += 16 * ng) {
+      uint32_t a0[16], a1[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        a0[j] = 0;
+        a1[j] = 0;
+      }
+      for (int p = 0; p < split; ++p) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          a0[j] += (uint32_t)dsmem_ld_s32(p0 + (uint32_t)((j0 + j) * kRows) * 4, p);
+          if (nacc == 2) a1[j] += (uint32_t)dsmem_ld_s32(p0 + (uint32_t)((NT + j0 + j) * kRows) * 4, p);
+        }
+      }
+      if (live) epi.put16(rw, s_tok[0] + j0, tok0 + j0, min(16, sh.M - tok0 - j0), a0, a1, nacc == 2);
+    }
+  }
+  cluster_sync();      // peers have read this CTA's partials
+  if (threadIdx.x == 0) stamp(7);
 }
 
 // ------------------------------------------------------------------------------------ host side
@@ -289,40 +564,45 @@ int* err_flag() {
   return p;
 }
 
-// Token tile, split factor, stages and shared memory for a GEMM of `tiles` row tiles.
-bool plan(MmaShape& sh, int tiles, int* smem) {
+// Token tile, mode (split-K factor or persistent), stages, shared memory and grid.
+bool plan(MmaShape& sh, int tiles, int* smem, int* grid) {
   sh.NT = std::min(256, (sh.M + 15) / 16 * 16);
-  sh.ntt = (sh.M + sh.NT - 1) / sh.NT;
+  int ntt = (sh.M + sh.NT - 1) / sh.NT;
   const int nkb = sh.nkb1 + sh.nkb2;
   int split = 1;
-  while (split < 8 && tiles * sh.ntt * split * 2 <= 2 * 148 && nkb >= split * 2 * 2) split *= 2;
-  if (split > 1 && sh.nacc * sh.NT * kRows * 4 > kSmemBudget) {   // the partial tile must fit
-    sh.NT = 128;
-    sh.ntt = (sh.M + sh.NT - 1) / sh.NT;
-  }
+  while (split < 8 && tiles * ntt * split * 2 <= 2 * kSMs && nkb >= split * 4) split *= 2;
   sh.split = split;
+  sh.nbuf = split > 1 ? 1 : 2;
+  // the partial tile (split-K) or both accumulators (persistent) must fit
+  if ((split > 1 && sh.nacc * sh.NT * kRows * 4 > kSmemBudget) || sh.nbuf * sh.nacc * sh.NT > 512) sh.NT = 128;
+  sh.ntt = (sh.M + sh.NT - 1) / sh.NT;
+  sh.items = tiles * sh.ntt;
   const int per = (nkb + split - 1) / split;
   const int na = sh.gated ? 2 : 1;
   const int stage = na * kRows * kSlice + sh.NT * kSlice;
-  sh.stages = std::max(1, std::min({kMaxStages, per, kSmemBudget / stage}));
+  sh.stages = std::max(1, std::min(kMaxStages, kSmemBudget / stage));
+  if (split > 1) sh.stages = std::min(sh.stages, per);
   const int part = split > 1 ? sh.nacc * sh.NT * kRows * 4 : 0;
   *smem = std::max(sh.stages * stage, part) + 1024;
-  // CTAs that share an SM must fit in its 512 TMEM columns together: a CTA blocked in
-  // tcgen05.alloc must never wait on a cluster peer that holds the columns it needs.
+  // CTAs that share an SM must fit in its 512 TMEM columns together, so a CTA never waits in
+  // tcgen05.alloc
   int ncols = 32;
-  while (ncols < sh.nacc * sh.NT) ncols <<= 1;
+  while (ncols < sh.nbuf * sh.nacc * sh.NT) ncols <<= 1;
   const int max_res = 512 / ncols;
   *smem = std::max(*smem, kSmemPerSM / (max_res + 1) + 64 - 1024);
+  const int res = std::max(1, std::min(max_res, kSmemPerSM / (*smem + 1024 + 256)));
+  *grid = split > 1 ? sh.items * split : std::min(sh.items, kSMs * res);
+  sh.trace = g_trace_on.load();
   sh.err = err_flag();
-  return sh.stages >= 1 && sh.err != nullptr;
+  return sh.err != nullptr;
 }
 
 template <class Epi>
-cudaError_t launch(const MmaMaps& maps, const MmaShape& sh, const Epi& epi, int tiles, int smem, cudaStream_t st) {
+cudaError_t launch(const MmaMaps& maps, const MmaShape& sh, const Epi& epi, int grid, int smem, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(k_mma_i8<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(tiles * sh.ntt * sh.split);
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -332,7 +612,7 @@ cudaError_t launch(const MmaMaps& maps, const MmaShape& sh, const Epi& epi, int 
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = sh.split > 1 ? 1 : 0;       // a plain launch without split-K
   return cudaLaunchKernelEx(&cfg, k_mma_i8<Epi>, maps, sh, epi);
 }
 }  // namespace
@@ -365,15 +645,15 @@ cudaError_t eng_gemm_mma(const EngGemvArgs& g, cudaStream_t st) {
     tiles += (g.seg[s].n + kRows - 1) / kRows;
   }
   sh.tile0[nseg] = tiles;
-  int smem = 0;
-  if (!plan(sh, tiles, &smem)) return cudaErrorInvalidValue;
+  int smem = 0, grid = 0;
+  if (!plan(sh, tiles, &smem, &grid)) return cudaErrorInvalidValue;
   if (!make_map(&maps.x, g.A, g.K, g.M, g.lda, sh.NT)) return cudaErrorInvalidValue;
   for (int s = 0; s < g.nseg; ++s) {
     if (!make_map(&maps.w[2 * s], g.seg[s].W, g.kb, g.seg[s].n, g.kb, kRows)) return cudaErrorInvalidValue;
     if (two && !make_map(&maps.w[2 * s + 1], g.seg[s].W2, g.K - g.kb, g.seg[s].n, g.K - g.kb, kRows))
       return cudaErrorInvalidValue;
   }
-  return launch(maps, sh, EngEpi{g}, tiles, smem, st);
+  return launch(maps, sh, EngEpi{g}, grid, smem, st);
 }
 
 bool mma_machine_ok(const GemmArgs& g) {
@@ -393,11 +673,11 @@ cudaError_t gemm_mma(const GemmArgs& g, cudaStream_t st) {
   sh.tile0[0] = 0;
   sh.tile0[1] = tiles;
   sh.nrow[0] = g.N;
-  int smem = 0;
-  if (!plan(sh, tiles, &smem)) return cudaErrorInvalidValue;
+  int smem = 0, grid = 0;
+  if (!plan(sh, tiles, &smem, &grid)) return cudaErrorInvalidValue;
   if (!make_map(&maps.x, g.A, g.K, g.M, g.lda, sh.NT)) return cudaErrorInvalidValue;
   if (!make_map(&maps.w[0], g.W, g.K, g.N, g.K, kRows)) return cudaErrorInvalidValue;
-  return launch(maps, sh, MachEpi{g}, tiles, smem, st);
+  return launch(maps, sh, MachEpi{g}, grid, smem, st);
 }
 
 std::atomic<int> g_min_rows{-1};
@@ -419,6 +699,21 @@ int mma_error_code() {
 }
 
 }  // namespace tc
+
+extern "C" int tc_mma_trace(int32_t enable, uint64_t* out, uint32_t cap) {
+  if (enable && !tc::g_trace_on.load()) {
+    void* a = nullptr;
+    if (cudaGetSymbolAddress(&a, tc::g_mma_trace) != cudaSuccess ||
+        cudaMemset(a, 0, sizeof(tc::g_mma_trace)) != cudaSuccess)
+      return TC_ERR_CUDA;
+  }
+  tc::g_trace_on.store(enable ? 1 : 0);
+  if (!out || !cap) return 0;
+  const uint32_t n = std::min<uint32_t>(cap, tc::kTraceCtas * tc::kTraceStamps);
+  if (cudaDeviceSynchronize() != cudaSuccess) return TC_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(out, tc::g_mma_trace, n * sizeof(uint64_t)) != cudaSuccess) return TC_ERR_CUDA;
+  return (int)n;
+}
 
 extern "C" int tc_set_mma_min_rows(int32_t rows) {
   const int prev = tc::mma_min_rows();

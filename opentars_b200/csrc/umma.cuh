@@ -40,6 +40,9 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 // Waits for the phase of `parity` to complete; false (and *err = code) after kSpinLimit polls.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   for (uint32_t i = 0; i < kSpinLimit; ++i)
@@ -106,8 +109,9 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Thread-block clusters: barrier over every thread of the cluster, and a load from the shared
-// memory of CTA `rank` at the offset of this CTA's `local` address.
+// Thread-block clusters: barrier over every thread of the cluster (it orders the shared-memory
+// accesses around it), and a load from the shared memory of CTA `rank` at the offset of this
+// CTA's `local` address (no memory clobber, so independent loads are issued back to back).
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -119,8 +123,8 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ int dsmem_ld_s32(uint32_t local, uint32_t rank) {
   uint32_t remote;
   int v;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
-  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(remote) : "memory");
+  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(remote));
   return v;
 }
 

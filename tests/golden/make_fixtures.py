@@ -12,6 +12,8 @@ What it stores (all small):
   models.json      (--models) per-step logits SHA-256 / argmax of the reference's QwenLowering
                    + golden Machine greedy decode for small Qwen3 / Gemma-3 configs, and the
                    SHA-256 of the lowered DDR image and queue bytes
+  gemm_sweep.json  (--gemm) config 1: the SHA-256 of every (M, shape) output of bench.py's GEMM
+                   sweep image (bench.build_gemm, seed 1234) run on the reference golden Machine
 """
 from __future__ import annotations
 
@@ -253,12 +255,25 @@ def make_full_models(ref: str, only: str = ""):
     return out
 
 
+def make_gemm_sweep(G):
+    import bench
+    p = bench.build_gemm(1, 0)
+    m = G.Machine(bytearray(p["ddr"].tobytes()))
+    assert m.run_queue(p["q_setup"], p["n_setup"]).done
+    assert m.run_queue(p["q_main"], p["n_main"]).done
+    y0, yn = p["y_region"]
+    region = np.frombuffer(bytes(m.ddr[y0:y0 + yn]), np.uint8)
+    return dict(seed=1234, M=list(bench.GEMM_M), shapes=[list(s) for s in bench.GEMM_SHAPES],
+                sha256=bench.gemm_hashes(bench.gemm_outputs(p, [region])))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("OPENTARS_REF", ""), required=False)
     ap.add_argument("--models", action="store_true")
     ap.add_argument("--skip-queues", action="store_true")
     ap.add_argument("--full", default="", help="full-size models: 'all' or one name")
+    ap.add_argument("--gemm", action="store_true", help="config 1's GEMM sweep")
     a = ap.parse_args()
     if not a.ref:
         raise SystemExit("--ref <path to the openTARS checkout> is required")
@@ -280,6 +295,9 @@ def main():
         old.update(make_full_models(a.ref, "" if a.full == "all" else a.full))
         path.write_text(json.dumps(old, indent=1))
         print(f"full models in {time.time() - t:.1f}s")
+    if a.gemm:
+        (HERE / "gemm_sweep.json").write_text(json.dumps(make_gemm_sweep(G), indent=1))
+        print(f"gemm sweep in {time.time() - t:.1f}s")
 
 
 if __name__ == "__main__":

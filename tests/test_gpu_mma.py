@@ -132,3 +132,25 @@ def test_engine_on_tensor_cores_matches_oracle(batch, mma_min_rows):
             assert ids[b] == oids, (name, b)
             assert all(np.array_equal(lg[b].view(np.uint32), ol.view(np.uint32))
                        for lg, ol in zip(logits, ologits)), (name, b)
+
+
+def test_gemm_sweep_matches_reference():
+    """Config 1 (bench.py --workload gemm): every (M, shape) output of the whole sweep, run through
+    the board runtime on the GPU, against the reference golden Machine's hashes."""
+    import json
+
+    import bench
+    from opentars_b200.board import Cuda
+    from tests import fixtures as FX
+    want = json.loads((FX.GOLDEN / "gemm_sweep.json").read_text())["sha256"]
+    p = bench.build_gemm(1, 0)
+    dev = Cuda(len(p["ddr"]))
+    dev.mem[:] = p["ddr"]
+    dev.to_dev(0, len(p["ddr"]))
+    assert dev.run(p["q_setup"], p["n_setup"])[0]
+    assert dev.run(p["q_main"], p["n_main"])[0]
+    y0, yn = p["y_region"]
+    dev.from_dev(y0, yn)
+    got = bench.gemm_hashes(bench.gemm_outputs(p, [dev.mem[y0:y0 + yn]]))
+    dev.close()
+    assert got == want, [k for k in got if got[k] != want[k]]

@@ -150,3 +150,20 @@ def test_oracle_error_priority_and_overlap():
     mem[0x2000:0x2040] = C.encode({**good, "Y_OFF": 0x200})
     with pytest.raises(ContractError):
         OracleMachine(mem).run_queue(0x2000, 1)
+
+
+def test_oracle_reproduces_reference_gemm_sweep_small_m():
+    """Config 1's sweep image (bench.build_gemm) at M = 4 and 16 through the oracle: the same
+    output hashes as the reference golden Machine's run of the full sweep."""
+    import json
+
+    import bench
+    from oracle.machine import OracleMachine
+    want = json.loads((FX.GOLDEN / "gemm_sweep.json").read_text())["sha256"]
+    p = bench.build_gemm(1, 0, ms=(4, 16))
+    o = OracleMachine(bytearray(p["ddr"].tobytes()))
+    assert o.run_queue(p["q_setup"], p["n_setup"]).done
+    assert o.run_queue(p["q_main"], p["n_main"]).done
+    y0, yn = p["y_region"]
+    got = bench.gemm_hashes(bench.gemm_outputs(p, [np.frombuffer(bytes(o.ddr[y0:y0 + yn]), np.uint8)]))
+    assert got == {k: want[k] for k in got}
