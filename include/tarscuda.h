@@ -94,12 +94,12 @@ int tc_synchronize(tc_machine* m);
  * Default 16 (or the environment variable TARSCUDA_MMA_MIN_M). Returns the previous value; it
  * applies to every machine and engine of the process, to launches enqueued afterwards. */
 int tc_set_mma_min_rows(int32_t rows);
-/* Tracing of the tensor-core GEMM: with enable != 0, launches enqueued afterwards record per CTA
- * (the first 2048 CTAs of a launch) 8 globaltimer stamps in nanoseconds: entry, setup done, first
- * TMA load issued, first stage consumed by the MMA thread, last MMA issued, first accumulator
- * read by the epilogue, epilogue done, exit. Turning tracing on zeroes the stamps; traced
- * launches then overwrite them CTA by CTA (trace one launch at a time). With out != NULL, waits
- * for the device and copies min(cap, 2048 * 8) stamps; returns that count (or TC_ERR_CUDA). */
+/* Tracing of the tensor-core GEMM: with enable = n > 0, the n-th tensor-core GEMM launch enqueued
+ * (or captured) after this call records per CTA (its first 2048 CTAs) 8 globaltimer stamps in
+ * nanoseconds: entry, setup done, first TMA load issued, first stage consumed by the MMA thread,
+ * last MMA issued, first accumulator read by the epilogue, epilogue done, exit. Enabling zeroes
+ * the stamps; enable = 0 turns tracing off. With out != NULL, waits for the device and copies
+ * min(cap, 2048 * 8) stamps; returns that count (or TC_ERR_CUDA). */
 int tc_mma_trace(int32_t enable, uint64_t* out, uint32_t cap);
 
 /* Host-only helpers (no device needed). golden.Machine.validate (golden.py:59-169): decodes the

@@ -16,6 +16,7 @@
 #include "../../include/tarscuda.h"
 #include "../../include/tarscuda_engine.h"
 #include "engine.h"
+#include "mma.h"
 
 using namespace tc;
 
@@ -44,7 +45,7 @@ struct tc_engine {
   float* E = nullptr;                       // fp32 embedding table [vocab][H]
   int *tok = nullptr, *next = nullptr, *pos = nullptr;
   float *x = nullptr, *x1 = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *att = nullptr;
-  float *o = nullptr, *g = nullptr, *d = nullptr, *logits = nullptr;
+  float *o = nullptr, *g = nullptr, *u = nullptr, *d = nullptr, *logits = nullptr;
   int8_t* q8 = nullptr;                      // quantised rows [M][max(H, I, qw)]
   float* qs = nullptr;
   float *kc = nullptr, *vc = nullptr;        // [L][B][Tp][kvw]
@@ -170,15 +171,25 @@ int enqueue_step(tc_engine* e, int n, const int* tok_in) {
       else { a.mode = 0; a.in = e->x1; a.ld_in = H; }
       KERNEL(kKNormQuant, (uint64_t)a.rows * a.H * (a.mode ? 13 : 5), eng_norm_quant(a, st));
     }
-    {  // gate, up: act(gate) * up
+    // gate, up. On the tensor cores (M >= the MMA threshold) as one plain GEMM of two segments,
+    // act(gate) * up fused into the row quantiser (its 1024-thread rows hide the activation's
+    // latency); on the GEMV path act(gate) * up in the GEMM epilogue, then the plain quantiser.
+    if (M >= mma_min_rows()) {
+      EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, M, H);
+      add_seg(g, L.gate, e->g, I);
+      add_seg(g, L.up, e->u, I);
+      g.mode = kEpiStore;
+      KERNEL(kKGemv, gemv_bytes(g), eng_gemv(g, st));
+      KERNEL(kKQuant, (uint64_t)M * I * 9, eng_quant_gated(e->g, e->u, I, I, md.act, e->q8, ldq, e->qs, M, st));
+    } else {
       EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, M, H);
       add_seg(g, L.gate, e->g, I);
       add_seg(g, L.up, e->g, I);
       g.mode = kEpiGated;
       g.act = md.act;
       KERNEL(kKGemv, gemv_bytes(g), eng_gemv(g, st));
+      KERNEL(kKQuant, (uint64_t)M * I * 5, eng_quant(e->g, I, I, e->q8, ldq, e->qs, M, st));
     }
-    KERNEL(kKQuant, (uint64_t)M * I * 5, eng_quant(e->g, I, I, e->q8, ldq, e->qs, M, st));
     {  // down (K blocks on Gemma); Qwen3 adds the residual into x
       EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, M, I);
       Lin dl = L.down[0];
@@ -276,6 +287,7 @@ int tc_engine_create(tc_machine* image, const tc_model_desc* md, const tc_layer_
   if (c == cudaSuccess) c = alloc((void**)&e->k, (size_t)M * e->kvw * 4);
   if (c == cudaSuccess) c = alloc((void**)&e->v, (size_t)M * e->kvw * 4);
   if (c == cudaSuccess) c = alloc((void**)&e->g, (size_t)M * e->I * 4);
+  if (c == cudaSuccess) c = alloc((void**)&e->u, (size_t)M * e->I * 4);
   if (c == cudaSuccess) c = alloc((void**)&e->logits, (size_t)e->B * md->vocab * 4);
   if (c == cudaSuccess) c = alloc((void**)&e->q8, (size_t)M * ldq);
   if (c == cudaSuccess) c = alloc((void**)&e->qs, (size_t)M * 4);
@@ -294,7 +306,7 @@ int tc_engine_destroy(tc_engine* e) {
   if (!e) return TC_OK;
   if (e->st) cudaStreamSynchronize(e->st);
   for (auto& gx : e->graph) if (gx) cudaGraphExecDestroy(gx);
-  void* bufs[] = {e->E, e->tok, e->next, e->pos, e->x, e->x1, e->q, e->k, e->v, e->qr, e->att, e->o, e->g, e->d,
+  void* bufs[] = {e->E, e->tok, e->next, e->pos, e->x, e->x1, e->q, e->k, e->v, e->qr, e->att, e->o, e->g, e->u, e->d,
                   e->logits, e->q8, e->qs, e->kc, e->vc};
   for (void* p : bufs) if (p) cudaFree(p);
   if (e->st) cudaStreamDestroy(e->st);

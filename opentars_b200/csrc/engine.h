@@ -61,6 +61,9 @@ struct AttnArgs {
 cudaError_t eng_embed(const float* E, const int* tok, float* x, int H, int scale_on, float scale, int rows, cudaStream_t st);
 cudaError_t eng_norm_quant(const NormQuantArgs& a, cudaStream_t st);
 cudaError_t eng_quant(const float* x, int ldx, int N, int8_t* q, int ldq, float* qs, int rows, cudaStream_t st);
+// rows of ftz(fmul(ftz(act(gate)), up)) quantised per row (the gated MLP's product and ROW_QUANT)
+cudaError_t eng_quant_gated(const float* gate, const float* up, int ld, int N, int act, int8_t* q, int ldq, float* qs,
+                            int rows, cudaStream_t st);
 cudaError_t eng_gemv(const EngGemvArgs& g, cudaStream_t st);
 cudaError_t eng_qk_rope(const QkRopeArgs& a, cudaStream_t st);
 cudaError_t eng_attention(const AttnArgs& a, int batch, cudaStream_t st);

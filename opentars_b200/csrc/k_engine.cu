@@ -137,6 +137,36 @@ __global__ void __launch_bounds__(256) k_quant(const float* x, int ldx, int N, i
   if (threadIdx.x == 0) qs[r] = ftz(fmul(amax, bf(0x3C010204u)));
 }
 
+// The gated MLP's product and its row quantisation in one pass (llm.py's act(gate) * up, then
+// ROW_QUANT): gate and up hold the two GEMMs' fp32 outputs (no activation applied). Per element
+// v = ftz(fmul(ftz(act(gate)), up)) - the bits the gated GEMM epilogue (act, store) and ELT_MUL
+// (fmul, store) produce - then the row's absmax and the int8 codes as in k_quant. One block of
+// 1024 threads per row: the activation's long dependent chains get the whole SM to overlap.
+template <int ACT>
+__global__ void __launch_bounds__(1024) k_quant_gated(const float* gate, const float* up, int ld, int N, int act,
+                                                      int8_t* q, int ldq, float* qs) {
+  extern __shared__ float4 qrow4[];
+  float* row = reinterpret_cast<float*>(qrow4);
+  __shared__ float red[33];
+  const int r = blockIdx.x;
+  const float* gs = gate + (uint64_t)r * ld;
+  const float* us = up + (uint64_t)r * ld;
+  float amax = 0.0f;
+  for (int j = threadIdx.x; j < N; j += blockDim.x) {
+    float a;
+    if constexpr (ACT == 4) a = silu_f(gs[j]);
+    else if constexpr (ACT == 3) a = gelu_f(gs[j]);
+    else a = act_fn(gs[j], act);
+    const float v = ftz(fmul(ftz(a), us[j]));
+    row[j] = v;
+    amax = fmax_c(amax, fabs_c(v));
+  }
+  amax = block_max(amax, red);
+  const float inv = fmul(127.0f, recip_f(amax));
+  for (int j = threadIdx.x; j < N; j += blockDim.x) q[(uint64_t)r * ldq + j] = q8(row[j], inv);
+  if (threadIdx.x == 0) qs[r] = ftz(fmul(amax, bf(0x3C010204u)));
+}
+
 // ------------------------------------------------------------------------------- GEMV
 // y[m][col] over the concatenated output columns of up to kMaxSegs weight blocks. Epilogue per
 // output: y = fmul(fmul(i2f(acc), srow[m]), scale[n]) (golden.py:336-344), then by mode:
@@ -571,6 +601,21 @@ cudaError_t eng_quant(const float* x, int ldx, int N, int8_t* q, int ldq, float*
   }
   k_quant<<<rows, 256, smem, st>>>(x, ldx, N, q, ldq, qs);
   return cudaGetLastError();
+}
+cudaError_t eng_quant_gated(const float* gate, const float* up, int ld, int N, int act, int8_t* q, int ldq, float* qs,
+                            int rows, cudaStream_t st) {
+  const int smem = N * 4;
+  auto go = [&](auto kern) {
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+    }
+    kern<<<rows, 1024, smem, st>>>(gate, up, ld, N, act, q, ldq, qs);
+    return cudaGetLastError();
+  };
+  if (act == 4) return go(k_quant_gated<4>);
+  if (act == 3) return go(k_quant_gated<3>);
+  return go(k_quant_gated<-1>);
 }
 template <int MB, int KU>
 static cudaError_t gemv_mk(const EngGemvArgs& g, cudaStream_t st) {

@@ -16,11 +16,12 @@
 //   persistent  CTAs loop over tiles; two TMEM accumulators, so the epilogue of one tile overlaps
 //               the loads and MMAs of the next
 //   split-K     few tiles: the K slices of one tile are shared by the `split` CTAs of a thread-
-//               block cluster. Each CTA writes its partial tile to its own shared memory and frees
-//               its TMEM; after a cluster barrier CTA r sums rows [r*128/split, (r+1)*128/split)
-//               over all peers through distributed shared memory and runs the epilogue for them.
-//               No global workspace, so concurrent launches never share state, and no CTA holds
-//               TMEM while it waits on another CTA.
+//               block cluster. CTA r owns rows [r*128/split, (r+1)*128/split) of the tile; every
+//               CTA pushes each owner its partial rows with st.async into a slot of the owner's
+//               shared memory (completing on the owner's mbarrier), frees its TMEM, waits for its
+//               own slots, sums them and runs the epilogue for its rows. No global workspace, so
+//               concurrent launches never share state, and no CTA holds TMEM while it waits on
+//               another CTA.
 // Two accumulators per tile: the gated MLP (gate rows -> acc 0, up rows -> acc 1 from one staged
 // token slice) and the K-split linear (first K block -> acc 0, second -> acc 1).
 #include <cuda.h>
@@ -47,7 +48,7 @@ constexpr int kSlice = 128;         // K bytes per stage (one swizzle row)
 constexpr int kEpiWarps = 8;                // two per TMEM lane quarter, alternating 16-column chunks
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxStages = 8;
-constexpr int kSmemBudget = 200 * 1024;
+constexpr int kSmemBudget = 176 * 1024;
 constexpr int kSmemPerSM = 228 * 1024;     // shared memory of one SM (1 KB of it reserved per CTA)
 constexpr int kSMs = 148;
 
@@ -61,7 +62,8 @@ struct MmaMaps {
 // epilogue, epilogue done, exit. Off unless enabled; it changes no work.
 constexpr int kTraceCtas = 2048, kTraceStamps = 8;
 __device__ unsigned long long g_mma_trace[kTraceCtas * kTraceStamps];
-std::atomic<int> g_trace_on{0};
+std::atomic<int> g_trace_on{0};     // 0 off, n > 0: trace the n-th tensor-core launch from now on
+std::atomic<int> g_trace_count{0};
 
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
@@ -134,30 +136,30 @@ struct EngEpi {
   }
   __device__ __forceinline__ float tok(int m) const { return g.srow[m]; }
 
-  template <int ACT>
-  __device__ __forceinline__ void gated16(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[16],
-                                          const uint32_t (&v1)[16]) const {
-    float y[16];
+  template <int ACT, int N>
+  __device__ __forceinline__ void gated(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[N],
+                                        const uint32_t (&v1)[N]) const {
+    float y[N];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < N; ++j) {
       const float yg = ep_fast((int)v0[j], tk[j], r.s0);
       const float yu = ep_fast((int)v1[j], tk[j], r.s1);
       y[j] = ftz(fmul(ftz(act_static<ACT>(yg, g.act)), yu));
     }
-    store16(r, m0, mc, y);
+    store<N>(r, m0, mc, y);
   }
-  template <bool RES, bool KSPLIT>
-  __device__ __forceinline__ void plain16(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[16],
-                                          const uint32_t (&v1)[16], bool two) const {
-    float y[16];
-    float pre[16];
+  template <bool RES, bool KSPLIT, int N>
+  __device__ __forceinline__ void plain(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[N],
+                                        const uint32_t (&v1)[N], bool two) const {
+    float y[N];
+    float pre[N];
     if constexpr (RES) {
       const float* rp = g.res + r.col;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) pre[j] = rp[(uint64_t)(m0 + min(j, mc - 1)) * g.ldres];
+      for (int j = 0; j < N; ++j) pre[j] = rp[(uint64_t)(m0 + min(j, mc - 1)) * g.ldres];
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < N; ++j) {
       const int a0 = (int)v0[j], a1 = two ? (int)v1[j] : 0;
       float v;
       if constexpr (KSPLIT) v = fadd(ftz(ep_fast(a0, tk[j], r.s0)), ftz(ep_fast(a1, tk[j], r.s0)));
@@ -165,27 +167,30 @@ struct EngEpi {
       if constexpr (RES) v = fadd(pre[j], v);
       y[j] = ftz(v);
     }
-    store16(r, m0, mc, y);
+    store<N>(r, m0, mc, y);
   }
-  __device__ __forceinline__ void store16(const Row& r, int m0, int mc, const float (&y)[16]) const {
+  template <int N>
+  __device__ __forceinline__ void store(const Row& r, int m0, int mc, const float (&y)[N]) const {
     float* o = r.out + (uint64_t)m0 * r.ldo;
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
+    for (int j = 0; j < N; ++j)
       if (j < mc) o[(uint64_t)j * r.ldo] = y[j];
   }
-  __device__ __forceinline__ void put16(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[16],
-                                        const uint32_t (&v1)[16], bool two) const {
+  // N consecutive tokens m0.. (mc of them real) of one weight row
+  template <int N>
+  __device__ __forceinline__ void put(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[N],
+                                      const uint32_t (&v1)[N], bool two) const {
     if (mc <= 0) return;
     if (g.mode == kEpiGated) {
-      if (g.act == 4) gated16<4>(r, tk, m0, mc, v0, v1);
-      else if (g.act == 3) gated16<3>(r, tk, m0, mc, v0, v1);
-      else gated16<-1>(r, tk, m0, mc, v0, v1);
+      if (g.act == 4) gated<4, N>(r, tk, m0, mc, v0, v1);
+      else if (g.act == 3) gated<3, N>(r, tk, m0, mc, v0, v1);
+      else gated<-1, N>(r, tk, m0, mc, v0, v1);
     } else if (g.mode == kEpiKSplit) {
-      if (g.res) plain16<true, true>(r, tk, m0, mc, v0, v1, two);
-      else plain16<false, true>(r, tk, m0, mc, v0, v1, two);
+      if (g.res) plain<true, true, N>(r, tk, m0, mc, v0, v1, two);
+      else plain<false, true, N>(r, tk, m0, mc, v0, v1, two);
     } else {
-      if (g.res) plain16<true, false>(r, tk, m0, mc, v0, v1, two);
-      else plain16<false, false>(r, tk, m0, mc, v0, v1, two);
+      if (g.res) plain<true, false, N>(r, tk, m0, mc, v0, v1, two);
+      else plain<false, false, N>(r, tk, m0, mc, v0, v1, two);
     }
   }
 };
@@ -206,13 +211,13 @@ struct MachEpi {
   }
   __device__ __forceinline__ float tok(int m) const { return g.srow ? ld_f32(g.srow + 4 * (uint64_t)m) : 1.0f; }
 
-  template <int ACT, int OUT>
-  __device__ __forceinline__ void run16(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[16],
-                                        const uint32_t (&v1)[16], bool two) const {
+  template <int ACT, int OUT, int N>
+  __device__ __forceinline__ void run(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[N],
+                                      const uint32_t (&v1)[N], bool two) const {
     const bool srow = g.srow != nullptr, bias = g.bias != nullptr;
-    uint32_t bits[16];
+    uint32_t bits[N];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < N; ++j) {
       float y = i2f((int)v0[j] + (two ? (int)v1[j] : 0));
       const float ys = fmul_ff(y, tk[j]);
       y = srow ? ys : y;
@@ -227,7 +232,7 @@ struct MachEpi {
     }
     uint8_t* yrow = g.Y + (uint64_t)m0 * g.ldy;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < N; ++j) {
       if (j < mc) {
         uint8_t* p = yrow + (uint64_t)j * g.ldy;
         if constexpr (OUT == 0) st_u32(p + 4 * (uint64_t)r.n, bits[j]);
@@ -236,21 +241,24 @@ struct MachEpi {
       }
     }
   }
-  template <int ACT>
-  __device__ __forceinline__ void run_act(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[16],
-                                          const uint32_t (&v1)[16], bool two) const {
+  template <int ACT, int N>
+  __device__ __forceinline__ void run_act(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[N],
+                                          const uint32_t (&v1)[N], bool two) const {
     switch (g.out) {
-      case 0: run16<ACT, 0>(r, tk, m0, mc, v0, v1, two); break;
-      case 1: run16<ACT, 1>(r, tk, m0, mc, v0, v1, two); break;
-      case 2: run16<ACT, 2>(r, tk, m0, mc, v0, v1, two); break;
-      default: run16<ACT, 3>(r, tk, m0, mc, v0, v1, two); break;
+      case 0: run<ACT, 0, N>(r, tk, m0, mc, v0, v1, two); break;
+      case 1: run<ACT, 1, N>(r, tk, m0, mc, v0, v1, two); break;
+      case 2: run<ACT, 2, N>(r, tk, m0, mc, v0, v1, two); break;
+      default: run<ACT, 3, N>(r, tk, m0, mc, v0, v1, two); break;
     }
   }
-  __device__ __forceinline__ void put16(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[16],
-                                        const uint32_t (&v1)[16], bool two) const {
+  template <int N>
+  __device__ __forceinline__ void put(const Row& r, const float* tk, int m0, int mc, const uint32_t (&v0)[N],
+                                      const uint32_t (&v1)[N], bool two) const {
     if (mc <= 0) return;
-    if (g.act <= 2) run_act<0>(r, tk, m0, mc, v0, v1, two);
-    else run_act<-1>(r, tk, m0, mc, v0, v1, two);
+    if (g.act <= 2) run_act<0, N>(r, tk, m0, mc, v0, v1, two);
+    else if (g.act == 4 && g.out == 0) run<4, 0, N>(r, tk, m0, mc, v0, v1, two);    // prefill's SiLU gate
+    else if (g.act == 3 && g.out == 0) run<3, 0, N>(r, tk, m0, mc, v0, v1, two);    // and GELU gate
+    else run_act<-1, N>(r, tk, m0, mc, v0, v1, two);
   }
 };
 
@@ -260,7 +268,7 @@ template <class Epi>
 __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ MmaMaps maps, const MmaShape sh,
                                                         const Epi epi) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_full[kMaxStages], bar_empty[kMaxStages], bar_accf[2], bar_acce[2];
+  __shared__ uint64_t bar_full[kMaxStages], bar_empty[kMaxStages], bar_accf[2], bar_acce[2], bar_recv;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ float s_tok[2][256];             // the tile's token factors (double buffered per tile)
@@ -318,6 +326,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
       mbar_init(&bar_acce[i], kEpiWarps);
     }
     s_abort = 0;
+    if (split > 1) {
+      // the owner's slots receive (split - 1) peers' partial rows
+      mbar_init(&bar_recv, 1);
+      mbar_expect_tx(&bar_recv, (uint32_t)((split - 1) * (kRows / split) * NT * 4 * nacc));
+    }
     mbar_fence_init();
     tma_prefetch_desc(&maps.x);
   }
@@ -326,6 +339,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
+  // split-K: the barriers of every CTA are initialised before any peer pushes into them
+  if (split > 1) cluster_arrive_relaxed();
+  const int RL = NT + 4;                         // slot row: NT int32 + 16 bytes of padding
+  int* R = reinterpret_cast<int*>(smem + S * stage_bytes);   // slots [acc][sender][row][RL]
   if (threadIdx.x == 0) stamp(1);
 
   if (warp == 0) {
@@ -426,6 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
     const int et = threadIdx.x - 64;             // 0..255
     const uint32_t tlane = tmem + ((uint32_t)(ew * 32) << 16);
     int t = 0;
+    bool waited = false;
     for (int item = item0; item < sh.items; item += istride, ++t) {
       const int buf = sh.nbuf == 2 ? (t & 1) : 0;
       const uint32_t use = sh.nbuf == 2 ? (t >> 1) : t;
@@ -443,17 +461,70 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
       tc_fence_after();
       const uint32_t tb = tlane + buf * acc_cols;
       if (split > 1) {
-        // the partial tile to shared memory: P[a][token][row]
-        int* P = reinterpret_cast<int*>(smem);
+        // push this CTA's partial rows to their owners (16 tokens of one row per 4 st.async)
+        cluster_wait();
+        waited = true;
+        const int rs = kRows / split, owner = r / rs, rl = r % rs;
+        const uint32_t slot = smem_u32(R) + (uint32_t)(((crank * rs + rl) * RL) * 4);
+        const uint32_t accb = (uint32_t)(split * rs * RL * 4);
+        const uint32_t rbar = cluster_map(smem_u32(&bar_recv), owner);
         for (int j0 = 16 * half; j0 < NT; j0 += 32) {
-          uint32_t v0[16], v1[16];
-          tmem_ld16(tb + j0, v0);
-          if (nacc == 2) tmem_ld16(tb + NT + j0, v1);
+          uint32_t v[2][16];
+          tmem_ld16(tb + j0, v[0]);
+          if (nacc == 2) tmem_ld16(tb + NT + j0, v[1]);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            P[(j0 + j) * kRows + r] = used0 ? (int)v0[j] : 0;
-            if (nacc == 2) P[(NT + j0 + j) * kRows + r] = used1 ? (int)v1[j] : 0;
+          for (int a = 0; a < 2; ++a) {
+            if (a >= nacc) break;
+            const bool used = a == 0 ? used0 : used1;
+            const uint32_t dst = slot + a * accb + (uint32_t)j0 * 4;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t x0 = used ? v[a][4 * q] : 0u, x1 = used ? v[a][4 * q + 1] : 0u;
+              const uint32_t x2 = used ? v[a][4 * q + 2] : 0u, x3 = used ? v[a][4 * q + 3] : 0u;
+              if (owner == crank) {
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst + 16 * q), "r"(x0), "r"(x1),
+                             "r"(x2), "r"(x3)
+                             : "memory");
+              } else {
+                st_async_v4(cluster_map(dst + 16 * q, owner), x0, x1, x2, x3, rbar);
+              }
+            }
+          }
+        }
+        // TMEM is read: hand it back (warp 1 frees it) before waiting on the peers
+        tc_fence_before();
+        asm volatile("bar.arrive 2, %0;" ::"n"(32 + 32 * kEpiWarps) : "memory");
+        const bool got = mbar_wait(&bar_recv, 0, sh.err, 5);
+        if (epi_sync_or(!got)) {
+          s_abort = 1;
+          break;
+        }
+        // sum the slots of this CTA's rows and run the epilogue: one row x 4 tokens per unit, so
+        // every epilogue thread has work and a few short chains to interleave
+        const int units = rs * (NT / 4);
+        for (int u = et; u < units; u += 32 * kEpiWarps) {
+          const int url = u % rs, uj0 = 4 * (u / rs);
+          const int cc = row0 + crank * rs + url;
+          uint32_t a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+          for (int p = 0; p < split; ++p) {
+            const int* src = R + (p * rs + url) * RL + uj0;
+            const int4 x = *reinterpret_cast<const int4*>(src);
+            a0[0] += x.x;
+            a0[1] += x.y;
+            a0[2] += x.z;
+            a0[3] += x.w;
+            if (nacc == 2) {
+              const int4 y = *reinterpret_cast<const int4*>(src + split * rs * RL);
+              a1[0] += y.x;
+              a1[1] += y.y;
+              a1[2] += y.z;
+              a1[3] += y.w;
+            }
+          }
+          if (cc < sh.nrow[s]) {
+            const typename Epi::Row rw2 = epi.row(s, cc);
+            epi.template put<4>(rw2, tk + uj0, tok0 + uj0, min(4, sh.M - tok0 - uj0), a0, a1, nacc == 2);
           }
         }
         break;                                   // one tile per CTA in this mode
@@ -473,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
           __syncwarp();
           if (lane == 0) mbar_arrive(&bar_acce[buf]);
         }
-        if (live) epi.put16(rw, tk + j0, tok0 + j0, min(16, sh.M - tok0 - j0), v0, v1, nacc == 2);
+        if (live) epi.template put<16>(rw, tk + j0, tok0 + j0, min(16, sh.M - tok0 - j0), v0, v1, nacc == 2);
       }
       if (NT <= 16 * half && sh.nbuf == 2) {     // no chunk for this warp: release at once
         tc_fence_before();
@@ -481,49 +552,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
         if (lane == 0) mbar_arrive(&bar_acce[buf]);
       }
     }
+    if (split > 1 && !waited) {                  // aborted before the push: keep the barriers paired
+      cluster_wait();
+      asm volatile("bar.arrive 2, %0;" ::"n"(32 + 32 * kEpiWarps) : "memory");
+    }
   }
 
   __syncwarp();                              // lanes 1-31 of warps 0 / 1 wait for their lane 0
   if (threadIdx.x == 64) stamp(6);
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, ncols);
-  if (split == 1) {
+  if (split > 1 && warp < 2) cluster_wait();
+  if (split > 1) {
+    // warp 1 frees TMEM once the epilogue warps have read it (named barrier 2), not at the end
+    if (warp == 1) {
+      asm volatile("bar.sync 2, %0;" ::"n"(32 + 32 * kEpiWarps) : "memory");
+      tc_fence_after();
+      tmem_dealloc(tmem, ncols);
+    }
     if (threadIdx.x == 0) stamp(7);
     return;
   }
-
-  // split-K: sum the peers' partial tiles for this CTA's rows, then the epilogue (16 tokens of one
-  // row per thread and pass; s_tok[0] holds the tile's token factors)
-  cluster_sync();
-  {
-    int s, row0, tok0;
-    coords(item0, s, row0, tok0);
-    const int rs = kRows / split, r0 = crank * rs, ng = kThreads / rs;
-    const int rr = r0 + threadIdx.x % rs, jg = threadIdx.x / rs;
-    const int c = row0 + rr;
-    const bool live = !aborted(&s_abort) && c < sh.nrow[s];
-    const uint32_t p0 = smem_u32(smem) + (uint32_t)rr * 4;
-    typename Epi::Row rw{};
-    if (live) rw = epi.row(s, c);
-    for (int j0 = 16 * jg; j0 < NT; j0 += 16 * ng) {
-      uint32_t a0[16], a1[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        a0[j] = 0;
-        a1[j] = 0;
-      }
-      for (int p = 0; p < split; ++p) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          a0[j] += (uint32_t)dsmem_ld_s32(p0 + (uint32_t)((j0 + j) * kRows) * 4, p);
-          if (nacc == 2) a1[j] += (uint32_t)dsmem_ld_s32(p0 + (uint32_t)((NT + j0 + j) * kRows) * 4, p);
-        }
-      }
-      if (live) epi.put16(rw, s_tok[0] + j0, tok0 + j0, min(16, sh.M - tok0 - j0), a0, a1, nacc == 2);
-    }
-  }
-  cluster_sync();      // peers have read this CTA's partials
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, ncols);
   if (threadIdx.x == 0) stamp(7);
 }
 
@@ -568,22 +618,33 @@ int* err_flag() {
 bool plan(MmaShape& sh, int tiles, int* smem, int* grid) {
   sh.NT = std::min(256, (sh.M + 15) / 16 * 16);
   int ntt = (sh.M + sh.NT - 1) / sh.NT;
+  // too few tiles for the SMs: narrower token tiles first (their weight tiles are shared through
+  // L2), then split-K over a cluster
+  while (tiles * ntt < kSMs && sh.NT > 16) {
+    sh.NT = std::max(16, (sh.NT / 2 + 15) / 16 * 16);
+    ntt = (sh.M + sh.NT - 1) / sh.NT;
+  }
   const int nkb = sh.nkb1 + sh.nkb2;
   int split = 1;
-  while (split < 8 && tiles * ntt * split * 2 <= 2 * kSMs && nkb >= split * 4) split *= 2;
+  if (tiles * ntt < kSMs / 2)
+    while (split < 8 && tiles * ntt * split * 2 <= kSMs && nkb >= split * 4) split *= 2;   // one wave
   sh.split = split;
   sh.nbuf = split > 1 ? 1 : 2;
-  // the partial tile (split-K) or both accumulators (persistent) must fit
-  if ((split > 1 && sh.nacc * sh.NT * kRows * 4 > kSmemBudget) || sh.nbuf * sh.nacc * sh.NT > 512) sh.NT = 128;
+  // the slots (split-K) with a stage, or both accumulators (persistent), must fit
+  const int na0 = sh.gated ? 2 : 1;
+  auto slots = [&](int nt) { return sh.nacc * kRows * (nt + 4) * 4; };
+  if ((split > 1 && slots(sh.NT) + na0 * kRows * kSlice + sh.NT * kSlice > kSmemBudget) ||
+      sh.nbuf * sh.nacc * sh.NT > 512)
+    sh.NT = std::min(sh.NT, 128);
   sh.ntt = (sh.M + sh.NT - 1) / sh.NT;
   sh.items = tiles * sh.ntt;
   const int per = (nkb + split - 1) / split;
   const int na = sh.gated ? 2 : 1;
   const int stage = na * kRows * kSlice + sh.NT * kSlice;
-  sh.stages = std::max(1, std::min(kMaxStages, kSmemBudget / stage));
+  const int part = split > 1 ? slots(sh.NT) : 0;
+  sh.stages = std::max(1, std::min(kMaxStages, (kSmemBudget - part) / stage));
   if (split > 1) sh.stages = std::min(sh.stages, per);
-  const int part = split > 1 ? sh.nacc * sh.NT * kRows * 4 : 0;
-  *smem = std::max(sh.stages * stage, part) + 1024;
+  *smem = sh.stages * stage + part + 1024;
   // CTAs that share an SM must fit in its 512 TMEM columns together, so a CTA never waits in
   // tcgen05.alloc
   int ncols = 32;
@@ -592,7 +653,8 @@ bool plan(MmaShape& sh, int tiles, int* smem, int* grid) {
   *smem = std::max(*smem, kSmemPerSM / (max_res + 1) + 64 - 1024);
   const int res = std::max(1, std::min(max_res, kSmemPerSM / (*smem + 1024 + 256)));
   *grid = split > 1 ? sh.items * split : std::min(sh.items, kSMs * res);
-  sh.trace = g_trace_on.load();
+  const int want = g_trace_on.load();
+  sh.trace = want > 0 && g_trace_count.fetch_add(1) + 1 == want;
   sh.err = err_flag();
   return sh.err != nullptr;
 }
@@ -701,13 +763,14 @@ int mma_error_code() {
 }  // namespace tc
 
 extern "C" int tc_mma_trace(int32_t enable, uint64_t* out, uint32_t cap) {
-  if (enable && !tc::g_trace_on.load()) {
+  if (enable > 0) {
     void* a = nullptr;
     if (cudaGetSymbolAddress(&a, tc::g_mma_trace) != cudaSuccess ||
         cudaMemset(a, 0, sizeof(tc::g_mma_trace)) != cudaSuccess)
       return TC_ERR_CUDA;
   }
-  tc::g_trace_on.store(enable ? 1 : 0);
+  tc::g_trace_on.store(enable > 0 ? enable : 0);
+  tc::g_trace_count.store(0);
   if (!out || !cap) return 0;
   const uint32_t n = std::min<uint32_t>(cap, tc::kTraceCtas * tc::kTraceStamps);
   if (cudaDeviceSynchronize() != cudaSuccess) return TC_ERR_CUDA;
