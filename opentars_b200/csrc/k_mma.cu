@@ -48,7 +48,7 @@ constexpr int kSlice = 128;         // K bytes per stage (one swizzle row)
 constexpr int kEpiWarps = 8;                // two per TMEM lane quarter, alternating 16-column chunks
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxStages = 8;
-constexpr int kSmemBudget = 176 * 1024;
+constexpr int kSmemBudget = 144 * 1024;
 constexpr int kSmemPerSM = 228 * 1024;     // shared memory of one SM (1 KB of it reserved per CTA)
 constexpr int kSMs = 148;
 
