@@ -51,7 +51,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
-// 2-D tiled TMA load into this CTA's shared memory, completing on `bar` (no multicast).
+// 2-D tiled TMA load into this CTA's own shared memory only, completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -60,7 +60,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
       : "memory");
 }
 // 1-D bulk copy global -> this CTA's shared memory (16-byte aligned, size a multiple of 16),
-// completing on `bar` (no multicast).
+// completing on `bar`; the destination is this CTA's own shared memory only.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    smem_u32(dst)),
