@@ -529,8 +529,9 @@ template <int HD>
 static cudaError_t attention_hd(const AttnArgs& a, int batch, cudaStream_t st) {
   const int R = (a.nh / a.nkv) * a.n;
   const int fixed = (R * HD + R * kT) * 4;
-  const int budget = 200 * 1024 - fixed;                  // shared memory left for a K / V tile
-  const int tile = std::min(kT, budget / ((HD + 4) * 4)) / 16 * 16;
+  // K / V tiles of about 40 KB: several blocks share an SM (all (sequence, kv head) blocks of a
+  // batch of 64 in one wave) instead of one block streaming all keys at once
+  const int tile = std::min(kT, (40 * 1024) / ((HD + 4) * 4)) / 16 * 16;
   if (tile < 16) return cudaErrorInvalidValue;
   const int smem = fixed + tile * (HD + 4) * 4;
   cudaError_t e = cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
