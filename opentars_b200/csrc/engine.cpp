@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -16,12 +17,20 @@
 #include "../../include/tarscuda.h"
 #include "../../include/tarscuda_engine.h"
 #include "engine.h"
+#include "pdl.cuh"
 #include "mma.h"
 
 using namespace tc;
 
 struct tc_machine;
 extern "C" uint64_t tc_device_ptr(tc_machine* m);
+
+namespace tc {
+bool& pdl_launches() {
+  static thread_local bool on = false;
+  return on;
+}
+}  // namespace tc
 
 namespace {
 struct Lin { const int8_t* W; const float* s; int n, k; };
@@ -340,7 +349,13 @@ int tc_engine_step(tc_engine* e, const int32_t* tokens_host, int32_t n) {
   if (!e->graph[slot]) {
     cudaGraph_t graph;
     TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeRelaxed));
+    // programmatic dependent launch between the step's kernels when its GEMMs run on the tensor
+    // cores (measured: neutral to slightly faster there, slower for the GEMV path at batch 1);
+    // TARSCUDA_PDL=0 turns it off
+    const char* pdl = getenv("TARSCUDA_PDL");
+    pdl_launches() = !(pdl && pdl[0] == '0') && e->B * n >= mma_min_rows();
     const int rc = enqueue_step(e, n, src);
+    pdl_launches() = false;
     cudaError_t c = cudaStreamEndCapture(e->st, &graph);
     if (rc != TC_OK) return rc;
     if (c != cudaSuccess) return fail(e, "end capture", c);

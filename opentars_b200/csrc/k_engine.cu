@@ -14,6 +14,8 @@
 #include "engine.h"
 #include "mma.h"
 #include "fp32.cuh"
+#include "umma.cuh"
+#include "pdl.cuh"
 
 namespace tc {
 namespace {
@@ -63,6 +65,8 @@ __device__ __forceinline__ float block_sum16(const float* v, int N, float* red) 
 // ------------------------------------------------------------------------------- embedding
 // x[r] = E[tok[r]] (Gemma: times fp32(sqrt(H)) in IEEE fp32, as the host's numpy does), llm.py:198-204
 __global__ void k_embed(const float* E, const int* tok, float* x, int H, int scale_on, float scale, int rows) {
+  griddep_launch();
+  griddep_wait();
   const int r = blockIdx.x;
   if (r >= rows) return;
   const float* e = E + (uint64_t)tok[r] * H;
@@ -76,6 +80,8 @@ __global__ void k_embed(const float* E, const int* tok, float* x, int H, int sca
 //   mode 2: x = fadd(res, rmsnorm(in, pre_gamma)), written   (Gemma 3: attn_norm / mlp_norm)
 // Outputs the int8 row and its row scale (llm.py:97-104, numerics.py:353-390).
 __global__ void __launch_bounds__(256) k_norm_quant(NormQuantArgs a) {
+  griddep_launch();
+  griddep_wait();
   extern __shared__ float sm[];
   float* sx = sm;
   float* sv = sm + a.H;
@@ -120,51 +126,64 @@ __global__ void __launch_bounds__(256) k_norm_quant(NormQuantArgs a) {
 }
 
 // ROW_QUANT alone (attention output, gate * up), numerics.py:383-390
-__global__ void __launch_bounds__(256) k_quant(const float* x, int ldx, int N, int8_t* q, int ldq, float* qs) {
+// Row quantisation with a row spread over a cluster of kQCluster CTAs (every SM busy at batch
+// 64): CTA c takes a contiguous quarter of the row (for the gated MLP computing its elements
+// v = ftz(fmul(ftz(act(gate)), up)) first), the CTAs exchange their partial absmax through
+// distributed shared memory (max is order-free), then each quantises its slice.
+constexpr int kQCluster = 4;
+template <int ACT, bool GATED>
+__global__ void __launch_bounds__(256) k_quant_cl(const float* x, const float* up, int ld, int N, int act, int8_t* q,
+                                                  int ldq, float* qs) {
+  griddep_launch();
+  griddep_wait();
   extern __shared__ float4 qrow4[];
   float* row = reinterpret_cast<float*>(qrow4);
   __shared__ float red[33];
-  const int r = blockIdx.x;
-  const float* src = x + (uint64_t)r * ldx;
-  for (int j4 = threadIdx.x; j4 < N / 4; j4 += blockDim.x) cp16(row + 4 * j4, src + 4 * j4);
-  cp_wait_all();
-  __syncthreads();
+  __shared__ float s_part;
+  const int r = blockIdx.x / kQCluster, c = (int)cluster_rank();
+  const int S = ((N + kQCluster - 1) / kQCluster + 3) / 4 * 4;
+  const int j0 = min(N, c * S), j1 = min(N, j0 + S);
+  const float* src = x + (uint64_t)r * ld;
   float amax = 0.0f;
-  for (int j = threadIdx.x; j < N; j += blockDim.x) amax = fmax_c(amax, fabs_c(row[j]));
-  amax = block_max(amax, red);
-  const float inv = fmul(127.0f, recip_f(amax));
-  for (int j = threadIdx.x; j < N; j += blockDim.x) q[(uint64_t)r * ldq + j] = q8(row[j], inv);
-  if (threadIdx.x == 0) qs[r] = ftz(fmul(amax, bf(0x3C010204u)));
-}
-
-// The gated MLP's product and its row quantisation in one pass (llm.py's act(gate) * up, then
-// ROW_QUANT): gate and up hold the two GEMMs' fp32 outputs (no activation applied). Per element
-// v = ftz(fmul(ftz(act(gate)), up)) - the bits the gated GEMM epilogue (act, store) and ELT_MUL
-// (fmul, store) produce - then the row's absmax and the int8 codes as in k_quant. One block of
-// 1024 threads per row: the activation's long dependent chains get the whole SM to overlap.
-template <int ACT>
-__global__ void __launch_bounds__(1024) k_quant_gated(const float* gate, const float* up, int ld, int N, int act,
-                                                      int8_t* q, int ldq, float* qs) {
-  extern __shared__ float4 qrow4[];
-  float* row = reinterpret_cast<float*>(qrow4);
-  __shared__ float red[33];
-  const int r = blockIdx.x;
-  const float* gs = gate + (uint64_t)r * ld;
-  const float* us = up + (uint64_t)r * ld;
-  float amax = 0.0f;
-  for (int j = threadIdx.x; j < N; j += blockDim.x) {
-    float a;
-    if constexpr (ACT == 4) a = silu_f(gs[j]);
-    else if constexpr (ACT == 3) a = gelu_f(gs[j]);
-    else a = act_fn(gs[j], act);
-    const float v = ftz(fmul(ftz(a), us[j]));
-    row[j] = v;
-    amax = fmax_c(amax, fabs_c(v));
+  if constexpr (GATED) {
+    const float* us = up + (uint64_t)r * ld;
+    for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
+      float a;
+      if constexpr (ACT == 4) a = silu_f(src[j]);
+      else if constexpr (ACT == 3) a = gelu_f(src[j]);
+      else a = act_fn(src[j], act);
+      const float v = ftz(fmul(ftz(a), us[j]));
+      row[j - j0] = v;
+      amax = fmax_c(amax, fabs_c(v));
+    }
+  } else {
+    for (int j4 = j0 / 4 + threadIdx.x; j4 < j1 / 4; j4 += blockDim.x) cp16(row + 4 * j4 - j0, src + 4 * j4);
+    cp_wait_all();
+    __syncthreads();
+    for (int j = threadIdx.x; j < j1 - j0; j += blockDim.x) amax = fmax_c(amax, fabs_c(row[j]));
   }
   amax = block_max(amax, red);
+  if (threadIdx.x == 0) s_part = amax;
+  cluster_sync();
+  amax = s_part;
+  for (int p = 0; p < kQCluster; ++p)
+    if (p != c) amax = fmax_c(amax, __int_as_float(dsmem_ld_s32(smem_u32(&s_part), p)));
   const float inv = fmul(127.0f, recip_f(amax));
-  for (int j = threadIdx.x; j < N; j += blockDim.x) q[(uint64_t)r * ldq + j] = q8(row[j], inv);
-  if (threadIdx.x == 0) qs[r] = ftz(fmul(amax, bf(0x3C010204u)));
+  for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) q[(uint64_t)r * ldq + j] = q8(row[j - j0], inv);
+  if (c == 0 && threadIdx.x == 0) qs[r] = ftz(fmul(amax, bf(0x3C010204u)));
+  cluster_sync();                                 // the peers have read s_part
+}
+
+template <class Kern>
+static cudaError_t launch_quant_cl(Kern kern, const float* x, const float* up, int ld, int N, int act, int8_t* q,
+                                   int ldq, float* qs, int rows, cudaStream_t st) {
+  const int S = ((N + kQCluster - 1) / kQCluster + 3) / 4 * 4;
+  const int smem = S * 4;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_ex(kern, dim3(rows * kQCluster), dim3(256), smem, st, kQCluster, x, up, ld, N, act, q, ldq, qs);
 }
 
 // ------------------------------------------------------------------------------- GEMV
@@ -183,6 +202,8 @@ __global__ void __launch_bounds__(256) k_eng_gemv(EngGemvArgs g) {
   const int nw = gridDim.x * 8;
   const int ncols = g.mode == kEpiGated ? g.seg[0].n : g.ncols;
   const int kv = g.K / 16;
+  griddep_launch();
+  griddep_wait();
   for (int i = threadIdx.x; i < mb * kv; i += blockDim.x) {
     const int m = i / kv, kk = (i - m * kv) * 16;
     cp16(&sA[m * 512 * KU + kk], g.A + (uint64_t)(m0 + m) * g.lda + kk);
@@ -276,6 +297,8 @@ __global__ void __launch_bounds__(256) k_eng_gemv(EngGemvArgs g) {
 // Same segments and epilogue modes as k_eng_gemv.
 template <int KU>
 __global__ void __launch_bounds__(128) k_eng_gemm_tl(EngGemvArgs g) {
+  griddep_launch();
+  griddep_wait();
   extern __shared__ __align__(16) int8_t sAt[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * 32;
@@ -354,6 +377,8 @@ __global__ void __launch_bounds__(128) k_eng_gemm_tl(EngGemvArgs g) {
 // table row of the token's position (llm.py:718-734, numerics.py:353-358, 412-424). q -> qr;
 // k -> the K cache row of (sequence, position). One half-warp per (row, head).
 __global__ void __launch_bounds__(128) k_qk_rope(QkRopeArgs a) {
+  griddep_launch();
+  griddep_wait();
   const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
   const int heads = a.nh + a.nkv;
   const int item = blockIdx.x * 8 + hw;
@@ -409,6 +434,8 @@ constexpr int kMaxRows = 16;                 // G * n query rows per block
 // at the same column, and the padding puts each 16-byte access of a phase in its own bank group.
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a, int tile) {
+  griddep_launch();
+  griddep_wait();
   constexpr int LD = HD + 4;
   extern __shared__ float4 smem4[];
   const int n = a.n, G = a.nh / a.nkv, R = G * n;
@@ -536,13 +563,14 @@ static cudaError_t attention_hd(const AttnArgs& a, int batch, cudaStream_t st) {
   const int smem = fixed + tile * (HD + 4) * 4;
   cudaError_t e = cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  k_attention<HD><<<batch * a.nkv, kAttnThreads, smem, st>>>(a, tile);
-  return cudaGetLastError();
+  return launch_ex(k_attention<HD>, dim3(batch * a.nkv), dim3(kAttnThreads), smem, st, 1, a, tile);
 }
 
 // ------------------------------------------------------------------------------- greedy pick
 // np.argmax of each sequence's logits: the first maximum; the first NaN wins over numbers.
 __global__ void __launch_bounds__(1024) k_argmax(const float* logits, int vocab, int* tok_out, int tok_stride) {
+  griddep_launch();
+  griddep_wait();
   const int b = blockIdx.x;
   const float* row = logits + (uint64_t)b * vocab;
   float best = 0.0f;
@@ -576,13 +604,17 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* logits, int vocab,
   if (threadIdx.x == 0) tok_out[b * tok_stride] = si[0];
 }
 
-__global__ void k_advance(int* pos, int n) { *pos += n; }
+__global__ void k_advance(int* pos, int n) {
+  griddep_wait();
+  *pos += n;
+}
 
 }  // namespace
 
 // --------------------------------------------------------------------------------- launchers
 cudaError_t eng_embed(const float* E, const int* tok, float* x, int H, int scale_on, float scale, int rows, cudaStream_t st) {
-  k_embed<<<rows, 256, 0, st>>>(E, tok, x, H, scale_on, scale, rows);
+  cudaError_t e = launch_ex(k_embed, dim3(rows), dim3(256), 0, st, 1, E, tok, x, H, scale_on, scale, rows);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 cudaError_t eng_norm_quant(const NormQuantArgs& a, cudaStream_t st) {
@@ -591,38 +623,26 @@ cudaError_t eng_norm_quant(const NormQuantArgs& a, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(k_norm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
   }
-  k_norm_quant<<<a.rows, 256, smem, st>>>(a);
+  cudaError_t e2 = launch_ex(k_norm_quant, dim3(a.rows), dim3(256), smem, st, 1, a);
+  if (e2 != cudaSuccess) return e2;
   return cudaGetLastError();
 }
 cudaError_t eng_quant(const float* x, int ldx, int N, int8_t* q, int ldq, float* qs, int rows, cudaStream_t st) {
-  const int smem = N * 4;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(k_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-  }
-  k_quant<<<rows, 256, smem, st>>>(x, ldx, N, q, ldq, qs);
-  return cudaGetLastError();
+  if (N % 4 || ldx % 4 || (uintptr_t)x % 16) return cudaErrorInvalidValue;
+  return launch_quant_cl(k_quant_cl<0, false>, x, nullptr, ldx, N, 0, q, ldq, qs, rows, st);
 }
 cudaError_t eng_quant_gated(const float* gate, const float* up, int ld, int N, int act, int8_t* q, int ldq, float* qs,
                             int rows, cudaStream_t st) {
-  const int smem = N * 4;
-  auto go = [&](auto kern) {
-    if (smem > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return e;
-    }
-    kern<<<rows, 1024, smem, st>>>(gate, up, ld, N, act, q, ldq, qs);
-    return cudaGetLastError();
-  };
-  if (act == 4) return go(k_quant_gated<4>);
-  if (act == 3) return go(k_quant_gated<3>);
-  return go(k_quant_gated<-1>);
+  if (act == 4) return launch_quant_cl(k_quant_cl<4, true>, gate, up, ld, N, act, q, ldq, qs, rows, st);
+  if (act == 3) return launch_quant_cl(k_quant_cl<3, true>, gate, up, ld, N, act, q, ldq, qs, rows, st);
+  return launch_quant_cl(k_quant_cl<-1, true>, gate, up, ld, N, act, q, ldq, qs, rows, st);
 }
 template <int MB, int KU>
 static cudaError_t gemv_mk(const EngGemvArgs& g, cudaStream_t st) {
   const int ncols = g.mode == kEpiGated ? g.seg[0].n : g.ncols;
   const int blocks = std::min((ncols + 7) / 8, 148 * 4);
-  k_eng_gemv<MB, KU><<<dim3(blocks, (g.M + MB - 1) / MB), 256, 0, st>>>(g);
+  cudaError_t e = launch_ex(k_eng_gemv<MB, KU>, dim3(blocks, (g.M + MB - 1) / MB), dim3(256), 0, st, 1, g);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 template <int MB>
@@ -641,7 +661,8 @@ static cudaError_t gemm_tl(const EngGemvArgs& g, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   const int yb = (g.M + 31) / 32;
   const int blocks = std::min((ncols + 3) / 4, std::max(1, 148 * 8 / yb));
-  k_eng_gemm_tl<KU><<<dim3(blocks, yb), 128, smem, st>>>(g);
+  e = launch_ex(k_eng_gemm_tl<KU>, dim3(blocks, yb), dim3(128), smem, st, 1, g);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -661,7 +682,8 @@ cudaError_t eng_gemv(const EngGemvArgs& g, cudaStream_t st) {
 }
 cudaError_t eng_qk_rope(const QkRopeArgs& a, cudaStream_t st) {
   const int items = a.rows * (a.nh + a.nkv);
-  k_qk_rope<<<(items + 7) / 8, 128, 0, st>>>(a);
+  cudaError_t e = launch_ex(k_qk_rope, dim3((items + 7) / 8), dim3(128), 0, st, 1, a);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 cudaError_t eng_attention(const AttnArgs& a, int batch, cudaStream_t st) {
@@ -675,11 +697,13 @@ cudaError_t eng_attention(const AttnArgs& a, int batch, cudaStream_t st) {
   }
 }
 cudaError_t eng_argmax(const float* logits, int vocab, int batch, int* tok_out, int tok_stride, cudaStream_t st) {
-  k_argmax<<<batch, 1024, 0, st>>>(logits, vocab, tok_out, tok_stride);
+  cudaError_t e = launch_ex(k_argmax, dim3(batch), dim3(1024), 0, st, 1, logits, vocab, tok_out, tok_stride);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 cudaError_t eng_advance(int* pos, int n, cudaStream_t st) {
-  k_advance<<<1, 1, 0, st>>>(pos, n);
+  cudaError_t e = launch_ex(k_advance, dim3(1), dim3(1), 0, st, 1, pos, n);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -39,6 +39,7 @@
 #include "mma.h"
 #include "ops.h"
 #include "umma.cuh"
+#include "pdl.cuh"
 
 namespace tc {
 
@@ -333,6 +334,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
     }
     mbar_fence_init();
     tma_prefetch_desc(&maps.x);
+    for (int i = 0; i < 2 * sh.nseg; ++i) tma_prefetch_desc(&maps.w[i]);   // descriptors used by this launch
+    if (sh.gated) tma_prefetch_desc(&maps.w[2]);
   }
   if (warp == 1) tmem_alloc(&s_tmem, ncols);
   tc_fence_before();
@@ -348,6 +351,33 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
   if (warp == 0) {
     if (lane == 0 && nk > 0) {
       // producer: K slice q (counted over all items of this CTA) into stage q % S
+      auto load_w = [&](int st, int s, int row0, int k) {   // the weight box(es) of K slice k
+        uint8_t* sa = smem + st * stage_bytes;
+        if (sh.gated) {
+          tma_load_2d(sa, &maps.w[0], k * kSlice, row0, &bar_full[st]);
+          tma_load_2d(sa + a_bytes, &maps.w[2], k * kSlice, row0, &bar_full[st]);
+        } else if (k < sh.nkb1) {
+          tma_load_2d(sa, &maps.w[2 * s], k * kSlice, row0, &bar_full[st]);
+        } else {
+          tma_load_2d(sa, &maps.w[2 * s + 1], (k - sh.nkb1) * kSlice, row0, &bar_full[st]);
+        }
+      };
+      auto load_x = [&](int st, int tok0, int k) {           // the token box of K slice k
+        const int xk = k < sh.nkb1 || sh.gated ? k * kSlice : sh.kb + (k - sh.nkb1) * kSlice;
+        tma_load_2d(smem + st * stage_bytes + na * a_bytes, &maps.x, xk, tok0, &bar_full[st]);
+      };
+      // the weights do not depend on the previous kernel: the first stages' weight boxes are
+      // in flight before the wait for its outputs (programmatic dependent launch)
+      const int pre = min(S, nk);
+      {
+        int s, row0, tok0;
+        coords(item0, s, row0, tok0);
+        for (int i = 0; i < pre; ++i) {
+          mbar_expect_tx(&bar_full[i], stage_bytes);
+          load_w(i, s, row0, k_lo + i);
+        }
+      }
+      griddep_wait();
       uint32_t q = 0;
       bool stop = false;
       for (int item = item0; item < sh.items && !stop; item += istride) {
@@ -355,7 +385,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
         coords(item, s, row0, tok0);
         for (int i = 0; i < nk; ++i, ++q) {
           const int st = q % S;
-          if (q >= (uint32_t)S && !mbar_wait(&bar_empty[st], ((q / S) & 1) ^ 1, sh.err, 1)) {
+          const int k = k_lo + i;
+          if (q < (uint32_t)pre) {
+            load_x(st, tok0, k);
+            if (q == 0) stamp(2);
+            continue;
+          }
+          if (!mbar_wait(&bar_empty[st], ((q / S) & 1) ^ 1, sh.err, 1)) {
             s_abort = 1;
             stop = true;
             break;
@@ -364,23 +400,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
             stop = true;
             break;
           }
-          uint8_t* sa = smem + st * stage_bytes;
-          const int k = k_lo + i;
-          int xk;
           mbar_expect_tx(&bar_full[st], stage_bytes);
-          if (sh.gated) {
-            tma_load_2d(sa, &maps.w[0], k * kSlice, row0, &bar_full[st]);
-            tma_load_2d(sa + a_bytes, &maps.w[2], k * kSlice, row0, &bar_full[st]);
-            xk = k * kSlice;
-          } else if (k < sh.nkb1) {
-            tma_load_2d(sa, &maps.w[2 * s], k * kSlice, row0, &bar_full[st]);
-            xk = k * kSlice;
-          } else {
-            tma_load_2d(sa, &maps.w[2 * s + 1], (k - sh.nkb1) * kSlice, row0, &bar_full[st]);
-            xk = sh.kb + (k - sh.nkb1) * kSlice;
-          }
-          tma_load_2d(sa + na * a_bytes, &maps.x, xk, tok0, &bar_full[st]);
-          if (q == 0) stamp(2);
+          load_w(st, s, row0, k);
+          load_x(st, tok0, k);
         }
       }
       if (stop) {   // wait (bounded) for the copies still in flight before the CTA ends
@@ -442,6 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
     const int r = ew * 32 + lane;
     const int et = threadIdx.x - 64;             // 0..255
     const uint32_t tlane = tmem + ((uint32_t)(ew * 32) << 16);
+    griddep_wait();                              // token factors and residuals come from predecessors
     int t = 0;
     bool waited = false;
     for (int item = item0; item < sh.items; item += istride, ++t) {
@@ -663,19 +686,7 @@ template <class Epi>
 cudaError_t launch(const MmaMaps& maps, const MmaShape& sh, const Epi& epi, int grid, int smem, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(k_mma_i8<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = sh.split;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = sh.split > 1 ? 1 : 0;       // a plain launch without split-K
-  return cudaLaunchKernelEx(&cfg, k_mma_i8<Epi>, maps, sh, epi);
+  return launch_ex(k_mma_i8<Epi>, dim3(grid), dim3(kThreads), smem, st, sh.split, maps, sh, epi);
 }
 }  // namespace
 

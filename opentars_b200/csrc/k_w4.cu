@@ -174,7 +174,7 @@ __device__ __forceinline__ int group_dot(WordOf word, ChunkOf chunk, int qsum) {
 // packed weights of its groups (lane, lane + 32) for this column and the next one in registers.
 template <int MB>
 __global__ void __launch_bounds__(kThreads) k_gemv_w4(W4Args g, bool vec) {
-  extern __shared__ __align__(16) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   uint32_t* sX = reinterpret_cast<uint32_t*>(smem);                                 // [MB][K] fp32 bits
   int16_t* sQ = reinterpret_cast<int16_t*>(smem + (size_t)MB * g.K * 4);             // [MB][64][kQStride]
   uint32_t* sS = reinterpret_cast<uint32_t*>(smem + (size_t)MB * g.K * 4 + (size_t)MB * 64 * kQStride * 2);
