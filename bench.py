@@ -821,8 +821,11 @@ def run_decode(a, world, rank, local) -> dict | None:
     peak = peaks.get("hbm_gbs", 6650.0)
     g = kinds["gemv"]
     achieved = g[2] / (g[1] / 1e3) / 1e9
+    tfile = ROOT / "profiles" / "traffic_decode.json"
+    traffic = json.loads(tfile.read_text()).get("bytes_per_step") if tfile.exists() and a.workload == "decode" else None
     roofline = dict(bound="hbm", achieved=round(achieved, 1), peak=peak, unit="GB/s", frac=round(achieved / peak, 4),
-                    traffic=None, kernel="k_eng_gemv (W8A8 GEMV, all linears and the head)",
+                    traffic=traffic, traffic_unit="DRAM bytes per step of the GEMM launches (ncu, B=64)",
+                    kernel="k_mma_i8 (tcgen05 W8A8 GEMM; k_eng_gemv below 16 rows): all linears and the head",
                     kernel_bytes_per_step=g[2], kernel_launches_per_step=g[0], kernel_ms_per_step=round(g[1], 4),
                     peak_source="measured" if peaks else "fallback",
                     step_breakdown_ms={k: round(v[1], 4) for k, v in kinds.items()})
