@@ -467,13 +467,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
     griddep_wait();                              // token factors and residuals come from predecessors
     int t = 0;
     bool waited = false;
+    // the next tile's token factor (one per thread: NT <= 256 epilogue threads) and weight-row
+    // constants are loaded while this tile is written out, so their latency is hidden
+    float tk_next = 0.0f;
+    typename Epi::Row rw_next{};
+    bool live_next = false;
     for (int item = item0; item < sh.items; item += istride, ++t) {
       const int buf = sh.nbuf == 2 ? (t & 1) : 0;
       const uint32_t use = sh.nbuf == 2 ? (t >> 1) : t;
       int s, row0, tok0;
       coords(item, s, row0, tok0);
       float* tk = s_tok[t & 1];
-      for (int j = et; j < NT; j += 32 * kEpiWarps) tk[j] = ftz(epi.tok(min(tok0 + j, sh.M - 1)));
+      if (t == 0) {
+        for (int j = et; j < NT; j += 32 * kEpiWarps) tk[j] = ftz(epi.tok(min(tok0 + j, sh.M - 1)));
+      } else if (et < NT) {
+        tk[et] = tk_next;
+      }
       if (epi_sync_or(aborted(&s_abort))) break;
       bool ok = true;
       if (nk > 0) {
@@ -553,9 +562,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
         break;                                   // one tile per CTA in this mode
       }
       const int c = row0 + r;
-      const bool live = ok && c < sh.nrow[s];
       typename Epi::Row rw{};
-      if (live) rw = epi.row(s, c);
+      bool live;
+      if (t == 0) {
+        live = c < sh.nrow[s];
+        if (live) rw = epi.row(s, c);
+      } else {
+        live = live_next;
+        rw = rw_next;
+      }
+      live = live && ok;
+      if (item + istride < sh.items) {           // prefetch for the next tile
+        int s2, row2, tok2;
+        coords(item + istride, s2, row2, tok2);
+        if (et < NT) tk_next = ftz(epi.tok(min(tok2 + et, sh.M - 1)));
+        live_next = row2 + r < sh.nrow[s2];
+        if (live_next) rw_next = epi.row(s2, row2 + r);
+      }
       const int last = (NT - 16 - 16 * half) / 32 * 32 + 16 * half;   // this warp's last chunk
       for (int j0 = 16 * half; j0 < NT; j0 += 32) {
         uint32_t v0[16], v1[16];
