@@ -83,7 +83,8 @@ def build_gemv(R: int, seed: int, M: int = 1, K: int = 1024, N: int = 3072):
     gemm_bytes = N * K + 4 * N + M * K + 4 * M + 4 * M * N          # 3,171,332 at config 0
     quant_bytes = 4 * M * K + M * K + 4 * M
     return dict(ddr=ddr, qa=qa, qlen=2 * R, units=R, unit_bytes=gemm_bytes + quant_bytes,
-                kernel_bytes=gemm_bytes, kernel_desc=lambda i: i % 2 == 1, kernel="k_gemv_i8 (W8A8 GEMV)",
+                kernel_bytes=R * gemm_bytes, roof=(2, lambda i: i == 1),
+                kernel=f"k_gemv8_group (W8A8 GEMV, {R} units in one launch)",
                 inputs=(x0, R * 4 * M * K), outputs=(y0, R * 4 * M * N),
                 config=dict(workload="config0_w8a8_gemv", M=M, K=K, N=N, units_per_step=R,
                             weights_bytes_per_step=R * N * K,
@@ -111,7 +112,7 @@ def build_w4(R: int, seed: int, M: int = 1, K: int = 8192, N: int = 16384):
                   Y_OFF=y0 + r * 4 * M * N, M=M, N=N, K=K, GROUP_SIZE=128)
         ddr[qa + 64 * r:qa + 64 * (r + 1)] = np.frombuffer(d, np.uint8)
     unit = N * K // 2 + 2 * N * G + 4 * M * K + 4 * M * N               # 69,304,320 here
-    return dict(ddr=ddr, qa=qa, qlen=R, units=R, unit_bytes=unit, kernel_bytes=unit, kernel_desc=lambda i: True,
+    return dict(ddr=ddr, qa=qa, qlen=R, units=R, unit_bytes=unit, kernel_bytes=unit, roof=(1, lambda i: True),
                 kernel="k_gemv_w4 (W4A16 GEMV)", inputs=(x0, R * 4 * M * K), outputs=(y0, R * 4 * M * N),
                 config=dict(workload="config2_w4a16_gemv", M=M, K=K, N=N, units_per_step=R,
                             weights_bytes_per_step=R * N * K // 2,
@@ -251,6 +252,7 @@ def run_ours(a, world, rank, local) -> dict | None:
     dev.to_dev(0, len(ddr))
     g, st = dev.graph(p["qa"], p["qlen"])
     assert g is not None and st.done, "the benchmark queue must capture"
+    kernels_per_step = check(L.tc_graph_kernels(g), dev.h, "graph_kernels")
     stream = torch.cuda.ExternalStream(L.tc_stream(dev.h), device=local)
 
     # parity spot check: unit 0 against the oracle happens after timing (rank 0)
@@ -271,10 +273,13 @@ def run_ours(a, world, rank, local) -> dict | None:
     total_bytes = world * R * p["unit_bytes"] * a.steps
     value = total_bytes / (ms_max / 1e3) / 1e9
 
-    # roofline: per-descriptor device times from a graph captured with events between descriptors
+    # roofline: device times of the dominant kernel from a graph captured with events between
+    # dependency levels (config 0: level 1 is the one grouped GEMV launch of all R units) or
+    # between descriptors (config 2: each W4A16 GEMV alone)
     from opentars_b200._lib import Status_t
+    mode, pick = p["roof"]
     st2, cop, gt = Status_t(), ctypes.c_int32(-1), ctypes.c_void_p()
-    check(L.tc_queue_capture(dev.h, p["qa"], p["qlen"], 0, 0, 1, ctypes.byref(st2), ctypes.byref(cop),
+    check(L.tc_queue_capture(dev.h, p["qa"], p["qlen"], 0, 0, mode, ctypes.byref(st2), ctypes.byref(cop),
                              ctypes.byref(gt)), dev.h)
     kt = []
     for _ in range(3):
@@ -282,9 +287,9 @@ def run_ours(a, world, rank, local) -> dict | None:
         check(L.tc_synchronize(dev.h), dev.h)
         arr = (ctypes.c_float * p["qlen"])()
         n = check(L.tc_graph_times(gt, arr, p["qlen"]), dev.h, "graph_times")
-        kt += [arr[i] for i in range(n) if p["kernel_desc"](i)]
+        kt += [arr[i] for i in range(n) if pick(i)]
     if not kt:
-        raise RuntimeError("no per-descriptor timings")
+        raise RuntimeError("no kernel timings")
     L.tc_graph_destroy(gt)
     k_ms = statistics.mean(kt)
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
@@ -338,7 +343,7 @@ def run_ours(a, world, rank, local) -> dict | None:
         "data": "synthetic, seeded (BASELINE config distributions)",
         "config": dict(p["config"], parallelism=f"replicas x{world} (independent GEMV batches per GPU)"),
         "roofline": roofline, "e2e": e2e,
-        "gpu_launches": a.steps * p["qlen"], "clocks": clk.summary(), "bit_exact_unit0": bit_exact,
+        "gpu_launches": a.steps * kernels_per_step, "clocks": clk.summary(), "bit_exact_unit0": bit_exact,
     }
     if world == 1 and not a.no_cpu:
         cb = cpu_oracle_gbs(a.workload, a.cpu_seconds, os.cpu_count() or 1)
@@ -519,6 +524,7 @@ def run_gemm(a, world, rank, local) -> dict | None:
     ok = dev.run(p["q_setup"], p["n_setup"])[0]
     g, st = dev.graph(p["q_main"], p["n_main"])
     assert ok and g is not None and st.done, "the GEMM queue must capture"
+    kernels_per_step = check(L.tc_graph_kernels(g), dev.h, "graph_kernels")
     stream = torch.cuda.ExternalStream(L.tc_stream(dev.h), device=local)
     y0, yn = p["y_region"]
     base = int(L.tc_device_ptr(dev.h))
@@ -634,7 +640,7 @@ def run_gemm(a, world, rank, local) -> dict | None:
                        descriptors_per_step=p["n_main"],
                        parallelism=f"N split over {world} GPUs + NCCL all-gather of the outputs" if world > 1
                        else "1 GPU", l2="weights (170 MB per step) larger than L2, streamed once per step"),
-        "roofline": roofline, "e2e": e2e, "gpu_launches": a.steps * p["n_main"], "clocks": clk.summary(),
+        "roofline": roofline, "e2e": e2e, "gpu_launches": a.steps * kernels_per_step, "clocks": clk.summary(),
         "bit_exact_vs_reference": bit_exact,
     }
     if world == 1 and not a.no_cpu:

@@ -74,8 +74,12 @@ uint32_t tc_stats(tc_machine* m, tc_opstat* out, uint32_t cap);
 /* Checks a queue exactly as tc_run_queue does and captures its kernels as one CUDA graph without
  * running them; *st is the status the run would end with. The board runtime runs one fixed queue
  * per position (tars_board.py:316-329, llm.py:548-571), so a queue is checked once and replayed.
- * timing != 0 records an event between descriptors (tc_graph_times). A queue whose descriptors
- * rewrite later descriptors of the same queue is refused (TC_ERR_ARG). */
+ * timing == 0: the graph of dependency levels (independent descriptors of a level run side by
+ * side; decode GEMVs of one kernel class and row ops of a level are batched into one launch each);
+ * timing == 1: the descriptors one after another with an event between them (tc_graph_times gives
+ * per-descriptor times); timing == 2: the level graph with an event between levels (per-level
+ * times). A queue whose descriptors rewrite later descriptors of the same queue is refused
+ * (TC_ERR_ARG). */
 int tc_queue_capture(tc_machine* m, uint64_t queue_addr, uint32_t queue_len, int32_t core_id,
                      int32_t gemv_only, int32_t timing, tc_status* st, int32_t* contract_op,
                      tc_graph** out);
@@ -85,6 +89,10 @@ int tc_graph_launch(tc_graph* g, void* stream);
 /* Per-descriptor milliseconds of the last launch of a graph captured with timing; returns the count. */
 int tc_graph_times(tc_graph* g, float* ms, uint32_t cap);
 int tc_graph_destroy(tc_graph* g);
+/* Kernel launches one replay of the graph makes (the capture batches independent GEMVs and row ops
+ * of a dependency level into one launch, so this is usually below the descriptor count). No
+ * reference counterpart: the reference executes descriptors one at a time. */
+int tc_graph_kernels(tc_graph* g);
 /* Waits for everything enqueued on the machine's stream. */
 int tc_synchronize(tc_machine* m);
 

@@ -54,6 +54,7 @@ SIGNATURES = {
     "tc_graph_launch": (ctypes.c_int, [P, VP]),
     "tc_graph_times": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_float), ctypes.c_uint32]),
     "tc_graph_destroy": (ctypes.c_int, [P]),
+    "tc_graph_kernels": (ctypes.c_int, [P]),
     "tc_synchronize": (ctypes.c_int, [P]),
     "tc_set_mma_min_rows": (ctypes.c_int, [ctypes.c_int32]),
     "tc_mma_trace": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint64), ctypes.c_uint32]),

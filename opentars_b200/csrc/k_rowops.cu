@@ -121,12 +121,11 @@ __device__ __forceinline__ float block_sum16(const float* v, int N, float* red) 
 
 // One block per row: the row (flushed) is staged in shared memory with 16-byte loads when
 // aligned; elementwise work is spread over the block, the ordered sums run on 16 threads.
-__global__ void __launch_bounds__(kRT) k_rowop(RowArgs a) {
-  extern __shared__ float sm[];
+// `sm` holds 2 * a.N floats.
+__device__ __forceinline__ void rowop_body(const RowArgs& a, int m, float* sm, float* red) {
   float* sx = sm;                  // the row
   float* sv = sm + a.N;            // per-element terms (x*x, d*d, e)
-  __shared__ float red[kRT / 32 + 1];
-  const int m = blockIdx.x, N = a.N, t = threadIdx.x;
+  const int N = a.N, t = threadIdx.x;
   const uint8_t* x = a.X + (uint64_t)m * a.lda;
   uint8_t* y = a.Y + (uint64_t)m * a.ldy;
   if (((uintptr_t)x & 15) == 0) {
@@ -180,6 +179,28 @@ __global__ void __launch_bounds__(kRT) k_rowop(RowArgs a) {
     if (a.beta) o = fadd(o, ld_f32(a.beta + 4 * (uint64_t)j));
     store_out(y, j, o, a.out, a.out_scale);
   }
+}
+
+__global__ void __launch_bounds__(kRT) k_rowop(RowArgs a) {
+  extern __shared__ float sm[];
+  __shared__ float red[kRT / 32 + 1];
+  rowop_body(a, blockIdx.x, sm, red);
+}
+
+// Independent row ops of one dependency level in one launch: block b runs row b - row0[j] of
+// entry j, where row0[j] <= b < row0[j + 1] (a block-uniform search over at most kGroupMax
+// entries). Each row is computed exactly as k_rowop computes it.
+__global__ void __launch_bounds__(kRT) k_rowop_group(const __grid_constant__ RowGroup grp) {
+  extern __shared__ float sm[];
+  __shared__ float red[kRT / 32 + 1];
+  const int b = blockIdx.x;
+  int lo = 0, hi = grp.n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (grp.row0[mid] <= b) lo = mid;
+    else hi = mid - 1;
+  }
+  rowop_body(grp.a[lo], b - grp.row0[lo], sm, red);
 }
 
 __global__ void k_act(ActArgs a) {
@@ -290,6 +311,16 @@ cudaError_t launch_rowop(const RowArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
   }
   k_rowop<<<a.M, kRT, smem, st>>>(a);
+  return cudaGetLastError();
+}
+bool rowop_groupable(const RowArgs& a) { return a.N <= kRowSmem && a.M > 0; }
+cudaError_t launch_rowop_group(const RowGroup& g, cudaStream_t st) {
+  const int smem = 2 * g.nmax * 4;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_rowop_group, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * kRowSmem * 4);
+    if (e != cudaSuccess) return e;
+  }
+  k_rowop_group<<<g.row0[g.n], kRT, smem, st>>>(g);
   return cudaGetLastError();
 }
 cudaError_t launch_act(const ActArgs& a, cudaStream_t st) {

@@ -11,6 +11,8 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <functional>
+#include <memory>
 #include <string>
 #include <thread>
 #include <vector>
@@ -31,8 +33,7 @@ struct tc_machine {
   uint8_t* scratch = nullptr;
   uint64_t scratch_size = 0;
   std::string err;
-  cudaStream_t cur = nullptr;                          // the stream launch() enqueues on
-  std::vector<cudaStream_t> lanes;                     // extra capture streams (dependency graphs)
+  std::vector<cudaStream_t> lanes;                     // extra capture streams (one level's launches)
 };
 
 // A validated queue captured as one CUDA graph (tc_queue_capture).
@@ -43,6 +44,7 @@ struct tc_graph {
   std::vector<tc_opstat> stats;
   std::vector<std::pair<uint64_t, uint64_t>> written;
   tc_status status{};
+  int kernels = 0;                                     // kernel nodes of the graph
 };
 
 namespace {
@@ -73,9 +75,37 @@ cudaError_t ensure_scratch(tc_machine* m, uint64_t n) {
   return e;
 }
 
+// The kernel arguments of a W8A8 GEMM descriptor (A as the descriptor names it; a conv's gather
+// buffer replaces it at launch) and of a row-op descriptor.
+void gemm_args(tc_machine* mc, const Desc& d, GemmArgs* g) {
+  uint8_t* B = mc->dev + d[F_BASE_ADDR];
+  const Strides s = strides(d);
+  g->A = B + d[F_A_OFF]; g->lda = s.lda;
+  g->W = B + d[F_W_OFF]; g->scale = B + d[F_SCALE_OFF];
+  g->per_channel = d.qmode() != QM_TENSOR;
+  g->srow = (d.qmode() == QM_ROWCOL) ? mc->dev + d[F_BASE_ADDR] + 16 * d[F_HDR_RSV] : nullptr;
+  g->bias = d.bias() ? B + d[F_BIAS_OFF] : nullptr;
+  g->Y = B + d[F_Y_OFF]; g->ldy = s.ldy;
+  g->M = (int)d[F_M]; g->N = (int)d[F_N]; g->K = (int)d[F_K];
+  g->act = d.act(); g->out = d.out(); g->out_scale = f32(d[F_OUT_SCALE]);
+}
+void row_args(tc_machine* mc, const Desc& d, RowArgs* a) {
+  uint8_t* B = mc->dev + d[F_BASE_ADDR];
+  const Strides s = strides(d);
+  a->X = B + d[F_A_OFF]; a->lda = s.lda; a->Y = B + d[F_Y_OFF]; a->ldy = s.ldy;
+  a->fn = (int)(d[F_CTRL] & 7);
+  a->M = (int)d[F_M]; a->N = (int)d[F_N]; a->K = (int)d[F_K]; a->out = d.out(); a->out_scale = f32(d[F_OUT_SCALE]);
+  if (a->fn == ROW_QUANT) a->scale_out = B + d[F_SCALE_OFF];
+  if (a->fn == ROW_LAYERNORM || a->fn == ROW_RMSNORM || a->fn == ROW_L2NORM) {
+    a->gamma = B + d[F_SCALE_OFF];
+    a->beta = d.bias() ? B + d[F_BIAS_OFF] : nullptr;
+    a->eps = f32(d[F_W_OFF]);
+  }
+}
+
 // Enqueues the kernels of one validated, in-range descriptor.
 cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream);
-cudaError_t launch(tc_machine* mc, const Desc& d) { return launch_on(mc, d, mc->cur ? mc->cur : mc->stream); }
+cudaError_t launch(tc_machine* mc, const Desc& d) { return launch_on(mc, d, mc->stream); }
 
 cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream) {
   uint8_t* B = mc->dev + d[F_BASE_ADDR];
@@ -95,7 +125,7 @@ cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream) {
       return launch_gemm_w4a16(g, stream);
     }
     GemmArgs g{};
-    g.A = B + d[F_A_OFF]; g.lda = s.lda;
+    gemm_args(mc, d, &g);
     if (d.conv()) {
       const ConvGeom cg = conv_geom(d);
       const uint64_t need = d[F_M] * d[F_K];
@@ -109,13 +139,6 @@ cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream) {
       if (e != cudaSuccess) return e;
       g.A = mc->scratch; g.lda = d[F_K];
     }
-    g.W = B + d[F_W_OFF]; g.scale = B + d[F_SCALE_OFF];
-    g.per_channel = d.qmode() != QM_TENSOR;
-    g.srow = (d.qmode() == QM_ROWCOL) ? mc->dev + d[F_BASE_ADDR] + 16 * d[F_HDR_RSV] : nullptr;
-    g.bias = d.bias() ? B + d[F_BIAS_OFF] : nullptr;
-    g.Y = B + d[F_Y_OFF]; g.ldy = s.ldy;
-    g.M = (int)d[F_M]; g.N = (int)d[F_N]; g.K = (int)d[F_K];
-    g.act = d.act(); g.out = d.out(); g.out_scale = osc;
     return launch_gemm_w8a8(g, stream);
   }
   if (op == OP_RELU) {
@@ -126,15 +149,7 @@ cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream) {
   }
   if (op == OP_ROW) {
     RowArgs a{};
-    a.X = B + d[F_A_OFF]; a.lda = s.lda; a.Y = B + d[F_Y_OFF]; a.ldy = s.ldy;
-    a.fn = (int)(d[F_CTRL] & 7);
-    a.M = (int)d[F_M]; a.N = (int)d[F_N]; a.K = (int)d[F_K]; a.out = d.out(); a.out_scale = osc;
-    if (a.fn == ROW_QUANT) a.scale_out = B + d[F_SCALE_OFF];
-    if (a.fn == ROW_LAYERNORM || a.fn == ROW_RMSNORM || a.fn == ROW_L2NORM) {
-      a.gamma = B + d[F_SCALE_OFF];
-      a.beta = d.bias() ? B + d[F_BIAS_OFF] : nullptr;
-      a.eps = f32(d[F_W_OFF]);
-    }
+    row_args(mc, d, &a);
     return launch_rowop(a, stream);
   }
   if (op == OP_ELT) {
@@ -195,12 +210,13 @@ uint64_t read_bytes(const Footprint& fp) {
   return (uint64_t)s;
 }
 
-// The in-order loop shared by tc_run_queue and tc_queue_capture. `before(i)` runs before the
-// kernels of descriptor i are enqueued; `capturing` forbids host synchronisation (a queue that
-// rewrites its own later descriptors cannot be captured).
-template <class Before, class After>
+// The in-order loop shared by tc_run_queue and tc_queue_capture. `before(i)` runs before
+// `run(d)` enqueues (or records) the kernels of descriptor i; `capturing` forbids host
+// synchronisation (a queue that rewrites its own later descriptors cannot be captured).
+template <class Before, class After, class Run>
 int execute(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, int32_t gemv_only, tc_status* st,
-            int32_t* contract_op, const std::vector<uint8_t>& q0, bool capturing, Before before, After after) {
+            int32_t* contract_op, const std::vector<uint8_t>& q0, bool capturing, Before before, After after,
+            Run run) {
   std::vector<uint8_t> q = q0;
   const u128 size = m->size;
   auto fetch = [&](uint32_t from) -> cudaError_t {
@@ -236,7 +252,7 @@ int execute(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, int32
       break;
     }
     before(i, d, fp);
-    cudaError_t e = launch(m, d);
+    cudaError_t e = run(d);
     if (e != cudaSuccess) { rc = fail(m, "launch", e); break; }
     after(i);
     const int op = d.op();
@@ -283,15 +299,18 @@ uint64_t scratch_need(const std::vector<uint8_t>& q, uint32_t qlen, int core_id,
   }
   return need;
 }
-// Captures a queue as a graph whose edges are the queue's real hazards. Every descriptor's byte
-// footprint (bounding interval per input tensor and per output) is compared with those of the
-// earlier descriptors; a read-after-write, write-after-read or write-after-write overlap orders
-// the pair, anything else may run concurrently. Each descriptor goes on the capture stream of its
-// latest predecessor (so that edge is the stream order) and waits for its other predecessors'
-// events. The conv gather buffer counts as a written input of every conv. Independent work
-// commutes, so the bytes written are those of the in-order run.
+// Captures a queue as a graph of dependency levels. Every descriptor's byte footprint (bounding
+// interval per input tensor and per output) is compared with those of the earlier descriptors; a
+// read-after-write, write-after-read or write-after-write overlap orders the pair. A descriptor's
+// level is one more than the highest level among the earlier descriptors it overlaps, so the
+// descriptors of one level are pairwise independent and every hazard points to a lower level.
+// Each level runs after the previous one; inside a level the row ops, and (in a level of nothing
+// but GEMVs and row ops) the decode GEMVs of one kernel class, become one launch each (up to
+// kGroupMax entries), and the remaining descriptors and groups run side by side on the capture
+// streams. The conv gather buffer counts as a written
+// input of every conv. Independent work commutes, so the bytes written are those of the in-order
+// run.
 struct Iv { u128 lo, hi; };
-struct DagNode { std::vector<Iv> r, w; int lane; };
 
 bool hits(const std::vector<Iv>& a, const std::vector<Iv>& b) {
   for (const Iv& x : a)
@@ -300,8 +319,15 @@ bool hits(const std::vector<Iv>& a, const std::vector<Iv>& b) {
   return false;
 }
 
-int capture_dag(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, int32_t gemv_only, tc_status* st,
-                int32_t* contract_op, const std::vector<uint8_t>& q, std::vector<cudaEvent_t>& evs) {
+struct LevelNode {
+  Desc d;
+  std::vector<Iv> r, w;
+  int level;
+};
+
+int capture_grouped(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, int32_t gemv_only, tc_status* st,
+                    int32_t* contract_op, const std::vector<uint8_t>& q, std::vector<cudaEvent_t>& evs,
+                    std::vector<cudaEvent_t>* marks) {
   const int kLanes = 16;
   while ((int)m->lanes.size() < kLanes) {
     cudaStream_t s;
@@ -309,64 +335,134 @@ int capture_dag(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, i
     if (e != cudaSuccess) return fail(m, "capture streams", e);
     m->lanes.push_back(s);
   }
+  std::vector<LevelNode> nodes;
+  int top = -1;                                     // highest level so far
+  const u128 kScratch = ((u128)1) << 120;          // a key outside every image for the gather buffer
+  int rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, true,
+                   [&](uint32_t, const Desc& d, const Footprint& fp) {
+    LevelNode nd;
+    nd.d = d;
+    for (const auto& t : fp.reads)
+      for (const auto& sg : t) nd.r.push_back(Iv{sg.base, seg_end(sg)});
+    nd.w.push_back(Iv{fp.y.base, seg_end(fp.y)});
+    if (fp.has_extra) nd.w.push_back(Iv{fp.extra.base, seg_end(fp.extra)});
+    if (d.conv()) nd.w.push_back(Iv{kScratch, kScratch + 1});
+    int lvl = 0;
+    for (int k = (int)nodes.size() - 1; k >= 0 && lvl <= top; --k) {
+      const LevelNode& o = nodes[k];
+      if (o.level < lvl) continue;                  // cannot raise the level
+      if (hits(o.w, nd.r) || hits(o.w, nd.w) || hits(o.r, nd.w)) lvl = o.level + 1;
+    }
+    nd.level = lvl;
+    top = std::max(top, lvl);
+    nodes.push_back(std::move(nd));
+  }, [](uint32_t) {}, [](const Desc&) { return cudaSuccess; });
+  if (rc != TC_OK) return rc;
+
   auto new_event = [&]() {
     cudaEvent_t ev;
     cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
     evs.push_back(ev);
     return ev;
   };
-  // fork: every lane joins the capture after the origin stream's work so far
-  cudaEvent_t fork = new_event();
-  cudaEventRecord(fork, m->stream);
-  for (auto s : m->lanes) cudaStreamWaitEvent(s, fork, 0);
-  std::vector<DagNode> nodes;
-  std::vector<cudaEvent_t> done;
-  std::vector<int> lane_last(kLanes, -1);
-  int rr = 0;
-  const u128 kScratch = ((u128)1) << 120;          // a key outside every image for the gather buffer
-  int rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, true,
-                   [&](uint32_t, const Desc& d, const Footprint& fp) {
-    DagNode nd;
-    for (const auto& t : fp.reads)
-      for (const auto& sg : t) nd.r.push_back(Iv{sg.base, seg_end(sg)});
-    nd.w.push_back(Iv{fp.y.base, seg_end(fp.y)});
-    if (fp.has_extra) nd.w.push_back(Iv{fp.extra.base, seg_end(fp.extra)});
-    if (d.conv()) nd.w.push_back(Iv{kScratch, kScratch + 1});
-    std::vector<int> latest(kLanes, -1);
-    int pick = -1;
-    for (int k = (int)nodes.size() - 1; k >= 0; --k) {
-      const DagNode& o = nodes[k];
-      if (latest[o.lane] >= 0) continue;              // a later one on that lane already orders us
-      if (hits(o.w, nd.r) || hits(o.w, nd.w) || hits(o.r, nd.w)) {
-        latest[o.lane] = k;
-        if (pick < 0) pick = o.lane;                  // the most recent predecessor's lane
+  std::vector<std::vector<int>> levels(top + 1);
+  for (int i = 0; i < (int)nodes.size(); ++i) levels[nodes[i].level].push_back(i);
+  // marks: an external (timing) event before each level and one after the last
+  auto mark = [&]() {
+    if (!marks) return;
+    cudaEvent_t ev;
+    cudaEventCreate(&ev);
+    marks->push_back(ev);
+    cudaEventRecordWithFlags(ev, m->stream, cudaEventRecordExternal);
+  };
+  for (const auto& lv : levels) {
+    mark();
+    // the level's launch units: GEMV groups per class, row-op groups, single descriptors
+    std::vector<std::function<cudaError_t(cudaStream_t)>> units;
+    std::vector<std::pair<int, std::vector<GemmArgs>>> gemvs;   // class -> entries
+    std::vector<RowArgs> rows;
+    for (int i : lv) {
+      const Desc& d = nodes[i].d;
+      if (d.op() == OP_GEMM && !d.conv() && !d.w4()) {
+        GemmArgs g{};
+        gemm_args(m, d, &g);
+        const int cls = gemv8_class(g);
+        if (cls >= 0) {
+          auto it = std::find_if(gemvs.begin(), gemvs.end(), [&](const auto& c) { return c.first == cls; });
+          if (it == gemvs.end()) gemvs.push_back({cls, {g}});
+          else it->second.push_back(g);
+          continue;
+        }
+      } else if (d.op() == OP_ROW) {
+        RowArgs a{};
+        row_args(m, d, &a);
+        if (rowop_groupable(a)) {
+          rows.push_back(a);
+          continue;
+        }
+      }
+      units.push_back([m, d](cudaStream_t s) { return launch_on(m, d, s); });
+    }
+    // the streaming GEMV group fills every SM's shared memory; beside other work in the level (a
+    // tensor-core GEMM, a W4A16 GEMV, ...) the GEMVs run as launches of their own instead
+    const bool alone = units.empty();
+    for (size_t ci = 0; ci < gemvs.size(); ++ci) {
+      const int cls = gemvs[ci].first;
+      const auto& gs = gemvs[ci].second;
+      if (!alone) {
+        for (const GemmArgs& g : gs) units.push_back([g](cudaStream_t s) { return launch_gemm_w8a8(g, s); });
+        continue;
+      }
+      for (size_t j0 = 0; j0 < gs.size(); j0 += kGroupMax) {
+        const int n = (int)std::min<size_t>(kGroupMax, gs.size() - j0);
+        if (n == 1) {
+          const GemmArgs g = gs[j0];
+          units.push_back([g](cudaStream_t s) { return launch_gemm_w8a8(g, s); });
+          continue;
+        }
+        auto grp = std::make_shared<GemvGroup>();
+        grp->n = n; grp->mb = cls >> 4; grp->ku = cls & 15;
+        for (int j = 0; j < n; ++j) grp->g[j] = gs[j0 + j];
+        units.push_back([grp](cudaStream_t s) { return launch_gemv8_group(*grp, s); });
       }
     }
-    if (pick < 0) {                                   // independent: the least recently used lane
-      pick = rr;
-      rr = (rr + 1) % kLanes;
+    for (size_t j0 = 0; j0 < rows.size(); j0 += kGroupMax) {
+      const int n = (int)std::min<size_t>(kGroupMax, rows.size() - j0);
+      if (n == 1) {
+        const RowArgs a = rows[j0];
+        units.push_back([a](cudaStream_t s) { return launch_rowop(a, s); });
+        continue;
+      }
+      auto grp = std::make_shared<RowGroup>();
+      grp->n = n; grp->nmax = 0; grp->row0[0] = 0;
+      for (int j = 0; j < n; ++j) {
+        grp->a[j] = rows[j0 + j];
+        grp->nmax = std::max(grp->nmax, grp->a[j].N);
+        grp->row0[j + 1] = grp->row0[j] + grp->a[j].M;
+      }
+      units.push_back([grp](cudaStream_t s) { return launch_rowop_group(*grp, s); });
     }
-    for (int l = 0; l < kLanes; ++l)
-      if (l != pick && latest[l] >= 0) cudaStreamWaitEvent(m->lanes[pick], done[latest[l]], 0);
-    nd.lane = pick;
-    m->cur = m->lanes[pick];
-    nodes.push_back(std::move(nd));
-  }, [&](uint32_t) {
-    cudaEvent_t ev = new_event();
-    cudaEventRecord(ev, m->cur);                      // this descriptor's completion on its lane
-    done.push_back(ev);
-    lane_last[nodes.back().lane] = (int)done.size() - 1;
-  });
-  m->cur = nullptr;
-  // join: the origin stream waits for every lane's last descriptor
-  for (int l = 0; l < kLanes; ++l)
-    if (lane_last[l] >= 0) cudaStreamWaitEvent(m->stream, done[lane_last[l]], 0);
-    else {
-      cudaEvent_t ev = new_event();                   // an idle lane still has to rejoin
-      cudaEventRecord(ev, m->lanes[l]);
-      cudaStreamWaitEvent(m->stream, ev, 0);
+    if (units.size() == 1) {
+      cudaError_t e = units[0](m->stream);
+      if (e != cudaSuccess) return fail(m, "launch", e);
+      continue;
     }
-  (void)evs;
+    // fork: the lanes start after everything before this level; join: the next level waits for all
+    cudaEvent_t fork = new_event();
+    cudaEventRecord(fork, m->stream);
+    const int used = (int)std::min<size_t>(units.size(), kLanes);
+    for (int l = 0; l < used; ++l) cudaStreamWaitEvent(m->lanes[l], fork, 0);
+    for (size_t u = 0; u < units.size(); ++u) {
+      cudaError_t e = units[u](m->lanes[u % kLanes]);
+      if (e != cudaSuccess) return fail(m, "launch", e);
+    }
+    for (int l = 0; l < used; ++l) {
+      cudaEvent_t join = new_event();
+      cudaEventRecord(join, m->lanes[l]);
+      cudaStreamWaitEvent(m->stream, join, 0);
+    }
+  }
+  if (!levels.empty()) mark();
   return rc;
 }
 }  // namespace
@@ -385,7 +481,8 @@ int tc_run_queue(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, 
   cudaError_t e = fetch_queue(m, qaddr, qlen, q);
   if (e != cudaSuccess) return fail(m, "queue fetch", e);
   int rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, false,
-                   [](uint32_t, const Desc&, const Footprint&) {}, [](uint32_t) {});
+                   [](uint32_t, const Desc&, const Footprint&) {}, [](uint32_t) {},
+                   [m](const Desc& d) { return launch(m, d); });
   cudaError_t se = cudaStreamSynchronize(m->stream);
   if (se != cudaSuccess && rc >= 0) rc = fail(m, "queue run", se);
   return rc;
@@ -406,7 +503,7 @@ int tc_queue_capture(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_
   if (e != cudaSuccess) return fail(m, "capture setup", e);
   tc_graph* g = new tc_graph();
   g->m = m;
-  if (timing) {
+  if (timing == 1) {
     g->events.resize((size_t)qlen + 1);
     for (auto& ev : g->events) cudaEventCreate(&ev);
   }
@@ -415,20 +512,33 @@ int tc_queue_capture(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_
   uint32_t last = 0;
   int rc;
   std::vector<cudaEvent_t> dag_events;
-  if (timing) {
+  if (timing == 1) {
     rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, true,
                  [&](uint32_t i, const Desc&, const Footprint&) {
       // an external record node: a plain cudaEventRecord inside a capture only orders work
       cudaEventRecordWithFlags(g->events[i], m->stream, cudaEventRecordExternal);
       last = i + 1;
-    }, [](uint32_t) {});
+    }, [](uint32_t) {}, [m](const Desc& d) { return launch(m, d); });
     if (last) cudaEventRecordWithFlags(g->events[last], m->stream, cudaEventRecordExternal);
   } else {
-    rc = capture_dag(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, dag_events);
+    rc = capture_grouped(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, dag_events,
+                         timing == 2 ? &g->events : nullptr);
   }
   cudaGraph_t graph = nullptr;
   cudaError_t ce = cudaStreamEndCapture(m->stream, &graph);
   if (rc == TC_OK && ce != cudaSuccess) rc = fail(m, "end capture", ce);
+  if (rc == TC_OK) {
+    size_t nn = 0;
+    ce = cudaGraphGetNodes(graph, nullptr, &nn);
+    std::vector<cudaGraphNode_t> nodes(nn);
+    if (ce == cudaSuccess && nn) ce = cudaGraphGetNodes(graph, nodes.data(), &nn);
+    for (size_t k = 0; ce == cudaSuccess && k < nn; ++k) {
+      cudaGraphNodeType t;
+      ce = cudaGraphNodeGetType(nodes[k], &t);
+      if (ce == cudaSuccess && t == cudaGraphNodeTypeKernel) ++g->kernels;
+    }
+    if (ce != cudaSuccess) rc = fail(m, "graph nodes", ce);
+  }
   if (rc == TC_OK) {
     ce = cudaGraphInstantiate(&g->exec, graph, 0);
     if (ce != cudaSuccess) rc = fail(m, "instantiate", ce);
@@ -441,7 +551,7 @@ int tc_queue_capture(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_
     delete g;
     return rc;
   }
-  if (timing) g->events.resize(last + (last ? 1 : 0));
+  if (timing == 1) g->events.resize(last + (last ? 1 : 0));
   g->stats = m->stats;
   g->written = m->written;
   g->status = *st;
@@ -468,6 +578,8 @@ int tc_graph_times(tc_graph* g, float* ms, uint32_t cap) {
   }
   return (int)n;
 }
+
+int tc_graph_kernels(tc_graph* g) { return g ? g->kernels : TC_ERR_ARG; }
 
 int tc_graph_destroy(tc_graph* g) {
   if (!g) return TC_OK;

@@ -24,6 +24,24 @@ struct GemmArgs {
 };
 cudaError_t launch_gemm_w8a8(const GemmArgs& g, cudaStream_t st);
 
+// Independent descriptors of one dependency level batched into one launch (queue capture).
+// Every entry is computed exactly as its own launch would compute it.
+constexpr int kGroupMax = 64;
+
+// Decode GEMVs of one kernel class (token rows per pass MB, K <= 512 * KU), streamed in chunks of
+// 16 output columns: entry j owns chunks [c0[j], c0[j + 1]), ncx[j] = N / 16 chunks per pass of
+// MB token rows.
+struct GemvGroup {
+  int n, mb, ku;
+  int c0[kGroupMax + 1];
+  int ncx[kGroupMax];
+  GemmArgs g[kGroupMax];
+};
+// The class of a GEMM that the grouped decode GEMV computes (MB * 16 + KU), or -1.
+int gemv8_class(const GemmArgs& g);
+// Fills grp.c0 / grp.ncx and launches.
+cudaError_t launch_gemv8_group(GemvGroup& grp, cudaStream_t st);
+
 // W4A16 GEMM / GEMV, golden.py:295-324
 struct W4Args {
   const uint8_t* A;  uint64_t lda;   // fp32 or bf16 [M, K] rows
@@ -56,6 +74,16 @@ struct RowArgs {
   float eps, out_scale;
 };
 cudaError_t launch_rowop(const RowArgs& a, cudaStream_t st);
+
+// Row ops of one dependency level: entry j owns blocks (rows) [row0[j], row0[j + 1]); nmax is the
+// longest row (floats) of the group.
+struct RowGroup {
+  int n, nmax;
+  int row0[kGroupMax + 1];
+  RowArgs a[kGroupMax];
+};
+bool rowop_groupable(const RowArgs& a);
+cudaError_t launch_rowop_group(const RowGroup& g, cudaStream_t st);
 
 struct ActArgs {
   const uint8_t* X;  uint64_t lda;
