@@ -59,6 +59,9 @@ struct tc_engine {
   float* qs = nullptr;
   float *kc = nullptr, *vc = nullptr;        // [L][B][Tp][kvw]
   cudaGraphExec_t graph[5] = {};
+  // q / k norm + RoPE, attention and the output quantiser as one cluster launch
+  // (TARSCUDA_FUSE_ATTN=0: three launches, the same bits)
+  bool fuse_attn = true;
   std::string err;
   // profiling (tc_engine_profile): events around every kernel of one uncaptured step
   bool prof = false;
@@ -153,19 +156,23 @@ int enqueue_step(tc_engine* e, int n, const int* tok_in) {
       KERNEL(kKGemv, gemv_bytes(g), eng_gemv(g, st));
     }
     {
-      QkRopeArgs a{};
-      a.q = e->q; a.k = e->k; a.v = e->v; a.qr = e->qr; a.kc = kc; a.vc = vc; a.qn = L.qn; a.kn = L.kn;
-      a.tab = L.tab; a.pos = e->pos; a.rows = M; a.n = n; a.nh = md.n_heads; a.nkv = md.n_kv; a.hd = md.head_dim;
-      a.rot = md.rot; a.Tp = e->Tp; a.eps = eps;
-      KERNEL(kKQkRope, (uint64_t)M * (qw + 3 * kvw) * 8, eng_qk_rope(a, st));
-    }
-    {
+      QkRopeArgs r{};
+      r.q = e->q; r.k = e->k; r.v = e->v; r.qr = e->qr; r.kc = kc; r.vc = vc; r.qn = L.qn; r.kn = L.kn;
+      r.tab = L.tab; r.pos = e->pos; r.rows = M; r.n = n; r.nh = md.n_heads; r.nkv = md.n_kv; r.hd = md.head_dim;
+      r.rot = md.rot; r.Tp = e->Tp; r.eps = eps;
       AttnArgs a{};
       a.qr = e->qr; a.kc = kc; a.vc = vc; a.att = e->att; a.pos = e->pos; a.n = n; a.nh = md.n_heads;
       a.nkv = md.n_kv; a.hd = md.head_dim; a.Tp = e->Tp;
-      KERNEL(kKAttention, 0, eng_attention(a, B, st));
+      if (e->fuse_attn && md.n_kv <= 8) {
+        // q / k norm + RoPE, attention and the output quantiser in one cluster launch
+        const AttnQuantArgs f{r, e->q8, (uint64_t)ldq, e->qs};
+        KERNEL(kKAttention, (uint64_t)M * (qw + 3 * kvw) * 8, eng_attention_quant(a, f, B, st));
+      } else {
+        KERNEL(kKQkRope, (uint64_t)M * (qw + 3 * kvw) * 8, eng_qk_rope(r, st));
+        KERNEL(kKAttention, 0, eng_attention(a, B, st));
+        KERNEL(kKQuant, (uint64_t)M * qw * 5, eng_quant(e->att, qw, qw, e->q8, ldq, e->qs, M, st));
+      }
     }
-    KERNEL(kKQuant, (uint64_t)M * qw * 5, eng_quant(e->att, qw, qw, e->q8, ldq, e->qs, M, st));
     {  // o; Qwen3 adds the residual in the epilogue
       EngGemvArgs g = gemv_args(e->q8, ldq, e->qs, M, qw);
       add_seg(g, L.o, md.gemma ? e->o : e->x1, H);
@@ -252,6 +259,10 @@ int tc_engine_create(tc_machine* image, const tc_model_desc* md, const tc_layer_
                      int32_t batch, tc_engine** out) {
   *out = nullptr;
   tc_engine* e = new tc_engine();
+  {
+    const char* fa = getenv("TARSCUDA_FUSE_ATTN");
+    e->fuse_attn = !(fa && fa[0] == '0');
+  }
   e->md = *md;
   const uint8_t* base = (const uint8_t*)(uintptr_t)tc_device_ptr(image);
   e->B = batch;

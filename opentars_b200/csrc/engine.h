@@ -67,6 +67,16 @@ cudaError_t eng_quant_gated(const float* gate, const float* up, int ld, int N, i
 cudaError_t eng_gemv(const EngGemvArgs& g, cudaStream_t st);
 cudaError_t eng_qk_rope(const QkRopeArgs& a, cudaStream_t st);
 cudaError_t eng_attention(const AttnArgs& a, int batch, cudaStream_t st);
+// q / k RMSNorm + RoPE (and the K / V cache writes), attention and the ROW_QUANT of the attention
+// output rows in one launch: one block per (sequence, kv head), the kv heads of a sequence one
+// thread-block cluster (n_kv <= 8) that shares the row absmax. Same bits as eng_qk_rope +
+// eng_attention + eng_quant; r.qr and a.qr / a.att are not used.
+struct AttnQuantArgs {
+  QkRopeArgs r;
+  int8_t* q8;  uint64_t ldq;
+  float* qs;
+};
+cudaError_t eng_attention_quant(const AttnArgs& a, const AttnQuantArgs& f, int batch, cudaStream_t st);
 cudaError_t eng_argmax(const float* logits, int vocab, int batch, int* tok_out, int tok_stride, cudaStream_t st);
 cudaError_t eng_advance(int* pos, int n, cudaStream_t st);
 

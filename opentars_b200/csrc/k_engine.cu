@@ -432,8 +432,13 @@ constexpr int kAttnThreads = 256;
 constexpr int kMaxRows = 16;                 // G * n query rows per block
 // K / V rows in shared memory are padded by 4 floats: a warp's 32 threads read 32 different rows
 // at the same column, and the padding puts each 16-byte access of a phase in its own bank group.
-template <int HD>
-__global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a, int tile) {
+// FUSED: the block first runs k_qk_rope's work for its rows - the G query heads into shared
+// memory, the kv head's K row (normalised, rotated) and V row into the caches - and ends with the
+// ROW_QUANT of the attention output rows (k_quant_cl's steps): each block's absmax per token row,
+// the order-free max over the cluster's blocks (the sequence's kv heads) through distributed
+// shared memory, then each block quantises its own columns and rank 0 writes the row scales.
+template <int HD, bool FUSED>
+__global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a, int tile, AttnQuantArgs f) {
   griddep_launch();
   griddep_wait();
   constexpr int LD = HD + 4;
@@ -447,9 +452,59 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a, int tile
   const int t0 = *a.pos;
   const int nk = ((t0 + n) + 15) / 16 * 16;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int i = tid; i < R * HD; i += kAttnThreads) {
-    const int r = i / HD, d = i - r * HD, g = r / n, m = r - g * n;
-    sq[i] = ftz(a.qr[((uint64_t)(b * n + m) * a.nh + kvh * G + g) * HD + d]);
+  if constexpr (FUSED) {
+    // one half-warp per (query head, row) or (kv head, row); the K / V tile area is free yet and
+    // holds each half-warp's normalised row. Dead half-warps still join the shuffles.
+    const QkRopeArgs& q = f.r;
+    const int hw = tid >> 4, l = tid & 15;
+    float* sn = skv + hw * HD;
+    const int items = (G + 1) * n;
+    for (int base = 0; base < items; base += kAttnThreads / 16) {
+      const int item = base + hw;
+      const bool live = item < items;
+      const int it = live ? item : 0;
+      const bool isq = it < G * n;
+      const int g = isq ? it / n : 0, m = isq ? it - g * n : it - G * n;
+      const int r = b * n + m, t = t0 + m;
+      const float* src = isq ? q.q + (uint64_t)r * a.nh * HD + (kvh * G + g) * HD : q.k + ((uint64_t)r * a.nkv + kvh) * HD;
+      const float* gam = isq ? q.qn : q.kn;
+      float v[HD / 16];
+      float s = 0.0f;
+#pragma unroll
+      for (int i = 0; i < HD / 16; ++i) {
+        v[i] = ftz(src[l + 16 * i]);
+        s = fadd_nc(s, fmul(v[i], v[i]));
+      }
+      s = sum16_fold(canon(s));
+      const float rs = rsqrt_f(fadd(fmul(s, recip_f(i2f(HD))), q.eps));
+#pragma unroll
+      for (int i = 0; i < HD / 16; ++i) sn[l + 16 * i] = ftz(fmul(fmul(v[i], rs), gam[l + 16 * i]));
+      __syncwarp();
+      if (live) {
+        const float* tab = q.tab + (uint64_t)t * q.rot;
+        const int half = q.rot / 2;
+        float* dst = isq ? sq + (g * n + m) * HD : q.kc + (((uint64_t)b * a.Tp + t) * a.nkv + kvh) * HD;
+        for (int j = l; j < HD; j += 16) {
+          float y;
+          if (j < half) y = fadd(fmul(sn[j], ftz(tab[j])), neg(fmul(sn[j + half], ftz(tab[half + j]))));
+          else if (j < q.rot) y = fadd(fmul(sn[j], ftz(tab[j - half])), fmul(sn[j - half], ftz(tab[j])));
+          else y = sn[j];
+          dst[j] = ftz(y);
+        }
+        if (!isq) {                                // V goes to the cache as the GEMM wrote it
+          const float* vs = q.v + ((uint64_t)r * a.nkv + kvh) * HD;
+          float* vd = q.vc + (((uint64_t)b * a.Tp + t) * a.nkv + kvh) * HD;
+          for (int j = l; j < HD; j += 16) vd[j] = vs[j];
+        }
+      }
+      __syncwarp();
+    }
+    __threadfence_block();                         // the cache rows before the tiles read them
+  } else {
+    for (int i = tid; i < R * HD; i += kAttnThreads) {
+      const int r = i / HD, d = i - r * HD, g = r / n, m = r - g * n;
+      sq[i] = ftz(a.qr[((uint64_t)(b * n + m) * a.nh + kvh * G + g) * HD + d]);
+    }
   }
   const uint64_t kstride = (uint64_t)a.nkv * HD;
   const float* K = a.kc + ((uint64_t)b * a.Tp * a.nkv + kvh) * HD;
@@ -542,28 +597,67 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a, int tile
       }
     }
   }
+  if constexpr (!FUSED) {
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    const int o = tid + i * kAttnThreads;
-    if (o < R * HD) {
-      const int r = o / HD, d = o - r * HD, g = r / n, m = r - g * n;
-      a.att[((uint64_t)(b * n + m) * a.nh + kvh * G + g) * HD + d] = ftz(canon(acc[i]));
+    for (int i = 0; i < kPer; ++i) {
+      const int o = tid + i * kAttnThreads;
+      if (o < R * HD) {
+        const int r = o / HD, d = o - r * HD, g = r / n, m = r - g * n;
+        a.att[((uint64_t)(b * n + m) * a.nh + kvh * G + g) * HD + d] = ftz(canon(acc[i]));
+      }
     }
+  } else {
+    __shared__ float red[33];
+    __shared__ float s_amax[kMaxRows];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) acc[i] = ftz(canon(acc[i]));   // the values the att rows held
+    for (int m = 0; m < n; ++m) {
+      float mx = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int o = tid + i * kAttnThreads;
+        if (o < R * HD && (o / HD) % n == m) mx = fmax_c(mx, fabs_c(acc[i]));
+      }
+      mx = block_max(mx, red);
+      if (tid == 0) s_amax[m] = mx;
+    }
+    __shared__ float s_inv[kMaxRows];
+    cluster_sync();
+    if (tid < n) {                                  // thread m: row m's max over the cluster
+      const int m = tid;
+      const uint32_t crank = cluster_rank();
+      float mx = s_amax[m];
+      for (int p = 0; p < a.nkv; ++p)
+        if (p != (int)crank) mx = fmax_c(mx, __int_as_float(dsmem_ld_s32(smem_u32(&s_amax[m]), p)));
+      s_inv[m] = fmul(127.0f, recip_f(mx));
+      if (crank == 0) f.qs[b * n + m] = ftz(fmul(mx, bf(0x3C010204u)));
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int o = tid + i * kAttnThreads;
+      if (o < R * HD) {
+        const int r = o / HD, d = o - r * HD, g = r / n, m = r - g * n;
+        f.q8[(uint64_t)(b * n + m) * f.ldq + (kvh * G + g) * HD + d] = q8(acc[i], s_inv[m]);
+      }
+    }
+    cluster_sync();                                 // the peers have read s_amax
   }
 }
 
-template <int HD>
-static cudaError_t attention_hd(const AttnArgs& a, int batch, cudaStream_t st) {
+template <int HD, bool FUSED>
+static cudaError_t attention_hd(const AttnArgs& a, const AttnQuantArgs& f, int batch, cudaStream_t st) {
   const int R = (a.nh / a.nkv) * a.n;
   const int fixed = (R * HD + R * kT) * 4;
   // K / V tiles of about 40 KB: several blocks share an SM (all (sequence, kv head) blocks of a
   // batch of 64 in one wave) instead of one block streaming all keys at once
   const int tile = std::min(kT, (40 * 1024) / ((HD + 4) * 4)) / 16 * 16;
-  if (tile < 16) return cudaErrorInvalidValue;
+  if (tile < 16) return cudaErrorInvalidValue;                // (the fused prologue needs 16 rows)
   const int smem = fixed + tile * (HD + 4) * 4;
-  cudaError_t e = cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaFuncSetAttribute(k_attention<HD, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  return launch_ex(k_attention<HD>, dim3(batch * a.nkv), dim3(kAttnThreads), smem, st, 1, a, tile);
+  return launch_ex(k_attention<HD, FUSED>, dim3(batch * a.nkv), dim3(kAttnThreads), smem, st, FUSED ? a.nkv : 1, a,
+                   tile, f);
 }
 
 // ------------------------------------------------------------------------------- greedy pick
@@ -689,10 +783,24 @@ cudaError_t eng_qk_rope(const QkRopeArgs& a, cudaStream_t st) {
 cudaError_t eng_attention(const AttnArgs& a, int batch, cudaStream_t st) {
   const int R = (a.nh / a.nkv) * a.n;
   if (a.nh % a.nkv || R > kMaxRows) return cudaErrorInvalidValue;
+  const AttnQuantArgs f{};
   switch (a.hd) {
-    case 64: return attention_hd<64>(a, batch, st);
-    case 128: return attention_hd<128>(a, batch, st);
-    case 256: return attention_hd<256>(a, batch, st);
+    case 64: return attention_hd<64, false>(a, f, batch, st);
+    case 128: return attention_hd<128, false>(a, f, batch, st);
+    case 256: return attention_hd<256, false>(a, f, batch, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t eng_attention_quant(const AttnArgs& a, const AttnQuantArgs& f, int batch, cudaStream_t st) {
+  const int R = (a.nh / a.nkv) * a.n;
+  if (a.nh % a.nkv || R > kMaxRows || a.nkv > 8 || a.n > kMaxRows || f.r.hd != a.hd || f.r.rot > a.hd ||
+      f.r.rot % 2)
+    return cudaErrorInvalidValue;
+  switch (a.hd) {
+    case 64: return attention_hd<64, true>(a, f, batch, st);
+    case 128: return attention_hd<128, true>(a, f, batch, st);
+    case 256: return attention_hd<256, true>(a, f, batch, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -264,8 +264,11 @@ __global__ void __launch_bounds__(32 * (1 + s_stages<KU>()), 2)
   uint4 areg[MB == 1 ? KU : 1];                               // M = 1: the activation row in registers
   int areg_j = -1;
   for (int c = c_begin + st, t = st; c < c_end; c += S, t += S) {
-    if (*(volatile int*)&s_stop || !mbar_wait(&full[st], (t / S) & 1, nullptr, 0)) {
+    const bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[st], (t / S) & 1, nullptr, 0);
+    if (!__all_sync(0xFFFFFFFFu, ok)) {                           // the whole warp stops together
       s_stop = 1;
+      // the stage's copies may still be in flight: wait for them (bounded) before the block exits
+      mbar_wait(&full[st], (t / S) & 1, nullptr, 0);
       break;
     }
     while (c >= grp.c0[j + 1]) ++j;

@@ -371,7 +371,8 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
   for (int c = blockIdx.x; c < nchunk; c += gridDim.x, ++t) {
     const int st = t % kW4Stages;
     load_ws((c + gridDim.x) * kW4Cols + cw, wsn);
-    if (*(volatile int*)&s_stop || !mbar_wait(&full[st], (t / kW4Stages) & 1, nullptr, 0)) {
+    const bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[st], (t / kW4Stages) & 1, nullptr, 0);
+    if (!__all_sync(0xFFFFFFFFu, ok)) {                           // the whole warp stops together
       s_stop = 1;
       break;
     }

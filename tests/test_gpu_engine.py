@@ -45,6 +45,26 @@ def test_engine_batch_each_sequence_matches_oracle(name, batch):
         assert all(np.array_equal(lg[b].view(np.uint32), ol.view(np.uint32)) for lg, ol in zip(logits, ologits)), b
 
 
+@pytest.mark.parametrize("name", sorted(FX.models()))
+def test_engine_three_launch_attention_matches_fused(name, monkeypatch):
+    """TARSCUDA_FUSE_ATTN=0 (q / k norm + RoPE, attention and the output quantiser as three
+    launches) and the default single cluster launch give the same tokens and logits bits."""
+    from opentars_b200.engine import DecodeEngine
+    fx = FX.models()[name]
+    rng = np.random.default_rng(5)
+    P = len(fx["prompt"])
+    prompts = [list(map(int, rng.integers(0, fx["vocab"], P))) for _ in range(5)]
+    outs = []
+    for fuse in ("1", "0"):
+        monkeypatch.setenv("TARSCUDA_FUSE_ATTN", fuse)
+        eng = DecodeEngine(build_lowering(fx), batch=5)
+        ids, logits = eng.generate(prompts, 3, chunk=4)
+        eng.close()
+        outs.append((ids, [lg.view(np.uint32).copy() for lg in logits]))
+    assert outs[0][0] == outs[1][0]
+    assert all(np.array_equal(a, b) for a, b in zip(outs[0][1], outs[1][1]))
+
+
 def _full():
     p = FX.GOLDEN / "full_models.json"
     return json.loads(p.read_text()) if p.exists() else {}
