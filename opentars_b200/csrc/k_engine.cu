@@ -49,12 +49,21 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   for (int i = 1; i < (int)(blockDim.x >> 5); ++i) r = fmax_c(r, red[i]);
   return r;
 }
-// sum16 of v[0..N) (shared memory) in the contract's order, broadcast to the block
+// sum16 of v[0..N) (shared memory) in the contract's order, broadcast to the block. Each chain
+// loads 8 of its values before their 8 dependent adds (the order of the adds is unchanged).
 __device__ __forceinline__ float block_sum16(const float* v, int N, float* red) {
   __syncthreads();
   if (threadIdx.x < 16) {
     float acc = 0.0f;
-    for (int j = threadIdx.x; j < N; j += 16) acc = fadd_nc(acc, v[j]);
+    int j = threadIdx.x;
+    for (; j + 16 * 7 < N; j += 16 * 8) {
+      float t[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) t[u] = v[j + 16 * u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = fadd_nc(acc, t[u]);
+    }
+    for (; j < N; j += 16) acc = fadd_nc(acc, v[j]);
     acc = sum16_fold(canon(acc), 0x0000FFFFu);
     if (threadIdx.x == 0) red[32] = acc;
   }
@@ -81,12 +90,26 @@ __global__ void k_embed(const float* E, const int* tok, float* x, int H, int sca
 // Outputs the int8 row and its row scale (llm.py:97-104, numerics.py:353-390).
 __global__ void __launch_bounds__(256) k_norm_quant(NormQuantArgs a) {
   griddep_launch();
-  griddep_wait();
   extern __shared__ float sm[];
   float* sx = sm;
   float* sv = sm + a.H;
+  float* sg = sm + 2 * a.H;                      // gamma, then pre_gamma (mode 2)
+  float* spg = sm + 3 * a.H;
   __shared__ float red[33];
   const int r = blockIdx.x, H = a.H, t = threadIdx.x;
+  // the norms' weights do not depend on the previous kernel: staged before the dependency wait
+  if ((((uintptr_t)a.gamma | (uintptr_t)a.pre_gamma) & 15) == 0 && H % 4 == 0) {
+    for (int j4 = t; j4 < H / 4; j4 += blockDim.x) {
+      cp16(sg + 4 * j4, a.gamma + 4 * j4);
+      if (a.mode == 2) cp16(spg + 4 * j4, a.pre_gamma + 4 * j4);
+    }
+  } else {
+    for (int j = t; j < H; j += blockDim.x) {
+      sg[j] = a.gamma[j];
+      if (a.mode == 2) spg[j] = a.pre_gamma[j];
+    }
+  }
+  griddep_wait();
   const float kinv = recip_f(i2f(H));
   const float* in = a.in + (uint64_t)r * a.ld_in;
   for (int j4 = t; j4 < H / 4; j4 += blockDim.x) cp16(sx + 4 * j4, in + 4 * j4);
@@ -98,7 +121,7 @@ __global__ void __launch_bounds__(256) k_norm_quant(NormQuantArgs a) {
     for (int j = t; j < H; j += blockDim.x) sv[j] = fmul(sx[j], sx[j]);
     const float s = block_sum16(sv, H, red);
     const float rs = rsqrt_f(fadd(fmul(s, kinv), a.eps));
-    for (int j = t; j < H; j += blockDim.x) sx[j] = ftz(fmul(fmul(sx[j], rs), a.pre_gamma[j]));
+    for (int j = t; j < H; j += blockDim.x) sx[j] = ftz(fmul(fmul(sx[j], rs), spg[j]));
   }
   if (a.mode >= 1) {
     const float* res = a.res + (uint64_t)r * H;
@@ -114,7 +137,7 @@ __global__ void __launch_bounds__(256) k_norm_quant(NormQuantArgs a) {
   const float rs = rsqrt_f(fadd(fmul(s, kinv), a.eps));
   float amax = 0.0f;
   for (int j = t; j < H; j += blockDim.x) {
-    const float h = ftz(fmul(fmul(sx[j], rs), a.gamma[j]));
+    const float h = ftz(fmul(fmul(sx[j], rs), sg[j]));
     sv[j] = h;
     amax = fmax_c(amax, fabs_c(h));
   }
@@ -712,7 +735,7 @@ cudaError_t eng_embed(const float* E, const int* tok, float* x, int H, int scale
   return cudaGetLastError();
 }
 cudaError_t eng_norm_quant(const NormQuantArgs& a, cudaStream_t st) {
-  const int smem = 2 * a.H * 4;
+  const int smem = 4 * a.H * 4;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k_norm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
