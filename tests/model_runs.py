@@ -22,6 +22,43 @@ def build_lowering(fx: dict, full: bool = False):
     return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096)
 
 
+def build_export_lowering(fx: dict):
+    """A fixture's small model with its embedding table rounded to bf16 (an export stores the table
+    as bf16), for the export-format tests."""
+    from opentars_b200 import models as Mo
+    from opentars_b200.export import bf16_exact
+    from opentars_b200.lowering import QwenLowering
+    base = dict(Mo.CFG_G3_SMALL, intermediate_size=4608) if fx["base"] == "G3_SMALL_K2" else getattr(Mo, fx["base"])
+    cfg = Mo.make_config(base, fx["types"], vocab=fx["vocab"])
+    w = Mo.random_weights(cfg, seed=0, embed=True)
+    w["embed_tokens.weight"] = bf16_exact(w["embed_tokens.weight"])
+    return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096)
+
+
+class OracleDevice:
+    """The CPU oracle as a board device (mem / to_dev / from_dev / run), as tars_board's Golden
+    backend is the reference golden model: test infrastructure only."""
+    params = dict(backend="oracle")
+
+    def __init__(self, mem: int):
+        self.buf = bytearray(mem)
+        self.mem = np.frombuffer(self.buf, np.uint8)
+
+    def to_dev(self, a, n):
+        pass
+
+    def from_dev(self, a, n):
+        pass
+
+    def run(self, q, n, timeout=None):
+        from oracle.machine import OracleMachine
+        m = OracleMachine(self.buf)
+        st = m.run_queue(q, n)
+        if m.ddr is not self.buf:
+            self.mem[:] = np.frombuffer(bytes(m.ddr), np.uint8)
+        return st.done, st.err_code, st.op_idx, 0
+
+
 def sha(a) -> str:
     return hashlib.sha256(bytes(a)).hexdigest()
 
