@@ -151,23 +151,30 @@ __device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
 }
 // The exact dot of one 128-group: 16 words of packed nibbles against 16 chunks (in word order)
 // of the aligned mantissas split as q = 256 qh + ql; u = nibble ^ 8 = w + 8, so
-// sum(w q) = 256 sum(u qh) + sum(u ql) - 8 sum(q). Four independent accumulator chains.
+// sum(w q) = 256 sum(u qh) + sum(u ql) - 8 sum(q). Four independent accumulator chains. The odd
+// nibbles stay in the high half of each byte (16 u), so their sums are 16 times their value and
+// are shifted back exactly (multiples of 16): two logic operations per packed word.
 template <class WordOf, class ChunkOf>
 __device__ __forceinline__ int group_dot(WordOf word, ChunkOf chunk, int qsum) {
   int h0 = 0, h1 = 0, l0 = 0, l1 = 0;
 #pragma unroll
   for (int c = 0; c < 16; ++c) {
-    const uint32_t w = word(c);
-    const uint32_t ev = (w & 0x0F0F0F0Fu) ^ 0x08080808u;          // u of k = 8c + 0, 2, 4, 6
-    const uint32_t od = ((w >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;   // u of k = 8c + 1, 3, 5, 7
+    const uint32_t w = word(c) ^ 0x88888888u;                      // u = nibble ^ 8 in every nibble
+    const uint32_t ev = w & 0x0F0F0F0Fu;                          // u of k = 8c + 0, 2, 4, 6
+    const uint32_t od = w & 0xF0F0F0F0u;                          // 16 u of k = 8c + 1, 3, 5, 7
     const uint4 qc = chunk(c);
     h0 = dp4a_us(ev, qc.x, h0);
     h1 = dp4a_us(od, qc.y, h1);
     l0 = dp4a_uu(ev, qc.z, l0);
     l1 = dp4a_uu(od, qc.w, l1);
   }
-  return 256 * (h0 + h1) + (l0 + l1) - 8 * qsum;
+  return 256 * (h0 + (h1 >> 4)) + (l0 + (l1 >> 4)) - 8 * qsum;
 }
+
+// term = fmul(fmul(i2f(dot), ws), xs) without the input flushes: i2f of an int, a widened fp16 and
+// a block-FP scale (2^e, 0, inf or NaN) are never denormal; a NaN stays a NaN through the products
+// and the bank's final canon makes it 0x7FC00000.
+__device__ __forceinline__ float group_term(int dot, float ws, float xs) { return fmul_ff(fmul_ff(i2f(dot), ws), xs); }
 
 // One persistent block stages its activation rows once (16-byte loads when aligned), aligns them
 // in shared memory, then its warps stream columns n = gw, gw + nw, ...; each lane keeps the
@@ -240,7 +247,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_w4(W4Args g, bool vec) {
                   return (c & 3) == 0 ? v.x : (c & 3) == 1 ? v.y : (c & 3) == 2 ? v.z : v.w;
                 },
                 [&](int c) { return q[c]; }, sSum[m * 64 + gi]);
-            term[m][slot] = fmul(fmul(i2f(dot), ws), bf(sS[m * 64 + gi]));
+            term[m][slot] = group_term(dot, ws, bf(sS[m * 64 + gi]));
           }
         }
       }
@@ -249,14 +256,9 @@ __global__ void __launch_bounds__(kThreads) k_gemv_w4(W4Args g, bool vec) {
     const int b = lane & 3;
 #pragma unroll
     for (int m = 0; m < MB; ++m) {
-      float t[16];
+      float t[16];                                                // group b + 4 i: lane (b + 4 i) mod 32
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int gi = b + 4 * i;
-        const float t0 = __shfl_sync(0xFFFFFFFFu, term[m][0], gi & 31);
-        const float t1 = __shfl_sync(0xFFFFFFFFu, term[m][1], gi & 31);
-        t[i] = gi < 32 ? t0 : t1;
-      }
+      for (int i = 0; i < 16; ++i) t[i] = __shfl_sync(0xFFFFFFFFu, term[m][i < 8 ? 0 : 1], (b + 4 * i) & 31);
       float bank = 0.0f;
 #pragma unroll
       for (int i = 0; i < 16; ++i)
@@ -404,7 +406,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
                     return (c & 3) == 0 ? v.x : (c & 3) == 1 ? v.y : (c & 3) == 2 ? v.z : v.w;
                   },
                   [&](int c) { return q[pc[c >> 2] * 4 + (c & 3)]; }, sSum[m * 64 + gi]);
-              term[m][slot] = fmul(fmul(i2f(dot), ws), bf(sS[m * 64 + gi]));
+              term[m][slot] = group_term(dot, ws, bf(sS[m * 64 + gi]));
             }
           }
         }
@@ -414,14 +416,9 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
       const int b = lane & 3;
 #pragma unroll
       for (int m = 0; m < MB; ++m) {
-        float tt[16];
+        float tt[16];                                             // group b + 4 i: lane (b + 4 i) mod 32
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int gi = b + 4 * i;
-          const float t0 = __shfl_sync(0xFFFFFFFFu, term[m][0], gi & 31);
-          const float t1 = __shfl_sync(0xFFFFFFFFu, term[m][1], gi & 31);
-          tt[i] = gi < 32 ? t0 : t1;
-        }
+        for (int i = 0; i < 16; ++i) tt[i] = __shfl_sync(0xFFFFFFFFu, term[m][i < 8 ? 0 : 1], (b + 4 * i) & 31);
         float bank = 0.0f;
 #pragma unroll
         for (int i = 0; i < 16; ++i)
