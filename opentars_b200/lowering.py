@@ -1,15 +1,17 @@
-"""The step driver: Qwen3 / Gemma 3 models lowered to tars_mini v0.4 descriptors.
+"""The step driver: Qwen3 / Gemma 3 / Qwen3.5 text models lowered to tars_mini v0.4 descriptors.
 
 Restates, for the families on the hot path, the reference's program builder and LLM lowering so
 that the same DDR image and the same descriptor queues come out byte for byte (pinned by the
 committed fixtures):
   * Program (alloc / _put / _emit / build)       tars_mini/compiler.py:134-155, 186-188, 384-391
-  * V, Dev emitters (rowop, norm, quant, gemm_rc, gemm_w4, fdot, elt, rope)   tars_mini/llm.py:34-178
-  * QwenLowering: weights, state, chunk, _fa_block, _mlp, _head, stage, put_input, logits_of,
-    logits_rows, generate                                                     llm.py:213-836
-Every linear is W8A8 (ROW_QUANT then GEMM QM_ROWCOL); Gemma 3's down projection runs as equal
-K blocks (llm.py:303-321) whose fp32 partials are added by ELT ADD in block order. Qwen3.5's
-linear attention, MTP and Gemma 4 are outside this path.
+  * V, Dev emitters (rowop, norm, quant, gemm_rc, gemm_w4, fdot, elt, act, rope)  tars_mini/llm.py:34-178
+  * QwenLowering: weights, state, chunk, _la (Qwen3.5's gated DeltaNet layers), _fa_block (with
+    Qwen3.5's attention output gate), _mlp, _head, stage, put_input, logits_of, logits_rows,
+    generate                                                                  llm.py:213-836
+Every linear is W8A8 (ROW_QUANT then GEMM QM_ROWCOL) or W4A16; Gemma 3's down projection runs as
+equal K blocks (llm.py:303-321) whose fp32 partials are added by ELT ADD in block order. The
+DeltaNet state may be fp16 (state_dtype, the STATE_FP16 ELT / FDOT forms). MTP speculation and
+Gemma 4 are outside this path.
 """
 from __future__ import annotations
 
@@ -176,6 +178,12 @@ class Dev(Program):
                    GROUP_SIZE=g, LDA16=0 if arow else _ld16(a.ld, C.ESIZE[a.fmt] * N),
                    LDY16=_ld16(y.ld, N * C.ESIZE[y.fmt]))
 
+    def act(self, x: V, act: int, y: V) -> None:
+        """The activation op (OPCODE RELU with EPI.act): y = act(x)."""
+        self._emit(OPCODE=C.OP_RELU, CTRL=0, EPI=C.epi(act, y.fmt), A_OFF=x.off, Y_OFF=y.off,
+                   M=x.rows, N=x.cols, LDA16=_ld16(x.ld, 4 * x.cols),
+                   LDY16=_ld16(y.ld, y.cols * C.ESIZE[y.fmt]))
+
     def rope(self, x: V, tab: V, rows_per_pos: int, rot: int, y: V) -> None:
         self._emit(OPCODE=C.OP_ROPE, CTRL=0, EPI=C.epi(C.ACT_NONE, y.fmt), A_OFF=x.off, W_OFF=tab.off,
                    Y_OFF=y.off, M=x.rows, N=x.cols, K=rot, GROUP_SIZE=rows_per_pos,
@@ -191,12 +199,16 @@ class QwenLowering:
 
     def __init__(self, cfg, weights: dict[str, np.ndarray], max_tokens: int, ddr_bytes: int = 1 << 27,
                  head: bool = False, queue_cap: int = 0, scratch_bytes: int = 1 << 22, verify_rows: int = 1,
-                 keep_layers: bool = True, wbits: int = 8):
+                 keep_layers: bool = True, wbits: int = 8, state_dtype: str = "fp32"):
         if wbits not in (4, 8):
             raise ValueError("wbits must be 4 (W4A16) or 8 (W8A8)")
+        if state_dtype not in ("fp32", "fp16"):
+            raise ValueError("state_dtype must be fp32 or fp16")
         mt = getattr(cfg, "model_type", "")
-        if mt not in ("qwen3", "gemma3_text"):
-            raise ValueError(f"model type {mt!r}: this lowering covers Qwen3 and Gemma 3")
+        if mt not in ("qwen3", "gemma3_text", "qwen3_5_text"):
+            raise ValueError(f"model type {mt!r}: this lowering covers Qwen3, Gemma 3 and Qwen3.5 text")
+        self.state_fmt = C.OUT_FP16 if state_dtype == "fp16" else C.OUT_FP32
+        self.parity, self.spec = 0, False          # the DeltaNet state copy in use (one copy here)
         self.wbits, self.keep_layers = wbits, keep_layers
         self.cfg, self.w, self.T = cfg, weights, max_tokens
         self.verify_rows = verify_rows
@@ -210,13 +222,20 @@ class QwenLowering:
             assert cfg.attn_logit_softcapping is None and cfg.final_logit_softcapping is None
             assert cfg.hidden_activation == "gelu_pytorch_tanh"
             assert max_tokens <= cfg.sliding_window, "the context must fit the sliding window"
-        else:
+        elif self.q3:
             assert set(self.types) == {"full_attention"}
+        else:
+            assert set(self.types) <= {"linear_attention", "full_attention"}
+        # Qwen3.5's linear-attention (gated DeltaNet) dimensions
+        self.nk, self.nv = getattr(cfg, "linear_num_key_heads", 0), getattr(cfg, "linear_num_value_heads", 0)
+        self.dk, self.dv = getattr(cfg, "linear_key_head_dim", 0), getattr(cfg, "linear_value_head_dim", 0)
+        assert self.nk == self.nv, "the GQA repeat of linear attention is not lowered"
         self.nh, self.nkv, self.hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         self.rot = self.hd if self.gemma else int(self.hd * cfg.rope_parameters.get("partial_rotary_factor", 1.0))
         self.qmul = cfg.query_pre_attn_scalar ** -0.5 if self.gemma else self.hd ** -0.5
         self.Tp = pad16(max_tokens)
         self.head = head
+        self.taps = getattr(cfg, "linear_conv_kernel_dim", 4)
         self.vocab = weights["embed_tokens.weight"].shape[0] if head else 0
         self._state()
         self.queue_cap = queue_cap
@@ -255,8 +274,8 @@ class QwenLowering:
                 for c in range(0, qw.k, kb)]
 
     def gamma1(self, w: np.ndarray, mul: float = 1.0) -> V:
-        """Qwen3: the RMSNorm weight itself; Gemma 3: fp32(1 + w). Times `mul` (the attention
-        scaling folded into q_norm)."""
+        """Qwen3: the RMSNorm weight itself; Gemma 3 and Qwen3.5 (zero-centred weights): fp32(1 + w).
+        Times `mul` (the attention scaling folded into q_norm)."""
         g = np.asarray(w, F32) if self.q3 else (F32(1.0) + np.asarray(w, F32)).astype(F32)
         return self.p.const((g * F32(mul)).astype(F32))
 
@@ -266,6 +285,33 @@ class QwenLowering:
         else:
             xq, xs = self.p.quant(x) if qs is None else qs
             self.p.gemm_rc(xq, xs, w, y, act)
+
+    def _la_weights(self, L: str) -> dict:
+        """A gated DeltaNet layer: q / k / v as three linears (rows of in_proj_qkv), z, b, a (with
+        dt_bias as the GEMM bias), -exp(A_log), the conv taps per channel block, the gated norm."""
+        W, p = self.w, self.p
+        la = L + "linear_attn."
+        kd, vd = self.nk * self.dk, self.nv * self.dv
+        qkv = W[la + "in_proj_qkv.weight"]
+        d = dict(
+            ln_in=self.gamma1(W[L + "input_layernorm.weight"]),
+            ln_post=self.gamma1(W[L + "post_attention_layernorm.weight"]),
+            q=self.lin(qkv[:kd]), k=self.lin(qkv[kd:2 * kd]), v=self.lin(qkv[2 * kd:]),
+            z=self.lin(W[la + "in_proj_z.weight"]),
+            b=self.lin(W[la + "in_proj_b.weight"]),
+            a=self.lin(W[la + "in_proj_a.weight"], W[la + "dt_bias"]),
+            negA=p.const(-np.exp(W[la + "A_log"].astype(F32))),
+            out=self.lin(W[la + "out_proj.weight"]),
+            gnorm=p.const(W[la + "norm.weight"]),
+            qscale=p.const(np.full(self.dk, F32(self.dk ** -0.5))),
+            kscale=p.const(np.ones(self.dk, F32)),
+            gate=self.lin(W[L + "mlp.gate_proj.weight"]), up=self.lin(W[L + "mlp.up_proj.weight"]),
+            down=self.lin(W[L + "mlp.down_proj.weight"]))
+        cw = W[la + "conv1d.weight"][:, 0, :]                  # [channels, taps]
+        self.taps = cw.shape[1]
+        d["conv"] = {n: [p.const(cw[o:o + dd, j]) for j in range(self.taps)]
+                     for n, o, dd in (("q", 0, kd), ("k", kd, kd), ("v", 2 * kd, vd))}
+        return d
 
     def _fa_weights(self, A: str) -> dict:
         W = self.w
@@ -281,11 +327,15 @@ class QwenLowering:
                 o=self.lin(W[sa + "o_proj.weight"]),
                 gate=self.lin(W[A + "mlp.gate_proj.weight"]), up=self.lin(W[A + "mlp.up_proj.weight"]),
                 down=self.lin_k(W[A + "mlp.down_proj.weight"]))
-        q = self.lin(W[sa + "q_proj.weight"])
+        if self.q3:                                            # no output gate
+            q, g = self.lin(W[sa + "q_proj.weight"]), None
+        else:                                                  # Qwen3.5, per head: the query's rows, then the gate's
+            qp = W[sa + "q_proj.weight"].reshape(self.nh, 2, self.hd, self.H)
+            q, g = self.lin(qp[:, 0].reshape(-1, self.H)), self.lin(qp[:, 1].reshape(-1, self.H))
         return dict(
             ln_in=self.gamma1(W[A + "input_layernorm.weight"]),
             ln_post=self.gamma1(W[A + "post_attention_layernorm.weight"]),
-            q=q, g=None,
+            q=q, g=g,
             k=self.lin(W[sa + "k_proj.weight"]), v=self.lin(W[sa + "v_proj.weight"]),
             qn=self.gamma1(W[sa + "q_norm.weight"], self.qmul), kn=self.gamma1(W[sa + "k_norm.weight"]),
             o=self.lin(W[sa + "o_proj.weight"]),
@@ -294,7 +344,9 @@ class QwenLowering:
 
     def _weights(self) -> None:
         p = self.p
-        self.lw = [self._fa_weights(f"layers.{i}.") for i in range(len(self.types))]
+        self.taps = 4
+        self.lw = [self._la_weights(f"layers.{i}.") if t == "linear_attention" else self._fa_weights(f"layers.{i}.")
+                   for i, t in enumerate(self.types)]
         if self.gemma:
             for w, t in zip(self.lw, self.types):
                 w["rope"] = t
@@ -330,8 +382,16 @@ class QwenLowering:
             xb0, xb1 = p.mat(T, H), p.mat(T, H)
             self.xs = [self.x0] + [xb0 if i % 2 == 0 else xb1 for i in range(len(self.types))]
         self.y = p.mat(T, H)
-        self.st = [dict(kc=p.mat(self.Tp, self.nkv * self.hd), vc=p.mat(self.Tp, self.nkv * self.hd))
-                   for _ in self.types]
+        kd, vd, hist = self.nk * self.dk, self.nv * self.dv, self.taps - 1
+        self.st = []
+        for t in self.types:
+            if t == "linear_attention":
+                # the conv inputs (rows t + hist; the first hist rows are the zero history) and the
+                # DeltaNet state, one [dk, dv] matrix per value head
+                self.st.append(dict(cin={n: p.mat(T + hist, d) for n, d in (("q", kd), ("k", kd), ("v", vd))},
+                                    S=[[p.mat(self.dk, self.dv, self.state_fmt) for _ in range(self.nv)]]))
+            else:
+                self.st.append(dict(kc=p.mat(self.Tp, self.nkv * self.hd), vc=p.mat(self.Tp, self.nkv * self.hd)))
         self.logits = p.mat(self.verify_rows, self.vocab) if self.head else None
 
     def input(self, x: np.ndarray, t0: int = 0) -> None:
@@ -344,9 +404,12 @@ class QwenLowering:
         token's logits (all_rows: every token's)."""
         assert not all_rows or n <= self.verify_rows
         p = self.p
-        for i in range(len(self.types)):
-            p.top = self.scratch0
-            self._fa_block(self.lw[i], self.st[i], self.xs[i].rowv(t0, n), self.xs[i + 1].rowv(t0, n), t0, n)
+        for i, t in enumerate(self.types):
+            p.top = self.scratch0                  # this layer's temporaries over the last layer's
+            if t == "linear_attention":
+                self._la(i, t0, n)
+            else:
+                self._fa_block(self.lw[i], self.st[i], self.xs[i].rowv(t0, n), self.xs[i + 1].rowv(t0, n), t0, n)
             assert p.top <= self.scratch_end, "scratch_bytes too small for this chunk"
         p.top = self.scratch0
         p.norm(self.xs[-1].rowv(t0, n), self.final_norm, self.eps, self.y.rowv(t0, n))
@@ -394,6 +457,67 @@ class QwenLowering:
             d = dn
         p.elt(C.ELT_ADD, x, d, out)
 
+    def _la(self, li: int, t0: int, n: int) -> None:
+        """A gated DeltaNet layer (llm.py:642-700): ln_in + quant; the q, k, v projections into the
+        conv input rows, z, beta = sigmoid(b), softplus(a + dt_bias); g = -exp(A_log) * softplus,
+        decay = exp(g); the causal depthwise conv over the last taps rows (ELT MUL, then MULADD in
+        tap order) and SiLU; q and k L2-normed per head (q times dk^-0.5 through gamma); then token
+        by token and head by head S = S * decay, kv_mem = S^T k, delta = (v - kv_mem) * beta,
+        S += k (x) delta, out = S^T q; the gated RMSNorm per head, times silu(z), out_proj, the
+        residual and the MLP."""
+        p, w, st = self.p, self.lw[li], self.st[li]
+        kd, vd, hist = self.nk * self.dk, self.nv * self.dv, self.taps - 1
+        x = self.xs[li].rowv(t0, n)
+        h = p.mat(n, self.H)
+        p.norm(x, w["ln_in"], self.eps, h)
+        qs = p.quant(h) if self.wbits == 8 else None
+        for nm in ("q", "k", "v"):
+            self.linear(h, w[nm], st["cin"][nm].rowv(hist + t0, n), qs=qs)
+        z = p.mat(n, vd)
+        self.linear(h, w["z"], z, qs=qs)
+        beta, sp = p.mat(n, self.nv), p.mat(n, self.nv)
+        self.linear(h, w["b"], beta, act=C.ACT_SIGMOID, qs=qs)
+        self.linear(h, w["a"], sp, act=C.ACT_SOFTPLUS, qs=qs)
+        g = p.mat(n, self.nv)
+        p.elt(C.ELT_MUL, sp, w["negA"], g, bmode=C.BM_ROW)
+        decay = p.mat(n, self.nv)
+        p.act(g, C.ACT_EXP, decay)
+        conv = {}
+        for nm, d in (("q", kd), ("k", kd), ("v", vd)):
+            src, acc = st["cin"][nm], p.mat(n, d)
+            p.elt(C.ELT_MUL, src.rowv(t0, n), w["conv"][nm][0], acc, bmode=C.BM_ROW)
+            for j in range(1, self.taps):
+                p.elt(C.ELT_MULADD, src.rowv(t0 + j, n), w["conv"][nm][j], acc, bmode=C.BM_ROW, c=acc)
+            o = p.mat(n, d)
+            p.act(acc, C.ACT_SILU, o)
+            conv[nm] = o
+        qn, kn = p.mat(n, kd), p.mat(n, kd)
+        p.norm(conv["q"].heads(self.dk), w["qscale"], 1e-6, qn.heads(self.dk), l2=True)
+        p.norm(conv["k"].heads(self.dk), w["kscale"], 1e-6, kn.heads(self.dk), l2=True)
+        qh, kh, vh = qn.heads(self.dk), kn.heads(self.dk), conv["v"].heads(self.dv)
+        o = p.mat(n, vd)
+        oh = o.heads(self.dv)
+        kvm, dl = p.mat(1, self.dv), p.mat(1, self.dv)
+        for t in range(n):
+            for hh in range(self.nv):
+                r = t * self.nv + hh
+                S0 = st["S"][self.parity][hh]
+                S = S0
+                p.elt(C.ELT_MUL, S0, decay.rowv(t, 1).colv(hh, 1), S, bmode=C.BM_SCALAR)
+                p.fdot(kh.rowv(r, 1), S, kvm, nn=True)
+                p.elt(C.ELT_SUB, vh.rowv(r, 1), kvm, dl)
+                p.elt(C.ELT_MUL, dl, beta.rowv(t, 1).colv(hh, 1), dl, bmode=C.BM_SCALAR)
+                p.elt(C.ELT_MULADD, dl, kh.rowv(r, 1), S, bmode=C.BM_COL, arow=True, c=S)
+                p.fdot(qh.rowv(r, 1), S, oh.rowv(r, 1), nn=True)
+        on, og = p.mat(n, vd), p.mat(n, vd)
+        p.norm(oh, w["gnorm"], self.eps, on.heads(self.dv))
+        p.elt(C.ELT_MUL, z, on, og, act=C.ACT_SILU)
+        a = p.mat(n, self.H)
+        self.linear(og, w["out"], a)
+        x1 = p.mat(n, self.H)
+        p.elt(C.ELT_ADD, x, a, x1)
+        self._mlp(w, x1, self.xs[li + 1].rowv(t0, n))
+
     def _fa_block(self, w: dict, st: dict, x: V, out: V, t0: int, n: int) -> None:
         p = self.p
         kc, vc = st["kc"], st["vc"]
@@ -403,6 +527,9 @@ class QwenLowering:
         qs = p.quant(h) if self.wbits == 8 else None
         q = p.mat(n, nh * hd)
         self.linear(h, w["q"], q, qs=qs)
+        if w["g"] is not None:
+            g = p.mat(n, nh * hd)
+            self.linear(h, w["g"], g, qs=qs)
         qn = p.mat(n, nh * hd)
         p.norm(q.heads(hd), w["qn"], self.eps, qn.heads(hd))
         qr = p.mat(n, nh * hd)
@@ -425,6 +552,10 @@ class QwenLowering:
             p.fdot(qv, kmat, sc, nn=False)
             p.softmax_causal(sc, pr, t0 + 1)
             p.fdot(pr, vmat, V(att.off + hh * hd * 4, n, hd, att.ld), nn=True)
+        if w["g"] is not None:
+            ga = p.mat(n, nh * hd)
+            p.elt(C.ELT_MUL, g, att, ga, act=C.ACT_SIGMOID)          # sigmoid(gate) * attention
+            att = ga
         aqs = p.quant(att) if self.wbits == 8 else None
         o = p.mat(n, self.H)
         self._linear_k(att, w["o"], aqs, o)

@@ -1,6 +1,6 @@
 """Host model data for the lowering: configs, seeded random weights, weight quantisers.
 
-Restates, for the model families on the hot path (Qwen3 and Gemma 3 text models):
+Restates, for the model families on the hot path (Qwen3, Gemma 3 and Qwen3.5 text models):
   * make_config          tars_mini/qwen_ref.py:109-146 (transformers config objects)
   * random_weights       qwen_ref.py:165-198 (same generator, same draw order: the model's state_dict)
   * head_rows            qwen_ref.py:371-378 (the vocabulary in the fewest equal blocks <= 65535 rows)
@@ -36,9 +36,25 @@ CFG_G3_1B = dict(model_type="gemma3_text", hidden_size=1152, intermediate_size=6
 CFG_G3_SMALL = dict(CFG_G3_1B, hidden_size=256, intermediate_size=512, num_attention_heads=4,
                     num_key_value_heads=2, head_dim=64, query_pre_attn_scalar=64, sliding_window=64)
 
+# Qwen3.5-0.8B's text model (qwen_ref.py:20-33): 3 gated-DeltaNet layers to 1 gated full-attention
+# layer, partial rotary 0.25 (text positions: plain RoPE), tied embeddings; the small variant of the
+# block tests (qwen_ref.py:86-88)
+VOCAB_08B = 248320
+LAYERS_08B = (["linear_attention"] * 3 + ["full_attention"]) * 6
+CFG_08B = dict(model_type="qwen3_5_text", hidden_size=1024, intermediate_size=3584, num_attention_heads=8,
+               num_key_value_heads=2, head_dim=256, linear_conv_kernel_dim=4, linear_key_head_dim=128,
+               linear_value_head_dim=128, linear_num_key_heads=16, linear_num_value_heads=16, rms_norm_eps=1e-6,
+               vocab_size=16, max_position_embeddings=262144, attn_output_gate=True,
+               rope_parameters=dict(rope_type="default", rope_theta=10000000.0, partial_rotary_factor=0.25,
+                                    mrope_section=[11, 11, 10], mrope_interleaved=True))
+CFG_Q35_SMALL = dict(CFG_08B, hidden_size=256, intermediate_size=512, num_attention_heads=4, num_key_value_heads=2,
+                     head_dim=128, linear_key_head_dim=16, linear_value_head_dim=16, linear_num_key_heads=16,
+                     linear_num_value_heads=16)
+
 
 def make_config(base: dict, layer_types: list[str] | None = None, vocab: int | None = None):
-    """A transformers config for a Qwen3 or Gemma 3 text model (tied embeddings, eager attention)."""
+    """A transformers config for a Qwen3, Gemma 3 or Qwen3.5 text model (tied embeddings, eager
+    attention)."""
     b = {k: v for k, v in base.items() if k != "model_type"}
     if base.get("model_type") == "gemma3_text":
         from transformers.models.gemma3.configuration_gemma3 import Gemma3TextConfig
@@ -51,8 +67,13 @@ def make_config(base: dict, layer_types: list[str] | None = None, vocab: int | N
         b.pop("num_hidden_layers", None)
         cfg = Qwen3Config(**dict(b, vocab_size=vocab or b["vocab_size"], tie_word_embeddings=True),
                           num_hidden_layers=n, layer_types=["full_attention"] * n)
+    elif base.get("model_type") == "qwen3_5_text":
+        from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
+        lt = list(layer_types or ["linear_attention", "full_attention"])
+        cfg = Qwen3_5TextConfig(**dict(b, vocab_size=vocab or b["vocab_size"], tie_word_embeddings=True),
+                                num_hidden_layers=len(lt), layer_types=lt)
     else:
-        raise ValueError(f"model type {base.get('model_type')!r} is not on this path (Qwen3, Gemma 3)")
+        raise ValueError(f"model type {base.get('model_type')!r} is not on this path (Qwen3, Gemma 3, Qwen3.5)")
     cfg._attn_implementation = "eager"
     return cfg
 
@@ -62,6 +83,8 @@ def param_shapes(cfg) -> list[tuple[str, tuple[int, ...]]]:
     import torch
     if cfg.model_type == "qwen3":
         from transformers.models.qwen3.modeling_qwen3 import Qwen3Model as Model
+    elif cfg.model_type == "qwen3_5_text":
+        from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5TextModel as Model
     else:
         from transformers.models.gemma3.modeling_gemma3 import Gemma3TextModel as Model
     with torch.device("meta"):
@@ -70,8 +93,10 @@ def param_shapes(cfg) -> list[tuple[str, tuple[int, ...]]]:
 
 
 def random_weights(cfg, seed: int = 0, embed: bool = False) -> dict[str, np.ndarray]:
-    """Linears N(0, 0.02) with 2 % of the output rows x4; norms 1 + N(0, 0.1) (Qwen3) or N(0, 0.1)
-    (Gemma 3, zero-centred); with `embed` the tied embedding N(0, 0.02), drawn 8192 rows at a time."""
+    """Linears N(0, 0.02) with 2 % of the output rows x4; Qwen3.5's conv taps N(0, 0.3), A_log =
+    log U(1, 16), dt_bias U(0.5, 1.5), the gated norm 1 + N(0, 0.1); norms 1 + N(0, 0.1) (Qwen3) or
+    N(0, 0.1) (Gemma 3 and Qwen3.5, zero-centred); with `embed` the tied embedding N(0, 0.02), drawn
+    8192 rows at a time."""
     rng = np.random.default_rng(seed)
     w = {}
     for name, shape in param_shapes(cfg):
@@ -84,6 +109,14 @@ def random_weights(cfg, seed: int = 0, embed: bool = False) -> dict[str, np.ndar
             continue
         if len(shape) == 2:
             a = rng.normal(0, 0.02, shape) * np.where(rng.random(shape[0]) < 0.02, 4.0, 1.0)[:, None]
+        elif "conv1d" in name:
+            a = rng.normal(0, 0.3, shape)
+        elif name.endswith("A_log"):
+            a = np.log(rng.uniform(1, 16, shape))
+        elif name.endswith("dt_bias"):
+            a = rng.uniform(0.5, 1.5, shape)
+        elif name.endswith("linear_attn.norm.weight"):
+            a = 1 + rng.normal(0, 0.1, shape)
         elif cfg.model_type == "qwen3":
             a = 1 + rng.normal(0, 0.1, shape)
         else:

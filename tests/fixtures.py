@@ -30,6 +30,13 @@ def models() -> dict:
     return json.loads(p.read_text()) if p.exists() else {}
 
 
+def engine_models() -> dict:
+    """The model fixtures the batched decode engine serves (Qwen3, Gemma 3: attention layers only;
+    Qwen3.5's DeltaNet layers run through the descriptor path)."""
+    return {k: v for k, v in models().items()
+            if set(v["types"]) <= {"full_attention", "sliding_attention"}}
+
+
 def queue_params():
     """(set name, case) pairs for parametrisation."""
     q = queues()

@@ -19,7 +19,8 @@ def build_lowering(fx: dict, full: bool = False):
     base = dict(Mo.CFG_G3_SMALL, intermediate_size=4608) if fx["base"] == "G3_SMALL_K2" else getattr(Mo, fx["base"])
     cfg = Mo.make_config(base, fx["types"], vocab=fx["vocab"])
     w = Mo.random_weights(cfg, seed=0, embed=True)
-    return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096)
+    return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096,
+                        state_dtype=fx.get("state_dtype", "fp32"))
 
 
 def build_export_lowering(fx: dict):

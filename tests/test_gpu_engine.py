@@ -12,10 +12,10 @@ from tests.model_runs import build_lowering, logits_sha, machine_runner
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("name", sorted(FX.models()))
+@pytest.mark.parametrize("name", sorted(FX.engine_models()))
 def test_engine_batch1_matches_reference_small(name):
     from opentars_b200.engine import DecodeEngine
-    fx = FX.models()[name]
+    fx = FX.engine_models()[name]
     low = build_lowering(fx)
     eng = DecodeEngine(low, batch=1)
     ids, logits = eng.generate([fx["prompt"]], fx["new"], chunk=4)
@@ -25,13 +25,13 @@ def test_engine_batch1_matches_reference_small(name):
 
 
 @pytest.mark.parametrize("batch", [3, 33])
-@pytest.mark.parametrize("name", sorted(FX.models()))
+@pytest.mark.parametrize("name", sorted(FX.engine_models()))
 def test_engine_batch_each_sequence_matches_oracle(name, batch):
     """Prompts decoded together (batch 33: the batched-GEMM path, two row blocks); each sequence
     equals its own single-sequence oracle run."""
     from opentars_b200.engine import DecodeEngine
     from oracle.machine import OracleMachine
-    fx = FX.models()[name]
+    fx = FX.engine_models()[name]
     rng = np.random.default_rng(11)
     P = len(fx["prompt"])
     prompts = [fx["prompt"]] + [list(map(int, rng.integers(0, fx["vocab"], P))) for _ in range(batch - 1)]
@@ -45,12 +45,12 @@ def test_engine_batch_each_sequence_matches_oracle(name, batch):
         assert all(np.array_equal(lg[b].view(np.uint32), ol.view(np.uint32)) for lg, ol in zip(logits, ologits)), b
 
 
-@pytest.mark.parametrize("name", sorted(FX.models()))
+@pytest.mark.parametrize("name", sorted(FX.engine_models()))
 def test_engine_three_launch_attention_matches_fused(name, monkeypatch):
     """TARSCUDA_FUSE_ATTN=0 (q / k norm + RoPE, attention and the output quantiser as three
     launches) and the default single cluster launch give the same tokens and logits bits."""
     from opentars_b200.engine import DecodeEngine
-    fx = FX.models()[name]
+    fx = FX.engine_models()[name]
     rng = np.random.default_rng(5)
     P = len(fx["prompt"])
     prompts = [list(map(int, rng.integers(0, fx["vocab"], P))) for _ in range(5)]

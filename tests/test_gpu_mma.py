@@ -119,7 +119,7 @@ def test_engine_on_tensor_cores_matches_oracle(batch, mma_min_rows):
     from tests import fixtures as FX
     from tests.model_runs import build_lowering, machine_runner
     mma_min_rows(2)
-    for name, fx in sorted(FX.models().items()):
+    for name, fx in sorted(FX.engine_models().items()):
         rng = np.random.default_rng(3)
         P = len(fx["prompt"])
         prompts = [fx["prompt"]] + [list(map(int, rng.integers(0, fx["vocab"], P))) for _ in range(batch - 1)]

@@ -1,5 +1,5 @@
 """Whole-model decode on the GPU against the reference golden model's logits (committed fixtures),
-bit for bit: small Qwen3 / Gemma 3 models through the drop-in Machine and the board backend,
+bit for bit: small Qwen3 / Gemma 3 / Qwen3.5 (fp32 and fp16 DeltaNet state) models through the drop-in Machine and the board backend,
 and the full-size Qwen3-0.6B / Gemma-3-1B shapes (configs 3 and 4) through the board backend."""
 import pytest
 
