@@ -10,8 +10,9 @@ committed fixtures):
     generate                                                                  llm.py:213-836
 Every linear is W8A8 (ROW_QUANT then GEMM QM_ROWCOL) or W4A16; Gemma 3's down projection runs as
 equal K blocks (llm.py:303-321) whose fp32 partials are added by ELT ADD in block order. The
-DeltaNet state may be fp16 (state_dtype, the STATE_FP16 ELT / FDOT forms). MTP speculation and
-Gemma 4 are outside this path.
+DeltaNet state may be fp16 (state_dtype, the STATE_FP16 ELT / FDOT forms). Qwen3.5's MTP head
+(mtp=True: mtp_chunk, two DeltaNet state copies, swap_state, generate_mtp; llm.py:573-612,
+838-886) drafts one token per round for greedy speculative decoding. Gemma 4 is outside this path.
 """
 from __future__ import annotations
 
@@ -199,7 +200,7 @@ class QwenLowering:
 
     def __init__(self, cfg, weights: dict[str, np.ndarray], max_tokens: int, ddr_bytes: int = 1 << 27,
                  head: bool = False, queue_cap: int = 0, scratch_bytes: int = 1 << 22, verify_rows: int = 1,
-                 keep_layers: bool = True, wbits: int = 8, state_dtype: str = "fp32"):
+                 keep_layers: bool = True, wbits: int = 8, state_dtype: str = "fp32", mtp: bool = False):
         if wbits not in (4, 8):
             raise ValueError("wbits must be 4 (W4A16) or 8 (W8A8)")
         if state_dtype not in ("fp32", "fp16"):
@@ -208,7 +209,8 @@ class QwenLowering:
         if mt not in ("qwen3", "gemma3_text", "qwen3_5_text"):
             raise ValueError(f"model type {mt!r}: this lowering covers Qwen3, Gemma 3 and Qwen3.5 text")
         self.state_fmt = C.OUT_FP16 if state_dtype == "fp16" else C.OUT_FP32
-        self.parity, self.spec = 0, False          # the DeltaNet state copy in use (one copy here)
+        self.parity, self.spec = 0, False          # the DeltaNet state copy in use; a verify's last token
+        self.mtp = mtp                             # Qwen3.5's MTP head (weights["mtp.*"])
         self.wbits, self.keep_layers = wbits, keep_layers
         self.cfg, self.w, self.T = cfg, weights, max_tokens
         self.verify_rows = verify_rows
@@ -351,6 +353,12 @@ class QwenLowering:
             for w, t in zip(self.lw, self.types):
                 w["rope"] = t
         self.final_norm = self.gamma1(self.w["norm.weight"])
+        if self.mtp:
+            W = self.w
+            self.mw = dict(self._fa_weights("mtp.layers.0."), fc=self.lin(W["mtp.fc.weight"]),
+                           ge=self.gamma1(W["mtp.pre_fc_norm_embedding.weight"]),
+                           gh=self.gamma1(W["mtp.pre_fc_norm_hidden.weight"]),
+                           norm=self.gamma1(W["mtp.norm.weight"]))
 
         def table(theta: float) -> V:
             """RoPE rows t = cos(t * inv_freq), sin(t * inv_freq) in fp32, as torch computes them."""
@@ -388,10 +396,14 @@ class QwenLowering:
             if t == "linear_attention":
                 # the conv inputs (rows t + hist; the first hist rows are the zero history) and the
                 # DeltaNet state, one [dk, dv] matrix per value head
+                # (two copies with the MTP head: a verify's last token updates the other one)
                 self.st.append(dict(cin={n: p.mat(T + hist, d) for n, d in (("q", kd), ("k", kd), ("v", vd))},
-                                    S=[[p.mat(self.dk, self.dv, self.state_fmt) for _ in range(self.nv)]]))
+                                    S=[[p.mat(self.dk, self.dv, self.state_fmt) for _ in range(self.nv)]
+                                       for _ in range(2 if self.mtp else 1)]))
             else:
                 self.st.append(dict(kc=p.mat(self.Tp, self.nkv * self.hd), vc=p.mat(self.Tp, self.nkv * self.hd)))
+        if self.mtp:                               # the MTP layer's KV cache (row r: token r + 1, hidden r)
+            self.mst = dict(kc=p.mat(self.Tp, self.nkv * self.hd), vc=p.mat(self.Tp, self.nkv * self.hd))
         self.logits = p.mat(self.verify_rows, self.vocab) if self.head else None
 
     def input(self, x: np.ndarray, t0: int = 0) -> None:
@@ -399,10 +411,13 @@ class QwenLowering:
         self.p.ddr[a:a + x.size * 4] = np.asarray(x, F32).tobytes()
 
     # ------------------------------------------------------------------ blocks
-    def chunk(self, t0: int, n: int, all_rows: bool = False) -> None:
+    def chunk(self, t0: int, n: int, all_rows: bool = False, parity: int = 0, spec: bool = False) -> None:
         """Tokens t0 .. t0 + n - 1 through every layer, the final norm and (with the head) the last
-        token's logits (all_rows: every token's)."""
+        token's logits (all_rows: every token's, for a speculative verify). parity: the DeltaNet
+        state copy in use; spec: the last token writes the other copy, so a rejected draft leaves
+        this one as it was after token n - 2 (accepted: the parity flips)."""
         assert not all_rows or n <= self.verify_rows
+        self.parity, self.spec = parity, spec
         p = self.p
         for i, t in enumerate(self.types):
             p.top = self.scratch0                  # this layer's temporaries over the last layer's
@@ -416,6 +431,35 @@ class QwenLowering:
         if self.head:
             r = n if all_rows else 1
             self._head(self.y.rowv(t0 + n - r, r))
+        assert p.top <= self.scratch_end, "scratch_bytes too small for this chunk"
+        p.top = self.end
+
+    def swap_state(self) -> None:
+        """The second DeltaNet state copy into the first (ELT MUL by an exact 1.0), so that plain
+        queues (parity 0) can follow a speculative run."""
+        p = self.p
+        for st, w in zip(self.st, self.lw):
+            if "S" in st:
+                one = replace(w["kscale"], rows=1, cols=1, ld=4)
+                for a, b in zip(st["S"][1], st["S"][0]):
+                    p.elt(C.ELT_MUL, a, one, b, bmode=C.BM_SCALAR)
+
+    def mtp_chunk(self, r0: int, n: int, head: bool = True) -> None:
+        """MTP rows r0 .. r0 + n - 1 (row r: the embedding of token r + 1 and the hidden state of
+        position r, predicting token r + 2): fc over the two norms, one gated full-attention layer
+        with its own KV cache, the norm and (head) the last row's logits on the tied head."""
+        p, w, H = self.p, self.mw, self.H
+        p.top = self.scratch0
+        cat = p.mat(n, 2 * H)
+        p.norm(self.x0.rowv(r0 + 1, n), w["ge"], self.eps, cat.colv(0, H))
+        p.norm(self.y.rowv(r0, n), w["gh"], self.eps, cat.colv(H, H))
+        x, out = p.mat(n, H), p.mat(n, H)
+        self.linear(cat, w["fc"], x)
+        self._fa_block(w, self.mst, x, out, r0, n)
+        if head:
+            y = p.mat(1, H)
+            p.norm(out.rowv(n - 1, 1), w["norm"], self.eps, y)
+            self._head(y)
         assert p.top <= self.scratch_end, "scratch_bytes too small for this chunk"
         p.top = self.end
 
@@ -501,8 +545,9 @@ class QwenLowering:
         for t in range(n):
             for hh in range(self.nv):
                 r = t * self.nv + hh
+                # the decay pass reads the state in use; a verify's last token writes the other copy
                 S0 = st["S"][self.parity][hh]
-                S = S0
+                S = st["S"][1 - self.parity][hh] if self.spec and t == n - 1 else S0
                 p.elt(C.ELT_MUL, S0, decay.rowv(t, 1).colv(hh, 1), S, bmode=C.BM_SCALAR)
                 p.fdot(kh.rowv(r, 1), S, kvm, nn=True)
                 p.elt(C.ELT_SUB, vh.rowv(r, 1), kvm, dl)
@@ -615,3 +660,53 @@ class QwenLowering:
                 counts.append(cnt)
                 ids.append(int(np.argmax(lg)))
         return ids, logits, counts
+
+    def generate_mtp(self, run, prompt, n_new: int, oracle=None):
+        """Greedy speculative decoding with the MTP head: the tokens of generate(). Each round
+        verifies [current, draft] as two rows; a hit emits two tokens and flips the state copy, a
+        miss emits the correction and keeps it; the MTP then takes the rows the verify made known
+        and drafts the next token. oracle(t, draft) may replace a draft (tests). Returns (token ids,
+        {position: its logits}, rounds)."""
+        assert self.head and self.mtp and self.verify_rows >= 2
+        state = dict(ddr=self.p.ddr)
+
+        def go(emit) -> None:
+            a = len(self.p.descs)
+            emit()
+            q, c = self.stage(state["ddr"], a, len(self.p.descs))
+            out = run(state["ddr"], q, c)
+            state["ddr"] = out if isinstance(out, bytearray) else bytearray(out)
+
+        def put(t: int, toks) -> None:
+            self.put_input(state["ddr"], t, self.embed(toks))
+        ids, P, par, rounds = list(prompt), len(prompt), 0, 0
+        put(0, ids)
+        go(lambda: self.chunk(0, P))
+        lg = {P - 1: self.logits_of(state["ddr"])}
+        ids.append(int(np.argmax(lg[P - 1])))
+        put(P, ids[P:])
+        go(lambda: self.mtp_chunk(0, P))                    # rows 0 .. P - 1; the last one drafts
+        t = P                                               # ids[t]: known, not yet in the cache
+        while len(ids) < P + n_new + 1:
+            d = int(np.argmax(self.logits_of(state["ddr"])))
+            if oracle is not None:
+                d = oracle(t, d)
+            put(t + 1, [d])
+            go(lambda: self.chunk(t, 2, all_rows=True, parity=par, spec=True))
+            rows = self.logits_rows(state["ddr"], 2)
+            rounds += 1
+            lg[t] = rows[0]
+            x = int(np.argmax(rows[0]))
+            ids.append(x)
+            if x == d:
+                lg[t + 1] = rows[1]
+                ids.append(int(np.argmax(rows[1])))
+                par = 1 - par
+                put(t + 2, ids[t + 2:t + 3])
+                go(lambda: self.mtp_chunk(t, 2))
+                t += 2
+            else:
+                put(t + 1, [x])
+                go(lambda: self.mtp_chunk(t, 1))
+                t += 1
+        return ids, lg, rounds

@@ -125,6 +125,22 @@ def random_weights(cfg, seed: int = 0, embed: bool = False) -> dict[str, np.ndar
     return w
 
 
+def random_mtp(cfg, seed: int = 5) -> dict[str, np.ndarray]:
+    """Random Qwen3.5 MTP-head weights (qwen_ref.py:258-270): the linears N(0, 0.02) and the norms
+    N(0, 0.1), drawn in this order, under the checkpoint's names (mtp.*)."""
+    rng = np.random.default_rng(seed)
+    H, I, hd = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    nq, nkv = cfg.num_attention_heads * hd, cfg.num_key_value_heads * hd
+    lin = {"fc": (H, 2 * H), "layers.0.self_attn.q_proj": (2 * nq, H), "layers.0.self_attn.k_proj": (nkv, H),
+           "layers.0.self_attn.v_proj": (nkv, H), "layers.0.self_attn.o_proj": (H, nq),
+           "layers.0.mlp.gate_proj": (I, H), "layers.0.mlp.up_proj": (I, H), "layers.0.mlp.down_proj": (H, I)}
+    nrm = {"norm": H, "pre_fc_norm_embedding": H, "pre_fc_norm_hidden": H, "layers.0.input_layernorm": H,
+           "layers.0.post_attention_layernorm": H, "layers.0.self_attn.q_norm": hd, "layers.0.self_attn.k_norm": hd}
+    w = {f"mtp.{k}.weight": rng.normal(0, 0.02, s).astype(np.float32) for k, s in lin.items()}
+    w.update({f"mtp.{k}.weight": rng.normal(0, 0.1, n).astype(np.float32) for k, n in nrm.items()})
+    return w
+
+
 def head_rows(vocab: int) -> int:
     for b in range(1, vocab // 16 + 1):
         r = vocab // b

@@ -9,6 +9,8 @@ What it stores (all small):
                    end status, ContractError flag, per-descriptor stats and the SHA-256 of the
                    whole DDR image after the run
   numerics.npz     seeded inputs' output bits from the reference's numerics.py functions
+  mtp.json         (--models) Qwen3.5 with the MTP head: speculative decoding's queues, tokens,
+                   verified logits and rounds on the reference's lowering and golden Machine
   models.json      (--models) per-step logits SHA-256 / argmax of the reference's QwenLowering
                    + golden Machine greedy decode for small Qwen3 / Gemma-3 configs, and the
                    SHA-256 of the lowered DDR image and queue bytes
@@ -207,6 +209,51 @@ def make_models(ref: str):
     return out
 
 
+# name, layer types, vocab, max_tokens, prompt, new tokens, DeltaNet state dtype
+MTP_CASES = [
+    ("qwen35_mtp", ["linear_attention"] * 3 + ["full_attention"], 4096, 48, [5, 77, 901, 12, 3000], 8, "fp32"),
+    ("qwen35_mtp_fp16", ["linear_attention"] * 3 + ["full_attention"], 4096, 48, [5, 77, 901, 12, 3000], 8, "fp16"),
+]
+def make_mtp(ref: str):
+    """Qwen3.5 with the MTP head on the reference's lowering and golden Machine: plain greedy decode,
+    then greedy speculative decode with drafts forced to hit or miss (mtp_oracle); the queues, the
+    tokens, every verified position's logits, the round count, and swap_state's queue."""
+    import tars_mini.qwen_ref as Q
+    from tars_mini import golden as G
+    from tars_mini.llm import QwenLowering
+
+    from tests.model_runs import mtp_oracle
+    out = {}
+    for name, types, vocab, T, prompt, new, state_dtype in MTP_CASES:
+        cfg = Q.make_config(Q.CFG_SMALL, types, vocab=vocab)
+        w = {**Q.random_weights(cfg, embed=True), **Q.random_mtp(cfg)}
+
+        def mk(**k):
+            return QwenLowering(cfg, w, max_tokens=T, ddr_bytes=1 << 25, head=True, queue_cap=8192,
+                                state_dtype=state_dtype, **k)
+        queues = []
+
+        def run(ddr, q, n):
+            queues.append(hashlib.sha256(bytes(ddr[q:q + 64 * n])).hexdigest())
+            m = G.Machine(ddr)
+            assert m.run_queue(q, n).done
+            return m.ddr
+        plain_ids, _, _ = mk().generate(run, prompt, new)
+        queues.clear()
+        low = mk(verify_rows=2, mtp=True)
+        image_sha = hashlib.sha256(bytes(low.p.ddr)).hexdigest()
+        ids, lg, rounds = low.generate_mtp(run, prompt, new, mtp_oracle(plain_ids, vocab))
+        a = len(low.p.descs)
+        low.swap_state()
+        swap = b"".join(bytes(d) for d in low.p.descs[a:])
+        out[name] = dict(types=types, vocab=vocab, T=T, prompt=prompt, new=new, state_dtype=state_dtype,
+                         plain_ids=plain_ids, image_sha256=image_sha, queue_sha256=queues, ids=ids, rounds=rounds,
+                         logits_sha256={str(k): hashlib.sha256(v.astype("<f4").tobytes()).hexdigest()
+                                        for k, v in sorted(lg.items())},
+                         swap_sha256=hashlib.sha256(swap).hexdigest())
+    return out
+
+
 # name, base config, layer types (None: the model's own), prompt seed, new tokens, prefill chunk
 FULL_CASES = [
     ("qwen3_0.6b", "CFG_Q3_06B", None, "VOCAB_Q3_06B", 0, 3, 4),
@@ -297,6 +344,7 @@ def main():
     if a.models:
         m = make_models(a.ref)
         (HERE / "models.json").write_text(json.dumps(m, indent=1))
+        (HERE / "mtp.json").write_text(json.dumps(make_mtp(a.ref), indent=1))
         print(f"models in {time.time() - t:.1f}s")
     if a.full:
         path = HERE / "full_models.json"

@@ -60,6 +60,45 @@ class OracleDevice:
         return st.done, st.err_code, st.op_idx, 0
 
 
+def mtp_oracle(plain_ids: list[int], vocab: int, seed: int = 2):
+    """The draft replacement of the speculative tests: each draft at random the right token (plain
+    decoding's next token) or a wrong one, so rounds both hit and miss."""
+    rng = np.random.default_rng(seed)
+
+    def oracle(t, d):
+        right = rng.random() < 0.5 and t + 1 < len(plain_ids)
+        return plain_ids[t + 1] if right else (plain_ids[min(t + 1, len(plain_ids) - 1)] + 1) % vocab
+    return oracle
+
+
+def build_mtp_lowering(fx: dict, **kw):
+    """A tests/golden/mtp.json case's Qwen3.5 model (with the MTP head weights)."""
+    from opentars_b200 import models as Mo
+    from opentars_b200.lowering import QwenLowering
+    cfg = Mo.make_config(Mo.CFG_Q35_SMALL, fx["types"], vocab=fx["vocab"])
+    w = {**Mo.random_weights(cfg, embed=True), **Mo.random_mtp(cfg)}
+    return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 25, head=True, queue_cap=8192,
+                        state_dtype=fx["state_dtype"], **kw)
+
+
+def check_mtp(fx: dict, machine_cls) -> None:
+    """Speculative decoding through machine_cls against the reference's run (mtp.json): the image,
+    every queue, the tokens (those of plain decoding), every verified position's logits, the
+    rounds and swap_state's queue."""
+    low = build_mtp_lowering(fx, verify_rows=2, mtp=True)
+    assert sha(low.p.ddr) == fx["image_sha256"]
+    queues = []
+    ids, lg, rounds = low.generate_mtp(machine_runner(machine_cls, queues, gemv_only=False), fx["prompt"],
+                                       fx["new"], mtp_oracle(fx["plain_ids"], fx["vocab"]))
+    assert queues == fx["queue_sha256"]
+    assert ids == fx["ids"] and ids == fx["plain_ids"][:len(ids)]
+    assert rounds == fx["rounds"]
+    assert {str(k): logits_sha(v) for k, v in sorted(lg.items())} == fx["logits_sha256"]
+    a = len(low.p.descs)
+    low.swap_state()
+    assert sha(b"".join(bytes(d) for d in low.p.descs[a:])) == fx["swap_sha256"]
+
+
 def sha(a) -> str:
     return hashlib.sha256(bytes(a)).hexdigest()
 

@@ -33,6 +33,17 @@ def test_small_models_through_board_backend(name):
     run.dev.close()
 
 
+@pytest.mark.parametrize("name", ["qwen35_mtp", "qwen35_mtp_fp16"])
+def test_mtp_speculative_decoding_through_drop_in_machine(name):
+    """Qwen3.5 with the MTP head (tests/golden/mtp.json): speculative decoding on the GPU gives the
+    reference's queues, tokens, verified logits and rounds, bit for bit."""
+    import json
+
+    from opentars_b200.machine import Machine
+    from tests.model_runs import check_mtp
+    check_mtp(json.loads((FX.GOLDEN / "mtp.json").read_text())[name], Machine)
+
+
 def _full():
     import json
     p = FX.GOLDEN / "full_models.json"

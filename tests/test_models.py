@@ -1,11 +1,15 @@
 """The package's lowering (opentars_b200.lowering) against the reference's own lowering + golden
 model (committed fixtures): identical DDR image, identical descriptor queues, identical logits,
 run here through the CPU oracle."""
+import json
+
 import numpy as np
 import pytest
 
 from tests import fixtures as FX
-from tests.model_runs import build_lowering, logits_sha, machine_runner, sha
+from tests.model_runs import build_lowering, check_mtp, logits_sha, machine_runner, sha
+
+MTP = json.loads((FX.GOLDEN / "mtp.json").read_text())
 
 
 @pytest.mark.parametrize("name", sorted(FX.models()))
@@ -31,3 +35,11 @@ def test_chunked_prefill_equals_whole_prompt_logits():
     ids2, lg2, _ = b.generate(machine_runner(OracleMachine, []), fx["prompt"], 2, chunk=4)
     assert ids1 == ids2
     assert all(np.array_equal(x.view(np.uint32), y.view(np.uint32)) for x, y in zip(lg1, lg2))
+
+
+@pytest.mark.parametrize("name", sorted(MTP))
+def test_mtp_speculative_decoding_matches_reference(name):
+    """Qwen3.5 with the MTP head, drafts forced to hit and miss: the reference's queues, tokens
+    (plain decoding's), verified logits, rounds and swap_state queue, through the CPU oracle."""
+    from oracle.machine import OracleMachine
+    check_mtp(MTP[name], OracleMachine)
