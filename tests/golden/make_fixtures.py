@@ -9,6 +9,8 @@ What it stores (all small):
                    end status, ContractError flag, per-descriptor stats and the SHA-256 of the
                    whole DDR image after the run
   numerics.npz     seeded inputs' output bits from the reference's numerics.py functions
+  vision.json      (--models) the small Qwen3.5 vision tower on the reference's VisionLowering and
+                   golden Machine: built image, queue and output per test image
   mtp.json         (--models) Qwen3.5 with the MTP head: speculative decoding's queues, tokens,
                    verified logits and rounds on the reference's lowering and golden Machine
   models.json      (--models) per-step logits SHA-256 / argmax of the reference's QwenLowering
@@ -254,6 +256,46 @@ def make_mtp(ref: str):
     return out
 
 
+VIT_SMALL = dict(depth=2, hidden_size=64, intermediate_size=256, num_heads=2, patch_size=4,
+                 spatial_merge_size=2, temporal_patch_size=2, out_hidden_size=48, num_position_embeddings=36)
+VIT_IMAGES = (8, 32, 64)             # sides: 4, 64 and 256 patches
+
+
+def vit_image(size: int, seed: int = 3) -> np.ndarray:
+    """A normalised test image [3, size, size]: smooth gradients plus noise."""
+    rng = np.random.default_rng(seed)
+    yy, xx = np.meshgrid(np.arange(size), np.arange(size), indexing="ij")
+    base = (np.sin(xx / 3.0) + np.cos(yy / 5.0))[:, :, None] / 2.0 + rng.normal(0, 0.3, (size, size, 3))
+    return np.ascontiguousarray(base.transpose(2, 0, 1), np.float32)
+
+
+def make_vision(ref: str):
+    """The small Qwen3.5 vision tower on the reference's VisionLowering and golden Machine, per test
+    image: the built image and queue, the merged tokens and the hidden state after one block. The
+    patches, position rows and rotary rows come from opentars_b200.vision (the reference's host
+    helpers need a newer transformers than this one; tests/test_vision.py pins ours to the
+    installed tower's own computations)."""
+    from tars_mini import qwen_vit as RV
+
+    from opentars_b200 import vision as OV
+    cfg = RV.vision_config(**VIT_SMALL)
+    w = RV.random_vision(cfg, seed=0)
+    out = {}
+    for size in VIT_IMAGES:
+        px, grid = OV.patchify(vit_image(size), cfg)
+        pos, rope = OV.position_embeddings(cfg, w, grid), OV.rope_table(cfg, grid)
+        low = RV.VisionLowering(cfg, w, patches_max=len(px), ddr_bytes=1 << 23)
+        one = low.run(px, pos, rope, blocks=1)
+        tokens = low.run(px, pos, rope)
+        ddr, q, n = low.p.build()
+        out[str(size)] = dict(patches=len(px), host_sha256=hashlib.sha256(px.tobytes() + pos.tobytes()
+                                                                          + rope.tobytes()).hexdigest(),
+                              image_sha256=hashlib.sha256(bytes(ddr)).hexdigest(), queue=[q, n],
+                              tokens_sha256=hashlib.sha256(tokens.astype("<f4").tobytes()).hexdigest(),
+                              block1_sha256=hashlib.sha256(one.astype("<f4").tobytes()).hexdigest())
+    return dict(config=VIT_SMALL, seed=0, images=out)
+
+
 # name, base config, layer types (None: the model's own), prompt seed, new tokens, prefill chunk
 FULL_CASES = [
     ("qwen3_0.6b", "CFG_Q3_06B", None, "VOCAB_Q3_06B", 0, 3, 4),
@@ -345,6 +387,7 @@ def main():
         m = make_models(a.ref)
         (HERE / "models.json").write_text(json.dumps(m, indent=1))
         (HERE / "mtp.json").write_text(json.dumps(make_mtp(a.ref), indent=1))
+        (HERE / "vision.json").write_text(json.dumps(make_vision(a.ref), indent=1))
         print(f"models in {time.time() - t:.1f}s")
     if a.full:
         path = HERE / "full_models.json"
