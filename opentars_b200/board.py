@@ -144,13 +144,14 @@ class Qwen:
         dev = Cuda(manifest_mem(data)); model = Qwen(dev, data)
         logits = model.prefill(prompt_ids); logits = model.step(token)
 
-    Exports with speculative-decoding queues or Gemma 4 per-layer embeddings are refused."""
+    Gemma 4 exports add the per-layer token table (ple_bf16.bin). Exports with speculative-decoding
+    queues are refused."""
 
     def __init__(self, dev, data, log=print):
         self.dev, self.d = dev, Path(data)
         m = json.loads((self.d / "manifest.json").read_text())
-        if m.get("ple_cols") or m.get("spec"):
-            raise ValueError(f"{self.d}: per-layer embeddings / speculative queues are not supported")
+        if m.get("spec"):
+            raise ValueError(f"{self.d}: speculative-decoding queues are not supported")
         self.m = m
         self.T, self.H, self.vocab = int(m["max_tokens"]), int(m["hidden"]), int(m["vocab"])
         t = time.time()
@@ -183,6 +184,10 @@ class Qwen:
                                        {int(t0): (int(o), int(k)) for t0, o, k in index})
         s = m.get("embed_scale")
         self.embed_scale = None if s is None else np.float32(s)
+        self.ple_cols = int(m.get("ple_cols", 0))         # Gemma 4: per-layer token rows
+        self.ple = np.memmap(self.d / "ple_bf16.bin", np.uint16, "r", shape=(self.vocab, self.ple_cols)) \
+            if self.ple_cols else None
+        self.ple_scale = np.float32(m["ple_scale"]) if self.ple_cols else None
         self.bos = [int(v) for v in m.get("bos_ids", [])]
         self.turn_end = m.get("turn_end", "<|im_end|>\n")
         self.cycles = 0
@@ -210,7 +215,8 @@ class Qwen:
 
     def _put(self, t: int, tokens) -> None:
         """The input rows t, t + 1, ...: each token's bf16 embedding widened exactly (Gemma: times
-        the manifest's fp32 embed_scale)."""
+        the manifest's fp32 embed_scale); Gemma 4 also writes the token's per-layer row (bf16
+        widened, times ple_scale) at ple0 (tars_board.py:298-314)."""
         if t + len(tokens) > self.T:
             raise OverflowError(f"context full ({self.T} tokens)")
         x0, ld = int(self.m["x0_off"]), int(self.m["x0_ld"])
@@ -221,6 +227,11 @@ class Qwen:
             a = x0 + (t + i) * ld
             self.dev.mem[a:a + 4 * self.H] = np.frombuffer(np.asarray(x, "<f4").tobytes(), np.uint8)
             self.dev.to_dev(a, 4 * self.H)
+            if self.ple is not None:
+                pr = (self.ple[int(token)].astype(np.uint32) << 16).view(np.float32) * self.ple_scale
+                pa = int(self.m["ple0_off"]) + (t + i) * int(self.m["ple0_ld"])
+                self.dev.mem[pa:pa + 4 * self.ple_cols] = np.frombuffer(np.asarray(pr, "<f4").tobytes(), np.uint8)
+                self.dev.to_dev(pa, 4 * self.ple_cols)
 
     def _run(self, queues, off: int, n: int, what: str) -> int:
         q, cap, cyc = int(self.m["qbase"]), int(self.m["queue_cap"]), 0

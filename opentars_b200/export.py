@@ -1,9 +1,11 @@
 """Writes a model lowered by QwenLowering as a board export directory - the file set that
-tools/export_kv260.py:14-33 describes and tars_board.py:212-435 (and board.Qwen) reads:
+tools/export_kv260.py:14-33 describes (the PLE fields: 234-237) and tars_board.py:212-435 (and board.Qwen) reads:
 
     image.bin        the DDR image from address 0: the zeroed state, the queue region, scratch,
                      the quantised weights
     embed_bf16.bin   the embedding table [vocab, H] as bf16 (the table must be bf16-exact)
+    ple_bf16.bin     Gemma 4: the per-layer token table [vocab, L * ple_dim] as bf16 (bf16-exact),
+                     scaled on the host by the manifest's ple_scale
     queues.bin       one descriptor queue per token position t (t0 = t, one token), back to back
     queues_c<n>.bin  prefill: one queue per chunk of n tokens at t0 = 0, align, 2 align, ...
     manifest.json    the addresses and sizes the runtime needs and the queue indexes
@@ -49,6 +51,12 @@ def write_export(low, out, chunks=(4,), align: int = 4, bos_ids=(), eos_ids=(), 
     if (bits & 0xFFFF).any():
         raise ValueError("the embedding table is not bf16-exact (round it with bf16_exact first)")
     (bits >> 16).astype("<u2").tofile(out / "embed_bf16.bin")
+    if low.ple_dim:
+        ple = np.ascontiguousarray(low.w["embed_tokens_per_layer.weight"], np.float32)
+        pbits = ple.view(np.uint32)
+        if (pbits & 0xFFFF).any():
+            raise ValueError("the per-layer embedding table is not bf16-exact (round it with bf16_exact first)")
+        (pbits >> 16).astype("<u2").tofile(out / "ple_bf16.bin")
 
     def queue(t0: int, n: int) -> tuple[bytes, int]:
         a = len(p.descs)
@@ -85,5 +93,10 @@ def write_export(low, out, chunks=(4,), align: int = 4, bos_ids=(), eos_ids=(), 
         chat_prefix=chat_prefix, chat_suffix=chat_suffix)
     if low.gemma:
         m["embed_scale"] = float(np.float32(low.H ** 0.5))
+    if low.ple_dim:
+        from .models import ple_embedding
+        m.update(ple_cols=len(low.types) * low.ple_dim,
+                 ple_scale=float(ple_embedding(low.cfg, np.ones((1, 1), np.float32))[0, 0]),
+                 ple0_off=int(low.ple0.off), ple0_ld=int(low.ple0.ld))
     (out / "manifest.json").write_text(json.dumps(m))
     return m

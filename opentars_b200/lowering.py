@@ -1,4 +1,5 @@
-"""The step driver: Qwen3 / Gemma 3 / Qwen3.5 text models lowered to tars_mini v0.4 descriptors.
+"""The step driver: Qwen3 / Gemma 3 / Gemma 4 / Qwen3.5 text models lowered to tars_mini v0.4
+descriptors.
 
 Restates, for the families on the hot path, the reference's program builder and LLM lowering so
 that the same DDR image and the same descriptor queues come out byte for byte (pinned by the
@@ -12,7 +13,9 @@ Every linear is W8A8 (ROW_QUANT then GEMM QM_ROWCOL) or W4A16; Gemma 3's down pr
 equal K blocks (llm.py:303-321) whose fp32 partials are added by ELT ADD in block order. The
 DeltaNet state may be fp16 (state_dtype, the STATE_FP16 ELT / FDOT forms). Qwen3.5's MTP head
 (mtp=True: mtp_chunk, two DeltaNet state copies, swap_state, generate_mtp; llm.py:573-612,
-838-886) drafts one token per round for greedy speculative decoding. Gemma 4 is outside this path.
+838-886) drafts one token per round for greedy speculative decoding. Gemma 4 (per-type head dims,
+proportional RoPE, KV sharing, V norm, per-layer embeddings, layer_scalar, the softcapped head)
+follows llm.py's gemma4 paths.
 """
 from __future__ import annotations
 
@@ -21,7 +24,7 @@ from dataclasses import dataclass, replace
 import numpy as np
 
 from . import contract as C
-from .models import head_rows, input_embedding, quantize_weight, quantize_weight4
+from .models import head_rows, input_embedding, ple_embedding, quantize_weight, quantize_weight4
 
 F32 = np.float32
 ALIGN = 128
@@ -206,8 +209,8 @@ class QwenLowering:
         if state_dtype not in ("fp32", "fp16"):
             raise ValueError("state_dtype must be fp32 or fp16")
         mt = getattr(cfg, "model_type", "")
-        if mt not in ("qwen3", "gemma3_text", "qwen3_5_text"):
-            raise ValueError(f"model type {mt!r}: this lowering covers Qwen3, Gemma 3 and Qwen3.5 text")
+        if mt not in ("qwen3", "gemma3_text", "gemma4_text", "qwen3_5_text"):
+            raise ValueError(f"model type {mt!r}: this lowering covers Qwen3, Gemma 3 / 4 and Qwen3.5 text")
         self.state_fmt = C.OUT_FP16 if state_dtype == "fp16" else C.OUT_FP32
         self.parity, self.spec = 0, False          # the DeltaNet state copy in use; a verify's last token
         self.mtp = mtp                             # Qwen3.5's MTP head (weights["mtp.*"])
@@ -218,11 +221,19 @@ class QwenLowering:
         self.H, self.eps = cfg.hidden_size, cfg.rms_norm_eps
         self.q3 = mt == "qwen3"
         self.gemma = mt == "gemma3_text"
+        self.gemma4 = mt == "gemma4_text"
         self.types = list(cfg.layer_types)
         if self.gemma:
             assert set(self.types) <= {"sliding_attention", "full_attention"}
             assert cfg.attn_logit_softcapping is None and cfg.final_logit_softcapping is None
             assert cfg.hidden_activation == "gelu_pytorch_tanh"
+            assert max_tokens <= cfg.sliding_window, "the context must fit the sliding window"
+        elif self.gemma4:
+            assert set(self.types) <= {"sliding_attention", "full_attention"}
+            assert getattr(cfg, "attn_logit_softcapping", None) is None
+            assert cfg.hidden_activation == "gelu_pytorch_tanh"
+            assert not getattr(cfg, "enable_moe_block", False) and not getattr(cfg, "attention_k_eq_v", False)
+            assert getattr(cfg, "num_global_key_value_heads", None) in (None, cfg.num_key_value_heads)
             assert max_tokens <= cfg.sliding_window, "the context must fit the sliding window"
         elif self.q3:
             assert set(self.types) == {"full_attention"}
@@ -232,9 +243,27 @@ class QwenLowering:
         self.nk, self.nv = getattr(cfg, "linear_num_key_heads", 0), getattr(cfg, "linear_num_value_heads", 0)
         self.dk, self.dv = getattr(cfg, "linear_key_head_dim", 0), getattr(cfg, "linear_value_head_dim", 0)
         assert self.nk == self.nv, "the GQA repeat of linear attention is not lowered"
-        self.nh, self.nkv, self.hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
-        self.rot = self.hd if self.gemma else int(self.hd * cfg.rope_parameters.get("partial_rotary_factor", 1.0))
-        self.qmul = cfg.query_pre_attn_scalar ** -0.5 if self.gemma else self.hd ** -0.5
+        self.nh, self.nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        if self.gemma4:
+            # head dims per layer type: a config's per-layer table where it has one, else head_dim for
+            # sliding and global_head_dim for full layers (the model's own parameter shapes)
+            plc = getattr(cfg, "per_layer_config", None)
+            dims = [plc[i].head_dim if plc else (getattr(cfg, "global_head_dim", None) or cfg.head_dim)
+                    if t == "full_attention" else cfg.head_dim for i, t in enumerate(self.types)]
+            by_type = dict(zip(self.types, dims))
+            assert all(by_type[t] == d for t, d in zip(self.types, dims))
+            assert not plc or all(p.num_key_value_heads == self.nkv for p in plc)
+            self.hd = by_type.get("sliding_attention", by_type["full_attention"])
+            self.ghd = by_type.get("full_attention", self.hd)
+        else:
+            self.hd = self.ghd = cfg.head_dim
+        self.ple_dim = (getattr(cfg, "hidden_size_per_layer_input", 0) or 0) if self.gemma4 else 0
+        self.first_kv_shared = len(self.types) - (getattr(cfg, "num_kv_shared_layers", 0) if self.gemma4 else 0)
+        self.softcap = getattr(cfg, "final_logit_softcapping", None) if self.gemma4 else None
+        self.rot = self.hd if (self.gemma or self.gemma4) \
+            else int(self.hd * cfg.rope_parameters.get("partial_rotary_factor", 1.0))
+        # the attention scaling, folded into q_norm's gamma (Gemma 4: scaling 1.0)
+        self.qmul = 1.0 if self.gemma4 else (cfg.query_pre_attn_scalar ** -0.5 if self.gemma else self.hd ** -0.5)
         self.Tp = pad16(max_tokens)
         self.head = head
         self.taps = getattr(cfg, "linear_conv_kernel_dim", 4)
@@ -275,10 +304,13 @@ class QwenLowering:
         return [QLin(self.p.put(np.ascontiguousarray(qw.q[:, c:c + kb]), "i1"), s, None, qw.n, kb)
                 for c in range(0, qw.k, kb)]
 
+    def _layer_hd(self, t: str) -> int:
+        return self.ghd if (self.gemma4 and t == "full_attention") else self.hd
+
     def gamma1(self, w: np.ndarray, mul: float = 1.0) -> V:
-        """Qwen3: the RMSNorm weight itself; Gemma 3 and Qwen3.5 (zero-centred weights): fp32(1 + w).
-        Times `mul` (the attention scaling folded into q_norm)."""
-        g = np.asarray(w, F32) if self.q3 else (F32(1.0) + np.asarray(w, F32)).astype(F32)
+        """Qwen3 / Gemma 4: the RMSNorm weight itself; Gemma 3 and Qwen3.5 (zero-centred weights):
+        fp32(1 + w). Times `mul` (the attention scaling folded into q_norm)."""
+        g = np.asarray(w, F32) if (self.q3 or self.gemma4) else (F32(1.0) + np.asarray(w, F32)).astype(F32)
         return self.p.const((g * F32(mul)).astype(F32))
 
     def linear(self, x: V, w: QLin, y: V, act: int = C.ACT_NONE, qs: tuple[V, int] | None = None) -> None:
@@ -315,9 +347,33 @@ class QwenLowering:
                      for n, o, dd in (("q", 0, kd), ("k", kd, kd), ("v", 2 * kd, vd))}
         return d
 
-    def _fa_weights(self, A: str) -> dict:
+    def _fa_weights(self, A: str, li: int | None = None) -> dict:
         W = self.w
         sa = A + "self_attn."
+        if self.gemma4:
+            t = self.types[li]
+            hd = self._layer_hd(t)
+            shared = li >= self.first_kv_shared
+            g1 = lambda n, mul=1.0: self.gamma1(W[A + n + ".weight"], mul)  # noqa: E731
+            d = dict(
+                hd=hd, rot=hd, rope=t, kv_shared=shared,
+                ln_in=g1("input_layernorm"), attn_norm=g1("post_attention_layernorm"),
+                ln_post=g1("pre_feedforward_layernorm"), mlp_norm=g1("post_feedforward_layernorm"),
+                q=self.lin(W[sa + "q_proj.weight"]), g=None,
+                k=None if shared else self.lin(W[sa + "k_proj.weight"]),
+                v=None if shared else self.lin(W[sa + "v_proj.weight"]),
+                qn=g1("self_attn.q_norm", self.qmul),
+                kn=None if shared else g1("self_attn.k_norm"),
+                vn=None if shared else self.p.const(np.ones(hd, F32)),       # V RMSNorm without scale
+                o=self.lin_k(W[sa + "o_proj.weight"]),
+                gate=self.lin(W[A + "mlp.gate_proj.weight"]), up=self.lin(W[A + "mlp.up_proj.weight"]),
+                down=self.lin_k(W[A + "mlp.down_proj.weight"]),
+                layer_scalar=self.p.const(W[A + "layer_scalar"]))
+            if self.ple_dim:
+                d.update(ple_gate=self.lin(W[A + "per_layer_input_gate.weight"]),
+                         ple_proj=self.lin(W[A + "per_layer_projection.weight"]),
+                         ple_norm=g1("post_per_layer_input_norm"))
+            return d
         if self.gemma:
             g1 = lambda n, mul=1.0: self.gamma1(W[A + n + ".weight"], mul)  # noqa: E731
             return dict(
@@ -347,11 +403,17 @@ class QwenLowering:
     def _weights(self) -> None:
         p = self.p
         self.taps = 4
-        self.lw = [self._la_weights(f"layers.{i}.") if t == "linear_attention" else self._fa_weights(f"layers.{i}.")
+        self.lw = [self._la_weights(f"layers.{i}.") if t == "linear_attention" else self._fa_weights(f"layers.{i}.", i)
                    for i, t in enumerate(self.types)]
         if self.gemma:
             for w, t in zip(self.lw, self.types):
                 w["rope"] = t
+        if self.ple_dim:
+            self.ple_w = dict(
+                model_proj=self.lin(self.w["per_layer_model_projection.weight"]),
+                proj_scale=p.const(np.array([F32(self.H ** -0.5)], F32)),
+                proj_norm=self.gamma1(self.w["per_layer_projection_norm.weight"]),
+                in_scale=p.const(np.array([F32(2.0 ** -0.5)], F32)))
         self.final_norm = self.gamma1(self.w["norm.weight"])
         if self.mtp:
             W = self.w
@@ -366,10 +428,31 @@ class QwenLowering:
             inv = (1.0 / (th ** (np.arange(0, self.rot, 2, dtype=F32) / F32(self.rot)))).astype(F32)
             fr = (np.arange(self.T, dtype=F32)[:, None] * inv[None, :]).astype(F32)
             return p.const(np.concatenate([np.cos(fr), np.sin(fr)], axis=1).astype(F32))
-        if self.gemma:
+        if self.gemma4:
+            # per layer type, over that type's head dim: default RoPE, or proportional (only the
+            # first partial_rotary_factor of the angles rotate; the rest have frequency 0)
+            self.rope_tabs = {}
+            for t in sorted(set(self.types)):
+                hd = self._layer_hd(t)
+                rp = self.cfg.rope_parameters[t]
+                th = F32(rp["rope_theta"])
+                rt = rp.get("rope_type", "default")
+                assert rt in ("default", "proportional")
+                prop = rp.get("partial_rotary_factor", 1.0) if rt == "proportional" else 1.0
+                ang = int(prop * hd // 2)
+                inv = np.zeros(hd // 2, F32)
+                inv[:ang] = (1.0 / (th ** (np.arange(0, 2 * ang, 2, dtype=F32) / F32(hd)))).astype(F32)
+                fr = (np.arange(self.T, dtype=F32)[:, None] * inv[None, :]).astype(F32)
+                self.rope_tabs[t] = p.const(np.concatenate([np.cos(fr), np.sin(fr)], axis=1).astype(F32))
+        elif self.gemma:
             self.rope_tabs = {t: table(self.cfg.rope_parameters[t]["rope_theta"]) for t in sorted(set(self.types))}
         else:
             self.rope_tab = table(self.cfg.rope_parameters["rope_theta"])
+        if self.softcap is not None:
+            sc = float(self.softcap)
+            self.sc_inv2 = p.const(np.array([F32(2.0 / sc)], F32))
+            self.sc_two = p.const(np.array([F32(2.0 * sc)], F32))
+            self.sc_val = p.const(np.array([F32(sc)], F32))
         self.head_lins = []
         if self.head:
             e = self.w["embed_tokens.weight"]
@@ -389,10 +472,17 @@ class QwenLowering:
             self.x0 = p.mat(T, H)
             xb0, xb1 = p.mat(T, H), p.mat(T, H)
             self.xs = [self.x0] + [xb0 if i % 2 == 0 else xb1 for i in range(len(self.types))]
+        if self.ple_dim:
+            cols = len(self.types) * self.ple_dim
+            self.ple0 = p.mat(T, cols)             # the host's per-layer token rows [T, L * ple_dim]
+            self.ple = p.mat(T, cols)              # projected
+        else:
+            self.ple0 = self.ple = None
         self.y = p.mat(T, H)
         kd, vd, hist = self.nk * self.dk, self.nv * self.dv, self.taps - 1
         self.st = []
-        for t in self.types:
+        last_kv: dict[str, dict] = {}
+        for i, t in enumerate(self.types):
             if t == "linear_attention":
                 # the conv inputs (rows t + hist; the first hist rows are the zero history) and the
                 # DeltaNet state, one [dk, dv] matrix per value head
@@ -400,15 +490,27 @@ class QwenLowering:
                 self.st.append(dict(cin={n: p.mat(T + hist, d) for n, d in (("q", kd), ("k", kd), ("v", vd))},
                                     S=[[p.mat(self.dk, self.dv, self.state_fmt) for _ in range(self.nv)]
                                        for _ in range(2 if self.mtp else 1)]))
-            else:
-                self.st.append(dict(kc=p.mat(self.Tp, self.nkv * self.hd), vc=p.mat(self.Tp, self.nkv * self.hd)))
+            elif i < self.first_kv_shared:         # a KV cache (zero padded)
+                hd = self._layer_hd(t)
+                kv = dict(kc=p.mat(self.Tp, self.nkv * hd), vc=p.mat(self.Tp, self.nkv * hd))
+                self.st.append(kv)
+                last_kv[t] = kv
+            else:                                  # KV-shared: the last cache of the same layer type
+                self.st.append(last_kv[t])
         if self.mtp:                               # the MTP layer's KV cache (row r: token r + 1, hidden r)
             self.mst = dict(kc=p.mat(self.Tp, self.nkv * self.hd), vc=p.mat(self.Tp, self.nkv * self.hd))
         self.logits = p.mat(self.verify_rows, self.vocab) if self.head else None
 
-    def input(self, x: np.ndarray, t0: int = 0) -> None:
+    def embed_ple(self, ids) -> np.ndarray:
+        """Gemma 4's per-layer token rows [len(ids), L * ple_dim] (the host's lookup)."""
+        return ple_embedding(self.cfg, self.w["embed_tokens_per_layer.weight"][np.asarray(ids)])
+
+    def input(self, x: np.ndarray, t0: int = 0, ple: np.ndarray | None = None) -> None:
         a = self.p.base + self.x0.off + t0 * self.x0.ld
         self.p.ddr[a:a + x.size * 4] = np.asarray(x, F32).tobytes()
+        if ple is not None:
+            pa = self.p.base + self.ple0.off + t0 * self.ple0.ld
+            self.p.ddr[pa:pa + ple.size * 4] = np.asarray(ple, F32).tobytes()
 
     # ------------------------------------------------------------------ blocks
     def chunk(self, t0: int, n: int, all_rows: bool = False, parity: int = 0, spec: bool = False) -> None:
@@ -419,12 +521,16 @@ class QwenLowering:
         assert not all_rows or n <= self.verify_rows
         self.parity, self.spec = parity, spec
         p = self.p
+        if self.ple_dim:
+            p.top = self.scratch0
+            self._project_ple(t0, n)
+            assert p.top <= self.scratch_end, "scratch_bytes too small for the per-layer projection"
         for i, t in enumerate(self.types):
             p.top = self.scratch0                  # this layer's temporaries over the last layer's
             if t == "linear_attention":
                 self._la(i, t0, n)
             else:
-                self._fa_block(self.lw[i], self.st[i], self.xs[i].rowv(t0, n), self.xs[i + 1].rowv(t0, n), t0, n)
+                self._fa_block(self.lw[i], self.st[i], self.xs[i].rowv(t0, n), self.xs[i + 1].rowv(t0, n), t0, n, i)
             assert p.top <= self.scratch_end, "scratch_bytes too small for this chunk"
         p.top = self.scratch0
         p.norm(self.xs[-1].rowv(t0, n), self.final_norm, self.eps, self.y.rowv(t0, n))
@@ -433,6 +539,20 @@ class QwenLowering:
             self._head(self.y.rowv(t0 + n - r, r))
         assert p.top <= self.scratch_end, "scratch_bytes too small for this chunk"
         p.top = self.end
+
+    def _project_ple(self, t0: int, n: int) -> None:
+        """Gemma 4's per-layer inputs: the rows' projection [n, L * ple_dim] times H^-0.5, the RMSNorm
+        per layer block, plus the host's per-layer token rows, times 2^-0.5."""
+        p, P, L_n = self.p, self.ple_dim, len(self.types)
+        pw = self.ple_w
+        proj = p.mat(n, L_n * P)
+        self.linear(self.x0.rowv(t0, n), pw["model_proj"], proj)
+        p.elt(C.ELT_MUL, proj, pw["proj_scale"], proj, bmode=C.BM_SCALAR)
+        proj_n = p.mat(n, L_n * P)
+        p.norm(proj.heads(P), pw["proj_norm"], self.eps, proj_n.heads(P))
+        dst = self.ple.rowv(t0, n)
+        p.elt(C.ELT_ADD, proj_n, self.ple0.rowv(t0, n), dst)
+        p.elt(C.ELT_MUL, dst, pw["in_scale"], dst, bmode=C.BM_SCALAR)
 
     def swap_state(self) -> None:
         """The second DeltaNet state copy into the first (ELT MUL by an exact 1.0), so that plain
@@ -469,6 +589,11 @@ class QwenLowering:
         for lin in self.head_lins:
             out = V(self.logits.off + 4 * c0 * r, r, lin.n, 4 * lin.n)
             self.linear(y, lin, out, qs=qs)
+            if self.softcap is not None:
+                # sc * tanh(x / sc) as 2 sc * sigmoid(2 x / sc) - sc
+                p.elt(C.ELT_MUL, out, self.sc_inv2, out, bmode=C.BM_SCALAR)
+                p.elt(C.ELT_MUL, out, self.sc_two, out, bmode=C.BM_SCALAR, act=C.ACT_SIGMOID)
+                p.elt(C.ELT_SUB, out, self.sc_val, out, bmode=C.BM_SCALAR)
             c0 += lin.n
 
     def _linear_k(self, x: V, lins, qs, out: V) -> None:
@@ -489,7 +614,7 @@ class QwenLowering:
         p.norm(x, w["ln_post"], self.eps, h)
         qs = p.quant(h) if self.wbits == 8 else None
         g, u = p.mat(n, w["gate"].n), p.mat(n, w["up"].n)
-        self.linear(h, w["gate"], g, act=C.ACT_GELU if self.gemma else C.ACT_SILU, qs=qs)
+        self.linear(h, w["gate"], g, act=C.ACT_GELU if (self.gemma or self.gemma4) else C.ACT_SILU, qs=qs)
         self.linear(h, w["up"], u, qs=qs)
         p.elt(C.ELT_MUL, g, u, g)
         gqs = p.quant(g) if self.wbits == 8 else None
@@ -563,10 +688,11 @@ class QwenLowering:
         p.elt(C.ELT_ADD, x, a, x1)
         self._mlp(w, x1, self.xs[li + 1].rowv(t0, n))
 
-    def _fa_block(self, w: dict, st: dict, x: V, out: V, t0: int, n: int) -> None:
+    def _fa_block(self, w: dict, st: dict, x: V, out: V, t0: int, n: int, li: int | None = None) -> None:
         p = self.p
         kc, vc = st["kc"], st["vc"]
-        nh, nkv, hd, rot = self.nh, self.nkv, self.hd, self.rot
+        nh, nkv = self.nh, self.nkv
+        hd, rot = w.get("hd", self.hd), w.get("rot", self.rot)
         h = p.mat(n, self.H)
         p.norm(x, w["ln_in"], self.eps, h)
         qs = p.quant(h) if self.wbits == 8 else None
@@ -580,12 +706,18 @@ class QwenLowering:
         qr = p.mat(n, nh * hd)
         tab = (self.rope_tabs[w["rope"]] if "rope" in w else self.rope_tab).rowv(t0, (n * nh - 1) // nh + 1)
         p.rope(qn.heads(hd), tab, nh, rot, qr.heads(hd))
-        k = p.mat(n, nkv * hd)
-        self.linear(h, w["k"], k, qs=qs)
-        self.linear(h, w["v"], vc.rowv(t0, n), qs=qs)          # V straight into the cache
-        kn = p.mat(n, nkv * hd)
-        p.norm(k.heads(hd), w["kn"], self.eps, kn.heads(hd))
-        p.rope(kn.heads(hd), tab, nkv, rot, kc.rowv(t0, n).heads(hd))
+        if not w.get("kv_shared", False):          # a KV-shared layer reads an earlier layer's cache
+            k = p.mat(n, nkv * hd)
+            self.linear(h, w["k"], k, qs=qs)
+            if w.get("vn") is not None:            # Gemma 4: V through an RMSNorm without scale
+                vr = p.mat(n, nkv * hd)
+                self.linear(h, w["v"], vr, qs=qs)
+                p.norm(vr.heads(hd), w["vn"], self.eps, vc.rowv(t0, n).heads(hd))
+            else:
+                self.linear(h, w["v"], vc.rowv(t0, n), qs=qs)  # V straight into the cache
+            kn = p.mat(n, nkv * hd)
+            p.norm(k.heads(hd), w["kn"], self.eps, kn.heads(hd))
+            p.rope(kn.heads(hd), tab, nkv, rot, kc.rowv(t0, n).heads(hd))
         nk = pad16(t0 + n)
         att = p.mat(n, nh * hd)
         sc, pr = p.mat(n, nk), p.mat(n, nk)
@@ -610,7 +742,20 @@ class QwenLowering:
             o = on
         x1 = p.mat(n, self.H)
         p.elt(C.ELT_ADD, x, o, x1)
-        self._mlp(w, x1, out)
+        x2 = p.mat(n, self.H) if "ple_gate" in w else out
+        self._mlp(w, x1, x2)
+        if "ple_gate" in w:                        # Gemma 4: the layer's per-layer input, gated
+            P = self.ple_dim
+            pg = p.mat(n, P)
+            self.linear(x2, w["ple_gate"], pg, act=C.ACT_GELU)
+            p.elt(C.ELT_MUL, pg, self.ple.rowv(t0, n).colv(li * P, P), pg)
+            pp = p.mat(n, self.H)
+            self.linear(pg, w["ple_proj"], pp)
+            ppn = p.mat(n, self.H)
+            p.norm(pp, w["ple_norm"], self.eps, ppn)
+            p.elt(C.ELT_ADD, x2, ppn, out)
+        if w.get("layer_scalar") is not None:
+            p.elt(C.ELT_MUL, out, w["layer_scalar"], out, bmode=C.BM_SCALAR)
 
     # ------------------------------------------------------------------ running chunk by chunk
     def stage(self, ddr: bytearray, a: int, b: int) -> tuple[int, int]:
@@ -620,9 +765,12 @@ class QwenLowering:
             ddr[q + 64 * (i - a):q + 64 * (i - a + 1)] = self.p.descs[i]
         return q, b - a
 
-    def put_input(self, ddr: bytearray, t0: int, x: np.ndarray) -> None:
+    def put_input(self, ddr: bytearray, t0: int, x: np.ndarray, ple: np.ndarray | None = None) -> None:
         a = self.p.base + self.x0.off + t0 * self.x0.ld
         ddr[a:a + x.size * 4] = np.asarray(x, F32).tobytes()
+        if ple is not None:
+            pa = self.p.base + self.ple0.off + t0 * self.ple0.ld
+            ddr[pa:pa + ple.size * 4] = np.asarray(ple, F32).tobytes()
 
     def logits_of(self, ddr) -> np.ndarray:
         a = self.p.base + self.logits.off
@@ -648,7 +796,8 @@ class QwenLowering:
             [(0, len(prompt))]
         for i in range(len(spans) + n_new):
             t0, n = spans[i] if i < len(spans) else (len(ids) - 1, 1)
-            self.put_input(ddr, t0, self.embed(ids[t0:t0 + n]))
+            toks = ids[t0:t0 + n]
+            self.put_input(ddr, t0, self.embed(toks), self.embed_ple(toks) if self.ple_dim else None)
             a = len(self.p.descs)
             self.chunk(t0, n)
             q, cnt = self.stage(ddr, a, len(self.p.descs))

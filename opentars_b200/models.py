@@ -1,12 +1,12 @@
 """Host model data for the lowering: configs, seeded random weights, weight quantisers.
 
-Restates, for the model families on the hot path (Qwen3, Gemma 3 and Qwen3.5 text models):
+Restates, for the model families on the hot path (Qwen3, Gemma 3 / 4 and Qwen3.5 text models):
   * make_config          tars_mini/qwen_ref.py:109-146 (transformers config objects)
   * random_weights       qwen_ref.py:165-198 (same generator, same draw order: the model's state_dict)
   * head_rows            qwen_ref.py:371-378 (the vocabulary in the fewest equal blocks <= 65535 rows)
   * quantize_weight      tars_mini/compiler.py:51-57 (per-channel symmetric INT8, float64 then fp32)
   * quantize_weight4     compiler.py:69-85 (group-128 INT4 with binary16 scales)
-  * input_embedding      tars_mini/llm.py:198-204
+  * input_embedding, ple_embedding   tars_mini/llm.py:198-211
 The host quantisers define data, not device arithmetic: they run once when an image is built.
 """
 from __future__ import annotations
@@ -36,6 +36,24 @@ CFG_G3_1B = dict(model_type="gemma3_text", hidden_size=1152, intermediate_size=6
 CFG_G3_SMALL = dict(CFG_G3_1B, hidden_size=256, intermediate_size=512, num_attention_heads=4,
                     num_key_value_heads=2, head_dim=64, query_pre_attn_scalar=64, sliding_window=64)
 
+# Gemma 4 E2B's text model (qwen_ref.py:59-81): 4 sliding layers to 1 full layer, head_dim 256 /
+# 512 (full), proportional 25 % RoPE on full layers, KV sharing over the last layers, double-wide
+# MLP on them, per-layer embeddings, V-norm without scale, layer_scalar, softcapped tied head
+VOCAB_G4_E2B = 262144
+LAYERS_G4_E2B = (["sliding_attention"] * 4 + ["full_attention"]) * 7
+CFG_G4_E2B = dict(model_type="gemma4_text", hidden_size=1536, intermediate_size=6144, num_attention_heads=8,
+                  num_key_value_heads=1, head_dim=256, global_head_dim=512, hidden_size_per_layer_input=256,
+                  vocab_size_per_layer_input=262144, num_kv_shared_layers=20, use_double_wide_mlp=True,
+                  enable_moe_block=False, attention_k_eq_v=False, rms_norm_eps=1e-6, vocab_size=16,
+                  sliding_window=512, hidden_activation="gelu_pytorch_tanh", max_position_embeddings=131072,
+                  final_logit_softcapping=30.0,
+                  rope_parameters={"full_attention": dict(rope_type="proportional", rope_theta=1000000.0,
+                                                          partial_rotary_factor=0.25),
+                                   "sliding_attention": dict(rope_type="default", rope_theta=10000.0)})
+CFG_G4_SMALL = dict(CFG_G4_E2B, hidden_size=256, intermediate_size=512, num_attention_heads=4, num_key_value_heads=1,
+                    head_dim=64, global_head_dim=128, hidden_size_per_layer_input=128, vocab_size_per_layer_input=16,
+                    num_kv_shared_layers=2, sliding_window=64)
+
 # Qwen3.5-0.8B's text model (qwen_ref.py:20-33): 3 gated-DeltaNet layers to 1 gated full-attention
 # layer, partial rotary 0.25 (text positions: plain RoPE), tied embeddings; the small variant of the
 # block tests (qwen_ref.py:86-88)
@@ -53,10 +71,21 @@ CFG_Q35_SMALL = dict(CFG_08B, hidden_size=256, intermediate_size=512, num_attent
 
 
 def make_config(base: dict, layer_types: list[str] | None = None, vocab: int | None = None):
-    """A transformers config for a Qwen3, Gemma 3 or Qwen3.5 text model (tied embeddings, eager
-    attention)."""
+    """A transformers config for a Qwen3, Gemma 3, Gemma 4 or Qwen3.5 text model (tied embeddings,
+    eager attention)."""
     b = {k: v for k, v in base.items() if k != "model_type"}
-    if base.get("model_type") == "gemma3_text":
+    if base.get("model_type") == "gemma4_text":
+        from transformers.models.gemma4 import Gemma4TextConfig
+        lt = list(layer_types or ["sliding_attention", "full_attention", "sliding_attention", "full_attention"])
+        vs = vocab or b["vocab_size"]
+        # the per-layer table follows the vocabulary unless the base gives a distinct one
+        vs_ple = vs if vocab is not None or b.get("vocab_size_per_layer_input") == b["vocab_size"] \
+            else b["vocab_size_per_layer_input"]
+        n_shared = min(b.get("num_kv_shared_layers", 0), max(0, len(lt) - 2))
+        cfg = Gemma4TextConfig(**dict(b, vocab_size=vs, vocab_size_per_layer_input=vs_ple,
+                                      num_kv_shared_layers=n_shared, tie_word_embeddings=True),
+                               num_hidden_layers=len(lt), layer_types=lt)
+    elif base.get("model_type") == "gemma3_text":
         from transformers.models.gemma3.configuration_gemma3 import Gemma3TextConfig
         lt = list(layer_types or ["sliding_attention", "full_attention"])
         cfg = Gemma3TextConfig(**dict(b, vocab_size=vocab or b["vocab_size"], tie_word_embeddings=True),
@@ -73,7 +102,7 @@ def make_config(base: dict, layer_types: list[str] | None = None, vocab: int | N
         cfg = Qwen3_5TextConfig(**dict(b, vocab_size=vocab or b["vocab_size"], tie_word_embeddings=True),
                                 num_hidden_layers=len(lt), layer_types=lt)
     else:
-        raise ValueError(f"model type {base.get('model_type')!r} is not on this path (Qwen3, Gemma 3, Qwen3.5)")
+        raise ValueError(f"model type {base.get('model_type')!r} is not on this path (Qwen3, Gemma 3 / 4, Qwen3.5)")
     cfg._attn_implementation = "eager"
     return cfg
 
@@ -85,6 +114,8 @@ def param_shapes(cfg) -> list[tuple[str, tuple[int, ...]]]:
         from transformers.models.qwen3.modeling_qwen3 import Qwen3Model as Model
     elif cfg.model_type == "qwen3_5_text":
         from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5TextModel as Model
+    elif cfg.model_type == "gemma4_text":
+        from transformers.models.gemma4 import Gemma4TextModel as Model
     else:
         from transformers.models.gemma3.modeling_gemma3 import Gemma3TextModel as Model
     with torch.device("meta"):
@@ -94,9 +125,10 @@ def param_shapes(cfg) -> list[tuple[str, tuple[int, ...]]]:
 
 def random_weights(cfg, seed: int = 0, embed: bool = False) -> dict[str, np.ndarray]:
     """Linears N(0, 0.02) with 2 % of the output rows x4; Qwen3.5's conv taps N(0, 0.3), A_log =
-    log U(1, 16), dt_bias U(0.5, 1.5), the gated norm 1 + N(0, 0.1); norms 1 + N(0, 0.1) (Qwen3) or
-    N(0, 0.1) (Gemma 3 and Qwen3.5, zero-centred); with `embed` the tied embedding N(0, 0.02), drawn
-    8192 rows at a time."""
+    log U(1, 16), dt_bias (and Gemma 4's layer_scalar) U(0.5, 1.5), the gated norm 1 + N(0, 0.1);
+    norms 1 + N(0, 0.1) (Qwen3, Gemma 4) or N(0, 0.1) (Gemma 3 and Qwen3.5, zero-centred); with
+    `embed` the embedding tables (the tied one, Gemma 4's per-layer one) N(0, 0.02), drawn 8192
+    rows at a time."""
     rng = np.random.default_rng(seed)
     w = {}
     for name, shape in param_shapes(cfg):
@@ -113,11 +145,11 @@ def random_weights(cfg, seed: int = 0, embed: bool = False) -> dict[str, np.ndar
             a = rng.normal(0, 0.3, shape)
         elif name.endswith("A_log"):
             a = np.log(rng.uniform(1, 16, shape))
-        elif name.endswith("dt_bias"):
+        elif name.endswith("dt_bias") or name.endswith(".layer_scalar"):
             a = rng.uniform(0.5, 1.5, shape)
         elif name.endswith("linear_attn.norm.weight"):
             a = 1 + rng.normal(0, 0.1, shape)
-        elif cfg.model_type == "qwen3":
+        elif cfg.model_type in ("qwen3", "gemma4_text"):
             a = 1 + rng.normal(0, 0.1, shape)
         else:
             a = rng.normal(0, 0.1, shape)
@@ -150,11 +182,18 @@ def head_rows(vocab: int) -> int:
 
 
 def input_embedding(cfg, rows: np.ndarray) -> np.ndarray:
-    """Gemma scales embedding rows by fp32(sqrt(hidden)), one fp32 rounding."""
+    """Gemma 3 / 4 scale embedding rows by fp32(sqrt(hidden)), one fp32 rounding (llm.py:198-204)."""
     rows = np.asarray(rows, F32)
-    if getattr(cfg, "model_type", "") != "gemma3_text":
+    if getattr(cfg, "model_type", "") not in ("gemma3_text", "gemma4_text"):
         return rows
     return (rows * F32(cfg.hidden_size ** 0.5)).astype(F32)
+
+
+def ple_embedding(cfg, rows: np.ndarray) -> np.ndarray:
+    """Gemma 4's per-layer token embedding rows [n, L * ple_dim] times fp32(sqrt(ple_dim))
+    (llm.py:207-211)."""
+    rows = np.asarray(rows, F32)
+    return (rows * F32(cfg.hidden_size_per_layer_input ** 0.5)).astype(F32)
 
 
 @dataclass

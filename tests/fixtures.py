@@ -32,9 +32,9 @@ def models() -> dict:
 
 def engine_models() -> dict:
     """The model fixtures the batched decode engine serves (Qwen3, Gemma 3: attention layers only;
-    Qwen3.5's DeltaNet layers run through the descriptor path)."""
+    Qwen3.5's DeltaNet layers and Gemma 4 run through the descriptor path)."""
     return {k: v for k, v in models().items()
-            if set(v["types"]) <= {"full_attention", "sliding_attention"}}
+            if set(v["types"]) <= {"full_attention", "sliding_attention"} and not v["base"].startswith("CFG_G4")}
 
 
 def queue_params():

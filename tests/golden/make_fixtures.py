@@ -177,8 +177,23 @@ MODEL_CASES = [
      [5, 77, 901, 12, 3000, 2, 9], 4, "fp32"),
     ("qwen35_small_fp16", "CFG_Q35_SMALL", ["linear_attention", "full_attention", "linear_attention"], 4096, 32,
      [5, 77, 901, 12, 3000, 2, 9], 4, "fp16"),
+    ("gemma4_small", "CFG_G4_SMALL", ["sliding_attention", "full_attention", "sliding_attention", "full_attention"],
+     4096, 32, [5, 77, 901, 12, 3000, 2], 4, "fp32"),
 ]
 REF_BASE = {"CFG_Q35_SMALL": "CFG_SMALL"}     # the reference's name of a base config, where it differs
+
+
+def gemma4_head_dims(cfg) -> None:
+    """The reference's Gemma 4 lowering reads cfg.per_layer_config (per layer: head_dim and
+    num_key_value_heads), a field of a newer transformers than the one installed here, whose
+    Gemma4TextConfig carries head_dim (sliding layers) and global_head_dim (full layers) instead.
+    Give the reference those same dims in that field."""
+    from types import SimpleNamespace
+    if getattr(cfg, "model_type", "") != "gemma4_text" or hasattr(cfg, "per_layer_config"):
+        return
+    cfg.per_layer_config = [SimpleNamespace(
+        head_dim=cfg.global_head_dim if t == "full_attention" else cfg.head_dim,
+        num_key_value_heads=cfg.num_key_value_heads) for t in cfg.layer_types]
 
 
 def make_models(ref: str):
@@ -190,6 +205,7 @@ def make_models(ref: str):
         bcfg = dict(Q.CFG_G3_SMALL, intermediate_size=4608) if base == "G3_SMALL_K2" \
             else getattr(Q, REF_BASE.get(base, base))
         cfg = Q.make_config(bcfg, types, vocab=vocab)
+        gemma4_head_dims(cfg)
         w = Q.random_weights(cfg, seed=0, embed=True)
         low = QwenLowering(cfg, w, max_tokens=T, ddr_bytes=1 << 26, head=True, queue_cap=4096,
                            state_dtype=state_dtype)

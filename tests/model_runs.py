@@ -33,6 +33,8 @@ def build_export_lowering(fx: dict):
     cfg = Mo.make_config(base, fx["types"], vocab=fx["vocab"])
     w = Mo.random_weights(cfg, seed=0, embed=True)
     w["embed_tokens.weight"] = bf16_exact(w["embed_tokens.weight"])
+    if "embed_tokens_per_layer.weight" in w:
+        w["embed_tokens_per_layer.weight"] = bf16_exact(w["embed_tokens_per_layer.weight"])
     return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096)
 
 
