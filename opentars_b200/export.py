@@ -25,6 +25,8 @@ from pathlib import Path
 
 import numpy as np
 
+from . import contract as C
+
 
 def bf16_exact(a: np.ndarray) -> np.ndarray:
     """fp32 values rounded to the nearest bf16 (ties to even), as fp32: a table the export can
@@ -86,6 +88,9 @@ def write_export(low, out, chunks=(4,), align: int = 4, bos_ids=(), eos_ids=(), 
     (out / "image.bin").write_bytes(image)
     m = dict(
         model_type=getattr(low.cfg, "model_type", ""), max_tokens=low.T, hidden=low.H, vocab=low.vocab,
+        wbits=int(low.wbits), state_dtype="fp16" if (low.state_fmt == C.OUT_FP16 and "linear_attention" in low.types) else "fp32",
+        keep_layers=bool(low.keep_layers),
+        turn_end="<turn|>\n" if low.gemma4 else ("<end_of_turn>\n" if low.gemma else "<|im_end|>\n"),
         image_bytes=len(image), mem_bytes=len(image), state_end=int(low.qbase),
         x0_off=int(low.x0.off), x0_ld=int(low.x0.ld), qbase=int(low.qbase), queue_cap=int(low.queue_cap),
         logits_off=int(low.logits.off), head_blocks=[int(lin.n) for lin in low.head_lins],

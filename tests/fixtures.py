@@ -32,9 +32,10 @@ def models() -> dict:
 
 def engine_models() -> dict:
     """The model fixtures the batched decode engine serves (Qwen3, Gemma 3: attention layers only;
-    Qwen3.5's DeltaNet layers and Gemma 4 run through the descriptor path)."""
+    W8A8; Qwen3.5's DeltaNet layers, Gemma 4 and W4A16 models run through the descriptor path)."""
     return {k: v for k, v in models().items()
-            if set(v["types"]) <= {"full_attention", "sliding_attention"} and not v["base"].startswith("CFG_G4")}
+            if set(v["types"]) <= {"full_attention", "sliding_attention"} and "G4" not in v["base"]
+            and v.get("wbits", 8) == 8}
 
 
 def queue_params():

@@ -168,17 +168,21 @@ def make_numerics(F):
 
 # ------------------------------------------------------------------------- model fixtures
 MODEL_CASES = [
-    # name, base config (opentars_b200.models name), layer types, vocab, max_tokens, prompt, new tokens,
-    # DeltaNet state dtype
-    ("qwen3_small", "CFG_Q3_SMALL", ["full_attention"] * 3, 4096, 32, [5, 77, 901, 12, 3000, 2, 9], 4, "fp32"),
+    # name, base config (opentars_b200.models name, or a tests.model_runs.DERIVED name), layer types,
+    # vocab, max_tokens, prompt, new tokens, DeltaNet state dtype, weight bits (8: W8A8, 4: W4A16)
+    ("qwen3_small", "CFG_Q3_SMALL", ["full_attention"] * 3, 4096, 32, [5, 77, 901, 12, 3000, 2, 9], 4, "fp32", 8),
     ("gemma3_small", "G3_SMALL_K2", ["sliding_attention", "full_attention", "sliding_attention"], 4096, 32,
-     [5, 77, 901, 12, 3000, 2], 4, "fp32"),
+     [5, 77, 901, 12, 3000, 2], 4, "fp32", 8),
     ("qwen35_small", "CFG_Q35_SMALL", ["linear_attention", "full_attention", "linear_attention"], 4096, 32,
-     [5, 77, 901, 12, 3000, 2, 9], 4, "fp32"),
+     [5, 77, 901, 12, 3000, 2, 9], 4, "fp32", 8),
     ("qwen35_small_fp16", "CFG_Q35_SMALL", ["linear_attention", "full_attention", "linear_attention"], 4096, 32,
-     [5, 77, 901, 12, 3000, 2, 9], 4, "fp16"),
+     [5, 77, 901, 12, 3000, 2, 9], 4, "fp16", 8),
     ("gemma4_small", "CFG_G4_SMALL", ["sliding_attention", "full_attention", "sliding_attention", "full_attention"],
-     4096, 32, [5, 77, 901, 12, 3000, 2], 4, "fp32"),
+     4096, 32, [5, 77, 901, 12, 3000, 2], 4, "fp32", 8),
+    ("qwen3_small_w4", "CFG_Q3_SMALL", ["full_attention"] * 3, 4096, 32, [5, 77, 901, 12, 3000, 2, 9], 4, "fp32", 4),
+    ("gemma4_small_w4", "G4_SMALL_P256",
+     ["sliding_attention", "full_attention", "sliding_attention", "full_attention"], 4096, 32,
+     [5, 77, 901, 12, 3000, 2], 4, "fp32", 4),
 ]
 REF_BASE = {"CFG_Q35_SMALL": "CFG_SMALL"}     # the reference's name of a base config, where it differs
 
@@ -200,15 +204,14 @@ def make_models(ref: str):
     import tars_mini.qwen_ref as Q
     from tars_mini import golden as G
     from tars_mini.llm import QwenLowering
+    from tests.model_runs import base_config
     out = {}
-    for name, base, types, vocab, T, prompt, new, state_dtype in MODEL_CASES:
-        bcfg = dict(Q.CFG_G3_SMALL, intermediate_size=4608) if base == "G3_SMALL_K2" \
-            else getattr(Q, REF_BASE.get(base, base))
-        cfg = Q.make_config(bcfg, types, vocab=vocab)
+    for name, base, types, vocab, T, prompt, new, state_dtype, wbits in MODEL_CASES:
+        cfg = Q.make_config(base_config(Q, base, REF_BASE), types, vocab=vocab)
         gemma4_head_dims(cfg)
         w = Q.random_weights(cfg, seed=0, embed=True)
         low = QwenLowering(cfg, w, max_tokens=T, ddr_bytes=1 << 26, head=True, queue_cap=4096,
-                           state_dtype=state_dtype)
+                           state_dtype=state_dtype, wbits=wbits)
         image_sha = hashlib.sha256(bytes(low.p.ddr)).hexdigest()
         queues = []
 
@@ -219,7 +222,7 @@ def make_models(ref: str):
             return m.ddr
         ids, logits, counts = low.generate(run, prompt, new)
         out[name] = dict(base=base, types=types, vocab=vocab, T=T, prompt=prompt, new=new, state_dtype=state_dtype,
-                         image_sha256=image_sha,
+                         wbits=wbits, image_sha256=image_sha,
                          queue_sha256=queues, counts=counts, ids=ids,
                          logits_sha256=[hashlib.sha256(lg.astype("<f4").tobytes()).hexdigest() for lg in logits],
                          logits_head=[lg[:8].astype(np.float32).view(np.uint32).tolist() for lg in logits],

@@ -7,6 +7,22 @@ import hashlib
 import numpy as np
 
 
+# fixture bases that are a named config with a few fields changed: name -> (config, changes)
+DERIVED = {"G3_SMALL_K2": ("CFG_G3_SMALL", dict(intermediate_size=4608)),
+           # W4A16 needs K >= 256 on every linear: the per-layer-input projection's K is ple_dim
+           "G4_SMALL_P256": ("CFG_G4_SMALL", dict(hidden_size_per_layer_input=256))}
+
+
+def base_config(mod, name: str, rename: dict | None = None) -> dict:
+    """The base config `name` of a fixture from module `mod` (opentars_b200.models, or the
+    reference's qwen_ref with its own names in `rename`)."""
+    rename = rename or {}
+    if name in DERIVED:
+        b, changes = DERIVED[name]
+        return dict(getattr(mod, rename.get(b, b)), **changes)
+    return getattr(mod, rename.get(name, name))
+
+
 def build_lowering(fx: dict, full: bool = False):
     from opentars_b200 import models as Mo
     from opentars_b200.lowering import QwenLowering
@@ -16,11 +32,10 @@ def build_lowering(fx: dict, full: bool = False):
         cfg = Mo.make_config(base, types, vocab=fx["vocab"])
         w = Mo.random_weights(cfg, seed=0, embed=True)
         return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=3 << 29, head=True, queue_cap=8192)
-    base = dict(Mo.CFG_G3_SMALL, intermediate_size=4608) if fx["base"] == "G3_SMALL_K2" else getattr(Mo, fx["base"])
-    cfg = Mo.make_config(base, fx["types"], vocab=fx["vocab"])
+    cfg = Mo.make_config(base_config(Mo, fx["base"]), fx["types"], vocab=fx["vocab"])
     w = Mo.random_weights(cfg, seed=0, embed=True)
     return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096,
-                        state_dtype=fx.get("state_dtype", "fp32"))
+                        state_dtype=fx.get("state_dtype", "fp32"), wbits=fx.get("wbits", 8))
 
 
 def build_export_lowering(fx: dict):
@@ -29,13 +44,13 @@ def build_export_lowering(fx: dict):
     from opentars_b200 import models as Mo
     from opentars_b200.export import bf16_exact
     from opentars_b200.lowering import QwenLowering
-    base = dict(Mo.CFG_G3_SMALL, intermediate_size=4608) if fx["base"] == "G3_SMALL_K2" else getattr(Mo, fx["base"])
-    cfg = Mo.make_config(base, fx["types"], vocab=fx["vocab"])
+    cfg = Mo.make_config(base_config(Mo, fx["base"]), fx["types"], vocab=fx["vocab"])
     w = Mo.random_weights(cfg, seed=0, embed=True)
     w["embed_tokens.weight"] = bf16_exact(w["embed_tokens.weight"])
     if "embed_tokens_per_layer.weight" in w:
         w["embed_tokens_per_layer.weight"] = bf16_exact(w["embed_tokens_per_layer.weight"])
-    return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096)
+    return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096,
+                        wbits=fx.get("wbits", 8))
 
 
 class OracleDevice:
