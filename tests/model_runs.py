@@ -135,7 +135,8 @@ def machine_runner(machine_cls, queues: list, gemv_only: bool = True):
 
 class BoardRunner:
     """run(ddr, q, n) over the board backend: the image uploaded once, then per run only the
-    input rows and the queue go up and the logits come back (as the board runtime moves data)."""
+    input rows (Gemma 4: and the per-layer input rows) and the queue go up and the logits come
+    back (as the board runtime moves data)."""
 
     def __init__(self, low, graphs: bool = True):
         from opentars_b200.board import Cuda
@@ -150,6 +151,10 @@ class BoardRunner:
         x0, ld, T = low.p.base + low.x0.off, low.x0.ld, low.T
         dev.mem[x0:x0 + ld * T] = np.frombuffer(bytes(ddr[x0:x0 + ld * T]), np.uint8)
         dev.to_dev(x0, ld * T)
+        if low.ple_dim:
+            p0, pld = low.p.base + low.ple0.off, low.ple0.ld
+            dev.mem[p0:p0 + pld * T] = np.frombuffer(bytes(ddr[p0:p0 + pld * T]), np.uint8)
+            dev.to_dev(p0, pld * T)
         dev.mem[q:q + 64 * n] = np.frombuffer(bytes(ddr[q:q + 64 * n]), np.uint8)
         dev.to_dev(q, 64 * n)
         self.queues.append(sha(ddr[q:q + 64 * n]))
