@@ -80,7 +80,7 @@ def build_gemv(R: int, seed: int, M: int = 1, K: int = 1024, N: int = 3072):
                    SCALE_OFF=s0 + r * 4 * N, Y_OFF=y0 + r * 4 * M * N, M=M, N=N, K=K, HDR_RSV=sr // 16)
         ddr[qa + 128 * r:qa + 128 * r + 64] = np.frombuffer(d0, np.uint8)
         ddr[qa + 128 * r + 64:qa + 128 * (r + 1)] = np.frombuffer(d1, np.uint8)
-    gemm_bytes = N * K + 4 * N + M * K + 4 * M + 4 * M * N          # 3,171,332 at config 0
+    gemm_bytes = N * K + 4 * N + M * K + 4 * M + 4 * M * N          # 3,171,332 bytes at config 0
     quant_bytes = 4 * M * K + M * K + 4 * M
     return dict(ddr=ddr, qa=qa, qlen=2 * R, units=R, unit_bytes=gemm_bytes + quant_bytes,
                 kernel_bytes=R * gemm_bytes, roof=(2, lambda i: i == 1),
@@ -111,7 +111,7 @@ def build_w4(R: int, seed: int, M: int = 1, K: int = 8192, N: int = 16384):
                   A_OFF=x0 + r * 4 * M * K, W_OFF=w0 + r * N * K // 2, SCALE_OFF=s0 + r * 2 * N * G,
                   Y_OFF=y0 + r * 4 * M * N, M=M, N=N, K=K, GROUP_SIZE=128)
         ddr[qa + 64 * r:qa + 64 * (r + 1)] = np.frombuffer(d, np.uint8)
-    unit = N * K // 2 + 2 * N * G + 4 * M * K + 4 * M * N               # 69,304,320 here
+    unit = N * K // 2 + 2 * N * G + 4 * M * K + 4 * M * N               # 69,304,320 bytes here
     return dict(ddr=ddr, qa=qa, qlen=R, units=R, unit_bytes=unit, kernel_bytes=unit, roof=(1, lambda i: True),
                 kernel="k_gemv_w4 (W4A16 GEMV)", inputs=(x0, R * 4 * M * K), outputs=(y0, R * 4 * M * N),
                 config=dict(workload="config2_w4a16_gemv", M=M, K=K, N=N, units_per_step=R,
