@@ -67,6 +67,11 @@ int tc_engine_sync(tc_engine* e);
  * 4 attention, 5 quant, 6 argmax, 7 position) and the kernel's algorithmic bytes[i]. Returns the
  * number of kernels (the step counts as a decode step: the position advances). */
 int tc_engine_profile(tc_engine* e, float* ms, int32_t* kind, uint64_t* bytes, uint32_t cap);
+/* The engine's greedy pick on its own: tok_out[r] = np.argmax(logits[r]) for rows r < rows of
+ * device logits [rows][vocab] (the first maximum; the first NaN wins over numbers): the
+ * np.argmax of llm.py:834 and of tars_board.py:355. Device pointers; enqueued on `stream` (NULL:
+ * the default stream). */
+int tc_argmax(const float* logits, int32_t vocab, int32_t rows, int32_t* tok_out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -684,41 +684,108 @@ static cudaError_t attention_hd(const AttnArgs& a, const AttnQuantArgs& f, int b
 }
 
 // ------------------------------------------------------------------------------- greedy pick
-// np.argmax of each sequence's logits: the first maximum; the first NaN wins over numbers.
-__global__ void __launch_bounds__(1024) k_argmax(const float* logits, int vocab, int* tok_out, int tok_stride) {
+// np.argmax of each sequence's logits: the first maximum; the first NaN wins over numbers. A row
+// is spread over a cluster of kPickCluster CTAs (every SM busy at batch 64): CTA c scans a
+// contiguous slice with 16-byte loads, each thread keeping four candidates (one per vector lane)
+// so four independent compare chains overlap the loads; candidates combine under a rule that is
+// order-free (NaN first, then the larger value, then the smaller index), per warp by shuffles, per
+// CTA in shared memory, and across the cluster through distributed shared memory.
+constexpr int kPickCluster = 8, kPickThreads = 256;
+
+struct Pick {
+  float v;
+  int i;       // -1: no element yet
+  int nan;
+};
+// elements of one chain arrive in increasing index order, so a tie keeps the earlier one
+__device__ __forceinline__ void pick_step(Pick& p, float v, int j) {
+  const int vn = is_nan(v);
+  const bool take = (p.i < 0) | (vn & !p.nan) | (!p.nan & !vn & (v > p.v));
+  p.v = take ? v : p.v;
+  p.i = take ? j : p.i;
+  p.nan = take ? vn : p.nan;
+}
+__device__ __forceinline__ Pick pick_comb(Pick a, Pick b) {
+  bool take_b;
+  if (b.i < 0) take_b = false;
+  else if (a.i < 0) take_b = true;
+  else if (a.nan != b.nan) take_b = b.nan;
+  else if (a.nan) take_b = b.i < a.i;
+  else take_b = b.v > a.v || (b.v == a.v && b.i < a.i);
+  return take_b ? b : a;
+}
+__device__ __forceinline__ Pick pick_shfl(Pick p, int o) {
+  Pick q;
+  q.v = __shfl_xor_sync(0xFFFFFFFFu, p.v, o);
+  q.i = __shfl_xor_sync(0xFFFFFFFFu, p.i, o);
+  q.nan = __shfl_xor_sync(0xFFFFFFFFu, p.nan, o);
+  return q;
+}
+
+__global__ void __launch_bounds__(kPickThreads) k_argmax(const float* logits, int vocab, int* tok_out, int tok_stride) {
   griddep_launch();
   griddep_wait();
-  const int b = blockIdx.x;
+  __shared__ Pick s_warp[kPickThreads / 32];
+  __shared__ int s_cand[3];                      // this CTA's candidate: value bits, index, nan
+  const int b = blockIdx.x / kPickCluster, c = (int)cluster_rank();
+  const int S = ((vocab + kPickCluster - 1) / kPickCluster + 3) / 4 * 4;
+  const int lo = min(vocab, c * S), hi = min(vocab, lo + S);
   const float* row = logits + (uint64_t)b * vocab;
-  float best = 0.0f;
-  int bi = -1;
-  bool bnan = false;
-  for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
-    const float v = row[j];
-    const bool vn = is_nan(v);
-    if (bi < 0 || (vn && !bnan) || (!bnan && !vn && v > best)) { best = v; bi = j; bnan = vn; }
-  }
-  // combine (value, index, nan) pairs: smaller index wins ties
-  __shared__ float sv[1024];
-  __shared__ int si[1024];
-  __shared__ int sn[1024];
-  sv[threadIdx.x] = best; si[threadIdx.x] = bi; sn[threadIdx.x] = bnan;
-  __syncthreads();
-  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
-    if (threadIdx.x < o) {
-      const int j = threadIdx.x + o;
-      if (si[j] >= 0) {
-        bool take;
-        if (si[threadIdx.x] < 0) take = true;
-        else if (sn[j] != sn[threadIdx.x]) take = sn[j];
-        else if (sn[j]) take = si[j] < si[threadIdx.x];
-        else take = sv[j] > sv[threadIdx.x] || (sv[j] == sv[threadIdx.x] && si[j] < si[threadIdx.x]);
-        if (take) { sv[threadIdx.x] = sv[j]; si[threadIdx.x] = si[j]; sn[threadIdx.x] = sn[j]; }
-      }
+  Pick p[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) p[u] = Pick{0.0f, -1, 0};
+  if ((vocab & 3) == 0 && ((uintptr_t)logits & 15) == 0) {
+    // lo and hi are multiples of 4: vectors only, two in flight per thread
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    int j4 = lo / 4 + threadIdx.x;
+    const int e4 = hi / 4;
+    for (; j4 + kPickThreads < e4; j4 += 2 * kPickThreads) {
+      const float4 x = __ldg(r4 + j4), y = __ldg(r4 + j4 + kPickThreads);
+      pick_step(p[0], x.x, 4 * j4);
+      pick_step(p[1], x.y, 4 * j4 + 1);
+      pick_step(p[2], x.z, 4 * j4 + 2);
+      pick_step(p[3], x.w, 4 * j4 + 3);
+      const int k4 = j4 + kPickThreads;
+      pick_step(p[0], y.x, 4 * k4);
+      pick_step(p[1], y.y, 4 * k4 + 1);
+      pick_step(p[2], y.z, 4 * k4 + 2);
+      pick_step(p[3], y.w, 4 * k4 + 3);
     }
-    __syncthreads();
+    if (j4 < e4) {
+      const float4 x = __ldg(r4 + j4);
+      pick_step(p[0], x.x, 4 * j4);
+      pick_step(p[1], x.y, 4 * j4 + 1);
+      pick_step(p[2], x.z, 4 * j4 + 2);
+      pick_step(p[3], x.w, 4 * j4 + 3);
+    }
+  } else {
+    for (int j = lo + threadIdx.x; j < hi; j += kPickThreads) pick_step(p[0], row[j], j);
   }
-  if (threadIdx.x == 0) tok_out[b * tok_stride] = si[0];
+  Pick m = pick_comb(pick_comb(p[0], p[1]), pick_comb(p[2], p[3]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = pick_comb(m, pick_shfl(m, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) s_warp[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    Pick t = s_warp[0];
+#pragma unroll
+    for (int w = 1; w < kPickThreads / 32; ++w) t = pick_comb(t, s_warp[w]);
+    s_cand[0] = __float_as_int(t.v);
+    s_cand[1] = t.i;
+    s_cand[2] = t.nan;
+  }
+  cluster_sync();
+  if (c == 0 && threadIdx.x == 0) {
+    Pick t{__int_as_float(s_cand[0]), s_cand[1], s_cand[2]};
+    for (int r = 1; r < kPickCluster; ++r) {
+      const Pick u{__int_as_float(dsmem_ld_s32(smem_u32(&s_cand[0]), r)), dsmem_ld_s32(smem_u32(&s_cand[1]), r),
+                   dsmem_ld_s32(smem_u32(&s_cand[2]), r)};
+      t = pick_comb(t, u);
+    }
+    tok_out[b * tok_stride] = t.i;
+  }
+  cluster_sync();                                 // the peers' candidates have been read
 }
 
 __global__ void k_advance(int* pos, int n) {
@@ -828,7 +895,8 @@ cudaError_t eng_attention_quant(const AttnArgs& a, const AttnQuantArgs& f, int b
   }
 }
 cudaError_t eng_argmax(const float* logits, int vocab, int batch, int* tok_out, int tok_stride, cudaStream_t st) {
-  cudaError_t e = launch_ex(k_argmax, dim3(batch), dim3(1024), 0, st, 1, logits, vocab, tok_out, tok_stride);
+  cudaError_t e = launch_ex(k_argmax, dim3(batch * kPickCluster), dim3(kPickThreads), 0, st, kPickCluster, logits,
+                            vocab, tok_out, tok_stride);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

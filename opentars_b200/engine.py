@@ -55,6 +55,7 @@ ENGINE_SIGNATURES = {
     "tc_engine_logits": (ctypes.c_int, [P, P]),
     "tc_engine_sync": (ctypes.c_int, [P]),
     "tc_engine_profile": (ctypes.c_int, [P, P, P, P, ctypes.c_uint32]),
+    "tc_argmax": (ctypes.c_int, [P, ctypes.c_int32, ctypes.c_int32, P, P]),
 }
 KERNEL_KINDS = ("embed", "norm_quant", "gemv", "qk_rope", "attention", "quant", "argmax", "advance")
 
