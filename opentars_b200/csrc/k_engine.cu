@@ -112,7 +112,13 @@ __global__ void __launch_bounds__(256) k_norm_quant(NormQuantArgs a) {
   griddep_wait();
   const float kinv = recip_f(i2f(H));
   const float* in = a.in + (uint64_t)r * a.ld_in;
-  for (int j4 = t; j4 < H / 4; j4 += blockDim.x) cp16(sx + 4 * j4, in + 4 * j4);
+  const float* res = a.res + (uint64_t)r * H;
+  float* sres = sm + 4 * H;                      // the residual row, staged with the input row
+  const bool res_v = a.mode >= 1 && ((uintptr_t)a.res & 15) == 0 && H % 4 == 0;
+  for (int j4 = t; j4 < H / 4; j4 += blockDim.x) {
+    cp16(sx + 4 * j4, in + 4 * j4);
+    if (res_v) cp16(sres + 4 * j4, res + 4 * j4);
+  }
   cp_wait_all();
   __syncthreads();
   for (int j = t; j < H; j += blockDim.x) sx[j] = ftz(sx[j]);
@@ -124,9 +130,8 @@ __global__ void __launch_bounds__(256) k_norm_quant(NormQuantArgs a) {
     for (int j = t; j < H; j += blockDim.x) sx[j] = ftz(fmul(fmul(sx[j], rs), spg[j]));
   }
   if (a.mode >= 1) {
-    const float* res = a.res + (uint64_t)r * H;
     for (int j = t; j < H; j += blockDim.x) {
-      const float v = fadd(res[j], sx[j]);
+      const float v = fadd(res_v ? sres[j] : res[j], sx[j]);
       sx[j] = ftz(v);
       a.x_out[(uint64_t)r * H + j] = ftz(v);
     }
@@ -802,7 +807,7 @@ cudaError_t eng_embed(const float* E, const int* tok, float* x, int H, int scale
   return cudaGetLastError();
 }
 cudaError_t eng_norm_quant(const NormQuantArgs& a, cudaStream_t st) {
-  const int smem = 4 * a.H * 4;
+  const int smem = 5 * a.H * 4;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k_norm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;

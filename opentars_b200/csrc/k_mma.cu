@@ -483,6 +483,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
       } else if (et < NT) {
         tk[et] = tk_next;
       }
+      // the first tile's weight-row constants load while its MMAs run (later tiles take them from
+      // the previous iteration's prefetch): split-K, the rows of this thread's first two units
+      typename Epi::Row rw_first{}, rw_unit0{}, rw_unit1{};
+      if (t == 0) {
+        if (split > 1) {
+          const int rs = kRows / split;
+          const int u0 = et, u1 = et + 32 * kEpiWarps;
+          if (u0 < rs * (NT / 4) && row0 + crank * rs + u0 % rs < sh.nrow[s]) rw_unit0 = epi.row(s, row0 + crank * rs + u0 % rs);
+          if (u1 < rs * (NT / 4) && row0 + crank * rs + u1 % rs < sh.nrow[s]) rw_unit1 = epi.row(s, row0 + crank * rs + u1 % rs);
+        } else if (row0 + r < sh.nrow[s]) {
+          rw_first = epi.row(s, row0 + r);
+        }
+      }
       if (epi_sync_or(aborted(&s_abort))) break;
       bool ok = true;
       if (nk > 0) {
@@ -535,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
         // sum the slots of this CTA's rows and run the epilogue: one row x 4 tokens per unit, so
         // every epilogue thread has work and a few short chains to interleave
         const int units = rs * (NT / 4);
-        for (int u = et; u < units; u += 32 * kEpiWarps) {
+        for (int u = et, ui = 0; u < units; u += 32 * kEpiWarps, ++ui) {
           const int url = u % rs, uj0 = 4 * (u / rs);
           const int cc = row0 + crank * rs + url;
           uint32_t a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
@@ -555,7 +568,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
             }
           }
           if (cc < sh.nrow[s]) {
-            const typename Epi::Row rw2 = epi.row(s, cc);
+            const typename Epi::Row rw2 = ui == 0 ? rw_unit0 : (ui == 1 ? rw_unit1 : epi.row(s, cc));
             epi.template put<4>(rw2, tk + uj0, tok0 + uj0, min(4, sh.M - tok0 - uj0), a0, a1, nacc == 2);
           }
         }
@@ -566,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
       bool live;
       if (t == 0) {
         live = c < sh.nrow[s];
-        if (live) rw = epi.row(s, c);
+        rw = rw_first;
       } else {
         live = live_next;
         rw = rw_next;
