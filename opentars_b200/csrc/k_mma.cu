@@ -501,6 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
       if (nk > 0) {
         ok = mbar_wait(&bar_accf[buf], use & 1, sh.err, 4);
         if (!ok) s_abort = 1;
+        if (split > 1 && threadIdx.x == 64) stamp(7);   // split-K: the accumulator is ready
       }
       __syncwarp();
       tc_fence_after();
@@ -541,6 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
         tc_fence_before();
         asm volatile("bar.arrive 2, %0;" ::"n"(32 + 32 * kEpiWarps) : "memory");
         const bool got = mbar_wait(&bar_recv, 0, sh.err, 5);
+        if (threadIdx.x == 64) stamp(5);                // the peers' partial rows have arrived
         if (epi_sync_or(!got)) {
           s_abort = 1;
           break;
@@ -627,7 +629,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
       tc_fence_after();
       tmem_dealloc(tmem, ncols);
     }
-    if (threadIdx.x == 0) stamp(7);
     return;
   }
   tc_fence_before();
