@@ -183,6 +183,10 @@ MODEL_CASES = [
     ("gemma4_small_w4", "G4_SMALL_P256",
      ["sliding_attention", "full_attention", "sliding_attention", "full_attention"], 4096, 32,
      [5, 77, 901, 12, 3000, 2], 4, "fp32", 4),
+    ("gemma3_small_w4", "G3_SMALL_K2", ["sliding_attention", "full_attention", "sliding_attention"], 4096, 32,
+     [5, 77, 901, 12, 3000, 2], 4, "fp32", 4),
+    ("qwen35_small_w4", "CFG_Q35_SMALL", ["linear_attention", "full_attention", "linear_attention"], 4096, 32,
+     [5, 77, 901, 12, 3000, 2, 9], 4, "fp32", 4),
 ]
 REF_BASE = {"CFG_Q35_SMALL": "CFG_SMALL"}     # the reference's name of a base config, where it differs
 
