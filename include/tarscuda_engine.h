@@ -70,7 +70,7 @@ int tc_engine_profile(tc_engine* e, float* ms, int32_t* kind, uint64_t* bytes, u
 /* The engine's greedy pick on its own: tok_out[r] = np.argmax(logits[r]) for rows r < rows of
  * device logits [rows][vocab] (the first maximum; the first NaN wins over numbers): the
  * np.argmax of llm.py:834 and of tars_board.py:355. Device pointers; enqueued on `stream` (NULL:
- * the default stream). */
+ * the default stream). TC_ERR_ARG for null pointers, vocab or rows <= 0, or rows > 2^24. */
 int tc_argmax(const float* logits, int32_t vocab, int32_t rows, int32_t* tok_out, void* stream);
 
 #ifdef __cplusplus

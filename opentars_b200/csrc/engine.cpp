@@ -430,7 +430,7 @@ int tc_engine_sync(tc_engine* e) {
 }
 
 int tc_argmax(const float* logits, int32_t vocab, int32_t rows, int32_t* tok_out, void* stream) {
-  if (!logits || !tok_out || vocab <= 0 || rows <= 0) return TC_ERR_ARG;
+  if (!logits || !tok_out || vocab <= 0 || rows <= 0 || rows > (1 << 24)) return TC_ERR_ARG;
   return tc::eng_argmax(logits, vocab, rows, tok_out, 1, static_cast<cudaStream_t>(stream)) == cudaSuccess
              ? TC_OK
              : TC_ERR_CUDA;

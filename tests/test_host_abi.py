@@ -34,6 +34,27 @@ def test_library_exports_every_declared_symbol(L):
     assert L.tc_version() == 1
 
 
+def test_library_exports_every_engine_symbol(L):
+    """include/tarscuda_engine.h: the decode engine's entry points and the greedy pick."""
+    header = (ROOT / "include" / "tarscuda_engine.h").read_text()
+    declared = set(re.findall(r"\b(tc_[a-z_0-9]+)\s*\(", header))
+    from opentars_b200.engine import ENGINE_SIGNATURES
+    assert declared == set(ENGINE_SIGNATURES), declared ^ set(ENGINE_SIGNATURES)
+    for name in declared:
+        assert hasattr(L, name), name
+
+
+def test_pick_rejects_bad_arguments_before_any_device_call(L):
+    from opentars_b200.engine import lib as engine_lib
+    E = engine_lib()
+    buf = ctypes.c_void_p(16)                      # never dereferenced: the checks come first
+    assert E.tc_argmax(None, 16, 1, buf, None) == -2
+    assert E.tc_argmax(buf, 16, 1, None, None) == -2
+    assert E.tc_argmax(buf, 0, 1, buf, None) == -2
+    assert E.tc_argmax(buf, 16, 0, buf, None) == -2
+    assert E.tc_argmax(buf, 16, (1 << 24) + 1, buf, None) == -2
+
+
 def _validate(L, raw, core_id=0, gemv_only=0):
     f = (ctypes.c_uint64 * 23)()
     err = L.tc_validate(bytes(raw), core_id, gemv_only, f)
