@@ -45,7 +45,8 @@ typedef struct {
 } tc_model_desc;
 
 /* A decode engine over the weights in `image` for `batch` sequences; uploads the fp32 embedding
- * table [vocab][hidden] from embed_host; KV caches zeroed, position 0. */
+ * table [vocab][hidden] from embed_host; KV caches zeroed, position 0. TC_ERR_ARG (and *out = NULL)
+ * for a missing argument or a model the engine does not serve. */
 int tc_engine_create(tc_machine* image, const tc_model_desc* md, const tc_layer_desc* layers,
                      const float* embed_host, int32_t batch, tc_engine** out);
 int tc_engine_destroy(tc_engine* e);

@@ -257,7 +257,9 @@ extern "C" {
 
 int tc_engine_create(tc_machine* image, const tc_model_desc* md, const tc_layer_desc* layers, const float* embed_host,
                      int32_t batch, tc_engine** out) {
+  if (!out) return TC_ERR_ARG;
   *out = nullptr;
+  if (!image || !md || !layers || !embed_host || md->n_layers < 1 || md->vocab < 1) return TC_ERR_ARG;
   tc_engine* e = new tc_engine();
   {
     const char* fa = getenv("TARSCUDA_FUSE_ATTN");

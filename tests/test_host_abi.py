@@ -55,6 +55,15 @@ def test_pick_rejects_bad_arguments_before_any_device_call(L):
     assert E.tc_argmax(buf, 16, (1 << 24) + 1, buf, None) == -2
 
 
+def test_engine_create_rejects_missing_arguments_before_any_device_call(L):
+    from opentars_b200.engine import lib as engine_lib
+    E = engine_lib()
+    out = ctypes.c_void_p(7)
+    assert E.tc_engine_create(None, None, None, None, 1, None) == -2
+    assert E.tc_engine_create(None, None, None, None, 1, ctypes.byref(out)) == -2
+    assert out.value is None                      # the handle is cleared on every error
+
+
 def _validate(L, raw, core_id=0, gemv_only=0):
     f = (ctypes.c_uint64 * 23)()
     err = L.tc_validate(bytes(raw), core_id, gemv_only, f)
