@@ -85,3 +85,20 @@ def test_runtime_refuses_mismatched_or_unsupported_exports(tmp_path, export_dir)
     (bad / "manifest.json").write_text(json.dumps(dict(m, spec={"m1": []})))
     with pytest.raises(ValueError, match="speculative"):
         Qwen(OracleDevice(m["image_bytes"]), bad, log=lambda *a, **k: None)
+
+
+def test_writer_refuses_what_an_export_cannot_hold(tmp_path):
+    """write_export stores the embedding tables as bf16 and needs the head and a queue region."""
+    from opentars_b200.export import bf16_exact, write_export
+    from tests.model_runs import build_lowering
+    low = build_lowering(FX.models()["qwen3_small"])             # fp32 embedding, not bf16-exact
+    with pytest.raises(ValueError, match="bf16-exact"):
+        write_export(low, tmp_path / "a")
+    g4 = build_export_lowering(FX.models()["gemma4_small"])
+    g4.w["embed_tokens_per_layer.weight"] = g4.w["embed_tokens_per_layer.weight"] + np.float32(1e-3)
+    assert not np.array_equal(bf16_exact(g4.w["embed_tokens_per_layer.weight"]), g4.w["embed_tokens_per_layer.weight"])
+    with pytest.raises(ValueError, match="per-layer"):
+        write_export(g4, tmp_path / "b")
+    low.head = False
+    with pytest.raises(ValueError, match="head"):
+        write_export(low, tmp_path / "c")
