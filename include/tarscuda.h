@@ -104,11 +104,19 @@ int tc_synchronize(tc_machine* m);
 int tc_set_mma_min_rows(int32_t rows);
 /* Tracing of the tensor-core GEMM: with enable = n > 0, the n-th tensor-core GEMM launch enqueued
  * (or captured) after this call records per CTA (its first 2048 CTAs) 8 globaltimer stamps in
- * nanoseconds: entry, setup done, first TMA load issued, first stage consumed by the MMA thread,
- * last MMA issued, first accumulator read by the epilogue, epilogue done, exit. Enabling zeroes
- * the stamps; enable = 0 turns tracing off. With out != NULL, waits for the device and copies
- * min(cap, 2048 * 8) stamps; returns that count (or TC_ERR_CUDA). */
+ * nanoseconds: 0 entry, 1 setup done, 2 first token slice issued, 3 first stage consumed by the
+ * MMA thread, 4 last MMA committed, 5 (split-K) the peers' partial rows received, 6 epilogue done,
+ * 7 exit (persistent) or the accumulator ready in the epilogue (split-K). Enabling zeroes the
+ * stamps; enable = 0 turns tracing off. With out != NULL, waits for the device and copies
+ * min(cap, 2048 * 8) stamps; returns that count (or TC_ERR_CUDA). No counterpart in the reference
+ * (a diagnostic). */
 int tc_mma_trace(int32_t enable, uint64_t* out, uint32_t cap);
+/* The device word in which the streaming kernels (tensor-core GEMM, grouped GEMV, streamed W4A16
+ * GEMV) record a bounded wait that gave up instead of hanging: 0 = none, else the code of the
+ * first one (GEMM 1-5, grouped GEMV 21-22, W4A16 GEMV 11-12); a kernel that gave up skipped the
+ * rest of its work, so its outputs are incomplete. clear != 0 resets the word. Synchronous;
+ * TC_ERR_CUDA if it cannot be read. No counterpart in the reference (its golden model never waits). */
+int tc_wait_error(int32_t clear);
 
 /* Host-only helpers (no device needed). golden.Machine.validate (golden.py:59-169): decodes the
  * 23 fields of contract.py:14-38 into fields[23] (in that table's order) and returns the first

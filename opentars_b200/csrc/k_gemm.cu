@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(32 * (1 + s_stages<KU>()), 2)
       int t = 0;
       for (int c = c_begin; c < c_end; ++c, ++t) {
         const int st = t % S;
-        if (!mbar_wait(&empty[st], ((t / S) & 1) ^ 1, nullptr, 0)) {
+        if (!mbar_wait(&empty[st], ((t / S) & 1) ^ 1, grp.err, 21)) {
           s_stop = 1;
           break;
         }
@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(32 * (1 + s_stages<KU>()), 2)
   uint4 areg[MB == 1 ? KU : 1];                               // M = 1: the activation row in registers
   int areg_j = -1;
   for (int c = c_begin + st, t = st; c < c_end; c += S, t += S) {
-    const bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[st], (t / S) & 1, nullptr, 0);
+    const bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[st], (t / S) & 1, grp.err, 22);
     if (!__all_sync(0xFFFFFFFFu, ok)) {                           // the whole warp stops together
       s_stop = 1;
       // the stage's copies may still be in flight: wait for them (bounded) before the block exits
@@ -415,6 +415,7 @@ int gemv8_class(const GemmArgs& g) {
 }
 
 cudaError_t launch_gemv8_group(GemvGroup& grp, cudaStream_t st) {
+  grp.err = wait_error_flag();
   switch (grp.mb * 16 + grp.ku) {
     case 1 * 16 + 2: return launch_group<1, 2>(grp, st);
     case 1 * 16 + 4: return launch_group<1, 4>(grp, st);

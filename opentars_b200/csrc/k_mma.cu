@@ -819,7 +819,21 @@ int mma_error_code() {
   return v;
 }
 
+int* wait_error_flag() { return err_flag(); }
+
 }  // namespace tc
+
+extern "C" int tc_wait_error(int32_t clear) {
+  int* p = tc::wait_error_flag();
+  if (!p) return TC_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return TC_ERR_CUDA;
+  if (clear && v) {
+    const int zero = 0;
+    if (cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return TC_ERR_CUDA;
+  }
+  return v;
+}
 
 extern "C" int tc_mma_trace(int32_t enable, uint64_t* out, uint32_t cap) {
   if (enable > 0) {

@@ -20,6 +20,7 @@
 #include <algorithm>
 
 #include "fp32.cuh"
+#include "mma.h"
 #include "ops.h"
 #include "umma.cuh"
 
@@ -348,7 +349,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
       int t = issued;
       for (int c = blockIdx.x + issued * gridDim.x; c < nchunk; c += gridDim.x, ++t) {
         const int st = t % kW4Stages;
-        if (!mbar_wait(&empty[st], ((t / kW4Stages) & 1) ^ 1, nullptr, 0)) {
+        if (!mbar_wait(&empty[st], ((t / kW4Stages) & 1) ^ 1, g.err, 11)) {
           s_stop = 1;
           break;
         }
@@ -373,7 +374,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
   for (int c = blockIdx.x; c < nchunk; c += gridDim.x, ++t) {
     const int st = t % kW4Stages;
     load_ws((c + gridDim.x) * kW4Cols + cw, wsn);
-    const bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[st], (t / kW4Stages) & 1, nullptr, 0);
+    const bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[st], (t / kW4Stages) & 1, g.err, 12);
     if (!__all_sync(0xFFFFFFFFu, ok)) {                           // the whole warp stops together
       s_stop = 1;
       break;
@@ -444,7 +445,9 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
 }
 
 template <int MB>
-cudaError_t launch_w4s(const W4Args& g, cudaStream_t st) {
+cudaError_t launch_w4s(const W4Args& g0, cudaStream_t st) {
+  W4Args g = g0;
+  g.err = wait_error_flag();
   const size_t smem = (size_t)kW4Stages * kW4Cols * (g.K / 2) + (size_t)MB * g.K * 4 +
                       (size_t)MB * 64 * kQStride * 2 + (size_t)MB * 64 * 8;
   auto kern = k_gemv_w4s<MB>;

@@ -17,5 +17,8 @@ cudaError_t gemm_mma(const GemmArgs& g, cudaStream_t st);
 int mma_min_rows();
 // Nonzero when a bounded wait of the tensor-core kernel gave up (1 producer, 2 MMA, 3 epilogue).
 int mma_error_code();
+// The device word every streaming kernel records a given-up bounded wait in (codes: tensor-core
+// GEMM 1-5, grouped GEMV 21-22, streamed W4A16 GEMV 11-12); read by tc_wait_error.
+int* wait_error_flag();
 
 }  // namespace tc
