@@ -111,12 +111,19 @@ int tc_set_mma_min_rows(int32_t rows);
  * min(cap, 2048 * 8) stamps; returns that count (or TC_ERR_CUDA). No counterpart in the reference
  * (a diagnostic). */
 int tc_mma_trace(int32_t enable, uint64_t* out, uint32_t cap);
-/* The device word in which the streaming kernels (tensor-core GEMM, grouped GEMV, streamed W4A16
- * GEMV) record a bounded wait that gave up instead of hanging: 0 = none, else the code of the
- * first one (GEMM 1-5, grouped GEMV 21-22, W4A16 GEMV 11-12); a kernel that gave up skipped the
- * rest of its work, so its outputs are incomplete. clear != 0 resets the word. Synchronous;
- * TC_ERR_CUDA if it cannot be read. No counterpart in the reference (its golden model never waits). */
+/* The device word (one per device: the current device's is read) in which the streaming kernels
+ * (tensor-core GEMM, grouped GEMV, streamed W4A16 GEMV) record a bounded wait that gave up instead
+ * of hanging: 0 = none, else the code of the first one since the word was last cleared (GEMM 1-5,
+ * grouped GEMV 21-22, W4A16 GEMV 11-12); a kernel that gave up skipped the rest of its work, so its
+ * outputs are incomplete. clear != 0 resets the word. Synchronous; TC_ERR_CUDA if it cannot be
+ * read. No counterpart in the reference (its golden model never waits). */
 int tc_wait_error(int32_t clear);
+/* The number of polls after which the bounded waits for work give up, for launches enqueued from
+ * now on (default and maximum 2^22, about a second on a B200; 0 makes every such wait give up at
+ * once, which is how the give-up path is tested without a hang or a fault). The waits that let a
+ * block's in-flight copies land before it exits keep the full limit. Returns the previous value.
+ * No counterpart in the reference. */
+uint32_t tc_set_spin_limit(uint32_t polls);
 
 /* Host-only helpers (no device needed). golden.Machine.validate (golden.py:59-169): decodes the
  * 23 fields of contract.py:14-38 into fields[23] (in that table's order) and returns the first
@@ -134,9 +141,11 @@ int tc_footprint(const uint8_t* raw64, tc_seg* out, uint32_t cap, uint32_t* coun
  * (img: H*W pixel rows of Cin int8 with row stride ld; weights: int8 [N, KH*KW*Cin]; scale: fp32
  * [N] or [1]; bias: fp32 [N] or NULL; y: OH*OW rows with stride ldy in format out: 0 fp32,
  * 1 bf16, 2 int8 via out_scale); work is enqueued on `stream` (a cudaStream_t, NULL = default).
- * The first call on a device looks the array up with that device current. Calls share the array
- * and it keeps the last call's contents (every byte a call reads it writes first); calls that
- * overlap on the GPU race, so order them on one stream. */
+ * The first call on a device looks the array up with that device current; under CUDA's lazy
+ * module loading that call also loads the array onto the device, so make it before any stream
+ * capture. Calls share the array and it keeps the last call's contents (every byte a call reads it
+ * writes first); calls that overlap on the GPU race, so order them on one stream. TC_ERR_ARG for
+ * pad >= KH or KW, or more than 2^31 pixels. */
 int tc_conv_w8a8_noalloc(const uint8_t* img, uint64_t ld, int32_t H, int32_t W, int32_t Cin, int32_t KH,
                          int32_t KW, int32_t stride, int32_t pad, const uint8_t* weights, const float* scale,
                          int32_t per_channel, const float* bias, uint8_t* y, uint64_t ldy, int32_t N,

@@ -59,6 +59,7 @@ SIGNATURES = {
     "tc_set_mma_min_rows": (ctypes.c_int, [ctypes.c_int32]),
     "tc_mma_trace": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint64), ctypes.c_uint32]),
     "tc_wait_error": (ctypes.c_int, [ctypes.c_int32]),
+    "tc_set_spin_limit": (ctypes.c_uint32, [ctypes.c_uint32]),
     "tc_conv_w8a8_noalloc": (ctypes.c_int, [VP, ctypes.c_uint64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                             ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, VP, VP,
                                             ctypes.c_int32, VP, VP, ctypes.c_uint64, ctypes.c_int32, ctypes.c_int32,

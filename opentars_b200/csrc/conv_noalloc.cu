@@ -6,8 +6,7 @@
 // for its own allocator up front, an embedder that must keep a fixed, load-time-known device
 // footprint, or a latency-critical loop that cannot afford the device-wide synchronisation that
 // cudaMalloc / cudaFree may cause. This entry point serves them: the gather buffer is a fixed
-// array in device global memory that exists from the moment the library is loaded, so a call
-// allocates nothing.
+// array in device global memory, so a call allocates nothing.
 //
 // Limits and sharing rules:
 //   * the gathered matrix (OH*OW rows of KH*KW*Cin bytes) must fit kNoAllocScratch bytes;
@@ -18,7 +17,10 @@
 //     clearing between calls, but two calls whose work overlaps on the GPU (different streams,
 //     or different host threads without ordering) race on the array: order them on one stream.
 //   * the first call on each device looks up the array's device address (cudaGetSymbolAddress)
-//     with that device current; later calls reuse it.
+//     with that device current; later calls reuse it. Under CUDA's lazy module loading (the
+//     default) that first call is also what loads the array's module onto the device, so the
+//     16 MiB are taken at the first call on a device, not when the library is loaded. Make that
+//     first call before capturing a stream into a CUDA graph.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -61,11 +63,14 @@ extern "C" int tc_conv_w8a8_noalloc(const uint8_t* img, uint64_t ld, int32_t H, 
                                     uint64_t ldy, int32_t N, int32_t act, int32_t out, float out_scale,
                                     void* stream) {
   if (!img || !weights || !scale || !y || H <= 0 || W <= 0 || Cin <= 0 || KH <= 0 || KW <= 0 || stride <= 0 ||
-      pad < 0 || N <= 0 || act < 0 || act > 7 || out < 0 || out > 2 || ld < (uint64_t)Cin)
+      pad < 0 || pad >= KH || pad >= KW || N <= 0 || act < 0 || act > 7 || out < 0 || out > 2 || ld < (uint64_t)Cin)
     return TC_ERR_ARG;
-  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
-  if (H + 2 * pad < KH || W + 2 * pad < KW || OH < 1 || OW < 1) return TC_ERR_ARG;
-  const uint64_t K = (uint64_t)KH * KW * Cin, M = (uint64_t)OH * OW;
+  // every index the gather computes stays far inside 64 bits: at most 2^31 pixels
+  if ((uint64_t)H * (uint64_t)W > (1ull << 31)) return TC_ERR_ARG;
+  const int64_t HP = (int64_t)H + 2 * (int64_t)pad, WP = (int64_t)W + 2 * (int64_t)pad;
+  if (HP < KH || WP < KW) return TC_ERR_ARG;
+  const int64_t OH = (HP - KH) / stride + 1, OW = (WP - KW) / stride + 1;
+  const uint64_t K = (uint64_t)KH * KW * Cin, M = (uint64_t)OH * (uint64_t)OW;
   if (K % 16 || M > 65535 || K > 65535 || ldy < (uint64_t)N * (out == 0 ? 4 : out == 1 ? 2 : 1)) return TC_ERR_ARG;
   if (M * K > kNoAllocScratch) return TC_ERR_TOO_LARGE;
   void* scratch = nullptr;
@@ -74,7 +79,7 @@ extern "C" int tc_conv_w8a8_noalloc(const uint8_t* img, uint64_t ld, int32_t H, 
 
   tc::Im2colArgs ia{};
   ia.img = img; ia.ld = ld; ia.out = (uint8_t*)scratch;
-  ia.H = H; ia.W = W; ia.KH = KH; ia.KW = KW; ia.S = stride; ia.P = pad; ia.Cin = Cin; ia.OH = OH; ia.OW = OW;
+  ia.H = H; ia.W = W; ia.KH = KH; ia.KW = KW; ia.S = stride; ia.P = pad; ia.Cin = Cin; ia.OH = (int)OH; ia.OW = (int)OW;
   if (tc::launch_im2col(ia, st) != cudaSuccess) return TC_ERR_CUDA;
 
   tc::GemmArgs g{};

@@ -237,12 +237,97 @@ __global__ void __launch_bounds__(32 * (1 + s_stages<KU>()), 2)
   __syncthreads();
   int j = 0;                                                  // the entry of chunk c_begin
   while (c_begin >= grp.c0[j + 1] && j + 1 < grp.n) ++j;
+  __shared__ int s_issued;
+  // consumer warp st + 1 owns stage st and takes every S-th chunk
+  auto consume = [&](const int st) {
+    const uint8_t* stage = smem + (size_t)st * kStage;
+    uint4 areg[MB == 1 ? KU : 1];                               // M = 1: the activation row in registers
+    int areg_j = -1;
+    for (int c = c_begin + st, t = st; c < c_end; c += S, t += S) {
+      const bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[st], (t / S) & 1, grp.err, 22, grp.spin);
+      if (!__all_sync(0xFFFFFFFFu, ok)) {                           // the whole warp stops together
+        s_stop = 1;
+        break;
+      }
+      while (c >= grp.c0[j + 1]) ++j;
+      const GemmArgs& g = grp.g[j];
+      const int local = c - grp.c0[j], ncx = grp.ncx[j];
+      const int by = local / ncx, cx = local - by * ncx;
+      const int m0 = by * MB, mb = min(MB, g.M - m0);
+      const uint8_t* arow = g.A + (uint64_t)m0 * g.lda;
+      if constexpr (MB == 1) {
+        if (areg_j != j) {
+#pragma unroll
+          for (int u = 0; u < KU; ++u) {
+            const int k = lane * 16 + 512 * u;
+            areg[u] = k < g.K ? ldg_l1(arow + k) : make_uint4(0, 0, 0, 0);
+          }
+          areg_j = j;
+        }
+      }
+      const float* ssc = reinterpret_cast<const float*>(stage + kWB);
+      const float* sbi = reinterpret_cast<const float*>(stage + kWB + 64);
+      // the epilogue lanes' scale and bias before the stage is released
+      const int i_mine = lane >> 1, m_mine = i_mine / CB, c_mine = i_mine - m_mine * CB;
+      float sc[kSCols / CB], bi[kSCols / CB];
+#pragma unroll
+      for (int b = 0; b < kSCols / CB; ++b) {
+        sc[b] = g.per_channel ? ssc[b * CB + c_mine] : 0.0f;
+        bi[b] = g.bias ? sbi[b * CB + c_mine] : 0.0f;
+      }
+      int res[kSCols / CB];
+#pragma unroll
+      for (int b = 0; b < kSCols / CB; ++b) {
+        int acc[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = 0;
+#pragma unroll
+        for (int u = 0; u < KU; ++u) {
+          const int k = lane * 16 + 512 * u;
+          if (k < g.K) {
+            uint4 a[MB];
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+              if constexpr (MB == 1) a[m] = areg[u];
+              else a[m] = m < mb ? ldg_l1(arow + (uint64_t)m * g.lda + k) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int cc = 0; cc < CB; ++cc) {
+              const uint4 w = *reinterpret_cast<const uint4*>(stage + (size_t)(b * CB + cc) * g.K + k);
+#pragma unroll
+              for (int m = 0; m < MB; ++m) acc[m * CB + cc] = dot16(a[m], w, acc[m * CB + cc]);
+            }
+          }
+        }
+        // transpose reduction: after the step with offset o, lane bit o selects which half it keeps
+#pragma unroll
+        for (int o = 16, v = 16; o >= 2; o >>= 1, v >>= 1) {
+          const bool hi = (lane & o) != 0;
+#pragma unroll
+          for (int i = 0; i < v / 2; ++i) {
+            const int send = hi ? acc[i] : acc[i + v / 2];
+            const int keep = hi ? acc[i + v / 2] : acc[i];
+            acc[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, o);
+          }
+        }
+        res[b] = acc[0] + __shfl_xor_sync(0xFFFFFFFFu, acc[0], 1);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);                   // the stage's bytes are consumed
+      const float sc0 = g.per_channel ? 0.0f : ld_f32(g.scale);
+      if ((lane & 1) == 0 && m_mine < mb) {
+#pragma unroll
+        for (int b = 0; b < kSCols / CB; ++b)
+          gemm_epilogue_v(g, m0 + m_mine, cx * kSCols + b * CB + c_mine, res[b], g.per_channel ? sc[b] : sc0, bi[b]);
+      }
+    }
+  };
   if (warp == 0) {
     if (lane == 0) {
       int t = 0;
       for (int c = c_begin; c < c_end; ++c, ++t) {
         const int st = t % S;
-        if (!mbar_wait(&empty[st], ((t / S) & 1) ^ 1, grp.err, 21)) {
+        if (!mbar_wait(&empty[st], ((t / S) & 1) ^ 1, grp.err, 21, grp.spin)) {
           s_stop = 1;
           break;
         }
@@ -256,93 +341,16 @@ __global__ void __launch_bounds__(32 * (1 + s_stages<KU>()), 2)
         if (g.per_channel) bulk_load(dst + kWB, g.scale + 64 * (uint64_t)cx, 64, &full[st]);
         if (g.bias) bulk_load(dst + kWB + 64, g.bias + 64 * (uint64_t)cx, 64, &full[st]);
       }
+      s_issued = t;
     }
-    return;
+  } else {
+    consume(warp - 1);
   }
-  const int st = warp - 1;                                    // this warp's stage
-  const uint8_t* stage = smem + (size_t)st * kStage;
-  uint4 areg[MB == 1 ? KU : 1];                               // M = 1: the activation row in registers
-  int areg_j = -1;
-  for (int c = c_begin + st, t = st; c < c_end; c += S, t += S) {
-    const bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[st], (t / S) & 1, grp.err, 22);
-    if (!__all_sync(0xFFFFFFFFu, ok)) {                           // the whole warp stops together
-      s_stop = 1;
-      // the stage's copies may still be in flight: wait for them (bounded) before the block exits
-      mbar_wait(&full[st], (t / S) & 1, nullptr, 0);
-      break;
-    }
-    while (c >= grp.c0[j + 1]) ++j;
-    const GemmArgs& g = grp.g[j];
-    const int local = c - grp.c0[j], ncx = grp.ncx[j];
-    const int by = local / ncx, cx = local - by * ncx;
-    const int m0 = by * MB, mb = min(MB, g.M - m0);
-    const uint8_t* arow = g.A + (uint64_t)m0 * g.lda;
-    if constexpr (MB == 1) {
-      if (areg_j != j) {
-#pragma unroll
-        for (int u = 0; u < KU; ++u) {
-          const int k = lane * 16 + 512 * u;
-          areg[u] = k < g.K ? ldg_l1(arow + k) : make_uint4(0, 0, 0, 0);
-        }
-        areg_j = j;
-      }
-    }
-    const float* ssc = reinterpret_cast<const float*>(stage + kWB);
-    const float* sbi = reinterpret_cast<const float*>(stage + kWB + 64);
-    // the epilogue lanes' scale and bias before the stage is released
-    const int i_mine = lane >> 1, m_mine = i_mine / CB, c_mine = i_mine - m_mine * CB;
-    float sc[kSCols / CB], bi[kSCols / CB];
-#pragma unroll
-    for (int b = 0; b < kSCols / CB; ++b) {
-      sc[b] = g.per_channel ? ssc[b * CB + c_mine] : 0.0f;
-      bi[b] = g.bias ? sbi[b * CB + c_mine] : 0.0f;
-    }
-    int res[kSCols / CB];
-#pragma unroll
-    for (int b = 0; b < kSCols / CB; ++b) {
-      int acc[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i] = 0;
-#pragma unroll
-      for (int u = 0; u < KU; ++u) {
-        const int k = lane * 16 + 512 * u;
-        if (k < g.K) {
-          uint4 a[MB];
-#pragma unroll
-          for (int m = 0; m < MB; ++m) {
-            if constexpr (MB == 1) a[m] = areg[u];
-            else a[m] = m < mb ? ldg_l1(arow + (uint64_t)m * g.lda + k) : make_uint4(0, 0, 0, 0);
-          }
-#pragma unroll
-          for (int cc = 0; cc < CB; ++cc) {
-            const uint4 w = *reinterpret_cast<const uint4*>(stage + (size_t)(b * CB + cc) * g.K + k);
-#pragma unroll
-            for (int m = 0; m < MB; ++m) acc[m * CB + cc] = dot16(a[m], w, acc[m * CB + cc]);
-          }
-        }
-      }
-      // transpose reduction: after the step with offset o, lane bit o selects which half it keeps
-#pragma unroll
-      for (int o = 16, v = 16; o >= 2; o >>= 1, v >>= 1) {
-        const bool hi = (lane & o) != 0;
-#pragma unroll
-        for (int i = 0; i < v / 2; ++i) {
-          const int send = hi ? acc[i] : acc[i + v / 2];
-          const int keep = hi ? acc[i + v / 2] : acc[i];
-          acc[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, o);
-        }
-      }
-      res[b] = acc[0] + __shfl_xor_sync(0xFFFFFFFFu, acc[0], 1);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);                   // the stage's bytes are consumed
-    const float sc0 = g.per_channel ? 0.0f : ld_f32(g.scale);
-    if ((lane & 1) == 0 && m_mine < mb) {
-#pragma unroll
-      for (int b = 0; b < kSCols / CB; ++b)
-        gemm_epilogue_v(g, m0 + m_mine, cx * kSCols + b * CB + c_mine, res[b], g.per_channel ? sc[b] : sc0, bi[b]);
-    }
-  }
+  // After a wait gave up, copies of the last chunks issued may still be in flight: the block does
+  // not exit before they land (these waits always have the full limit).
+  __syncthreads();
+  if (threadIdx.x == 0 && s_stop)
+    for (int u = s_issued > S ? s_issued - S : 0; u < s_issued; ++u) mbar_wait(&full[u % S], (u / S) & 1, nullptr, 0);
 }
 
 template <int MB, int KU>
@@ -369,7 +377,7 @@ __global__ void k_im2col(Im2colArgs a) {
     const int oy = r / a.OW, ox = r - oy * a.OW;
     const int iy = oy * a.S - a.P + ky, ix = ox * a.S - a.P + kx;
     uint8_t v = 0;
-    if (iy >= 0 && iy < a.H && ix >= 0 && ix < a.W) v = a.img[(uint64_t)(iy * a.W + ix) * a.ld + ci];
+    if (iy >= 0 && iy < a.H && ix >= 0 && ix < a.W) v = a.img[((uint64_t)iy * a.W + ix) * a.ld + ci];
     a.out[i] = v;
   }
 }
@@ -416,6 +424,7 @@ int gemv8_class(const GemmArgs& g) {
 
 cudaError_t launch_gemv8_group(GemvGroup& grp, cudaStream_t st) {
   grp.err = wait_error_flag();
+  grp.spin = spin_limit();
   switch (grp.mb * 16 + grp.ku) {
     case 1 * 16 + 2: return launch_group<1, 2>(grp, st);
     case 1 * 16 + 4: return launch_group<1, 4>(grp, st);

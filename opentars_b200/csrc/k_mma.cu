@@ -31,6 +31,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdlib>
+#include <mutex>
 
 #include "../../include/tarscuda.h"
 #include "engine.h"
@@ -79,6 +80,7 @@ struct MmaShape {
   int nkb1, nkb2, kb;               // K slices of the two K blocks; kb = first token column of block 2
   int gated, nacc, split, stages, items, nbuf, trace;
   int* err;
+  uint32_t spin;                    // poll limit of the bounded waits for work
 };
 
 // Epilogues. row() holds what depends on the weight row only (scales pre-flushed), tok() the
@@ -269,7 +271,7 @@ template <class Epi>
 __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ MmaMaps maps, const MmaShape sh,
                                                         const Epi epi) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_full[kMaxStages], bar_empty[kMaxStages], bar_accf[2], bar_acce[2], bar_recv;
+  __shared__ uint64_t bar_full[kMaxStages], bar_empty[kMaxStages], bar_accf[2], bar_acce[2], bar_recv, bar_drain;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ float s_tok[2][256];             // the tile's token factors (double buffered per tile)
@@ -326,6 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
       mbar_init(&bar_accf[i], 1);
       mbar_init(&bar_acce[i], kEpiWarps);
     }
+    mbar_init(&bar_drain, 1);
     s_abort = 0;
     if (split > 1) {
       // the owner's slots receive (split - 1) peers' partial rows
@@ -348,6 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
   int* R = reinterpret_cast<int*>(smem + S * stage_bytes);   // slots [acc][sender][row][RL]
   if (threadIdx.x == 0) stamp(1);
 
+  uint32_t issued = 0;                           // the producer's count of K slices issued
   if (warp == 0) {
     if (lane == 0 && nk > 0) {
       // producer: K slice q (counted over all items of this CTA) into stage q % S
@@ -391,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
             if (q == 0) stamp(2);
             continue;
           }
-          if (!mbar_wait(&bar_empty[st], ((q / S) & 1) ^ 1, sh.err, 1)) {
+          if (!mbar_wait(&bar_empty[st], ((q / S) & 1) ^ 1, sh.err, 1, sh.spin)) {
             s_abort = 1;
             stop = true;
             break;
@@ -405,9 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
           load_x(st, tok0, k);
         }
       }
-      if (stop) {   // wait (bounded) for the copies still in flight before the CTA ends
-        for (uint32_t i = q > (uint32_t)S ? q - S : 0; i < q; ++i) mbar_wait(&bar_full[i % S], (i / S) & 1, nullptr, 0);
-      }
+      issued = q;
     }
   } else if (warp == 1) {
     if (lane == 0 && nk > 0) {
@@ -419,8 +421,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
       for (int item = item0; item < sh.items && !stop; item += istride, ++t) {
         const int buf = sh.nbuf == 2 ? (t & 1) : 0;
         const uint32_t use = sh.nbuf == 2 ? (t >> 1) : t;
-        if (use > 0 && !mbar_wait(&bar_acce[buf], (use & 1) ^ 1, sh.err, 2)) {
+        if (use > 0 && !mbar_wait(&bar_acce[buf], (use & 1) ^ 1, sh.err, 2, sh.spin)) {
           s_abort = 1;
+          stop = true;
           break;
         }
         tc_fence_after();
@@ -428,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
         bool first0 = true, first1 = true;
         for (int i = 0; i < nk; ++i, ++q) {
           const int st = q % S;
-          if (!mbar_wait(&bar_full[st], (q / S) & 1, sh.err, 3) || aborted(&s_abort)) {
+          if (!mbar_wait(&bar_full[st], (q / S) & 1, sh.err, 3, sh.spin) || aborted(&s_abort)) {
             s_abort = 1;
             stop = true;
             break;
@@ -455,6 +458,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
           mma_commit(&bar_empty[st]);
         }
         mma_commit(&bar_accf[buf]);
+      }
+      if (q > 0) {
+        // every MMA issued has completed before the block frees TMEM or exits, also when a wait
+        // elsewhere gave up (this wait always has the full limit)
+        mma_commit(&bar_drain);
+        mbar_wait(&bar_drain, 0, nullptr, 0);
       }
       stamp(4);
     }
@@ -496,10 +505,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
           rw_first = epi.row(s, row0 + r);
         }
       }
-      if (epi_sync_or(aborted(&s_abort))) break;
+      // (split-K: every CTA pushes its rows even after a give-up, so no owner waits in vain)
+      if (split == 1 && epi_sync_or(aborted(&s_abort))) break;
       bool ok = true;
       if (nk > 0) {
-        ok = mbar_wait(&bar_accf[buf], use & 1, sh.err, 4);
+        ok = mbar_wait(&bar_accf[buf], use & 1, sh.err, 4, sh.spin);
         if (!ok) s_abort = 1;
         if (split > 1 && threadIdx.x == 64) stamp(7);   // split-K: the accumulator is ready
       }
@@ -541,9 +551,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
         // TMEM is read: hand it back (warp 1 frees it) before waiting on the peers
         tc_fence_before();
         asm volatile("bar.arrive 2, %0;" ::"n"(32 + 32 * kEpiWarps) : "memory");
+        // every peer pushes its rows, so this wait ends; it has the full limit because the
+        // block must not exit while a peer's stores into its shared memory are in flight
         const bool got = mbar_wait(&bar_recv, 0, sh.err, 5);
         if (threadIdx.x == 64) stamp(5);                // the peers' partial rows have arrived
-        if (epi_sync_or(!got)) {
+        if (epi_sync_or(!got || !ok)) {
           s_abort = 1;
           break;
         }
@@ -629,12 +641,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
       tc_fence_after();
       tmem_dealloc(tmem, ncols);
     }
-    return;
+  } else {
+    tc_fence_before();
   }
-  tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, ncols);
-  if (threadIdx.x == 0) stamp(7);
+  if (split == 1 && warp == 1) tmem_dealloc(tmem, ncols);
+  if (threadIdx.x == 0) {
+    if (split == 1) stamp(7);
+    // after a give-up, the last K slices issued may still be in flight: they land before the
+    // block exits (these waits always have the full limit)
+    if (aborted(&s_abort))
+      for (uint32_t i = issued > (uint32_t)S ? issued - S : 0; i < issued; ++i)
+        mbar_wait(&bar_full[i % S], (i / S) & 1, nullptr, 0);
+  }
 }
 
 // ------------------------------------------------------------------------------------ host side
@@ -663,16 +682,25 @@ bool make_map(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uin
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Error code of the bounded waits (static device memory: the kernel allocates nothing).
+// Error code of the bounded waits (static device memory: the kernel allocates nothing). The
+// symbol has its own address on every device, so the address is looked up (once) per device,
+// with that device current.
 __device__ int g_mma_err;
+constexpr int kMaxDevices = 64;
+std::mutex g_err_mutex;
+int* g_err_ptr[kMaxDevices] = {};
 int* err_flag() {
-  static int* p = nullptr;
-  if (!p) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_err_mutex);
+  if (!g_err_ptr[dev]) {
     void* a = nullptr;
-    if (cudaGetSymbolAddress(&a, g_mma_err) == cudaSuccess) p = static_cast<int*>(a);
+    if (cudaGetSymbolAddress(&a, g_mma_err) != cudaSuccess) return nullptr;
+    g_err_ptr[dev] = static_cast<int*>(a);
   }
-  return p;
+  return g_err_ptr[dev];
 }
+std::atomic<uint32_t> g_spin{kSpinLimit};
 
 // Token tile, mode (split-K factor or persistent), stages, shared memory and grid.
 bool plan(MmaShape& sh, int tiles, int* smem, int* grid) {
@@ -727,6 +755,7 @@ bool plan(MmaShape& sh, int tiles, int* smem, int* grid) {
   const int want = g_trace_on.load();
   sh.trace = want > 0 && g_trace_count.fetch_add(1) + 1 == want;
   sh.err = err_flag();
+  sh.spin = spin_limit();
   return sh.err != nullptr;
 }
 
@@ -821,7 +850,13 @@ int mma_error_code() {
 
 int* wait_error_flag() { return err_flag(); }
 
+uint32_t spin_limit() { return g_spin.load(); }
+
 }  // namespace tc
+
+extern "C" uint32_t tc_set_spin_limit(uint32_t polls) {
+  return tc::g_spin.exchange(polls == 0 ? 0u : std::min(polls, tc::kSpinLimit));
+}
 
 extern "C" int tc_wait_error(int32_t clear) {
   int* p = tc::wait_error_flag();

@@ -343,111 +343,123 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
   align_rows<MB>(g, mb, sX, sQ, sS, sSum);
   __syncthreads();
 
+  // consumer warp cw + 1 computes column cw of every chunk
+  auto compute = [&](const int cw) {
+    // the fp16 group scales of this warp's next column are loaded one column ahead
+    auto load_ws = [&](int col, uint16_t (&h)[2]) {
+#pragma unroll
+      for (int slot = 0; slot < 2; ++slot) {
+        const int gi = lane + 32 * slot;
+        h[slot] = (col < g.N && gi < G) ? ld_u16(g.scale + 2 * ((uint64_t)col * G + gi)) : (uint16_t)0;
+      }
+    };
+    uint16_t wsh[2], wsn[2];
+    load_ws(blockIdx.x * kW4Cols + cw, wsh);
+    int t = 0;
+    for (int c = blockIdx.x; c < nchunk; c += gridDim.x, ++t) {
+      const int st = t % kW4Stages;
+      load_ws((c + gridDim.x) * kW4Cols + cw, wsn);
+      const bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[st], (t / kW4Stages) & 1, g.err, 12, g.spin);
+      if (!__all_sync(0xFFFFFFFFu, ok)) {                           // the whole warp stops together
+        s_stop = 1;
+        break;
+      }
+      const int n = c * kW4Cols + cw;
+      if (n < g.N) {
+        const uint8_t* colp = ring + st * stage_b + cw * colb;
+        float term[MB][2];
+#pragma unroll
+        for (int slot = 0; slot < 2; ++slot) {
+          const int gi = lane + 32 * slot;
+#pragma unroll
+          for (int m = 0; m < MB; ++m) term[m][slot] = 0.0f;
+          if (gi < G) {
+            const float ws = from_fp16(wsh[slot]);
+            uint4 wv[4];
+            int pc[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              pc[i] = (i + (lane >> 1)) & 3;
+              wv[i] = *reinterpret_cast<const uint4*>(colp + gi * 64 + 16 * pc[i]);
+            }
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+              if (m < mb) {
+                const uint4* q = reinterpret_cast<const uint4*>(sQ + (m * 64 + gi) * kQStride);
+                const int dot = group_dot(
+                    [&](int c) {
+                      const uint4& v = wv[c >> 2];
+                      return (c & 3) == 0 ? v.x : (c & 3) == 1 ? v.y : (c & 3) == 2 ? v.z : v.w;
+                    },
+                    [&](int c) { return q[pc[c >> 2] * 4 + (c & 3)]; }, sSum[m * 64 + gi]);
+                term[m][slot] = group_term(dot, ws, bf(sS[m * 64 + gi]));
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);                     // the weights are in registers
+        const int b = lane & 3;
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+          float tt[16];                                             // group b + 4 i: lane (b + 4 i) mod 32
+#pragma unroll
+          for (int i = 0; i < 16; ++i) tt[i] = __shfl_sync(0xFFFFFFFFu, term[m][i < 8 ? 0 : 1], (b + 4 * i) & 31);
+          float bank = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (b + 4 * i < G) bank = fadd_nc(bank, tt[i]);
+          bank = canon(bank);
+          const float b1 = __shfl_sync(0xFFFFFFFFu, bank, 1);
+          const float b2 = __shfl_sync(0xFFFFFFFFu, bank, 2);
+          const float b3 = __shfl_sync(0xFFFFFFFFu, bank, 3);
+          if (lane == 0 && m < mb) {
+            float y = fadd(fadd(bank, b1), fadd(b2, b3));
+            if (g.bias) y = fadd(y, ld_f32(g.bias + 4 * (uint64_t)n));
+            y = act_fn(y, g.act);
+            store_out(g.Y + (uint64_t)(m0 + m) * g.ldy, n, y, g.out, g.out_scale);
+          }
+        }
+      } else {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+      }
+      wsh[0] = wsn[0];
+      wsh[1] = wsn[1];
+    }
+  };
+  __shared__ int s_issued;
   if (warp == 0) {
     if (lane == 0) {
       // producer: chunk t of this block into stage t % kW4Stages once its 8 columns are done
       int t = issued;
       for (int c = blockIdx.x + issued * gridDim.x; c < nchunk; c += gridDim.x, ++t) {
         const int st = t % kW4Stages;
-        if (!mbar_wait(&empty[st], ((t / kW4Stages) & 1) ^ 1, g.err, 11)) {
+        if (!mbar_wait(&empty[st], ((t / kW4Stages) & 1) ^ 1, g.err, 11, g.spin)) {
           s_stop = 1;
           break;
         }
         mbar_expect_tx(&full[st], chunk_bytes(c));
         bulk_load(ring + st * stage_b, g.W + (uint64_t)c * stage_b, chunk_bytes(c), &full[st]);
       }
+      s_issued = t;
     }
-    return;
+  } else {
+    compute(warp - 1);
   }
-  const int cw = warp - 1;                                        // this warp's column in a chunk
-  // the fp16 group scales of this warp's next column are loaded one column ahead
-  auto load_ws = [&](int col, uint16_t (&h)[2]) {
-#pragma unroll
-    for (int slot = 0; slot < 2; ++slot) {
-      const int gi = lane + 32 * slot;
-      h[slot] = (col < g.N && gi < G) ? ld_u16(g.scale + 2 * ((uint64_t)col * G + gi)) : (uint16_t)0;
-    }
-  };
-  uint16_t wsh[2], wsn[2];
-  load_ws(blockIdx.x * kW4Cols + cw, wsh);
-  int t = 0;
-  for (int c = blockIdx.x; c < nchunk; c += gridDim.x, ++t) {
-    const int st = t % kW4Stages;
-    load_ws((c + gridDim.x) * kW4Cols + cw, wsn);
-    const bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[st], (t / kW4Stages) & 1, g.err, 12);
-    if (!__all_sync(0xFFFFFFFFu, ok)) {                           // the whole warp stops together
-      s_stop = 1;
-      break;
-    }
-    const int n = c * kW4Cols + cw;
-    if (n < g.N) {
-      const uint8_t* colp = ring + st * stage_b + cw * colb;
-      float term[MB][2];
-#pragma unroll
-      for (int slot = 0; slot < 2; ++slot) {
-        const int gi = lane + 32 * slot;
-#pragma unroll
-        for (int m = 0; m < MB; ++m) term[m][slot] = 0.0f;
-        if (gi < G) {
-          const float ws = from_fp16(wsh[slot]);
-          uint4 wv[4];
-          int pc[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            pc[i] = (i + (lane >> 1)) & 3;
-            wv[i] = *reinterpret_cast<const uint4*>(colp + gi * 64 + 16 * pc[i]);
-          }
-#pragma unroll
-          for (int m = 0; m < MB; ++m) {
-            if (m < mb) {
-              const uint4* q = reinterpret_cast<const uint4*>(sQ + (m * 64 + gi) * kQStride);
-              const int dot = group_dot(
-                  [&](int c) {
-                    const uint4& v = wv[c >> 2];
-                    return (c & 3) == 0 ? v.x : (c & 3) == 1 ? v.y : (c & 3) == 2 ? v.z : v.w;
-                  },
-                  [&](int c) { return q[pc[c >> 2] * 4 + (c & 3)]; }, sSum[m * 64 + gi]);
-              term[m][slot] = group_term(dot, ws, bf(sS[m * 64 + gi]));
-            }
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);                     // the weights are in registers
-      const int b = lane & 3;
-#pragma unroll
-      for (int m = 0; m < MB; ++m) {
-        float tt[16];                                             // group b + 4 i: lane (b + 4 i) mod 32
-#pragma unroll
-        for (int i = 0; i < 16; ++i) tt[i] = __shfl_sync(0xFFFFFFFFu, term[m][i < 8 ? 0 : 1], (b + 4 * i) & 31);
-        float bank = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (b + 4 * i < G) bank = fadd_nc(bank, tt[i]);
-        bank = canon(bank);
-        const float b1 = __shfl_sync(0xFFFFFFFFu, bank, 1);
-        const float b2 = __shfl_sync(0xFFFFFFFFu, bank, 2);
-        const float b3 = __shfl_sync(0xFFFFFFFFu, bank, 3);
-        if (lane == 0 && m < mb) {
-          float y = fadd(fadd(bank, b1), fadd(b2, b3));
-          if (g.bias) y = fadd(y, ld_f32(g.bias + 4 * (uint64_t)n));
-          y = act_fn(y, g.act);
-          store_out(g.Y + (uint64_t)(m0 + m) * g.ldy, n, y, g.out, g.out_scale);
-        }
-      }
-    } else {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-    }
-    wsh[0] = wsn[0];
-    wsh[1] = wsn[1];
-  }
+  // After a wait gave up, copies of the last chunks issued may still be in flight: the block does
+  // not exit before they land (these waits always have the full limit).
+  __syncthreads();
+  if (threadIdx.x == 0 && s_stop)
+    for (int u = s_issued > kW4Stages ? s_issued - kW4Stages : 0; u < s_issued; ++u)
+      mbar_wait(&full[u % kW4Stages], (u / kW4Stages) & 1, nullptr, 0);
 }
 
 template <int MB>
 cudaError_t launch_w4s(const W4Args& g0, cudaStream_t st) {
   W4Args g = g0;
   g.err = wait_error_flag();
+  g.spin = spin_limit();
   const size_t smem = (size_t)kW4Stages * kW4Cols * (g.K / 2) + (size_t)MB * g.K * 4 +
                       (size_t)MB * 64 * kQStride * 2 + (size_t)MB * 64 * 8;
   auto kern = k_gemv_w4s<MB>;

@@ -37,6 +37,7 @@ struct GemvGroup {
   int ncx[kGroupMax];
   GemmArgs g[kGroupMax];
   int* err;                          // device word for a bounded wait that gave up (set by the launcher)
+  uint32_t spin;                     // poll limit of the bounded waits (set by the launcher)
 };
 // The class of a GEMM that the grouped decode GEMV computes (MB * 16 + KU), or -1.
 int gemv8_class(const GemmArgs& g);
@@ -54,6 +55,7 @@ struct W4Args {
   int M, N, K, act, out;
   float out_scale;
   int* err;                          // device word for a bounded wait that gave up (set by the launcher)
+  uint32_t spin;                     // poll limit of the bounded waits (set by the launcher)
 };
 cudaError_t launch_gemm_w4a16(const W4Args& g, cudaStream_t st);
 

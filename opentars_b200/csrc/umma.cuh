@@ -9,14 +9,19 @@
 //   instruction descriptor (32 bit): [4,6) D format (2 = s32), [7,10) A format (1 = s8),
 //     [10,13) B format (1 = s8), bit 15 / 16 A / B major (0 = K-major), [17,23) N >> 3,
 //     [24,29) M >> 4.
-// Every wait on an mbarrier is bounded: after kSpinLimit polls it records an error code and
-// returns false, and the callers then skip the rest of their work (no fault, no hang).
+// Every wait on an mbarrier is bounded: after a given number of polls it records an error code and
+// returns false, and the callers then skip the rest of their work (no fault, no hang). The waits
+// for work take their limit from the launch (spin_limit(): kSpinLimit unless a caller lowered it
+// with tc_set_spin_limit); the waits that drain copies still in flight before a block exits always
+// use kSpinLimit, so a block never leaves while a copy into its shared memory is pending.
 #pragma once
 #include <cstdint>
 
 namespace tc {
 
 constexpr uint32_t kSpinLimit = 1u << 22;
+// The poll limit the launchers pass to the bounded waits of their kernels (host side).
+uint32_t spin_limit();
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -43,11 +48,13 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-// Waits for the phase of `parity` to complete; false (and *err = code) after kSpinLimit polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+// Waits for the phase of `parity` to complete; false after `limit` polls, and then the first code
+// recorded since the word was last cleared stays in *err (later give-ups do not overwrite it).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          uint32_t limit = kSpinLimit) {
+  for (uint32_t i = 0; i < limit; ++i)
     if (mbar_test(bar, parity)) return true;
-  if (err) atomicExch(err, code);
+  if (err) atomicCAS(err, 0, code);
   return false;
 }
 

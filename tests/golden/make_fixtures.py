@@ -16,6 +16,9 @@ What it stores (all small):
   models.json      (--models) per-step logits SHA-256 / argmax of the reference's QwenLowering
                    + golden Machine greedy decode for small Qwen3 / Gemma-3 configs, and the
                    SHA-256 of the lowered DDR image and queue bytes
+  context.json     (--context) the whole 256-token context at the real head dims (Qwen3: 16 q /
+                   8 kv heads of 128; Gemma 3: 4 q / 1 kv head of 256, 5 sliding layers to 1 full):
+                   per prompt, every run's logits SHA-256 from the last prompt token to position 255
   gemm_sweep.json  (--gemm) config 1: the SHA-256 of every (M, shape) output of bench.py's GEMM
                    sweep image (bench.build_gemm, seed 1234) run on the reference golden Machine
 """
@@ -376,6 +379,58 @@ def make_full_models(ref: str, only: str = ""):
     return out
 
 
+# The whole context (max_tokens 256, positions 0 .. 255) at the real head dims: name, base config,
+# layer types, vocab, prompt seeds (one run per prompt). Each prompt is fed one token per run (the
+# prefill of a sequence that joins a running batch), then greedy decode up to position 255.
+CONTEXT_CASES = [
+    ("qwen3_hd128", "Q3_HD128", ["full_attention"] * 2, 4096, (1, 2)),
+    ("gemma3_hd256", "G3_HD256", ["sliding_attention"] * 5 + ["full_attention"], 4096, (1, 2)),
+]
+CONTEXT_T, CONTEXT_PROMPT = 256, 20
+
+
+def make_context(ref: str, only: str = ""):
+    """Per case and prompt: the SHA-256 of the image, and for every run from the last prompt token
+    on, its logits' SHA-256, first 8 logits and argmax (the next token)."""
+    import tars_mini.qwen_ref as Q
+    from tars_mini import golden as G
+    from tars_mini.llm import QwenLowering
+    from tests.model_runs import base_config
+    out = {}
+    for name, base, types, vocab, seeds in CONTEXT_CASES:
+        if only and only != name:
+            continue
+        cfg = Q.make_config(base_config(Q, base, REF_BASE), types, vocab=vocab)
+        w = Q.random_weights(cfg, seed=0, embed=True)
+        runs = []
+        for seed in seeds:
+            t = time.time()
+            low = QwenLowering(cfg, w, max_tokens=CONTEXT_T, ddr_bytes=1 << 26, head=True, queue_cap=4096)
+            image_sha = hashlib.sha256(bytes(low.p.ddr)).hexdigest()
+            prompt = prompt_ids(seed, vocab, CONTEXT_PROMPT)
+
+            ddr, ids, logits = low.p.ddr, list(prompt), []
+            for t0 in range(CONTEXT_T):              # one token per run, as generate() stages a chunk
+                low.put_input(ddr, t0, low.embed(ids[t0:t0 + 1]))
+                a = len(low.p.descs)
+                low.chunk(t0, 1)
+                q, cnt = low.stage(ddr, a, len(low.p.descs))
+                m = G.Machine(ddr, gemv_only=True)
+                assert m.run_queue(q, cnt).done
+                ddr = m.ddr
+                if t0 >= len(prompt) - 1:
+                    lg = low.logits_of(ddr)
+                    logits.append(lg)
+                    if t0 + 1 < CONTEXT_T:
+                        ids.append(int(np.argmax(lg)))
+            runs.append(dict(seed=seed, prompt=prompt, ids=ids,
+                             logits_sha256=[hashlib.sha256(lg.astype("<f4").tobytes()).hexdigest() for lg in logits],
+                             logits_head=[lg[:8].view(np.uint32).tolist() for lg in logits]))
+            print(name, seed, f"{time.time() - t:.1f}s", flush=True)
+        out[name] = dict(base=base, types=types, vocab=vocab, T=CONTEXT_T, image_sha256=image_sha, runs=runs)
+    return out
+
+
 def make_gemm_sweep(G):
     import bench
     p = bench.build_gemm(1, 0)
@@ -395,6 +450,7 @@ def main():
     ap.add_argument("--skip-queues", action="store_true")
     ap.add_argument("--full", default="", help="full-size models: 'all' or one name")
     ap.add_argument("--gemm", action="store_true", help="config 1's GEMM sweep")
+    ap.add_argument("--context", default="", help="whole-context cases: 'all' or one name")
     a = ap.parse_args()
     if not a.ref:
         raise SystemExit("--ref <path to the openTARS checkout> is required")
@@ -418,6 +474,12 @@ def main():
         old.update(make_full_models(a.ref, "" if a.full == "all" else a.full))
         path.write_text(json.dumps(old, indent=1))
         print(f"full models in {time.time() - t:.1f}s")
+    if a.context:
+        path = HERE / "context.json"
+        old = json.loads(path.read_text()) if path.exists() else {}
+        old.update(make_context(a.ref, "" if a.context == "all" else a.context))
+        path.write_text(json.dumps(old))
+        print(f"context cases in {time.time() - t:.1f}s")
     if a.gemm:
         (HERE / "gemm_sweep.json").write_text(json.dumps(make_gemm_sweep(G), indent=1))
         print(f"gemm sweep in {time.time() - t:.1f}s")

@@ -9,6 +9,10 @@ import numpy as np
 
 # fixture bases that are a named config with a few fields changed: name -> (config, changes)
 DERIVED = {"G3_SMALL_K2": ("CFG_G3_SMALL", dict(intermediate_size=4608)),
+           # the whole-context cases: the real head layouts of Qwen3-0.6B (16 q / 8 kv heads of 128)
+           # and Gemma-3-1B (4 q / 1 kv head of 256, down_proj in two K blocks) on a narrow residual
+           "Q3_HD128": ("CFG_Q3_06B", dict(hidden_size=256, intermediate_size=512)),
+           "G3_HD256": ("CFG_G3_1B", dict(hidden_size=256, intermediate_size=4608)),
            # W4A16 needs K >= 256 on every linear: the per-layer-input projection's K is ple_dim
            "G4_SMALL_P256": ("CFG_G4_SMALL", dict(hidden_size_per_layer_input=256))}
 

@@ -1,7 +1,9 @@
-"""tc_conv_w8a8_noalloc, the convolution entry point that allocates no device memory, against the
-regular conv path (a conv descriptor through the drop-in Machine): identical output bytes, on two
-calls in a row with different inputs (the shared fixed buffer keeps the previous call's contents,
-which must not leak into the next result). This file is collected last on purpose."""
+"""tc_conv_w8a8_noalloc, the convolution entry point for callers that cannot let the library
+allocate device memory during a call, against the CPU oracle's conv descriptor and against the
+regular conv path (the same descriptor through the drop-in Machine): identical output bytes on
+three calls in a row - 63 output rows (tensor-core GEMM), then 4 rows (the M <= 8 GEMV) and 12 rows
+(the generic GEMV) after it, so a smaller gather reuses the fixed buffer that a larger one filled
+and stale bytes would show. This file is collected last on purpose."""
 import ctypes
 
 import numpy as np
@@ -12,9 +14,13 @@ from oracle import contract as C
 pytestmark = pytest.mark.gpu
 
 
+# (H, W, KH, KW, stride, pad, Cin, N): OH*OW = 63, 4 and 12 output rows
+SHAPES = [(9, 7, 3, 3, 1, 1, 32, 48), (4, 4, 3, 3, 2, 1, 32, 32), (6, 8, 3, 3, 2, 1, 16, 64)]
+
+
 def _case(seed):
     rng = np.random.default_rng(seed)
-    H, W, KH, KW, S, P, cin, N = 9, 7, 3, 3, 1 + seed % 2, 1, 32, 48
+    H, W, KH, KW, S, P, cin, N = SHAPES[seed]
     OH, OW = (H + 2 * P - KH) // S + 1, (W + 2 * P - KW) // S + 1
     K = KH * KW * cin
     img = rng.integers(-128, 128, (H * W, cin), dtype=np.int8)
@@ -25,9 +31,8 @@ def _case(seed):
                 act=C.ACT_GELU, out=C.OUT_FP32)
 
 
-def _machine_conv(c) -> bytes:
-    """The same convolution as one conv descriptor through the drop-in Machine."""
-    from opentars_b200.machine import Machine
+def _conv_program(c):
+    """The same convolution as one conv descriptor in a DDR image."""
     ddr = bytearray(1 << 20)
     a_off, w_off, s_off, b_off, y_off, qa = 0x1000, 0x10000, 0x40000, 0x41000, 0x50000, 0xF0000
     ddr[a_off:a_off + c["img"].size] = c["img"].tobytes()
@@ -39,19 +44,34 @@ def _machine_conv(c) -> bytes:
         EPI=C.epi(c["act"], c["out"], 1), A_OFF=a_off, W_OFF=w_off, SCALE_OFF=s_off, BIAS_OFF=b_off, Y_OFF=y_off,
         M=c["OH"] * c["OW"], N=c["N"], K=c["K"], GROUP_SIZE=c["W"],
         HDR_RSV=c["H"] << 12 | c["KH"] << 8 | c["KW"] << 4 | (c["S"] - 1) << 2 | c["P"]))
+    return ddr, qa, slice(y_off, y_off + 4 * c["N"] * c["OH"] * c["OW"])
+
+
+def _oracle_conv(c) -> bytes:
+    from oracle.machine import OracleMachine
+    ddr, qa, ys = _conv_program(c)
+    m = OracleMachine(ddr)
+    assert m.run_queue(qa, 1).done
+    return bytes(m.ddr[ys])
+
+
+def _machine_conv(c) -> bytes:
+    from opentars_b200.machine import Machine
+    ddr, qa, ys = _conv_program(c)
     m = Machine(ddr)
     assert m.run_queue(qa, 1).done
-    return bytes(m.ddr[y_off:y_off + 4 * c["N"] * c["OH"] * c["OW"]])
+    return bytes(m.ddr[ys])
 
 
-def test_noalloc_conv_matches_the_descriptor_path_twice():
+def test_noalloc_conv_matches_the_oracle_on_calls_in_a_row():
     import torch
     from opentars_b200._lib import lib
     L = lib()
     dev = torch.device("cuda", 0)
-    for seed in (0, 1):                      # two calls in a row, different shapes of stride and data
+    for seed in range(len(SHAPES)):          # calls in a row: a large gather, then smaller ones
         c = _case(seed)
-        want = _machine_conv(c)
+        want = _oracle_conv(c)
+        assert _machine_conv(c) == want, seed
         img = torch.from_numpy(c["img"].view(np.uint8).copy()).to(dev)
         w = torch.from_numpy(c["w"].view(np.uint8).copy()).to(dev)
         sc = torch.from_numpy(c["sc"].copy()).to(dev)
@@ -79,3 +99,8 @@ def test_noalloc_conv_rejects_oversized_and_bad_arguments():
                                   ctypes.c_float(0), None) == TC_ERR_TOO_LARGE
     assert L.tc_conv_w8a8_noalloc(None, 32, 8, 8, 32, 3, 3, 1, 1, fake, fake, 1, None, fake, 64, 16, 0, 0,
                                   ctypes.c_float(0), None) == TC_ERR_ARG
+    # padding as wide as the window, and an image of more than 2^31 pixels: refused before any work
+    assert L.tc_conv_w8a8_noalloc(fake, 32, 8, 8, 32, 3, 3, 1, 3, fake, fake, 1, None, fake, 64, 16, 0, 0,
+                                  ctypes.c_float(0), None) == TC_ERR_ARG
+    assert L.tc_conv_w8a8_noalloc(fake, 32, 100000, 100000, 32, 3, 3, 1000, 1, fake, fake, 1, None, fake, 64, 16,
+                                  0, 0, ctypes.c_float(0), None) == TC_ERR_ARG
