@@ -68,6 +68,34 @@ int tc_engine_sync(tc_engine* e);
  * 4 attention, 5 quant, 6 argmax, 7 position) and the kernel's algorithmic bytes[i]. Returns the
  * number of kernels (the step counts as a decode step: the position advances). */
 int tc_engine_profile(tc_engine* e, float* ms, int32_t* kind, uint64_t* bytes, uint32_t cap);
+/* Starts sequence b afresh (a new conversation in that slot of a running batch): zeroes its KV
+ * cache rows in every layer and sets its position to 0; the other sequences keep theirs. Sequences
+ * at different positions step together: every step advances each sequence by the chunk's n tokens
+ * (the continuous batching of a server; the reference decodes one sequence at a time). A step that
+ * would take any sequence past max_tokens, or a host token id outside the vocabulary, is refused
+ * (TC_ERR_ARG) before anything runs. */
+int tc_engine_reset_seq(tc_engine* e, int32_t b);
+/* Each sequence's position (its next token's index) [batch] into the host. */
+int tc_engine_positions(tc_engine* e, int32_t* pos_host);
+/* The fused decode step: one-token steps run as one cooperative kernel over every SM (all layers,
+ * the final norm and the head; then the greedy pick) when the model and batch fit it (batch <= 64,
+ * every K a multiple of 128, head dim 64 / 128 / 256); otherwise, and for chunks of more tokens, as
+ * the per-kernel graph. enable 1 / 0 turns it on / off (on only where it was set up), -1 only asks;
+ * returns whether it was on. tc_engine_fused_why says why it is not available. No counterpart in
+ * the reference. */
+int tc_engine_fused(tc_engine* e, int32_t enable);
+const char* tc_engine_fused_why(tc_engine* e);
+/* Where the fused step's first bounded wait gave up, if one did (tc_wait_error then reads its
+ * code): out4 = {code (31 grid barrier, 41 weight slot, 42 rows copy, 43 accumulator free, 44
+ * weight slice, 45 accumulator ready), CTA, grid barriers passed, detail}; zeros when none did.
+ * Synchronous. */
+int tc_engine_fused_diag(tc_engine* e, int32_t* out4);
+/* Runs one fused decode step (the previous picks as input) with a globaltimer stamp (ns) at the
+ * kernel's grid barriers, taken by its first CTA: per layer 8 phases (norm + quant, q|k|v GEMM,
+ * attention, o GEMM, norm + quant, gate|up GEMM, gated quant, down GEMM), then the final norm and
+ * the head; stamps[0] is the kernel's start. Returns the number of stamps (TC_ERR_ARG when the
+ * fused step is off). The step counts as a decode step. */
+int tc_engine_phase_times(tc_engine* e, uint64_t* stamps, uint32_t cap);
 /* The engine's greedy pick on its own: tok_out[r] = np.argmax(logits[r]) for rows r < rows of
  * device logits [rows][vocab] (the first maximum; the first NaN wins over numbers): the
  * np.argmax of llm.py:834 and of tars_board.py:355. Device pointers; enqueued on `stream` (NULL:

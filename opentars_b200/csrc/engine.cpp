@@ -19,6 +19,7 @@
 #include "engine.h"
 #include "pdl.cuh"
 #include "mma.h"
+#include "step.h"
 
 using namespace tc;
 
@@ -63,6 +64,23 @@ struct tc_engine {
   // (TARSCUDA_FUSE_ATTN=0: three launches, the same bits)
   bool fuse_attn = true;
   std::string err;
+  // the fused decode step (step.h) for one-token steps, when the model and batch fit it
+  bool step_ok = false;
+  int grid = 0;
+  StepArgs sa{};
+  std::vector<StepLayer> slayers;
+  StepLayer* d_layers = nullptr;
+  uint8_t* wt = nullptr;                     // the weights re-laid out for the fused step
+  uint8_t* q8t = nullptr;                    // its int8 rows in the operand layout
+  int* sdiag = nullptr;
+  float* qs2 = nullptr;
+  int* part = nullptr;
+  float *satt = nullptr, *samax = nullptr;
+  unsigned* ssync = nullptr;
+  unsigned long long* strace = nullptr;
+  int ntrace = 0;
+  std::string step_why;                      // why the fused step is not used, when it is not
+  std::vector<int> hpos;                     // the host's copy of every sequence's position
   // profiling (tc_engine_profile): events around every kernel of one uncaptured step
   bool prof = false;
   std::vector<cudaEvent_t> pev;
@@ -71,9 +89,21 @@ struct tc_engine {
 };
 
 namespace {
+constexpr bool kFusedDefault = false;
 int fail(tc_engine* e, const char* what, cudaError_t c) {
   e->err = std::string(what) + ": " + cudaGetErrorString(c);
   return TC_ERR_CUDA;
+}
+// A step of n tokens per sequence may run only while every sequence has room for them: the KV
+// caches and RoPE tables hold max_tokens positions. Advances the host's copy of the positions.
+bool take_positions(tc_engine* e, int n) {
+  for (int p : e->hpos)
+    if (p + n > e->T) {
+      e->err = "a sequence would pass max_tokens (reset it first)";
+      return false;
+    }
+  for (int& p : e->hpos) p += n;
+  return true;
 }
 #define TRY(expr)                                   \
   do {                                              \
@@ -248,7 +278,145 @@ int enqueue_step(tc_engine* e, int n, const int* tok_in) {
     KERNEL(kKGemv, gemv_bytes(g), eng_gemv(g, st));
     KERNEL(kKArgmax, (uint64_t)B * md.vocab * 4, eng_argmax(e->logits, md.vocab, B, e->next, 1, st));
   }
-  KERNEL(kKAdvance, 0, eng_advance(e->pos, n, st));
+  KERNEL(kKAdvance, 0, eng_advance(e->pos, n, B, st));
+  return TC_OK;
+}
+
+// ------------------------------------------------------------------------------ the fused step
+// Sets up the fused decode step (step.h): the weights re-laid out per GEMM, the per-layer table,
+// the GEMM plans and the step's buffers. Leaves step_ok false (and step_why) when the model or the
+// batch does not fit it; the per-kernel path then serves every step.
+bool setup_step(tc_engine* e) {
+  const tc_model_desc& md = e->md;
+  auto no = [&](const char* why) {
+    e->step_why = why;
+    return false;
+  };
+  const char* env = getenv("TARSCUDA_STEP");
+  if (env && env[0] == '0') return no("TARSCUDA_STEP=0");
+  const int B = e->B, ntok = (B + 15) / 16 * 16;
+  if (B > kStepMaxTok) return no("batch above 64");
+  if (e->H % 128 || e->qw % 128 || e->I % 128) return no("a K dimension is not a multiple of 128");
+  if (md.head_dim != 64 && md.head_dim != 128 && md.head_dim != 256) return no("head dim");
+  // the attention prologue gives each of 16 half-warps one row: G query heads, the K and the V row
+  if (md.n_heads % md.n_kv || md.n_heads / md.n_kv > 14 || md.rot > md.head_dim || md.rot % 2) return no("heads");
+  if (md.n_head_blocks < 1 || md.n_head_blocks > kStepSegs) return no("head blocks");
+  const int G = md.n_heads / md.n_kv;
+  const int tile = step_attn_tile(md.head_dim, G);
+  if (tile < 16) return no("attention tile");
+  if (2 * e->H * 4 > step_region_bytes() || e->I * 4 > step_region_bytes()) return no("row staging");
+  int dev = 0, coop = 0, nsm = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  if (!coop || nsm < 1) return no("no cooperative launch");
+  if (step_occupancy(&per_sm) != cudaSuccess || per_sm < 1) return no("occupancy");
+  const int grid = nsm;
+  uint64_t part_bytes = 0;
+  // plan every GEMM; its weights are re-laid out as [tile][slice] blocks (step.h) below
+  struct Pending { StepGemm* g; std::vector<Lin> segs; const Lin* second; int K; };
+  std::vector<Pending> todo;
+  auto gemm = [&](StepGemm& g, const std::vector<Lin>& segs, const Lin* second, int K, bool fused) {
+    g = StepGemm{};
+    g.nseg = (int)segs.size();
+    int tiles = 0, cols = 0;
+    for (int s = 0; s < g.nseg; ++s) {
+      const Lin& l = segs[s];
+      if (l.k != (second ? segs[0].k : K)) return false;
+      g.tile0[s] = tiles;
+      g.col0[s] = cols;
+      g.scale[s] = l.s;
+      tiles += (l.n + 127) / 128;
+      cols += l.n;
+    }
+    g.tile0[g.nseg] = tiles;
+    g.col0[g.nseg] = cols;
+    g.nslices = K / 128;
+    g.kb = second ? segs[0].k / 128 : g.nslices;
+    if (second && (segs[0].k % 128 || second->k != K - segs[0].k)) return false;
+    if (!step_plan_gemm(g, ntok, grid, fused)) return false;
+    if (!fused) part_bytes = std::max(part_bytes, (uint64_t)g.ksplit * B * cols * 4);
+    todo.push_back(Pending{&g, segs, second, K});
+    return true;
+  };
+  e->slayers.assign(md.n_layers, StepLayer{});
+  for (int li = 0; li < md.n_layers; ++li) {
+    const Layer& L = e->layers[li];
+    StepLayer& S = e->slayers[li];
+    if (L.n_down > 2) return no("down in more than two K blocks");
+    if (!gemm(S.qkv, {L.q, L.k, L.v}, nullptr, e->H, false)) return no("q|k|v plan");
+    if (!gemm(S.o, {L.o}, nullptr, e->qw, false)) return no("o plan");
+    if (!gemm(S.gu, {L.gate, L.up}, nullptr, e->H, false)) return no("gate|up plan");
+    if (!gemm(S.down, {L.down[0]}, L.n_down == 2 ? &L.down[1] : nullptr, e->I, false)) return no("down plan");
+    S.ln_in = L.ln_in; S.ln_post = L.ln_post; S.attn_norm = L.attn_norm; S.mlp_norm = L.mlp_norm;
+    S.qn = L.qn; S.kn = L.kn; S.tab = L.tab;
+    S.kc = e->kc + (uint64_t)li * e->B * e->Tp * e->kvw;
+    S.vc = e->vc + (uint64_t)li * e->B * e->Tp * e->kvw;
+  }
+  StepArgs& a = e->sa;
+  if (!gemm(a.head, e->head, nullptr, e->H, true)) return no("head plan");
+  uint64_t wt_bytes = 0;
+  for (const Pending& p : todo) wt_bytes += (uint64_t)p.g->tile0[p.g->nseg] * p.g->nslices * kStepSliceBytes;
+  cudaError_t c = cudaMalloc((void**)&e->wt, wt_bytes);
+  uint64_t off = 0;
+  for (const Pending& p : todo) {
+    if (c != cudaSuccess) break;
+    StepGemm& g = *p.g;
+    g.wt = e->wt + off;
+    for (int s = 0; s < g.nseg && c == cudaSuccess; ++s) {
+      const Lin& l = p.segs[s];
+      uint8_t* out = e->wt + off + (uint64_t)g.tile0[s] * g.nslices * kStepSliceBytes;
+      c = step_retile(l.W, p.second ? p.second->W : nullptr, l.n, p.K, p.second ? l.k : p.K, out, e->st);
+    }
+    off += (uint64_t)g.tile0[g.nseg] * g.nslices * kStepSliceBytes;
+  }
+  const int ldq = std::max(std::max(e->H, e->I), e->qw);
+  const size_t q8t_bytes = (size_t)(ldq / 128) * ntok * 128;
+  if (c == cudaSuccess) c = cudaMalloc((void**)&e->d_layers, e->slayers.size() * sizeof(StepLayer));
+  if (c == cudaSuccess)
+    c = cudaMemcpy(e->d_layers, e->slayers.data(), e->slayers.size() * sizeof(StepLayer), cudaMemcpyHostToDevice);
+  if (c == cudaSuccess) c = cudaMalloc((void**)&e->q8t, q8t_bytes);
+  if (c == cudaSuccess) c = cudaMemsetAsync(e->q8t, 0, q8t_bytes, e->st);   // the padding rows stay zero
+  if (c == cudaSuccess) c = cudaMalloc((void**)&e->qs2, (size_t)B * 4);
+  if (c == cudaSuccess) c = cudaMalloc((void**)&e->part, std::max<uint64_t>(part_bytes, 16));
+  if (c == cudaSuccess) c = cudaMalloc((void**)&e->satt, (size_t)B * e->qw * 4);
+  if (c == cudaSuccess) c = cudaMalloc((void**)&e->samax, (size_t)B * md.n_kv * 4);
+  if (c == cudaSuccess) c = cudaMalloc((void**)&e->ssync, (size_t)(1 + B) * 4);
+  if (c == cudaSuccess) c = cudaMalloc((void**)&e->sdiag, 4 * sizeof(int));
+  if (c == cudaSuccess) c = cudaMemsetAsync(e->sdiag, 0, 4 * sizeof(int), e->st);
+  e->ntrace = 9 * md.n_layers + 4;
+  if (c == cudaSuccess) c = cudaMalloc((void**)&e->strace, (size_t)e->ntrace * 8);
+  if (c == cudaSuccess) c = cudaStreamSynchronize(e->st);
+  if (c != cudaSuccess) return no("allocation or weight layout");
+  a.layers = e->d_layers;
+  a.L = md.n_layers; a.B = B; a.ntok = ntok; a.H = e->H; a.I = e->I; a.nh = md.n_heads; a.nkv = md.n_kv;
+  a.hd = md.head_dim; a.rot = md.rot; a.Tp = e->Tp; a.vocab = md.vocab; a.gemma = md.gemma; a.act = md.act;
+  a.ldq = ldq; a.tile = tile;
+  a.eps = md.eps; a.embed_scale = md.embed_scale;
+  a.E = e->E; a.pos = e->pos; a.final_norm = e->final_norm;
+  a.x = e->x; a.x1 = e->x1; a.q8t = e->q8t; a.qsa = e->qs; a.qsb = e->qs2;
+  a.part = e->part; a.att = e->satt; a.amax = e->samax; a.logits = e->logits; a.sync = e->ssync;
+  a.diag = e->sdiag;
+  a.err = wait_error_flag();
+  if (!a.err) return no("error word");
+  e->grid = grid;
+  return true;
+}
+
+// One fused decode step (tokens already on the device at tok), then the greedy pick and the
+// positions' advance.
+int step_fused(tc_engine* e, const int* tok, bool trace) {
+  StepArgs a = e->sa;
+  a.tok = tok;
+  // time limits: the poll limit's scale (2^22 polls: about 0.2 s; 0: give up at once)
+  a.wait_ns = (uint64_t)spin_limit() * 50;
+  a.drain_ns = 20000000ull;
+  a.trace = trace ? e->strace : nullptr;
+  TRY(cudaMemsetAsync(e->ssync, 0, (size_t)(1 + e->B) * 4, e->st));
+  if (trace) TRY(cudaMemsetAsync(e->strace, 0, (size_t)e->ntrace * 8, e->st));
+  TRY(step_launch(a, e->grid, e->st));
+  TRY(eng_argmax(e->logits, e->md.vocab, e->B, e->next, 1, e->st));
+  TRY(eng_advance(e->pos, 1, e->B, e->st));
   return TC_OK;
 }
 }  // namespace
@@ -300,7 +468,7 @@ int tc_engine_create(tc_machine* image, const tc_model_desc* md, const tc_layer_
   if (c == cudaSuccess) c = cudaMemcpy(e->E, embed_host, (size_t)md->vocab * e->H * 4, cudaMemcpyHostToDevice);
   if (c == cudaSuccess) c = alloc((void**)&e->tok, (size_t)M * 4);
   if (c == cudaSuccess) c = alloc((void**)&e->next, (size_t)e->B * 4);
-  if (c == cudaSuccess) c = alloc((void**)&e->pos, 4);
+  if (c == cudaSuccess) c = alloc((void**)&e->pos, (size_t)e->B * 4);
   float** fbufs[] = {&e->x, &e->x1, &e->o, &e->d};
   for (auto p : fbufs) if (c == cudaSuccess) c = alloc((void**)p, (size_t)M * e->H * 4);
   if (c == cudaSuccess) c = alloc((void**)&e->q, (size_t)M * e->qw * 4);
@@ -320,6 +488,9 @@ int tc_engine_create(tc_machine* image, const tc_model_desc* md, const tc_layer_
     tc_engine_destroy(e);
     return TC_ERR_CUDA;
   }
+  // set up where the model fits; on by default only once validated (tc_engine_fused switches it)
+  e->step_ok = setup_step(e) && kFusedDefault;
+  cudaGetLastError();                        // a refused setup leaves no error state behind
   *out = e;
   return tc_engine_reset(e);
 }
@@ -329,7 +500,8 @@ int tc_engine_destroy(tc_engine* e) {
   if (e->st) cudaStreamSynchronize(e->st);
   for (auto& gx : e->graph) if (gx) cudaGraphExecDestroy(gx);
   void* bufs[] = {e->E, e->tok, e->next, e->pos, e->x, e->x1, e->q, e->k, e->v, e->qr, e->att, e->o, e->g, e->u, e->d,
-                  e->logits, e->q8, e->qs, e->kc, e->vc};
+                  e->logits, e->q8, e->qs, e->kc, e->vc, e->d_layers, e->wt, e->q8t, e->sdiag, e->qs2, e->part,
+                  e->satt, e->samax, e->ssync, e->strace};
   for (void* p : bufs) if (p) cudaFree(p);
   if (e->st) cudaStreamDestroy(e->st);
   delete e;
@@ -343,9 +515,59 @@ int tc_engine_reset(tc_engine* e) {
   const size_t cache = (size_t)e->md.n_layers * e->B * e->Tp * e->kvw * 4;
   TRY(cudaMemsetAsync(e->kc, 0, cache, e->st));
   TRY(cudaMemsetAsync(e->vc, 0, cache, e->st));
-  TRY(cudaMemsetAsync(e->pos, 0, 4, e->st));
+  TRY(cudaMemsetAsync(e->pos, 0, (size_t)e->B * 4, e->st));
+  TRY(cudaStreamSynchronize(e->st));
+  e->hpos.assign(e->B, 0);
+  return TC_OK;
+}
+
+int tc_engine_reset_seq(tc_engine* e, int32_t b) {
+  if (!e || b < 0 || b >= e->B) return TC_ERR_ARG;
+  const size_t rows = (size_t)e->Tp * e->kvw * 4;
+  for (int li = 0; li < e->md.n_layers; ++li) {
+    const uint64_t off = ((uint64_t)li * e->B + b) * e->Tp * e->kvw;
+    TRY(cudaMemsetAsync(e->kc + off, 0, rows, e->st));
+    TRY(cudaMemsetAsync(e->vc + off, 0, rows, e->st));
+  }
+  TRY(cudaMemsetAsync(e->pos + b, 0, 4, e->st));
+  e->hpos[b] = 0;
+  return TC_OK;
+}
+
+int tc_engine_positions(tc_engine* e, int32_t* pos_host) {
+  TRY(cudaMemcpyAsync(pos_host, e->pos, (size_t)e->B * 4, cudaMemcpyDeviceToHost, e->st));
   TRY(cudaStreamSynchronize(e->st));
   return TC_OK;
+}
+
+int tc_engine_fused(tc_engine* e, int32_t enable) {
+  if (!e) return TC_ERR_ARG;
+  const bool was = e->step_ok;
+  if (enable >= 0) {
+    if (enable && !e->d_layers) return TC_ERR_ARG;       // never set up for this model / batch
+    e->step_ok = enable != 0;
+  }
+  return was ? 1 : 0;
+}
+
+const char* tc_engine_fused_why(tc_engine* e) { return e ? e->step_why.c_str() : ""; }
+
+int tc_engine_fused_diag(tc_engine* e, int32_t* out4) {
+  if (!e || !e->sdiag || !out4) return TC_ERR_ARG;
+  TRY(cudaStreamSynchronize(e->st));
+  TRY(cudaMemcpy(out4, e->sdiag, 4 * sizeof(int), cudaMemcpyDeviceToHost));
+  return TC_OK;
+}
+
+int tc_engine_phase_times(tc_engine* e, uint64_t* stamps, uint32_t cap) {
+  if (!e || !e->step_ok) return TC_ERR_ARG;
+  if (!take_positions(e, 1)) return TC_ERR_ARG;
+  const int rc = step_fused(e, e->next, true);
+  if (rc != TC_OK) return rc;
+  TRY(cudaStreamSynchronize(e->st));
+  const uint32_t n = std::min<uint32_t>(cap, (uint32_t)e->ntrace);
+  if (stamps && n) TRY(cudaMemcpy(stamps, e->strace, (size_t)n * 8, cudaMemcpyDeviceToHost));
+  return (int)n;
 }
 
 // Runs one chunk of n tokens per sequence (tokens_host: [B][n] ids, or NULL to feed each
@@ -353,11 +575,19 @@ int tc_engine_reset(tc_engine* e) {
 // first use for that n and replayed afterwards; the position advances on the device.
 int tc_engine_step(tc_engine* e, const int32_t* tokens_host, int32_t n) {
   if (n < 1 || n > e->nmax || (!tokens_host && n != 1)) { e->err = "bad chunk"; return TC_ERR_ARG; }
+  if (tokens_host)
+    for (int i = 0; i < e->B * n; ++i)
+      if (tokens_host[i] < 0 || tokens_host[i] >= e->md.vocab) {
+        e->err = "token id outside the vocabulary";
+        return TC_ERR_ARG;
+      }
+  if (!take_positions(e, n)) return TC_ERR_ARG;
   const int* src = e->next;
   if (tokens_host) {
     TRY(cudaMemcpyAsync(e->tok, tokens_host, (size_t)e->B * n * 4, cudaMemcpyHostToDevice, e->st));
     src = e->tok;
   }
+  if (n == 1 && e->step_ok) return step_fused(e, src, false);
   const int slot = tokens_host ? n : 0;
   if (!e->graph[slot]) {
     cudaGraph_t graph;
@@ -383,6 +613,7 @@ int tc_engine_step(tc_engine* e, const int32_t* tokens_host, int32_t n) {
 int tc_engine_profile(tc_engine* e, float* ms, int32_t* kind, uint64_t* bytes, uint32_t cap) {
   // The step is captured with an event node on each side of every kernel and launched once, so
   // the times are the kernels' own (no host work between the events, as in the timed graphs).
+  if (!take_positions(e, 1)) return TC_ERR_ARG;
   e->prof = true;
   e->pev.clear(); e->pkind.clear(); e->pbytes.clear();
   cudaGraph_t graph = nullptr;

@@ -46,7 +46,7 @@ struct QkRopeArgs {
   float* qr;  float* kc;  float* vc;
   const float* qn;  const float* kn;
   const float* tab;
-  const int* pos;
+  const int* pos;                      // each sequence's position [batch]
   int rows, n, nh, nkv, hd, rot, Tp;
   float eps;
 };
@@ -54,7 +54,7 @@ struct QkRopeArgs {
 struct AttnArgs {
   const float* qr;  const float* kc;  const float* vc;
   float* att;
-  const int* pos;
+  const int* pos;                      // each sequence's position [batch]
   int n, nh, nkv, hd, Tp;
 };
 
@@ -78,6 +78,6 @@ struct AttnQuantArgs {
 };
 cudaError_t eng_attention_quant(const AttnArgs& a, const AttnQuantArgs& f, int batch, cudaStream_t st);
 cudaError_t eng_argmax(const float* logits, int vocab, int batch, int* tok_out, int tok_stride, cudaStream_t st);
-cudaError_t eng_advance(int* pos, int n, cudaStream_t st);
+cudaError_t eng_advance(int* pos, int n, int batch, cudaStream_t st);
 
 }  // namespace tc

@@ -414,7 +414,7 @@ __global__ void __launch_bounds__(128) k_qk_rope(QkRopeArgs a) {
   const int r = live ? item / heads : 0, h = live ? item % heads : 0;
   const bool isq = h < a.nh;
   const int b = r / a.n, m = r - b * a.n;
-  const int t = *a.pos + m;
+  const int t = a.pos[b] + m;
   const int hd = a.hd;
   const float* src = isq ? a.q + (uint64_t)r * a.nh * hd + h * hd : a.k + (uint64_t)r * a.nkv * hd + (h - a.nh) * hd;
   const float* gam = isq ? a.qn : a.kn;
@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a, int tile
   float* skv = sp + R * kT;                       // [tile][LD] K or V rows
   __shared__ float srow[2][kMaxRows];             // per row: max, then 1 / sum
   const int b = blockIdx.x / a.nkv, kvh = blockIdx.x - b * a.nkv;
-  const int t0 = *a.pos;
+  const int t0 = a.pos[b];
   const int nk = ((t0 + n) + 15) / 16 * 16;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if constexpr (FUSED) {
@@ -793,9 +793,9 @@ __global__ void __launch_bounds__(kPickThreads) k_argmax(const float* logits, in
   cluster_sync();                                 // the peers' candidates have been read
 }
 
-__global__ void k_advance(int* pos, int n) {
+__global__ void k_advance(int* pos, int n, int batch) {
   griddep_wait();
-  *pos += n;
+  for (int b = threadIdx.x; b < batch; b += blockDim.x) pos[b] += n;
 }
 
 }  // namespace
@@ -905,8 +905,8 @@ cudaError_t eng_argmax(const float* logits, int vocab, int batch, int* tok_out, 
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
-cudaError_t eng_advance(int* pos, int n, cudaStream_t st) {
-  cudaError_t e = launch_ex(k_advance, dim3(1), dim3(1), 0, st, 1, pos, n);
+cudaError_t eng_advance(int* pos, int n, int batch, cudaStream_t st) {
+  cudaError_t e = launch_ex(k_advance, dim3(1), dim3(256), 0, st, 1, pos, n, batch);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

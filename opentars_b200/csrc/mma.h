@@ -20,5 +20,7 @@ int mma_error_code();
 // The device word every streaming kernel records a given-up bounded wait in (codes: tensor-core
 // GEMM 1-5, grouped GEMV 21-22, streamed W4A16 GEMV 11-12); read by tc_wait_error.
 int* wait_error_flag();
+// The poll limit of the bounded waits for work (tc_set_spin_limit).
+uint32_t spin_limit();
 
 }  // namespace tc

@@ -56,7 +56,17 @@ ENGINE_SIGNATURES = {
     "tc_engine_sync": (ctypes.c_int, [P]),
     "tc_engine_profile": (ctypes.c_int, [P, P, P, P, ctypes.c_uint32]),
     "tc_argmax": (ctypes.c_int, [P, ctypes.c_int32, ctypes.c_int32, P, P]),
+    "tc_engine_reset_seq": (ctypes.c_int, [P, ctypes.c_int32]),
+    "tc_engine_positions": (ctypes.c_int, [P, P]),
+    "tc_engine_fused": (ctypes.c_int, [P, ctypes.c_int32]),
+    "tc_engine_fused_why": (ctypes.c_char_p, [P]),
+    "tc_engine_fused_diag": (ctypes.c_int, [P, P]),
+    "tc_engine_phase_times": (ctypes.c_int, [P, P, ctypes.c_uint32]),
 }
+# the fused step's phases, in the order of tc_engine_phase_times' stamps (per layer, then the tail)
+LAYER_PHASES = ("norm_quant", "gemm_qkv", "attention", "gemm_o", "norm_quant", "gemm_gate_up", "gated_quant",
+                "gemm_down")
+TAIL_PHASES = ("norm_quant", "gemm_head")
 KERNEL_KINDS = ("embed", "norm_quant", "gemv", "qk_rope", "attention", "quant", "argmax", "advance")
 
 
@@ -174,6 +184,41 @@ class DecodeEngine:
 
     def sync(self):
         self._check(lib().tc_engine_sync(self.h), "sync")
+
+    def reset_seq(self, b: int) -> None:
+        """Start sequence b afresh (zeroed KV cache rows, position 0); the others keep theirs."""
+        self._check(lib().tc_engine_reset_seq(self.h, int(b)), "reset_seq")
+
+    def positions(self) -> np.ndarray:
+        out = np.zeros(self.B, np.int32)
+        self._check(lib().tc_engine_positions(self.h, out.ctypes.data_as(ctypes.c_void_p)), "positions")
+        return out
+
+    def fused(self, enable: bool | None = None) -> bool:
+        """Whether one-token steps run as the fused step kernel (and switch it when enable is given)."""
+        rc = lib().tc_engine_fused(self.h, -1 if enable is None else int(bool(enable)))
+        if rc < 0:
+            raise RuntimeError(f"the fused step is not available: {self.fused_why()}")
+        return bool(rc)
+
+    def fused_why(self) -> str:
+        return lib().tc_engine_fused_why(self.h).decode()
+
+    def fused_diag(self) -> list[int]:
+        out = np.zeros(4, np.int32)
+        self._check(lib().tc_engine_fused_diag(self.h, out.ctypes.data_as(ctypes.c_void_p)), "fused_diag")
+        return [int(v) for v in out]
+
+    def phase_times(self) -> list[tuple[str, int, float]]:
+        """One fused decode step phase by phase: [(phase, layer (-1: the tail), microseconds)]."""
+        cap = 9 * len(self.low.types) + 4
+        st = np.zeros(cap, np.uint64)
+        n = lib().tc_engine_phase_times(self.h, st.ctypes.data_as(ctypes.c_void_p), cap)
+        if n < 0:
+            self._check(n, "phase_times")
+        names = [(p, li) for li in range(len(self.low.types)) for p in LAYER_PHASES] + [(p, -1) for p in TAIL_PHASES]
+        t = st[:n].astype(np.int64)
+        return [(names[i][0], names[i][1], float(t[i + 1] - t[i]) / 1e3) for i in range(min(len(names), n - 1))]
 
     def profile(self) -> list[tuple[str, float, int]]:
         """One decode step kernel by kernel: [(kind, ms, algorithmic bytes)]."""
