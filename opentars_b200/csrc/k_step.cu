@@ -501,24 +501,27 @@ __device__ void attn_unit(const StepArgs& a, const StepLayer& Ly, int b, int kvh
       s = fadd_nc(s, fmul(v[i], v[i]));
     }
     s = sum16_fold(canon(s));
+    // the two half-warps of a warp may take different branches below: both __syncwarp calls stay
+    // outside them, so every lane of the warp meets at the same two points
     float* sn = skv + hw * HD;
-    if (it <= G) {
+    const bool qk = it <= G;                           // a query head or the K row: norm + RoPE
+    if (qk) {
       const float rs = rsqrt_f(fadd(fmul(s, recip_f(i2f(HD))), a.eps));
       const float* gam = it < G ? Ly.qn : Ly.kn;
 #pragma unroll
       for (int i = 0; i < HD / 16; ++i) sn[l + 16 * i] = ftz(fmul(fmul(v[i], rs), gam[l + 16 * i]));
-      __syncwarp();
-      if (live) {
-        const float* tab = Ly.tab + (uint64_t)t0 * a.rot;
-        const int half = a.rot / 2;
-        float* dst = it < G ? sq + it * HD : Ly.kc + (((uint64_t)b * a.Tp + t0) * a.nkv + kvh) * HD;
-        for (int j = l; j < HD; j += 16) {
-          float y;
-          if (j < half) y = fadd(fmul(sn[j], ftz(tab[j])), neg(fmul(sn[j + half], ftz(tab[half + j]))));
-          else if (j < a.rot) y = fadd(fmul(sn[j], ftz(tab[j - half])), fmul(sn[j - half], ftz(tab[j])));
-          else y = sn[j];
-          dst[j] = ftz(y);
-        }
+    }
+    __syncwarp();
+    if (live && qk) {
+      const float* tab = Ly.tab + (uint64_t)t0 * a.rot;
+      const int half = a.rot / 2;
+      float* dst = it < G ? sq + it * HD : Ly.kc + (((uint64_t)b * a.Tp + t0) * a.nkv + kvh) * HD;
+      for (int j = l; j < HD; j += 16) {
+        float y;
+        if (j < half) y = fadd(fmul(sn[j], ftz(tab[j])), neg(fmul(sn[j + half], ftz(tab[half + j]))));
+        else if (j < a.rot) y = fadd(fmul(sn[j], ftz(tab[j - half])), fmul(sn[j - half], ftz(tab[j])));
+        else y = sn[j];
+        dst[j] = ftz(y);
       }
     } else if (live) {                                 // V goes to the cache as the GEMM gave it
       float* vd = Ly.vc + (((uint64_t)b * a.Tp + t0) * a.nkv + kvh) * HD;
