@@ -75,7 +75,7 @@ struct tc_engine {
   int* sdiag = nullptr;
   float* qs2 = nullptr;
   int* part = nullptr;
-  float *satt = nullptr, *samax = nullptr;
+  float *satt = nullptr, *samax = nullptr, *sgv = nullptr, *sgmax = nullptr;
   unsigned* ssync = nullptr;
   unsigned long long* strace = nullptr;
   int ntrace = 0;
@@ -302,9 +302,16 @@ bool setup_step(tc_engine* e) {
   if (md.n_heads % md.n_kv || md.n_heads / md.n_kv > 14 || md.rot > md.head_dim || md.rot % 2) return no("heads");
   if (md.n_head_blocks < 1 || md.n_head_blocks > kStepSegs) return no("head blocks");
   const int G = md.n_heads / md.n_kv;
-  const int tile = step_attn_tile(md.head_dim, G);
+  int nsm0 = 0, dev0 = 0;
+  cudaGetDevice(&dev0);
+  cudaDeviceGetAttribute(&nsm0, cudaDevAttrMultiProcessorCount, dev0);
+  // concurrent attention units per CTA: enough groups for every (sequence, kv head) in one pass
+  int agroups = 1;
+  while (agroups < 4 && B * md.n_kv > nsm0 * agroups && step_attn_tile(md.head_dim, G, agroups * 2) >= 16)
+    agroups *= 2;
+  const int tile = step_attn_tile(md.head_dim, G, agroups);
   if (tile < 16) return no("attention tile");
-  if (2 * e->H * 4 > step_region_bytes() || e->I * 4 > step_region_bytes()) return no("row staging");
+  if (5 * e->H * 4 > step_region_bytes() || md.rot % 4) return no("row staging");
   int dev = 0, coop = 0, nsm = 0, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
@@ -381,17 +388,22 @@ bool setup_step(tc_engine* e) {
   if (c == cudaSuccess) c = cudaMalloc((void**)&e->part, std::max<uint64_t>(part_bytes, 16));
   if (c == cudaSuccess) c = cudaMalloc((void**)&e->satt, (size_t)B * e->qw * 4);
   if (c == cudaSuccess) c = cudaMalloc((void**)&e->samax, (size_t)B * md.n_kv * 4);
-  if (c == cudaSuccess) c = cudaMalloc((void**)&e->ssync, (size_t)(1 + B) * 4);
+  // gated MLP units of 512 columns (the last one of a row may be shorter)
+  const int gchunks = std::max(1, (e->I + 511) / 512);
+  if (c == cudaSuccess) c = cudaMalloc((void**)&e->sgv, (size_t)B * e->I * 4);
+  if (c == cudaSuccess) c = cudaMalloc((void**)&e->sgmax, (size_t)B * gchunks * 4);
+  if (c == cudaSuccess) c = cudaMalloc((void**)&e->ssync, (size_t)(1 + 2 * B) * 4);
   if (c == cudaSuccess) c = cudaMalloc((void**)&e->sdiag, 4 * sizeof(int));
   if (c == cudaSuccess) c = cudaMemsetAsync(e->sdiag, 0, 4 * sizeof(int), e->st);
-  e->ntrace = 9 * md.n_layers + 4;
+  e->ntrace = 1024 + (9 * md.n_layers + 8) * grid;
   if (c == cudaSuccess) c = cudaMalloc((void**)&e->strace, (size_t)e->ntrace * 8);
   if (c == cudaSuccess) c = cudaStreamSynchronize(e->st);
   if (c != cudaSuccess) return no("allocation or weight layout");
   a.layers = e->d_layers;
   a.L = md.n_layers; a.B = B; a.ntok = ntok; a.H = e->H; a.I = e->I; a.nh = md.n_heads; a.nkv = md.n_kv;
   a.hd = md.head_dim; a.rot = md.rot; a.Tp = e->Tp; a.vocab = md.vocab; a.gemma = md.gemma; a.act = md.act;
-  a.ldq = ldq; a.tile = tile;
+  a.ldq = ldq; a.tile = tile; a.agroups = agroups; a.gchunks = gchunks;
+  a.gv = e->sgv; a.gmax = e->sgmax;
   a.eps = md.eps; a.embed_scale = md.embed_scale;
   a.E = e->E; a.pos = e->pos; a.final_norm = e->final_norm;
   a.x = e->x; a.x1 = e->x1; a.q8t = e->q8t; a.qsa = e->qs; a.qsb = e->qs2;
@@ -412,7 +424,7 @@ int step_fused(tc_engine* e, const int* tok, bool trace) {
   a.wait_ns = (uint64_t)spin_limit() * 50;
   a.drain_ns = 20000000ull;
   a.trace = trace ? e->strace : nullptr;
-  TRY(cudaMemsetAsync(e->ssync, 0, (size_t)(1 + e->B) * 4, e->st));
+  TRY(cudaMemsetAsync(e->ssync, 0, (size_t)(1 + 2 * e->B) * 4, e->st));
   if (trace) TRY(cudaMemsetAsync(e->strace, 0, (size_t)e->ntrace * 8, e->st));
   TRY(step_launch(a, e->grid, e->st));
   TRY(eng_argmax(e->logits, e->md.vocab, e->B, e->next, 1, e->st));
@@ -501,7 +513,7 @@ int tc_engine_destroy(tc_engine* e) {
   for (auto& gx : e->graph) if (gx) cudaGraphExecDestroy(gx);
   void* bufs[] = {e->E, e->tok, e->next, e->pos, e->x, e->x1, e->q, e->k, e->v, e->qr, e->att, e->o, e->g, e->u, e->d,
                   e->logits, e->q8, e->qs, e->kc, e->vc, e->d_layers, e->wt, e->q8t, e->sdiag, e->qs2, e->part,
-                  e->satt, e->samax, e->ssync, e->strace};
+                  e->satt, e->samax, e->sgv, e->sgmax, e->ssync, e->strace};
   for (void* p : bufs) if (p) cudaFree(p);
   if (e->st) cudaStreamDestroy(e->st);
   delete e;

@@ -52,7 +52,9 @@ struct StepLayer {
 struct StepArgs {
   const StepLayer* layers;          // [L], device memory
   StepGemm head;
-  int L, B, ntok, H, I, nh, nkv, hd, rot, Tp, vocab, gemma, act, ldq, tile;
+  int L, B, ntok, H, I, nh, nkv, hd, rot, Tp, vocab, gemma, act, ldq;
+  int tile, agroups;                // attention: keys per staged tile; concurrent units per CTA
+  int gchunks;                      // gated MLP: units per row
   float eps, embed_scale;
   const float* E;                   // fp32 embedding table [vocab][H]
   const int* tok;                   // the step's token ids [B]
@@ -64,13 +66,17 @@ struct StepArgs {
   int* part;                        // int32 partial sums
   float* att;                       // attention output rows [B][nh * hd]
   float* amax;                      // per (sequence, kv head) absmax of the attention output
+  float* gv;                        // the gated MLP's rows act(gate) * up [B][I]
+  float* gmax;                      // their absmax per (row, unit)
   float* logits;                    // [B][vocab]
-  unsigned* sync;                   // [0] grid barrier count, [1 + b] arrivals of sequence b;
-                                    // zeroed before every launch
+  unsigned* sync;                   // [0] grid barrier count, [1 + b] arrivals of sequence b's
+                                    // attention units, [1 + B + m] of row m's gated units; zeroed
+                                    // before every launch
   int* err;                         // the device word of bounded waits that gave up
   int* diag;                        // the first give-up: code, CTA, barrier count, detail
   uint64_t wait_ns, drain_ns;       // time limits of the waits for work / for copies in flight
-  unsigned long long* trace;        // globaltimer at every barrier (CTA 0), or null
+  unsigned long long* trace;        // [0, 1024): CTA 0 leaving every barrier (0: the kernel's
+                                    // start); from 1024: per barrier every CTA's arrival; or null
 };
 
 // Shared memory a CTA of the step kernel uses, and its staging region for rows / attention.
@@ -78,8 +84,9 @@ size_t step_smem_bytes();
 int step_region_bytes();
 // Plans one GEMM (KC, ksplit, groups) for `grid` CTAs; false when it does not fit.
 bool step_plan_gemm(StepGemm& g, int ntok, int grid, bool fused);
-// The attention's K / V tile (keys per staged tile) for a head dim and query heads per kv head.
-int step_attn_tile(int hd, int G);
+// The attention's K / V tile (keys per staged tile) for a head dim, query heads per kv head and
+// concurrent units per CTA; 0 when they do not fit.
+int step_attn_tile(int hd, int G, int ngroups);
 cudaError_t step_launch(const StepArgs& a, int grid, cudaStream_t st);
 // CTAs of the step kernel that fit one SM (1 when it fits at all).
 cudaError_t step_occupancy(int* per_sm);

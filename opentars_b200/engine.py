@@ -66,7 +66,7 @@ ENGINE_SIGNATURES = {
 # the fused step's phases, in the order of tc_engine_phase_times' stamps (per layer, then the tail)
 LAYER_PHASES = ("norm_quant", "gemm_qkv", "attention", "gemm_o", "norm_quant", "gemm_gate_up", "gated_quant",
                 "gemm_down")
-TAIL_PHASES = ("norm_quant", "gemm_head")
+TAIL_PHASES = ("norm_quant", "gemm_head", "empty", "empty", "empty", "empty")
 KERNEL_KINDS = ("embed", "norm_quant", "gemv", "qk_rope", "attention", "quant", "argmax", "advance")
 
 
@@ -209,28 +209,27 @@ class DecodeEngine:
         self._check(lib().tc_engine_fused_diag(self.h, out.ctypes.data_as(ctypes.c_void_p)), "fused_diag")
         return [int(v) for v in out]
 
-    def phase_times(self) -> list[tuple[str, int, float]]:
-        """One fused decode step phase by phase: [(phase, layer (-1: the tail), microseconds)]."""
-        cap = 9 * len(self.low.types) + 4
+    def phase_times(self) -> list[tuple[str, int, float, float, float]]:
+        """One fused decode step phase by phase: [(phase, layer (-1: the tail), microseconds from
+        the previous barrier to the next, of which until the last CTA arrived at it, and of which
+        the barrier itself)]. The tail ends with four empty phases: the barrier alone."""
+        L = len(self.low.types)
+        nph = 8 * L + 6
+        cap = 1024 + (9 * L + 8) * 1024
         st = np.zeros(cap, np.uint64)
         n = lib().tc_engine_phase_times(self.h, st.ctypes.data_as(ctypes.c_void_p), cap)
         if n < 0:
             self._check(n, "phase_times")
-        names = [(p, li) for li in range(len(self.low.types)) for p in LAYER_PHASES] + [(p, -1) for p in TAIL_PHASES]
-        t = st[:n].astype(np.int64)
-        return [(names[i][0], names[i][1], float(t[i + 1] - t[i]) / 1e3) for i in range(min(len(names), n - 1))]
-
-    def profile(self) -> list[tuple[str, float, int]]:
-        """One decode step kernel by kernel: [(kind, ms, algorithmic bytes)]."""
-        cap = 4096
-        ms = np.zeros(cap, np.float32)
-        kind = np.zeros(cap, np.int32)
-        nb = np.zeros(cap, np.uint64)
-        n = lib().tc_engine_profile(self.h, ms.ctypes.data_as(ctypes.c_void_p), kind.ctypes.data_as(ctypes.c_void_p),
-                                    nb.ctypes.data_as(ctypes.c_void_p), cap)
-        if n < 0:
-            self._check(n, "profile")
-        return [(KERNEL_KINDS[kind[i]], float(ms[i]), int(nb[i])) for i in range(n)]
+        grid = (n - 1024) // (9 * L + 8)
+        ex = st[:1024].astype(np.int64)
+        arr = st[1024:1024 + grid * (nph + 1)].astype(np.int64).reshape(nph + 1, grid)
+        names = [(p, li) for li in range(L) for p in LAYER_PHASES] + [(p, -1) for p in TAIL_PHASES]
+        out = []
+        for i in range(1, nph + 1):
+            last = int(arr[i].max())
+            out.append((names[i - 1][0], names[i - 1][1], (ex[i] - ex[i - 1]) / 1e3, (last - ex[i - 1]) / 1e3,
+                        (ex[i] - last) / 1e3))
+        return out
 
     def generate(self, prompts, n_new: int, chunk: int = 4, keep_logits: bool = True):
         """Greedy decoding of B prompts of equal length: prefill in chunks of `chunk` tokens, then
