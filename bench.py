@@ -395,7 +395,7 @@ def build_gemm(world: int = 1, rank: int = 0, seed: int = 1234, ms=GEMM_M, shape
     fp32 partial results added by an ELT descriptor. N above the descriptor's 16-bit field runs as
     row blocks. Returns the image, both queues, the output region and per-descriptor metadata."""
     from opentars_b200 import contract as C
-    from opentars_b200.lowering import Dev, QLin
+    from opentars_b200.program import Image, Linear
     rng = np.random.default_rng(seed)
     Mx = max(ms)
     Ks = sorted({K for K, _, _ in shapes})
@@ -407,46 +407,46 @@ def build_gemm(world: int = 1, rank: int = 0, seed: int = 1234, ms=GEMM_M, shape
     nl = [N // world for _, N, _ in shapes]
     need = sum(5 * Mx * K + 4 * Mx + 512 for K in Ks) + sum(n * K + 4 * n + 512 for n, (K, _, _) in zip(nl, shapes))
     need += sum(4 * M * n * (2 if kb else 1) + 512 for M in ms for n, (_, _, kb) in zip(nl, shapes)) + (1 << 16)
-    p = Dev(need)
-    xv = {K: p.const(xs[K]) for K in Ks}
-    qv = {K: p.quant(xv[K]) for K in Ks}
-    _, q_setup, n_setup = p.build()
+    p = Image(need)
+    xv = {K: p.constant(xs[K]) for K in Ks}
+    qv = {K: p.quantize(xv[K]) for K in Ks}
+    _, q_setup, n_setup = p.finish()
     p.descs, p.queue_off = [], None
     lins = []
     for (K, N, kb), (W, sc), n in zip(shapes, full, nl):
         Wl, sl = W[rank * n:(rank + 1) * n], sc[rank * n:(rank + 1) * n]
-        s_off = p.put(sl)
+        s_off = p.store(sl)
         if kb:
-            lins.append(("k", [QLin(p.put(np.ascontiguousarray(Wl[:, :kb]), "i1"), s_off, None, n, kb),
-                               QLin(p.put(np.ascontiguousarray(Wl[:, kb:]), "i1"), s_off, None, n, K - kb)]))
+            lins.append(("k", [Linear(p.store(np.ascontiguousarray(Wl[:, :kb]), "i1"), s_off, None, n, kb),
+                               Linear(p.store(np.ascontiguousarray(Wl[:, kb:]), "i1"), s_off, None, n, K - kb)]))
         else:
-            w_off = p.put(Wl, "i1")
-            lins.append(("n", [(c0, QLin(w_off + c0 * K, s_off + 4 * c0, None, c1 - c0, K))
+            w_off = p.store(Wl, "i1")
+            lins.append(("n", [(c0, Linear(w_off + c0 * K, s_off + 4 * c0, None, c1 - c0, K))
                                for c0, c1 in _row_blocks(n)]))
     # outputs: row-block-major for N above one descriptor block (the row stride field is 15 bits
-    # of 16 bytes), as the lowering lays out the vocabulary head's logits
+    # of 16 bytes), as the model image lays out the vocabulary head's logits
     y0 = p.top
-    ys = {(M, i): [(c0, p.mat(M, c1 - c0)) for c0, c1 in _row_blocks(n)] for M in ms for i, n in enumerate(nl)}
+    ys = {(M, i): [(c0, p.matrix(M, c1 - c0)) for c0, c1 in _row_blocks(n)] for M in ms for i, n in enumerate(nl)}
     y1 = p.top
     meta = []                      # per GEMM queue descriptor: (M, shape index, ops, weight bytes) or None
     for M in ms:
         for i, ((K, N, kb), (kind, parts), n) in enumerate(zip(shapes, lins, nl)):
             xq, xs_off = qv[K]
-            xq = xq.rowv(0, M)
+            xq = xq.rows_at(0, M)
             if kind == "n":
                 for (c0, lin), (_, y) in zip(parts, ys[(M, i)]):
-                    p.gemm_rc(xq, xs_off, lin, y)
+                    p.mm8(xq, xs_off, lin, y)
                     meta.append((M, i, 2 * M * lin.n * K, lin.n * K))
             else:
                 y = ys[(M, i)][0][1]
-                part = p.mat(M, n)
-                p.gemm_rc(xq.colv(0, kb), xs_off, parts[0], y)
+                part = p.matrix(M, n)
+                p.mm8(xq.cols_at(0, kb), xs_off, parts[0], y)
                 meta.append((M, i, 2 * M * n * kb, n * kb))
-                p.gemm_rc(xq.colv(kb, K - kb), xs_off, parts[1], part)
+                p.mm8(xq.cols_at(kb, K - kb), xs_off, parts[1], part)
                 meta.append((M, i, 2 * M * n * (K - kb), n * (K - kb)))
                 p.elt(C.ELT_ADD, y, part, y)
                 meta.append(None)
-    ddr, q_main, n_main = p.build()
+    ddr, q_main, n_main = p.finish()
     x_first, x_last = min(v.off for v in xv.values()), max(v.off + v.rows * v.ld for v in xv.values())
     return dict(ddr=np.frombuffer(bytes(ddr), np.uint8).copy(), q_setup=q_setup, n_setup=n_setup, q_main=q_main,
                 n_main=n_main, y_region=(y0, y1 - y0), x_region=(x_first, x_last - x_first), ys=ys, nl=nl,
@@ -682,12 +682,12 @@ def prompt_ids(seed: int, vocab: int, n: int = PROMPT_LEN) -> list[int]:
 def build_decode_model(workload: str):
     """The model lowered exactly as the reference lowers it (random weights, seed 0)."""
     from opentars_b200 import models as Mo
-    from opentars_b200.lowering import QwenLowering
+    from opentars_b200.model_image import ModelImage
     base, types, vocab_name, _ = DECODE_MODELS[workload]
     vocab = getattr(Mo, vocab_name)
     cfg = Mo.make_config(getattr(Mo, base), list(getattr(Mo, types)) if types else None, vocab=vocab)
     w = Mo.random_weights(cfg, seed=0, embed=True)
-    return QwenLowering(cfg, w, max_tokens=CONTEXT, ddr_bytes=3 << 29, head=True, queue_cap=8192)
+    return ModelImage(cfg, w, max_tokens=CONTEXT, ddr_bytes=3 << 29, head=True, queue_cap=8192)
 
 
 _CPU: dict = {}

@@ -1,12 +1,11 @@
 """The tars_mini v0.4 descriptor contract on the host: field table, codes, encode/decode.
 
 Mirrors the reference's tars_mini/contract.py call surface (contract.py:14-181) so descriptor
-emitters (the compiler and the lowering) and tests written against it run unchanged. The device
+emitters (the compiler and the program builders) and tests written against it run unchanged. The device
 side decodes and validates in C++ (libtarscuda); this module only builds and reads descriptors.
 """
 from __future__ import annotations
 
-import struct
 import zlib
 
 import numpy as np
@@ -53,78 +52,111 @@ K_MAX = 65535
 CANON_NAN = 0x7FC00000
 
 
+def _span(name: str) -> tuple[int, int]:
+    """(first bit, width) of a field."""
+    hi, lo = LAYOUT[name]
+    return lo, hi - lo + 1
+
+
+def _pack(*parts: tuple[int, int]) -> int:
+    """Packs (value, width) pairs from bit 0 upwards, each value masked to its width."""
+    word, at = 0, 0
+    for val, w in parts:
+        word |= (val & ((1 << w) - 1)) << at
+        at += w
+    return word
+
+
+def _unpack(word: int, *widths: int) -> list[int]:
+    out, at = [], 0
+    for w in widths:
+        out.append(word >> at & ((1 << w) - 1))
+        at += w
+    return out
+
+
 def check_layout() -> None:
-    used = np.zeros(512, dtype=int)
-    for hi, lo in LAYOUT.values():
-        assert 511 >= hi >= lo >= 0
-        used[lo:hi + 1] += 1
-    assert (used == 1).all(), "fields overlap or leave holes"
+    """Every bit of the 512-bit descriptor belongs to exactly one field."""
+    nxt = 0
+    for lo, w in sorted(_span(n) for n in LAYOUT):
+        if lo != nxt or w < 1:
+            raise AssertionError("fields overlap or leave holes")
+        nxt = lo + w
+    if nxt != 8 * DESC_BYTES:
+        raise AssertionError("fields overlap or leave holes")
 
 
 def width(name: str) -> int:
-    hi, lo = LAYOUT[name]
-    return hi - lo + 1
+    return _span(name)[1]
 
 
 def conv_geom(h: int, kh: int, kw: int, stride: int = 1, pad: int = 0) -> int:
-    assert 0 < h < 4096 and 0 < kh < 16 and 0 < kw < 16 and 1 <= stride <= 4 and 0 <= pad <= 3
-    return h << 12 | kh << 8 | kw << 4 | (stride - 1) << 2 | pad
+    """The CONV geometry word in HDR_RSV: pad (2 bits), stride - 1 (2), KW (4), KH (4), H (12)."""
+    if not (0 < h < 4096 and 0 < kh < 16 and 0 < kw < 16 and 1 <= stride <= 4 and 0 <= pad <= 3):
+        raise AssertionError(f"conv geometry h={h} kh={kh} kw={kw} stride={stride} pad={pad}")
+    return _pack((pad, 2), (stride - 1, 2), (kw, 4), (kh, 4), (h, 12))
 
 
 def conv_params(d: dict) -> dict:
-    g = d["HDR_RSV"]
-    h, kh, kw, s, p, w = g >> 12, g >> 8 & 15, g >> 4 & 15, (g >> 2 & 3) + 1, g & 3, d["GROUP_SIZE"]
-    cin = d["K"] // (kh * kw) if kh and kw else 0
-    return dict(H=h, W=w, KH=kh, KW=kw, S=s, P=p, Cin=cin,
+    """A CONV descriptor's geometry: input H x W (W in GROUP_SIZE), kernel, stride, pad, input
+    channels (K / (KH KW)) and the output size."""
+    p, s1, kw, kh, h = _unpack(d["HDR_RSV"], 2, 2, 4, 4, 12)
+    s, w = s1 + 1, d["GROUP_SIZE"]
+    taps = kh * kw
+    return dict(H=h, W=w, KH=kh, KW=kw, S=s, P=p, Cin=d["K"] // taps if taps else 0,
                 OH=(h + 2 * p - kh) // s + 1, OW=(w + 2 * p - kw) // s + 1)
 
 
 def ctrl(qmode: int = QM_TENSOR, symmetric: int = 1, a_dtype: int = DT_INT8, w_dtype: int = DT_INT8,
          fusion: int = 0) -> int:
-    return (qmode & 7) | (symmetric & 1) << 3 | (a_dtype & 15) << 4 | (w_dtype & 15) << 8 | (fusion & 1) << 12
+    """CTRL of a GEMM: quant mode (3 bits), symmetric (1), A type (4), W type (4), fusion (1)."""
+    return _pack((qmode, 3), (symmetric, 1), (a_dtype, 4), (w_dtype, 4), (fusion, 1))
 
 
 def epi(act: int = ACT_NONE, out: int = OUT_FP32, bias: int = 0) -> int:
-    return (act & 3) | (out & 3) << 2 | (bias & 1) << 4 | (act >> 2 & 1) << 5
+    """EPI: activation bits 0-1, output format (2), bias flag (1), activation bit 2 (1)."""
+    return _pack((act, 2), (out, 2), (bias, 1), (act >> 2, 1))
 
 
 def act_of(e: int) -> int:
-    return (e & 3) | (e >> 5 & 1) << 2
+    lo2, _, _, hi1 = _unpack(e, 2, 2, 1, 1)
+    return lo2 | hi1 << 2
 
 
 def f32_bits(x: float) -> int:
-    return struct.unpack("<I", struct.pack("<f", x))[0]
+    return int(np.array(x, np.float32).view(np.uint32))
 
 
 def bits_f32(b: int) -> np.float32:
-    return np.frombuffer(struct.pack("<I", b & 0xFFFFFFFF), dtype="<f4")[0]
+    return np.array(b & 0xFFFFFFFF, np.uint32).view(np.float32)[()]
 
 
 def _crc(raw: bytes) -> int:
-    z = bytearray(raw)
-    z[4:8] = b"\0\0\0\0"
-    return zlib.crc32(bytes(z)) & 0xFFFFFFFF
+    """CRC-32/ISO-HDLC of the 64 bytes with the CRC field (bytes 4..7) read as zero."""
+    raw = bytes(raw)
+    return zlib.crc32(raw[8:], zlib.crc32(raw[:4] + bytes(4)))
 
 
 def encode(fields: dict, *, fix_crc: bool = True) -> bytes:
     """64 bytes, little endian; fields not given are 0; the CRC (CRC-32/ISO-HDLC over all 64
     bytes with bytes 4..7 zeroed) is filled in unless fix_crc is False."""
-    v = 0
+    word = 0
     for name, val in fields.items():
-        hi, lo = LAYOUT[name]
-        if not 0 <= val < (1 << (hi - lo + 1)):
-            raise ValueError(f"{name}={val} does not fit {hi - lo + 1} bits")
-        v |= val << lo
-    raw = bytearray(v.to_bytes(DESC_BYTES, "little"))
+        lo, w = _span(name)
+        val = int(val)
+        if val < 0 or val >> w:
+            raise ValueError(f"{name}={val} does not fit {w} bits")
+        word |= val << lo
+    raw = bytearray(word.to_bytes(DESC_BYTES, "little"))
     if fix_crc:
-        raw[4:8] = struct.pack("<I", _crc(bytes(raw)))
+        raw[4:8] = _crc(raw).to_bytes(4, "little")
     return bytes(raw)
 
 
 def decode(raw: bytes) -> dict:
-    v = int.from_bytes(raw, "little")
-    return {n: (v >> lo) & ((1 << (hi - lo + 1)) - 1) for n, (hi, lo) in LAYOUT.items()}
+    word = int.from_bytes(raw, "little")
+    return {name: word >> lo & ((1 << w) - 1) for name, (lo, w) in ((n, _span(n)) for n in LAYOUT)}
 
 
 def crc_ok(raw: bytes) -> bool:
-    return struct.unpack("<I", bytes(raw[4:8]))[0] == _crc(raw)
+    return int.from_bytes(bytes(raw[4:8]), "little") == _crc(raw)

@@ -595,13 +595,13 @@ __device__ __noinline__ void gated_unit(const StepArgs& a, int m, int c, const S
   amax = wmax(amax, red);
   stamp(a, 712);
   __shared__ int s_last;
+  // every worker's stores are ordered before the counting thread's fence by wmax's barrier, and the
+  // fence is cumulative: one fence before the count publishes them all
   if (tid == 0) {
     a.gmax[m * nch + c] = amax;
     __threadfence();
     const unsigned prev = atomicAdd(&a.sync[1 + a.B + m], 1u);
     s_last = (prev + 1) % (unsigned)nch == 0;
-  } else {
-    __threadfence();
   }
   sync_workers();
   stamp(a, 713);
@@ -656,35 +656,55 @@ __device__ __noinline__ void attn_unit(const StepArgs& a, const StepLayer& Ly, i
   const uint64_t ldp = g.col0[g.nseg], slab = (uint64_t)a.B * ldp;
   const float sr = ftz(a.qsa[b]);
   stamp(a, 720);
-  float* stab = skv + (2 * G + 3) * HD;               // the RoPE table row of t0
+  float* stab = skv + (2 * G + 3) * HD;               // the RoPE table row of t0, the q / k norm
+  float* sgq = stab + HD;                              // gammas: staged while the partials load
+  float* sgk = sgq + HD;
   for (int i = tid; i < a.rot / 4; i += gt) cp16(stab + 4 * i, Ly.tab + (uint64_t)t0 * a.rot + 4 * i);
+  for (int i = tid; i < Q4; i += gt) {
+    cp16(sgq + 4 * i, Ly.qn + 4 * i);
+    cp16(sgk + 4 * i, Ly.kn + 4 * i);
+  }
   asm volatile("cp.async.commit_group;" ::: "memory");
   // 1. the unit's q | k | v values (G query heads, the K row, the V row) from the partial sums,
   //    four columns per thread with every chunk's load issued before the sums
-  for (int i = tid; i < (G + 2) * Q4; i += gt) {
-    const int it = i / Q4, d = 4 * (i - it * Q4);
-    const int seg = it < G ? 0 : (it == G ? 1 : 2);
-    const int cis = (it < G ? (kvh * G + it) * HD : kvh * HD) + d;
-    const int* p = a.part + (uint64_t)b * ldp + g.col0[seg] + cis;
-    int4 v[8];
+  const int nq = (G + 2) * Q4;
+  for (int i0 = tid; i0 < nq; i0 += 2 * gt) {
+    int4 v[2][8];                                      // two quads' chunk loads in flight at once
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks)
-      if (ks < g.ksplit) v[ks] = *reinterpret_cast<const int4*>(p + ks * slab);
-    int4 acc = make_int4(0, 0, 0, 0);
+    for (int h = 0; h < 2; ++h) {
+      const int i = i0 + h * gt;
+      if (i >= nq) break;
+      const int it = i / Q4, d = 4 * (i - it * Q4);
+      const int seg = it < G ? 0 : (it == G ? 1 : 2);
+      const int cis = (it < G ? (kvh * G + it) * HD : kvh * HD) + d;
+      const int* p = a.part + (uint64_t)b * ldp + g.col0[seg] + cis;
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks)
-      if (ks < g.ksplit) {
-        acc.x += v[ks].x;
-        acc.y += v[ks].y;
-        acc.z += v[ks].z;
-        acc.w += v[ks].w;
-      }
-    const float4 sc = *reinterpret_cast<const float4*>(g.scale[seg] + cis);
-    float* dst = skv + it * HD + d;
-    dst[0] = ftz(ep_fast(acc.x, sr, ftz(sc.x)));
-    dst[1] = ftz(ep_fast(acc.y, sr, ftz(sc.y)));
-    dst[2] = ftz(ep_fast(acc.z, sr, ftz(sc.z)));
-    dst[3] = ftz(ep_fast(acc.w, sr, ftz(sc.w)));
+      for (int ks = 0; ks < 8; ++ks)
+        if (ks < g.ksplit) v[h][ks] = *reinterpret_cast<const int4*>(p + ks * slab);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int i = i0 + h * gt;
+      if (i >= nq) break;
+      const int it = i / Q4, d = 4 * (i - it * Q4);
+      const int seg = it < G ? 0 : (it == G ? 1 : 2);
+      const int cis = (it < G ? (kvh * G + it) * HD : kvh * HD) + d;
+      int4 acc = make_int4(0, 0, 0, 0);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        if (ks < g.ksplit) {
+          acc.x += v[h][ks].x;
+          acc.y += v[h][ks].y;
+          acc.z += v[h][ks].z;
+          acc.w += v[h][ks].w;
+        }
+      const float4 sc = *reinterpret_cast<const float4*>(g.scale[seg] + cis);
+      float* dst = skv + it * HD + d;
+      dst[0] = ftz(ep_fast(acc.x, sr, ftz(sc.x)));
+      dst[1] = ftz(ep_fast(acc.y, sr, ftz(sc.y)));
+      dst[2] = ftz(ep_fast(acc.z, sr, ftz(sc.z)));
+      dst[3] = ftz(ep_fast(acc.w, sr, ftz(sc.w)));
+    }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   stamp(a, 721);
@@ -706,7 +726,7 @@ __device__ __noinline__ void attn_unit(const StepArgs& a, const StepLayer& Ly, i
     }
     s = sum16_fold(canon(s));
     const float rs = rsqrt_f(fadd(fmul(s, recip_f(i2f(HD))), a.eps));
-    const float* gam = it < G ? Ly.qn : Ly.kn;
+    const float* gam = it < G ? sgq : sgk;
     if (live) {
 #pragma unroll
       for (int i = 0; i < HD / 16; ++i) sn[it * HD + l + 16 * i] = ftz(fmul(fmul(v[i], rs), gam[l + 16 * i]));
@@ -841,15 +861,13 @@ __device__ __noinline__ void attn_unit(const StepArgs& a, const StepLayer& Ly, i
   mx = warp_max(mx);
   if (lane == 0) gc->wred[warp] = mx;
   gr.sync();
-  if (tid == 0) {
+  if (tid == 0) {                                      // (one cumulative fence, as in gated_unit)
     float m = gc->wred[0];
     for (int w = 1; w < nwarps; ++w) m = fmax_c(m, gc->wred[w]);
     a.amax[b * a.nkv + kvh] = m;
     __threadfence();
     const unsigned prev = atomicAdd(&a.sync[1 + b], 1u);
     gc->last = (prev + 1) % (unsigned)a.nkv == 0;
-  } else {
-    __threadfence();
   }
   gr.sync();
   stamp(a, 726);
@@ -1026,7 +1044,7 @@ int step_attn_tile(int hd, int G, int ngroups) {
   const int region = kRegion / ngroups;
   const int fixed = (G * hd + G * kT) * 4;
   const int per = (hd + 4) * 4;
-  const int scratch = (2 * G + 4) * hd * 4;            // the prologue's rows and RoPE row, before the first tile
+  const int scratch = (2 * G + 6) * hd * 4;            // the prologue's rows, RoPE row and norm gammas
   int tile = (region - fixed) / per / 16 * 16;
   tile = std::min(tile, kT);
   if (tile < 16 || tile * per < scratch || G * hd > 8 * (256 / ngroups)) return 0;

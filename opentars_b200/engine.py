@@ -1,10 +1,10 @@
-"""Batched greedy decoding on one B200 (include/tarscuda_engine.h), fed from a QwenLowering.
+"""Batched greedy decoding on one B200 (include/tarscuda_engine.h), fed from a ModelImage.
 
-    low = QwenLowering(cfg, weights, max_tokens=256, head=True)
+    low = ModelImage(cfg, weights, max_tokens=256, head=True)
     eng = DecodeEngine(low, batch=64)
     ids, logits = eng.generate(prompts, n_new, chunk=4)     # prompts: [batch][len] token ids
 
-The engine reads the weights from the lowering's DDR image (uploaded once to HBM) and runs every
+The engine reads the weights from the model's DDR image (uploaded once to HBM) and runs every
 sequence's step on the GPU, B sequences at a time; per sequence the tokens and logits equal the
 descriptor path's (the reference golden model's) bit for bit. The host only moves token ids, and
 the logits when asked for.
@@ -129,11 +129,11 @@ class DecodeEngine:
         from ._lib import check
         from .machine import default_device
         if not low.head:
-            raise ValueError("the lowering needs its head (head=True)")
+            raise ValueError("the model image needs its head (head=True)")
         self.low, self.B = low, int(batch)
         self.device = default_device() if device is None else device
         L = lib()
-        img = ctypes.c_void_p()                                   # the weights: the lowering's image in HBM
+        img = ctypes.c_void_p()                                   # the weights: the model's image in HBM
         n = len(low.p.ddr)
         if L.tc_open(self.device, n, ctypes.byref(img)) != 0:
             raise RuntimeError(f"cannot open a {n}-byte image on CUDA device {self.device}")

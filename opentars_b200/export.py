@@ -1,4 +1,4 @@
-"""Writes a model lowered by QwenLowering as a board export directory - the file set that
+"""Writes a ModelImage as a board export directory - the file set that
 tools/export_kv260.py:14-33 describes (the PLE fields: 234-237) and tars_board.py:212-435 (and board.Qwen) reads:
 
     image.bin        the DDR image from address 0: the zeroed state, the queue region, scratch,
@@ -10,12 +10,12 @@ tools/export_kv260.py:14-33 describes (the PLE fields: 234-237) and tars_board.p
     queues_c<n>.bin  prefill: one queue per chunk of n tokens at t0 = 0, align, 2 align, ...
     manifest.json    the addresses and sizes the runtime needs and the queue indexes
 
-The queues are the lowering's own chunk(t0, n) descriptors (byte-identical to the reference
+The queues are the model image's own chunk(t0, n) descriptors (byte-identical to the reference
 lowering's), so an export of the same weights and configuration holds the same queues as the
 reference exporter's. Checkpoint loading, the tokenizer files and the golden check of
 expected.json belong to the reference's exporter and are not part of this writer.
 
-    low = QwenLowering(cfg, weights, max_tokens=T, head=True, queue_cap=4096)
+    low = ModelImage(cfg, weights, max_tokens=T, head=True, queue_cap=4096)
     write_export(low, "out/")
 """
 from __future__ import annotations
@@ -38,11 +38,11 @@ def bf16_exact(a: np.ndarray) -> np.ndarray:
 
 def write_export(low, out, chunks=(4,), align: int = 4, bos_ids=(), eos_ids=(), chat_prefix: str = "",
                  chat_suffix: str = "") -> dict:
-    """Writes the export of `low` (a QwenLowering built with head=True and a queue region) into
+    """Writes the export of `low` (a ModelImage built with head=True and a queue region) into
     `out`; returns the manifest. Every position 0 .. T-1 gets a one-token queue; chunk sizes in
     `chunks` get a queue at every t0 that is a multiple of `align` with t0 + n <= T."""
     if not low.head or not low.queue_cap:
-        raise ValueError("the lowering needs the head and a queue region (head=True, queue_cap > 0)")
+        raise ValueError("the model image needs the head and a queue region (head=True, queue_cap > 0)")
     if low.p.base:
         raise ValueError("an export's image starts at address 0 (base_addr = 0)")
     out = Path(out)

@@ -62,9 +62,9 @@ def main():
 
     from . import models as Mo
     from .engine import DecodeEngine
-    from .lowering import QwenLowering
+    from .model_image import ModelImage
     cfg = Mo.make_config(Mo.CFG_Q3_06B, None, vocab=Mo.VOCAB_Q3_06B)
-    low = QwenLowering(cfg, Mo.random_weights(cfg, seed=0, embed=True), max_tokens=256, ddr_bytes=3 << 29,
+    low = ModelImage(cfg, Mo.random_weights(cfg, seed=0, embed=True), max_tokens=256, ddr_bytes=3 << 29,
                        head=True, queue_cap=8192)
     os.environ.setdefault("TC_DEVICE", "0")
     torch.cuda.set_device(int(os.environ["TC_DEVICE"]))

@@ -1,4 +1,4 @@
-"""Host model data for the lowering: configs, seeded random weights, weight quantisers.
+"""Host model data for the model images: configs, seeded random weights, weight quantisers.
 
 Restates, for the model families on the hot path (Qwen3, Gemma 3 / 4 and Qwen3.5 text models):
   * make_config          tars_mini/qwen_ref.py:109-146 (transformers config objects)
@@ -123,70 +123,89 @@ def param_shapes(cfg) -> list[tuple[str, tuple[int, ...]]]:
     return [(n, tuple(p.shape)) for n, p in m.state_dict().items()]
 
 
+def _linear_rows(rng, shape) -> np.ndarray:
+    """N(0, 0.02), then 2 % of the output rows (one uniform draw per row) times 4."""
+    a = rng.normal(0.0, 0.02, shape)
+    a[rng.random(shape[0]) < 0.02] *= 4.0
+    return a
+
+
+def _drawer(cfg, name: str, shape: tuple[int, ...]):
+    """How one non-embedding parameter is drawn: a function of the generator."""
+    if len(shape) == 2:
+        return lambda rng: _linear_rows(rng, shape)
+    if "conv1d" in name:
+        return lambda rng: rng.normal(0.0, 0.3, shape)
+    if name.endswith("A_log"):
+        return lambda rng: np.log(rng.uniform(1.0, 16.0, shape))
+    if name.endswith(("dt_bias", ".layer_scalar")):
+        return lambda rng: rng.uniform(0.5, 1.5, shape)
+    # norm gains: around 1, except the zero-centred ones (gains applied as 1 + w)
+    centred = cfg.model_type not in ("qwen3", "gemma4_text") and not name.endswith("linear_attn.norm.weight")
+    return lambda rng: rng.normal(0.0 if centred else 1.0, 0.1, shape)
+
+
+def _table(rng, shape, std: float, block: int = 8192) -> np.ndarray:
+    """An embedding table drawn `block` rows at a time (bounded float64 temporaries)."""
+    out = np.empty(shape, F32)
+    for r0 in range(0, shape[0], block):
+        r1 = min(shape[0], r0 + block)
+        out[r0:r1] = rng.normal(0.0, std, (r1 - r0,) + tuple(shape[1:]))
+    return out
+
+
 def random_weights(cfg, seed: int = 0, embed: bool = False) -> dict[str, np.ndarray]:
     """Linears N(0, 0.02) with 2 % of the output rows x4; Qwen3.5's conv taps N(0, 0.3), A_log =
     log U(1, 16), dt_bias (and Gemma 4's layer_scalar) U(0.5, 1.5), the gated norm 1 + N(0, 0.1);
     norms 1 + N(0, 0.1) (Qwen3, Gemma 4) or N(0, 0.1) (Gemma 3 and Qwen3.5, zero-centred); with
     `embed` the embedding tables (the tied one, Gemma 4's per-layer one) N(0, 0.02), drawn 8192
-    rows at a time."""
+    rows at a time. One generator, parameters in state_dict order."""
     rng = np.random.default_rng(seed)
-    w = {}
+    out = {}
     for name, shape in param_shapes(cfg):
-        if name.startswith("embed_tokens"):
-            if embed:
-                e = np.empty(shape, np.float32)
-                for r in range(0, shape[0], 8192):
-                    e[r:r + 8192] = rng.normal(0, 0.02, (min(8192, shape[0] - r), shape[1]))
-                w[name] = e
-            continue
-        if len(shape) == 2:
-            a = rng.normal(0, 0.02, shape) * np.where(rng.random(shape[0]) < 0.02, 4.0, 1.0)[:, None]
-        elif "conv1d" in name:
-            a = rng.normal(0, 0.3, shape)
-        elif name.endswith("A_log"):
-            a = np.log(rng.uniform(1, 16, shape))
-        elif name.endswith("dt_bias") or name.endswith(".layer_scalar"):
-            a = rng.uniform(0.5, 1.5, shape)
-        elif name.endswith("linear_attn.norm.weight"):
-            a = 1 + rng.normal(0, 0.1, shape)
-        elif cfg.model_type in ("qwen3", "gemma4_text"):
-            a = 1 + rng.normal(0, 0.1, shape)
-        else:
-            a = rng.normal(0, 0.1, shape)
-        w[name] = a.astype(np.float32)
-    return w
+        if not name.startswith("embed_tokens"):
+            out[name] = _drawer(cfg, name, shape)(rng).astype(F32)
+        elif embed:
+            out[name] = _table(rng, shape, 0.02)
+    return out
 
 
 def random_mtp(cfg, seed: int = 5) -> dict[str, np.ndarray]:
     """Random Qwen3.5 MTP-head weights (qwen_ref.py:258-270): the linears N(0, 0.02) and the norms
     N(0, 0.1), drawn in this order, under the checkpoint's names (mtp.*)."""
-    rng = np.random.default_rng(seed)
     H, I, hd = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
     nq, nkv = cfg.num_attention_heads * hd, cfg.num_key_value_heads * hd
-    lin = {"fc": (H, 2 * H), "layers.0.self_attn.q_proj": (2 * nq, H), "layers.0.self_attn.k_proj": (nkv, H),
-           "layers.0.self_attn.v_proj": (nkv, H), "layers.0.self_attn.o_proj": (H, nq),
-           "layers.0.mlp.gate_proj": (I, H), "layers.0.mlp.up_proj": (I, H), "layers.0.mlp.down_proj": (H, I)}
-    nrm = {"norm": H, "pre_fc_norm_embedding": H, "pre_fc_norm_hidden": H, "layers.0.input_layernorm": H,
-           "layers.0.post_attention_layernorm": H, "layers.0.self_attn.q_norm": hd, "layers.0.self_attn.k_norm": hd}
-    w = {f"mtp.{k}.weight": rng.normal(0, 0.02, s).astype(np.float32) for k, s in lin.items()}
-    w.update({f"mtp.{k}.weight": rng.normal(0, 0.1, n).astype(np.float32) for k, n in nrm.items()})
-    return w
+    attn, mlp = "layers.0.self_attn.", "layers.0.mlp."
+    linears = [("fc", (H, 2 * H))]
+    linears += [(attn + f"{p}_proj", s) for p, s in (("q", (2 * nq, H)), ("k", (nkv, H)), ("v", (nkv, H)),
+                                                     ("o", (H, nq)))]
+    linears += [(mlp + f"{p}_proj", s) for p, s in (("gate", (I, H)), ("up", (I, H)), ("down", (H, I)))]
+    gains = [(k, H) for k in ("norm", "pre_fc_norm_embedding", "pre_fc_norm_hidden", "layers.0.input_layernorm",
+                              "layers.0.post_attention_layernorm")]
+    gains += [(attn + "q_norm", hd), (attn + "k_norm", hd)]
+    rng = np.random.default_rng(seed)
+    out = {}
+    for group, std in ((linears, 0.02), (gains, 0.1)):
+        for key, shape in group:
+            out[f"mtp.{key}.weight"] = rng.normal(0.0, std, shape).astype(F32)
+    return out
 
 
 def head_rows(vocab: int) -> int:
-    for b in range(1, vocab // 16 + 1):
-        r = vocab // b
-        if vocab % b == 0 and r <= 65535 and r % 16 == 0:
-            return r
-    raise ValueError(f"vocabulary {vocab}: no block split")
+    """Rows of one block when the vocabulary is cut into the fewest equal blocks of at most 65535
+    rows, each a multiple of 16: the largest such divisor."""
+    fits = [r for r in range(16, min(vocab, 65535) + 1, 16) if vocab % r == 0]
+    if not fits:
+        raise ValueError(f"vocabulary {vocab}: no block split")
+    return fits[-1]
 
 
 def input_embedding(cfg, rows: np.ndarray) -> np.ndarray:
     """Gemma 3 / 4 scale embedding rows by fp32(sqrt(hidden)), one fp32 rounding (llm.py:198-204)."""
-    rows = np.asarray(rows, F32)
-    if getattr(cfg, "model_type", "") not in ("gemma3_text", "gemma4_text"):
-        return rows
-    return (rows * F32(cfg.hidden_size ** 0.5)).astype(F32)
+    out = np.asarray(rows, F32)
+    if getattr(cfg, "model_type", "") in ("gemma3_text", "gemma4_text"):
+        out = np.multiply(out, F32(np.sqrt(cfg.hidden_size)), dtype=F32)
+    return out
 
 
 def ple_embedding(cfg, rows: np.ndarray) -> np.ndarray:
@@ -205,11 +224,17 @@ class QWeight:
 
 
 def quantize_weight(w: np.ndarray, per_channel: bool = True) -> QWeight:
-    w = np.asarray(w, dtype=np.float64)
-    amax = np.abs(w).max(axis=1) if per_channel else np.array([np.abs(w).max()])
-    s = np.where(amax > 0, amax / 127.0, 1.0)
-    q = np.clip(np.rint(w / (s[:, None] if per_channel else s[0])), -127, 127).astype(np.int8)
-    return QWeight(q=q, scale=s.astype(np.float32), n=w.shape[0], k=w.shape[1])
+    """Symmetric int8 weights (compiler.py:50-57): scale = absmax / 127 per output row (or one for
+    the whole matrix), 1 where the absmax is 0; q = round half to even of w / scale, clipped to
+    +-127; all in float64, the scales stored as fp32."""
+    w64 = np.asarray(w, np.float64)
+    amax = np.abs(w64).max(axis=1, keepdims=True)
+    if not per_channel:
+        amax = amax.max(keepdims=True)
+    scale = amax / 127.0
+    scale[amax == 0] = 1.0
+    q = np.rint(w64 / scale).clip(-127, 127).astype(np.int8)
+    return QWeight(q=q, scale=scale.reshape(-1).astype(np.float32), n=w64.shape[0], k=w64.shape[1])
 
 
 @dataclass

@@ -14,20 +14,22 @@ Restates, so that the same DDR image and the same descriptor queue come out byte
   * patchify                                           qwen_vit.py:115-129
   * position_embeddings, rope_table: the tower's fp32 host computations (its position-table
     interpolation and axial rotary angles), restated and pinned to transformers' tower
-  * VisionLowering (weights, buffers, the image's descriptors, run)   qwen_vit.py:226-418
+  * VisionImage (weights, buffers, the image's descriptors, run): the program the reference's
+    tower lowering builds (qwen_vit.py:226-418), byte for byte, from a builder of this package
 
     cfg = vision_config(**small); w = random_vision(cfg)
     px, grid = patchify(image, cfg)
-    low = VisionLowering(cfg, w, patches_max=len(px))
-    tokens = low.run(px, position_embeddings(cfg, w, grid), rope_table(cfg, grid))
+    tower = VisionImage(cfg, w, patches_max=len(px))
+    tokens = tower.run(px, position_embeddings(cfg, w, grid), rope_table(cfg, grid))
 """
 from __future__ import annotations
 
 import numpy as np
 
 from . import contract as C
-from .lowering import QLin, V, Dev, pad16
+from .model_image import pad16
 from .models import quantize_weight
+from .program import Buf, Image, Linear
 
 F32 = np.float32
 
@@ -43,14 +45,13 @@ def vision_config(path: str | None = None, **over):
     """A Qwen3_5VisionConfig: `path`'s config.json vision_config (else the 0.8B numbers), any
     keyword overriding a field."""
     from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5VisionConfig
-    base = dict(VIT_08B)
+    fields = dict(VIT_08B)
     if path is not None:
         import json
-        from pathlib import Path
-        vc = json.loads((Path(path) / "config.json").read_text())["vision_config"]
-        base = dict(base, **{k: v for k, v in vc.items() if k != "model_type"})
-    base.update(over)
-    cfg = Qwen3_5VisionConfig(**base)
+        import pathlib
+        with open(pathlib.Path(path, "config.json")) as f:
+            fields.update((k, v) for k, v in json.load(f)["vision_config"].items() if k != "model_type")
+    cfg = Qwen3_5VisionConfig(**{**fields, **over})
     cfg._attn_implementation = "eager"
     return cfg
 
@@ -66,19 +67,24 @@ def random_vision(cfg, seed: int = 0) -> dict[str, np.ndarray]:
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5VisionModel
     with torch.device("meta"):
         m = Qwen3_5VisionModel(cfg)
+    gains = ("norm.weight", "norm1.weight", "norm2.weight")
     rng = np.random.default_rng(seed)
-    w = {}
-    for name, p in m.state_dict().items():
-        shape = tuple(p.shape)
-        if name.endswith(("norm.weight", "norm1.weight", "norm2.weight")):
-            a = 1 + rng.normal(0, 0.1, shape)
-        else:
-            a = rng.normal(0, 0.02, shape)
-        w[name] = a.astype(F32)
-    return w
+    out = {}
+    for name, t in m.state_dict().items():
+        mean, std = (1.0, 0.1) if name.endswith(gains) else (0.0, 0.02)
+        out[name] = rng.normal(mean, std, tuple(t.shape)).astype(F32)
+    return out
 
 
 # ---------------------------------------------------------------------- host preprocessing
+def _merge_order(h: int, w: int, ms: int) -> np.ndarray:
+    """Row-major patch indices of an h x w grid in spatial-merge order: merge blocks row-major,
+    then the rows and columns inside a block."""
+    r = np.arange(h).reshape(h // ms, ms)[:, None, :, None]
+    c = np.arange(w).reshape(w // ms, ms)[None, :, None, :]
+    return np.broadcast_to(r * w + c, (h // ms, w // ms, ms, ms)).reshape(-1)
+
+
 def patchify(img, cfg) -> tuple[np.ndarray, np.ndarray]:
     """A normalised image [C, H, W] (sides multiples of patch * merge) as patches
     [P, C * temporal * patch * patch] in spatial-merge-block order (block row, block column, then
@@ -90,18 +96,10 @@ def patchify(img, cfg) -> tuple[np.ndarray, np.ndarray]:
     if c != cfg.in_channels or hh % (ps * ms) or ww % (ps * ms):
         raise ValueError(f"image {img.shape}: {cfg.in_channels} channels, sides multiples of {ps * ms}")
     gh, gw = hh // ps, ww // ps
-    # axes: channel, block row, row in block, pixel row, block column, column in block, pixel column
-    x = img.reshape(c, gh // ms, ms, ps, gw // ms, ms, ps).transpose(1, 4, 2, 5, 0, 3, 6)
-    x = np.broadcast_to(x[..., None, :, :], x.shape[:5] + (tp, ps, ps))
-    return np.ascontiguousarray(x, F32).reshape(gh * gw, c * tp * ps * ps), np.array([[1, gh, gw]])
-
-
-def _merge_order(h: int, w: int, ms: int) -> np.ndarray:
-    """Row-major patch indices of an h x w grid in spatial-merge order: merge blocks row-major,
-    then the rows and columns inside a block."""
-    r = np.arange(h).reshape(h // ms, ms)[:, None, :, None]
-    c = np.arange(w).reshape(w // ms, ms)[None, :, None, :]
-    return np.broadcast_to(r * w + c, (h // ms, w // ms, ms, ms)).reshape(-1)
+    # the patches row-major as [patch, channel, 1, row, column], then taken in merge order
+    tiles = img.reshape(c, gh, ps, gw, ps).transpose(1, 3, 0, 2, 4).reshape(gh * gw, c, 1, ps, ps)
+    tiles = tiles[_merge_order(gh, gw, ms)]
+    return np.repeat(tiles, tp, axis=2).reshape(gh * gw, -1).astype(F32), np.array([[1, gh, gw]])
 
 
 def position_embeddings(cfg, w, grid_thw) -> np.ndarray:
@@ -148,181 +146,172 @@ def rope_table(cfg, grid_thw) -> np.ndarray:
     return torch.cat([ang.cos(), ang.sin()], dim=-1).numpy().astype(F32)
 
 
-# ---------------------------------------------------------------------- the lowering
-class VisionLowering:
-    """The tower as v0.4 descriptors. The key axis is padded to a multiple of 16: the padded key
-    and value rows are zero and the padded scores are set to MASK_NEG (a MUL by a 0/1 row, then an
-    ADD of a 0 / MASK_NEG row), so the padding changes no sum. Weights and buffers are sized for
-    `patches_max`; the patches, the position and rotary rows and the two mask rows are written per
-    image, so one program serves any image up to that capacity. W8A8 only."""
+# ---------------------------------------------------------------------- the tower's program
+class VisionImage:
+    """The tower as one image and one descriptor queue (W8A8). Keys are padded to a multiple of 16:
+    the padded K and V rows stay zero and each head's padded scores are set to MASK_NEG (a MUL by a
+    0/1 row, then an ADD of a 0 / MASK_NEG row), so the padding changes no sum. Weights and buffers
+    are sized for `patches_max`; the patches, position and rotary rows and the two mask rows are
+    written per image, so one program serves any image up to that capacity. Image and queue are
+    byte-identical to those of the reference's tower lowering (qwen_vit.py:226-418) for the same
+    image (pinned by tests/golden/vision.json)."""
 
     def __init__(self, cfg, w, patches_max: int, ddr_bytes: int = 1 << 28, scratch_bytes: int | None = None,
                  wbits: int = 8):
         if wbits != 8:
-            raise ValueError("the vision tower is lowered W8A8")
+            raise ValueError("the vision tower is W8A8")
         self.cfg, self.w = cfg, w
-        self.H, self.I = cfg.hidden_size, cfg.intermediate_size
-        self.nh, self.hd = cfg.num_heads, head_dim(cfg)
-        self.K = cfg.in_channels * cfg.temporal_patch_size * cfg.patch_size ** 2
-        self.ms2 = cfg.spatial_merge_size ** 2
+        self.H, self.I, self.nh, self.hd = cfg.hidden_size, cfg.intermediate_size, cfg.num_heads, head_dim(cfg)
+        self.K = cfg.in_channels * cfg.temporal_patch_size * cfg.patch_size ** 2     # one patch vector
+        self.ms2 = cfg.spatial_merge_size ** 2                                       # patches per merged token
         self.P, self.npad = patches_max, pad16(patches_max)
-        assert self.nh * self.hd == self.H and self.H % 16 == 0 and self.K % 16 == 0
-        assert self.hd % 32 == 0, "the rotary width must be a multiple of 32"
+        if self.nh * self.hd != self.H or self.H % 16 or self.K % 16 or self.hd % 32:
+            raise ValueError("heads x head dim = hidden; hidden, patch vector multiples of 16; rotary of 32")
         self.eps = VIT_EPS
-        self.p = self.prog = Dev(ddr_bytes=ddr_bytes)
-        self._weights()
-        self._bufs()
-        self.scratch0 = self.p.top
-        if scratch_bytes is None:                    # the patches, position and rotary rows, widest quant
+        self.p = Image(ddr_bytes)
+        self._place_weights()
+        self._place_buffers()
+        if scratch_bytes is None:            # the image's patches, position and rotary rows, and slack
             scratch_bytes = 4 * patches_max * (self.K + self.ms2 * self.H + 2 * self.H) + (1 << 20)
-        self.scratch_end = self.p.alloc(scratch_bytes) + scratch_bytes
+        self.scratch0 = self.p.top
+        self.scratch_end = self.p.reserve(scratch_bytes) + scratch_bytes
         self.end = self.p.top
 
-    def lin(self, w: np.ndarray, b: np.ndarray | None = None) -> QLin:
-        qw = quantize_weight(np.asarray(w, np.float64), per_channel=True)
-        assert qw.n % 16 == 0 and qw.k % 16 == 0, (qw.n, qw.k)
-        b_off = self.p.put(np.asarray(b, F32)) if b is not None else None
-        return QLin(self.p.put(qw.q, "i1"), self.p.put(qw.scale), b_off, qw.n, qw.k)
+    def _linear(self, weight, bias) -> Linear:
+        qw = quantize_weight(np.asarray(weight, np.float64), per_channel=True)
+        if qw.n % 16 or qw.k % 16:
+            raise ValueError(f"linear {qw.n} x {qw.k}: multiples of 16")
+        b_off = self.p.store(np.asarray(bias, F32))
+        return Linear(self.p.store(qw.q, "i1"), self.p.store(qw.scale), b_off, qw.n, qw.k)
 
-    def _weights(self) -> None:
-        w, H, p = self.w, self.H, self.p
-        self.pe = self.lin(w["patch_embed.proj.weight"].reshape(H, -1), w["patch_embed.proj.bias"])
+    def _layernorm(self, name: str) -> tuple[Buf, Buf]:
+        return self.p.constant(self.w[name + ".weight"]), self.p.constant(self.w[name + ".bias"])
+
+    def _place_weights(self) -> None:
+        w, H = self.w, self.H
+        self.pe = self._linear(w["patch_embed.proj.weight"].reshape(H, -1), w["patch_embed.proj.bias"])
         self.blocks = []
         for i in range(self.cfg.depth):
-            b = f"blocks.{i}."
-            self.blocks.append(dict(
-                n1=(p.const(w[b + "norm1.weight"]), p.const(w[b + "norm1.bias"])),
-                n2=(p.const(w[b + "norm2.weight"]), p.const(w[b + "norm2.bias"])),
-                qkv=self.lin(w[b + "attn.qkv.weight"], w[b + "attn.qkv.bias"]),
-                proj=self.lin(w[b + "attn.proj.weight"], w[b + "attn.proj.bias"]),
-                fc1=self.lin(w[b + "mlp.linear_fc1.weight"], w[b + "mlp.linear_fc1.bias"]),
-                fc2=self.lin(w[b + "mlp.linear_fc2.weight"], w[b + "mlp.linear_fc2.bias"])))
-        self.m_norm = (p.const(w["merger.norm.weight"]), p.const(w["merger.norm.bias"]))
-        self.m_fc1 = self.lin(w["merger.linear_fc1.weight"], w["merger.linear_fc1.bias"])
-        self.m_fc2 = self.lin(w["merger.linear_fc2.weight"], w["merger.linear_fc2.bias"])
-        assert self.m_fc1.k == self.ms2 * H, "the merger takes the merge block's rows as one row"
-        self.sc_q = p.const(np.array([F32(self.hd ** -0.5)], F32))         # the attention scaling
+            pre = f"blocks.{i}."
+            blk = {"n1": self._layernorm(pre + "norm1"), "n2": self._layernorm(pre + "norm2")}
+            for key, name in (("qkv", "attn.qkv"), ("proj", "attn.proj"), ("fc1", "mlp.linear_fc1"),
+                              ("fc2", "mlp.linear_fc2")):
+                blk[key] = self._linear(w[pre + name + ".weight"], w[pre + name + ".bias"])
+            self.blocks.append(blk)
+        self.m_norm = self._layernorm("merger.norm")
+        self.m_fc1 = self._linear(w["merger.linear_fc1.weight"], w["merger.linear_fc1.bias"])
+        self.m_fc2 = self._linear(w["merger.linear_fc2.weight"], w["merger.linear_fc2.bias"])
+        if self.m_fc1.k != self.ms2 * H:
+            raise ValueError("the merger takes a merge block's rows as one row")
+        self.sc_q = self.p.constant(np.array([F32(self.hd ** -0.5)], F32))         # the attention scaling
 
-    def _bufs(self) -> None:
-        p, n, npad, H = self.p, self.P, self.npad, self.H
+    def _place_buffers(self) -> None:
+        p, n, npad, H, I = self.p, self.P, self.npad, self.H, self.I
+        zeros = lambda r, c: p.constant(np.zeros((r, c), F32))  # noqa: E731
+        self.kbuf, self.vbuf = zeros(npad, H), zeros(npad, H)                # K, V rows; padding stays 0
+        self.sc, self.prow = zeros(n, npad), zeros(n, npad)                  # one head's scores, softmax
+        keep = np.concatenate([np.ones((1, n), F32), np.zeros((1, npad - n), F32)], axis=1)
+        self.mask = p.constant(keep)
+        self.mbias = p.constant(np.where(keep > 0, F32(0), MASK_NEG).astype(F32))
+        self.zrow = zeros(1, H)                                              # a copy adds this row
+        self.q8 = p.matrix(n, max(I, self.ms2 * H), C.OUT_INT8)              # every GEMM's int8 rows
+        self.qs = p.reserve(4 * n)                                           # and their row scales
+        self.x, self.h = p.matrix(n, H), p.matrix(n, H)                      # residual, normed
+        self.qkv = p.matrix(n, 3 * H)
+        self.qd, self.kd, self.qr = p.matrix(n, H), p.matrix(n, H), p.matrix(n, H)
+        self.att, self.b = p.matrix(n, H), p.matrix(n, H)
+        self.ml = p.matrix(n, I)
         nm = n // self.ms2
-        self.kbuf = p.const(np.zeros((npad, H), F32))        # K and V rows; the padding stays zero
-        self.vbuf = p.const(np.zeros((npad, H), F32))
-        self.sc = p.const(np.zeros((n, npad), F32))          # one head's scores
-        self.prow = p.const(np.zeros((n, npad), F32))        # its softmax
-        self.mask = p.const(np.concatenate([np.ones((1, n), F32), np.zeros((1, npad - n), F32)], axis=1))
-        self.mbias = p.const(np.concatenate([np.zeros((1, n), F32), np.full((1, npad - n), MASK_NEG, F32)], axis=1))
-        self.zrow = p.const(np.zeros((1, H), F32))           # the zero row a copy adds
-        # one INT8 activation buffer and one row-scale row, shared by every GEMM
-        self.q8 = p.mat(n, max(self.I, self.ms2 * H), C.OUT_INT8)
-        self.qs = p.alloc(4 * n)
-        self.x = p.mat(n, H)                                 # the residual stream
-        self.h = p.mat(n, H)
-        self.qkv = p.mat(n, 3 * H)
-        self.qd = p.mat(n, H)                                # q and k, dense (the rope's inputs)
-        self.kd = p.mat(n, H)
-        self.qr = p.mat(n, H)                                # q rotated and scaled
-        self.att = p.mat(n, H)
-        self.b = p.mat(n, H)                                 # a projection's output
-        self.ml = p.mat(n, self.I)
-        self.mm = p.mat(nm, self.m_fc1.n)
-        self.mt = p.mat(nm, self.ms2 * H)
-        self.out = p.mat(nm, self.cfg.out_hidden_size)
+        self.mm = p.matrix(nm, self.m_fc1.n)
+        self.mt = p.matrix(nm, self.ms2 * H)
+        self.out = p.matrix(nm, self.cfg.out_hidden_size)
 
-    def _ln(self, x: V, nb: tuple[V, V], y: V) -> None:
-        self.p.rowop(x, C.ROW_LAYERNORM, y, nb[0], self.eps, beta=nb[1])
+    def _int8(self, x: Buf) -> tuple[Buf, int]:
+        """ROW_QUANT of x into the shared int8 buffer."""
+        return self.p.quantize(x, Buf(self.q8.off, x.rows, x.cols, self.q8.ld, C.OUT_INT8), self.qs)
 
-    def _quant(self, x: V) -> tuple[V, int]:
-        return self.p.quant(x, V(self.q8.off, x.rows, x.cols, self.q8.ld, C.OUT_INT8), self.qs)
+    def _dense(self, x: Buf, w: Linear, y: Buf, act: int = C.ACT_NONE) -> None:
+        xq, srow = self._int8(x)
+        self.p.mm8(xq, srow, w, y, act)
 
-    def _linear(self, x: V, w: QLin, y: V, act: int = C.ACT_NONE) -> None:
-        xq, xs = self._quant(x)
-        self.p.gemm_rc(xq, xs, w, y, act)
-
-    def _emit_image(self, patches: np.ndarray, pos: np.ndarray, rope: np.ndarray) -> V:
-        p, n, H, hd, nh, npad = self.p, patches.shape[0], self.H, self.hd, self.nh, self.npad
-        assert patches.shape[1] == self.K and n <= self.P and n % self.ms2 == 0
-        assert pos.shape == (n, H) and rope.shape == (n, hd)
+    def _record(self, patches: np.ndarray, pos: np.ndarray, rope: np.ndarray) -> Buf:
+        p, H, hd, nh, npad = self.p, self.H, self.hd, self.nh, self.npad
+        n = patches.shape[0]
+        if patches.shape[1] != self.K or n > self.P or n % self.ms2 or pos.shape != (n, H) or rope.shape != (n, hd):
+            raise ValueError("patches / position rows / rotary rows do not fit the program")
         p.top = self.scratch0
-        # the mask rows follow this image's patch count
-        on, ng = np.zeros(npad, F32), np.zeros(npad, F32)
-        on[:n], ng[n:] = 1.0, MASK_NEG
-        for buf, row in ((self.mask, on), (self.mbias, ng)):
-            a = p.base + buf.off
-            p.ddr[a:a + 4 * npad] = row.tobytes()
-        x = self.x.rowv(0, n)
-        self._linear(p.const(np.asarray(patches, F32)), self.pe, x)      # patch embedding
-        p.elt(C.ELT_ADD, x, p.const(np.asarray(pos, F32)), x)            # + position embedding
-        ropet = p.const(np.asarray(rope, F32))
-        sc = V(self.sc.off, n, npad, self.sc.ld)
-        for b in self.blocks:
-            h = self.h.rowv(0, n)
-            self._ln(x, b["n1"], h)
-            qkv = self.qkv.rowv(0, n)
-            p.gemm_rc(*self._quant(h), b["qkv"], qkv)
-            # q, k, v into dense buffers (uniform row strides for the rope and the head views)
-            p.elt(C.ELT_ADD, qkv.colv(0, H), self.zrow, self.qd.rowv(0, n), bmode=C.BM_ROW)
-            p.elt(C.ELT_ADD, qkv.colv(H, H), self.zrow, self.kd.rowv(0, n), bmode=C.BM_ROW)
-            p.elt(C.ELT_ADD, qkv.colv(2 * H, H), self.zrow, self.vbuf.rowv(0, n), bmode=C.BM_ROW)
-            qr = self.qr.rowv(0, n)
-            p.rope(self.qd.rowv(0, n).heads(hd), ropet, nh, hd, qr.heads(hd))
+        keep = np.arange(npad) < n                                           # this image's mask rows
+        for buf, row in ((self.mask, keep.astype(F32)), (self.mbias, np.where(keep, F32(0), MASK_NEG).astype(F32))):
+            at = p.base + buf.off
+            p.ddr[at:at + 4 * npad] = row.tobytes()
+        x = self.x.rows_at(0, n)
+        self._dense(p.constant(np.asarray(patches, F32)), self.pe, x)        # the patch embedding
+        p.elt(C.ELT_ADD, x, p.constant(np.asarray(pos, F32)), x)             # + the position rows
+        rot = p.constant(np.asarray(rope, F32))
+        scores, probs = self.sc._replace(rows=n), self.prow._replace(rows=n)
+        h, qkv, qd, kd, qr = (b.rows_at(0, n) for b in (self.h, self.qkv, self.qd, self.kd, self.qr))
+        att, proj, ml = self.att.rows_at(0, n), self.b.rows_at(0, n), self.ml.rows_at(0, n)
+        keys, vals = self.kbuf.rows_at(0, n), self.vbuf.rows_at(0, n)
+        for blk in self.blocks:
+            p.row_op(C.ROW_LAYERNORM, x, h, blk["n1"][0], self.eps, beta=blk["n1"][1])
+            p.mm8(*self._int8(h), blk["qkv"], qkv)
+            # q, k, v copied into dense matrices (one row stride for the rope and the head views)
+            for c0, dst in ((0, qd), (H, kd), (2 * H, vals)):
+                p.elt(C.ELT_ADD, qkv.cols_at(c0, H), self.zrow, dst, bmode=C.BM_ROW)
+            p.rotary(qd.as_heads(hd), rot, nh, hd, qr.as_heads(hd))
             p.elt(C.ELT_MUL, qr, self.sc_q, qr, bmode=C.BM_SCALAR)
-            p.rope(self.kd.rowv(0, n).heads(hd), ropet, nh, hd, self.kbuf.rowv(0, n).heads(hd))
-            att = self.att.rowv(0, n)
-            for hh in range(nh):
-                p.fdot(V(qr.off + hh * hd * 4, n, hd, 4 * H), V(self.kbuf.off + hh * hd * 4, npad, hd, 4 * H),
-                       sc, nn=False)
-                p.elt(C.ELT_MUL, sc, self.mask, sc, bmode=C.BM_ROW)     # padded columns -> +0
-                p.elt(C.ELT_ADD, sc, self.mbias, sc, bmode=C.BM_ROW)    # -> MASK_NEG
-                p.rowop(sc, C.ROW_SOFTMAX, V(self.prow.off, n, npad, self.prow.ld))
-                p.fdot(V(self.prow.off, n, npad, self.prow.ld), V(self.vbuf.off + hh * hd * 4, npad, hd, 4 * H),
-                       V(att.off + hh * hd * 4, n, hd, att.ld), nn=True)
-            self._linear(att, b["proj"], self.b.rowv(0, n))
-            p.elt(C.ELT_ADD, x, self.b.rowv(0, n), x)
-            self._ln(x, b["n2"], h)
-            ml = self.ml.rowv(0, n)
-            p.gemm_rc(*self._quant(h), b["fc1"], ml, C.ACT_GELU)
-            self._linear(ml, b["fc2"], self.b.rowv(0, n))
-            p.elt(C.ELT_ADD, x, self.b.rowv(0, n), x)
+            p.rotary(kd.as_heads(hd), rot, nh, hd, keys.as_heads(hd))
+            for head in range(nh):
+                p.fdot(qr.column_of(head, hd), self.kbuf.column_of(head, hd), scores, nn=False)
+                p.elt(C.ELT_MUL, scores, self.mask, scores, bmode=C.BM_ROW)      # padded columns: +0
+                p.elt(C.ELT_ADD, scores, self.mbias, scores, bmode=C.BM_ROW)     # then MASK_NEG
+                p.row_op(C.ROW_SOFTMAX, scores, probs)
+                p.fdot(probs, self.vbuf.column_of(head, hd), att.column_of(head, hd), nn=True)
+            self._dense(att, blk["proj"], proj)
+            p.elt(C.ELT_ADD, x, proj, x)
+            p.row_op(C.ROW_LAYERNORM, x, h, blk["n2"][0], self.eps, beta=blk["n2"][1])
+            p.mm8(*self._int8(h), blk["fc1"], ml, C.ACT_GELU)
+            self._dense(ml, blk["fc2"], proj)
+            p.elt(C.ELT_ADD, x, proj, x)
         nm = n // self.ms2
-        # the merger's norm per patch row, written so that the merge block's rows are one row
-        self._ln(x, self.m_norm, V(self.mt.off, n, H, 4 * H))
-        mt = self.mt.rowv(0, nm)
-        p.gemm_rc(*self._quant(mt), self.m_fc1, self.mm.rowv(0, nm), C.ACT_GELU)
-        out = self.out.rowv(0, nm)
-        self._linear(self.mm.rowv(0, nm), self.m_fc2, out)
-        assert p.top <= self.scratch_end, "scratch_bytes too small for one image"
+        # the merger's norm per patch row, laid out so that a merge block's rows are one row
+        p.row_op(C.ROW_LAYERNORM, x, Buf(self.mt.off, n, H, 4 * H), self.m_norm[0], self.eps, beta=self.m_norm[1])
+        p.mm8(*self._int8(self.mt.rows_at(0, nm)), self.m_fc1, self.mm.rows_at(0, nm), C.ACT_GELU)
+        out = self.out.rows_at(0, nm)
+        self._dense(self.mm.rows_at(0, nm), self.m_fc2, out)
+        if p.top > self.scratch_end:
+            raise MemoryError("scratch_bytes too small for one image")
         p.top = self.end
         return out
 
-    def emit(self, patches: np.ndarray, pos: np.ndarray, rope: np.ndarray, blocks: int | None = None) -> V:
-        """The image's descriptors (a previous image's queue is dropped); returns the output view
-        (the merged tokens, or with `blocks` the patches' hidden state after that many blocks)."""
-        n = patches.shape[0]
-        keep = self.blocks
+    def emit(self, patches: np.ndarray, pos: np.ndarray, rope: np.ndarray, blocks: int | None = None) -> Buf:
+        """The image's descriptors (replacing any earlier image's); returns the output matrix: the
+        merged tokens, or with `blocks` the patches' hidden state after that many blocks."""
+        every = self.blocks
         if blocks is not None:
-            self.blocks = keep[:blocks]
+            self.blocks = every[:blocks]
         try:
             self.p.descs.clear()
             self.p.queue_off = None
-            out = self._emit_image(patches, pos, rope)
-            return out if blocks is None else self.x.rowv(0, n)
+            out = self._record(patches, pos, rope)
+            return out if blocks is None else self.x.rows_at(0, patches.shape[0])
         finally:
-            self.blocks = keep
+            self.blocks = every
 
     def run(self, patches: np.ndarray, pos: np.ndarray, rope: np.ndarray, blocks: int | None = None,
             machine=None) -> np.ndarray:
-        """Lower the image, build the program and run it on `machine` (a Machine class; default
-        the B200 drop-in Machine): the visual tokens [P / merge^2, out_hidden]."""
+        """Record the image, build the program and run it on `machine` (a Machine class; default the
+        drop-in Machine): the visual tokens [P / merge^2, out_hidden]."""
         if machine is None:
             from .machine import Machine as machine
         out = self.emit(patches, pos, rope, blocks)
-        ddr, q, cnt = self.p.build()
+        ddr, q, cnt = self.p.finish()
         m = machine(bytearray(ddr))
         st = m.run_queue(q, cnt)
-        assert st.done, (st.err_code, st.op_idx)
+        if not st.done:
+            raise RuntimeError(f"the tower's queue stopped: {st.err_code} at {st.op_idx}")
         return self.read(m, out)
 
-    def read(self, m, v: V) -> np.ndarray:
-        a = self.p.base + v.off
-        return np.stack([np.frombuffer(m.read(a + r * v.ld, 4 * v.cols), "<f4") for r in range(v.rows)])
+    def read(self, m, v: Buf) -> np.ndarray:
+        at = self.p.base + v.off
+        return np.stack([np.frombuffer(m.read(at + r * v.ld, 4 * v.cols), "<f4") for r in range(v.rows)])

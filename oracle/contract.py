@@ -9,7 +9,6 @@ bytes 4..7 zeroed.
 """
 from __future__ import annotations
 
-import struct
 import zlib
 
 import numpy as np
@@ -46,64 +45,87 @@ K_MAX = 65535
 CANON_NAN = 0x7FC00000
 
 
+# sub-fields of CTRL and EPI: name -> (first bit, width) (contract.py:131-143); the 3-bit
+# activation code is split, its bit 2 stored at EPI bit 5
+CTRL_BITS = {"qmode": (0, 3), "symmetric": (3, 1), "a_dtype": (4, 4), "w_dtype": (8, 4), "fusion": (12, 1)}
+EPI_BITS = {"act_lo": (0, 2), "out": (2, 2), "bias": (4, 1), "act_hi": (5, 1)}
+# the CONV geometry word in HDR_RSV (contract.py:72-85)
+CONV_BITS = {"pad": (0, 2), "stride_m1": (2, 2), "kw": (4, 4), "kh": (8, 4), "h": (12, 12)}
+
+
+def _put(table: dict, **vals) -> int:
+    return sum((v & ((1 << table[k][1]) - 1)) << table[k][0] for k, v in vals.items())
+
+
+def _get(table: dict, word: int, key: str) -> int:
+    at, w = table[key]
+    return (word >> at) % (1 << w)
+
+
 def ctrl(qmode=QM_TENSOR, symmetric=1, a_dtype=DT_INT8, w_dtype=DT_INT8, fusion=0) -> int:
     """contract.py:131-134."""
-    return (qmode & 7) | (symmetric & 1) << 3 | (a_dtype & 15) << 4 | (w_dtype & 15) << 8 | (fusion & 1) << 12
+    return _put(CTRL_BITS, qmode=qmode, symmetric=symmetric, a_dtype=a_dtype, w_dtype=w_dtype, fusion=fusion)
 
 
 def epi(act=ACT_NONE, out=OUT_FP32, bias=0) -> int:
-    """contract.py:137-138 - the 3-bit activation code is EPI[1:0] | EPI[5] << 2."""
-    return (act & 3) | (out & 3) << 2 | (bias & 1) << 4 | (act >> 2 & 1) << 5
+    """contract.py:137-138."""
+    return _put(EPI_BITS, act_lo=act, out=out, bias=bias, act_hi=act >> 2)
 
 
 def act_of(e: int) -> int:
     """contract.py:141-143."""
-    return (e & 3) | (e >> 5 & 1) << 2
+    return _get(EPI_BITS, e, "act_lo") + 4 * _get(EPI_BITS, e, "act_hi")
 
 
 def f32_bits(x: float) -> int:
-    return struct.unpack("<I", struct.pack("<f", x))[0]
+    return int(np.float32(x).view(np.uint32))
 
 
 def bits_f32(b: int) -> np.float32:
-    return np.frombuffer(struct.pack("<I", b & 0xFFFFFFFF), "<f4")[0]
+    return np.uint32(b & 0xFFFFFFFF).view(np.float32)
 
 
 def crc32_desc(raw: bytes) -> int:
-    z = bytearray(raw)
-    z[4:8] = b"\0\0\0\0"
-    return zlib.crc32(bytes(z)) & 0xFFFFFFFF
+    """CRC-32/ISO-HDLC of the descriptor with bytes 4..7 taken as zero."""
+    return zlib.crc32(b"".join((bytes(raw[:4]), b"\0" * 4, bytes(raw[8:DESC_BYTES]))))
+
+
+def _bit_array(raw: bytes) -> np.ndarray:
+    """The 512 bits, bit i = bit i % 8 of byte i // 8."""
+    return np.unpackbits(np.frombuffer(bytes(raw), np.uint8), bitorder="little")
 
 
 def encode(fields: dict, *, fix_crc: bool = True) -> bytes:
-    """contract.py:154-170."""
-    v = 0
+    """contract.py:154-170, built bit by bit."""
+    bits = np.zeros(8 * DESC_BYTES, np.uint8)
     for name, val in fields.items():
         hi, lo = FIELDS[name]
-        if not 0 <= val < (1 << (hi - lo + 1)):
-            raise ValueError(f"{name}={val} does not fit {hi - lo + 1} bits")
-        v |= val << lo
-    raw = bytearray(v.to_bytes(DESC_BYTES, "little"))
+        n = hi - lo + 1
+        val = int(val)
+        if val < 0 or val.bit_length() > n:
+            raise ValueError(f"{name}={val} does not fit {n} bits")
+        bits[lo:hi + 1] = [(val >> i) & 1 for i in range(n)]
+    raw = bytearray(np.packbits(bits, bitorder="little").tobytes())
     if fix_crc:
-        raw[4:8] = struct.pack("<I", crc32_desc(bytes(raw)))
+        raw[4:8] = crc32_desc(raw).to_bytes(4, "little")
     return bytes(raw)
 
 
 def decode(raw: bytes) -> dict:
-    """contract.py:173-175."""
-    v = int.from_bytes(raw, "little")
-    return {n: (v >> lo) & ((1 << (hi - lo + 1)) - 1) for n, (hi, lo) in FIELDS.items()}
+    """contract.py:173-175, read bit by bit."""
+    bits = _bit_array(raw)
+    weights = [1 << i for i in range(64)]
+    return {name: sum(w for w, b in zip(weights, bits[lo:hi + 1]) if b) for name, (hi, lo) in FIELDS.items()}
 
 
 def crc_ok(raw: bytes) -> bool:
     """contract.py:178-181."""
-    return struct.unpack("<I", bytes(raw[4:8]))[0] == crc32_desc(raw)
+    return int.from_bytes(bytes(raw[4:8]), "little") == crc32_desc(raw)
 
 
 def conv_params(d: dict) -> dict:
     """contract.py:79-85 - conv geometry from HDR_RSV / GROUP_SIZE."""
-    g = d["HDR_RSV"]
-    h, kh, kw, s, p, w = g >> 12, g >> 8 & 15, g >> 4 & 15, (g >> 2 & 3) + 1, g & 3, d["GROUP_SIZE"]
-    cin = d["K"] // (kh * kw) if kh and kw else 0
-    return dict(H=h, W=w, KH=kh, KW=kw, S=s, P=p, Cin=cin,
-                OH=(h + 2 * p - kh) // s + 1, OW=(w + 2 * p - kw) // s + 1)
+    g = {k: _get(CONV_BITS, d["HDR_RSV"], k) for k in CONV_BITS}
+    h, w, kh, kw, p, s = g["h"], d["GROUP_SIZE"], g["kh"], g["kw"], g["pad"], g["stride_m1"] + 1
+    return dict(H=h, W=w, KH=kh, KW=kw, S=s, P=p, Cin=d["K"] // (kh * kw) if kh * kw else 0,
+                OH=(h - kh + 2 * p) // s + 1, OW=(w - kw + 2 * p) // s + 1)

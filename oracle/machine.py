@@ -23,6 +23,7 @@ class ContractError(Exception):
 
 @dataclass
 class Status:
+    """golden.py:21-26 - whether the queue finished, the error code, the index it stopped at."""
     done: bool = False
     err_code: int = C.E_OK
     op_idx: int = 0
@@ -73,12 +74,12 @@ def check(d: dict, raw: bytes, core_id: int, gemv_only: bool) -> int:
         return C.E_FIELD
     gemm = op == C.OP_GEMM or conv
     if gemm:
-        if w4:
-            if sym != 1 or adt not in (C.DT_FP32, C.DT_BF16) or d["HDR_RSV"] != 0 \
-                    or d["GROUP_SIZE"] != C.W4_GROUP:
-                return C.E_FIELD
-        elif qm not in (C.QM_TENSOR, C.QM_CHANNEL, C.QM_ROWCOL) or sym != 1 \
-                or adt != C.DT_INT8 or wdt != C.DT_INT8 or (conv and qm == C.QM_ROWCOL):
+        # W4A16: symmetric, fp32 or bf16 activations, groups of 128, no row-scale word; else
+        # symmetric int8 x int8 in the tensor / channel / row-col modes (row-col not for CONV)
+        w4_bad = (sym, d["HDR_RSV"], d["GROUP_SIZE"]) != (1, 0, C.W4_GROUP) or adt not in (C.DT_FP32, C.DT_BF16)
+        i8_bad = (sym, adt, wdt) != (1, C.DT_INT8, C.DT_INT8) or qm not in (C.QM_TENSOR, C.QM_CHANNEL, C.QM_ROWCOL) \
+            or (conv and qm == C.QM_ROWCOL)
+        if (w4 and w4_bad) or (not w4 and i8_bad):
             return C.E_FIELD
         if (act != C.ACT_NONE) != (fus == 1):
             return C.E_FIELD
@@ -140,12 +141,16 @@ def check(d: dict, raw: bytes, core_id: int, gemv_only: bool) -> int:
 
 
 def bstride(d: dict) -> tuple[int, int]:
-    """golden.py:171-178."""
-    if d["OPCODE"] == C.OP_FDOT:
-        brow = (2 if d["HDR_RSV"] & C.STATE_FP16 else 4) * (d["N"] if d["CTRL"] & 1 else d["K"])
+    """golden.py:171-178 - (row stride, row bytes) of B: an FDOT's [K][N] (NN, fp32 or fp16) or
+    [N][K] (NT) matrix, an ELT's dense b rows (0 bytes when b is broadcast); GROUP_SIZE, when set,
+    is the stride in 16-byte units."""
+    fdot = d["OPCODE"] == C.OP_FDOT
+    if fdot:
+        width = d["N"] if d["CTRL"] & 1 else d["K"]
+        nbytes = width * (2 if d["HDR_RSV"] & C.STATE_FP16 else 4)
     else:
-        brow = 4 * d["N"] if (d["HDR_RSV"] & 3) == C.BM_DENSE else 0
-    return (16 * d["GROUP_SIZE"] if d["GROUP_SIZE"] else brow), brow
+        nbytes = 4 * d["N"] * int(d["HDR_RSV"] & 3 == C.BM_DENSE)
+    return (d["GROUP_SIZE"] * 16 or nbytes), nbytes
 
 
 def strides(d: dict) -> tuple[int, int, int, int]:
@@ -198,36 +203,39 @@ def segments(d: dict):
             nb = K if d["CTRL"] & 1 else N
             reads.append([(w0 + i * ldb, w0 + i * ldb + brow) for i in range(nb)])
         return reads, y
+    def span(off, nbytes):                      # one contiguous read at base + off
+        return [(B + off, B + off + nbytes)]
+
     if op in C.CONV_OPS:
-        npx = C.conv_params(d)["H"] * C.conv_params(d)["W"]
-        a0 = B + d["A_OFF"]
-        reads = [[(a0, a0 + npx * arow)] if lda == arow else
-                 [(a0 + p * lda, a0 + p * lda + arow) for p in range(npx)]]
+        g = C.conv_params(d)
+        pixels = g["H"] * g["W"]                # the input image, one row of Cin per pixel
+        reads = [span(d["A_OFF"], pixels * arow) if lda == arow else rows(d["A_OFF"], lda, arow, pixels)]
     else:
         reads = [rows(d["A_OFF"], lda, arow)]
-    if op in (C.OP_GEMM,) + C.CONV_OPS:
-        w4 = is_w4(d)
-        ns = 1 if d["CTRL"] & 7 == C.QM_TENSOR else N
-        reads.append([(B + d["W_OFF"], B + d["W_OFF"] + N * K // (2 if w4 else 1))])
-        reads.append([(B + d["SCALE_OFF"], B + d["SCALE_OFF"] + (2 * N * (K // C.W4_GROUP) if w4 else 4 * ns))])
-        if d["EPI"] >> 4 & 1:
-            reads.append([(B + d["BIAS_OFF"], B + d["BIAS_OFF"] + 4 * N)])
-        if d["CTRL"] & 7 == C.QM_ROWCOL and not w4:
-            r0 = B + 16 * d["HDR_RSV"]
-            reads.append([(r0, r0 + 4 * M)])
+    has_bias = bool(d["EPI"] >> 4 & 1)
+    if op == C.OP_GEMM or op in C.CONV_OPS:
+        qm, w4 = d["CTRL"] & 7, is_w4(d)
+        if w4:
+            wbytes, sbytes = N * K // 2, 2 * N * (K // C.W4_GROUP)      # nibbles, binary16 per group
+        else:
+            wbytes, sbytes = N * K, 4 * (1 if qm == C.QM_TENSOR else N)
+        reads += [span(d["W_OFF"], wbytes), span(d["SCALE_OFF"], sbytes)]
+        if has_bias:
+            reads.append(span(d["BIAS_OFF"], 4 * N))
+        if qm == C.QM_ROWCOL and not w4:
+            reads.append(span(16 * d["HDR_RSV"], 4 * M))                 # the activation row scales
     elif op == C.OP_ROW and d["CTRL"] & 7 in (C.ROW_LAYERNORM, C.ROW_RMSNORM, C.ROW_L2NORM):
-        reads.append([(B + d["SCALE_OFF"], B + d["SCALE_OFF"] + 4 * N)])
-        if d["EPI"] >> 4 & 1:
-            reads.append([(B + d["BIAS_OFF"], B + d["BIAS_OFF"] + 4 * N)])
+        reads.append(span(d["SCALE_OFF"], 4 * N))
+        if has_bias:
+            reads.append(span(d["BIAS_OFF"], 4 * N))
     return reads, y
 
 
 def extra_out(d: dict):
     """golden.py:250-256 - ROW_QUANT's row scales: 4 M bytes at SCALE_OFF."""
-    if d["OPCODE"] == C.OP_ROW and d["CTRL"] & 7 == C.ROW_QUANT:
-        a = d["BASE_ADDR"] + d["SCALE_OFF"]
-        return [(a, a + 4 * d["M"])]
-    return []
+    quant = d["OPCODE"] == C.OP_ROW and d["CTRL"] & 7 == C.ROW_QUANT
+    lo = d["BASE_ADDR"] + d["SCALE_OFF"]
+    return [(lo, lo + 4 * d["M"])] if quant else []
 
 
 def overlaps(segs, y) -> bool:
@@ -245,11 +253,25 @@ def in_place(d: dict, i: int) -> bool:
     out = d["EPI"] >> 2 & 3
     if d["OPCODE"] != C.OP_ELT or out not in (C.OUT_FP32, C.OUT_FP16):
         return False
+    if i == 2:
+        return d["BIAS_OFF"] == d["Y_OFF"]
+    if i != 0:
+        return False
     lda, ldy = strides(d)[:2]
-    if i == 0:
-        afmt = C.OUT_FP16 if d["HDR_RSV"] & C.STATE_FP16 else C.OUT_FP32
-        return afmt == out and not (d["HDR_RSV"] >> 2 & 1) and d["A_OFF"] == d["Y_OFF"] and lda == ldy
-    return i == 2 and d["BIAS_OFF"] == d["Y_OFF"]
+    a_fp16 = bool(d["HDR_RSV"] & C.STATE_FP16)
+    same_format = out == (C.OUT_FP16 if a_fp16 else C.OUT_FP32)
+    one_row = bool(d["HDR_RSV"] >> 2 & 1)
+    return same_format and not one_row and (d["A_OFF"], lda) == (d["Y_OFF"], ldy)
+
+
+def _check_overlaps(i: int, d: dict, reads, y, extra) -> None:
+    """An output may overlap no input (except an ELT's in-place A or C), the row scales of
+    ROW_QUANT no input and not the output rows."""
+    for j, seg in enumerate(reads):
+        if (overlaps(seg, y) and not in_place(d, j)) or (extra and overlaps(seg, extra)):
+            raise ContractError(f"descriptor {i}: output overlaps an input")
+    if extra and overlaps(extra, y):
+        raise ContractError(f"descriptor {i}: the two outputs overlap")
 
 
 class OracleMachine:
@@ -263,10 +285,12 @@ class OracleMachine:
         self.stats: list[OpStat] = []
 
     def read(self, addr: int, n: int) -> bytes:
-        return bytes(self.ddr[addr:addr + n])
+        view = memoryview(self.ddr)
+        return view[addr:addr + n].tobytes()
 
     def write(self, addr: int, data: bytes) -> None:
-        self.ddr[addr:addr + len(data)] = data
+        n = len(data)
+        self.ddr[addr:addr + n] = data
 
     def validate(self, raw: bytes):
         d = C.decode(raw)
@@ -406,16 +430,14 @@ class OracleMachine:
             b = np.broadcast_to(v[None, :] if bm == C.BM_ROW else v[:, None] if bm == C.BM_COL else v[None, :1],
                                 (M, N))
         a = F.act_fn(a, C.act_of(e))
-        eop = d["CTRL"] & 3
-        if eop == C.ELT_MUL:
-            y = F.fmul(a, b)
-        elif eop == C.ELT_ADD:
-            y = F.fadd(a, b)
-        elif eop == C.ELT_SUB:
-            y = F.fadd(a, F.neg(F.ftz(b)))
-        else:
+        fn = d["CTRL"] & 3
+        if fn == C.ELT_MULADD:                  # c (at BIAS_OFF, the output's layout) + a b
             c = self._float_rows(B + d["BIAS_OFF"], ldy, M, N, e >> 2 & 3 == C.OUT_FP16)
             y = F.fadd(c, F.fmul(a, b))
+        else:
+            binop = {C.ELT_MUL: F.fmul, C.ELT_ADD: F.fadd,
+                     C.ELT_SUB: lambda p, q: F.fadd(p, F.neg(F.ftz(q)))}[fn]
+            y = binop(a, b)
         return self.convert(y, e >> 2 & 3, d["OUT_SCALE"])
 
     def _rope(self, d):
@@ -444,35 +466,31 @@ class OracleMachine:
         table = {C.OP_GEMM: self._gemm, C.OP_RELU: self._relu, C.OP_ROW: self._row,
                  C.OP_CONV: self._conv, C.OP_CONV_ACT: self._conv, C.OP_ELT: self._elt,
                  C.OP_ROPE: self._rope, C.OP_FDOT: self._fdot}
+        end = len(self.ddr)
         for i in range(queue_len):
-            qa = queue_addr + C.DESC_BYTES * i
-            if qa + C.DESC_BYTES > len(self.ddr):
-                self.status = Status(False, C.E_RANGE, i)
-                return self.status
-            raw = self.read(qa, C.DESC_BYTES)
-            err, d = self.validate(raw)
-            if err == C.E_OK:
-                reads, y = segments(d)
-                extra = extra_out(d)
-                if any(hi > len(self.ddr) for seg in reads + [y, extra] for _, hi in seg):
-                    err = C.E_RANGE
+            at = queue_addr + C.DESC_BYTES * i
+            if at + C.DESC_BYTES > end:
+                return self._stop(C.E_RANGE, i)
+            err, d = self.validate(self.read(at, C.DESC_BYTES))
             if err != C.E_OK:
-                self.status = Status(False, err, i)
-                return self.status
-            for j, seg in enumerate(reads):
-                if overlaps(seg, y) and not in_place(d, j):
-                    raise ContractError(f"descriptor {i}: output overlaps an input")
-                if extra and overlaps(seg, extra):
-                    raise ContractError(f"descriptor {i}: output overlaps an input")
-            if extra and overlaps(extra, y):
-                raise ContractError(f"descriptor {i}: the two outputs overlap")
+                return self._stop(err, i)
+            reads, y = segments(d)
+            extra = extra_out(d)
+            if max((hi for seg in (*reads, y, extra) for _, hi in seg), default=0) > end:
+                return self._stop(C.E_RANGE, i)
+            _check_overlaps(i, d, reads, y, extra)
             self._extra = None
-            rows = table[d["OPCODE"]](d)
-            for m in range(rows.shape[0]):
-                self.write(y[m][0], rows[m].tobytes())
+            out = table[d["OPCODE"]](d)
+            for m, row in enumerate(out):
+                self.write(y[m][0], row.tobytes())
             if self._extra:
                 self.write(*self._extra)
-            macs = d["M"] * d["N"] * d["K"] if d["OPCODE"] in (C.OP_GEMM, C.OP_FDOT) + C.CONV_OPS else 0
-            self.stats.append(OpStat(d["OPCODE"], macs, sum(hi - lo for seg in reads for lo, hi in seg), rows.size))
+            contraction = d["OPCODE"] == C.OP_GEMM or d["OPCODE"] == C.OP_FDOT or d["OPCODE"] in C.CONV_OPS
+            read_bytes = sum(hi - lo for seg in reads for lo, hi in seg)
+            self.stats.append(OpStat(d["OPCODE"], d["M"] * d["N"] * d["K"] * contraction, read_bytes, out.size))
         self.status = Status(True, C.E_OK, queue_len)
+        return self.status
+
+    def _stop(self, err: int, i: int) -> Status:
+        self.status = Status(False, err, i)
         return self.status

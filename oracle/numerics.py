@@ -83,9 +83,10 @@ def fabs(x) -> np.ndarray:
 
 def to_fp16_bits(x) -> np.ndarray:
     """numerics.py:14-18 - IEEE binary16, RNE, gradual underflow; NaN -> 0x7E00."""
+    x = np.asarray(x, F32)
     with np.errstate(over="ignore", invalid="ignore"):
-        h = np.asarray(x, F32).astype("<f2")
-    return np.where(np.isnan(h), np.uint16(0x7E00), h.view(np.uint16)).astype(np.uint16)
+        h = x.astype(np.float16).view(np.uint16)
+    return np.where(np.isnan(x), 0x7E00, h).astype(np.uint16)
 
 
 def from_fp16_bits(h) -> np.ndarray:
@@ -108,9 +109,8 @@ def bf16_bits_to_f32(h) -> np.ndarray:
 
 def q8(x, inv) -> np.ndarray:
     """numerics.py:282-286 - rint(fmul(x, inv)) ties-even, NaN -> 0, saturate to +-127."""
-    y = fmul(x, inv)
-    y = np.where(np.isnan(y), F32(0), y)
-    return np.clip(np.rint(y), -127, 127).astype(np.int8)
+    r = np.rint(fmul(x, inv))
+    return np.where(np.isnan(r), F32(0), np.clip(r, F32(-127), F32(127))).astype(np.int8)
 
 
 # ---------------------------------------------------------------- contract constants
@@ -137,19 +137,25 @@ def add_to_exponent(y, e) -> np.ndarray:
     return from_bits(out)
 
 
+def _horner(coeffs, z) -> np.ndarray:
+    """c0 z^k + ... + ck with one fmul and one fadd per step, highest power first."""
+    acc = np.full_like(z, coeffs[0])
+    for c in coeffs[1:]:
+        acc = fadd(fmul(acc, z), c)
+    return acc
+
+
 def exp_f(x) -> np.ndarray:
-    """numerics.py:135-150."""
+    """numerics.py:135-150 - n = rint(x log2 e) clamped to +-200, r = x - n ln2 (two-part ln2),
+    the degree-6 polynomial of r, n added to its exponent; +inf from 89 up, +0 from -104 down."""
     x = ftz(x)
     with np.errstate(invalid="ignore"):
         n = np.clip(np.rint(fmul(x, LOG2E)), -200, 200).astype(F32)
+        over, under = x >= EXP_HI, x <= EXP_LO
     r = fadd(fadd(x, fmul(n, NEG_LN2_HI)), fmul(n, NEG_LN2_LO))
-    p = np.full_like(r, EXP_POLY[0])
-    for c in EXP_POLY[1:]:
-        p = fadd(fmul(p, r), c)
-    y = add_to_exponent(p, np.nan_to_num(n, nan=0).astype(np.int64))
-    with np.errstate(invalid="ignore"):
-        y = np.where(x >= EXP_HI, F32(np.inf), np.where(x <= EXP_LO, F32(0), y))
-    return canon(np.where(np.isnan(x), F32(np.nan), y).astype(F32))
+    y = add_to_exponent(_horner(EXP_POLY, r), np.nan_to_num(n, nan=0).astype(np.int64))
+    y = np.select([np.isnan(x), over, under], [F32(np.nan), F32(np.inf), F32(0)], y)
+    return canon(y.astype(F32))
 
 
 def recip_f(x) -> np.ndarray:
@@ -181,12 +187,12 @@ def rsqrt_f(x) -> np.ndarray:
     y = from_bits(np.int64(RSQRT_MAGIC) - (mb >> 1))
     for _ in range(3):
         y = fadd(y, fmul(y, fadd(HALF, neg(fmul(HALF, fmul(fmul(m, y), y))))))
-    y = add_to_exponent(y, -k)
-    y = np.where((b & 0x7FFFFFFF) == 0, from_bits((b & 0x80000000) | 0x7F800000), y)
-    y = np.where(b == 0x7F800000, F32(0), y)
     with np.errstate(invalid="ignore"):
-        bad = np.isnan(x) | (x < F32(0))
-    return canon(np.where(bad, F32(np.nan), y).astype(F32))
+        nan_out = np.isnan(x) | (x < F32(0))
+    signed_inf = from_bits((b & 0x80000000) | 0x7F800000)
+    y = np.select([nan_out, b == 0x7F800000, (b & 0x7FFFFFFF) == 0], [F32(np.nan), F32(0), signed_inf],
+                  add_to_exponent(y, -k))
+    return canon(y.astype(F32))
 
 
 def gelu_f(x) -> np.ndarray:
@@ -215,14 +221,11 @@ def softplus_f(x) -> np.ndarray:
     x = ftz(x)
     t = exp_f(neg(fabs(x)))
     s = fmul(t, recip_f(fadd(t, TWO)))
-    z = fmul(s, s)
-    p = np.full_like(z, LOG1P_POLY[0])
-    for c in LOG1P_POLY[1:]:
-        p = fadd(fmul(p, z), c)
+    p = _horner(LOG1P_POLY, fmul(s, s))
     y = fadd(np.where(x > F32(0), x, F32(0)).astype(F32), fmul(fmul(TWO, s), p))
     with np.errstate(invalid="ignore"):
-        y = np.where(x > SP_HI, x, y)
-    return canon(np.where(np.isnan(x), F32(np.nan), y).astype(F32))
+        big = x > SP_HI
+    return canon(np.select([np.isnan(x), big], [F32(np.nan), x], y).astype(F32))
 
 
 def act_fn(x, act: int) -> np.ndarray:
@@ -260,8 +263,9 @@ def sum16(v) -> np.ndarray:
     blocks = v.reshape(M, N // 16, 16)
     for c in range(N // 16):
         lanes = fadd(lanes, blocks[:, c, :])
-    while lanes.shape[1] > 1:
-        lanes = fadd(lanes[:, 0::2], lanes[:, 1::2])
+    for half in (8, 4, 2, 1):                   # lane 2i + lane 2i+1 into lane i
+        pairs = lanes.reshape(M, half, 2)
+        lanes = fadd(pairs[:, :, 0], pairs[:, :, 1])
     return lanes[:, 0]
 
 
@@ -300,31 +304,33 @@ def softmax_rows_causal(x, valid) -> np.ndarray:
     return fmul(e, recip_f(sum16(e))[:, None])
 
 
+def _normalise(v, sq_sum, eps, gamma, beta) -> np.ndarray:
+    """The tail the three norms share: v * rsqrt(sq_sum + eps) * gamma [+ beta], per row."""
+    rs = rsqrt_f(fadd(sq_sum, eps))
+    out = fmul(fmul(v, rs[:, None]), gamma[None, :])
+    if beta is not None:
+        out = fadd(out, beta[None, :])
+    return out
+
+
 def layernorm_rows(x, gamma, beta, eps) -> np.ndarray:
-    """numerics.py:341-350."""
+    """numerics.py:341-350 - mean = sum16(x) / N, d = x - mean, variance = sum16(d d) / N."""
     x = ftz(x)
     k = inv_n(x.shape[1])
-    mean = fmul(sum16(x), k)[:, None]
-    d = fadd(x, neg(mean))
-    rs = rsqrt_f(fadd(fmul(sum16(fmul(d, d)), k), eps))[:, None]
-    y = fmul(fmul(d, rs), gamma[None, :])
-    return y if beta is None else fadd(y, beta[None, :])
+    d = fadd(x, neg(fmul(sum16(x), k)[:, None]))
+    return _normalise(d, fmul(sum16(fmul(d, d)), k), eps, gamma, beta)
 
 
 def rmsnorm_rows(x, gamma, beta, eps) -> np.ndarray:
-    """numerics.py:353-358."""
+    """numerics.py:353-358 - mean square sum16(x x) / N."""
     x = ftz(x)
-    rs = rsqrt_f(fadd(fmul(sum16(fmul(x, x)), inv_n(x.shape[1])), eps))[:, None]
-    y = fmul(fmul(x, rs), gamma[None, :])
-    return y if beta is None else fadd(y, beta[None, :])
+    return _normalise(x, fmul(sum16(fmul(x, x)), inv_n(x.shape[1])), eps, gamma, beta)
 
 
 def l2norm_rows(x, gamma, beta, eps) -> np.ndarray:
     """numerics.py:374-380 - RMSNorm without the 1/N."""
     x = ftz(x)
-    rs = rsqrt_f(fadd(sum16(fmul(x, x)), eps))[:, None]
-    y = fmul(fmul(x, rs), gamma[None, :])
-    return y if beta is None else fadd(y, beta[None, :])
+    return _normalise(x, sum16(fmul(x, x)), eps, gamma, beta)
 
 
 def quant_rows(x) -> tuple[np.ndarray, np.ndarray]:
@@ -332,8 +338,8 @@ def quant_rows(x) -> tuple[np.ndarray, np.ndarray]:
     s = amax * fp32(1/127)."""
     x = ftz(x)
     amax = max16(fabs(x))
-    inv = fmul(Q127, recip_f(amax))
-    return q8(x, inv[:, None]), fmul(amax, INV127)
+    row_scale = fmul(amax, INV127)
+    return q8(x, fmul(Q127, recip_f(amax))[:, None]), row_scale
 
 
 def fdot_nt(a, b) -> np.ndarray:

@@ -27,7 +27,7 @@ ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
 
 from tests import fixtures as FX  # noqa: E402
-from tests.model_runs import build_export_lowering  # noqa: E402
+from tests.model_runs import build_export_image  # noqa: E402
 
 N_NEW = 4
 
@@ -59,7 +59,7 @@ def main():
     from opentars_b200.export import write_export
     out = {}
     for name, fx in sorted(FX.models().items()):
-        low = build_export_lowering(fx)
+        low = build_export_image(fx)
         with tempfile.TemporaryDirectory() as d:
             m = write_export(low, d)
             dd = Path(d)

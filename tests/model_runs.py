@@ -1,5 +1,5 @@
 """Shared drivers for the model-level parity tests: build a fixture's model with the package's
-lowering and run its greedy decode through a given backend."""
+image builder (opentars_b200.model_image) and run its greedy decode through a given backend."""
 from __future__ import annotations
 
 import hashlib
@@ -27,33 +27,33 @@ def base_config(mod, name: str, rename: dict | None = None) -> dict:
     return getattr(mod, rename.get(name, name))
 
 
-def build_lowering(fx: dict, full: bool = False):
+def build_image(fx: dict, full: bool = False):
     from opentars_b200 import models as Mo
-    from opentars_b200.lowering import QwenLowering
+    from opentars_b200.model_image import ModelImage as ModelImage
     if full:
         base = getattr(Mo, fx["base"])
         types = list(getattr(Mo, fx["types"])) if fx["types"] else None
         cfg = Mo.make_config(base, types, vocab=fx["vocab"])
         w = Mo.random_weights(cfg, seed=0, embed=True)
-        return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=3 << 29, head=True, queue_cap=8192)
+        return ModelImage(cfg, w, max_tokens=fx["T"], ddr_bytes=3 << 29, head=True, queue_cap=8192)
     cfg = Mo.make_config(base_config(Mo, fx["base"]), fx["types"], vocab=fx["vocab"])
     w = Mo.random_weights(cfg, seed=0, embed=True)
-    return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096,
+    return ModelImage(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096,
                         state_dtype=fx.get("state_dtype", "fp32"), wbits=fx.get("wbits", 8))
 
 
-def build_export_lowering(fx: dict):
+def build_export_image(fx: dict):
     """A fixture's small model with its embedding table rounded to bf16 (an export stores the table
     as bf16), for the export-format tests."""
     from opentars_b200 import models as Mo
     from opentars_b200.export import bf16_exact
-    from opentars_b200.lowering import QwenLowering
+    from opentars_b200.model_image import ModelImage as ModelImage
     cfg = Mo.make_config(base_config(Mo, fx["base"]), fx["types"], vocab=fx["vocab"])
     w = Mo.random_weights(cfg, seed=0, embed=True)
     w["embed_tokens.weight"] = bf16_exact(w["embed_tokens.weight"])
     if "embed_tokens_per_layer.weight" in w:
         w["embed_tokens_per_layer.weight"] = bf16_exact(w["embed_tokens_per_layer.weight"])
-    return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096,
+    return ModelImage(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 26, head=True, queue_cap=4096,
                         wbits=fx.get("wbits", 8))
 
 
@@ -92,13 +92,13 @@ def mtp_oracle(plain_ids: list[int], vocab: int, seed: int = 2):
     return oracle
 
 
-def build_mtp_lowering(fx: dict, **kw):
+def build_mtp_image(fx: dict, **kw):
     """A tests/golden/mtp.json case's Qwen3.5 model (with the MTP head weights)."""
     from opentars_b200 import models as Mo
-    from opentars_b200.lowering import QwenLowering
+    from opentars_b200.model_image import ModelImage as ModelImage
     cfg = Mo.make_config(Mo.CFG_Q35_SMALL, fx["types"], vocab=fx["vocab"])
     w = {**Mo.random_weights(cfg, embed=True), **Mo.random_mtp(cfg)}
-    return QwenLowering(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 25, head=True, queue_cap=8192,
+    return ModelImage(cfg, w, max_tokens=fx["T"], ddr_bytes=1 << 25, head=True, queue_cap=8192,
                         state_dtype=fx["state_dtype"], **kw)
 
 
@@ -106,7 +106,7 @@ def check_mtp(fx: dict, machine_cls) -> None:
     """Speculative decoding through machine_cls against the reference's run (mtp.json): the image,
     every queue, the tokens (those of plain decoding), every verified position's logits, the
     rounds and swap_state's queue."""
-    low = build_mtp_lowering(fx, verify_rows=2, mtp=True)
+    low = build_mtp_image(fx, verify_rows=2, mtp=True)
     assert sha(low.p.ddr) == fx["image_sha256"]
     queues = []
     ids, lg, rounds = low.generate_mtp(machine_runner(machine_cls, queues, gemv_only=False), fx["prompt"],

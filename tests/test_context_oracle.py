@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 from tests import fixtures as FX
-from tests.model_runs import build_lowering, logits_sha, sha
+from tests.model_runs import build_image, logits_sha, sha
 
 CONTEXT = json.loads((FX.GOLDEN / "context.json").read_text())
 
@@ -18,7 +18,7 @@ def test_context_fixture_oracle_first_positions(name):
     from oracle.machine import OracleMachine
     fx = CONTEXT[name]
     run = fx["runs"][0]
-    low = build_lowering(dict(base=fx["base"], types=fx["types"], vocab=fx["vocab"], T=fx["T"]))
+    low = build_image(dict(base=fx["base"], types=fx["types"], vocab=fx["vocab"], T=fx["T"]))
     assert sha(low.p.ddr) == fx["image_sha256"]
     P = len(run["prompt"])
     ddr, ids = low.p.ddr, list(run["prompt"])

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 
 from tests import fixtures as FX
-from tests.model_runs import OracleDevice, build_export_lowering
+from tests.model_runs import OracleDevice, build_export_image
 
 REF = json.loads((FX.GOLDEN / "export_ref.json").read_text())
 
@@ -19,7 +19,7 @@ REF = json.loads((FX.GOLDEN / "export_ref.json").read_text())
 def export_dir(request, tmp_path_factory):
     from opentars_b200.export import write_export
     d = tmp_path_factory.mktemp(request.param)
-    write_export(build_export_lowering(FX.models()[request.param]), d)
+    write_export(build_export_image(FX.models()[request.param]), d)
     return request.param, d
 
 
@@ -90,11 +90,11 @@ def test_runtime_refuses_mismatched_or_unsupported_exports(tmp_path, export_dir)
 def test_writer_refuses_what_an_export_cannot_hold(tmp_path):
     """write_export stores the embedding tables as bf16 and needs the head and a queue region."""
     from opentars_b200.export import bf16_exact, write_export
-    from tests.model_runs import build_lowering
-    low = build_lowering(FX.models()["qwen3_small"])             # fp32 embedding, not bf16-exact
+    from tests.model_runs import build_image
+    low = build_image(FX.models()["qwen3_small"])             # fp32 embedding, not bf16-exact
     with pytest.raises(ValueError, match="bf16-exact"):
         write_export(low, tmp_path / "a")
-    g4 = build_export_lowering(FX.models()["gemma4_small"])
+    g4 = build_export_image(FX.models()["gemma4_small"])
     g4.w["embed_tokens_per_layer.weight"] = g4.w["embed_tokens_per_layer.weight"] + np.float32(1e-3)
     assert not np.array_equal(bf16_exact(g4.w["embed_tokens_per_layer.weight"]), g4.w["embed_tokens_per_layer.weight"])
     with pytest.raises(ValueError, match="per-layer"):

@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 
 from tests import fixtures as FX
-from tests.model_runs import build_lowering, logits_sha, machine_runner
+from tests.model_runs import build_image, logits_sha, machine_runner
 
 pytestmark = pytest.mark.gpu
 
@@ -16,7 +16,7 @@ pytestmark = pytest.mark.gpu
 def test_engine_batch1_matches_reference_small(name):
     from opentars_b200.engine import DecodeEngine
     fx = FX.engine_models()[name]
-    low = build_lowering(fx)
+    low = build_image(fx)
     eng = DecodeEngine(low, batch=1)
     ids, logits = eng.generate([fx["prompt"]], fx["new"], chunk=4)
     assert ids[0] == fx["ids"]
@@ -35,11 +35,11 @@ def test_engine_batch_each_sequence_matches_oracle(name, batch):
     rng = np.random.default_rng(11)
     P = len(fx["prompt"])
     prompts = [fx["prompt"]] + [list(map(int, rng.integers(0, fx["vocab"], P))) for _ in range(batch - 1)]
-    eng = DecodeEngine(build_lowering(fx), batch=batch)
+    eng = DecodeEngine(build_image(fx), batch=batch)
     ids, logits = eng.generate(prompts, 3, chunk=4)
     eng.close()
     for b, pr in enumerate(prompts):
-        low = build_lowering(fx)
+        low = build_image(fx)
         oids, ologits, _ = low.generate(machine_runner(OracleMachine, []), pr, 3, chunk=4)
         assert ids[b] == oids, b
         assert all(np.array_equal(lg[b].view(np.uint32), ol.view(np.uint32)) for lg, ol in zip(logits, ologits)), b
@@ -57,7 +57,7 @@ def test_engine_three_launch_attention_matches_fused(name, monkeypatch):
     outs = []
     for fuse in ("1", "0"):
         monkeypatch.setenv("TARSCUDA_FUSE_ATTN", fuse)
-        eng = DecodeEngine(build_lowering(fx), batch=5)
+        eng = DecodeEngine(build_image(fx), batch=5)
         ids, logits = eng.generate(prompts, 3, chunk=4)
         eng.close()
         outs.append((ids, [lg.view(np.uint32).copy() for lg in logits]))
@@ -78,7 +78,7 @@ def test_engine_full_size_logits_bit_exact(name):
     fx = _full().get(name)
     if fx is None:
         pytest.skip(f"no {name} fixture")
-    low = build_lowering(fx, full=True)
+    low = build_image(fx, full=True)
     rng = np.random.default_rng(5)
     prompts = [fx["prompt"], list(map(int, rng.integers(0, fx["vocab"], len(fx["prompt"]))))]
     eng = DecodeEngine(low, batch=2)

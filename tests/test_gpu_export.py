@@ -7,7 +7,7 @@ import json
 import pytest
 
 from tests import fixtures as FX
-from tests.model_runs import build_export_lowering
+from tests.model_runs import build_export_image
 from tests.test_export import run_conversation
 
 pytestmark = pytest.mark.gpu
@@ -18,7 +18,7 @@ REF = json.loads((FX.GOLDEN / "export_ref.json").read_text())
 def test_export_on_cuda_matches_the_reference_runtime(name, tmp_path):
     from opentars_b200.board import Cuda, Qwen, manifest_mem
     from opentars_b200.export import write_export
-    write_export(build_export_lowering(FX.models()[name]), tmp_path)
+    write_export(build_export_image(FX.models()[name]), tmp_path)
     dev = Cuda(manifest_mem(tmp_path))
     model = Qwen(dev, tmp_path, log=lambda *a, **k: None)
     want = REF[name]["runs"]

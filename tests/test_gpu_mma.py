@@ -117,17 +117,17 @@ def test_engine_on_tensor_cores_matches_oracle(batch, mma_min_rows):
     single-sequence oracle run."""
     from opentars_b200.engine import DecodeEngine
     from tests import fixtures as FX
-    from tests.model_runs import build_lowering, machine_runner
+    from tests.model_runs import build_image, machine_runner
     mma_min_rows(2)
     for name, fx in sorted(FX.engine_models().items()):
         rng = np.random.default_rng(3)
         P = len(fx["prompt"])
         prompts = [fx["prompt"]] + [list(map(int, rng.integers(0, fx["vocab"], P))) for _ in range(batch - 1)]
-        eng = DecodeEngine(build_lowering(fx), batch=batch)
+        eng = DecodeEngine(build_image(fx), batch=batch)
         ids, logits = eng.generate(prompts, 2, chunk=4)
         eng.close()
         for b in (0, batch - 1):
-            low = build_lowering(fx)
+            low = build_image(fx)
             oids, ologits, _ = low.generate(machine_runner(OracleMachine, []), prompts[b], 2, chunk=4)
             assert ids[b] == oids, (name, b)
             assert all(np.array_equal(lg[b].view(np.uint32), ol.view(np.uint32))

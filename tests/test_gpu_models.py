@@ -4,7 +4,7 @@ and the full-size Qwen3-0.6B / Gemma-3-1B shapes (configs 3 and 4) through the b
 import pytest
 
 from tests import fixtures as FX
-from tests.model_runs import BoardRunner, build_lowering, logits_sha, machine_runner, sha
+from tests.model_runs import BoardRunner, build_image, logits_sha, machine_runner, sha
 
 pytestmark = pytest.mark.gpu
 
@@ -13,7 +13,7 @@ pytestmark = pytest.mark.gpu
 def test_small_models_through_drop_in_machine(name):
     from opentars_b200.machine import Machine
     fx = FX.models()[name]
-    low = build_lowering(fx)
+    low = build_image(fx)
     queues = []
     ids, logits, counts = low.generate(machine_runner(Machine, queues), fx["prompt"], fx["new"])
     assert queues == fx["queue_sha256"]
@@ -24,7 +24,7 @@ def test_small_models_through_drop_in_machine(name):
 @pytest.mark.parametrize("name", sorted(FX.models()))
 def test_small_models_through_board_backend(name):
     fx = FX.models()[name]
-    low = build_lowering(fx)
+    low = build_image(fx)
     run = BoardRunner(low)
     ids, logits, counts = low.generate(run, fx["prompt"], fx["new"])
     assert run.queues == fx["queue_sha256"]
@@ -55,7 +55,7 @@ def test_full_size_model_logits_bit_exact(name):
     fx = _full().get(name)
     if fx is None:
         pytest.skip(f"no {name} fixture")
-    low = build_lowering(fx, full=True)
+    low = build_image(fx, full=True)
     assert sha(low.p.ddr) == fx["image_sha256"]
     run = BoardRunner(low)
     ids, logits, counts = low.generate(run, fx["prompt"], fx["new"], chunk=fx["chunk"])

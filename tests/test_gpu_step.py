@@ -19,7 +19,7 @@ import numpy as np
 import pytest
 
 from tests import fixtures as FX
-from tests.model_runs import build_lowering, logits_sha
+from tests.model_runs import build_image, logits_sha
 
 pytestmark = pytest.mark.gpu
 
@@ -47,7 +47,7 @@ def test_whole_context_staggered_sequences_match_reference(name, fused):
     fx = _context()[name]
     runs, T = fx["runs"], fx["T"]
     P = len(runs[0]["prompt"])
-    low = build_lowering(dict(base=fx["base"], types=fx["types"], vocab=fx["vocab"], T=T))
+    low = build_image(dict(base=fx["base"], types=fx["types"], vocab=fx["vocab"], T=T))
     assert hashlib.sha256(bytes(low.p.ddr)).hexdigest() == fx["image_sha256"]
     B = 40
     start = [3 * b for b in range(B)]                 # sequence b joins at step 3 b
@@ -92,7 +92,7 @@ def test_fused_step_equals_per_kernel_path(name, batch):
     prompts = [fx["prompt"]] + [list(map(int, rng.integers(0, fx["vocab"], P))) for _ in range(batch - 1)]
     outs = []
     for fused in (True, False):
-        eng = _engine(build_lowering(fx), batch, fused)
+        eng = _engine(build_image(fx), batch, fused)
         ids, logits = eng.generate(prompts, fx["new"], chunk=4)
         eng.close()
         outs.append((ids, [lg.view(np.uint32).copy() for lg in logits]))
@@ -106,7 +106,7 @@ def test_full_size_batch64_fused_equals_per_kernel_and_reference(name):
     """Configs 3 / 4 at the benched batch: all 64 sequences equal between the fused step and the
     per-kernel path at every step, and the fixture's sequence equals the reference."""
     fx = _full()[name]
-    low = build_lowering(fx, full=True)
+    low = build_image(fx, full=True)
     rng = np.random.default_rng(5)
     prompts = [fx["prompt"]] + [list(map(int, rng.integers(0, fx["vocab"], len(fx["prompt"])))) for _ in range(63)]
     outs = []
@@ -126,7 +126,7 @@ def test_full_size_batch64_fused_equals_per_kernel_and_reference(name):
 def test_engine_refuses_steps_past_the_context_and_bad_tokens():
     from opentars_b200.engine import DecodeEngine
     fx = FX.engine_models()["qwen3_small"]
-    low = build_lowering(fx)
+    low = build_image(fx)
     eng = DecodeEngine(low, batch=2)
     eng.reset()
     with pytest.raises(RuntimeError):

@@ -15,6 +15,6 @@ def test_tower_on_the_gpu_matches_the_reference(size):
     cfg = OV.vision_config(**VIS["config"])
     w = OV.random_vision(cfg, seed=VIS["seed"])
     px, _, pos, rope = host_data(cfg, w, int(size))
-    low = OV.VisionLowering(cfg, w, patches_max=len(px), ddr_bytes=1 << 23)
+    low = OV.VisionImage(cfg, w, patches_max=len(px), ddr_bytes=1 << 23)
     assert _sha(low.run(px, pos, rope, machine=Machine)) == VIS["images"][size]["tokens_sha256"]
     assert _sha(low.run(px, pos, rope, blocks=1, machine=Machine)) == VIS["images"][size]["block1_sha256"]

@@ -1,4 +1,4 @@
-"""The package's lowering (opentars_b200.lowering) against the reference's own lowering + golden
+"""The package's model images (opentars_b200.model_image) against the reference's own lowering + golden
 model (committed fixtures): identical DDR image, identical descriptor queues, identical logits,
 run here through the CPU oracle."""
 import json
@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 
 from tests import fixtures as FX
-from tests.model_runs import build_lowering, check_mtp, logits_sha, machine_runner, sha
+from tests.model_runs import build_image, check_mtp, logits_sha, machine_runner, sha
 
 MTP = json.loads((FX.GOLDEN / "mtp.json").read_text())
 
@@ -16,7 +16,7 @@ MTP = json.loads((FX.GOLDEN / "mtp.json").read_text())
 def test_lowering_matches_reference_small_models(name):
     from oracle.machine import OracleMachine
     fx = FX.models()[name]
-    low = build_lowering(fx)
+    low = build_image(fx)
     assert sha(low.p.ddr) == fx["image_sha256"]
     queues = []
     ids, logits, counts = low.generate(machine_runner(OracleMachine, queues), fx["prompt"], fx["new"])
@@ -30,7 +30,7 @@ def test_chunked_prefill_equals_whole_prompt_logits():
     reference pins chunk == single steps, test_v04.py:370-422)."""
     from oracle.machine import OracleMachine
     fx = FX.models()["qwen3_small"]
-    a, b = build_lowering(fx), build_lowering(fx)
+    a, b = build_image(fx), build_image(fx)
     ids1, lg1, _ = a.generate(machine_runner(OracleMachine, []), fx["prompt"], 2)
     ids2, lg2, _ = b.generate(machine_runner(OracleMachine, []), fx["prompt"], 2, chunk=4)
     assert ids1 == ids2

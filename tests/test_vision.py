@@ -66,10 +66,10 @@ def test_lowering_and_oracle_match_the_reference(tower, size):
     want = VIS["images"][size]
     px, _, pos, rope = host_data(cfg, w, int(size))
     assert len(px) == want["patches"] and _sha(px, pos, rope) == want["host_sha256"]
-    low = OV.VisionLowering(cfg, w, patches_max=len(px), ddr_bytes=1 << 23)
+    low = OV.VisionImage(cfg, w, patches_max=len(px), ddr_bytes=1 << 23)
     one = low.run(px, pos, rope, blocks=1, machine=OracleMachine)
     tokens = low.run(px, pos, rope, machine=OracleMachine)
-    ddr, q, n = low.p.build()
+    ddr, q, n = low.p.finish()
     assert hashlib.sha256(bytes(ddr)).hexdigest() == want["image_sha256"] and [q, n] == want["queue"]
     assert _sha(one) == want["block1_sha256"]
     assert _sha(tokens) == want["tokens_sha256"]
@@ -82,5 +82,5 @@ def test_one_program_serves_a_smaller_image(tower):
     from opentars_b200 import vision as OV
     cfg, w = tower
     px, _, pos, rope = host_data(cfg, w, 8)
-    got = OV.VisionLowering(cfg, w, patches_max=64, ddr_bytes=1 << 23).run(px, pos, rope, machine=OracleMachine)
+    got = OV.VisionImage(cfg, w, patches_max=64, ddr_bytes=1 << 23).run(px, pos, rope, machine=OracleMachine)
     assert _sha(got) == VIS["images"]["8"]["tokens_sha256"]
