@@ -7,8 +7,13 @@
 Workloads (synthetic seeded data with the configs' distributions):
   decode        (default) config 3: Qwen3-0.6B shapes, random-init weights, B sequences per GPU
                 (default 64) with seeded 20-token prompts prefilled in chunks of 4, then greedy
-                decode; a step = one token for every sequence; value in tok/s (all GPUs). Sequence
-                0 is checked bit for bit against the reference's logits (committed fixture).
+                decode; a step = one token for every sequence; value in tok/s (all GPUs). The
+                default K = 236 timed steps decode the whole context once (positions 20 -> 255),
+                each step timed with its own pair of events; ms_per_step_at_position gives the
+                steps near positions 32, 128 and 250. Sequence 0 is checked bit for bit against
+                the reference's logits (committed fixture). The line also carries config0_gemv
+                and config2_w4: the GEMV workloads below, 50 timed steps each (--decode-only
+                skips them).
   decode-gemma  config 4: the same for Gemma-3-1B shapes
   gemv  config 0: one unit = ROW_QUANT of x [1, 1024] + W8A8 GEMV (QM_ROWCOL) against W [3072, 1024];
         a step runs R units on R distinct weight copies (R * 3 MiB > the 126 MB L2)
@@ -235,6 +240,28 @@ def barrier(world: int):
 
 # ----------------------------------------------------------------------------- our arm
 def run_ours(a, world, rank, local) -> dict | None:
+    m = measure_units(a.workload, a.units, a.steps, a.warmup, world, rank, local)
+    if rank != 0:
+        return None
+    out = {
+        "metric": METRIC, "value": round(m["value"], 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": m["ms_per_step"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8" if a.workload == "gemv" else "int4xint16",
+        "data": "synthetic, seeded (BASELINE config distributions)",
+        "config": dict(m["config"], parallelism=f"replicas x{world} (independent GEMV batches per GPU)"),
+        "roofline": m["roofline"], "e2e": m["e2e"],
+        "gpu_launches": m["gpu_launches"], "clocks": m["clocks"], "bit_exact_unit0": m["bit_exact"],
+    }
+    if world == 1 and not a.no_cpu:
+        out["cpu_baseline"] = cpu_oracle_gbs(a.workload, a.cpu_seconds, os.cpu_count() or 1)
+    return out
+
+
+def measure_units(workload: str, units: int, steps: int, warmup: int, world: int, rank: int, local: int,
+                  e2e_steps: int | None = None) -> dict:
+    """Configs 0 / 2 on this GPU: `steps` timed launches of the captured queue of R units (device
+    time, max over ranks), the dominant kernel's roofline, the end-to-end number through the board
+    API and rank 0's unit 0 against the oracle."""
     import ctypes
 
     import torch
@@ -242,8 +269,8 @@ def run_ours(a, world, rank, local) -> dict | None:
     torch.cuda.set_device(local)
     from opentars_b200._lib import check, lib
     from opentars_b200.board import Cuda
-    build, R = WORKLOADS[a.workload]
-    R = a.units or R
+    build, R = WORKLOADS[workload]
+    R = units or R
     p = build(R, seed=1234 + rank)
     L = lib()
     ddr = p["ddr"]
@@ -256,21 +283,21 @@ def run_ours(a, world, rank, local) -> dict | None:
     stream = torch.cuda.ExternalStream(L.tc_stream(dev.h), device=local)
 
     # parity spot check: unit 0 against the oracle happens after timing (rank 0)
-    for _ in range(a.warmup):
+    for _ in range(warmup):
         check(L.tc_graph_launch(g, None), dev.h)
     check(L.tc_synchronize(dev.h), dev.h)
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         e0.record(stream)
-        for _ in range(a.steps):
+        for _ in range(steps):
             check(L.tc_graph_launch(g, None), dev.h)
         e1.record(stream)
         check(L.tc_synchronize(dev.h), dev.h)
     ms = e0.elapsed_time(e1)
     barrier(world)
     ms_max = max_over_ranks(ms, world)
-    total_bytes = world * R * p["unit_bytes"] * a.steps
+    total_bytes = world * R * p["unit_bytes"] * steps
     value = total_bytes / (ms_max / 1e3) / 1e9
 
     # roofline: device times of the dominant kernel from a graph captured with events between
@@ -295,7 +322,7 @@ def run_ours(a, world, rank, local) -> dict | None:
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = peaks.get("hbm_gbs", 6650.0)
     achieved = p["kernel_bytes"] / (k_ms / 1e3) / 1e9
-    traffic_file = ROOT / "profiles" / f"traffic_{a.workload}.json"
+    traffic_file = ROOT / "profiles" / f"traffic_{workload}.json"
     traffic = json.loads(traffic_file.read_text()).get("bytes_per_launch") if traffic_file.exists() else None
     roofline = dict(bound="hbm", achieved=round(achieved, 1), peak=peak, unit="GB/s", frac=round(achieved / peak, 4),
                     traffic=traffic, kernel=p["kernel"], kernel_bytes_per_launch=p["kernel_bytes"],
@@ -311,15 +338,17 @@ def run_ours(a, world, rank, local) -> dict | None:
         dev.to_dev(x0, xn)
         dev.run(p["qa"], p["qlen"])
         dev.from_dev(y0, yn)
+    n_e2e = steps if e2e_steps is None else e2e_steps
     barrier(world)
     t0 = time.perf_counter()
-    for i in range(a.steps):
+    for i in range(n_e2e):
         dev.mem[x0:x0 + xn] = xs[i % 4]
         dev.to_dev(x0, xn)
         dev.run(p["qa"], p["qlen"])
         dev.from_dev(y0, yn)
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
-    e2e = dict(value=round(total_bytes / e2e_s / 1e9, 2), unit="GB/s", h2d_bytes_per_step=xn, d2h_bytes_per_step=yn,
+    e2e = dict(value=round(world * R * p["unit_bytes"] * n_e2e / e2e_s / 1e9, 2), unit="GB/s",
+               h2d_bytes_per_step=xn, d2h_bytes_per_step=yn,
                api="opentars_b200.board.Cuda: mem write, to_dev, run (cached graph), from_dev")
 
     # parity: unit 0's output of the last run against the oracle
@@ -331,24 +360,11 @@ def run_ours(a, world, rank, local) -> dict | None:
         img = dev.mem.copy()
         o = OracleMachine(bytearray(img.tobytes()))
         qa = p["qa"]
-        o.run_queue(qa, 2 if a.workload == "gemv" else 1)
+        o.run_queue(qa, 2 if workload == "gemv" else 1)
         bit_exact = bytes(o.ddr[y0:y0 + yn // R]) == img[y0:y0 + yn // R].tobytes()
     dev.close()
-    if rank != 0:
-        return None
-    out = {
-        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
-        "warmup": a.warmup, "ms_per_step": round(ms_max / a.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8" if a.workload == "gemv" else "int4xint16",
-        "data": "synthetic, seeded (BASELINE config distributions)",
-        "config": dict(p["config"], parallelism=f"replicas x{world} (independent GEMV batches per GPU)"),
-        "roofline": roofline, "e2e": e2e,
-        "gpu_launches": a.steps * kernels_per_step, "clocks": clk.summary(), "bit_exact_unit0": bit_exact,
-    }
-    if world == 1 and not a.no_cpu:
-        cb = cpu_oracle_gbs(a.workload, a.cpu_seconds, os.cpu_count() or 1)
-        out["cpu_baseline"] = cb
-    return out
+    return dict(value=value, ms_per_step=round(ms_max / steps, 4), config=p["config"], roofline=roofline,
+                e2e=e2e, gpu_launches=steps * kernels_per_step, clocks=clk.summary(), bit_exact=bit_exact)
 
 
 # ----------------------------------------------------------------------------- the reference arm
@@ -790,27 +806,41 @@ def run_decode(a, world, rank, local) -> dict | None:
             got.append(hashlib.sha256(eng.logits()[0].astype("<f4").tobytes()).hexdigest())
         bit_exact = got == want
 
-    def decode_steps(k: int):
+    def decode_steps(k: int, events: list | None = None):
+        """k one-token steps; when the context is full the batch starts over (a prefill, outside
+        the per-step events). With `events`, (position, start, end) of every step."""
         nonlocal pos
         for _ in range(k):
             if pos + 1 > CONTEXT:                         # context full: start the batch over
                 pos = prefill()
-            eng.step(None)
+            if events is None:
+                eng.step(None)
+            else:
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record(stream)
+                eng.step(None)
+                ev[1].record(stream)
+                events.append((pos, *ev))
             pos += 1
 
     decode_steps(a.warmup)
+    pos = prefill()                                       # the timed steps start at the prompt's end
     eng.sync()
     barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    events: list = []
     with Clocks(local) as clk:
-        e0.record(stream)
-        decode_steps(a.steps)
-        e1.record(stream)
+        decode_steps(a.steps, events)
         eng.sync()
-    ms = e0.elapsed_time(e1)
+    step_ms = [(p_, e0.elapsed_time(e1)) for p_, e0, e1 in events]
+    ms = sum(t for _, t in step_ms)
     barrier(world)
     ms_max = max_over_ranks(ms, world)
     value = world * B * a.steps / (ms_max / 1e3)
+    at = {}
+    for t in (32, 128, 250):                              # steps whose position is within 2 of t
+        near = [ms_ for p_, ms_ in step_ms if abs(p_ - t) <= 2]
+        at[str(t)] = round(statistics.mean(near), 4) if near else None
+    positions = (min(p_ for p_, _ in step_ms), max(p_ for p_, _ in step_ms) + 1)
 
     # roofline: the step's GEMV kernels (the weight stream) from one profiled step
     if pos + 1 > CONTEXT:
@@ -842,7 +872,9 @@ def run_decode(a, world, rank, local) -> dict | None:
     # e2e: the host in the loop as the reference's generate runs it: each step the token ids go up
     # from pinned memory and the greedy picks come back
     host_tok = torch.empty(B, dtype=torch.int32, pin_memory=True).numpy()
+    pos = prefill()                                       # the same positions as the timed steps
     host_tok[:] = eng.tokens()
+    eng.sync()
     barrier(world)
     t0 = time.perf_counter()
     for _ in range(a.steps):
@@ -857,6 +889,15 @@ def run_decode(a, world, rank, local) -> dict | None:
     e2e = dict(value=round(world * B * a.steps / e2e_s, 1), unit="tok/s", h2d_bytes_per_step=4 * B,
                d2h_bytes_per_step=4 * B, api="opentars_b200.engine.DecodeEngine: set_tokens, step, tokens")
     eng.close()
+    # configs 0 and 2 beside it (the GEMV kernels alone): GB/s of algorithmic bytes
+    units = {}
+    if not a.decode_only:
+        for key, wl in (("config0_gemv", "gemv"), ("config2_w4", "w4")):
+            m = measure_units(wl, 0, 50, 5, world, rank, local, e2e_steps=20)
+            units[key] = dict(value=round(m["value"], 1), unit="GB/s", ms_per_step=m["ms_per_step"],
+                              roofline_frac=m["roofline"]["frac"], kernel_us=m["roofline"]["kernel_us"],
+                              e2e_gbs=m["e2e"]["value"], bit_exact_unit0=m["bit_exact"], config=m["config"],
+                              clocks=m["clocks"])
     if rank != 0:
         return None
     out = {
@@ -866,12 +907,17 @@ def run_decode(a, world, rank, local) -> dict | None:
         "data": "synthetic: random-init weights (seeded, the reference's random_weights), seeded prompts",
         "config": dict(workload=("config3_qwen3_0.6b_decode" if a.workload == "decode" else "config4_gemma3_1b_decode"),
                        batch_per_gpu=B, prompt=PROMPT_LEN, prefill_chunk=CHUNK, context=CONTEXT,
+                       timed_positions=f"{positions[0]} -> {positions[1]} (each step one token per sequence; "
+                                       f"a full context starts the batch over, untimed)",
                        parallelism=f"independent sequences, {B} per GPU x {world} GPUs",
                        l2="weights (596 MB Qwen3 / 1 GB Gemma-3) larger than L2, streamed once per step",
                        model_build_s=round(build_s, 1)),
+        "ms_per_step_at_position": at,
         "roofline": roofline, "e2e": e2e, "gpu_launches": a.steps * len(prof), "clocks": clk.summary(),
         "bit_exact_seq0_vs_reference": bit_exact,
     }
+    for key, m in units.items():
+        out[key] = m
     if cpu is not None:
         out["cpu_baseline"] = cpu
     return out
@@ -917,7 +963,8 @@ def run_decode_reference(a, world, rank) -> dict | None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: decode the whole context once, 236 steps; GEMV: 100)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS) + sorted(DECODE_MODELS) + ["gemm"])
     ap.add_argument("--batch", type=int, default=64, help="decode: sequences per GPU")
@@ -926,7 +973,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=3.0)
+    ap.add_argument("--decode-only", action="store_true", help="decode: skip the config 0 / 2 keys")
     a = ap.parse_args()
+    if a.steps is None:
+        a.steps = CONTEXT - PROMPT_LEN if a.workload in DECODE_MODELS and a.impl == "ours" else 100
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":                       # CPU only: no process group, no GPU
         world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))

@@ -767,6 +767,23 @@ cudaError_t launch(const MmaMaps& maps, const MmaShape& sh, const Epi& epi, int 
 }
 }  // namespace
 
+// uint8 matrix [rows, cols] (row stride ld bytes) in boxes of box_cols bytes x box_rows rows, with
+// the 128-byte swizzle (box_cols <= 128), zero fill past the edges.
+bool make_map_u8(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
+                 uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn || (uintptr_t)ptr % 16 || ld % 16 || cols == 0 || rows == 0 || box_cols % 16 || box_cols > 128)
+    return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+
 bool mma_engine_ok(const EngGemvArgs& g) {
   if (g.M < 2 || g.K % 16 || g.kb % 16 || (uintptr_t)g.A % 16 || g.lda % 16 || !encode_fn()) return false;
   for (int s = 0; s < g.nseg; ++s) {

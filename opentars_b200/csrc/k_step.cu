@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "fp32.cuh"
 #include "step.h"
@@ -1063,7 +1064,14 @@ bool step_plan_gemm(StepGemm& g, int ntok, int grid, bool fused) {
   } else {
     // enough K chunks to give every CTA work (at most 8 partial sums per output), K chunks of at
     // most maxkc slices that never straddle the boundary of two K blocks
-    const int want = std::min(8, std::max(1, (grid + ntiles - 1) / ntiles));
+    // TARSCUDA_STEP_KSPLIT caps the partial sums per output (fewer chunks: fewer CTAs stream the
+    // weights, less int32 traffic for the phase after the GEMM)
+    static const int cap = [] {
+      const char* v = getenv("TARSCUDA_STEP_KSPLIT");
+      const int c = v ? atoi(v) : 8;
+      return c >= 1 && c <= 8 ? c : 8;
+    }();
+    const int want = std::min(cap, std::max(1, (grid + ntiles - 1) / ntiles));
     KC = std::min(maxkc, (g.nslices + want - 1) / want);
     if (two) {
       int up = KC;

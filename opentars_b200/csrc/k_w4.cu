@@ -18,10 +18,12 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "fp32.cuh"
 #include "mma.h"
 #include "ops.h"
+#include "pdl.cuh"
 #include "umma.cuh"
 
 namespace tc {
@@ -41,102 +43,119 @@ __device__ __forceinline__ uint4 ldg_stream(const uint8_t* p) {
   return v;
 }
 
+// Block-FP alignment of four (row, group) pairs p0 .. p0 + 3 (pairs >= total are not written) by
+// one warp, four elements of each group per lane (lane L: elements 4L .. 4L + 3). bits(p) gives
+// the lane's four fp32 bit patterns of pair p. The sink receives, per pair, the aligned mantissas
+// as one 256-byte block of 16 chunks (chunk c: k = 8c .. 8c + 7 as qh of k = 8c + 0, 2, 4, 6 | qh of
+// k = 8c + 1, 3, 5, 7 | ql of the even k | ql of the odd k, q = 256 qh + ql with qh = q >> 8 in
+// [-64, 64] and ql = q & 255), the group's scale bits and the sum of its mantissas:
+// sink.q(p) -> the block, sink.scale(p, bits), sink.sum(p, s). The four groups' shuffle
+// reductions overlap.
+template <class Bits, class Sink>
+__device__ __forceinline__ void align_quad(int p0, int total, Bits bits, Sink& sink) {
+  const int lane = threadIdx.x & 31;
+  uint32_t b[4][4];
+  int e[4][4], emax[4];
+  bool nan[4], inf[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const uint4 v4 = bits(min(p0 + u, total - 1));
+    const uint32_t vv[4] = {v4.x, v4.y, v4.z, v4.w};
+    nan[u] = false;
+    inf[u] = false;
+    emax[u] = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t v = vv[j];
+      if ((v & 0x7F800000u) == 0) v &= 0x80000000u;          // ftz
+      b[u][j] = v;
+      e[u][j] = (int)((v >> 23) & 0xFF);
+      nan[u] |= e[u][j] == 255 && (v & 0x7FFFFFu);
+      inf[u] |= e[u][j] == 255 && !(v & 0x7FFFFFu);
+      emax[u] = max(emax[u], e[u][j]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) emax[u] = max(emax[u], __shfl_xor_sync(0xFFFFFFFFu, emax[u], o));
+  int qs[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const bool gnan = __any_sync(0xFFFFFFFFu, nan[u]);
+    const bool ginf = __any_sync(0xFFFFFFFFu, inf[u]) && !gnan;
+    const int eff = max(emax[u], 14);
+    int qv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int sh = 10 + eff - e[u][j];
+      const uint32_t uu = (1u << 23) | (b[u][j] & 0x7FFFFFu);
+      const int s = min(max(sh, 0), 31);
+      const uint32_t kept = uu >> s;
+      const uint32_t rem = uu & ((1u << s) - 1u);
+      const uint32_t half = 1u << min(max(s - 1, 0), 30);
+      const bool up = s > 0 && (rem > half || (rem == half && (kept & 1u)));
+      int mag = (e[u][j] == 0 || sh >= 25 || e[u][j] == 255) ? 0 : (int)(kept + (up ? 1u : 0u));
+      const bool isinf_j = e[u][j] == 255 && !(b[u][j] & 0x7FFFFFu);
+      if (isinf_j && !gnan) mag = 16384;
+      if (gnan) mag = 0;
+      qv[j] = (b[u][j] >> 31) ? -mag : mag;
+    }
+    qs[u] = qv[0] + qv[1] + qv[2] + qv[3];
+    const int p = p0 + u;
+    if (p < total) {
+      // element k = 4 lane + j: chunk c = lane / 2, k = 8c + 4h + j with h = lane & 1; this lane's
+      // even / odd elements are bytes 2h, 2h + 1 of the chunk's four words
+      uint8_t* dst = sink.q(p) + 16 * (lane >> 1) + 2 * (lane & 1);
+      auto hi = [](int q) { return (uint32_t)(uint8_t)(int8_t)(q >> 8); };
+      auto lo = [](int q) { return (uint32_t)(q & 0xFF); };
+      *reinterpret_cast<uint16_t*>(dst + 0) = (uint16_t)(hi(qv[0]) | hi(qv[2]) << 8);     // qh even
+      *reinterpret_cast<uint16_t*>(dst + 4) = (uint16_t)(hi(qv[1]) | hi(qv[3]) << 8);     // qh odd
+      *reinterpret_cast<uint16_t*>(dst + 8) = (uint16_t)(lo(qv[0]) | lo(qv[2]) << 8);     // ql even
+      *reinterpret_cast<uint16_t*>(dst + 12) = (uint16_t)(lo(qv[1]) | lo(qv[3]) << 8);    // ql odd
+      if (lane == 0) {
+        uint32_t sb = (uint32_t)min(max(eff - 13, 0), 255) << 23;
+        if (emax[u] == 0) sb = 0;
+        if (ginf) sb = 0x7F800000u;
+        if (gnan) sb = 0x7FC00000u;
+        sink.scale(p, sb);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) qs[u] += __shfl_xor_sync(0xFFFFFFFFu, qs[u], o);
+  if (lane == 0) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (p0 + u < total) sink.sum(p0 + u, qs[u]);
+  }
+}
+
 // Aligns rows [m0, m0 + mb) from their fp32 bit patterns in sX [MB][K] into sQ [MB][64][kQStride]
-// int16 (chunks of 8 in the order k = 8c + 0, 2, 4, 6, 1, 3, 5, 7), sS [MB][64] fp32 scale bits and
-// sSum [MB][64] (the sum of each group's mantissas). A warp aligns 4 groups at once (4 elements of
-// each per lane), so the shuffle reductions of the 4 groups overlap.
+// int16, sS [MB][64] fp32 scale bits and sSum [MB][64].
+struct SmemSink {
+  int16_t* sQ;
+  uint32_t* sS;
+  int* sSum;
+  int G;
+  __device__ uint8_t* q(int p) const { return reinterpret_cast<uint8_t*>(sQ + ((p / G) * 64 + p % G) * kQStride); }
+  __device__ void scale(int p, uint32_t v) const { sS[(p / G) * 64 + p % G] = v; }
+  __device__ void sum(int p, int v) const { sSum[(p / G) * 64 + p % G] = v; }
+};
 template <int MB>
 __device__ void align_rows(const W4Args& g, int mb, const uint32_t* sX, int16_t* sQ, uint32_t* sS, int* sSum) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = g.K / W4_GROUP;
   const int nwarps = blockDim.x >> 5;
   const int total = mb * G;
-  for (int p0 = 4 * warp; p0 < total; p0 += 4 * nwarps) {
-    uint32_t b[4][4];
-    int e[4][4], emax[4];
-    bool nan[4], inf[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int p = min(p0 + u, total - 1);
+  SmemSink sink{sQ, sS, sSum, G};
+  for (int p0 = 4 * warp; p0 < total; p0 += 4 * nwarps)
+    align_quad(p0, total, [&](int p) {
       const int m = p / G, gi = p - m * G;
-      const uint4 v4 = *reinterpret_cast<const uint4*>(sX + m * g.K + gi * W4_GROUP + lane * 4);
-      const uint32_t vv[4] = {v4.x, v4.y, v4.z, v4.w};
-      nan[u] = false;
-      inf[u] = false;
-      emax[u] = 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t v = vv[j];
-        if ((v & 0x7F800000u) == 0) v &= 0x80000000u;        // ftz
-        b[u][j] = v;
-        e[u][j] = (int)((v >> 23) & 0xFF);
-        nan[u] |= e[u][j] == 255 && (v & 0x7FFFFFu);
-        inf[u] |= e[u][j] == 255 && !(v & 0x7FFFFFu);
-        emax[u] = max(emax[u], e[u][j]);
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int u = 0; u < 4; ++u) emax[u] = max(emax[u], __shfl_xor_sync(0xFFFFFFFFu, emax[u], o));
-    int qs[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const bool gnan = __any_sync(0xFFFFFFFFu, nan[u]);
-      const bool ginf = __any_sync(0xFFFFFFFFu, inf[u]) && !gnan;
-      const int eff = max(emax[u], 14);
-      int qv[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int sh = 10 + eff - e[u][j];
-        const uint32_t uu = (1u << 23) | (b[u][j] & 0x7FFFFFu);
-        const int s = min(max(sh, 0), 31);
-        const uint32_t kept = uu >> s;
-        const uint32_t rem = uu & ((1u << s) - 1u);
-        const uint32_t half = 1u << min(max(s - 1, 0), 30);
-        const bool up = s > 0 && (rem > half || (rem == half && (kept & 1u)));
-        int mag = (e[u][j] == 0 || sh >= 25 || e[u][j] == 255) ? 0 : (int)(kept + (up ? 1u : 0u));
-        const bool isinf_j = e[u][j] == 255 && !(b[u][j] & 0x7FFFFFu);
-        if (isinf_j && !gnan) mag = 16384;
-        if (gnan) mag = 0;
-        qv[j] = (b[u][j] >> 31) ? -mag : mag;
-      }
-      qs[u] = qv[0] + qv[1] + qv[2] + qv[3];
-      const int p = p0 + u;
-      if (p < total) {
-        const int m = p / G, gi = p - m * G;
-        // element k = 4 lane + j: chunk c = lane / 2, k = 8c + 4h + j with h = lane & 1. A chunk is
-        // 16 bytes: qh of k = 8c + 0, 2, 4, 6 | qh of k = 8c + 1, 3, 5, 7 | ql (even k) | ql (odd k),
-        // q = 256 qh + ql with qh = q >> 8 in [-64, 64] and ql = q & 255; this lane's even / odd
-        // elements are bytes 2h, 2h + 1 of those words.
-        uint8_t* dst = reinterpret_cast<uint8_t*>(sQ + (m * 64 + gi) * kQStride) + 16 * (lane >> 1) + 2 * (lane & 1);
-        auto hi = [](int q) { return (uint32_t)(uint8_t)(int8_t)(q >> 8); };
-        auto lo = [](int q) { return (uint32_t)(q & 0xFF); };
-        *reinterpret_cast<uint16_t*>(dst + 0) = (uint16_t)(hi(qv[0]) | hi(qv[2]) << 8);     // qh even
-        *reinterpret_cast<uint16_t*>(dst + 4) = (uint16_t)(hi(qv[1]) | hi(qv[3]) << 8);     // qh odd
-        *reinterpret_cast<uint16_t*>(dst + 8) = (uint16_t)(lo(qv[0]) | lo(qv[2]) << 8);     // ql even
-        *reinterpret_cast<uint16_t*>(dst + 12) = (uint16_t)(lo(qv[1]) | lo(qv[3]) << 8);    // ql odd
-        if (lane == 0) {
-          uint32_t sb = (uint32_t)min(max(eff - 13, 0), 255) << 23;
-          if (emax[u] == 0) sb = 0;
-          if (ginf) sb = 0x7F800000u;
-          if (gnan) sb = 0x7FC00000u;
-          sS[m * 64 + gi] = sb;
-        }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int u = 0; u < 4; ++u) qs[u] += __shfl_xor_sync(0xFFFFFFFFu, qs[u], o);
-    if (lane == 0) {
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int p = p0 + u;
-        if (p < total) sSum[(p / G) * 64 + (p % G)] = qs[u];
-      }
-    }
-  }
+      return *reinterpret_cast<const uint4*>(sX + m * g.K + gi * W4_GROUP + lane * 4);
+    }, sink);
 }
 
 // Mixed-sign 4-way byte dots (PTX dp4a with an unsigned first operand): d = c + sum a.b[i] * b.b[i].
@@ -455,6 +474,289 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
       mbar_wait(&full[u % kW4Stages], (u / kW4Stages) & 1, nullptr, 0);
 }
 
+// ---------------------------------------------------------------------------------------------
+// The tiled W4A16 GEMV (M <= 4): a pre-pass aligns the activation rows once, the main kernel
+// streams the weights through TMA tiles.
+//
+// Pre-pass (k_w4_align): one warp per four (row, group) pairs writes, per row m, the aligned
+// mantissas as [G][256 bytes] (align_quad's chunk layout), the group scale bits [G] and the
+// mantissa sums [G] into a scratch buffer. It lets the main kernel start at once
+// (griddepcontrol.launch_dependents); the main kernel is launched with programmatic stream
+// serialisation and reads the scratch only after griddepcontrol.wait.
+//
+// Main kernel (k_gemv_w4t): a tile is 64 output columns (lane L: columns L and L + 32) x all of
+// K. Each block works on two tiles at a time; a tile belongs to a quad of four compute warps, warp
+// b adding the terms of the groups g = b (mod 4) - exactly the bank b of the reference's four-bank
+// sum, in increasing g - so no term crosses a warp until the four banks are combined. A producer
+// warp per quad fills the quad's ring with stages of four groups (two TMA boxes of 64 rows x 128
+// bytes, 128-byte swizzle: the lanes' 16-byte reads of one row chunk land on eight different bank
+// groups); the activation chunk a lane multiplies with is the same for all 32 lanes (a broadcast
+// read) and serves both of its columns. The fp16 group scales of the next tile are copied into
+// shared memory (4-byte cp.async, columns padded to an odd number of words) while the current
+// tile computes. Every wait is bounded; after a give-up the warps skip their remaining work but
+// keep the quad's barrier count, the producers stop issuing, and the block drains the copies in
+// flight.
+constexpr int kTQuads = 2, kTBanks = 4, kTCols = 64;
+constexpr int kTThreads = 32 * (kTQuads + kTQuads * kTBanks);      // 2 producer warps + 8 compute warps
+constexpr int kTStageB = 2 * kTCols * 128;                            // four groups of 64 columns
+constexpr int kTMaxStages = 16;
+
+__host__ __device__ constexpr uint32_t w4_scratch_row(int G) { return (uint32_t)G * (256 + 8); }
+
+struct AlignSink {
+  uint8_t* base;
+  int G;
+  __device__ uint8_t* q(int p) const { return base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)(p % G) * 256; }
+  __device__ void scale(int p, uint32_t v) const {
+    reinterpret_cast<uint32_t*>(base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)G * 256)[p % G] = v;
+  }
+  __device__ void sum(int p, int v) const {
+    reinterpret_cast<int*>(base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)G * 260)[p % G] = v;
+  }
+};
+
+__global__ void __launch_bounds__(256) k_w4_align(W4Args g, uint8_t* scratch) {
+  griddep_launch();
+  const int G = g.K / W4_GROUP, total = g.M * G;
+  const int lane = threadIdx.x & 31;
+  const int p0 = 4 * (blockIdx.x * 8 + (threadIdx.x >> 5));
+  if (p0 >= total) return;
+  AlignSink sink{scratch, G};
+  align_quad(p0, total, [&](int p) {
+    const int m = p / G, gi = p - m * G;
+    const uint8_t* row = g.A + (uint64_t)m * g.lda;
+    const uint64_t k = (uint64_t)gi * W4_GROUP + 4 * lane;
+    if (g.a_bf16)
+      return make_uint4((uint32_t)ld_u16(row + 2 * k) << 16, (uint32_t)ld_u16(row + 2 * k + 2) << 16,
+                        (uint32_t)ld_u16(row + 2 * k + 4) << 16, (uint32_t)ld_u16(row + 2 * k + 6) << 16);
+    if (((uintptr_t)(row + 4 * k) & 15) == 0) return *reinterpret_cast<const uint4*>(row + 4 * k);
+    return make_uint4(ld_u32(row + 4 * k), ld_u32(row + 4 * k + 4), ld_u32(row + 4 * k + 8), ld_u32(row + 4 * k + 12));
+  }, sink);
+}
+
+// Row stride (bytes) of one column's group scales in shared memory: at least 2 G, a multiple of 4
+// with an odd number of words, so the 32 lanes' 2-byte reads of one group hit 32 different banks.
+__host__ __device__ constexpr uint32_t w4t_scale_stride(int G) { return (uint32_t)((G + 1) / 2) % 2 ? 2 * G : 2 * G + 4; }
+
+template <int MB>
+__global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(W4Args g, const __grid_constant__ CUtensorMap wmap,
+                                                            const uint8_t* scratch, int stages) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t full[kTQuads][kTMaxStages], empty[kTQuads][kTMaxStages];
+  __shared__ float sbank[2][kTQuads][kTBanks][MB][kTCols];
+  __shared__ int s_stop, s_issued[kTQuads];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = g.K / W4_GROUP, nstage = (G + 3) / 4;
+  const int ntiles = (g.N + kTCols - 1) / kTCols;
+  const uint32_t row_b = w4_scratch_row(G), sstr = w4t_scale_stride(G);
+  uint8_t* ring = smem;                                             // [quad][stage][2 boxes][64][128]
+  uint8_t* sact = smem + (size_t)kTQuads * stages * kTStageB;      // [MB][G][256] | bits [G] | sums [G]
+  uint8_t* sscl = sact + (size_t)MB * row_b;                        // [quad][2][64 columns][sstr]
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < kTQuads; ++q)
+      for (int i = 0; i < stages; ++i) {
+        mbar_init(&full[q][i], 1);
+        mbar_init(&empty[q][i], kTBanks);
+      }
+    s_stop = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  // tiles of quad q: blockIdx.x + gridDim.x * (q + kTQuads * j)
+  if (warp < kTQuads) {
+    if (lane == 0) {
+      const int q = warp;
+      int it = 0;
+      for (int t = blockIdx.x + gridDim.x * q; t < ntiles; t += gridDim.x * kTQuads) {
+        for (int s = 0; s < nstage; ++s, ++it) {
+          const int st = it % stages;
+          if (*(volatile int*)&s_stop || !mbar_wait(&empty[q][st], ((it / stages) & 1) ^ 1, g.err, 13, g.spin)) {
+            s_stop = 1;
+            goto producer_done;
+          }
+          const bool two = 4 * s + 2 < G;
+          mbar_expect_tx(&full[q][st], two ? kTStageB : kTStageB / 2);
+          uint8_t* dst = ring + ((size_t)q * stages + st) * kTStageB;
+          tma_load_2d(dst, &wmap, 256 * s, kTCols * t, &full[q][st]);
+          if (two) tma_load_2d(dst + kTStageB / 2, &wmap, 256 * s + 128, kTCols * t, &full[q][st]);
+        }
+      }
+    producer_done:
+      s_issued[warp] = it;
+    }
+  } else {
+    const int cw = warp - kTQuads, q = cw / kTBanks, b = cw % kTBanks;
+    const int qt = threadIdx.x - 32 * (kTQuads + q * kTBanks);     // thread of the quad, 0..127
+    // the group scales of tile t into buffer `buf` of this quad (4-byte copies)
+    auto fetch_scales = [&](int t, int buf) {
+      uint8_t* dst = sscl + ((size_t)q * 2 + buf) * kTCols * sstr;
+      const int words = kTCols * (G / 2);
+      for (int w = qt; w < words; w += 32 * kTBanks) {
+        const int c = w / (G / 2), j = w - c * (G / 2);
+        const uint64_t n = (uint64_t)t * kTCols + c;
+        if (n < (uint64_t)g.N)
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst + c * sstr + 4 * j)),
+                       "l"(g.scale + 2 * (n * G + 2 * j))
+                       : "memory");
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    const int t0 = blockIdx.x + gridDim.x * q;
+    if (t0 < ntiles) fetch_scales(t0, 0);
+    // the aligned activation rows: written by the pre-pass
+    griddep_wait();
+    {
+      const uint32_t bytes = (uint32_t)MB * row_b;
+      const int mrows = min(MB, g.M);
+      for (uint32_t i = 16 * (threadIdx.x - 32 * kTQuads); i < bytes; i += 16 * (kTThreads - 32 * kTQuads))
+        if (i / row_b < (uint32_t)mrows) cp16(sact + i, scratch + i);
+      cp_wait_all();
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kTQuads * kTBanks) : "memory");
+    }
+    int it = 0, tl = 0;
+    for (int t = t0; t < ntiles; t += gridDim.x * kTQuads, ++tl) {
+      if (t + gridDim.x * kTQuads < ntiles) fetch_scales(t + gridDim.x * kTQuads, (tl + 1) & 1);
+      const uint8_t* scl = sscl + ((size_t)q * 2 + (tl & 1)) * kTCols * sstr;
+      float bank[2][MB];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int m = 0; m < MB; ++m) bank[h][m] = 0.0f;
+      for (int s = 0; s < nstage; ++s, ++it) {
+        const int st = it % stages, gi = 4 * s + b;
+        bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[q][st], (it / stages) & 1, g.err, 14, g.spin);
+        ok = __all_sync(0xFFFFFFFFu, ok);
+        if (!ok) {
+          s_stop = 1;
+          continue;                                  // skip the work, keep the barrier count
+        }
+        uint4 wv[2][4];
+        if (gi < G) {
+          // group gi = 4 s + b: box b / 2, chunks 4 (b & 1) .. + 3 of rows lane and lane + 32, swizzled
+          const uint8_t* box = ring + ((size_t)q * stages + st) * kTStageB + (b >> 1) * (kTStageB / 2);
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              wv[h][j] = *reinterpret_cast<const uint4*>(box + (lane + 32 * h) * 128 + 16 * ((4 * (b & 1) + j) ^ (lane & 7)));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[q][st]);
+        if (gi < G) {
+          float ws[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) ws[h] = from_fp16(*reinterpret_cast<const uint16_t*>(scl + (lane + 32 * h) * sstr + 2 * gi));
+#pragma unroll
+          for (int m = 0; m < MB; ++m) {
+            if (m < g.M) {
+              const uint8_t* arow = sact + (size_t)m * row_b;
+              const uint4* ac = reinterpret_cast<const uint4*>(arow + (size_t)gi * 256);
+              // both columns' exact dots, eight independent accumulator chains
+              int h0[2] = {0, 0}, h1[2] = {0, 0}, l0[2] = {0, 0}, l1[2] = {0, 0};
+#pragma unroll
+              for (int c = 0; c < 16; ++c) {
+                const uint4 qc = ac[c];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const uint4& v = wv[h][c >> 2];
+                  const uint32_t w = ((c & 3) == 0 ? v.x : (c & 3) == 1 ? v.y : (c & 3) == 2 ? v.z : v.w);
+                  const uint32_t ev = (w ^ 0x88888888u) & 0x0F0F0F0Fu;      // u = w + 8, k = 8c + 0, 2, 4, 6
+                  const uint32_t od = (w ^ 0x88888888u) & 0xF0F0F0F0u;      // 16 u, k = 8c + 1, 3, 5, 7
+                  h0[h] = dp4a_us(ev, qc.x, h0[h]);
+                  h1[h] = dp4a_us(od, qc.y, h1[h]);
+                  l0[h] = dp4a_uu(ev, qc.z, l0[h]);
+                  l1[h] = dp4a_uu(od, qc.w, l1[h]);
+                }
+              }
+              const int qsum = reinterpret_cast<const int*>(arow + (size_t)G * 260)[gi];
+              const float xs = bf(reinterpret_cast<const uint32_t*>(arow + (size_t)G * 256)[gi]);
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int dot = 256 * (h0[h] + (h1[h] >> 4)) + (l0[h] + (l1[h] >> 4)) - 8 * qsum;
+                bank[h][m] = fadd_nc(bank[h][m], group_term(dot, ws[h], xs));
+              }
+            }
+          }
+        }
+      }
+      // the four banks of the tile's columns: (b0 + b1) + (b2 + b3)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int m = 0; m < MB; ++m) sbank[tl & 1][q][b][m][lane + 32 * h] = canon(bank[h][m]);
+      asm volatile("cp.async.wait_group 0;" ::: "memory");     // the next tile's scales have landed
+      asm volatile("bar.sync %0, %1;" ::"r"(2 + q), "n"(32 * kTBanks) : "memory");
+      if (b < 2 && !*(volatile int*)&s_stop) {                // warps 0 / 1: columns lane / lane + 32
+        const int c = lane + 32 * b, n = t * kTCols + c;
+        if (n < g.N) {
+#pragma unroll
+          for (int m = 0; m < MB; ++m) {
+            if (m < g.M) {
+              const float(&bk)[kTBanks][MB][kTCols] = sbank[tl & 1][q];
+              float y = fadd(fadd(bk[0][m][c], bk[1][m][c]), fadd(bk[2][m][c], bk[3][m][c]));
+              if (g.bias) y = fadd(y, ld_f32(g.bias + 4 * (uint64_t)n));
+              y = act_fn(y, g.act);
+              store_out(g.Y + (uint64_t)m * g.ldy, n, y, g.out, g.out_scale);
+            }
+          }
+        }
+      }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+  }
+  // after a give-up, the copies of the last stages issued may still be in flight: they land
+  // before the block exits (these waits always have the full limit)
+  __syncthreads();
+  if (threadIdx.x < kTQuads && s_stop) {
+    const int q = threadIdx.x, n_is = s_issued[q];
+    for (int u = n_is > stages ? n_is - stages : 0; u < n_is; ++u)
+      mbar_wait(&full[q][u % stages], (u / stages) & 1, nullptr, 0);
+  }
+}
+
+// Dynamic shared memory the tiled kernel may use beside its static arrays (the banks of two tiles
+// per quad, the barriers).
+size_t w4t_smem_cap(int MB) { return 227 * 1024 - (size_t)4096 * MB - 1024; }
+
+// Shared memory of the tiled kernel for MB rows: the rings, the activation rows, the scales of two
+// tiles per quad, alignment slack.
+size_t w4t_smem(int MB, int G, int stages) {
+  return (size_t)kTQuads * stages * kTStageB + (size_t)MB * w4_scratch_row(G) +
+         (size_t)kTQuads * 2 * kTCols * w4t_scale_stride(G) + 1024;
+}
+
+template <int MB>
+cudaError_t launch_w4t(const W4Args& g0, cudaStream_t st) {
+  W4Args g = g0;
+  g.err = wait_error_flag();
+  g.spin = spin_limit();
+  const int G = g.K / W4_GROUP;
+  int stages = kTMaxStages;
+  while (stages > 2 && w4t_smem(MB, G, stages) > w4t_smem_cap(MB)) --stages;
+  const size_t smem = w4t_smem(MB, G, stages);
+  CUtensorMap map;
+  if (!make_map_u8(&map, g.W, g.K / 2, g.N, g.K / 2, 128, kTCols)) return cudaErrorInvalidValue;
+  k_w4_align<<<(g.M * G + 31) / 32, 256, 0, st>>>(g, g.scratch);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  auto kern = k_gemv_w4t<MB>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int ntiles = (g.N + kTCols - 1) / kTCols;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(std::min((ntiles + kTQuads - 1) / kTQuads, 148));
+  cfg.blockDim = dim3(kTThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, g, map, (const uint8_t*)g.scratch, stages);
+}
+
 template <int MB>
 cudaError_t launch_w4s(const W4Args& g0, cudaStream_t st) {
   W4Args g = g0;
@@ -483,7 +785,30 @@ cudaError_t launch_w4(const W4Args& g, cudaStream_t st) {
 }
 }  // namespace
 
+// TARSCUDA_W4_LEGACY=1 keeps the streamed kernel without the pre-pass (for comparisons).
+bool w4_legacy() {
+  static const bool v = [] {
+    const char* e = getenv("TARSCUDA_W4_LEGACY");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
+bool w4_tiled_ok(const W4Args& g) {
+  const int G = g.K / W4_GROUP;
+  const int mb = g.M <= 1 ? 1 : (g.M <= 2 ? 2 : 4);
+  return g.scratch && g.M >= 1 && g.M <= 4 && g.K % 256 == 0 && (uintptr_t)g.W % 16 == 0 &&
+         ((uintptr_t)g.scratch & 15) == 0 && w4t_smem(mb, G, 3) <= w4t_smem_cap(mb) && !w4_legacy();
+}
+
+uint64_t w4_scratch_bytes(int M, int K) { return (uint64_t)M * w4_scratch_row(K / W4_GROUP); }
+
 cudaError_t launch_gemm_w4a16(const W4Args& g, cudaStream_t st) {
+  if (w4_tiled_ok(g)) {
+    if (g.M == 1) return launch_w4t<1>(g, st);
+    if (g.M == 2) return launch_w4t<2>(g, st);
+    return launch_w4t<4>(g, st);
+  }
   // streamed through shared memory when the packed weights are 16-byte aligned (K % 256 == 0
   // makes every column a multiple of 128 bytes) and the ring fits next to the activations
   const size_t ring = (size_t)kW4Stages * kW4Cols * (g.K / 2);

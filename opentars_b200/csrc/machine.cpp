@@ -32,6 +32,8 @@ struct tc_machine {
   std::vector<std::pair<uint64_t, uint64_t>> written;  // [lo, hi) of the last run's outputs
   uint8_t* scratch = nullptr;
   uint64_t scratch_size = 0;
+  uint8_t* w4s = nullptr;                              // the W4A16 GEMV's aligned activation rows
+  uint64_t w4s_size = 0;
   std::string err;
   std::vector<cudaStream_t> lanes;                     // extra capture streams (one level's launches)
 };
@@ -61,19 +63,23 @@ float f32(uint64_t bits) {
   return f;
 }
 
-cudaError_t ensure_scratch(tc_machine* m, uint64_t n) {
-  if (n <= m->scratch_size) return cudaSuccess;
-  if (m->scratch) {
+// Grows a device buffer of the machine (after the machine's stream drained: queued work may still
+// use the old one).
+cudaError_t grow(tc_machine* m, uint8_t*& buf, uint64_t& size, uint64_t n) {
+  if (n <= size) return cudaSuccess;
+  if (buf) {
     cudaError_t e = cudaStreamSynchronize(m->stream);
     if (e != cudaSuccess) return e;
-    cudaFree(m->scratch);
-    m->scratch = nullptr;
-    m->scratch_size = 0;
+    cudaFree(buf);
+    buf = nullptr;
+    size = 0;
   }
-  cudaError_t e = cudaMalloc(&m->scratch, n);
-  if (e == cudaSuccess) m->scratch_size = n;
+  cudaError_t e = cudaMalloc(&buf, n);
+  if (e == cudaSuccess) size = n;
   return e;
 }
+cudaError_t ensure_scratch(tc_machine* m, uint64_t n) { return grow(m, m->scratch, m->scratch_size, n); }
+cudaError_t ensure_w4s(tc_machine* m, uint64_t n) { return grow(m, m->w4s, m->w4s_size, n); }
 
 // The kernel arguments of a W8A8 GEMM descriptor (A as the descriptor names it; a conv's gather
 // buffer replaces it at launch) and of a row-op descriptor.
@@ -122,6 +128,7 @@ cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream) {
       g.Y = B + d[F_Y_OFF]; g.ldy = s.ldy;
       g.M = (int)d[F_M]; g.N = (int)d[F_N]; g.K = (int)d[F_K];
       g.act = d.act(); g.out = d.out(); g.out_scale = osc;
+      if (g.M <= 4 && ensure_w4s(mc, w4_scratch_bytes(g.M, g.K)) == cudaSuccess) g.scratch = mc->w4s;
       return launch_gemm_w4a16(g, stream);
     }
     GemmArgs g{};
@@ -288,16 +295,18 @@ cudaError_t fetch_queue(tc_machine* m, uint64_t qaddr, uint32_t qlen, std::vecto
   return e;
 }
 
-// The conv scratch a queue needs (so capture never allocates).
-uint64_t scratch_need(const std::vector<uint8_t>& q, uint32_t qlen, int core_id, int gemv_only) {
-  uint64_t need = 0;
+// The conv gather scratch and the W4A16 row scratch a queue needs (so capture never allocates).
+std::pair<uint64_t, uint64_t> scratch_need(const std::vector<uint8_t>& q, uint32_t qlen, int core_id, int gemv_only) {
+  uint64_t conv = 0, w4 = 0;
   for (uint32_t i = 0; i < qlen; ++i) {
     const uint8_t* raw = q.data() + 64 * (size_t)i;
     Desc d;
     decode(raw, &d);
-    if (d.conv() && validate(raw, d, core_id, gemv_only) == E_OK) need = std::max<uint64_t>(need, d[F_M] * d[F_K]);
+    if (validate(raw, d, core_id, gemv_only) != E_OK) continue;
+    if (d.conv()) conv = std::max<uint64_t>(conv, d[F_M] * d[F_K]);
+    if (d.op() == OP_GEMM && d.w4() && d[F_M] <= 4) w4 = std::max<uint64_t>(w4, w4_scratch_bytes((int)d[F_M], (int)d[F_K]));
   }
-  return need;
+  return {conv, w4};
 }
 // Captures a queue as a graph of dependency levels. Every descriptor's byte footprint (bounding
 // interval per input tensor and per output) is compared with those of the earlier descriptors; a
@@ -347,6 +356,7 @@ int capture_grouped(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_i
     nd.w.push_back(Iv{fp.y.base, seg_end(fp.y)});
     if (fp.has_extra) nd.w.push_back(Iv{fp.extra.base, seg_end(fp.extra)});
     if (d.conv()) nd.w.push_back(Iv{kScratch, kScratch + 1});
+    if (d.op() == OP_GEMM && d.w4()) nd.w.push_back(Iv{kScratch + 2, kScratch + 3});   // the row scratch
     int lvl = 0;
     for (int k = (int)nodes.size() - 1; k >= 0 && lvl <= top; --k) {
       const LevelNode& o = nodes[k];
@@ -499,7 +509,11 @@ int tc_queue_capture(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_
   *contract_op = -1;
   std::vector<uint8_t> q;
   cudaError_t e = fetch_queue(m, qaddr, qlen, q);
-  if (e == cudaSuccess) e = ensure_scratch(m, scratch_need(q, qlen, core_id, gemv_only));
+  if (e == cudaSuccess) {
+    const auto need = scratch_need(q, qlen, core_id, gemv_only);
+    e = ensure_scratch(m, need.first);
+    if (e == cudaSuccess) e = ensure_w4s(m, need.second);
+  }
   if (e != cudaSuccess) return fail(m, "capture setup", e);
   tc_graph* g = new tc_graph();
   g->m = m;
@@ -625,6 +639,7 @@ int tc_close(tc_machine* m) {
   if (m->stream) cudaStreamSynchronize(m->stream);
   for (auto s : m->lanes) cudaStreamDestroy(s);
   if (m->scratch) cudaFree(m->scratch);
+  if (m->w4s) cudaFree(m->w4s);
   if (m->dev) cudaFree(m->dev);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;

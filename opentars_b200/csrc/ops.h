@@ -56,8 +56,12 @@ struct W4Args {
   float out_scale;
   int* err;                          // device word for a bounded wait that gave up (set by the launcher)
   uint32_t spin;                     // poll limit of the bounded waits (set by the launcher)
+  uint8_t* scratch;                  // w4_scratch_bytes(M, K) of device memory for the aligned rows,
+                                     // or nullptr (then the kernels align in every block)
 };
 cudaError_t launch_gemm_w4a16(const W4Args& g, cudaStream_t st);
+// Scratch the tiled W4A16 GEMV needs for M rows of K (16-byte aligned).
+uint64_t w4_scratch_bytes(int M, int K);
 
 // conv: the NHWC int8 image gathered into [OH*OW, KH*KW*Cin] rows (zero padding), golden.py:282-293
 struct Im2colArgs {

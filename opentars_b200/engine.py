@@ -231,6 +231,18 @@ class DecodeEngine:
                         (ex[i] - last) / 1e3))
         return out
 
+    def profile(self) -> list[tuple[str, float, int]]:
+        """One decode step kernel by kernel: [(kind, ms, algorithmic bytes)]."""
+        cap = 4096
+        ms = np.zeros(cap, np.float32)
+        kind = np.zeros(cap, np.int32)
+        nb = np.zeros(cap, np.uint64)
+        n = lib().tc_engine_profile(self.h, ms.ctypes.data_as(ctypes.c_void_p), kind.ctypes.data_as(ctypes.c_void_p),
+                                    nb.ctypes.data_as(ctypes.c_void_p), cap)
+        if n < 0:
+            self._check(n, "profile")
+        return [(KERNEL_KINDS[kind[i]], float(ms[i]), int(nb[i])) for i in range(n)]
+
     def generate(self, prompts, n_new: int, chunk: int = 4, keep_logits: bool = True):
         """Greedy decoding of B prompts of equal length: prefill in chunks of `chunk` tokens, then
         n_new single-token steps. Returns (ids [B][len + n_new + 1], logits per step [B][vocab])."""

@@ -57,9 +57,9 @@ def _give_up_then_recover(program, codes):
 
 
 def test_w4a16_stream_wait_gives_up_and_recovers():
-    """The streamed W4A16 GEMV (producer code 11, consumer code 12)."""
+    """The tiled W4A16 GEMV (producer code 13, consumer code 14)."""
     import __graft_entry__ as GE
-    _give_up_then_recover(GE._w4_program(), (11, 12))
+    _give_up_then_recover(GE._w4_program(), (13, 14))
 
 
 def test_tensor_core_gemm_wait_gives_up_and_recovers():
