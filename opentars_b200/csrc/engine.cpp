@@ -423,6 +423,11 @@ int step_fused(tc_engine* e, const int* tok, bool trace) {
   // time limits: the poll limit's scale (2^22 polls: about 0.2 s; 0: give up at once)
   a.wait_ns = (uint64_t)spin_limit() * 50;
   a.drain_ns = 20000000ull;
+  static const int lead = [] {                         // a tuning knob: how early weights stream
+    const char* v = getenv("TARSCUDA_STEP_LEAD");
+    return v ? atoi(v) : 1 << 20;
+  }();
+  a.lead = lead;
   a.trace = trace ? e->strace : nullptr;
   TRY(cudaMemsetAsync(e->ssync, 0, (size_t)(1 + 2 * e->B) * 4, e->st));
   if (trace) TRY(cudaMemsetAsync(e->strace, 0, (size_t)e->ntrace * 8, e->st));

@@ -768,9 +768,9 @@ cudaError_t launch(const MmaMaps& maps, const MmaShape& sh, const Epi& epi, int 
 }  // namespace
 
 // uint8 matrix [rows, cols] (row stride ld bytes) in boxes of box_cols bytes x box_rows rows, with
-// the 128-byte swizzle (box_cols <= 128), zero fill past the edges.
+// the 128-byte swizzle (box_cols <= 128) or dense rows, zero fill past the edges.
 bool make_map_u8(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
-                 uint32_t box_rows) {
+                 uint32_t box_rows, bool swizzle) {
   auto fn = encode_fn();
   if (!fn || (uintptr_t)ptr % 16 || ld % 16 || cols == 0 || rows == 0 || box_cols % 16 || box_cols > 128)
     return false;
@@ -779,8 +779,8 @@ bool make_map_u8(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, 
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 

@@ -196,9 +196,21 @@ __device__ __forceinline__ int seg_of(const StepGemm& g, int t) {
 // ------------------------------------------------------------------------------ weight producer
 __device__ __noinline__ uint32_t produce(const StepArgs& a, uint8_t* ring, uint64_t* full, uint64_t* empty, Ctl* ctl) {
   uint32_t q = 0;
-  auto gemm = [&](const StepGemm& g) -> bool {
+  // gs: the barrier after which the GEMM's phase runs; its slices are issued once this CTA has
+  // entered barrier gs - lead (so the stream does not crowd the latency-bound phases before it)
+  auto gemm = [&](const StepGemm& g, unsigned gs) -> bool {
     int ks, grp;
     if (!my_chunk(g, ks, grp)) return true;
+    if ((unsigned)a.lead < gs) {
+      const uint64_t t0 = gtime();
+      while (*(volatile unsigned*)&ctl->gen + (unsigned)a.lead < gs) {
+        if (*(volatile int*)&ctl->abort) return false;
+        if (gtime() - t0 >= a.wait_ns) {
+          give_up(a, ctl, 45, gs);
+          return false;
+        }
+      }
+    }
     const int k0 = ks * g.KC, k1 = min(g.nslices, k0 + g.KC);
     const int ntiles = g.tile0[g.nseg];
     for (int t = grp; t < ntiles; t += g.groups) {
@@ -214,9 +226,10 @@ __device__ __noinline__ uint32_t produce(const StepArgs& a, uint8_t* ring, uint6
   bool ok = true;
   for (int l = 0; l < a.L && ok; ++l) {
     const StepLayer& Ly = a.layers[l];
-    ok = gemm(Ly.qkv) && gemm(Ly.o) && gemm(Ly.gu) && gemm(Ly.down);
+    const unsigned g0 = 8u * l;                        // a layer's phases end at barriers 8l + 1 .. 8l + 8
+    ok = gemm(Ly.qkv, g0 + 1) && gemm(Ly.o, g0 + 3) && gemm(Ly.gu, g0 + 5) && gemm(Ly.down, g0 + 7);
   }
-  if (ok) gemm(a.head);
+  if (ok) gemm(a.head, 8u * a.L + 1);
   return q;
 }
 

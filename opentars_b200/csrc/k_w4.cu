@@ -19,6 +19,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 
 #include "fp32.cuh"
 #include "mma.h"
@@ -43,14 +44,26 @@ __device__ __forceinline__ uint4 ldg_stream(const uint8_t* p) {
   return v;
 }
 
+// The dp4a kernels' layout of a group's mantissas: one 256-byte block of 16 chunks (chunk c:
+// k = 8c .. 8c + 7 as qh of k = 8c + 0, 2, 4, 6 | qh of k = 8c + 1, 3, 5, 7 | ql of the even k | ql
+// of the odd k, q = 256 qh + ql with qh = q >> 8 in [-64, 64] and ql = q & 255). Element k = 4 lane
+// + j lies in chunk c = lane / 2 at k = 8c + 4h + j with h = lane & 1: this lane's even / odd
+// elements are bytes 2h, 2h + 1 of the chunk's four words.
+__device__ __forceinline__ void put_dp4a_chunks(uint8_t* block, int lane, const int (&qv)[4]) {
+  uint8_t* dst = block + 16 * (lane >> 1) + 2 * (lane & 1);
+  auto hi = [](int q) { return (uint32_t)(uint8_t)(int8_t)(q >> 8); };
+  auto lo = [](int q) { return (uint32_t)(q & 0xFF); };
+  *reinterpret_cast<uint16_t*>(dst + 0) = (uint16_t)(hi(qv[0]) | hi(qv[2]) << 8);     // qh even
+  *reinterpret_cast<uint16_t*>(dst + 4) = (uint16_t)(hi(qv[1]) | hi(qv[3]) << 8);     // qh odd
+  *reinterpret_cast<uint16_t*>(dst + 8) = (uint16_t)(lo(qv[0]) | lo(qv[2]) << 8);     // ql even
+  *reinterpret_cast<uint16_t*>(dst + 12) = (uint16_t)(lo(qv[1]) | lo(qv[3]) << 8);    // ql odd
+}
+
 // Block-FP alignment of four (row, group) pairs p0 .. p0 + 3 (pairs >= total are not written) by
 // one warp, four elements of each group per lane (lane L: elements 4L .. 4L + 3). bits(p) gives
-// the lane's four fp32 bit patterns of pair p. The sink receives, per pair, the aligned mantissas
-// as one 256-byte block of 16 chunks (chunk c: k = 8c .. 8c + 7 as qh of k = 8c + 0, 2, 4, 6 | qh of
-// k = 8c + 1, 3, 5, 7 | ql of the even k | ql of the odd k, q = 256 qh + ql with qh = q >> 8 in
-// [-64, 64] and ql = q & 255), the group's scale bits and the sum of its mantissas:
-// sink.q(p) -> the block, sink.scale(p, bits), sink.sum(p, s). The four groups' shuffle
-// reductions overlap.
+// the lane's four fp32 bit patterns of pair p. The sink receives, per pair, each lane's four
+// aligned mantissas (sink.put(p, lane, q[4])), the group's scale bits (sink.scale(p, bits)) and
+// the sum of its mantissas (sink.sum(p, s)). The four groups' shuffle reductions overlap.
 template <class Bits, class Sink>
 __device__ __forceinline__ void align_quad(int p0, int total, Bits bits, Sink& sink) {
   const int lane = threadIdx.x & 31;
@@ -104,15 +117,7 @@ __device__ __forceinline__ void align_quad(int p0, int total, Bits bits, Sink& s
     qs[u] = qv[0] + qv[1] + qv[2] + qv[3];
     const int p = p0 + u;
     if (p < total) {
-      // element k = 4 lane + j: chunk c = lane / 2, k = 8c + 4h + j with h = lane & 1; this lane's
-      // even / odd elements are bytes 2h, 2h + 1 of the chunk's four words
-      uint8_t* dst = sink.q(p) + 16 * (lane >> 1) + 2 * (lane & 1);
-      auto hi = [](int q) { return (uint32_t)(uint8_t)(int8_t)(q >> 8); };
-      auto lo = [](int q) { return (uint32_t)(q & 0xFF); };
-      *reinterpret_cast<uint16_t*>(dst + 0) = (uint16_t)(hi(qv[0]) | hi(qv[2]) << 8);     // qh even
-      *reinterpret_cast<uint16_t*>(dst + 4) = (uint16_t)(hi(qv[1]) | hi(qv[3]) << 8);     // qh odd
-      *reinterpret_cast<uint16_t*>(dst + 8) = (uint16_t)(lo(qv[0]) | lo(qv[2]) << 8);     // ql even
-      *reinterpret_cast<uint16_t*>(dst + 12) = (uint16_t)(lo(qv[1]) | lo(qv[3]) << 8);    // ql odd
+      sink.put(p, lane, qv);
       if (lane == 0) {
         uint32_t sb = (uint32_t)min(max(eff - 13, 0), 255) << 23;
         if (emax[u] == 0) sb = 0;
@@ -140,7 +145,9 @@ struct SmemSink {
   uint32_t* sS;
   int* sSum;
   int G;
-  __device__ uint8_t* q(int p) const { return reinterpret_cast<uint8_t*>(sQ + ((p / G) * 64 + p % G) * kQStride); }
+  __device__ void put(int p, int lane, const int (&qv)[4]) const {
+    put_dp4a_chunks(reinterpret_cast<uint8_t*>(sQ + ((p / G) * 64 + p % G) * kQStride), lane, qv);
+  }
   __device__ void scale(int p, uint32_t v) const { sS[(p / G) * 64 + p % G] = v; }
   __device__ void sum(int p, int v) const { sSum[(p / G) * 64 + p % G] = v; }
 };
@@ -506,7 +513,9 @@ __host__ __device__ constexpr uint32_t w4_scratch_row(int G) { return (uint32_t)
 struct AlignSink {
   uint8_t* base;
   int G;
-  __device__ uint8_t* q(int p) const { return base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)(p % G) * 256; }
+  __device__ void put(int p, int lane, const int (&qv)[4]) const {
+    put_dp4a_chunks(base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)(p % G) * 256, lane, qv);
+  }
   __device__ void scale(int p, uint32_t v) const {
     reinterpret_cast<uint32_t*>(base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)G * 256)[p % G] = v;
   }
@@ -785,11 +794,12 @@ cudaError_t launch_w4(const W4Args& g, cudaStream_t st) {
 }
 }  // namespace
 
-// TARSCUDA_W4_LEGACY=1 keeps the streamed kernel without the pre-pass (for comparisons).
-bool w4_legacy() {
-  static const bool v = [] {
-    const char* e = getenv("TARSCUDA_W4_LEGACY");
-    return e && e[0] == '1';
+// TARSCUDA_W4_PATH=legacy keeps the streamed dp4a kernel that aligns in every block (for
+// comparisons); the default is the tiled kernel with the alignment pre-pass.
+int w4_path() {
+  static const int v = [] {
+    const char* e = getenv("TARSCUDA_W4_PATH");
+    return e && !strcmp(e, "legacy") ? 0 : 1;
   }();
   return v;
 }
@@ -798,7 +808,7 @@ bool w4_tiled_ok(const W4Args& g) {
   const int G = g.K / W4_GROUP;
   const int mb = g.M <= 1 ? 1 : (g.M <= 2 ? 2 : 4);
   return g.scratch && g.M >= 1 && g.M <= 4 && g.K % 256 == 0 && (uintptr_t)g.W % 16 == 0 &&
-         ((uintptr_t)g.scratch & 15) == 0 && w4t_smem(mb, G, 3) <= w4t_smem_cap(mb) && !w4_legacy();
+         ((uintptr_t)g.scratch & 15) == 0 && w4t_smem(mb, G, 3) <= w4t_smem_cap(mb) && w4_path() >= 1;
 }
 
 uint64_t w4_scratch_bytes(int M, int K) { return (uint64_t)M * w4_scratch_row(K / W4_GROUP); }

@@ -23,9 +23,10 @@ int mma_error_code();
 int* wait_error_flag();
 // The poll limit of the bounded waits for work (tc_set_spin_limit).
 uint32_t spin_limit();
-// A TMA map of a uint8 matrix [rows, cols] (row stride ld) in boxes of box_cols x box_rows, 128-byte
-// swizzle; false when the driver entry point is missing or an alignment rule fails.
+// A TMA map of a uint8 matrix [rows, cols] (row stride ld) in boxes of box_cols x box_rows, with the
+// 128-byte swizzle or dense rows; false when the driver entry point is missing or an alignment rule
+// fails.
 bool make_map_u8(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
-                 uint32_t box_rows);
+                 uint32_t box_rows, bool swizzle = true);
 
 }  // namespace tc

@@ -75,6 +75,8 @@ struct StepArgs {
   int* err;                         // the device word of bounded waits that gave up
   int* diag;                        // the first give-up: code, CTA, barrier count, detail
   uint64_t wait_ns, drain_ns;       // time limits of the waits for work / for copies in flight
+  int lead;                         // the producer streams a GEMM's weights from `lead` barriers
+                                    // before its phase on (large: as soon as ring slots free up)
   unsigned long long* trace;        // [0, 1024): CTA 0 leaving every barrier (0: the kernel's
                                     // start); from 1024: per barrier every CTA's arrival; or null
 };

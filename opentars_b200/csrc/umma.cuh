@@ -98,7 +98,6 @@ __device__ __forceinline__ uint64_t sdesc_k128(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-
 // D[tmem] (+)= A[smem] . B[smem]^T, int8 x int8 -> int32, issued by one thread.
 __device__ __forceinline__ void mma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
