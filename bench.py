@@ -403,13 +403,18 @@ def _row_blocks(n: int, cap: int = DESC_N_MAX) -> list[tuple[int, int]]:
     return [(c, min(n, c + q)) for c in range(0, n, q)]
 
 
-def build_gemm(world: int = 1, rank: int = 0, seed: int = 1234, ms=GEMM_M, shapes=GEMM_SHAPES):
+def build_gemm(world: int = 1, rank: int = 0, seed: int = 1234, ms=GEMM_M, shapes=GEMM_SHAPES, split=None):
     """Config 1 on one rank: activations ~N(0,1) quantised per row (a setup queue), int8 weights
     uniform in [-127, 127] with per-channel scales uniform in [1e-3, 1e-2] (seeded, the same full
-    operands on every rank); rank r owns output columns [r N / world, (r+1) N / world) of every
-    shape. The (6912, 1152) shape runs as two K blocks (4096 + 2816) sharing the scales, their
-    fp32 partial results added by an ELT descriptor. N above the descriptor's 16-bit field runs as
-    row blocks. Returns the image, both queues, the output region and per-descriptor metadata."""
+    operands on every rank). The shapes in `split` (default: those above one descriptor's N, the
+    151936-row vocabulary) are N-split: rank r owns output columns [r N / world, (r+1) N / world);
+    the others run whole on every rank (replicas: 3 - 20 MB of weights, not worth a collective).
+    The split shapes' outputs form one contiguous region per M, and their GEMMs come first in the
+    queue, one segment per M ("split"), before one segment of every replicated GEMM ("rest"): each
+    M's outputs can be all-gathered while the next segments compute. The (6912, 1152) shape runs as two K blocks (4096 + 2816) sharing the
+    scales, their fp32 partial results added by an ELT descriptor. N above the descriptor's 16-bit
+    field runs as row blocks. Returns the image, both queues, the output region, the segments and
+    per-descriptor metadata."""
     from opentars_b200 import contract as C
     from opentars_b200.program import Image, Linear
     rng = np.random.default_rng(seed)
@@ -418,9 +423,12 @@ def build_gemm(world: int = 1, rank: int = 0, seed: int = 1234, ms=GEMM_M, shape
     xs = {K: rng.normal(0, 1, (max(GEMM_M), K)).astype(np.float32)[:Mx] for K in Ks}   # row m: the same for any ms
     full = [(rng.integers(-127, 128, (N, K), dtype=np.int8), rng.uniform(1e-3, 1e-2, N).astype(np.float32))
             for K, N, _ in shapes]
-    for K, N, _ in shapes:
-        assert N % (16 * world) == 0, "every shape's N splits into 16-column multiples per rank"
-    nl = [N // world for _, N, _ in shapes]
+    if split is None:
+        split = {i for i, (_, N, _) in enumerate(shapes) if N > DESC_N_MAX}
+    for i, (K, N, _) in enumerate(shapes):
+        assert i not in split or N % (16 * world) == 0, "a split shape's N splits into 16-column multiples"
+    nl = [N // world if i in split else N for i, (_, N, _) in enumerate(shapes)]
+    own = [(rank * n if i in split else 0) for i, n in enumerate(nl)]      # first owned output column
     need = sum(5 * Mx * K + 4 * Mx + 512 for K in Ks) + sum(n * K + 4 * n + 512 for n, (K, _, _) in zip(nl, shapes))
     need += sum(4 * M * n * (2 if kb else 1) + 512 for M in ms for n, (_, _, kb) in zip(nl, shapes)) + (1 << 16)
     p = Image(need)
@@ -429,8 +437,8 @@ def build_gemm(world: int = 1, rank: int = 0, seed: int = 1234, ms=GEMM_M, shape
     _, q_setup, n_setup = p.finish()
     p.descs, p.queue_off = [], None
     lins = []
-    for (K, N, kb), (W, sc), n in zip(shapes, full, nl):
-        Wl, sl = W[rank * n:(rank + 1) * n], sc[rank * n:(rank + 1) * n]
+    for (K, N, kb), (W, sc), n, c0 in zip(shapes, full, nl, own):
+        Wl, sl = W[c0:c0 + n], sc[c0:c0 + n]
         s_off = p.store(sl)
         if kb:
             lins.append(("k", [Linear(p.store(np.ascontiguousarray(Wl[:, :kb]), "i1"), s_off, None, n, kb),
@@ -442,41 +450,64 @@ def build_gemm(world: int = 1, rank: int = 0, seed: int = 1234, ms=GEMM_M, shape
     # outputs: row-block-major for N above one descriptor block (the row stride field is 15 bits
     # of 16 bytes), as the model image lays out the vocabulary head's logits
     y0 = p.top
-    ys = {(M, i): [(c0, p.matrix(M, c1 - c0)) for c0, c1 in _row_blocks(n)] for M in ms for i, n in enumerate(nl)}
+    order = sorted(range(len(shapes)), key=lambda i: i not in split)          # split shapes first
+    ys = {}
+    for first in (True, False):
+        for M in ms:
+            for i in order:
+                if (i in split) == first:
+                    ys[(M, i)] = [(c0, p.matrix(M, c1 - c0)) for c0, c1 in _row_blocks(nl[i])]
     y1 = p.top
     meta = []                      # per GEMM queue descriptor: (M, shape index, ops, weight bytes) or None
-    for M in ms:
-        for i, ((K, N, kb), (kind, parts), n) in enumerate(zip(shapes, lins, nl)):
-            xq, xs_off = qv[K]
-            xq = xq.rows_at(0, M)
-            if kind == "n":
-                for (c0, lin), (_, y) in zip(parts, ys[(M, i)]):
-                    p.mm8(xq, xs_off, lin, y)
-                    meta.append((M, i, 2 * M * lin.n * K, lin.n * K))
-            else:
-                y = ys[(M, i)][0][1]
-                part = p.matrix(M, n)
-                p.mm8(xq.cols_at(0, kb), xs_off, parts[0], y)
-                meta.append((M, i, 2 * M * n * kb, n * kb))
-                p.mm8(xq.cols_at(kb, K - kb), xs_off, parts[1], part)
-                meta.append((M, i, 2 * M * n * (K - kb), n * (K - kb)))
-                p.elt(C.ELT_ADD, y, part, y)
-                meta.append(None)
+    segments = []                  # (M or None, "split" | "rest", first descriptor, count)
+    for first in (True, False):
+        for M in ms:
+            for i in order:
+                if (i in split) != first:
+                    continue
+                (K, N, kb), (kind, parts), n = shapes[i], lins[i], nl[i]
+                key = (M, "split") if first else (None, "rest")
+                if not segments or segments[-1][:2] != key:
+                    segments.append((*key, len(p.descs), 0))
+                xq, xs_off = qv[K]
+                xq = xq.rows_at(0, M)
+                if kind == "n":
+                    for (c0, lin), (_, y) in zip(parts, ys[(M, i)]):
+                        p.mm8(xq, xs_off, lin, y)
+                        meta.append((M, i, 2 * M * lin.n * K, lin.n * K))
+                else:
+                    y = ys[(M, i)][0][1]
+                    part = p.matrix(M, n)
+                    p.mm8(xq.cols_at(0, kb), xs_off, parts[0], y)
+                    meta.append((M, i, 2 * M * n * kb, n * kb))
+                    p.mm8(xq.cols_at(kb, K - kb), xs_off, parts[1], part)
+                    meta.append((M, i, 2 * M * n * (K - kb), n * (K - kb)))
+                    p.elt(C.ELT_ADD, y, part, y)
+                    meta.append(None)
+                M_, sg, first_d, _ = segments[-1]
+                segments[-1] = (M_, sg, first_d, len(p.descs) - first_d)
     ddr, q_main, n_main = p.finish()
+    split_regions = {}             # M -> (offset, bytes) of its split outputs (contiguous)
+    for M in ms:
+        blocks = [v for i in order if i in split for _, v in ys[(M, i)]]
+        if blocks:
+            split_regions[M] = (blocks[0].off, blocks[-1].off + blocks[-1].rows * blocks[-1].ld - blocks[0].off)
     x_first, x_last = min(v.off for v in xv.values()), max(v.off + v.rows * v.ld for v in xv.values())
     return dict(ddr=np.frombuffer(bytes(ddr), np.uint8).copy(), q_setup=q_setup, n_setup=n_setup, q_main=q_main,
                 n_main=n_main, y_region=(y0, y1 - y0), x_region=(x_first, x_last - x_first), ys=ys, nl=nl,
-                meta=meta, ms=ms, shapes=shapes, world=world,
-                ops=sum(2 * M * N * K for M in ms for K, N, _ in shapes))
+                meta=meta, ms=ms, shapes=shapes, world=world, split=split, segments=segments,
+                split_regions=split_regions, ops=sum(2 * M * N * K for M in ms for K, N, _ in shapes))
 
 
 def gemm_outputs(p: dict, gathered: list[np.ndarray]) -> dict:
-    """Per (M, shape) the full [M, N] fp32 output from every rank's copy of its output region."""
+    """Per (M, shape) the full [M, N] fp32 output from every rank's copy of its output region (a
+    split shape's columns from every rank in rank order, a replicated one's from rank 0)."""
     y0 = p["y_region"][0]
+    split = p.get("split", set(range(len(p["shapes"]))))
     out = {}
     for (M, i), blocks in p["ys"].items():
-        cols = [g[v.off - y0:v.off - y0 + v.rows * v.ld].view("<f4").reshape(M, -1) for g in gathered
-                for _, v in blocks]
+        cols = [g[v.off - y0:v.off - y0 + v.rows * v.ld].view("<f4").reshape(M, -1)
+                for g in (gathered if i in split else gathered[:1]) for _, v in blocks]
         out[(M, i)] = np.concatenate(cols, axis=1)
     return out
 
@@ -538,21 +569,52 @@ def run_gemm(a, world, rank, local) -> dict | None:
     dev.mem[:] = ddr
     dev.to_dev(0, len(ddr))
     ok = dev.run(p["q_setup"], p["n_setup"])[0]
-    g, st = dev.graph(p["q_main"], p["n_main"])
-    assert ok and g is not None and st.done, "the GEMM queue must capture"
-    kernels_per_step = check(L.tc_graph_kernels(g), dev.h, "graph_kernels")
+    assert ok, "the quantisation queue must run"
+    # one graph for the whole queue on one GPU; on N GPUs one per segment (each M's split
+    # vocabulary GEMM, then the replicated shapes), each M's outputs all-gathered after its segment
+    if world > 1:
+        segs = []
+        for M, kind, first, count in p["segments"]:
+            g, st = dev.graph(p["q_main"] + 64 * first, count)
+            assert g is not None and st.done, "every GEMM segment must capture"
+            segs.append((M, kind, g))
+    else:
+        g, st = dev.graph(p["q_main"], p["n_main"])
+        assert g is not None and st.done, "the GEMM queue must capture"
+        segs = [(None, "rest", g)]
+    kernels_per_step = sum(check(L.tc_graph_kernels(g), dev.h, "graph_kernels") for _, _, g in segs)
     stream = torch.cuda.ExternalStream(L.tc_stream(dev.h), device=local)
     y0, yn = p["y_region"]
     base = int(L.tc_device_ptr(dev.h))
     yt = torch.as_tensor(_DevBytes(base + y0, yn), device=f"cuda:{local}")
-    gath = torch.empty(world * yn, dtype=torch.uint8, device=f"cuda:{local}") if world > 1 else None
+    side = torch.cuda.Stream(device=local) if world > 1 else None
+    mine, gath = {}, {}
+    if world > 1:
+        for M, (s_off, s_nb) in p["split_regions"].items():
+            mine[M] = torch.as_tensor(_DevBytes(base + s_off, s_nb), device=f"cuda:{local}")
+            gath[M] = torch.empty(world * s_nb, dtype=torch.uint8, device=f"cuda:{local}")
+    gather_ms = []
 
-    def step():
-        check(L.tc_graph_launch(g, None), dev.h)
-        if world > 1:                               # N-split: every rank gets every output block
-            import torch.distributed as dist
-            with torch.cuda.stream(stream):
-                dist.all_gather_into_tensor(gath, yt)
+    def step(timed_gathers: bool = False):
+        """The segments in order; after each M's split segment its outputs are all-gathered on a
+        second stream (NCCL over NVLink) while the next segments compute."""
+        import torch.distributed as dist
+        for M, kind, g in segs:
+            check(L.tc_graph_launch(g, None), dev.h)
+            if world > 1 and kind == "split":
+                ev = torch.cuda.Event()
+                ev.record(stream)
+                side.wait_event(ev)
+                with torch.cuda.stream(side):
+                    if timed_gathers:
+                        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        g0.record(side)
+                    dist.all_gather_into_tensor(gath[M], mine[M])
+                    if timed_gathers:
+                        g1.record(side)
+                        gather_ms.append((g0, g1))
+        if world > 1:
+            stream.wait_stream(side)
 
     for _ in range(a.warmup):
         step()
@@ -569,11 +631,25 @@ def run_gemm(a, world, rank, local) -> dict | None:
     barrier(world)
     ms_max = max_over_ranks(ms, world)
     value = p["ops"] * a.steps / (ms_max / 1e3) / 1e12
+    collective = None
+    if world > 1:                                   # the all-gathers' own device time, one more step
+        step(timed_gathers=True)
+        check(L.tc_synchronize(dev.h), dev.h)
+        torch.cuda.synchronize(local)
+        g_ms = sum(g0.elapsed_time(g1) for g0, g1 in gather_ms)
+        collective = dict(op="all_gather (NCCL) of each M's vocabulary output blocks, on a second stream",
+                          bytes_per_rank_per_step=sum(nb for _, nb in p["split_regions"].values()),
+                          ms_per_step=round(max_over_ranks(g_ms, world), 4),
+                          share_of_step=round(max_over_ranks(g_ms, world) / (ms_max / a.steps), 3),
+                          note="overlapped with the replicated GEMMs; share = its time / the step's")
 
-    # parity: the full outputs (gathered over ranks) against the reference oracle's hashes
+    # parity: the full outputs (every rank's output region gathered) against the reference's hashes
     torch.cuda.synchronize(local)
     if world > 1:
-        regions = [gath[r * yn:(r + 1) * yn].cpu().numpy() for r in range(world)]
+        import torch.distributed as dist
+        allreg = torch.empty(world * yn, dtype=torch.uint8, device=f"cuda:{local}")
+        dist.all_gather_into_tensor(allreg, yt)
+        regions = [allreg[r * yn:(r + 1) * yn].cpu().numpy() for r in range(world)]
     else:
         regions = [yt.cpu().numpy()]
     fx = ROOT / "tests" / "golden" / "gemm_sweep.json"
@@ -654,11 +730,15 @@ def run_gemm(a, world, rank, local) -> dict | None:
         "data": "synthetic, seeded (config 1 distributions)",
         "config": dict(workload="config1_w8a8_gemm_sweep", M=list(GEMM_M), shapes=[list(s) for s in GEMM_SHAPES],
                        descriptors_per_step=p["n_main"],
-                       parallelism=f"N split over {world} GPUs + NCCL all-gather of the outputs" if world > 1
-                       else "1 GPU", l2="weights (170 MB per step) larger than L2, streamed once per step"),
+                       parallelism=(f"the 151936-row vocabulary GEMM N-split over {world} GPUs, its outputs "
+                                    f"all-gathered (NCCL, second stream) while the replicated shapes compute"
+                                    if world > 1 else "1 GPU"),
+                       l2="weights (170 MB per step) larger than L2, streamed once per step"),
         "roofline": roofline, "e2e": e2e, "gpu_launches": a.steps * kernels_per_step, "clocks": clk.summary(),
         "bit_exact_vs_reference": bit_exact,
     }
+    if collective:
+        out["collective"] = collective
     if world == 1 and not a.no_cpu:
         out["cpu_baseline"] = cpu_oracle_gemm(a.cpu_seconds, os.cpu_count() or 1)
     return out

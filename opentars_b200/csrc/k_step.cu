@@ -500,6 +500,7 @@ __device__ __noinline__ void norm_row(const StepArgs& a, int m, int kind, const 
           a1[0] += v[ks].x; a1[1] += v[ks].y; a1[2] += v[ks].z; a1[3] += v[ks].w;
         }
       }
+      if (st && j4 == tid) stamp(a, 706);               // the partial sums have arrived
       const float4 sc4 = *reinterpret_cast<const float4*>(scale + j);
       const float scs[4] = {sc4.x, sc4.y, sc4.z, sc4.w};
       float y[4];
@@ -508,8 +509,10 @@ __device__ __noinline__ void norm_row(const StepArgs& a, int m, int kind, const 
         const float sc = ftz(scs[u]);
         y[u] = two ? ftz(fadd(ftz(ep_fast(a0[u], sr, sc)), ftz(ep_fast(a1[u], sr, sc)))) : ep_fast(a0[u], sr, sc);
       }
+      if (st && j4 == tid) stamp(a, 707);               // the scales have arrived
       if (kind == 1) {
         asm volatile("cp.async.wait_group 0;" ::: "memory");    // this thread's residual quad
+        if (st && j4 == tid) stamp(a, 708);
         float x[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) x[u] = ftz(fadd(sres[j + u], y[u]));

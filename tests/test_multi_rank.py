@@ -1,8 +1,10 @@
 """The N > 1 host logic on CPU with two gloo ranks (no GPU): config 1's N-split. Each rank builds
-its shard of the sweep image (bench.build_gemm: every shape's output columns split over the ranks),
-computes its outputs with the oracle, the ranks all-gather their output regions, and the
-reassembled full outputs must hash to the reference golden Machine's (tests/golden/gemm_sweep.json,
-M = 4). Also the max-over-ranks time of bench.py."""
+its shard of the sweep image (bench.build_gemm: the vocabulary shape's output columns split over
+the ranks, the other shapes whole on every rank), computes its outputs with the oracle, the ranks
+all-gather their output regions, and the reassembled full outputs (split columns in rank order,
+replicated shapes from rank 0) must hash to the reference golden Machine's
+(tests/golden/gemm_sweep.json, M = 4). Also the max-over-ranks time of bench.py and the queue
+segments the overlapped all-gathers follow."""
 import json
 import os
 import socket
@@ -27,6 +29,8 @@ def _rank(rank: int, world: int, port: int, out):
         import bench
         from oracle.machine import OracleMachine
         p = bench.build_gemm(world, rank, ms=(4,))
+        assert p["split"] == {2} and [seg[:2] for seg in p["segments"]] == [(4, "split"), (None, "rest")]
+        assert p["nl"][2] == 151936 // world and p["nl"][0] == 3072
         o = OracleMachine(bytearray(p["ddr"].tobytes()))
         assert o.run_queue(p["q_setup"], p["n_setup"]).done
         assert o.run_queue(p["q_main"], p["n_main"]).done
