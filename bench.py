@@ -21,8 +21,11 @@ Workloads (synthetic seeded data with the configs' distri
         a step runs R units on distinct weight copies
   gemm  config 1: the W8A8 prefill GEMM sweep, M in {4, 16, 64, 256} x (K, N) in {(1024, 3072),
         (3072, 1024), (1024, 151936), (6912, 1152) as K blocks 4096 + 2816}; a step = every GEMM of
-        the sweep (one queue); value in int8 TOPS (2 M N K per GEMM); on N GPUs every shape's N is
-        split over the ranks and the outputs are all-gathered with NCCL (strong scaling)
+        the sweep (one queue); value in int8 TOPS (2 M N K per GEMM); on N GPUs the vocabulary
+        shape's N is split over the ranks (each keeps its output columns, as a greedy pick over a
+        shard would), the small shapes run whole on every rank (strong scaling); the split outputs
+        are all-gathered with NCCL after the step's GEMMs (--gemm-gather overlap: each M's while the
+        later segments compute; none: outside the timed steps)
 gemv / w4 value: algorithmic bytes of all units of all ranks / device time of the timed steps
 (max over ranks), in GB/s. e2e: the same metric through the board-runtime API (opentars_b200.board.Cuda:
 host writes x into pinned memory, to_dev, run, from_dev of y) timed on the host clock.
@@ -601,7 +604,7 @@ def run_gemm(a, world, rank, local) -> dict | None:
         import torch.distributed as dist
         for M, kind, g in segs:
             check(L.tc_graph_launch(g, None), dev.h)
-            if world > 1 and kind == "split":
+            if world > 1 and kind == "split" and a.gemm_gather == "overlap":
                 ev = torch.cuda.Event()
                 ev.record(stream)
                 side.wait_event(ev)
@@ -612,6 +615,16 @@ def run_gemm(a, world, rank, local) -> dict | None:
                     dist.all_gather_into_tensor(gath[M], mine[M])
                     if timed_gathers:
                         g1.record(side)
+                        gather_ms.append((g0, g1))
+        if world > 1 and a.gemm_gather == "after":   # every gather once all GEMMs are done
+            with torch.cuda.stream(stream):
+                for M in gath:
+                    if timed_gathers:
+                        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        g0.record(stream)
+                    dist.all_gather_into_tensor(gath[M], mine[M])
+                    if timed_gathers:
+                        g1.record(stream)
                         gather_ms.append((g0, g1))
         if world > 1:
             stream.wait_stream(side)
@@ -632,16 +645,18 @@ def run_gemm(a, world, rank, local) -> dict | None:
     ms_max = max_over_ranks(ms, world)
     value = p["ops"] * a.steps / (ms_max / 1e3) / 1e12
     collective = None
-    if world > 1:                                   # the all-gathers' own device time, one more step
+    if world > 1 and a.gemm_gather != "none":       # the all-gathers' own device time, one more step
         step(timed_gathers=True)
         check(L.tc_synchronize(dev.h), dev.h)
         torch.cuda.synchronize(local)
         g_ms = sum(g0.elapsed_time(g1) for g0, g1 in gather_ms)
-        collective = dict(op="all_gather (NCCL) of each M's vocabulary output blocks, on a second stream",
+        collective = dict(op="all_gather (NCCL) of each M's vocabulary output blocks, " +
+                          ("on a second stream while the later segments compute" if a.gemm_gather == "overlap"
+                           else "after every GEMM of the step"),
                           bytes_per_rank_per_step=sum(nb for _, nb in p["split_regions"].values()),
                           ms_per_step=round(max_over_ranks(g_ms, world), 4),
                           share_of_step=round(max_over_ranks(g_ms, world) / (ms_max / a.steps), 3),
-                          note="overlapped with the replicated GEMMs; share = its time / the step's")
+                          note="share = the gathers' device time / the step's")
 
     # parity: the full outputs (every rank's output region gathered) against the reference's hashes
     torch.cuda.synchronize(local)
@@ -730,8 +745,13 @@ def run_gemm(a, world, rank, local) -> dict | None:
         "data": "synthetic, seeded (config 1 distributions)",
         "config": dict(workload="config1_w8a8_gemm_sweep", M=list(GEMM_M), shapes=[list(s) for s in GEMM_SHAPES],
                        descriptors_per_step=p["n_main"],
-                       parallelism=(f"the 151936-row vocabulary GEMM N-split over {world} GPUs, its outputs "
-                                    f"all-gathered (NCCL, second stream) while the replicated shapes compute"
+                       parallelism=(f"the 151936-row vocabulary GEMM N-split over {world} GPUs (each keeps its "
+                                    f"output columns), the other shapes whole on every GPU"
+                                    + {"overlap": ", the split outputs all-gathered (NCCL, second stream) while "
+                                                  "the later segments compute",
+                                       "after": ", the split outputs all-gathered (NCCL) after the step's GEMMs",
+                                       "none": "; no collective in the timed steps (the outputs are gathered "
+                                               "afterwards for the parity check)"}[a.gemm_gather]
                                     if world > 1 else "1 GPU"),
                        l2="weights (170 MB per step) larger than L2, streamed once per step"),
         "roofline": roofline, "e2e": e2e, "gpu_launches": a.steps * kernels_per_step, "clocks": clk.summary(),
@@ -1054,6 +1074,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=3.0)
     ap.add_argument("--decode-only", action="store_true", help="decode: skip the config 0 / 2 keys")
+    ap.add_argument("--gemm-gather", default="after", choices=["after", "overlap", "none"],
+                    help="gemm on N GPUs: all-gather the vocabulary outputs after the step's GEMMs, "
+                         "overlapped with the later segments, or not in the timed steps")
     a = ap.parse_args()
     if a.steps is None:
         a.steps = CONTEXT - PROMPT_LEN if a.workload in DECODE_MODELS and a.impl == "ours" else 100

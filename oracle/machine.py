@@ -9,7 +9,7 @@ OracleMachine has the call surface of the reference's golden Machine (golden.py:
 from __future__ import annotations
 
 import bisect
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import numpy as np
 
