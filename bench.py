@@ -23,9 +23,9 @@ Workloads (synthetic seeded data with the configs' distri
         (3072, 1024), (1024, 151936), (6912, 1152) as K blocks 4096 + 2816}; a step = every GEMM of
         the sweep (one queue); value in int8 TOPS (2 M N K per GEMM); on N GPUs the vocabulary
         shape's N is split over the ranks (each keeps its output columns, as a greedy pick over a
-        shard would), the small shapes run whole on every rank (strong scaling); the split outputs
-        are all-gathered with NCCL after the step's GEMMs (--gemm-gather overlap: each M's while the
-        later segments compute; none: outside the timed steps)
+        shard would), the small shapes run whole on every rank (strong scaling); each M's split
+        outputs are all-gathered with NCCL while the later segments compute (--gemm-gather after:
+        once the step's GEMMs are done; none: outside the timed steps)
 gemv / w4 value: algorithmic bytes of all units of all ranks / device time of the timed steps
 (max over ranks), in GB/s. e2e: the same metric through the board-runtime API (opentars_b200.board.Cuda:
 host writes x into pinned memory, to_dev, run, from_dev of y) timed on the host clock.
@@ -1074,7 +1074,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=3.0)
     ap.add_argument("--decode-only", action="store_true", help="decode: skip the config 0 / 2 keys")
-    ap.add_argument("--gemm-gather", default="after", choices=["after", "overlap", "none"],
+    ap.add_argument("--gemm-gather", default="overlap", choices=["overlap", "after", "none"],
                     help="gemm on N GPUs: all-gather the vocabulary outputs after the step's GEMMs, "
                          "overlapped with the later segments, or not in the timed steps")
     a = ap.parse_args()
