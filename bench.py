@@ -1023,6 +1023,89 @@ def run_decode(a, world, rank, local) -> dict | None:
     return out
 
 
+# ----------------------------------------------------------------------------- Qwen3.5 vision tower
+VISION_SIDE = 448                 # one 448 x 448 image: 28 x 28 patches of 16, 784 patches, 196 tokens
+
+
+def run_vision(a, world, rank, local) -> dict | None:
+    """The Qwen3.5-0.8B vision tower (12 blocks of hidden 768, 12 heads, the 2 x 2 merger to 1024)
+    on one seeded 448 x 448 image per GPU: every linear is a W8A8 GEMM with M = 784 patch rows (the
+    tensor-core kernel), attention is FDOT / softmax descriptors. A step = one image through the
+    captured queue; value in merged visual tokens per second over all GPUs."""
+    import torch
+    os.environ["TC_DEVICE"] = str(local)
+    torch.cuda.set_device(local)
+    from opentars_b200 import vision as OV
+    from opentars_b200._lib import check, lib
+    from opentars_b200.board import Cuda
+    t_build = time.perf_counter()
+    cfg = OV.vision_config()
+    w = OV.random_vision(cfg, seed=0)
+    img = np.random.default_rng(11 + rank).normal(0, 1, (cfg.in_channels, VISION_SIDE, VISION_SIDE)).astype(np.float32)
+    px, grid = OV.patchify(img, cfg)
+    pos, rope = OV.position_embeddings(cfg, w, grid), OV.rope_table(cfg, grid)
+    tower = OV.VisionImage(cfg, w, patches_max=len(px), ddr_bytes=1 << 28)
+    out = tower.emit(px, pos, rope)
+    ddr, qa, qn = tower.p.finish()
+    build_s = time.perf_counter() - t_build
+    L = lib()
+    dev = Cuda(len(ddr), device=local, pinned=True)
+    dev.mem[:] = np.frombuffer(bytes(ddr), np.uint8)
+    dev.to_dev(0, len(ddr))
+    g, st = dev.graph(qa, qn)
+    assert g is not None and st.done, "the tower's queue must capture"
+    kernels_per_step = check(L.tc_graph_kernels(g), dev.h, "graph_kernels")
+    stream = torch.cuda.ExternalStream(L.tc_stream(dev.h), device=local)
+    for _ in range(a.warmup):
+        check(L.tc_graph_launch(g, None), dev.h)
+    check(L.tc_synchronize(dev.h), dev.h)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(stream)
+        for _ in range(a.steps):
+            check(L.tc_graph_launch(g, None), dev.h)
+        e1.record(stream)
+        check(L.tc_synchronize(dev.h), dev.h)
+    ms_max = max_over_ranks(e0.elapsed_time(e1), world)
+    ntok = out.rows
+    value = world * ntok * a.steps / (ms_max / 1e3)
+    # e2e: the image's patch, position and rotary rows (the first three tensors of the scratch)
+    # up from pinned memory, the tower, the merged tokens back
+    from opentars_b200.program import GRANULE
+    x_lo = tower.p.base + tower.scratch0
+    x_n = sum(-(-4 * a.size // GRANULE) * GRANULE for a in (px, pos, rope))
+    y_lo, y_n = tower.p.base + out.off, out.rows * out.ld
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        dev.to_dev(x_lo, x_n)
+        dev.run(qa, qn)
+        dev.from_dev(y_lo, y_n)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    gemm_ops = 2 * len(px) * sum(lin.n * lin.k for blk in tower.blocks for lin in
+                                 (blk["qkv"], blk["proj"], blk["fc1"], blk["fc2"])) + \
+        2 * ntok * (tower.m_fc1.n * tower.m_fc1.k + tower.m_fc2.n * tower.m_fc2.k) + 2 * len(px) * tower.pe.n * tower.pe.k
+    dev.close()
+    if rank != 0:
+        return None
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "visual tok/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(ms_max / a.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic: random-init tower weights (seeded, the reference's random_vision), a seeded image",
+        "config": dict(workload="f4_qwen35_0.8b_vision_tower", image=f"{VISION_SIDE}x{VISION_SIDE}", patches=len(px),
+                       merged_tokens=ntok, descriptors=qn, parallelism=f"one image per GPU x {world} GPUs",
+                       model_build_s=round(build_s, 1)),
+        "gemm_tops": round(gemm_ops * a.steps / (ms_max / 1e3) / 1e12, 2),
+        "e2e": dict(value=round(world * ntok * a.steps / e2e_s, 1), unit="visual tok/s", h2d_bytes_per_step=x_n,
+                    d2h_bytes_per_step=y_n, api="opentars_b200.board.Cuda: to_dev (patch rows), run, from_dev"),
+        "gpu_launches": a.steps * kernels_per_step, "clocks": clk.summary(),
+        "parity": "the tower's queue and tokens are pinned to the reference at a small config "
+                  "(tests/golden/vision.json, tests/test_gpu_vision.py)",
+    }
+
+
 def _engine_stream(eng) -> int:
     from opentars_b200.engine import lib as elib
     return elib().tc_engine_stream(eng.h)
@@ -1066,7 +1149,8 @@ def main():
     ap.add_argument("--steps", type=int, default=None,
                     help="timed steps (default: decode the whole context once, 236 steps; GEMV: 100)")
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS) + sorted(DECODE_MODELS) + ["gemm"])
+    ap.add_argument("--workload", default="decode",
+                    choices=sorted(WORKLOADS) + sorted(DECODE_MODELS) + ["gemm", "vision"])
     ap.add_argument("--batch", type=int, default=64, help="decode: sequences per GPU")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--units", type=int, default=0)
@@ -1093,7 +1177,9 @@ def main():
             print(json.dumps(out), flush=True)
         return
     world, rank, local = dist_setup(a.gpus)
-    if a.workload == "gemm":
+    if a.workload == "vision":
+        out = run_vision(a, world, rank, local)
+    elif a.workload == "gemm":
         out = run_gemm(a, world, rank, local)
     elif a.workload in DECODE_MODELS:
         out = run_decode(a, world, rank, local)
