@@ -486,23 +486,35 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
 // streams the weights through TMA tiles.
 //
 // Pre-pass (k_w4_align): one warp per four (row, group) pairs writes, per row m, the aligned
-// mantissas as [G][256 bytes] (align_quad's chunk layout), the group scale bits [G] and the
-// mantissa sums [G] into a scratch buffer. It lets the main kernel start at once
+// mantissas as [G][four 64-byte digit planes] and the group scale bits [G] into a scratch
+// buffer. It lets the main kernel start at once
 // (griddepcontrol.launch_dependents); the main kernel is launched with programmatic stream
 // serialisation and reads the scratch only after griddepcontrol.wait.
 //
-// Main kernel (k_gemv_w4t): a tile is 64 output columns (lane L: columns L and L + 32) x all of
-// K. Each block works on two tiles at a time; a tile belongs to a quad of four compute warps, warp
-// b adding the terms of the groups g = b (mod 4) - exactly the bank b of the reference's four-bank
-// sum, in increasing g - so no term crosses a warp until the four banks are combined. A producer
-// warp per quad fills the quad's ring with stages of four groups (two TMA boxes of 64 rows x 128
-// bytes, 128-byte swizzle: the lanes' 16-byte reads of one row chunk land on eight different bank
-// groups); the activation chunk a lane multiplies with is the same for all 32 lanes (a broadcast
-// read) and serves both of its columns. The fp16 group scales of the next tile are copied into
-// shared memory (4-byte cp.async, columns padded to an odd number of words) while the current
-// tile computes. Every wait is bounded; after a give-up the warps skip their remaining work but
-// keep the quad's barrier count, the producers stop issuing, and the block drains the copies in
-// flight.
+// The exact group dots run on the tensor cores' warp MMA (mma.sync m16n8k32, u8 x s8 -> s32; the
+// tcgen05 MMA needs operands in shared memory in its own layout and the accumulator in TMEM, which
+// a per-group scale would have to read back every 128 k). A operand: the nibbles made unsigned
+// (u = nibble ^ 8 = w + 8), the even nibbles of a word as four bytes, the odd ones as 16 u in the
+// high halves (a second accumulator, shifted back exactly). B operand: the pre-pass writes each
+// aligned mantissa q (|q| <= 16384) as q = lo + 256 hi, lo in [-128, 127], hi in [-64, 64], two
+// signed-byte planes in the same even / odd split, so B column n is plane n & 1 and
+// sum(w q) = C_lo + 256 C_hi - 8 sum(q), exact in int32. The MMA's k order is a permutation of the
+// group's k applied alike to A and B (lane t: words 4 t .. 4 t + 3 of the row and of the planes),
+// which leaves the integer sum unchanged.
+//
+// Main kernel (k_gemv_w4t): a tile is 64 output columns x all of K. Each block works on two
+// tiles at a time; a tile belongs to a quad of four compute warps, warp b adding the terms of the
+// groups g = b (mod 4) - exactly the bank b of the reference's four-bank sum, in increasing g - so
+// no term crosses a warp until the four banks are combined. A producer warp per quad fills the
+// quad's ring with stages of four groups (two TMA boxes of 64 rows x 128 bytes, 128-byte swizzle).
+// Per group a warp issues four MMAs per block of 16 columns (MMA rows i and i + 8 are tile rows
+// 16 cb + r(i) and + 8, r = 0 4 1 5 2 6 3 7, so that the eight lanes of each 16-byte read phase
+// hit eight different bank groups of the swizzled rows); B columns 2..7 repeat the two planes, so
+// every lane holds whole dots, and lane (i, t) owns the columns of block t (rows r(i), r(i) + 8).
+// The fp16 group scales of the next tile are copied into shared memory (4-byte cp.async, columns
+// padded to an odd number of words) while the current tile computes. Every wait is bounded;
+// after a give-up the warps skip their remaining work but keep the quad's barrier count, the
+// producers stop issuing, and the block drains the copies in flight.
 constexpr int kTQuads = 2, kTBanks = 4, kTCols = 64;
 constexpr int kTThreads = 32 * (kTQuads + kTQuads * kTBanks);      // 2 producer warps + 8 compute warps
 constexpr int kTStageB = 2 * kTCols * 128;                            // four groups of 64 columns
@@ -510,11 +522,27 @@ constexpr int kTMaxStages = 16;
 
 __host__ __device__ constexpr uint32_t w4_scratch_row(int G) { return (uint32_t)G * (256 + 8); }
 
+// A group's mantissas for the tensor-core dot: q = lo + 256 hi with lo in [-128, 127] and hi in
+// [-64, 64] (|q| <= 16384), both signed bytes, as two 128-byte planes (lo, hi). Within a plane, word
+// w of the group (k = 8 w .. 8 w + 7) is split like the weights' nibbles: its even k (8 w + 0, 2, 4,
+// 6) are the four bytes at 32 (w / 4) + 4 (w % 4), its odd k the four bytes 16 further on, so that
+// lane t of the MMA reads its four words' even and odd parts as two 16-byte loads.
+__device__ __forceinline__ void put_s8_planes(uint8_t* block, int lane, const int (&qv)[4]) {
+  const int w = lane >> 1, h = lane & 1;                  // elements k = 8 w + 4 h + j, j = 0..3
+  uint8_t* at = block + 32 * (w >> 2) + 4 * (w & 3) + 2 * h;
+  auto lo = [](int q) { return (uint32_t)(q & 0xFF); };
+  auto hi = [](int q) { return (uint32_t)(((q + 128) >> 8) & 0xFF); };
+  *reinterpret_cast<uint16_t*>(at) = (uint16_t)(lo(qv[0]) | lo(qv[2]) << 8);             // lo, even k
+  *reinterpret_cast<uint16_t*>(at + 16) = (uint16_t)(lo(qv[1]) | lo(qv[3]) << 8);        // lo, odd k
+  *reinterpret_cast<uint16_t*>(at + 128) = (uint16_t)(hi(qv[0]) | hi(qv[2]) << 8);       // hi, even k
+  *reinterpret_cast<uint16_t*>(at + 144) = (uint16_t)(hi(qv[1]) | hi(qv[3]) << 8);       // hi, odd k
+}
+
 struct AlignSink {
   uint8_t* base;
   int G;
   __device__ void put(int p, int lane, const int (&qv)[4]) const {
-    put_dp4a_chunks(base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)(p % G) * 256, lane, qv);
+    put_s8_planes(base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)(p % G) * 256, lane, qv);
   }
   __device__ void scale(int p, uint32_t v) const {
     reinterpret_cast<uint32_t*>(base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)G * 256)[p % G] = v;
@@ -523,6 +551,15 @@ struct AlignSink {
     reinterpret_cast<int*>(base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)G * 260)[p % G] = v;
   }
 };
+
+// D += A B for one m16n8k32 tile (A 16 x 32 unsigned bytes row-major, B 32 x 8 signed bytes
+// column-major, s32 D).
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
 __global__ void __launch_bounds__(256) k_w4_align(W4Args g, uint8_t* scratch) {
   griddep_launch();
@@ -597,6 +634,11 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(W4Args g, const __gri
   } else {
     const int cw = warp - kTQuads, q = cw / kTBanks, b = cw % kTBanks;
     const int qt = threadIdx.x - 32 * (kTQuads + q * kTBanks);     // thread of the quad, 0..127
+    // MMA lane roles: row i = lane / 4 (tile row ri = 0 4 1 5 2 6 3 7 of it), tg = lane % 4; the
+    // lane's result columns cA = 16 tg + ri and cA + 8
+    const int mr = lane >> 2, tg = lane & 3;
+    const int ri = (mr >> 1) | ((mr & 1) << 2), cA = 16 * tg + ri;
+    const uint32_t woff = 16u * ((4 * (b & 1) + tg) ^ ri);
     // the group scales of tile t into buffer `buf` of this quad (4-byte copies)
     auto fetch_scales = [&](int t, int buf) {
       uint8_t* dst = sscl + ((size_t)q * 2 + buf) * kTCols * sstr;
@@ -640,51 +682,56 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(W4Args g, const __gri
           s_stop = 1;
           continue;                                  // skip the work, keep the barrier count
         }
-        uint4 wv[2][4];
+        uint4 wa[4], wb[4];                                         // MMA rows i, i + 8 of each block
         if (gi < G) {
-          // group gi = 4 s + b: box b / 2, chunks 4 (b & 1) .. + 3 of rows lane and lane + 32, swizzled
-          const uint8_t* box = ring + ((size_t)q * stages + st) * kTStageB + (b >> 1) * (kTStageB / 2);
+          // group gi = 4 s + b: box b / 2, 16-byte piece 4 (b & 1) + tg of rows 16 cb + ri (+ 8), swizzled
+          const uint8_t* box = ring + ((size_t)q * stages + st) * kTStageB + (b >> 1) * (kTStageB / 2) + woff;
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              wv[h][j] = *reinterpret_cast<const uint4*>(box + (lane + 32 * h) * 128 + 16 * ((4 * (b & 1) + j) ^ (lane & 7)));
+          for (int cb = 0; cb < 4; ++cb) {
+            wa[cb] = *reinterpret_cast<const uint4*>(box + (16 * cb + ri) * 128);
+            wb[cb] = *reinterpret_cast<const uint4*>(box + (16 * cb + ri + 8) * 128);
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[q][st]);
         if (gi < G) {
           float ws[2];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) ws[h] = from_fp16(*reinterpret_cast<const uint16_t*>(scl + (lane + 32 * h) * sstr + 2 * gi));
+          for (int h = 0; h < 2; ++h) ws[h] = from_fp16(*reinterpret_cast<const uint16_t*>(scl + (cA + 8 * h) * sstr + 2 * gi));
 #pragma unroll
           for (int m = 0; m < MB; ++m) {
             if (m < g.M) {
               const uint8_t* arow = sact + (size_t)m * row_b;
-              const uint4* ac = reinterpret_cast<const uint4*>(arow + (size_t)gi * 256);
-              // both columns' exact dots, eight independent accumulator chains
-              int h0[2] = {0, 0}, h1[2] = {0, 0}, l0[2] = {0, 0}, l1[2] = {0, 0};
+              // B column n = plane n & 1 of row m (lo, hi; columns 2..7 repeat 0, 1): lane tg's words
+              // 4 tg .. 4 tg + 3, their even-k bytes (de) and odd-k bytes (dd)
+              const uint8_t* pl = arow + (size_t)gi * 256 + 128 * (mr & 1) + 32 * tg;
+              const uint4 de = *reinterpret_cast<const uint4*>(pl), dd = *reinterpret_cast<const uint4*>(pl + 16);
+              int pa[4], pb[4];
 #pragma unroll
-              for (int c = 0; c < 16; ++c) {
-                const uint4 qc = ac[c];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const uint4& v = wv[h][c >> 2];
-                  const uint32_t w = ((c & 3) == 0 ? v.x : (c & 3) == 1 ? v.y : (c & 3) == 2 ? v.z : v.w);
-                  const uint32_t ev = (w ^ 0x88888888u) & 0x0F0F0F0Fu;      // u = w + 8, k = 8c + 0, 2, 4, 6
-                  const uint32_t od = (w ^ 0x88888888u) & 0xF0F0F0F0u;      // 16 u, k = 8c + 1, 3, 5, 7
-                  h0[h] = dp4a_us(ev, qc.x, h0[h]);
-                  h1[h] = dp4a_us(od, qc.y, h1[h]);
-                  l0[h] = dp4a_uu(ev, qc.z, l0[h]);
-                  l1[h] = dp4a_uu(od, qc.w, l1[h]);
-                }
+              for (int cb = 0; cb < 4; ++cb) {
+                // u = nibble ^ 8 = w + 8: even nibbles as bytes, odd nibbles as 16 u in the high halves
+                const uint32_t xa[4] = {wa[cb].x ^ 0x88888888u, wa[cb].y ^ 0x88888888u, wa[cb].z ^ 0x88888888u,
+                                        wa[cb].w ^ 0x88888888u};
+                const uint32_t xb[4] = {wb[cb].x ^ 0x88888888u, wb[cb].y ^ 0x88888888u, wb[cb].z ^ 0x88888888u,
+                                        wb[cb].w ^ 0x88888888u};
+                constexpr uint32_t E = 0x0F0F0F0Fu, O = 0xF0F0F0F0u;
+                int ce[4] = {0, 0, 0, 0}, co[4] = {0, 0, 0, 0};
+                mma_u8s8(ce, xa[0] & E, xb[0] & E, xa[1] & E, xb[1] & E, de.x, de.y);
+                mma_u8s8(ce, xa[2] & E, xb[2] & E, xa[3] & E, xb[3] & E, de.z, de.w);
+                mma_u8s8(co, xa[0] & O, xb[0] & O, xa[1] & O, xb[1] & O, dd.x, dd.y);
+                mma_u8s8(co, xa[2] & O, xb[2] & O, xa[3] & O, xb[3] & O, dd.z, dd.w);
+                // sum(u q) of rows i, i + 8: columns 2 tg (lo) and 2 tg + 1 (hi); the odd sums are
+                // multiples of 16, shifted back exactly
+                pa[cb] = ce[0] + (co[0] >> 4) + 256 * (ce[1] + (co[1] >> 4));
+                pb[cb] = ce[2] + (co[2] >> 4) + 256 * (ce[3] + (co[3] >> 4));
               }
-              const int qsum = reinterpret_cast<const int*>(arow + (size_t)G * 260)[gi];
+              // dot = sum(w q) = sum(u q) - 8 sum(q), for the block this lane owns (cb = tg)
+              const int qs8 = 8 * reinterpret_cast<const int*>(arow + (size_t)G * 260)[gi];
+              const int dota = (tg == 0 ? pa[0] : tg == 1 ? pa[1] : tg == 2 ? pa[2] : pa[3]) - qs8;
+              const int dotb = (tg == 0 ? pb[0] : tg == 1 ? pb[1] : tg == 2 ? pb[2] : pb[3]) - qs8;
               const float xs = bf(reinterpret_cast<const uint32_t*>(arow + (size_t)G * 256)[gi]);
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int dot = 256 * (h0[h] + (h1[h] >> 4)) + (l0[h] + (l1[h] >> 4)) - 8 * qsum;
-                bank[h][m] = fadd_nc(bank[h][m], group_term(dot, ws[h], xs));
-              }
+              bank[0][m] = fadd_nc(bank[0][m], group_term(dota, ws[0], xs));
+              bank[1][m] = fadd_nc(bank[1][m], group_term(dotb, ws[1], xs));
             }
           }
         }
@@ -693,7 +740,7 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(W4Args g, const __gri
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int m = 0; m < MB; ++m) sbank[tl & 1][q][b][m][lane + 32 * h] = canon(bank[h][m]);
+        for (int m = 0; m < MB; ++m) sbank[tl & 1][q][b][m][cA + 8 * h] = canon(bank[h][m]);
       asm volatile("cp.async.wait_group 0;" ::: "memory");     // the next tile's scales have landed
       asm volatile("bar.sync %0, %1;" ::"r"(2 + q), "n"(32 * kTBanks) : "memory");
       if (b < 2 && !*(volatile int*)&s_stop) {                // warps 0 / 1: columns lane / lane + 32
