@@ -34,6 +34,7 @@ struct tc_machine {
   uint64_t scratch_size = 0;
   uint8_t* w4s = nullptr;                              // the W4A16 GEMV's aligned activation rows
   uint64_t w4s_size = 0;
+  uint64_t w4s_slice = 0;                              // bytes per W4 GEMV of one capture level
   std::string err;
   std::vector<cudaStream_t> lanes;                     // extra capture streams (one level's launches)
 };
@@ -110,10 +111,12 @@ void row_args(tc_machine* mc, const Desc& d, RowArgs* a) {
 }
 
 // Enqueues the kernels of one validated, in-range descriptor.
-cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream);
+// `w4_off`: where in the W4 row scratch a W4A16 GEMV keeps its aligned activation rows (W4 GEMVs
+// that may run at the same time use different slices).
+cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream, uint64_t w4_off = 0);
 cudaError_t launch(tc_machine* mc, const Desc& d) { return launch_on(mc, d, mc->stream); }
 
-cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream) {
+cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream, uint64_t w4_off) {
   uint8_t* B = mc->dev + d[F_BASE_ADDR];
   const Strides s = strides(d);
   const int op = d.op();
@@ -128,7 +131,7 @@ cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream) {
       g.Y = B + d[F_Y_OFF]; g.ldy = s.ldy;
       g.M = (int)d[F_M]; g.N = (int)d[F_N]; g.K = (int)d[F_K];
       g.act = d.act(); g.out = d.out(); g.out_scale = osc;
-      if (g.M <= 4 && ensure_w4s(mc, w4_scratch_bytes(g.M, g.K)) == cudaSuccess) g.scratch = mc->w4s;
+      if (g.M <= 4 && ensure_w4s(mc, w4_off + w4_scratch_bytes(g.M, g.K)) == cudaSuccess) g.scratch = mc->w4s + w4_off;
       return launch_gemm_w4a16(g, stream);
     }
     GemmArgs g{};
@@ -295,18 +298,28 @@ cudaError_t fetch_queue(tc_machine* m, uint64_t qaddr, uint32_t qlen, std::vecto
   return e;
 }
 
-// The conv gather scratch and the W4A16 row scratch a queue needs (so capture never allocates).
-std::pair<uint64_t, uint64_t> scratch_need(const std::vector<uint8_t>& q, uint32_t qlen, int core_id, int gemv_only) {
+// At most this many W4A16 GEMVs share a capture level (each with its own scratch slice); more
+// move to later levels.
+constexpr int kW4Slices = 8;
+
+// The conv gather scratch, and the W4A16 row scratch a queue needs as (slice bytes, slices), so
+// that capture never allocates.
+struct ScratchNeed { uint64_t conv, w4_slice; int w4_slices; };
+ScratchNeed scratch_need(const std::vector<uint8_t>& q, uint32_t qlen, int core_id, int gemv_only) {
   uint64_t conv = 0, w4 = 0;
+  int nw4 = 0;
   for (uint32_t i = 0; i < qlen; ++i) {
     const uint8_t* raw = q.data() + 64 * (size_t)i;
     Desc d;
     decode(raw, &d);
     if (validate(raw, d, core_id, gemv_only) != E_OK) continue;
     if (d.conv()) conv = std::max<uint64_t>(conv, d[F_M] * d[F_K]);
-    if (d.op() == OP_GEMM && d.w4() && d[F_M] <= 4) w4 = std::max<uint64_t>(w4, w4_scratch_bytes((int)d[F_M], (int)d[F_K]));
+    if (d.op() == OP_GEMM && d.w4() && d[F_M] <= 4) {
+      w4 = std::max<uint64_t>(w4, w4_scratch_bytes((int)d[F_M], (int)d[F_K]));
+      ++nw4;
+    }
   }
-  return {conv, w4};
+  return {conv, (w4 + 255) / 256 * 256, std::min(nw4, kW4Slices)};
 }
 // Captures a queue as a graph of dependency levels. Every descriptor's byte footprint (bounding
 // interval per input tensor and per output) is compared with those of the earlier descriptors; a
@@ -316,9 +329,9 @@ std::pair<uint64_t, uint64_t> scratch_need(const std::vector<uint8_t>& q, uint32
 // Each level runs after the previous one; inside a level the row ops, and (in a level of nothing
 // but GEMVs and row ops) the decode GEMVs of one kernel class, become one launch each (up to
 // kGroupMax entries), and the remaining descriptors and groups run side by side on the capture
-// streams. The conv gather buffer counts as a written
-// input of every conv. Independent work commutes, so the bytes written are those of the in-order
-// run.
+// streams. The conv gather buffer counts as a written input of every conv; the W4A16 GEMVs of a
+// level each align their activation rows into a scratch slice of their own (at most kW4Slices
+// per level). Independent work commutes, so the bytes written are those of the in-order run.
 struct Iv { u128 lo, hi; };
 
 bool hits(const std::vector<Iv>& a, const std::vector<Iv>& b) {
@@ -332,6 +345,7 @@ struct LevelNode {
   Desc d;
   std::vector<Iv> r, w;
   int level;
+  uint64_t w4_off = 0;                              // the W4A16 GEMV's scratch slice
 };
 
 int capture_grouped(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_id, int32_t gemv_only, tc_status* st,
@@ -345,6 +359,7 @@ int capture_grouped(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_i
     m->lanes.push_back(s);
   }
   std::vector<LevelNode> nodes;
+  std::vector<int> w4_in_level;                     // W4A16 GEMVs (scratch slices) per level
   int top = -1;                                     // highest level so far
   const u128 kScratch = ((u128)1) << 120;          // a key outside every image for the gather buffer
   int rc = execute(m, qaddr, qlen, core_id, gemv_only, st, contract_op, q, true,
@@ -356,12 +371,20 @@ int capture_grouped(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_i
     nd.w.push_back(Iv{fp.y.base, seg_end(fp.y)});
     if (fp.has_extra) nd.w.push_back(Iv{fp.extra.base, seg_end(fp.extra)});
     if (d.conv()) nd.w.push_back(Iv{kScratch, kScratch + 1});
-    if (d.op() == OP_GEMM && d.w4()) nd.w.push_back(Iv{kScratch + 2, kScratch + 3});   // the row scratch
     int lvl = 0;
     for (int k = (int)nodes.size() - 1; k >= 0 && lvl <= top; --k) {
       const LevelNode& o = nodes[k];
       if (o.level < lvl) continue;                  // cannot raise the level
       if (hits(o.w, nd.r) || hits(o.w, nd.w) || hits(o.r, nd.w)) lvl = o.level + 1;
+    }
+    if (d.op() == OP_GEMM && d.w4() && d[F_M] <= 4) {
+      // a scratch slice of its own in the level; a full level sends it to a later one
+      while ((int)w4_in_level.size() <= lvl) w4_in_level.push_back(0);
+      while (w4_in_level[lvl] >= kW4Slices) {
+        ++lvl;
+        if ((int)w4_in_level.size() <= lvl) w4_in_level.push_back(0);
+      }
+      nd.w4_off = (uint64_t)w4_in_level[lvl]++ * m->w4s_slice;
     }
     nd.level = lvl;
     top = std::max(top, lvl);
@@ -411,7 +434,8 @@ int capture_grouped(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_i
           continue;
         }
       }
-      units.push_back([m, d](cudaStream_t s) { return launch_on(m, d, s); });
+      const uint64_t w4_off = nodes[i].w4_off;
+      units.push_back([m, d, w4_off](cudaStream_t s) { return launch_on(m, d, s, w4_off); });
     }
     // the streaming GEMV group fills every SM's shared memory; beside other work in the level (a
     // tensor-core GEMM, a W4A16 GEMV, ...) the GEMVs run as launches of their own instead
@@ -510,9 +534,10 @@ int tc_queue_capture(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_
   std::vector<uint8_t> q;
   cudaError_t e = fetch_queue(m, qaddr, qlen, q);
   if (e == cudaSuccess) {
-    const auto need = scratch_need(q, qlen, core_id, gemv_only);
-    e = ensure_scratch(m, need.first);
-    if (e == cudaSuccess) e = ensure_w4s(m, need.second);
+    const ScratchNeed need = scratch_need(q, qlen, core_id, gemv_only);
+    m->w4s_slice = need.w4_slice;
+    e = ensure_scratch(m, need.conv);
+    if (e == cudaSuccess) e = ensure_w4s(m, need.w4_slice * (uint64_t)need.w4_slices);
   }
   if (e != cudaSuccess) return fail(m, "capture setup", e);
   tc_graph* g = new tc_graph();

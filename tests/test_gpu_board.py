@@ -165,3 +165,65 @@ def test_level_capture_batches_and_matches_oracle():
         assert L.tc_graph_times(gt, ms, n) == 3 and all(0 < ms[i] < 100 for i in range(3))
         L.tc_graph_destroy(gt)
         dev.close()
+
+
+def _w4_level_program(seed):
+    """Ten independent W4A16 GEMVs (M 1 - 4, K 256 - 2048; more than one level's scratch slices, so
+    two spill into the next level) and two that read earlier outputs as their activations."""
+    from oracle import contract as C
+    rng = np.random.default_rng(seed)
+    shapes = [(1, 1024, 640), (2, 512, 384), (3, 2048, 256), (4, 256, 512), (1, 2048, 1024), (2, 1024, 512),
+              (1, 256, 208), (4, 1024, 96), (3, 512, 320), (1, 1024, 64)]
+
+    def align(x, a=128):
+        return -(-x // a) * a
+    off, lay = 0x1000, []
+    for M, K, N in shapes:
+        x = off; w = align(x + 4 * M * K); s = align(w + N * K // 2); y = align(s + 2 * N * (K // 128))
+        off = align(y + 4 * M * N)
+        lay.append((x, w, s, y))
+    # two chained GEMVs: unit 4's output (M 1, N 1024) and unit 5's (M 2, N 512) as activations
+    chain = []
+    for src, N in ((4, 256), (5, 192)):
+        M, K = shapes[src][0], shapes[src][2]
+        w = off; s = align(w + N * K // 2); y = align(s + 2 * N * (K // 128)); off = align(y + 4 * M * N)
+        chain.append((lay[src][3], M, K, N, w, s, y))
+    qa = off
+    ddr = bytearray(align(qa + 64 * 16 + 4096, 4096))
+    base = dict(MAGIC=C.MAGIC, VERSION=C.VERSION, VALID=1)
+    ctrl = C.ctrl(C.QM_GROUP, a_dtype=C.DT_FP32, w_dtype=C.DT_INT4)
+    descs = []
+    for (M, K, N), (x, w, s, y) in zip(shapes, lay):
+        ddr[x:x + 4 * M * K] = rng.normal(0, 1, M * K).astype("<f4").tobytes()
+        ddr[w:w + N * K // 2] = rng.integers(0, 256, N * K // 2, dtype=np.uint8).tobytes()
+        ddr[s:s + 2 * N * (K // 128)] = rng.uniform(1e-3, 2e-2, N * (K // 128)).astype("<f2").tobytes()
+        descs.append(C.encode(dict(base, OPCODE=C.OP_GEMM, CTRL=ctrl, EPI=C.epi(), A_OFF=x, W_OFF=w, SCALE_OFF=s,
+                                   Y_OFF=y, M=M, N=N, K=K, GROUP_SIZE=128)))
+    for x, M, K, N, w, s, y in chain:
+        ddr[w:w + N * K // 2] = rng.integers(0, 256, N * K // 2, dtype=np.uint8).tobytes()
+        ddr[s:s + 2 * N * (K // 128)] = rng.uniform(1e-3, 2e-2, N * (K // 128)).astype("<f2").tobytes()
+        descs.append(C.encode(dict(base, OPCODE=C.OP_GEMM, CTRL=ctrl, EPI=C.epi(), A_OFF=x, W_OFF=w, SCALE_OFF=s,
+                                   Y_OFF=y, M=M, N=N, K=K, GROUP_SIZE=128)))
+    for i, d in enumerate(descs):
+        ddr[qa + 64 * i:qa + 64 * (i + 1)] = d
+    return ddr, qa, len(descs)
+
+
+def test_w4_gemvs_of_a_level_run_side_by_side():
+    """Independent W4A16 GEMVs share a capture level (each aligns its rows into its own scratch
+    slice, eight per level, the rest in the next level) and the graph writes the in-order oracle's
+    bytes, replay after replay; the two GEMVs that read earlier outputs still see them."""
+    from opentars_b200.board import Cuda
+    from oracle.machine import OracleMachine
+    for seed in (3, 4):
+        ddr, qa, n = _w4_level_program(seed)
+        o = OracleMachine(bytearray(ddr))
+        assert o.run_queue(qa, n).done
+        dev = Cuda(len(ddr))
+        dev.mem[:] = np.frombuffer(bytes(ddr), np.uint8)
+        dev.to_dev(0, len(ddr))
+        for _ in range(3):
+            assert dev.run(qa, n)[0]
+            dev.from_dev(0, len(ddr))
+            assert dev.mem.tobytes() == bytes(o.ddr), seed
+        dev.close()
