@@ -482,92 +482,75 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// The tiled W4A16 GEMV (M <= 4): a pre-pass aligns the activation rows once, the main kernel
-// streams the weights through TMA tiles.
+// The tiled W4A16 GEMV (M <= 4) for up to kW4GroupMax independent GEMVs of one row block and one K
+// at once: a pre-pass aligns every GEMV's activation rows, then one persistent kernel streams the
+// weights of all of them through TMA tiles.
 //
-// Pre-pass (k_w4_align): one warp per four (row, group) pairs writes, per row m, the aligned
-// mantissas as [G][four 64-byte digit planes] and the group scale bits [G] into a scratch
-// buffer. It lets the main kernel start at once
+// Pre-pass (k_w4_align): one warp per four (row, group) pairs of one GEMV writes, per row m, the
+// aligned mantissas as [G][256 bytes] (align_quad's chunk layout) followed by [G][scale bits,
+// mantissa sum] into that GEMV's scratch. It lets the main kernel start at once
 // (griddepcontrol.launch_dependents); the main kernel is launched with programmatic stream
-// serialisation and reads the scratch only after griddepcontrol.wait.
+// serialisation and copies from the scratch only after griddepcontrol.wait.
 //
-// The exact group dots run on the tensor cores' warp MMA (mma.sync m16n8k32, u8 x s8 -> s32; the
-// tcgen05 MMA needs operands in shared memory in its own layout and the accumulator in TMEM, which
-// a per-group scale would have to read back every 128 k). A operand: the nibbles made unsigned
-// (u = nibble ^ 8 = w + 8), the even nibbles of a word as four bytes, the odd ones as 16 u in the
-// high halves (a second accumulator, shifted back exactly). B operand: the pre-pass writes each
-// aligned mantissa q (|q| <= 16384) as q = lo + 256 hi, lo in [-128, 127], hi in [-64, 64], two
-// signed-byte planes in the same even / odd split, so B column n is plane n & 1 and
-// sum(w q) = C_lo + 256 C_hi - 8 sum(q), exact in int32. The MMA's k order is a permutation of the
-// group's k applied alike to A and B (lane t: words 4 t .. 4 t + 3 of the row and of the planes),
-// which leaves the integer sum unchanged.
-//
-// Main kernel (k_gemv_w4t): a tile is 64 output columns x all of K. Each block works on two
-// tiles at a time; a tile belongs to a quad of four compute warps, warp b adding the terms of the
-// groups g = b (mod 4) - exactly the bank b of the reference's four-bank sum, in increasing g - so
-// no term crosses a warp until the four banks are combined. A producer warp per quad fills the
-// quad's ring with stages of four groups (two TMA boxes of 64 rows x 128 bytes, 128-byte swizzle).
-// Per group a warp issues four MMAs per block of 16 columns (MMA rows i and i + 8 are tile rows
-// 16 cb + r(i) and + 8, r = 0 4 1 5 2 6 3 7, so that the eight lanes of each 16-byte read phase
-// hit eight different bank groups of the swizzled rows); B columns 2..7 repeat the two planes, so
-// every lane holds whole dots, and lane (i, t) owns the columns of block t (rows r(i), r(i) + 8).
-// The fp16 group scales of the next tile are copied into shared memory (4-byte cp.async, columns
-// padded to an odd number of words) while the current tile computes. Every wait is bounded;
-// after a give-up the warps skip their remaining work but keep the quad's barrier count, the
-// producers stop issuing, and the block drains the copies in flight.
+// Main kernel (k_gemv_w4t): a tile is 64 output columns of one GEMV x all of K; the tiles of the
+// group's GEMVs are numbered one after another and dealt to the quads in turn. Each block works on
+// two tiles at a time; a tile belongs to a quad of four compute warps, warp b adding the terms of
+// the groups g = b (mod 4) - exactly the bank b of the reference's four-bank sum, in increasing g
+// - so no term crosses a warp until the four banks are combined. A producer warp per quad fills
+// the quad's ring with stages of four groups: two TMA boxes of 64 rows x 128 bytes of weights
+// (128-byte swizzle: the lanes' 16-byte reads of one row chunk land on eight different bank
+// groups) and, per activation row, the four groups' aligned mantissas (1 KB) and scale / sum
+// words (32 bytes), bulk copies from the scratch. The weights of the first ring-full are requested
+// before the pre-pass has finished; their activation copies follow griddepcontrol.wait. The
+// activation chunk a lane multiplies with is the same for all 32 lanes (a broadcast read) and
+// serves both of its columns (lane L: columns L and L + 32). The fp16 group scales of the next tile
+// are copied into shared memory (4-byte cp.async, columns padded to an odd number of words) while
+// the current tile computes. Every wait is bounded; after a give-up the warps skip their remaining
+// work but keep the quad's barrier count, the producers stop issuing (the activation copies of
+// stages whose weights were requested are still issued), and the block drains the copies in
+// flight.
 constexpr int kTQuads = 2, kTBanks = 4, kTCols = 64;
 constexpr int kTThreads = 32 * (kTQuads + kTQuads * kTBanks);      // 2 producer warps + 8 compute warps
 constexpr int kTStageB = 2 * kTCols * 128;                            // four groups of 64 columns
+constexpr int kTActRow = 4 * 256 + 4 * 8;                             // a stage's mantissas + words, one row
 constexpr int kTMaxStages = 16;
 
+// Scratch bytes of one activation row: [G][256] mantissas, then [G][scale bits, sum].
 __host__ __device__ constexpr uint32_t w4_scratch_row(int G) { return (uint32_t)G * (256 + 8); }
-
-// A group's mantissas for the tensor-core dot: q = lo + 256 hi with lo in [-128, 127] and hi in
-// [-64, 64] (|q| <= 16384), both signed bytes, as two 128-byte planes (lo, hi). Within a plane, word
-// w of the group (k = 8 w .. 8 w + 7) is split like the weights' nibbles: its even k (8 w + 0, 2, 4,
-// 6) are the four bytes at 32 (w / 4) + 4 (w % 4), its odd k the four bytes 16 further on, so that
-// lane t of the MMA reads its four words' even and odd parts as two 16-byte loads.
-__device__ __forceinline__ void put_s8_planes(uint8_t* block, int lane, const int (&qv)[4]) {
-  const int w = lane >> 1, h = lane & 1;                  // elements k = 8 w + 4 h + j, j = 0..3
-  uint8_t* at = block + 32 * (w >> 2) + 4 * (w & 3) + 2 * h;
-  auto lo = [](int q) { return (uint32_t)(q & 0xFF); };
-  auto hi = [](int q) { return (uint32_t)(((q + 128) >> 8) & 0xFF); };
-  *reinterpret_cast<uint16_t*>(at) = (uint16_t)(lo(qv[0]) | lo(qv[2]) << 8);             // lo, even k
-  *reinterpret_cast<uint16_t*>(at + 16) = (uint16_t)(lo(qv[1]) | lo(qv[3]) << 8);        // lo, odd k
-  *reinterpret_cast<uint16_t*>(at + 128) = (uint16_t)(hi(qv[0]) | hi(qv[2]) << 8);       // hi, even k
-  *reinterpret_cast<uint16_t*>(at + 144) = (uint16_t)(hi(qv[1]) | hi(qv[3]) << 8);       // hi, odd k
-}
 
 struct AlignSink {
   uint8_t* base;
   int G;
+  __device__ uint8_t* row(int p) const { return base + (uint64_t)(p / G) * w4_scratch_row(G); }
   __device__ void put(int p, int lane, const int (&qv)[4]) const {
-    put_s8_planes(base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)(p % G) * 256, lane, qv);
+    put_dp4a_chunks(row(p) + (uint64_t)(p % G) * 256, lane, qv);
   }
   __device__ void scale(int p, uint32_t v) const {
-    reinterpret_cast<uint32_t*>(base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)G * 256)[p % G] = v;
+    reinterpret_cast<uint32_t*>(row(p) + (uint64_t)G * 256)[2 * (p % G)] = v;
   }
-  __device__ void sum(int p, int v) const {
-    reinterpret_cast<int*>(base + (uint64_t)(p / G) * w4_scratch_row(G) + (uint64_t)G * 260)[p % G] = v;
-  }
+  __device__ void sum(int p, int v) const { reinterpret_cast<int*>(row(p) + (uint64_t)G * 256)[2 * (p % G) + 1] = v; }
 };
 
-// D += A B for one m16n8k32 tile (A 16 x 32 unsigned bytes row-major, B 32 x 8 signed bytes
-// column-major, s32 D).
-__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
+// The GEMVs of one tiled launch (one row block, one K) and their tiles: GEMV j owns tiles
+// tile0[j] .. tile0[j + 1] - 1.
+struct W4Group {
+  W4Args e[kW4GroupMax];
+  int tile0[kW4GroupMax + 1];
+  int n;
+};
+struct W4Maps {
+  CUtensorMap m[kW4GroupMax];
+};
 
-__global__ void __launch_bounds__(256) k_w4_align(W4Args g, uint8_t* scratch) {
+// blockIdx.y: the GEMV; eight warps per block, four (row, group) pairs per warp.
+__global__ void __launch_bounds__(256) k_w4_align(const __grid_constant__ W4Group grp) {
   griddep_launch();
+  const W4Args& g = grp.e[blockIdx.y];
   const int G = g.K / W4_GROUP, total = g.M * G;
   const int lane = threadIdx.x & 31;
   const int p0 = 4 * (blockIdx.x * 8 + (threadIdx.x >> 5));
   if (p0 >= total) return;
-  AlignSink sink{scratch, G};
+  AlignSink sink{g.scratch, G};
   align_quad(p0, total, [&](int p) {
     const int m = p / G, gi = p - m * G;
     const uint8_t* row = g.A + (uint64_t)m * g.lda;
@@ -585,20 +568,22 @@ __global__ void __launch_bounds__(256) k_w4_align(W4Args g, uint8_t* scratch) {
 __host__ __device__ constexpr uint32_t w4t_scale_stride(int G) { return (uint32_t)((G + 1) / 2) % 2 ? 2 * G : 2 * G + 4; }
 
 template <int MB>
-__global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(W4Args g, const __grid_constant__ CUtensorMap wmap,
-                                                            const uint8_t* scratch, int stages) {
+__global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant__ W4Group grp,
+                                                            const __grid_constant__ W4Maps maps, int stages) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full[kTQuads][kTMaxStages], empty[kTQuads][kTMaxStages];
   __shared__ float sbank[2][kTQuads][kTBanks][MB][kTCols];
   __shared__ int s_stop, s_issued[kTQuads];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = g.K / W4_GROUP, nstage = (G + 3) / 4;
-  const int ntiles = (g.N + kTCols - 1) / kTCols;
+  const int G = grp.e[0].K / W4_GROUP, nstage = (G + 3) / 4;
+  const int ntiles = grp.tile0[grp.n];
   const uint32_t row_b = w4_scratch_row(G), sstr = w4t_scale_stride(G);
+  int* const err = grp.e[0].err;
+  const uint32_t spin = grp.e[0].spin;
   uint8_t* ring = smem;                                             // [quad][stage][2 boxes][64][128]
-  uint8_t* sact = smem + (size_t)kTQuads * stages * kTStageB;      // [MB][G][256] | bits [G] | sums [G]
-  uint8_t* sscl = sact + (size_t)MB * row_b;                        // [quad][2][64 columns][sstr]
+  uint8_t* aring = ring + (size_t)kTQuads * stages * kTStageB;     // [quad][stage][MB][kTActRow]
+  uint8_t* sscl = aring + (size_t)kTQuads * stages * MB * kTActRow; // [quad][2][64 columns][sstr]
   if (threadIdx.x == 0) {
     for (int q = 0; q < kTQuads; ++q)
       for (int i = 0; i < stages; ++i) {
@@ -609,65 +594,87 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(W4Args g, const __gri
     mbar_fence_init();
   }
   __syncthreads();
-  // tiles of quad q: blockIdx.x + gridDim.x * (q + kTQuads * j)
+  // the GEMV of global tile t
+  auto entry_of = [&](int t) {
+    int j = 0;
+    while (j + 1 < grp.n && t >= grp.tile0[j + 1]) ++j;
+    return j;
+  };
+  // tiles of quad q: blockIdx.x + gridDim.x * (q + kTQuads * i)
   if (warp < kTQuads) {
     if (lane == 0) {
-      const int q = warp;
+      const int q = warp, tstep = gridDim.x * kTQuads;
+      // the activation rows of stage s of tile t into ring slot st (after griddepcontrol.wait)
+      auto issue_acts = [&](int t, int s, int st) {
+        const W4Args& e = grp.e[entry_of(t)];
+        const bool two = 4 * s + 2 < G;
+        uint8_t* dst = aring + ((size_t)q * stages + st) * MB * kTActRow;
+        for (int m = 0; m < min(e.M, MB); ++m) {
+          const uint8_t* src = e.scratch + (uint64_t)m * row_b;
+          bulk_load(dst + m * kTActRow, src + (uint64_t)s * 1024, two ? 1024 : 512, &full[q][st]);
+          bulk_load(dst + m * kTActRow + 1024, src + (uint64_t)G * 256 + (uint64_t)s * 32, two ? 32 : 16, &full[q][st]);
+        }
+      };
+      // the first ring-full went out without its activations: wait for the pre-pass, then send them
+      auto catch_up = [&](int upto) {
+        griddep_wait();
+        int k = 0;
+        for (int t = blockIdx.x + gridDim.x * q; t < ntiles && k < upto; t += tstep)
+          for (int s = 0; s < nstage && k < upto; ++s, ++k) issue_acts(t, s, k);
+      };
       int it = 0;
-      for (int t = blockIdx.x + gridDim.x * q; t < ntiles; t += gridDim.x * kTQuads) {
+      bool waited = false;
+      for (int t = blockIdx.x + gridDim.x * q; t < ntiles; t += tstep) {
+        const int j = entry_of(t), lt = t - grp.tile0[j];
+        const int mrows = min(grp.e[j].M, MB);
         for (int s = 0; s < nstage; ++s, ++it) {
           const int st = it % stages;
-          if (*(volatile int*)&s_stop || !mbar_wait(&empty[q][st], ((it / stages) & 1) ^ 1, g.err, 13, g.spin)) {
+          if (!waited && it == stages) {
+            catch_up(stages);
+            waited = true;
+          }
+          if (*(volatile int*)&s_stop || !mbar_wait(&empty[q][st], ((it / stages) & 1) ^ 1, err, 13, spin)) {
             s_stop = 1;
             goto producer_done;
           }
           const bool two = 4 * s + 2 < G;
-          mbar_expect_tx(&full[q][st], two ? kTStageB : kTStageB / 2);
+          mbar_expect_tx(&full[q][st], (two ? kTStageB : kTStageB / 2) + mrows * (two ? 1024 + 32 : 512 + 16));
           uint8_t* dst = ring + ((size_t)q * stages + st) * kTStageB;
-          tma_load_2d(dst, &wmap, 256 * s, kTCols * t, &full[q][st]);
-          if (two) tma_load_2d(dst + kTStageB / 2, &wmap, 256 * s + 128, kTCols * t, &full[q][st]);
+          tma_load_2d(dst, &maps.m[j], 256 * s, kTCols * lt, &full[q][st]);
+          if (two) tma_load_2d(dst + kTStageB / 2, &maps.m[j], 256 * s + 128, kTCols * lt, &full[q][st]);
+          if (waited) issue_acts(t, s, st);
         }
       }
     producer_done:
+      if (!waited) catch_up(min(it, stages));     // every stage requested gets its activations
       s_issued[warp] = it;
     }
   } else {
     const int cw = warp - kTQuads, q = cw / kTBanks, b = cw % kTBanks;
     const int qt = threadIdx.x - 32 * (kTQuads + q * kTBanks);     // thread of the quad, 0..127
-    // MMA lane roles: row i = lane / 4 (tile row ri = 0 4 1 5 2 6 3 7 of it), tg = lane % 4; the
-    // lane's result columns cA = 16 tg + ri and cA + 8
-    const int mr = lane >> 2, tg = lane & 3;
-    const int ri = (mr >> 1) | ((mr & 1) << 2), cA = 16 * tg + ri;
-    const uint32_t woff = 16u * ((4 * (b & 1) + tg) ^ ri);
     // the group scales of tile t into buffer `buf` of this quad (4-byte copies)
     auto fetch_scales = [&](int t, int buf) {
+      const W4Args& e = grp.e[entry_of(t)];
+      const int lt = t - grp.tile0[entry_of(t)];
       uint8_t* dst = sscl + ((size_t)q * 2 + buf) * kTCols * sstr;
       const int words = kTCols * (G / 2);
       for (int w = qt; w < words; w += 32 * kTBanks) {
-        const int c = w / (G / 2), j = w - c * (G / 2);
-        const uint64_t n = (uint64_t)t * kTCols + c;
-        if (n < (uint64_t)g.N)
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst + c * sstr + 4 * j)),
-                       "l"(g.scale + 2 * (n * G + 2 * j))
+        const int c = w / (G / 2), jw = w - c * (G / 2);
+        const uint64_t n = (uint64_t)lt * kTCols + c;
+        if (n < (uint64_t)e.N)
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst + c * sstr + 4 * jw)),
+                       "l"(e.scale + 2 * (n * G + 2 * jw))
                        : "memory");
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    const int t0 = blockIdx.x + gridDim.x * q;
+    const int tstep = gridDim.x * kTQuads, t0 = blockIdx.x + gridDim.x * q;
     if (t0 < ntiles) fetch_scales(t0, 0);
-    // the aligned activation rows: written by the pre-pass
-    griddep_wait();
-    {
-      const uint32_t bytes = (uint32_t)MB * row_b;
-      const int mrows = min(MB, g.M);
-      for (uint32_t i = 16 * (threadIdx.x - 32 * kTQuads); i < bytes; i += 16 * (kTThreads - 32 * kTQuads))
-        if (i / row_b < (uint32_t)mrows) cp16(sact + i, scratch + i);
-      cp_wait_all();
-      asm volatile("bar.sync 1, %0;" ::"n"(32 * kTQuads * kTBanks) : "memory");
-    }
     int it = 0, tl = 0;
-    for (int t = t0; t < ntiles; t += gridDim.x * kTQuads, ++tl) {
-      if (t + gridDim.x * kTQuads < ntiles) fetch_scales(t + gridDim.x * kTQuads, (tl + 1) & 1);
+    for (int t = t0; t < ntiles; t += tstep, ++tl) {
+      const int j = entry_of(t), lt = t - grp.tile0[j];
+      const W4Args& e = grp.e[j];
+      if (t + tstep < ntiles) fetch_scales(t + tstep, (tl + 1) & 1);
       const uint8_t* scl = sscl + ((size_t)q * 2 + (tl & 1)) * kTCols * sstr;
       float bank[2][MB];
 #pragma unroll
@@ -676,84 +683,78 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(W4Args g, const __gri
         for (int m = 0; m < MB; ++m) bank[h][m] = 0.0f;
       for (int s = 0; s < nstage; ++s, ++it) {
         const int st = it % stages, gi = 4 * s + b;
-        bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[q][st], (it / stages) & 1, g.err, 14, g.spin);
+        bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[q][st], (it / stages) & 1, err, 14, spin);
         ok = __all_sync(0xFFFFFFFFu, ok);
         if (!ok) {
           s_stop = 1;
           continue;                                  // skip the work, keep the barrier count
         }
-        uint4 wa[4], wb[4];                                         // MMA rows i, i + 8 of each block
         if (gi < G) {
-          // group gi = 4 s + b: box b / 2, 16-byte piece 4 (b & 1) + tg of rows 16 cb + ri (+ 8), swizzled
-          const uint8_t* box = ring + ((size_t)q * stages + st) * kTStageB + (b >> 1) * (kTStageB / 2) + woff;
+          uint4 wv[2][4];
+          // group gi = 4 s + b: box b / 2, chunks 4 (b & 1) .. + 3 of rows lane and lane + 32, swizzled
+          const uint8_t* box = ring + ((size_t)q * stages + st) * kTStageB + (b >> 1) * (kTStageB / 2);
 #pragma unroll
-          for (int cb = 0; cb < 4; ++cb) {
-            wa[cb] = *reinterpret_cast<const uint4*>(box + (16 * cb + ri) * 128);
-            wb[cb] = *reinterpret_cast<const uint4*>(box + (16 * cb + ri + 8) * 128);
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[q][st]);
-        if (gi < G) {
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj)
+              wv[h][jj] = *reinterpret_cast<const uint4*>(box + (lane + 32 * h) * 128 + 16 * ((4 * (b & 1) + jj) ^ (lane & 7)));
           float ws[2];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) ws[h] = from_fp16(*reinterpret_cast<const uint16_t*>(scl + (cA + 8 * h) * sstr + 2 * gi));
+          for (int h = 0; h < 2; ++h) ws[h] = from_fp16(*reinterpret_cast<const uint16_t*>(scl + (lane + 32 * h) * sstr + 2 * gi));
+          const uint8_t* arow0 = aring + ((size_t)q * stages + st) * MB * kTActRow;
 #pragma unroll
           for (int m = 0; m < MB; ++m) {
-            if (m < g.M) {
-              const uint8_t* arow = sact + (size_t)m * row_b;
-              // B column n = plane n & 1 of row m (lo, hi; columns 2..7 repeat 0, 1): lane tg's words
-              // 4 tg .. 4 tg + 3, their even-k bytes (de) and odd-k bytes (dd)
-              const uint8_t* pl = arow + (size_t)gi * 256 + 128 * (mr & 1) + 32 * tg;
-              const uint4 de = *reinterpret_cast<const uint4*>(pl), dd = *reinterpret_cast<const uint4*>(pl + 16);
-              int pa[4], pb[4];
+            if (m < e.M) {
+              const uint8_t* arow = arow0 + m * kTActRow;
+              const uint4* ac = reinterpret_cast<const uint4*>(arow + b * 256);
+              // both columns' exact dots, eight independent accumulator chains
+              int h0[2] = {0, 0}, h1[2] = {0, 0}, l0[2] = {0, 0}, l1[2] = {0, 0};
 #pragma unroll
-              for (int cb = 0; cb < 4; ++cb) {
-                // u = nibble ^ 8 = w + 8: even nibbles as bytes, odd nibbles as 16 u in the high halves
-                const uint32_t xa[4] = {wa[cb].x ^ 0x88888888u, wa[cb].y ^ 0x88888888u, wa[cb].z ^ 0x88888888u,
-                                        wa[cb].w ^ 0x88888888u};
-                const uint32_t xb[4] = {wb[cb].x ^ 0x88888888u, wb[cb].y ^ 0x88888888u, wb[cb].z ^ 0x88888888u,
-                                        wb[cb].w ^ 0x88888888u};
-                constexpr uint32_t E = 0x0F0F0F0Fu, O = 0xF0F0F0F0u;
-                int ce[4] = {0, 0, 0, 0}, co[4] = {0, 0, 0, 0};
-                mma_u8s8(ce, xa[0] & E, xb[0] & E, xa[1] & E, xb[1] & E, de.x, de.y);
-                mma_u8s8(ce, xa[2] & E, xb[2] & E, xa[3] & E, xb[3] & E, de.z, de.w);
-                mma_u8s8(co, xa[0] & O, xb[0] & O, xa[1] & O, xb[1] & O, dd.x, dd.y);
-                mma_u8s8(co, xa[2] & O, xb[2] & O, xa[3] & O, xb[3] & O, dd.z, dd.w);
-                // sum(u q) of rows i, i + 8: columns 2 tg (lo) and 2 tg + 1 (hi); the odd sums are
-                // multiples of 16, shifted back exactly
-                pa[cb] = ce[0] + (co[0] >> 4) + 256 * (ce[1] + (co[1] >> 4));
-                pb[cb] = ce[2] + (co[2] >> 4) + 256 * (ce[3] + (co[3] >> 4));
+              for (int c = 0; c < 16; ++c) {
+                const uint4 qc = ac[c];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const uint4& v = wv[h][c >> 2];
+                  const uint32_t w = ((c & 3) == 0 ? v.x : (c & 3) == 1 ? v.y : (c & 3) == 2 ? v.z : v.w);
+                  const uint32_t ev = (w ^ 0x88888888u) & 0x0F0F0F0Fu;      // u = w + 8, k = 8c + 0, 2, 4, 6
+                  const uint32_t od = (w ^ 0x88888888u) & 0xF0F0F0F0u;      // 16 u, k = 8c + 1, 3, 5, 7
+                  h0[h] = dp4a_us(ev, qc.x, h0[h]);
+                  h1[h] = dp4a_us(od, qc.y, h1[h]);
+                  l0[h] = dp4a_uu(ev, qc.z, l0[h]);
+                  l1[h] = dp4a_uu(od, qc.w, l1[h]);
+                }
               }
-              // dot = sum(w q) = sum(u q) - 8 sum(q), for the block this lane owns (cb = tg)
-              const int qs8 = 8 * reinterpret_cast<const int*>(arow + (size_t)G * 260)[gi];
-              const int dota = (tg == 0 ? pa[0] : tg == 1 ? pa[1] : tg == 2 ? pa[2] : pa[3]) - qs8;
-              const int dotb = (tg == 0 ? pb[0] : tg == 1 ? pb[1] : tg == 2 ? pb[2] : pb[3]) - qs8;
-              const float xs = bf(reinterpret_cast<const uint32_t*>(arow + (size_t)G * 256)[gi]);
-              bank[0][m] = fadd_nc(bank[0][m], group_term(dota, ws[0], xs));
-              bank[1][m] = fadd_nc(bank[1][m], group_term(dotb, ws[1], xs));
+              const uint2 wd = *reinterpret_cast<const uint2*>(arow + 1024 + 8 * b);   // scale bits, sum
+              const float xs = bf(wd.x);
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int dot = 256 * (h0[h] + (h1[h] >> 4)) + (l0[h] + (l1[h] >> 4)) - 8 * (int)wd.y;
+                bank[h][m] = fadd_nc(bank[h][m], group_term(dot, ws[h], xs));
+              }
             }
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[q][st]);   // the stage's weights and rows are read
       }
       // the four banks of the tile's columns: (b0 + b1) + (b2 + b3)
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int m = 0; m < MB; ++m) sbank[tl & 1][q][b][m][cA + 8 * h] = canon(bank[h][m]);
+        for (int m = 0; m < MB; ++m) sbank[tl & 1][q][b][m][lane + 32 * h] = canon(bank[h][m]);
       asm volatile("cp.async.wait_group 0;" ::: "memory");     // the next tile's scales have landed
       asm volatile("bar.sync %0, %1;" ::"r"(2 + q), "n"(32 * kTBanks) : "memory");
       if (b < 2 && !*(volatile int*)&s_stop) {                // warps 0 / 1: columns lane / lane + 32
-        const int c = lane + 32 * b, n = t * kTCols + c;
-        if (n < g.N) {
+        const int c = lane + 32 * b, n = lt * kTCols + c;
+        if (n < e.N) {
 #pragma unroll
           for (int m = 0; m < MB; ++m) {
-            if (m < g.M) {
+            if (m < e.M) {
               const float(&bk)[kTBanks][MB][kTCols] = sbank[tl & 1][q];
               float y = fadd(fadd(bk[0][m][c], bk[1][m][c]), fadd(bk[2][m][c], bk[3][m][c]));
-              if (g.bias) y = fadd(y, ld_f32(g.bias + 4 * (uint64_t)n));
-              y = act_fn(y, g.act);
-              store_out(g.Y + (uint64_t)m * g.ldy, n, y, g.out, g.out_scale);
+              if (e.bias) y = fadd(y, ld_f32(e.bias + 4 * (uint64_t)n));
+              y = act_fn(y, e.act);
+              store_out(e.Y + (uint64_t)m * e.ldy, n, y, e.out, e.out_scale);
             }
           }
         }
@@ -775,33 +776,40 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(W4Args g, const __gri
 // per quad, the barriers).
 size_t w4t_smem_cap(int MB) { return 227 * 1024 - (size_t)4096 * MB - 1024; }
 
-// Shared memory of the tiled kernel for MB rows: the rings, the activation rows, the scales of two
-// tiles per quad, alignment slack.
+// Shared memory of the tiled kernel for MB rows: the weight and activation rings, the scales of
+// two tiles per quad, alignment slack.
 size_t w4t_smem(int MB, int G, int stages) {
-  return (size_t)kTQuads * stages * kTStageB + (size_t)MB * w4_scratch_row(G) +
-         (size_t)kTQuads * 2 * kTCols * w4t_scale_stride(G) + 1024;
+  return (size_t)kTQuads * stages * (kTStageB + (size_t)MB * kTActRow) + (size_t)kTQuads * 2 * kTCols * w4t_scale_stride(G) +
+         1024;
 }
 
 template <int MB>
-cudaError_t launch_w4t(const W4Args& g0, cudaStream_t st) {
-  W4Args g = g0;
-  g.err = wait_error_flag();
-  g.spin = spin_limit();
-  const int G = g.K / W4_GROUP;
+cudaError_t launch_w4t(const W4Args* gs, int n, cudaStream_t st) {
+  W4Group grp{};
+  W4Maps maps{};
+  grp.n = n;
+  grp.tile0[0] = 0;
+  for (int j = 0; j < n; ++j) {
+    grp.e[j] = gs[j];
+    grp.e[j].err = wait_error_flag();
+    grp.e[j].spin = spin_limit();
+    grp.tile0[j + 1] = grp.tile0[j] + (gs[j].N + kTCols - 1) / kTCols;
+    if (!make_map_u8(&maps.m[j], gs[j].W, gs[j].K / 2, gs[j].N, gs[j].K / 2, 128, kTCols)) return cudaErrorInvalidValue;
+  }
+  const int G = gs[0].K / W4_GROUP;
   int stages = kTMaxStages;
   while (stages > 2 && w4t_smem(MB, G, stages) > w4t_smem_cap(MB)) --stages;
   const size_t smem = w4t_smem(MB, G, stages);
-  CUtensorMap map;
-  if (!make_map_u8(&map, g.W, g.K / 2, g.N, g.K / 2, 128, kTCols)) return cudaErrorInvalidValue;
-  k_w4_align<<<(g.M * G + 31) / 32, 256, 0, st>>>(g, g.scratch);
+  int pre = 1;
+  for (int j = 0; j < n; ++j) pre = std::max(pre, (gs[j].M * G + 31) / 32);
+  k_w4_align<<<dim3(pre, n), 256, 0, st>>>(grp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   auto kern = k_gemv_w4t<MB>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  const int ntiles = (g.N + kTCols - 1) / kTCols;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(std::min((ntiles + kTQuads - 1) / kTQuads, 148));
+  cfg.gridDim = dim3(std::min((grp.tile0[n] + kTQuads - 1) / kTQuads, 148));
   cfg.blockDim = dim3(kTThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -810,7 +818,7 @@ cudaError_t launch_w4t(const W4Args& g0, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, g, map, (const uint8_t*)g.scratch, stages);
+  return cudaLaunchKernelEx(&cfg, kern, grp, maps, stages);
 }
 
 template <int MB>
@@ -860,12 +868,24 @@ bool w4_tiled_ok(const W4Args& g) {
 
 uint64_t w4_scratch_bytes(int M, int K) { return (uint64_t)M * w4_scratch_row(K / W4_GROUP); }
 
+int w4_group_class(const W4Args& g) {
+  if (!w4_tiled_ok(g)) return -1;
+  const int mb = g.M <= 1 ? 1 : (g.M <= 2 ? 2 : 4);
+  return mb << 16 | g.K / 256;
+}
+
+cudaError_t launch_w4_group(const W4Args* gs, int n, cudaStream_t st) {
+  if (n < 1 || n > kW4GroupMax) return cudaErrorInvalidValue;
+  const int cls = w4_group_class(gs[0]);
+  for (int j = 0; j < n; ++j)
+    if (cls < 0 || w4_group_class(gs[j]) != cls) return cudaErrorInvalidValue;
+  if (cls >> 16 == 1) return launch_w4t<1>(gs, n, st);
+  if (cls >> 16 == 2) return launch_w4t<2>(gs, n, st);
+  return launch_w4t<4>(gs, n, st);
+}
+
 cudaError_t launch_gemm_w4a16(const W4Args& g, cudaStream_t st) {
-  if (w4_tiled_ok(g)) {
-    if (g.M == 1) return launch_w4t<1>(g, st);
-    if (g.M == 2) return launch_w4t<2>(g, st);
-    return launch_w4t<4>(g, st);
-  }
+  if (w4_tiled_ok(g)) return launch_w4_group(&g, 1, st);
   // streamed through shared memory when the packed weights are 16-byte aligned (K % 256 == 0
   // makes every column a multiple of 128 bytes) and the ring fits next to the activations
   const size_t ring = (size_t)kW4Stages * kW4Cols * (g.K / 2);

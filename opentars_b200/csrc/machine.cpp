@@ -96,6 +96,22 @@ void gemm_args(tc_machine* mc, const Desc& d, GemmArgs* g) {
   g->M = (int)d[F_M]; g->N = (int)d[F_N]; g->K = (int)d[F_K];
   g->act = d.act(); g->out = d.out(); g->out_scale = f32(d[F_OUT_SCALE]);
 }
+// The kernel arguments of a W4A16 GEMV descriptor; its aligned rows go to the W4 scratch at
+// `w4_off` (nullptr scratch when it cannot be had: the kernels then align in every block).
+W4Args w4_args(tc_machine* mc, const Desc& d, uint64_t w4_off) {
+  uint8_t* B = mc->dev + d[F_BASE_ADDR];
+  const Strides s = strides(d);
+  W4Args g{};
+  g.A = B + d[F_A_OFF]; g.lda = s.lda;
+  g.a_bf16 = ((d[F_CTRL] >> 4) & 15) == DT_BF16;
+  g.W = B + d[F_W_OFF]; g.scale = B + d[F_SCALE_OFF];
+  g.bias = d.bias() ? B + d[F_BIAS_OFF] : nullptr;
+  g.Y = B + d[F_Y_OFF]; g.ldy = s.ldy;
+  g.M = (int)d[F_M]; g.N = (int)d[F_N]; g.K = (int)d[F_K];
+  g.act = d.act(); g.out = d.out(); g.out_scale = f32(d[F_OUT_SCALE]);
+  if (g.M <= 4 && ensure_w4s(mc, w4_off + w4_scratch_bytes(g.M, g.K)) == cudaSuccess) g.scratch = mc->w4s + w4_off;
+  return g;
+}
 void row_args(tc_machine* mc, const Desc& d, RowArgs* a) {
   uint8_t* B = mc->dev + d[F_BASE_ADDR];
   const Strides s = strides(d);
@@ -122,18 +138,7 @@ cudaError_t launch_on(tc_machine* mc, const Desc& d, cudaStream_t stream, uint64
   const int op = d.op();
   const float osc = f32(d[F_OUT_SCALE]);
   if (op == OP_GEMM || d.conv()) {
-    if (d.w4()) {
-      W4Args g{};
-      g.A = B + d[F_A_OFF]; g.lda = s.lda;
-      g.a_bf16 = ((d[F_CTRL] >> 4) & 15) == DT_BF16;
-      g.W = B + d[F_W_OFF]; g.scale = B + d[F_SCALE_OFF];
-      g.bias = d.bias() ? B + d[F_BIAS_OFF] : nullptr;
-      g.Y = B + d[F_Y_OFF]; g.ldy = s.ldy;
-      g.M = (int)d[F_M]; g.N = (int)d[F_N]; g.K = (int)d[F_K];
-      g.act = d.act(); g.out = d.out(); g.out_scale = osc;
-      if (g.M <= 4 && ensure_w4s(mc, w4_off + w4_scratch_bytes(g.M, g.K)) == cudaSuccess) g.scratch = mc->w4s + w4_off;
-      return launch_gemm_w4a16(g, stream);
-    }
+    if (d.w4()) return launch_gemm_w4a16(w4_args(mc, d, w4_off), stream);
     GemmArgs g{};
     gemm_args(mc, d, &g);
     if (d.conv()) {
@@ -298,9 +303,9 @@ cudaError_t fetch_queue(tc_machine* m, uint64_t qaddr, uint32_t qlen, std::vecto
   return e;
 }
 
-// At most this many W4A16 GEMVs share a capture level (each with its own scratch slice); more
-// move to later levels.
-constexpr int kW4Slices = 8;
+// At most this many W4A16 GEMVs share a capture level (each with its own scratch slice, and one
+// grouped launch for those of one class); more move to later levels.
+constexpr int kW4Slices = kW4GroupMax;
 
 // The conv gather scratch, and the W4A16 row scratch a queue needs as (slice bytes, slices), so
 // that capture never allocates.
@@ -331,7 +336,8 @@ ScratchNeed scratch_need(const std::vector<uint8_t>& q, uint32_t qlen, int core_
 // kGroupMax entries), and the remaining descriptors and groups run side by side on the capture
 // streams. The conv gather buffer counts as a written input of every conv; the W4A16 GEMVs of a
 // level each align their activation rows into a scratch slice of their own (at most kW4Slices
-// per level). Independent work commutes, so the bytes written are those of the in-order run.
+// per level) and those of one row block and K become one grouped launch. Independent work
+// commutes, so the bytes written are those of the in-order run.
 struct Iv { u128 lo, hi; };
 
 bool hits(const std::vector<Iv>& a, const std::vector<Iv>& b) {
@@ -413,10 +419,20 @@ int capture_grouped(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_i
     // the level's launch units: GEMV groups per class, row-op groups, single descriptors
     std::vector<std::function<cudaError_t(cudaStream_t)>> units;
     std::vector<std::pair<int, std::vector<GemmArgs>>> gemvs;   // class -> entries
+    std::vector<std::pair<int, std::vector<W4Args>>> w4g;      // W4A16 class -> entries
     std::vector<RowArgs> rows;
     for (int i : lv) {
       const Desc& d = nodes[i].d;
-      if (d.op() == OP_GEMM && !d.conv() && !d.w4()) {
+      if (d.op() == OP_GEMM && !d.conv() && d.w4()) {
+        const W4Args g = w4_args(m, d, nodes[i].w4_off);
+        const int cls = w4_group_class(g);
+        if (cls >= 0) {
+          auto it = std::find_if(w4g.begin(), w4g.end(), [&](const auto& c) { return c.first == cls; });
+          if (it == w4g.end()) w4g.push_back({cls, {g}});
+          else it->second.push_back(g);
+          continue;
+        }
+      } else if (d.op() == OP_GEMM && !d.conv()) {
         GemmArgs g{};
         gemm_args(m, d, &g);
         const int cls = gemv8_class(g);
@@ -460,6 +476,13 @@ int capture_grouped(tc_machine* m, uint64_t qaddr, uint32_t qlen, int32_t core_i
         units.push_back([grp](cudaStream_t s) { return launch_gemv8_group(*grp, s); });
       }
     }
+    // the tiled W4A16 GEMVs of one class: one pre-pass and one streaming launch per kW4GroupMax
+    for (const auto& c : w4g)
+      for (size_t j0 = 0; j0 < c.second.size(); j0 += kW4GroupMax) {
+        auto grp = std::make_shared<std::vector<W4Args>>(
+            c.second.begin() + j0, c.second.begin() + std::min(c.second.size(), j0 + kW4GroupMax));
+        units.push_back([grp](cudaStream_t s) { return launch_w4_group(grp->data(), (int)grp->size(), s); });
+      }
     for (size_t j0 = 0; j0 < rows.size(); j0 += kGroupMax) {
       const int n = (int)std::min<size_t>(kGroupMax, rows.size() - j0);
       if (n == 1) {

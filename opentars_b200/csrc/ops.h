@@ -62,6 +62,12 @@ struct W4Args {
 cudaError_t launch_gemm_w4a16(const W4Args& g, cudaStream_t st);
 // Scratch the tiled W4A16 GEMV needs for M rows of K (16-byte aligned).
 uint64_t w4_scratch_bytes(int M, int K);
+// Up to kW4GroupMax independent W4A16 GEMVs as one pre-pass and one tiled launch; `w4_group_class`
+// is the key of GEMVs that may share a launch (the same row block and K), or -1 when the tiled
+// kernel does not take the GEMV (each entry then needs a launch of its own).
+constexpr int kW4GroupMax = 8;
+int w4_group_class(const W4Args& g);
+cudaError_t launch_w4_group(const W4Args* gs, int n, cudaStream_t st);
 
 // conv: the NHWC int8 image gathered into [OH*OW, KH*KW*Cin] rows (zero padding), golden.py:282-293
 struct Im2colArgs {
