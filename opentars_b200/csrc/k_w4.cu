@@ -518,12 +518,38 @@ constexpr int kTMaxStages = 16;
 // Scratch bytes of one activation row: [G][256] mantissas, then [G][scale bits, sum].
 __host__ __device__ constexpr uint32_t w4_scratch_row(int G) { return (uint32_t)G * (256 + 8); }
 
+// A group's mantissas for the tensor-core dot: q = lo + 256 hi with lo in [-128, 127] and hi in
+// [-64, 64] (|q| <= 16384), both signed bytes. Word w of the group (k = 8 w .. 8 w + 7) is split
+// like the weights' nibbles: the bytes of its even k (8 w + 0, 2, 4, 6) lie at 64 p + 4 w of the
+// 256-byte block (p = 0 for lo, 1 for hi), those of its odd k 128 bytes further on - so MMA lane t
+// reads its four words' even (odd) parts of plane p as one 16-byte load at 64 p + 16 t (+ 128),
+// and the eight lanes of a load phase read 128 contiguous bytes.
+__device__ __forceinline__ void put_s8_planes(uint8_t* block, int lane, const int (&qv)[4]) {
+  const int w = lane >> 1, h = lane & 1;                  // elements k = 8 w + 4 h + j, j = 0..3
+  uint8_t* at = block + 4 * w + 2 * h;
+  auto lo = [](int q) { return (uint32_t)(q & 0xFF); };
+  auto hi = [](int q) { return (uint32_t)(((q + 128) >> 8) & 0xFF); };
+  *reinterpret_cast<uint16_t*>(at) = (uint16_t)(lo(qv[0]) | lo(qv[2]) << 8);           // lo, even k
+  *reinterpret_cast<uint16_t*>(at + 128) = (uint16_t)(lo(qv[1]) | lo(qv[3]) << 8);     // lo, odd k
+  *reinterpret_cast<uint16_t*>(at + 64) = (uint16_t)(hi(qv[0]) | hi(qv[2]) << 8);      // hi, even k
+  *reinterpret_cast<uint16_t*>(at + 192) = (uint16_t)(hi(qv[1]) | hi(qv[3]) << 8);     // hi, odd k
+}
+
+// D += A B for one m16n8k32 tile (A 16 x 32 unsigned bytes row-major, B 32 x 8 signed bytes
+// column-major, s32 D).
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 struct AlignSink {
   uint8_t* base;
   int G;
   __device__ uint8_t* row(int p) const { return base + (uint64_t)(p / G) * w4_scratch_row(G); }
   __device__ void put(int p, int lane, const int (&qv)[4]) const {
-    put_dp4a_chunks(row(p) + (uint64_t)(p % G) * 256, lane, qv);
+    put_s8_planes(row(p) + (uint64_t)(p % G) * 256, lane, qv);
   }
   __device__ void scale(int p, uint32_t v) const {
     reinterpret_cast<uint32_t*>(row(p) + (uint64_t)G * 256)[2 * (p % G)] = v;
@@ -652,6 +678,11 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
   } else {
     const int cw = warp - kTQuads, q = cw / kTBanks, b = cw % kTBanks;
     const int qt = threadIdx.x - 32 * (kTQuads + q * kTBanks);     // thread of the quad, 0..127
+    // MMA lane roles: row i = lane / 4 (tile row ri = 0 4 1 5 2 6 3 7 of it), tg = lane % 4; the
+    // lane's result columns cA = 16 tg + ri and cA + 8
+    const int mr = lane >> 2, tg = lane & 3;
+    const int ri = (mr >> 1) | ((mr & 1) << 2), cA = 16 * tg + ri;
+    const uint32_t woff = 16u * ((4 * (b & 1) + tg) ^ ri);
     // the group scales of tile t into buffer `buf` of this quad (4-byte copies)
     auto fetch_scales = [&](int t, int buf) {
       const W4Args& e = grp.e[entry_of(t)];
@@ -690,47 +721,53 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
           continue;                                  // skip the work, keep the barrier count
         }
         if (gi < G) {
-          uint4 wv[2][4];
-          // group gi = 4 s + b: box b / 2, chunks 4 (b & 1) .. + 3 of rows lane and lane + 32, swizzled
-          const uint8_t* box = ring + ((size_t)q * stages + st) * kTStageB + (b >> 1) * (kTStageB / 2);
+          uint4 wa[4], wb[4];                                       // MMA rows i, i + 8 of each block
+          // group gi = 4 s + b: box b / 2, 16-byte piece 4 (b & 1) + tg of rows 16 cb + ri (+ 8), swizzled
+          const uint8_t* box = ring + ((size_t)q * stages + st) * kTStageB + (b >> 1) * (kTStageB / 2) + woff;
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj)
-              wv[h][jj] = *reinterpret_cast<const uint4*>(box + (lane + 32 * h) * 128 + 16 * ((4 * (b & 1) + jj) ^ (lane & 7)));
+          for (int cb = 0; cb < 4; ++cb) {
+            wa[cb] = *reinterpret_cast<const uint4*>(box + (16 * cb + ri) * 128);
+            wb[cb] = *reinterpret_cast<const uint4*>(box + (16 * cb + ri + 8) * 128);
+          }
           float ws[2];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) ws[h] = from_fp16(*reinterpret_cast<const uint16_t*>(scl + (lane + 32 * h) * sstr + 2 * gi));
+          for (int h = 0; h < 2; ++h) ws[h] = from_fp16(*reinterpret_cast<const uint16_t*>(scl + (cA + 8 * h) * sstr + 2 * gi));
           const uint8_t* arow0 = aring + ((size_t)q * stages + st) * MB * kTActRow;
 #pragma unroll
           for (int m = 0; m < MB; ++m) {
             if (m < e.M) {
               const uint8_t* arow = arow0 + m * kTActRow;
-              const uint4* ac = reinterpret_cast<const uint4*>(arow + b * 256);
-              // both columns' exact dots, eight independent accumulator chains
-              int h0[2] = {0, 0}, h1[2] = {0, 0}, l0[2] = {0, 0}, l1[2] = {0, 0};
+              // B column n = plane n & 1 (lo, hi; columns 2..7 repeat 0, 1): the even-k bytes (de)
+              // and odd-k bytes (dd) of lane tg's words 4 tg .. 4 tg + 3
+              const uint8_t* pl = arow + b * 256 + 64 * (mr & 1) + 16 * tg;
+              const uint4 de = *reinterpret_cast<const uint4*>(pl), dd = *reinterpret_cast<const uint4*>(pl + 128);
+              int pa[4], pb[4];
 #pragma unroll
-              for (int c = 0; c < 16; ++c) {
-                const uint4 qc = ac[c];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const uint4& v = wv[h][c >> 2];
-                  const uint32_t w = ((c & 3) == 0 ? v.x : (c & 3) == 1 ? v.y : (c & 3) == 2 ? v.z : v.w);
-                  const uint32_t ev = (w ^ 0x88888888u) & 0x0F0F0F0Fu;      // u = w + 8, k = 8c + 0, 2, 4, 6
-                  const uint32_t od = (w ^ 0x88888888u) & 0xF0F0F0F0u;      // 16 u, k = 8c + 1, 3, 5, 7
-                  h0[h] = dp4a_us(ev, qc.x, h0[h]);
-                  h1[h] = dp4a_us(od, qc.y, h1[h]);
-                  l0[h] = dp4a_uu(ev, qc.z, l0[h]);
-                  l1[h] = dp4a_uu(od, qc.w, l1[h]);
-                }
+              for (int cb = 0; cb < 4; ++cb) {
+                // u = nibble ^ 8 = w + 8: even nibbles as bytes, odd nibbles as 16 u in the high halves
+                const uint32_t xa[4] = {wa[cb].x ^ 0x88888888u, wa[cb].y ^ 0x88888888u, wa[cb].z ^ 0x88888888u,
+                                        wa[cb].w ^ 0x88888888u};
+                const uint32_t xb[4] = {wb[cb].x ^ 0x88888888u, wb[cb].y ^ 0x88888888u, wb[cb].z ^ 0x88888888u,
+                                        wb[cb].w ^ 0x88888888u};
+                constexpr uint32_t E = 0x0F0F0F0Fu, O = 0xF0F0F0F0u;
+                int ce[4] = {0, 0, 0, 0}, co[4] = {0, 0, 0, 0};
+                mma_u8s8(ce, xa[0] & E, xb[0] & E, xa[1] & E, xb[1] & E, de.x, de.y);
+                mma_u8s8(ce, xa[2] & E, xb[2] & E, xa[3] & E, xb[3] & E, de.z, de.w);
+                mma_u8s8(co, xa[0] & O, xb[0] & O, xa[1] & O, xb[1] & O, dd.x, dd.y);
+                mma_u8s8(co, xa[2] & O, xb[2] & O, xa[3] & O, xb[3] & O, dd.z, dd.w);
+                // sum(u q) of rows i, i + 8: columns 2 tg (lo) and 2 tg + 1 (hi); the odd sums are
+                // multiples of 16, shifted back exactly
+                pa[cb] = ce[0] + (co[0] >> 4) + 256 * (ce[1] + (co[1] >> 4));
+                pb[cb] = ce[2] + (co[2] >> 4) + 256 * (ce[3] + (co[3] >> 4));
               }
               const uint2 wd = *reinterpret_cast<const uint2*>(arow + 1024 + 8 * b);   // scale bits, sum
               const float xs = bf(wd.x);
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int dot = 256 * (h0[h] + (h1[h] >> 4)) + (l0[h] + (l1[h] >> 4)) - 8 * (int)wd.y;
-                bank[h][m] = fadd_nc(bank[h][m], group_term(dot, ws[h], xs));
-              }
+              // dot = sum(w q) = sum(u q) - 8 sum(q), for the block this lane owns (cb = tg)
+              const int qs8 = 8 * (int)wd.y;
+              const int dota = (tg == 0 ? pa[0] : tg == 1 ? pa[1] : tg == 2 ? pa[2] : pa[3]) - qs8;
+              const int dotb = (tg == 0 ? pb[0] : tg == 1 ? pb[1] : tg == 2 ? pb[2] : pb[3]) - qs8;
+              bank[0][m] = fadd_nc(bank[0][m], group_term(dota, ws[0], xs));
+              bank[1][m] = fadd_nc(bank[1][m], group_term(dotb, ws[1], xs));
             }
           }
         }
@@ -741,7 +778,7 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int m = 0; m < MB; ++m) sbank[tl & 1][q][b][m][lane + 32 * h] = canon(bank[h][m]);
+        for (int m = 0; m < MB; ++m) sbank[tl & 1][q][b][m][cA + 8 * h] = canon(bank[h][m]);
       asm volatile("cp.async.wait_group 0;" ::: "memory");     // the next tile's scales have landed
       asm volatile("bar.sync %0, %1;" ::"r"(2 + q), "n"(32 * kTBanks) : "memory");
       if (b < 2 && !*(volatile int*)&s_stop) {                // warps 0 / 1: columns lane / lane + 32
