@@ -544,6 +544,29 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D = A B (zero accumulator) for one m16n8k32 tile.
+__device__ __forceinline__ void mma_u8s8_first(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+               : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+// u = nibble ^ 8 of the even nibbles of w as bytes, and 16 u of the odd ones in the high halves:
+// one three-input logic operation each ((w ^ 0x88888888) & mask).
+__device__ __forceinline__ uint32_t nib_even(uint32_t w) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0x28;" : "=r"(d) : "r"(w), "n"(0x88888888u), "n"(0x0F0F0F0Fu));
+  return d;
+}
+__device__ __forceinline__ uint32_t nib_odd(uint32_t w) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0x28;" : "=r"(d) : "r"(w), "n"(0x88888888u), "n"(0xF0F0F0F0u));
+  return d;
+}
+
+// The waits of the tiled W4A16 kernel sleep in the poll (up to about this many nanoseconds).
+constexpr uint32_t kW4WaitNs = 1000;
+
 struct AlignSink {
   uint8_t* base;
   int G;
@@ -659,7 +682,8 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
             catch_up(stages);
             waited = true;
           }
-          if (*(volatile int*)&s_stop || !mbar_wait(&empty[q][st], ((it / stages) & 1) ^ 1, err, 13, spin)) {
+          if (*(volatile int*)&s_stop ||
+              !mbar_wait_hint(&empty[q][st], ((it / stages) & 1) ^ 1, err, 13, spin, kW4WaitNs)) {
             s_stop = 1;
             goto producer_done;
           }
@@ -714,7 +738,7 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
         for (int m = 0; m < MB; ++m) bank[h][m] = 0.0f;
       for (int s = 0; s < nstage; ++s, ++it) {
         const int st = it % stages, gi = 4 * s + b;
-        bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[q][st], (it / stages) & 1, err, 14, spin);
+        bool ok = !*(volatile int*)&s_stop && mbar_wait_hint(&full[q][st], (it / stages) & 1, err, 14, spin, kW4WaitNs);
         ok = __all_sync(0xFFFFFFFFu, ok);
         if (!ok) {
           s_stop = 1;
@@ -745,16 +769,12 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
 #pragma unroll
               for (int cb = 0; cb < 4; ++cb) {
                 // u = nibble ^ 8 = w + 8: even nibbles as bytes, odd nibbles as 16 u in the high halves
-                const uint32_t xa[4] = {wa[cb].x ^ 0x88888888u, wa[cb].y ^ 0x88888888u, wa[cb].z ^ 0x88888888u,
-                                        wa[cb].w ^ 0x88888888u};
-                const uint32_t xb[4] = {wb[cb].x ^ 0x88888888u, wb[cb].y ^ 0x88888888u, wb[cb].z ^ 0x88888888u,
-                                        wb[cb].w ^ 0x88888888u};
-                constexpr uint32_t E = 0x0F0F0F0Fu, O = 0xF0F0F0F0u;
-                int ce[4] = {0, 0, 0, 0}, co[4] = {0, 0, 0, 0};
-                mma_u8s8(ce, xa[0] & E, xb[0] & E, xa[1] & E, xb[1] & E, de.x, de.y);
-                mma_u8s8(ce, xa[2] & E, xb[2] & E, xa[3] & E, xb[3] & E, de.z, de.w);
-                mma_u8s8(co, xa[0] & O, xb[0] & O, xa[1] & O, xb[1] & O, dd.x, dd.y);
-                mma_u8s8(co, xa[2] & O, xb[2] & O, xa[3] & O, xb[3] & O, dd.z, dd.w);
+                const uint4 va = wa[cb], vb = wb[cb];
+                int ce[4], co[4];
+                mma_u8s8_first(ce, nib_even(va.x), nib_even(vb.x), nib_even(va.y), nib_even(vb.y), de.x, de.y);
+                mma_u8s8(ce, nib_even(va.z), nib_even(vb.z), nib_even(va.w), nib_even(vb.w), de.z, de.w);
+                mma_u8s8_first(co, nib_odd(va.x), nib_odd(vb.x), nib_odd(va.y), nib_odd(vb.y), dd.x, dd.y);
+                mma_u8s8(co, nib_odd(va.z), nib_odd(vb.z), nib_odd(va.w), nib_odd(vb.w), dd.z, dd.w);
                 // sum(u q) of rows i, i + 8: columns 2 tg (lo) and 2 tg + 1 (hi); the odd sums are
                 // multiples of 16, shifted back exactly
                 pa[cb] = ce[0] + (co[0] >> 4) + 256 * (ce[1] + (co[1] >> 4));

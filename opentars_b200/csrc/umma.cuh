@@ -48,12 +48,34 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// mbar_test with a suspend-time hint: a thread whose phase is not complete may sleep up to about
+// `ns` nanoseconds in the test (it wakes when the phase completes), so a waiting warp issues few
+// polls.
+__device__ __forceinline__ bool mbar_test_hint(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 // Waits for the phase of `parity` to complete; false after `limit` polls, and then the first code
 // recorded since the word was last cleared stays in *err (later give-ups do not overwrite it).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
                                           uint32_t limit = kSpinLimit) {
   for (uint32_t i = 0; i < limit; ++i)
     if (mbar_test(bar, parity)) return true;
+  if (err) atomicCAS(err, 0, code);
+  return false;
+}
+// mbar_wait with hinted polls of at most about `ns` nanoseconds each.
+__device__ __forceinline__ bool mbar_wait_hint(uint64_t* bar, uint32_t parity, int* err, int code, uint32_t limit,
+                                               uint32_t ns) {
+  for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_test_hint(bar, parity, ns)) return true;
   if (err) atomicCAS(err, 0, code);
   return false;
 }
