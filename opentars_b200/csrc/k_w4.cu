@@ -487,8 +487,8 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
 // weights of all of them through TMA tiles.
 //
 // Pre-pass (k_w4_align): one warp per four (row, group) pairs of one GEMV writes, per row m, the
-// aligned mantissas as [G][256 bytes] (align_quad's chunk layout) followed by [G][scale bits,
-// mantissa sum] into that GEMV's scratch. It lets the main kernel start at once
+// aligned mantissas as [G][256 bytes] (put_s8_planes' lo / hi byte planes) followed by [G][scale
+// bits, mantissa sum] into that GEMV's scratch. It lets the main kernel start at once
 // (griddepcontrol.launch_dependents); the main kernel is launched with programmatic stream
 // serialisation and copies from the scratch only after griddepcontrol.wait.
 //
@@ -501,9 +501,21 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
 // (128-byte swizzle: the lanes' 16-byte reads of one row chunk land on eight different bank
 // groups) and, per activation row, the four groups' aligned mantissas (1 KB) and scale / sum
 // words (32 bytes), bulk copies from the scratch. The weights of the first ring-full are requested
-// before the pre-pass has finished; their activation copies follow griddepcontrol.wait. The
-// activation chunk a lane multiplies with is the same for all 32 lanes (a broadcast read) and
-// serves both of its columns (lane L: columns L and L + 32). The fp16 group scales of the next tile
+// before the pre-pass has finished; their activation copies follow griddepcontrol.wait.
+//
+// The exact group dots run on the warp MMA (mma.sync m16n8k32, u8 x s8 -> s32; the tcgen05 MMA
+// wants its operands in shared memory in its own layout and its accumulator in TMEM, which a
+// per-group scale would have to read back every 128 k). A operand: the nibbles made unsigned
+// (u = nibble ^ 8 = w + 8), the even nibbles of a word as four bytes, the odd ones as 16 u in the
+// high halves (a second accumulator, shifted back exactly). B operand: q = lo + 256 hi as two
+// signed-byte planes in the same even / odd split, B column n = plane n & 1, so
+// sum(w q) = C_lo + 256 C_hi - 8 sum(q), exact in int32. The MMA's k order is a permutation of the
+// group's k applied alike to A and B (lane t: words 4 t .. 4 t + 3 of the row and of the planes),
+// which leaves the integer sum unchanged. Per group a warp issues four MMAs per block of 16
+// columns; MMA rows i and i + 8 are tile rows 16 cb + r(i) and + 8 with r = 0 4 1 5 2 6 3 7, so the
+// eight lanes of each 16-byte read phase hit eight different bank groups of the swizzled rows. B
+// columns 2..7 repeat the two planes, so every lane holds whole dots; lane (i, t) owns the columns
+// of block t (rows r(i), r(i) + 8). The fp16 group scales of the next tile
 // are copied into shared memory (4-byte cp.async, columns padded to an odd number of words) while
 // the current tile computes. Every wait is bounded; after a give-up the warps skip their remaining
 // work but keep the quad's barrier count, the producers stop issuing (the activation copies of
