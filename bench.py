@@ -120,8 +120,9 @@ def build_w4(R: int, seed: int, M: int = 1, K: int = 8192, N: int = 16384):
                   Y_OFF=y0 + r * 4 * M * N, M=M, N=N, K=K, GROUP_SIZE=128)
         ddr[qa + 64 * r:qa + 64 * (r + 1)] = np.frombuffer(d, np.uint8)
     unit = N * K // 2 + 2 * N * G + 4 * M * K + 4 * M * N               # 69,304,320 bytes here
-    return dict(ddr=ddr, qa=qa, qlen=R, units=R, unit_bytes=unit, kernel_bytes=unit, roof=(1, lambda i: True),
-                kernel="k_gemv_w4 (W4A16 GEMV)", inputs=(x0, R * 4 * M * K), outputs=(y0, R * 4 * M * N),
+    return dict(ddr=ddr, qa=qa, qlen=R, units=R, unit_bytes=unit, kernel_bytes=R * unit, roof=(2, lambda i: i == 0),
+                kernel="k_w4_align + k_gemv_w4t: the step's R W4A16 GEMVs as one grouped launch (one dependency level)",
+                inputs=(x0, R * 4 * M * K), outputs=(y0, R * 4 * M * N),
                 config=dict(workload="config2_w4a16_gemv", M=M, K=K, N=N, units_per_step=R,
                             weights_bytes_per_step=R * N * K // 2,
                             l2="inputs larger than L2: each step streams R distinct weight copies"))
@@ -304,8 +305,8 @@ def measure_units(workload: str, units: int, steps: int, warmup: int, world: int
     value = total_bytes / (ms_max / 1e3) / 1e9
 
     # roofline: device times of the dominant kernel from a graph captured with events between
-    # dependency levels (config 0: level 1 is the one grouped GEMV launch of all R units) or
-    # between descriptors (config 2: each W4A16 GEMV alone)
+    # dependency levels (config 0: level 1 is the one grouped GEMV launch of all R units; config 2:
+    # level 0 is the grouped pre-pass and GEMV launch of all R units)
     from opentars_b200._lib import Status_t
     mode, pick = p["roof"]
     st2, cop, gt = Status_t(), ctypes.c_int32(-1), ctypes.c_void_p()
