@@ -114,7 +114,9 @@ int tc_mma_trace(int32_t enable, uint64_t* out, uint32_t cap);
 /* The device word (one per device: the current device's is read) in which the streaming kernels
  * (tensor-core GEMM, grouped GEMV, streamed W4A16 GEMV) record a bounded wait that gave up instead
  * of hanging: 0 = none, else the code of the first one since the word was last cleared (GEMM 1-5,
- * grouped GEMV 21-22, W4A16 GEMV 11-12); a kernel that gave up skipped the rest of its work, so its
+ * grouped GEMV 21-22, streamed W4A16 GEMV 11-12, tiled W4A16 GEMV 13-15: weight ring producer,
+ * consumer, the hand-over of a tile's partial sums between the quads of a block); a kernel that
+ * gave up skipped the rest of its work, so its
  * outputs are incomplete. clear != 0 resets the word. Synchronous; TC_ERR_CUDA if it cannot be
  * read. No counterpart in the reference (its golden model never waits). */
 int tc_wait_error(int32_t clear);

@@ -493,8 +493,9 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
 // serialisation and copies from the scratch only after griddepcontrol.wait.
 //
 // Main kernel (k_gemv_w4t): a tile is 64 output columns of one GEMV x all of K; the tiles of the
-// group's GEMVs are numbered one after another and dealt to the quads in turn. Each block works on
-// two tiles at a time; a tile belongs to a quad of four compute warps, warp b adding the terms of
+// group's GEMVs are numbered one after another, each block takes a contiguous run of them, and its
+// two quads split the run's stages in halves (W4Plan: the tile cut at the midpoint hands its partial
+// bank sums from one quad to the other through shared memory). A quad is four compute warps, warp b adding the terms of
 // the groups g = b (mod 4) - exactly the bank b of the reference's four-bank sum, in increasing g
 // - so no term crosses a warp until the four banks are combined. A producer warp per quad fills
 // the quad's ring with stages of four groups: two TMA boxes of 64 rows x 128 bytes of weights
@@ -628,12 +629,47 @@ __global__ void __launch_bounds__(256) k_w4_align(const __grid_constant__ W4Grou
 // with an odd number of words, so the 32 lanes' 2-byte reads of one group hit 32 different banks.
 __host__ __device__ constexpr uint32_t w4t_scale_stride(int G) { return (uint32_t)((G + 1) / 2) % 2 ? 2 * G : 2 * G + 4; }
 
+// The work of one quad of a block, in order. Block b takes the contiguous tiles
+// [ntiles * b / nblk, ntiles * (b + 1) / nblk) and its two quads half of their stages each: quad 0
+// the first stages of the tile cut at the midpoint (kind 1: its bank sums are handed to quad 1)
+// and then the whole tiles before it (kind 0); quad 1 the whole tiles after it and then the cut
+// tile's remaining stages (kind 2: starting from the handed-over sums, so every bank still adds
+// its groups in increasing g).
+struct W4Piece {
+  int t, s0, s1, kind;
+};
+struct W4Plan {
+  int t_lo, t_hi, ts, r, nstage;
+  __device__ W4Plan(int ntiles, int nstage_, int blk, int nblk) : nstage(nstage_) {
+    t_lo = (int)((int64_t)ntiles * blk / nblk);
+    t_hi = (int)((int64_t)ntiles * (blk + 1) / nblk);
+    const int half = (t_hi - t_lo) * nstage / 2;
+    ts = t_lo + half / nstage;
+    r = half % nstage;
+  }
+  __device__ int count(int q) const { return q == 0 ? (r > 0) + (ts - t_lo) : t_hi - ts; }
+  __device__ W4Piece piece(int q, int p) const {
+    if (q == 0) {
+      if (r > 0) {
+        if (p == 0) return {ts, 0, r, 1};
+        --p;
+      }
+      return {t_lo + p, 0, nstage, 0};
+    }
+    const int f0 = ts + (r > 0);
+    if (p < t_hi - f0) return {f0 + p, 0, nstage, 0};
+    return {ts, r, nstage, 2};
+  }
+};
+
 template <int MB>
 __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant__ W4Group grp,
                                                             const __grid_constant__ W4Maps maps, int stages) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full[kTQuads][kTMaxStages], empty[kTQuads][kTMaxStages];
   __shared__ float sbank[2][kTQuads][kTBanks][MB][kTCols];
+  __shared__ float xbank[kTBanks][MB][kTCols];                      // the cut tile's bank sums
+  __shared__ uint64_t xbar;
   __shared__ int s_stop, s_issued[kTQuads];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -651,6 +687,7 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
         mbar_init(&full[q][i], 1);
         mbar_init(&empty[q][i], kTBanks);
       }
+    mbar_init(&xbar, kTBanks);
     s_stop = 0;
     mbar_fence_init();
   }
@@ -661,10 +698,10 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
     while (j + 1 < grp.n && t >= grp.tile0[j + 1]) ++j;
     return j;
   };
-  // tiles of quad q: blockIdx.x + gridDim.x * (q + kTQuads * i)
+  const W4Plan plan(ntiles, nstage, blockIdx.x, gridDim.x);
   if (warp < kTQuads) {
     if (lane == 0) {
-      const int q = warp, tstep = gridDim.x * kTQuads;
+      const int q = warp, np = plan.count(q);
       // the activation rows of stage s of tile t into ring slot st (after griddepcontrol.wait)
       auto issue_acts = [&](int t, int s, int st) {
         const W4Args& e = grp.e[entry_of(t)];
@@ -680,22 +717,24 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
       auto catch_up = [&](int upto) {
         griddep_wait();
         int k = 0;
-        for (int t = blockIdx.x + gridDim.x * q; t < ntiles && k < upto; t += tstep)
-          for (int s = 0; s < nstage && k < upto; ++s, ++k) issue_acts(t, s, k);
+        for (int p = 0; p < np && k < upto; ++p) {
+          const W4Piece pc = plan.piece(q, p);
+          for (int s = pc.s0; s < pc.s1 && k < upto; ++s, ++k) issue_acts(pc.t, s, k);
+        }
       };
-      int it = 0;
+      int it = 0, st = 0, ph = 0;                  // stages issued; ring slot and its phase
       bool waited = false;
-      for (int t = blockIdx.x + gridDim.x * q; t < ntiles; t += tstep) {
-        const int j = entry_of(t), lt = t - grp.tile0[j];
+      for (int p = 0; p < np; ++p) {
+        const W4Piece pc = plan.piece(q, p);
+        const int t = pc.t, j = entry_of(t), lt = t - grp.tile0[j];
         const int mrows = min(grp.e[j].M, MB);
-        for (int s = 0; s < nstage; ++s, ++it) {
-          const int st = it % stages;
+        for (int s = pc.s0; s < pc.s1; ++s, ++it, st = st + 1 < stages ? st + 1 : (ph ^= 1, 0)) {
           if (!waited && it == stages) {
             catch_up(stages);
             waited = true;
           }
           if (*(volatile int*)&s_stop ||
-              !mbar_wait_hint(&empty[q][st], ((it / stages) & 1) ^ 1, err, 13, spin, kW4WaitNs)) {
+              !mbar_wait_hint(&empty[q][st], ph ^ 1, err, 13, spin, kW4WaitNs)) {
             s_stop = 1;
             goto producer_done;
           }
@@ -735,22 +774,30 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    const int tstep = gridDim.x * kTQuads, t0 = blockIdx.x + gridDim.x * q;
-    if (t0 < ntiles) fetch_scales(t0, 0);
-    int it = 0, tl = 0;
-    for (int t = t0; t < ntiles; t += tstep, ++tl) {
-      const int j = entry_of(t), lt = t - grp.tile0[j];
+    const int np = plan.count(q);
+    if (np > 0) fetch_scales(plan.piece(q, 0).t, 0);
+    int st = 0, ph = 0;                              // ring slot and its phase
+    for (int tl = 0; tl < np; ++tl) {
+      const W4Piece pc = plan.piece(q, tl);
+      const int t = pc.t, j = entry_of(t), lt = t - grp.tile0[j];
       const W4Args& e = grp.e[j];
-      if (t + tstep < ntiles) fetch_scales(t + tstep, (tl + 1) & 1);
+      const int eM = e.M;                              // (kept in a register across the stage loop)
+      if (tl + 1 < np) fetch_scales(plan.piece(q, tl + 1).t, (tl + 1) & 1);
       const uint8_t* scl = sscl + ((size_t)q * 2 + (tl & 1)) * kTCols * sstr;
       float bank[2][MB];
+      bool from_x = false;
+      if (pc.kind == 2) {                            // continue the bank sums quad 0 handed over
+        from_x = !*(volatile int*)&s_stop && mbar_wait_hint(&xbar, 0, err, 15, spin, kW4WaitNs);
+        from_x = __all_sync(0xFFFFFFFFu, from_x);
+        if (!from_x) s_stop = 1;
+      }
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int m = 0; m < MB; ++m) bank[h][m] = 0.0f;
-      for (int s = 0; s < nstage; ++s, ++it) {
-        const int st = it % stages, gi = 4 * s + b;
-        bool ok = !*(volatile int*)&s_stop && mbar_wait_hint(&full[q][st], (it / stages) & 1, err, 14, spin, kW4WaitNs);
+        for (int m = 0; m < MB; ++m) bank[h][m] = from_x ? xbank[b][m][cA + 8 * h] : 0.0f;
+      for (int s = pc.s0; s < pc.s1; ++s, st = st + 1 < stages ? st + 1 : (ph ^= 1, 0)) {
+        const int gi = 4 * s + b;
+        bool ok = !*(volatile int*)&s_stop && mbar_wait_hint(&full[q][st], ph, err, 14, spin, kW4WaitNs);
         ok = __all_sync(0xFFFFFFFFu, ok);
         if (!ok) {
           s_stop = 1;
@@ -771,7 +818,7 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
           const uint8_t* arow0 = aring + ((size_t)q * stages + st) * MB * kTActRow;
 #pragma unroll
           for (int m = 0; m < MB; ++m) {
-            if (m < e.M) {
+            if (m < eM) {
               const uint8_t* arow = arow0 + m * kTActRow;
               // B column n = plane n & 1 (lo, hi; columns 2..7 repeat 0, 1): the even-k bytes (de)
               // and odd-k bytes (dd) of lane tg's words 4 tg .. 4 tg + 3
@@ -805,6 +852,17 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[q][st]);   // the stage's weights and rows are read
+      }
+      if (pc.kind == 1) {                            // hand the bank sums (as they are) to quad 1
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int m = 0; m < MB; ++m) xbank[b][m][cA + 8 * h] = bank[h][m];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xbar);
+        asm volatile("cp.async.wait_group 0;" ::: "memory");   // the next piece's scales have landed
+        asm volatile("bar.sync %0, %1;" ::"r"(2 + q), "n"(32 * kTBanks) : "memory");
+        continue;
       }
       // the four banks of the tile's columns: (b0 + b1) + (b2 + b3)
 #pragma unroll
@@ -842,8 +900,8 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
 }
 
 // Dynamic shared memory the tiled kernel may use beside its static arrays (the banks of two tiles
-// per quad, the barriers).
-size_t w4t_smem_cap(int MB) { return 227 * 1024 - (size_t)4096 * MB - 1024; }
+// per quad and of the cut tile, the barriers).
+size_t w4t_smem_cap(int MB) { return 227 * 1024 - (size_t)5120 * MB - 1024; }
 
 // Shared memory of the tiled kernel for MB rows: the weight and activation rings, the scales of
 // two tiles per quad, alignment slack.
@@ -878,7 +936,7 @@ cudaError_t launch_w4t(const W4Args* gs, int n, cudaStream_t st) {
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(std::min((grp.tile0[n] + kTQuads - 1) / kTQuads, 148));
+  cfg.gridDim = dim3(std::min(grp.tile0[n], 148));
   cfg.blockDim = dim3(kTThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;

@@ -57,9 +57,9 @@ def _give_up_then_recover(program, codes):
 
 
 def test_w4a16_stream_wait_gives_up_and_recovers():
-    """The tiled W4A16 GEMV (producer code 13, consumer code 14)."""
+    """The tiled W4A16 GEMV (producer code 13, consumer code 14, partial-sum hand-over 15)."""
     import __graft_entry__ as GE
-    _give_up_then_recover(GE._w4_program(), (13, 14))
+    _give_up_then_recover(GE._w4_program(), (13, 14, 15))
 
 
 def test_tensor_core_gemm_wait_gives_up_and_recovers():
