@@ -702,9 +702,9 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
   if (warp < kTQuads) {
     if (lane == 0) {
       const int q = warp, np = plan.count(q);
-      // the activation rows of stage s of tile t into ring slot st (after griddepcontrol.wait)
-      auto issue_acts = [&](int t, int s, int st) {
-        const W4Args& e = grp.e[entry_of(t)];
+      // the activation rows of stage s of GEMV j into ring slot st (after griddepcontrol.wait)
+      auto issue_acts = [&](int j, int s, int st) {
+        const W4Args& e = grp.e[j];
         const bool two = 4 * s + 2 < G;
         uint8_t* dst = aring + ((size_t)q * stages + st) * MB * kTActRow;
         for (int m = 0; m < min(e.M, MB); ++m) {
@@ -719,7 +719,8 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
         int k = 0;
         for (int p = 0; p < np && k < upto; ++p) {
           const W4Piece pc = plan.piece(q, p);
-          for (int s = pc.s0; s < pc.s1 && k < upto; ++s, ++k) issue_acts(pc.t, s, k);
+          const int j = entry_of(pc.t);
+          for (int s = pc.s0; s < pc.s1 && k < upto; ++s, ++k) issue_acts(j, s, k);
         }
       };
       int it = 0, st = 0, ph = 0;                  // stages issued; ring slot and its phase
@@ -743,7 +744,7 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
           uint8_t* dst = ring + ((size_t)q * stages + st) * kTStageB;
           tma_load_2d(dst, &maps.m[j], 256 * s, kTCols * lt, &full[q][st]);
           if (two) tma_load_2d(dst + kTStageB / 2, &maps.m[j], 256 * s + 128, kTCols * lt, &full[q][st]);
-          if (waited) issue_acts(t, s, st);
+          if (waited) issue_acts(j, s, st);
         }
       }
     producer_done:
@@ -752,30 +753,33 @@ __global__ void __launch_bounds__(kTThreads, 1) k_gemv_w4t(const __grid_constant
     }
   } else {
     const int cw = warp - kTQuads, q = cw / kTBanks, b = cw % kTBanks;
-    const int qt = threadIdx.x - 32 * (kTQuads + q * kTBanks);     // thread of the quad, 0..127
     // MMA lane roles: row i = lane / 4 (tile row ri = 0 4 1 5 2 6 3 7 of it), tg = lane % 4; the
     // lane's result columns cA = 16 tg + ri and cA + 8
     const int mr = lane >> 2, tg = lane & 3;
     const int ri = (mr >> 1) | ((mr & 1) << 2), cA = 16 * tg + ri;
     const uint32_t woff = 16u * ((4 * (b & 1) + tg) ^ ri);
-    // the group scales of tile t into buffer `buf` of this quad (4-byte copies)
+    // the group scales of tile t into buffer `buf` of this quad (4-byte copies): warp b copies
+    // columns b, b + 4, ..., its lanes consecutive words of one column
     auto fetch_scales = [&](int t, int buf) {
-      const W4Args& e = grp.e[entry_of(t)];
-      const int lt = t - grp.tile0[entry_of(t)];
+      const int j = entry_of(t);
+      const W4Args& e = grp.e[j];
+      const int lt = t - grp.tile0[j], nc = min(kTCols, e.N - lt * kTCols);
       uint8_t* dst = sscl + ((size_t)q * 2 + buf) * kTCols * sstr;
-      const int words = kTCols * (G / 2);
-      for (int w = qt; w < words; w += 32 * kTBanks) {
-        const int c = w / (G / 2), jw = w - c * (G / 2);
-        const uint64_t n = (uint64_t)lt * kTCols + c;
-        if (n < (uint64_t)e.N)
+      for (int c = b; c < nc; c += kTBanks) {
+        const uint8_t* src = e.scale + 2 * ((uint64_t)(lt * kTCols + c) * G);
+        for (int jw = lane; jw < G / 2; jw += 32)
           asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst + c * sstr + 4 * jw)),
-                       "l"(e.scale + 2 * (n * G + 2 * jw))
+                       "l"(src + 4 * jw)
                        : "memory");
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
     const int np = plan.count(q);
     if (np > 0) fetch_scales(plan.piece(q, 0).t, 0);
+    // the first piece's scales, copied by all four warps, before any warp reads them (later
+    // pieces' scales are waited for at the end of the piece before)
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    asm volatile("bar.sync %0, %1;" ::"r"(2 + q), "n"(32 * kTBanks) : "memory");
     int st = 0, ph = 0;                              // ring slot and its phase
     for (int tl = 0; tl < np; ++tl) {
       const W4Piece pc = plan.piece(q, tl);
