@@ -196,6 +196,8 @@ __global__ void __launch_bounds__(kThreads) k_gemv8(GemmArgs g) {
 // and 16 lanes run the epilogue of k_gemv8 at once. int32 sums are exact in any order.
 // Every wait is bounded; after a timeout the block skips its remaining chunks.
 constexpr int kSCols = 16;
+// The group's waits sleep in the poll (up to about this many nanoseconds).
+constexpr uint32_t kGroupWaitNs = 1000;
 
 template <int KU>
 __host__ __device__ constexpr int s_stages() { return KU <= 2 ? 6 : (KU <= 4 ? 3 : 2); }
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(32 * (1 + s_stages<KU>()), 2)
     uint4 areg[MB == 1 ? KU : 1];                               // M = 1: the activation row in registers
     int areg_j = -1;
     for (int c = c_begin + st, t = st; c < c_end; c += S, t += S) {
-      const bool ok = !*(volatile int*)&s_stop && mbar_wait(&full[st], (t / S) & 1, grp.err, 22, grp.spin);
+      const bool ok = !*(volatile int*)&s_stop && mbar_wait_hint(&full[st], (t / S) & 1, grp.err, 22, grp.spin, kGroupWaitNs);
       if (!__all_sync(0xFFFFFFFFu, ok)) {                           // the whole warp stops together
         s_stop = 1;
         break;
@@ -327,7 +329,7 @@ __global__ void __launch_bounds__(32 * (1 + s_stages<KU>()), 2)
       int t = 0;
       for (int c = c_begin; c < c_end; ++c, ++t) {
         const int st = t % S;
-        if (!mbar_wait(&empty[st], ((t / S) & 1) ^ 1, grp.err, 21, grp.spin)) {
+        if (!mbar_wait_hint(&empty[st], ((t / S) & 1) ^ 1, grp.err, 21, grp.spin, kGroupWaitNs)) {
           s_stop = 1;
           break;
         }
