@@ -252,7 +252,7 @@ def run_ours(a, world, rank, local) -> dict | None:
         "warmup": a.warmup, "ms_per_step": m["ms_per_step"], "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8" if a.workload == "gemv" else "int4xint16",
         "data": "synthetic, seeded (BASELINE config distributions)",
-        "config": dict(m["config"], parallelism=f"replicas x{world} (independent GEMV batches per GPU)"),
+        "config": gemv_config(m["config"], world),
         "roofline": m["roofline"], "e2e": m["e2e"],
         "gpu_launches": m["gpu_launches"], "clocks": m["clocks"], "bit_exact_unit0": m["bit_exact"],
     }
@@ -372,6 +372,11 @@ def measure_units(workload: str, units: int, steps: int, warmup: int, world: int
 
 
 # ----------------------------------------------------------------------------- the reference arm
+def gemv_config(cfg: dict, world: int) -> dict:
+    """The `config` of a GEMV workload's line (both arms print the same)."""
+    return dict(cfg, parallelism=f"replicas x{world} (independent GEMV batches per GPU)")
+
+
 def run_reference(a, world, rank) -> dict | None:
     if rank != 0:
         return None
@@ -381,12 +386,12 @@ def run_reference(a, world, rank) -> dict | None:
     vals = [cpu_oracle_gbs(a.workload, a.ref_seconds, procs) for _ in range(a.steps)]
     v = statistics.mean(x["value"] for x in vals)
     build, R = WORKLOADS[a.workload]
-    cfg = build(1, 0)["config"]
+    cfg = build(a.units or R, 0)["config"]                    # the workload our arm measures
     return {
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8" if a.workload == "gemv" else "int4xint16", "data": "synthetic, seeded",
-        "config": dict(cfg, units_per_step="bounded CPU sample"),
+        "config": gemv_config(cfg, world),
         "cpu_baseline": dict(value=round(v, 4), unit="GB/s", cores=procs, kind="port",
                              sample=vals[-1]["sample"]),
         "e2e": dict(value=round(v, 4), unit="GB/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
@@ -744,17 +749,7 @@ def run_gemm(a, world, rank, local) -> dict | None:
         "warmup": a.warmup, "ms_per_step": round(ms_max / a.steps, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic, seeded (config 1 distributions)",
-        "config": dict(workload="config1_w8a8_gemm_sweep", M=list(GEMM_M), shapes=[list(s) for s in GEMM_SHAPES],
-                       descriptors_per_step=p["n_main"],
-                       parallelism=(f"the 151936-row vocabulary GEMM N-split over {world} GPUs (each keeps its "
-                                    f"output columns), the other shapes whole on every GPU"
-                                    + {"overlap": ", the split outputs all-gathered (NCCL, second stream) while "
-                                                  "the later segments compute",
-                                       "after": ", the split outputs all-gathered (NCCL) after the step's GEMMs",
-                                       "none": "; no collective in the timed steps (the outputs are gathered "
-                                               "afterwards for the parity check)"}[a.gemm_gather]
-                                    if world > 1 else "1 GPU"),
-                       l2="weights (170 MB per step) larger than L2, streamed once per step"),
+        "config": gemm_config(world, a.gemm_gather, p["n_main"]),
         "roofline": roofline, "e2e": e2e, "gpu_launches": a.steps * kernels_per_step, "clocks": clk.summary(),
         "bit_exact_vs_reference": bit_exact,
     }
@@ -765,9 +760,25 @@ def run_gemm(a, world, rank, local) -> dict | None:
     return out
 
 
+def gemm_config(world: int, gather: str, n_main: int) -> dict:
+    """The `config` of config 1's line (both arms print the same)."""
+    return dict(workload="config1_w8a8_gemm_sweep", M=list(GEMM_M), shapes=[list(s) for s in GEMM_SHAPES],
+                descriptors_per_step=n_main,
+                parallelism=(f"the 151936-row vocabulary GEMM N-split over {world} GPUs (each keeps its "
+                             f"output columns), the other shapes whole on every GPU"
+                             + {"overlap": ", the split outputs all-gathered (NCCL, second stream) while "
+                                           "the later segments compute",
+                                "after": ", the split outputs all-gathered (NCCL) after the step's GEMMs",
+                                "none": "; no collective in the timed steps (the outputs are gathered "
+                                        "afterwards for the parity check)"}[gather]
+                             if world > 1 else "1 GPU"),
+                l2="weights (170 MB per step) larger than L2, streamed once per step")
+
+
 def run_gemm_reference(a, world, rank) -> dict | None:
     if rank != 0:
         return None
+    n_main = build_gemm(world, rank)["n_main"]
     procs = os.cpu_count() or 1
     vals = [cpu_oracle_gemm(a.ref_seconds, procs) for _ in range(a.warmup + a.steps)][a.warmup:]
     v = statistics.mean(x["value"] for x in vals)
@@ -775,7 +786,7 @@ def run_gemm_reference(a, world, rank) -> dict | None:
         "impl": "reference", "metric": METRIC, "value": round(v, 6), "unit": "TOPS", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int8", "data": "synthetic, seeded",
-        "config": dict(workload="config1_w8a8_gemm_sweep", sample="bounded CPU sample"),
+        "config": gemm_config(world, a.gemm_gather, n_main),
         "cpu_baseline": dict(value=round(v, 6), unit="TOPS", cores=procs, kind="port", sample=vals[-1]["sample"]),
         "e2e": dict(value=round(v, 6), unit="TOPS", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
         "note": "the reference is Python (numpy golden model); its restatement in oracle/ is timed here",
@@ -941,7 +952,6 @@ def run_decode(a, world, rank, local) -> dict | None:
     for t in (32, 128, 250):                              # steps whose position is within 2 of t
         near = [ms_ for p_, ms_ in step_ms if abs(p_ - t) <= 2]
         at[str(t)] = round(statistics.mean(near), 4) if near else None
-    positions = (min(p_ for p_, _ in step_ms), max(p_ for p_, _ in step_ms) + 1)
 
     # roofline: the step's GEMV kernels (the weight stream) from one profiled step
     if pos + 1 > CONTEXT:
@@ -1006,13 +1016,7 @@ def run_decode(a, world, rank, local) -> dict | None:
         "warmup": a.warmup, "ms_per_step": round(ms_max / a.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic: random-init weights (seeded, the reference's random_weights), seeded prompts",
-        "config": dict(workload=("config3_qwen3_0.6b_decode" if a.workload == "decode" else "config4_gemma3_1b_decode"),
-                       batch_per_gpu=B, prompt=PROMPT_LEN, prefill_chunk=CHUNK, context=CONTEXT,
-                       timed_positions=f"{positions[0]} -> {positions[1]} (each step one token per sequence; "
-                                       f"a full context starts the batch over, untimed)",
-                       parallelism=f"independent sequences, {B} per GPU x {world} GPUs",
-                       l2="weights (596 MB Qwen3 / 1 GB Gemma-3) larger than L2, streamed once per step",
-                       model_build_s=round(build_s, 1)),
+        "config": decode_config(a.workload, B, world, a.steps), "model_build_s": round(build_s, 1),
         "ms_per_step_at_position": at,
         "roofline": roofline, "e2e": e2e, "gpu_launches": a.steps * len(prof), "clocks": clk.summary(),
         "bit_exact_seq0_vs_reference": bit_exact,
@@ -1112,6 +1116,20 @@ def _engine_stream(eng) -> int:
     return elib().tc_engine_stream(eng.h)
 
 
+def decode_config(workload: str, B: int, world: int, steps: int) -> dict:
+    """The `config` of a decode line (both arms print the same): the timed steps decode positions
+    PROMPT_LEN onwards, a full context starting the batch over."""
+    last = PROMPT_LEN + steps
+    span = (f"{PROMPT_LEN} -> {last}" if last <= CONTEXT else
+            f"{PROMPT_LEN} -> {CONTEXT}, then again from {PROMPT_LEN} ({steps} steps)")
+    return dict(workload=("config3_qwen3_0.6b_decode" if workload == "decode" else "config4_gemma3_1b_decode"),
+                batch_per_gpu=B, prompt=PROMPT_LEN, prefill_chunk=CHUNK, context=CONTEXT,
+                timed_positions=span + " (each step one token per sequence; a full context starts the batch "
+                                       "over, untimed)",
+                parallelism=f"independent sequences, {B} per GPU x {world} GPUs",
+                l2="weights (596 MB Qwen3 / 1 GB Gemma-3) larger than L2, streamed once per step")
+
+
 def run_decode_reference(a, world, rank) -> dict | None:
     """The reference arm for decode: the oracle's golden-Machine restatement on all host cores.
     Each step every worker runs the next 1/16 of a decode step's queue (cycling in order)."""
@@ -1130,8 +1148,7 @@ def run_decode_reference(a, world, rank) -> dict | None:
             if i >= a.warmup:
                 vals.append(sum(d for d, _ in res) / _CPU["n"] / dt)
     v = statistics.mean(vals)
-    cfg = dict(workload=("config3_qwen3_0.6b_decode" if a.workload == "decode" else "config4_gemma3_1b_decode"),
-               batch_per_gpu="one sequence per core", context=CONTEXT)
+    cfg = decode_config(a.workload, a.batch, world, a.steps)
     return {
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -1164,7 +1181,7 @@ def main():
                          "overlapped with the later segments, or not in the timed steps")
     a = ap.parse_args()
     if a.steps is None:
-        a.steps = CONTEXT - PROMPT_LEN if a.workload in DECODE_MODELS and a.impl == "ours" else 100
+        a.steps = CONTEXT - PROMPT_LEN if a.workload in DECODE_MODELS else 100
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":                       # CPU only: no process group, no GPU
         world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
