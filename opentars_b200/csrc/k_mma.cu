@@ -382,20 +382,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
         }
       }
       griddep_wait();
-      uint32_t q = 0;
+      uint32_t q = 0, ph = 0;                  // slices issued; stage st = q mod S, ph its phase bit
+      int st = 0;
       bool stop = false;
       for (int item = item0; item < sh.items && !stop; item += istride) {
         int s, row0, tok0;
         coords(item, s, row0, tok0);
-        for (int i = 0; i < nk; ++i, ++q) {
-          const int st = q % S;
+        for (int i = 0; i < nk; ++i, ++q, st = st + 1 < S ? st + 1 : (ph ^= 1, 0)) {
           const int k = k_lo + i;
           if (q < (uint32_t)pre) {
             load_x(st, tok0, k);
             if (q == 0) stamp(2);
             continue;
           }
-          if (!mbar_wait(&bar_empty[st], ((q / S) & 1) ^ 1, sh.err, 1, sh.spin)) {
+          if (!mbar_wait(&bar_empty[st], ph ^ 1, sh.err, 1, sh.spin)) {
             s_abort = 1;
             stop = true;
             break;
@@ -415,7 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
     if (lane == 0 && nk > 0) {
       // MMA issuer
       const uint32_t idesc = idesc_i8(kRows, NT);
-      uint32_t q = 0;
+      uint32_t q = 0, ph = 0;                  // slices consumed; stage st = q mod S, ph its phase bit
+      int st = 0;
       int t = 0;
       bool stop = false;
       for (int item = item0; item < sh.items && !stop; item += istride, ++t) {
@@ -429,9 +430,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_mma_i8(const __grid_constant__ 
         tc_fence_after();
         const uint32_t d0 = tmem + buf * acc_cols;
         bool first0 = true, first1 = true;
-        for (int i = 0; i < nk; ++i, ++q) {
-          const int st = q % S;
-          if (!mbar_wait(&bar_full[st], (q / S) & 1, sh.err, 3, sh.spin) || aborted(&s_abort)) {
+        for (int i = 0; i < nk; ++i, ++q, st = st + 1 < S ? st + 1 : (ph ^= 1, 0)) {
+          if (!mbar_wait(&bar_full[st], ph, sh.err, 3, sh.spin) || aborted(&s_abort)) {
             s_abort = 1;
             stop = true;
             break;
