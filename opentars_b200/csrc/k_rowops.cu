@@ -264,34 +264,86 @@ __global__ void k_rope(RopeArgs a) {
   }
 }
 
-// FDOT NT: one half-warp per output (m, n), sum16 order over k.
-__global__ void __launch_bounds__(128) k_fdot_nt(FdotArgs a) {
-  const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
-  const uint64_t o = blockIdx.x * 8ull + hw;
-  const bool live = o < (uint64_t)a.M * a.N;
-  const int m = live ? (int)(o / a.N) : 0, n = live ? (int)(o % a.N) : 0;
-  const uint8_t* ar = a.A + (uint64_t)m * a.lda;
-  const uint8_t* br = a.B + (uint64_t)n * a.ldb;
-  float s = 0.0f;
-  for (int k = l; k < a.K; k += 16) s = fadd(s, fmul(ld_f32(ar + 4 * k), ld_f32(br + 4 * k)));
-  s = sum16_fold(s);
-  if (live && l == 0) store_out(a.Y + (uint64_t)m * a.ldy, n, s, a.out, a.out_scale);
+// FDOT NT (numerics.py:393-399), tiled: a block computes a 16 x 16 tile of outputs, one per
+// thread. The tile's 16 A rows and 16 B rows are staged in shared memory (flushed once) in chunks
+// of kFdKC k; each thread runs the 16 lane chains of sum16 (element k to chain k mod 16, in k order,
+// each from +0) and their pairwise fold in registers. Products are flushed; sums use the
+// flush-to-zero add; a NaN, once made, stays a NaN through every later product and sum, so making
+// it canonical once at the end gives the bits of the reference's per-step canonicalisation.
+constexpr int kFdT = 16, kFdKC = 256, kFdLD = kFdKC + 4;    // +4: a row's float4 reads in their own banks
+__global__ void __launch_bounds__(256) k_fdot_nt(FdotArgs a) {
+  __shared__ __align__(16) float sa[kFdT][kFdLD];
+  __shared__ __align__(16) float sb[kFdT][kFdLD];
+  const int tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+  const int m0 = blockIdx.y * kFdT, n0 = blockIdx.x * kFdT;
+  float c[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) c[i] = 0.0f;
+  for (int k0 = 0; k0 < a.K; k0 += kFdKC) {
+    const int kc = min(kFdKC, a.K - k0);                     // a multiple of 16
+    __syncthreads();
+    for (int r = 0; r < kFdT; ++r) {
+      const int m = m0 + r, n = n0 + r;
+      for (int k = tid; k < kc; k += 256) {
+        sa[r][k] = m < a.M ? ftz(ld_f32(a.A + (uint64_t)m * a.lda + 4 * (uint64_t)(k0 + k))) : 0.0f;
+        sb[r][k] = n < a.N ? ftz(ld_f32(a.B + (uint64_t)n * a.ldb + 4 * (uint64_t)(k0 + k))) : 0.0f;
+      }
+    }
+    __syncthreads();
+    const float* ar = sa[tr];
+    const float* br = sb[tc];
+    for (int k = 0; k < kc; k += 16) {
+#pragma unroll
+      for (int l4 = 0; l4 < 4; ++l4) {
+        const float4 av = *reinterpret_cast<const float4*>(ar + k + 4 * l4);
+        const float4 bv = *reinterpret_cast<const float4*>(br + k + 4 * l4);
+        c[4 * l4 + 0] = fadd_nc(c[4 * l4 + 0], fmul_ff(av.x, bv.x));
+        c[4 * l4 + 1] = fadd_nc(c[4 * l4 + 1], fmul_ff(av.y, bv.y));
+        c[4 * l4 + 2] = fadd_nc(c[4 * l4 + 2], fmul_ff(av.z, bv.z));
+        c[4 * l4 + 3] = fadd_nc(c[4 * l4 + 3], fmul_ff(av.w, bv.w));
+      }
+    }
+  }
+#pragma unroll
+  for (int w = 1; w < 16; w *= 2)                              // lane 2i + lane 2i + 1 into lane i
+#pragma unroll
+    for (int l = 0; l < 16; l += 2 * w) c[l] = fadd_nc(c[l], c[l + w]);
+  const int m = m0 + tr, n = n0 + tc;
+  if (m < a.M && n < a.N) store_out(a.Y + (uint64_t)m * a.ldy, n, canon(c[0]), a.out, a.out_scale);
 }
 
-// FDOT NN: one thread per output, y = (((+0 + a0 b0) + a1 b1) + ...) in k order.
-__global__ void k_fdot_nn(FdotArgs a) {
-  const uint64_t total = (uint64_t)a.M * a.N;
-  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
-    const int m = (int)(i / a.N), n = (int)(i - (uint64_t)m * a.N);
-    const uint8_t* ar = a.A + (uint64_t)m * a.lda;
-    float s = 0.0f;
-    for (int k = 0; k < a.K; ++k) {
-      const uint8_t* bp = a.B + (uint64_t)k * a.ldb;
-      const float bv = a.b_fp16 ? from_fp16(ld_u16(bp + 2 * (uint64_t)n)) : ld_f32(bp + 4 * (uint64_t)n);
-      s = fadd(s, fmul(ld_f32(ar + 4 * (uint64_t)k), bv));
+// FDOT NN (numerics.py:402-409), tiled: a block computes 4 rows x 64 columns of outputs, one per
+// thread, each the sequential chain (((+0 + a0 b0) + a1 b1) + ...) in k order; the 4 A rows and
+// kNnK rows of B at a time are staged in shared memory (flushed once). NaN as in k_fdot_nt.
+constexpr int kNnR = 4, kNnC = 64, kNnK = 64;
+__global__ void __launch_bounds__(256) k_fdot_nn(FdotArgs a) {
+  __shared__ float sa[kNnR][kNnK];
+  __shared__ float sb[kNnK][kNnC];
+  const int tid = threadIdx.x, tr = tid >> 6, tc = tid & 63;
+  const int m0 = blockIdx.y * kNnR, n0 = blockIdx.x * kNnC;
+  float s = 0.0f;
+  for (int k0 = 0; k0 < a.K; k0 += kNnK) {
+    const int kc = min(kNnK, a.K - k0);
+    __syncthreads();
+    {
+      const int r = tid >> 6, k = tid & 63, m = m0 + r;       // 256 threads: the 4 x 64 A tile
+      sa[r][k] = (k < kc && m < a.M) ? ftz(ld_f32(a.A + (uint64_t)m * a.lda + 4 * (uint64_t)(k0 + k))) : 0.0f;
     }
-    store_out(a.Y + (uint64_t)m * a.ldy, n, s, a.out, a.out_scale);
+    for (int i = tid; i < kNnK * kNnC; i += 256) {
+      const int k = i >> 6, cc = i & 63, n = n0 + cc;
+      float v = 0.0f;
+      if (k < kc && n < a.N) {
+        const uint8_t* bp = a.B + (uint64_t)(k0 + k) * a.ldb;
+        v = ftz(a.b_fp16 ? from_fp16(ld_u16(bp + 2 * (uint64_t)n)) : ld_f32(bp + 4 * (uint64_t)n));
+      }
+      sb[k][cc] = v;
+    }
+    __syncthreads();
+    const float* ar = sa[tr];
+    for (int k = 0; k < kc; ++k) s = fadd_nc(s, fmul_ff(ar[k], sb[k][tc]));
   }
+  const int m = m0 + tr, n = n0 + tc;
+  if (m < a.M && n < a.N) store_out(a.Y + (uint64_t)m * a.ldy, n, canon(s), a.out, a.out_scale);
 }
 
 inline int grid_for(uint64_t total, int threads) {
@@ -337,10 +389,9 @@ cudaError_t launch_rope(const RopeArgs& a, cudaStream_t st) {
 }
 cudaError_t launch_fdot(const FdotArgs& a, cudaStream_t st) {
   if (a.nn) {
-    k_fdot_nn<<<grid_for((uint64_t)a.M * a.N, 128), 128, 0, st>>>(a);
+    k_fdot_nn<<<dim3((a.N + kNnC - 1) / kNnC, (a.M + kNnR - 1) / kNnR), 256, 0, st>>>(a);
   } else {
-    const uint64_t outs = (uint64_t)a.M * a.N;
-    k_fdot_nt<<<(unsigned)((outs + 7) / 8), 128, 0, st>>>(a);
+    k_fdot_nt<<<dim3((a.N + kFdT - 1) / kFdT, (a.M + kFdT - 1) / kFdT), 256, 0, st>>>(a);
   }
   return cudaGetLastError();
 }
