@@ -282,11 +282,23 @@ __global__ void __launch_bounds__(256) k_fdot_nt(FdotArgs a) {
   for (int k0 = 0; k0 < a.K; k0 += kFdKC) {
     const int kc = min(kFdKC, a.K - k0);                     // a multiple of 16
     __syncthreads();
-    for (int r = 0; r < kFdT; ++r) {
-      const int m = m0 + r, n = n0 + r;
-      for (int k = tid; k < kc; k += 256) {
-        sa[r][k] = m < a.M ? ftz(ld_f32(a.A + (uint64_t)m * a.lda + 4 * (uint64_t)(k0 + k))) : 0.0f;
-        sb[r][k] = n < a.N ? ftz(ld_f32(a.B + (uint64_t)n * a.ldb + 4 * (uint64_t)(k0 + k))) : 0.0f;
+    // float4 i of the chunk: row i / 64, k 4 (i % 64); four per thread and matrix
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = tid + 256 * j, r = i >> 6, k = 4 * (i & 63);
+      if (k < kc) {
+        const int m = m0 + r, n = n0 + r;
+        float4 va = make_float4(0.0f, 0.0f, 0.0f, 0.0f), vb = va;
+        const uint8_t* ap = a.A + (uint64_t)m * a.lda + 4 * (uint64_t)(k0 + k);
+        const uint8_t* bp = a.B + (uint64_t)n * a.ldb + 4 * (uint64_t)(k0 + k);
+        if (m < a.M)
+          va = a.vec ? *reinterpret_cast<const float4*>(ap)
+                     : make_float4(ld_f32(ap), ld_f32(ap + 4), ld_f32(ap + 8), ld_f32(ap + 12));
+        if (n < a.N)
+          vb = a.vec ? *reinterpret_cast<const float4*>(bp)
+                     : make_float4(ld_f32(bp), ld_f32(bp + 4), ld_f32(bp + 8), ld_f32(bp + 12));
+        *reinterpret_cast<float4*>(&sa[r][k]) = make_float4(ftz(va.x), ftz(va.y), ftz(va.z), ftz(va.w));
+        *reinterpret_cast<float4*>(&sb[r][k]) = make_float4(ftz(vb.x), ftz(vb.y), ftz(vb.z), ftz(vb.w));
       }
     }
     __syncthreads();
@@ -315,31 +327,43 @@ __global__ void __launch_bounds__(256) k_fdot_nt(FdotArgs a) {
 // FDOT NN (numerics.py:402-409), tiled: a block computes 4 rows x 64 columns of outputs, one per
 // thread, each the sequential chain (((+0 + a0 b0) + a1 b1) + ...) in k order; the 4 A rows and
 // kNnK rows of B at a time are staged in shared memory (flushed once). NaN as in k_fdot_nt.
-constexpr int kNnR = 4, kNnC = 64, kNnK = 64;
+constexpr int kNnR = 4, kNnC = 64, kNnK = 128;
 __global__ void __launch_bounds__(256) k_fdot_nn(FdotArgs a) {
-  __shared__ float sa[kNnR][kNnK];
-  __shared__ float sb[kNnK][kNnC];
+  __shared__ __align__(16) float sa[kNnR][kNnK];
+  __shared__ __align__(16) float sb[kNnK][kNnC];
   const int tid = threadIdx.x, tr = tid >> 6, tc = tid & 63;
   const int m0 = blockIdx.y * kNnR, n0 = blockIdx.x * kNnC;
   float s = 0.0f;
   for (int k0 = 0; k0 < a.K; k0 += kNnK) {
     const int kc = min(kNnK, a.K - k0);
     __syncthreads();
-    {
-      const int r = tid >> 6, k = tid & 63, m = m0 + r;       // 256 threads: the 4 x 64 A tile
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {                             // the 4 x 128 A tile
+      const int i = tid + 256 * j, r = i >> 7, k = i & 127, m = m0 + r;
       sa[r][k] = (k < kc && m < a.M) ? ftz(ld_f32(a.A + (uint64_t)m * a.lda + 4 * (uint64_t)(k0 + k))) : 0.0f;
     }
-    for (int i = tid; i < kNnK * kNnC; i += 256) {
-      const int k = i >> 6, cc = i & 63, n = n0 + cc;
-      float v = 0.0f;
-      if (k < kc && n < a.N) {
-        const uint8_t* bp = a.B + (uint64_t)(k0 + k) * a.ldb;
-        v = ftz(a.b_fp16 ? from_fp16(ld_u16(bp + 2 * (uint64_t)n)) : ld_f32(bp + 4 * (uint64_t)n));
+    if (a.vec && !a.b_fp16 && n0 + kNnC <= a.N) {             // 128 x 64 fp32: eight float4 per thread
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = tid + 256 * j, k = i >> 4, c4 = 4 * (i & 15);
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (k < kc) v = *reinterpret_cast<const float4*>(a.B + (uint64_t)(k0 + k) * a.ldb + 4 * (uint64_t)(n0 + c4));
+        *reinterpret_cast<float4*>(&sb[k][c4]) = make_float4(ftz(v.x), ftz(v.y), ftz(v.z), ftz(v.w));
       }
-      sb[k][cc] = v;
+    } else {
+      for (int i = tid; i < kNnK * kNnC; i += 256) {
+        const int k = i >> 6, cc = i & 63, n = n0 + cc;
+        float v = 0.0f;
+        if (k < kc && n < a.N) {
+          const uint8_t* bp = a.B + (uint64_t)(k0 + k) * a.ldb;
+          v = ftz(a.b_fp16 ? from_fp16(ld_u16(bp + 2 * (uint64_t)n)) : ld_f32(bp + 4 * (uint64_t)n));
+        }
+        sb[k][cc] = v;
+      }
     }
     __syncthreads();
     const float* ar = sa[tr];
+#pragma unroll 8
     for (int k = 0; k < kc; ++k) s = fadd_nc(s, fmul_ff(ar[k], sb[k][tc]));
   }
   const int m = m0 + tr, n = n0 + tc;
@@ -387,7 +411,9 @@ cudaError_t launch_rope(const RopeArgs& a, cudaStream_t st) {
   k_rope<<<grid_for((uint64_t)a.M * a.N, 256), 256, 0, st>>>(a);
   return cudaGetLastError();
 }
-cudaError_t launch_fdot(const FdotArgs& a, cudaStream_t st) {
+cudaError_t launch_fdot(const FdotArgs& a0, cudaStream_t st) {
+  FdotArgs a = a0;
+  a.vec = (((uintptr_t)a.A | a.lda | (uintptr_t)a.B | a.ldb) & 15) == 0;
   if (a.nn) {
     k_fdot_nn<<<dim3((a.N + kNnC - 1) / kNnC, (a.M + kNnR - 1) / kNnR), 256, 0, st>>>(a);
   } else {

@@ -137,6 +137,7 @@ struct FdotArgs {
   uint8_t* Y;  uint64_t ldy;
   int M, N, K, out;
   float out_scale;
+  int vec;                           // set by the launcher: A and B rows 16-byte aligned
 };
 cudaError_t launch_fdot(const FdotArgs& a, cudaStream_t st);
 
