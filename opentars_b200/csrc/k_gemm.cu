@@ -445,7 +445,23 @@ cudaError_t launch_gemv8_group(GemvGroup& grp, cudaStream_t st) {
 }
 
 cudaError_t launch_gemm_w8a8(const GemmArgs& g, cudaStream_t st) {
-  if (g.M >= mma_min_rows() && mma_machine_ok(g)) return gemm_mma(g, st);
+  if (g.M >= mma_min_rows() && mma_machine_ok(g)) {
+    // A transcendental activation (GELU, SiLU, sigmoid, softplus, exp: about 200 dependent steps
+    // per element) on fp32 output runs as its own elementwise pass over the whole GPU instead of in
+    // the tensor-core GEMM's few epilogue warps: the GEMM stores the fp32 pre-activation values in
+    // the output, the pass applies the activation in place - the same value per element.
+    if (g.act >= 3 && g.out == OUT_FP32) {
+      GemmArgs g2 = g;
+      g2.act = 0;
+      cudaError_t e = gemm_mma(g2, st);
+      if (e != cudaSuccess) return e;
+      ActArgs a{};
+      a.X = g.Y; a.lda = g.ldy; a.Y = g.Y; a.ldy = g.ldy;
+      a.M = g.M; a.N = g.N; a.act = g.act; a.out = OUT_FP32; a.out_scale = g.out_scale;
+      return launch_act(a, st);
+    }
+    return gemm_mma(g, st);
+  }
   const bool vec = gemv8_ok(g);
   if (vec && g.K <= 4096 && g.M <= 8) {
     if (g.M == 1) return launch_gemv8_k<1>(g, st);
