@@ -333,43 +333,22 @@ __global__ void __launch_bounds__(256) k_fdot_nn(FdotArgs a) {
   __shared__ __align__(16) float sb[kNnK][kNnC];
   const int tid = threadIdx.x, tr = tid >> 6, tc = tid & 63;
   const int m0 = blockIdx.y * kNnR, n0 = blockIdx.x * kNnC;
-  // fp32 B in 16-byte rows and a whole 64-column tile: the next chunk's loads are in registers
-  // while the current chunk computes
-  const bool fast = a.vec && !a.b_fp16 && n0 + kNnC <= a.N;
-  float pa[2];
-  float4 pb[8];
-  auto fetch = [&](int k0) {
+  float s = 0.0f;
+  for (int k0 = 0; k0 < a.K; k0 += kNnK) {
     const int kc = min(kNnK, a.K - k0);
+    __syncthreads();
 #pragma unroll
     for (int j = 0; j < 2; ++j) {                             // the 4 x 128 A tile
       const int i = tid + 256 * j, r = i >> 7, k = i & 127, m = m0 + r;
-      pa[j] = (k < kc && m < a.M) ? ld_f32(a.A + (uint64_t)m * a.lda + 4 * (uint64_t)(k0 + k)) : 0.0f;
+      sa[r][k] = (k < kc && m < a.M) ? ftz(ld_f32(a.A + (uint64_t)m * a.lda + 4 * (uint64_t)(k0 + k))) : 0.0f;
     }
-    if (fast) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {                           // 128 x 64 fp32: eight float4 per thread
-        const int i = tid + 256 * j, k = i >> 4, c4 = 4 * (i & 15);
-        pb[j] = k < kc ? *reinterpret_cast<const float4*>(a.B + (uint64_t)(k0 + k) * a.ldb + 4 * (uint64_t)(n0 + c4))
-                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      }
-    }
-  };
-  float s = 0.0f;
-  fetch(0);
-  for (int k0 = 0; k0 < a.K; k0 += kNnK) {
-    const int kc = min(kNnK, a.K - k0);
-    __syncthreads();                                          // the previous chunk is used
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int i = tid + 256 * j;
-      sa[i >> 7][i & 127] = ftz(pa[j]);
-    }
-    if (fast) {
+    if (a.vec && !a.b_fp16 && n0 + kNnC <= a.N) {             // 128 x 64 fp32: eight float4 per thread
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int i = tid + 256 * j;
-        *reinterpret_cast<float4*>(&sb[i >> 4][4 * (i & 15)]) =
-            make_float4(ftz(pb[j].x), ftz(pb[j].y), ftz(pb[j].z), ftz(pb[j].w));
+        const int i = tid + 256 * j, k = i >> 4, c4 = 4 * (i & 15);
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (k < kc) v = *reinterpret_cast<const float4*>(a.B + (uint64_t)(k0 + k) * a.ldb + 4 * (uint64_t)(n0 + c4));
+        *reinterpret_cast<float4*>(&sb[k][c4]) = make_float4(ftz(v.x), ftz(v.y), ftz(v.z), ftz(v.w));
       }
     } else {
       for (int i = tid; i < kNnK * kNnC; i += 256) {
@@ -383,7 +362,6 @@ __global__ void __launch_bounds__(256) k_fdot_nn(FdotArgs a) {
       }
     }
     __syncthreads();
-    if (k0 + kNnK < a.K) fetch(k0 + kNnK);
     const float* ar = sa[tr];
 #pragma unroll 8
     for (int k = 0; k < kc; ++k) s = fadd_nc(s, fmul_ff(ar[k], sb[k][tc]));
