@@ -1037,6 +1037,8 @@ def run_vision(a, world, rank, local) -> dict | None:
     on one seeded 448 x 448 image per GPU: every linear is a W8A8 GEMM with M = 784 patch rows (the
     tensor-core kernel), attention is FDOT / softmax descriptors. A step = one image through the
     captured queue; value in merged visual tokens per second over all GPUs."""
+    import ctypes
+
     import torch
     os.environ["TC_DEVICE"] = str(local)
     torch.cuda.set_device(local)
@@ -1088,6 +1090,30 @@ def run_vision(a, world, rank, local) -> dict | None:
         dev.run(qa, qn)
         dev.from_dev(y_lo, y_n)
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    # where the image's time goes: the queue captured with events between descriptors (each time
+    # includes a few microseconds of event overhead), summed per op kind and shape
+    from opentars_b200 import contract as C
+    from opentars_b200._lib import Status_t
+    st2, cop, gt = Status_t(), ctypes.c_int32(-1), ctypes.c_void_p()
+    check(L.tc_queue_capture(dev.h, qa, qn, 0, 0, 1, ctypes.byref(st2), ctypes.byref(cop), ctypes.byref(gt)), dev.h)
+    arr = (ctypes.c_float * qn)()
+    for _ in range(2):
+        check(L.tc_graph_launch(gt, None), dev.h)
+        check(L.tc_synchronize(dev.h), dev.h)
+    nt = check(L.tc_graph_times(gt, arr, qn), dev.h, "graph_times")
+    L.tc_graph_destroy(gt)
+    names = {C.OP_GEMM: "GEMM", C.OP_ROW: "ROW", C.OP_ELT: "ELT", C.OP_FDOT: "FDOT", C.OP_ROPE: "ROPE"}
+    kinds: dict = {}
+    for i in range(nt):
+        d = C.decode(bytes(ddr[qa + 64 * i:qa + 64 * (i + 1)]))
+        op = names.get(d["OPCODE"], str(d["OPCODE"]))
+        if d["OPCODE"] == C.OP_FDOT:
+            op += " NN" if d["CTRL"] & 1 else " NT"
+        key = f"{op} {d['M']}x{d['N']}" + (f"x{d['K']}" if d["K"] else "")
+        c, t = kinds.get(key, (0, 0.0))
+        kinds[key] = (c + 1, t + arr[i])
+    top = sorted(kinds.items(), key=lambda kv: -kv[1][1])[:8]
+    descriptor_times = [[k, c, round(1e3 * t / c, 1)] for k, (c, t) in top]     # kind, count, us each
     gemm_ops = 2 * len(px) * sum(lin.n * lin.k for blk in tower.blocks for lin in
                                  (blk["qkv"], blk["proj"], blk["fc1"], blk["fc2"])) + \
         2 * ntok * (tower.m_fc1.n * tower.m_fc1.k + tower.m_fc2.n * tower.m_fc2.k) + 2 * len(px) * tower.pe.n * tower.pe.k
@@ -1103,6 +1129,8 @@ def run_vision(a, world, rank, local) -> dict | None:
                        merged_tokens=ntok, descriptors=qn, parallelism=f"one image per GPU x {world} GPUs",
                        model_build_s=round(build_s, 1)),
         "gemm_tops": round(gemm_ops * a.steps / (ms_max / 1e3) / 1e12, 2),
+        "descriptor_us": {"top_kinds": descriptor_times, "note": "events between descriptors: kind, count, "
+                          "microseconds each (a few of them event overhead)"},
         "e2e": dict(value=round(world * ntok * a.steps / e2e_s, 1), unit="visual tok/s", h2d_bytes_per_step=x_n,
                     d2h_bytes_per_step=y_n, api="opentars_b200.board.Cuda: to_dev (patch rows), run, from_dev"),
         "gpu_launches": a.steps * kernels_per_step, "clocks": clk.summary(),
