@@ -203,10 +203,14 @@ __global__ void __launch_bounds__(kRT) k_rowop_group(const __grid_constant__ Row
   rowop_body(grp.a[lo], b - grp.row0[lo], sm, red);
 }
 
+// The row of flat element i of an M x N matrix: M and N are 16-bit descriptor fields, so i < 2^32
+// and a 32-bit division is exact.
+__device__ __forceinline__ int row_of(uint64_t i, int N) { return (int)((uint32_t)i / (uint32_t)N); }
+
 __global__ void k_act(ActArgs a) {
   const uint64_t total = (uint64_t)a.M * a.N;
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
-    const int m = (int)(i / a.N), n = (int)(i - (uint64_t)m * a.N);
+    const int m = row_of(i, a.N), n = (int)((uint32_t)i - (uint32_t)m * (uint32_t)a.N);
     const float v = ld_f32(a.X + (uint64_t)m * a.lda + 4 * (uint64_t)n);
     store_out(a.Y + (uint64_t)m * a.ldy, n, act_fn(v, a.act), a.out, a.out_scale);
   }
@@ -215,7 +219,7 @@ __global__ void k_act(ActArgs a) {
 __global__ void k_elt(EltArgs a) {
   const uint64_t total = (uint64_t)a.M * a.N;
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
-    const int m = (int)(i / a.N), n = (int)(i - (uint64_t)m * a.N);
+    const int m = row_of(i, a.N), n = (int)((uint32_t)i - (uint32_t)m * (uint32_t)a.N);
     const uint8_t* ap = a.A + (uint64_t)m * a.lda;
     float av = a.a_fp16 ? from_fp16(ld_u16(ap + 2 * (uint64_t)n)) : ld_f32(ap + 4 * (uint64_t)n);
     float bv;
@@ -246,7 +250,7 @@ __global__ void k_rope(RopeArgs a) {
   const uint64_t total = (uint64_t)a.M * a.N;
   const int h = a.R / 2;
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
-    const int m = (int)(i / a.N), n = (int)(i - (uint64_t)m * a.N);
+    const int m = row_of(i, a.N), n = (int)((uint32_t)i - (uint32_t)m * (uint32_t)a.N);
     const uint8_t* x = a.X + (uint64_t)m * a.lda;
     const uint8_t* t = a.tab + (uint64_t)(m / a.G) * 4 * a.R;
     float r;
