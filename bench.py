@@ -1,7 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the tars_mini hot path on B200s (one JSON line from rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|decode-gemma|gemv|w4]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload decode|decode-gemma|gemv|w4|gemm|vision]
                     [--batch B] [--impl ours|reference]
 
 Workloads (synthetic seeded data with the configs' distributions):
@@ -12,8 +13,9 @@ Workloads (synthetic seeded data with the configs' distri
                 each step timed with its own pair of events; ms_per_step_at_position gives the
                 steps near positions 32, 128 and 250. Sequence 0 is checked bit for bit against
                 the reference's logits (committed fixture). The line also carries config0_gemv
-                and config2_w4: the GEMV workloads below, 50 timed steps each (--decode-only
-                skips them).
+                and config2_w4: the GEMV workloads below, 50 timed steps each, and on one GPU
+                config1_gemm (the sweep, 20 steps) and config4_gemma3_decode (Gemma-3-1B decode,
+                positions 20 -> 60) (--decode-only skips them).
   decode-gemma  config 4: the same for Gemma-3-1B shapes
   gemv  config 0: one unit = ROW_QUANT of x [1, 1024] + W8A8 GEMV (QM_ROWCOL) against W [3072, 1024];
         a step runs R units on R distinct weight copies (R * 3 MiB > the 126 MB L2)
@@ -1009,6 +1011,27 @@ def run_decode(a, world, rank, local) -> dict | None:
                               roofline_frac=m["roofline"]["frac"], kernel_us=m["roofline"]["kernel_us"],
                               e2e_gbs=m["e2e"]["value"], bit_exact_unit0=m["bit_exact"], config=m["config"],
                               clocks=m["clocks"])
+        if world == 1 and a.workload == "decode":
+            # config 1 (the GEMM sweep) and config 4 (Gemma-3-1B decode, the first 40 positions)
+            # on one GPU, so the default line carries every BASELINE config
+            import copy
+            ga = copy.copy(a)
+            ga.steps, ga.warmup, ga.no_cpu = 20, 3, True
+            gm = run_gemm(ga, world, rank, local)
+            if gm is not None:
+                units["config1_gemm"] = dict(value=gm["value"], unit=gm["unit"], ms_per_step=gm["ms_per_step"],
+                                             roofline_frac=gm["roofline"]["frac"], e2e=gm["e2e"]["value"],
+                                             bit_exact_vs_reference=gm["bit_exact_vs_reference"],
+                                             config=gm["config"], clocks=gm["clocks"])
+            da = copy.copy(a)
+            da.workload, da.steps, da.warmup, da.no_cpu, da.decode_only = "decode-gemma", 40, 3, True, True
+            dm = run_decode(da, world, rank, local)
+            if dm is not None:
+                units["config4_gemma3_decode"] = dict(
+                    value=dm["value"], unit=dm["unit"], ms_per_step=dm["ms_per_step"],
+                    ms_per_step_at_position=dm["ms_per_step_at_position"], e2e=dm["e2e"]["value"],
+                    bit_exact_seq0_vs_reference=dm["bit_exact_seq0_vs_reference"], config=dm["config"],
+                    clocks=dm["clocks"])
     if rank != 0:
         return None
     out = {
