@@ -2,7 +2,7 @@
 """Benchmark of the tars_mini hot path on B200s (one JSON line from rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--workload decode|decode-gemma|gemv|w4|gemm|vision]
+                    [--workload decode|decode-gemma|gemv|w4|gemm|vision|qwen35]
                     [--batch B] [--impl ours|reference]
 
 Workloads (synthetic seeded data with the configs' distributions):
@@ -1051,6 +1051,110 @@ def run_decode(a, world, rank, local) -> dict | None:
     return out
 
 
+# ----------------------------------------------------------------------------- Qwen3.5 text model
+def run_qwen35(a, world, rank, local) -> dict | None:
+    """Qwen3.5-0.8B shapes (18 gated-DeltaNet and 6 gated full-attention layers, vocab 248320,
+    random-init seeded weights, its MTP head) on the descriptor path through the board runtime:
+    the device time of one decode position's captured queue (one sequence, position PROMPT_LEN,
+    replayed a.steps times - the work of that position, the recurrent state advancing each time),
+    and of an MTP round (the 2-row verify chunk, then the MTP head over the known rows: two tokens
+    when the draft is accepted, one when it is not). Parity of the same queues is pinned at small
+    shapes by the reference's fixtures (models.json qwen35_small*, mtp.json)."""
+    import ctypes
+
+    import torch
+    os.environ["TC_DEVICE"] = str(local)
+    torch.cuda.set_device(local)
+    from opentars_b200 import models as Mo
+    from opentars_b200._lib import check, lib
+    from opentars_b200.board import Cuda
+    from opentars_b200.model_image import ModelImage
+    t_build = time.perf_counter()
+    cfg = Mo.make_config(Mo.CFG_08B, Mo.LAYERS_08B, Mo.VOCAB_08B)
+    w = {**Mo.random_weights(cfg, seed=0, embed=True), **Mo.random_mtp(cfg)}
+    low = ModelImage(cfg, w, max_tokens=CONTEXT, ddr_bytes=3 << 29, head=True, queue_cap=16384, verify_rows=2,
+                     mtp=True)
+    build_s = time.perf_counter() - t_build
+    host = low.p.ddr
+    L = lib()
+    dev = Cuda(len(host), device=local, pinned=True)
+    dev.mem[:] = np.frombuffer(host, np.uint8)
+    dev.to_dev(0, len(host))
+
+    def put(t0: int, toks) -> None:                    # input rows t0 .. up to the device
+        low.put_input(host, t0, low.embed(toks))
+        at = low.p.base + low.x0.off + t0 * low.x0.ld
+        n = len(toks) * low.x0.ld
+        dev.mem[at:at + n] = np.frombuffer(host, np.uint8, count=n, offset=at)
+        dev.to_dev(at, n)
+
+    def queue(record):                                 # the recorded descriptors, staged and uploaded
+        a0 = len(low.p.descs)
+        record()
+        q, n = low.stage(host, a0, len(low.p.descs))
+        dev.mem[q:q + 64 * n] = np.frombuffer(host, np.uint8, count=64 * n, offset=q)
+        dev.to_dev(q, 64 * n)
+        g, st = dev.graph(q, n)
+        assert g is not None and st.done, "the queue must capture"
+        return g, n
+
+    stream = torch.cuda.ExternalStream(L.tc_stream(dev.h), device=local)
+
+    def timed(graphs) -> float:                        # ms per replay of the graphs, in order
+        for _ in range(a.warmup):
+            for g in graphs:
+                check(L.tc_graph_launch(g, None), dev.h)
+        check(L.tc_synchronize(dev.h), dev.h)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(a.steps):
+            for g in graphs:
+                check(L.tc_graph_launch(g, None), dev.h)
+        e1.record(stream)
+        check(L.tc_synchronize(dev.h), dev.h)
+        return e0.elapsed_time(e1) / a.steps
+
+    P = PROMPT_LEN
+    prompt = [int(x) for x in np.random.default_rng(3).integers(0, Mo.VOCAB_08B, P)]
+    n_pre = 0
+    for t0 in range(0, P, CHUNK):                      # the prompt in chunks, as the board runtime feeds it
+        n = min(CHUNK, P - t0)
+        put(t0, prompt[t0:t0 + n])
+        g_pre, k = queue(lambda: low.chunk(t0, n))
+        n_pre += k
+        check(L.tc_graph_launch(g_pre, None), dev.h)
+    put(P, [prompt[-1]])
+    g_dec, n_dec = queue(lambda: low.chunk(P, 1))
+    ms_dec = timed([g_dec])
+    # MTP: the head over the prompt, then rounds at position P (verify 2 rows, MTP over 2 or 1)
+    g_m0, _ = queue(lambda: low.mtp_chunk(0, P))
+    check(L.tc_graph_launch(g_m0, None), dev.h)
+    put(P, [prompt[-1], prompt[0]])
+    g_ver, n_ver = queue(lambda: low.chunk(P, 2, all_rows=True, parity=0, spec=True))
+    g_hit, n_hit = queue(lambda: low.mtp_chunk(P, 2))
+    g_miss, n_miss = queue(lambda: low.mtp_chunk(P, 1))
+    ms_hit = timed([g_ver, g_hit])
+    ms_miss = timed([g_ver, g_miss])
+    kernels = check(L.tc_graph_kernels(g_dec), dev.h, "graph_kernels")
+    dev.close()
+    if rank != 0:
+        return None
+    return {
+        "metric": METRIC, "value": round(1e3 / ms_dec, 1), "unit": "tok/s (one sequence)", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_dec, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic: random-init weights (seeded, the reference's random_weights / random_mtp), seeded prompt",
+        "config": dict(workload="f2_f3_qwen35_0.8b_decode_mtp", layers="18 gated DeltaNet + 6 gated attention",
+                       position=P, path="descriptor queues (board runtime, captured graphs)",
+                       descriptors=dict(decode=n_dec, verify=n_ver, mtp_hit=n_hit, mtp_miss=n_miss, prefill=n_pre)),
+        "model_build_s": round(build_s, 1),
+        "mtp": dict(ms_per_round_accepted=round(ms_hit, 4), tok_s_all_accepted=round(2e3 / ms_hit, 1),
+                    ms_per_round_rejected=round(ms_miss, 4), tok_s_all_rejected=round(1e3 / ms_miss, 1)),
+        "gpu_launches": a.steps * kernels,
+        "parity": "the same queues at small shapes are pinned by tests/golden/models.json and mtp.json",
+    }
+
+
 # ----------------------------------------------------------------------------- Qwen3.5 vision tower
 VISION_SIDE = 448                 # one 448 x 448 image: 28 x 28 patches of 16, 784 patches, 196 tokens
 
@@ -1219,7 +1323,7 @@ def main():
                     help="timed steps (default: decode the whole context once, 236 steps; GEMV: 100)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="decode",
-                    choices=sorted(WORKLOADS) + sorted(DECODE_MODELS) + ["gemm", "vision"])
+                    choices=sorted(WORKLOADS) + sorted(DECODE_MODELS) + ["gemm", "vision", "qwen35"])
     ap.add_argument("--batch", type=int, default=64, help="decode: sequences per GPU")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--units", type=int, default=0)
@@ -1248,6 +1352,8 @@ def main():
     world, rank, local = dist_setup(a.gpus)
     if a.workload == "vision":
         out = run_vision(a, world, rank, local)
+    elif a.workload == "qwen35":
+        out = run_qwen35(a, world, rank, local)
     elif a.workload == "gemm":
         out = run_gemm(a, world, rank, local)
     elif a.workload in DECODE_MODELS:
