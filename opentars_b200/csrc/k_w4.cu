@@ -494,10 +494,11 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
 //
 // Main kernel (k_gemv_w4t): a tile is 64 output columns of one GEMV x all of K; the tiles of the
 // group's GEMVs are numbered one after another, each block takes a contiguous run of them, and its
-// two quads split the run's stages in halves (W4Plan: the tile cut at the midpoint hands its partial
-// bank sums from one quad to the other through shared memory). A quad is four compute warps, warp b adding the terms of
-// the groups g = b (mod 4) - exactly the bank b of the reference's four-bank sum, in increasing g
-// - so no term crosses a warp until the four banks are combined. A producer warp per quad fills
+// two quads split the run's stages in halves (W4Plan: the tile cut at the midpoint hands its
+// partial bank sums from one quad to the other through shared memory). A quad is four compute
+// warps, warp b adding the terms of the groups g = b (mod 4) - exactly the bank b of the
+// reference's four-bank sum, in increasing g - so no term crosses a warp until the four banks are
+// combined. A producer warp per quad fills
 // the quad's ring with stages of four groups: two TMA boxes of 64 rows x 128 bytes of weights
 // (128-byte swizzle: the lanes' 16-byte reads of one row chunk land on eight different bank
 // groups) and, per activation row, the four groups' aligned mantissas (1 KB) and scale / sum
@@ -516,9 +517,10 @@ __global__ void __launch_bounds__(kW4Threads, 1) k_gemv_w4s(W4Args g) {
 // columns; MMA rows i and i + 8 are tile rows 16 cb + r(i) and + 8 with r = 0 4 1 5 2 6 3 7, so the
 // eight lanes of each 16-byte read phase hit eight different bank groups of the swizzled rows. B
 // columns 2..7 repeat the two planes, so every lane holds whole dots; lane (i, t) owns the columns
-// of block t (rows r(i), r(i) + 8). The fp16 group scales of the next tile
-// are copied into shared memory (4-byte cp.async, columns padded to an odd number of words) while
-// the current tile computes. Every wait is bounded; after a give-up the warps skip their remaining
+// of block t (rows r(i), r(i) + 8). The fp16 group scales of the next piece's tile are copied
+// into shared memory (4-byte cp.async, one warp per column, columns padded to an odd number of
+// words) while the current piece computes; the ring slot and its phase advance without integer
+// divisions, and the barrier polls sleep (suspend-time hint). Every wait is bounded; after a give-up the warps skip their remaining
 // work but keep the quad's barrier count, the producers stop issuing (the activation copies of
 // stages whose weights were requested are still issued), and the block drains the copies in
 // flight.
